@@ -1,0 +1,160 @@
+/*
+ * vx.h -- C ABI of libvx.so, the B200 (sm_100a) batch distance + top-k scan behind the
+ * integrallis/vectors index SPI.
+ *
+ * The entry points are what a Java 25 Foreign Function & Memory binding of the reference's
+ * IndexSpi backends would call (Linker.nativeLinker().downcallHandle, the pattern of
+ * vectors-storage/.../io/MadviseUtil.java:52-58).  Plain pointers and sizes only; every
+ * function returns a vx_status and leaves a message for vx_last_error() on failure.
+ *
+ * Conventions
+ *   - Ordinals are int32 (0..n-1), scores are float32 on the reference's scale, results are
+ *     ordered by (score desc, ordinal asc), the canonical order of TopK.select
+ *     (vectors-core/.../TopK.java:58-116).
+ *   - Output arrays are [nq][k] row-major; out_counts[q] valid entries per query (<= k; the
+ *     unused tail holds ordinal -1, score 0).
+ *   - "host" entry points take host buffers (pinned or pageable) and block until the results
+ *     are in them; "_device" entry points take device pointers and a cudaStream_t (as void*)
+ *     and return once the work is queued, except where a query needs the exact fallback scan,
+ *     which synchronises the stream internally.
+ *   - An index is safe for concurrent searches from several host threads; builds and frees
+ *     must not overlap searches on the same index (the facade's read/write lock,
+ *     FlatScanAdapter.java:31-33).
+ */
+#ifndef VX_H
+#define VX_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define VX_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define VX_API __attribute__((visibility("default")))
+#else
+#define VX_API
+#endif
+
+/* Status codes.  The Java shim maps them onto the reference's exceptions. */
+typedef enum vx_status {
+  VX_OK = 0,
+  VX_ERR_INVALID_ARGUMENT = 1, /* IllegalArgumentException (FlatScanAdapter.java:53-62,108-135) */
+  VX_ERR_NULL_POINTER = 2,     /* NullPointerException (Objects.requireNonNull) */
+  VX_ERR_GPU_UNAVAILABLE = 3,  /* GpuUnavailableException (CuVsBruteForceAdapter.java:67-70) */
+  VX_ERR_CUDA = 4,             /* GpuUnavailableException wrapping a native failure (:86-89,117-119) */
+  VX_ERR_OUT_OF_MEMORY = 5,
+  VX_ERR_UNSUPPORTED = 6,      /* UnsupportedOperationException */
+  VX_ERR_DEVICE_TIMEOUT = 7    /* a bounded device-side wait expired; the context stays usable */
+} vx_status;
+
+/* SimilarityFunction ordinals (vectors-core/.../SimilarityFunction.java:30-120). */
+typedef enum vx_metric {
+  VX_EUCLIDEAN = 0,
+  VX_DOT_PRODUCT = 1,
+  VX_COSINE = 2,
+  VX_MAXIMUM_INNER_PRODUCT = 3
+} vx_metric;
+
+typedef enum vx_index_kind {
+  VX_KIND_FLAT = 0,  /* IndexType.FLAT, QuantizerKind.NONE  -> FlatScanAdapter          */
+  VX_KIND_FP16 = 1,  /* QuantizerKind.FP16 -> QuantizedFlatScanAdapter(Fp16QuantizedVectors) */
+  VX_KIND_SQ8 = 2,   /* QuantizerKind.SQ8  -> QuantizedFlatScanAdapter(ScalarQuantizedVectors) */
+  VX_KIND_BQ = 3,    /* QuantizerKind.BQ (SIGN_BIT) -> QuantizedFlatScanAdapter(BinaryQuantizedVectors) */
+  VX_KIND_IVFPQ = 4  /* IndexType.IVF_PQ -> IvfPqAdapter / IvfIndex.pqSearch                 */
+} vx_index_kind;
+
+typedef struct vx_index vx_index;
+
+/* ---- library ------------------------------------------------------------------------ */
+VX_API int vx_abi_version(void);
+/* Message of the last failed call on this host thread ("" if none). */
+VX_API const char* vx_last_error(void);
+/* Number of usable CUDA devices; GpuProvider.availability() (vectors-gpu/.../GpuProvider.java). */
+VX_API int vx_device_count(int32_t* count);
+/* Kernels launched by this library since load (cumulative, all threads). */
+VX_API int vx_kernel_launches(int64_t* count);
+/* Test hook: the next vx_* call on this host thread fails with `status` before touching the
+ * GPU (host-side fault injection; status 0 clears it). */
+VX_API int vx_debug_fail_next(int32_t status);
+
+/* ---- index construction (the handle owns device copies; inputs are not retained) ----- */
+/* FlatScanAdapter.build(float[][] vectors, SimilarityFunction metric)
+ * (vectors-db/.../index/FlatScanAdapter.java:42-48).  row_stride in floats (>= dim); use
+ * alignUp(dim*4, 64)/4 to read a persistent vectors.bin (MemorySegmentVectors.java:39-45). */
+VX_API int vx_flat_build(int32_t device, const float* vectors, int64_t n, int32_t dim, int64_t row_stride,
+                  int32_t metric, vx_index** out);
+/* Fp16QuantizedVectors (vectors-quantization/.../Fp16QuantizedVectors.java:40-94) wrapped as in
+ * QuantizedFlatScanAdapter (vectors-db/.../index/QuantizedFlatScanAdapter.java:34-51).  codes:
+ * [n][dim] little-endian binary16 (Fp16Quantizer.encode, Fp16Quantizer.java:72-85).  vectors
+ * (fp32, optional) enable the exact rescore of vx_search_batch; NULL keeps codes only. */
+VX_API int vx_fp16_build(int32_t device, const uint16_t* codes, int64_t n, int32_t dim, int32_t metric,
+                  const float* vectors, int64_t row_stride, vx_index** out);
+/* ScalarQuantizedVectors INT8 (ScalarQuantizedVectors.java:40-107): codes [n][dim] in 0..127,
+ * per-row corrections, the quantizer's quantiles (ScalarQuantizer.fromQuantiles,
+ * ScalarQuantizer.java:144-151). */
+VX_API int vx_sq8_build(int32_t device, const int8_t* codes, const float* corrections, int64_t n,
+                 int32_t dim, float min_quantile, float max_quantile, int32_t metric,
+                 const float* vectors, int64_t row_stride, vx_index** out);
+/* BinaryQuantizedVectors SIGN_BIT (BinaryQuantizedVectors.java:40-107): words [n][ceil(dim/64)]
+ * as produced by BinaryQuantizer.packBits + bytesToLongs (BinaryQuantizer.java:207-232). */
+VX_API int vx_bq_build(int32_t device, const uint64_t* words, int64_t n, int32_t dim, int32_t metric,
+                const float* vectors, int64_t row_stride, vx_index** out);
+/* IvfIndex.fromPrebuilt(buoy, partitions, vectors, metric, pq, codes)
+ * (vectors-ivf/.../IvfIndex.java:343-351): centroids [nlist][dim]; partitions as CSR
+ * (list_offsets[nlist+1], list_ordinals); PQ with m subspaces of ks centroids, codebooks
+ * concatenated per subspace (ProductQuantizer.codebooks(), subspace sizes from
+ * computeSubspaceSizesAndOffsets, ProductQuantizer.java:686-700), no global centroid; codes
+ * [n][m] in ordinal order (IvfIndex.java:59).  nprobe / rescore_factor are the adapter's
+ * defaults (IvfPqAdapter.java:84-109); vectors (optional) enable rescore_factor > 1. */
+VX_API int vx_ivfpq_build(int32_t device, const float* centroids, int32_t nlist, int32_t dim,
+                   const int64_t* list_offsets, const int32_t* list_ordinals, int32_t m, int32_t ks,
+                   const float* codebooks, const uint8_t* codes, int64_t n, int32_t metric,
+                   const float* vectors, int32_t nprobe, int32_t rescore_factor, vx_index** out);
+/* IndexSpi.size() and the index's shape. */
+VX_API int vx_index_info(const vx_index* index, int32_t* kind, int64_t* size, int32_t* dim,
+                  int32_t* metric);
+/* IndexSpi.close() (IndexSpi.java:157-159). */
+VX_API int vx_index_free(vx_index* index);
+
+/* ---- search --------------------------------------------------------------------------- */
+/* IndexSpi.searchBatch(float[][] queries, int k, int searchListSize, float overQueryFactor)
+ * (IndexSpi.java:127-152; FlatScanAdapter.java:106-175; QuantizedFlatScanAdapter.java:59-95;
+ * IvfPqAdapter.java:124-158).  queries: [nq][dim] fp32. */
+VX_API int vx_search_batch(vx_index* index, const float* queries, int32_t nq, int32_t dim, int32_t k,
+                    int32_t search_list_size, float over_query_factor, int32_t* out_ids,
+                    float* out_scores, int32_t* out_counts);
+VX_API int vx_search_batch_device(vx_index* index, const float* d_queries, int32_t nq, int32_t dim,
+                           int32_t k, int32_t search_list_size, float over_query_factor,
+                           int32_t* d_ids, float* d_scores, int32_t* d_counts, void* stream);
+/* QuantizedFlatScanAdapter.selectApproximateCandidates (QuantizedFlatScanAdapter.java:97-113):
+ * the k best rows by the compressed ScoreFunction (SQ8 / BQ / FP16 scores), no rescore. */
+VX_API int vx_scan_candidates(vx_index* index, const float* queries, int32_t nq, int32_t dim, int32_t k,
+                       int32_t* out_ids, float* out_scores, int32_t* out_counts);
+VX_API int vx_scan_candidates_device(vx_index* index, const float* d_queries, int32_t nq, int32_t dim,
+                              int32_t k, int32_t* d_ids, float* d_scores, int32_t* d_counts,
+                              void* stream);
+/* IvfIndex.search(new IvfSearchRequest(query, k, nprobe, 0f, minScore, rescoreFactor))
+ * (IvfIndex.java:170-171,539-619; IvfSearchRequest.java:32-65). */
+VX_API int vx_ivfpq_search(vx_index* index, const float* queries, int32_t nq, int32_t dim, int32_t k,
+                    int32_t nprobe, int32_t rescore_factor, float min_score, int32_t* out_ids,
+                    float* out_scores, int32_t* out_counts);
+VX_API int vx_ivfpq_search_device(vx_index* index, const float* d_queries, int32_t nq, int32_t dim,
+                           int32_t k, int32_t nprobe, int32_t rescore_factor, float min_score,
+                           int32_t* d_ids, float* d_scores, int32_t* d_counts, void* stream);
+
+/* ---- shards ---------------------------------------------------------------------------- */
+/* IndexShards.mergeWithOffsets (vectors-db/.../index/IndexShards.java:168-211): shard s holds
+ * shard_counts[s*nq+q] (ordinal, score) pairs of query q at [(s*nq+q)*kin]; ordinals are
+ * shifted by offsets[s]; result: the k best by (score desc, ordinal asc).  Device buffers. */
+VX_API int vx_merge_shards_device(int32_t device, int32_t nshards, const int64_t* d_offsets,
+                           const int32_t* d_shard_ids, const float* d_shard_scores,
+                           const int32_t* d_shard_counts, int32_t kin, int32_t nq, int32_t k,
+                           int32_t* d_ids, float* d_scores, int32_t* d_counts, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* VX_H */

@@ -1,0 +1,91 @@
+"""C ABI checks that need no GPU: the library loads, exports exactly what include/vx.h declares,
+and the SPI mirror reports the reference's errors (IndexSpi.java, FlatScanAdapter.java:51-175)."""
+import os
+import re
+import subprocess
+
+import numpy as np
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _declared():
+    src = open(os.path.join(ROOT, "include", "vx.h")).read()
+    return sorted(set(re.findall(r"^VX_API\s+[\w\s\*]+?\b(vx_\w+)\(", src, flags=re.M)))
+
+
+def test_library_loads_and_exports_every_declared_symbol():
+    import vectors_b200._native as N
+
+    lib = N.lib()
+    declared = _declared()
+    assert len(declared) >= 19
+    for name in declared:
+        assert hasattr(lib, name), name
+    out = subprocess.run(["nm", "-D", "--defined-only", N.LIB_PATH], capture_output=True, text=True).stdout
+    exported = sorted(line.split()[-1] for line in out.splitlines() if " T vx_" in line)
+    assert exported == declared
+    assert sorted(N.exported_symbols()) == declared
+
+
+def test_abi_version():
+    import vectors_b200._native as N
+
+    assert N.lib().vx_abi_version() == 1
+
+
+def test_no_gpu_reports_gpu_unavailable():
+    import vectors_b200 as vx
+
+    if vx.device_count() > 0:
+        pytest.skip("a GPU is present")
+    f = vx.FlatScanAdapter()
+    with pytest.raises(vx.GpuUnavailableException):
+        f.build(np.zeros((4, 3), np.float32), vx.SimilarityFunction.COSINE)
+
+
+def test_injected_failure_maps_to_exception():
+    import vectors_b200 as vx
+    import vectors_b200._native as N
+
+    N.lib().vx_debug_fail_next(N.VX_ERR_INVALID_ARGUMENT)
+    with pytest.raises(vx.IllegalArgumentException, match="injected"):
+        vx.FlatScanAdapter().build(np.zeros((4, 3), np.float32), vx.SimilarityFunction.COSINE)
+    N.lib().vx_debug_fail_next(N.VX_ERR_CUDA)
+    with pytest.raises(vx.GpuUnavailableException, match="injected"):
+        vx.FlatScanAdapter().build(np.zeros((4, 3), np.float32), vx.SimilarityFunction.COSINE)
+
+
+def test_argument_validation_before_gpu():
+    import vectors_b200 as vx
+
+    f = vx.FlatScanAdapter()
+    with pytest.raises(vx.NullPointerException):
+        f.build(None, vx.SimilarityFunction.COSINE)
+    with pytest.raises(vx.NullPointerException):
+        f.build(np.zeros((2, 2), np.float32), None)
+    # empty index: searches return empty outcomes, bad k / empty batch are rejected
+    with pytest.raises(vx.IllegalArgumentException):
+        f.search_batch([], 3)
+    with pytest.raises(vx.IllegalArgumentException):
+        f.search_batch([[1.0, 2.0]], 0)
+    with pytest.raises(vx.NullPointerException):
+        f.search_batch(None, 3)
+    with pytest.raises(vx.NullPointerException):
+        f.search(None, 3)
+    out = f.search_batch([[1.0, 2.0], [3.0, 4.0]], 3)
+    assert len(out) == 2 and all(len(o.ordinals) == 0 for o in out)
+    with pytest.raises(vx.IllegalArgumentException):
+        vx.SearchOutcome(np.zeros(2, np.int32), np.zeros(3, np.float32))
+
+
+def test_null_pointer_status_from_c():
+    import ctypes as C
+
+    import vectors_b200._native as N
+
+    st = N.lib().vx_flat_build(0, None, 5, 4, 4, 0, C.byref(C.c_void_p()))
+    assert st in (N.VX_ERR_NULL_POINTER, N.VX_ERR_GPU_UNAVAILABLE)
+    assert N.lib().vx_device_count(None) == N.VX_ERR_NULL_POINTER
+    assert "null" in N.last_error()

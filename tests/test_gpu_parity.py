@@ -1,0 +1,208 @@
+"""GPU parity: the CUDA scans (through the C ABI) against the CPU oracle on seeded inputs.
+
+Bar: bit-exact ordinals and scores for the integer / code paths (SQ8, BQ, IVF-PQ ADC); for the
+fp32 / fp16 paths identical ordinals and scores within 1e-4 relative (the exact re-score runs
+in the reference's operation order, so scores are expected to agree to the bit as well).
+"""
+import numpy as np
+import pytest
+
+import vectors_b200 as vx
+
+pytestmark = pytest.mark.gpu
+
+SEED_C, SEED_DB, SEED_Q = 0xC0FFEE03, 0xC0FFEE01, 0xC0FFEE02
+REL = 1e-4
+
+
+def _check_float(got, ids, sc, cnt, tag, exact_scores=False):
+    for i, o in enumerate(got):
+        c = cnt[i]
+        assert len(o.ordinals) == c, f"{tag}: query {i} count {len(o.ordinals)} != {c}"
+        assert list(o.ordinals) == list(ids[i, :c]), f"{tag}: query {i} ids {o.ordinals[:8]} vs {ids[i, :8]}"
+        if exact_scores:
+            assert np.array_equal(o.scores, sc[i, :c]), f"{tag}: query {i} scores differ"
+        else:
+            np.testing.assert_allclose(o.scores, sc[i, :c], rtol=REL, atol=0, err_msg=tag)
+
+
+def _data(O, n, dim, nq, comps=16, sigma=0.3, normalize=True):
+    db = O.gen_mixture(n, dim, comps, sigma, SEED_C, SEED_DB, normalize)
+    q = O.gen_mixture(nq, dim, comps, sigma, SEED_C, SEED_Q, normalize)
+    return db, q
+
+
+# ------------------------------------------------------------------ FLAT
+@pytest.mark.parametrize("metric", [0, 1, 2, 3])
+@pytest.mark.parametrize("n,dim,nq,k", [(5000, 128, 64, 10), (3000, 100, 33, 7), (1000, 768, 10, 100), (257, 64, 130, 5)])
+def test_flat_matches_oracle(oracle, metric, n, dim, nq, k):
+    db, q = _data(oracle, n, dim, nq, normalize=(metric != 3))
+    f = vx.FlatScanAdapter()
+    f.build(db, vx.SimilarityFunction(metric))
+    got = f.search_batch(q, k)
+    ids, sc, cnt = oracle.flat_search(db, q, metric, k)
+    _check_float(got, ids, sc, cnt, f"flat m={metric} n={n} dim={dim}")
+    f.close()
+
+
+def test_flat_single_query_and_small_index(oracle):
+    db, q = _data(oracle, 5, 32, 3)
+    f = vx.FlatScanAdapter()
+    f.build(db, vx.SimilarityFunction.COSINE)
+    got = f.search_batch(q, 10)  # k > n
+    ids, sc, cnt = oracle.flat_search(db, q, oracle.COSINE, 10)
+    _check_float(got, ids, sc, cnt, "flat k>n")
+    one = f.search(q[0], 3)
+    assert list(one.ordinals) == list(ids[0, :3])
+
+
+def test_flat_duplicates_take_exact_fallback(oracle):
+    # many identical rows: the approximate window cannot separate them, so the exact scan
+    # decides and ties resolve to the lowest ordinals
+    rng = np.random.default_rng(0)
+    base = rng.standard_normal((1, 64)).astype(np.float32)
+    db = np.repeat(base, 600, axis=0)
+    db[::7] += 0.5 * rng.standard_normal((len(db[::7]), 64)).astype(np.float32)
+    q = base + 0.01 * rng.standard_normal((4, 64)).astype(np.float32)
+    for metric in (1, 2):
+        f = vx.FlatScanAdapter()
+        f.build(db, vx.SimilarityFunction(metric))
+        got = f.search_batch(q, 20)
+        ids, sc, cnt = oracle.flat_search(db, q, metric, 20)
+        _check_float(got, ids, sc, cnt, f"flat duplicates m={metric}")
+
+
+def test_flat_empty_index(oracle):
+    f = vx.FlatScanAdapter()
+    f.build(np.zeros((0, 0), np.float32), vx.SimilarityFunction.COSINE)
+    out = f.search_batch(np.ones((2, 8), np.float32), 4)
+    assert [len(o.ordinals) for o in out] == [0, 0]
+
+
+def test_flat_dimension_mismatch(oracle):
+    db, q = _data(oracle, 100, 16, 2)
+    f = vx.FlatScanAdapter()
+    f.build(db, vx.SimilarityFunction.COSINE)
+    with pytest.raises(vx.IllegalArgumentException, match="dimension"):
+        f.search_batch(np.ones((2, 17), np.float32), 4)
+
+
+# ------------------------------------------------------------------ SQ8
+@pytest.mark.parametrize("metric", [0, 1, 2, 3])
+@pytest.mark.parametrize("n,dim,nq,k", [(6000, 768, 40, 100), (2500, 100, 129, 10)])
+def test_sq8_bit_exact(oracle, metric, n, dim, nq, k):
+    db, q = _data(oracle, n, dim, nq)
+    lo, hi = oracle.sq8_train(db)
+    codes, corr = oracle.sq8_encode_all(lo, hi, db)
+    a = vx.QuantizedFlatScanAdapter()
+    a.build_sq8(codes, corr, lo, hi, vx.SimilarityFunction(metric))
+    got = a.scan_candidates(q, k)
+    ids, sc, cnt = oracle.sq8_search(codes, corr, lo, hi, q, metric, k)
+    _check_float(got, ids, sc, cnt, f"sq8 m={metric}", exact_scores=True)
+
+
+def test_sq8_two_pass(oracle):
+    db, q = _data(oracle, 4000, 128, 20)
+    lo, hi = oracle.sq8_train(db)
+    codes, corr = oracle.sq8_encode_all(lo, hi, db)
+    a = vx.QuantizedFlatScanAdapter()
+    a.build_sq8(codes, corr, lo, hi, vx.SimilarityFunction.DOT_PRODUCT, vectors=db)
+    got = a.search_batch(q, 10, 0, 4.0)
+    ids, sc, cnt = oracle.quantized_two_pass(0, codes, corr, lo, hi, db, q, oracle.DOT_PRODUCT, 10, 4.0)
+    _check_float(got, ids, sc, cnt, "sq8 two-pass")
+    got = a.search_batch(q, 10, 0, 1.0)  # oqf <= 1 delegates to the exact scan
+    ids, sc, cnt = oracle.flat_search(db, q, oracle.DOT_PRODUCT, 10)
+    _check_float(got, ids, sc, cnt, "sq8 exact delegate")
+
+
+# ------------------------------------------------------------------ BQ
+@pytest.mark.parametrize("metric", [0, 1, 2, 3])
+@pytest.mark.parametrize("n,dim,nq,k", [(20000, 1024, 300, 100), (3000, 100, 17, 10), (999, 64, 5, 3)])
+def test_bq_bit_exact(oracle, metric, n, dim, nq, k):
+    db, q = _data(oracle, n, dim, nq, sigma=0.5, normalize=False)
+    words = oracle.bq_encode_all(db)
+    a = vx.QuantizedFlatScanAdapter()
+    a.build_bq(words, dim, vx.SimilarityFunction(metric))
+    got = a.scan_candidates(q, k)
+    ids, sc, cnt = oracle.bq_search(words, dim, q, metric, k)
+    _check_float(got, ids, sc, cnt, f"bq m={metric} dim={dim}", exact_scores=True)
+
+
+def test_bq_all_equal_rows_ties_by_ordinal(oracle):
+    db = np.ones((5000, 128), np.float32)
+    q = np.ones((3, 128), np.float32)
+    words = oracle.bq_encode_all(db)
+    a = vx.QuantizedFlatScanAdapter()
+    a.build_bq(words, 128, vx.SimilarityFunction.COSINE)
+    got = a.scan_candidates(q, 50)
+    for o in got:
+        assert list(o.ordinals) == list(range(50))
+
+
+# ------------------------------------------------------------------ FP16
+@pytest.mark.parametrize("metric", [0, 1, 3])
+def test_fp16_candidates_match_oracle(oracle, metric):
+    db, q = _data(oracle, 6000, 256, 50, normalize=(metric != 3))
+    codes = oracle.fp16_encode_all(db)
+    a = vx.QuantizedFlatScanAdapter()
+    a.build_fp16(codes, vx.SimilarityFunction(metric))
+    got = a.scan_candidates(q, 100)
+    ids, sc, cnt = oracle.fp16_search(codes, q, metric, 100)
+    _check_float(got, ids, sc, cnt, f"fp16 m={metric}")
+
+
+# ------------------------------------------------------------------ IVF-PQ
+def _ivf(oracle, n=20000, dim=64, nlist=64, m=8, ks=256, comps=32):
+    db = oracle.gen_mixture(n, dim, comps, 0.3, SEED_C, SEED_DB, False)
+    q = oracle.gen_mixture(40, dim, comps, 0.3, SEED_C, SEED_Q, False)
+    cent = oracle.kmeans_train(db[:5000], nlist, 10, 42)
+    assign = oracle.kmeans_assign(db, cent)
+    off, ords = oracle.build_ivf_lists(assign, nlist)
+    resid = db - cent[assign]
+    cb = oracle.pq_train(resid, m, ks)
+    codes = oracle.pq_encode_all(resid, m, ks, cb)
+    return db, q, cent, off, ords, cb, codes
+
+
+@pytest.mark.parametrize("metric", [0, 1])
+def test_ivfpq_bit_exact(oracle, metric):
+    db, q, cent, off, ords, cb, codes = _ivf(oracle)
+    a = vx.IvfPqAdapter(nprobe=8)
+    a.build_prebuilt(cent, off, ords, cb, codes, 8, 256, vx.SimilarityFunction(metric), vectors=db)
+    got = a.ivf_search(q, 10, 8)
+    ids, sc, cnt = oracle.ivfpq_search(cent, off, ords, 8, 256, cb, codes, q, metric, 10, 8)
+    _check_float(got, ids, sc, cnt, f"ivfpq m={metric}", exact_scores=True)
+    got = a.ivf_search(q, 10, 8, rescore_factor=4)
+    ids, sc, cnt = oracle.ivfpq_search(cent, off, ords, 8, 256, cb, codes, q, metric, 10, 8, 4, db)
+    _check_float(got, ids, sc, cnt, f"ivfpq rescore m={metric}")
+
+
+def test_ivfpq_routing_matches_oracle(oracle):
+    db, q, cent, off, ords, cb, codes = _ivf(oracle)
+    lids, _ = oracle.route(cent, q, oracle.EUCLIDEAN, 8)
+    ref_lids, _ = oracle.route(cent, q, oracle.EUCLIDEAN, 8, oracle.REFERENCE_HEAP)
+    assert np.array_equal(np.sort(lids, 1), np.sort(ref_lids, 1))
+
+
+# ------------------------------------------------------------------ shards
+def test_merge_shards_device(oracle):
+    import torch
+
+    db, q = _data(oracle, 3000, 64, 9)
+    S = 3
+    offs = vx.shard_offsets(3000, S)
+    parts = []
+    for s in range(S):
+        f = vx.FlatScanAdapter()
+        f.build(db[offs[s]:offs[s + 1]], vx.SimilarityFunction.COSINE)
+        ids, sc, cnt = f.search_batch_device(torch.from_numpy(q).cuda(), 10)
+        parts.append((ids, sc, cnt))
+        f.close()
+    ids = torch.stack([p[0] for p in parts])
+    sc = torch.stack([p[1] for p in parts])
+    cnt = torch.stack([p[2] for p in parts])
+    mi, ms, mc = vx.merge_shards_device(ids, sc, cnt, torch.tensor(offs[:S]), 10)
+    torch.cuda.synchronize()
+    ref = oracle.flat_search(db, q, oracle.COSINE, 10)
+    assert np.array_equal(mi.cpu().numpy(), ref[0])
+    np.testing.assert_allclose(ms.cpu().numpy(), ref[1], rtol=REL)

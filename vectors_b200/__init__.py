@@ -1,0 +1,40 @@
+"""vectors_b200: the integrallis/vectors batch distance + top-k scan on NVIDIA B200 (sm_100a).
+
+The scans (FLAT exact search, the SQ8 / FP16 / sign-bit BQ quantized scans and the IVF-PQ ADC
+list scan) run as hand-written CUDA kernels in ``libvx.so``; this package is the host-side
+mirror of the reference's index SPI over that library's C ABI (include/vx.h).
+"""
+from ._native import VxError, device_count, kernel_launches, lib  # noqa: F401
+from .index_spi import (  # noqa: F401
+    FlatScanAdapter,
+    GpuUnavailableException,
+    IllegalArgumentException,
+    IndexSpi,
+    IvfPqAdapter,
+    NullPointerException,
+    QuantizedFlatScanAdapter,
+    SearchOutcome,
+    SimilarityFunction,
+    UnsupportedOperationException,
+    merge_shards_device,
+    shard_offsets,
+)
+
+__all__ = [
+    "FlatScanAdapter",
+    "QuantizedFlatScanAdapter",
+    "IvfPqAdapter",
+    "IndexSpi",
+    "SearchOutcome",
+    "SimilarityFunction",
+    "IllegalArgumentException",
+    "NullPointerException",
+    "GpuUnavailableException",
+    "UnsupportedOperationException",
+    "merge_shards_device",
+    "shard_offsets",
+    "device_count",
+    "kernel_launches",
+    "lib",
+    "VxError",
+]

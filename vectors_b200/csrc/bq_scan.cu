@@ -1,0 +1,205 @@
+// bq_scan.cu -- sign-bit binary quantization (BQ) Hamming scan with fused top-K.
+//
+// Restates, batched over queries, QuantizedFlatScanAdapter.selectApproximateCandidates
+// (vectors-db/.../index/QuantizedFlatScanAdapter.java:97-113) over
+// BinaryQuantizedVectors.signBitScoreFunction (vectors-quantization/.../
+// BinaryQuantizedVectors.java:81-107): h = sum_w popcount(q_w XOR v_w).  Every score
+// function of h is strictly decreasing in h for 0 <= h <= dim, so ranking by (h asc, id asc)
+// equals ranking by (score desc, id asc); scores are recovered from h at the end.
+//
+// Layout: the database is row-major, 8*nw_pad bytes per row (the reference's long[] words,
+// BinaryQuantizer.java:207-232, zero-padded to nw_pad words).  Each CTA owns a contiguous
+// range of rows (a "part") and streams it through shared memory in 128-row tiles; every
+// thread owns one query (its words live in registers) and scores each staged row against
+// it.  The database is read from HBM once per batch; the binding roof is the integer/popc
+// pipe.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace vx {
+
+namespace {
+
+constexpr int kBqTile = 128;
+constexpr int kBqThreads = 256;
+
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem, bool valid) {
+  uint32_t s = (uint32_t)__cvta_generic_to_shared(smem);
+  int sz = valid ? 16 : 0;
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(s), "l"(gmem), "r"(sz)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
+
+template <int NW, int R>
+__global__ void __launch_bounds__(kBqThreads, 2)
+    bq_scan_kernel(const uint64_t* __restrict__ db, int64_t n, const uint64_t* __restrict__ qw,
+                   int nq, int64_t rows_per_part, int K, int C, uint64_t* __restrict__ bufs,
+                   uint32_t* __restrict__ cnts, uint64_t* __restrict__ thrs) {
+  extern __shared__ __align__(16) uint64_t s_tile[];  // [2][kBqTile * NW]
+  const int part = blockIdx.x;
+  const int64_t r0 = (int64_t)part * rows_per_part;
+  int64_t r1 = r0 + rows_per_part;
+  if (r1 > n) r1 = n;
+  const int64_t nrows = r1 > r0 ? r1 - r0 : 0;
+  const int ntiles = (int)((nrows + kBqTile - 1) / kBqTile);
+  constexpr int kChunks = kBqTile * NW / 2;  // 16-byte chunks per tile
+
+  auto stage = [&](int t) {
+    uint64_t* dst = s_tile + (t & 1) * (kBqTile * NW);
+    const int64_t base_row = r0 + (int64_t)t * kBqTile;
+    for (int c = threadIdx.x; c < kChunks; c += kBqThreads) {
+      int row = c / (NW / 2 > 0 ? NW / 2 : 1);
+      bool valid = (base_row + row) < r1;
+      const uint64_t* src = valid ? db + (base_row * NW) + (int64_t)c * 2 : db;
+      cp_async16(dst + c * 2, src, valid);
+    }
+  };
+
+  if (ntiles > 0) stage(0);
+  cp_async_commit();
+  for (int t = 0; t < ntiles; t++) {
+    if (t + 1 < ntiles) stage(t + 1);
+    cp_async_commit();
+    cp_async_wait1();
+    __syncthreads();
+    const uint64_t* T = s_tile + (t & 1) * (kBqTile * NW);
+    const int64_t base_row = r0 + (int64_t)t * kBqTile;
+    const int rows = (int)((r1 - base_row) < kBqTile ? (r1 - base_row) : kBqTile);
+    for (int qb = 0; qb < nq; qb += kBqThreads) {
+      const int q = qb + threadIdx.x;
+      const bool active = q < nq;
+      uint64_t qr[NW];
+#pragma unroll
+      for (int w = 0; w < NW; w++) qr[w] = active ? qw[(size_t)q * NW + w] : 0ull;
+      const size_t sidx = (size_t)part * nq + (active ? q : 0);
+      LaneStream st;
+      st.base = bufs + sidx * (size_t)C;
+      st.cnt = active ? cnts[sidx] : 0u;
+      st.thr = active ? thrs[sidx] : ~0ull;
+      for (int rr = 0; rr < rows; rr += 32) {
+        const int re = (rr + 32 < rows) ? rr + 32 : rows;
+        for (int r = rr; r < re; r++) {
+          const uint64_t* row = T + r * NW;
+          uint32_t h = 0;
+#pragma unroll
+          for (int w = 0; w < NW; w++) h += (uint32_t)__popcll(qr[w] ^ row[w]);
+          st.offer(make_key(0xFFFFFFFFu - h, (uint32_t)(base_row + r)));
+        }
+        warp_compact_lanes<R>(st.cnt > (uint32_t)(C - 32), st.base, st.cnt, st.thr, (uint32_t)K);
+      }
+      if (active) {
+        cnts[sidx] = st.cnt;
+        thrs[sidx] = st.thr;
+      }
+    }
+    __syncthreads();
+  }
+  // Leave every stream of this part with at most K keys.
+  for (int qb = 0; qb < nq; qb += kBqThreads) {
+    const int q = qb + threadIdx.x;
+    const bool active = q < nq;
+    const size_t sidx = (size_t)part * nq + (active ? q : 0);
+    uint64_t* base = bufs + sidx * (size_t)C;
+    uint32_t cnt = active ? cnts[sidx] : 0u;
+    uint64_t thr = active ? thrs[sidx] : ~0ull;
+    warp_compact_lanes<R>(cnt > (uint32_t)K, base, cnt, thr, (uint32_t)K);
+    if (active) cnts[sidx] = cnt;
+  }
+}
+
+template <int NW>
+cudaError_t launch_nw(const uint64_t* db, int64_t n, const uint64_t* qw, int nq, int parts,
+                      const StreamGeom& g, uint64_t* bufs, uint32_t* cnts, uint64_t* thrs,
+                      cudaStream_t st) {
+  int64_t rows_per_part = (n + parts - 1) / parts;
+  size_t smem = 2ull * kBqTile * NW * sizeof(uint64_t);
+#define VX_BQ_CASE(RR)                                                                         \
+  case RR: {                                                                                   \
+    auto kern = bq_scan_kernel<NW, RR>;                                                        \
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,    \
+                                         (int)smem);                                           \
+    if (e != cudaSuccess) return e;                                                            \
+    kern<<<parts, kBqThreads, smem, st>>>(db, n, qw, nq, rows_per_part, g.K, g.C, bufs, cnts,   \
+                                          thrs);                                               \
+    return cudaGetLastError();                                                                 \
+  }
+  switch (g.R) {
+    VX_BQ_CASE(2)
+    VX_BQ_CASE(3)
+    VX_BQ_CASE(5)
+    VX_BQ_CASE(9)
+    VX_BQ_CASE(17)
+    VX_BQ_CASE(33)
+    default: return cudaErrorInvalidValue;
+  }
+#undef VX_BQ_CASE
+}
+
+// Packs fp32 queries into sign-bit words: bit (d & 63) of word (d >> 6) is set iff
+// v[d] >= 0 (BinaryQuantizer.packBits / bytesToLongs, BinaryQuantizer.java:207-232).
+__global__ void bq_pack_kernel(const float* __restrict__ q, int nq, int dim, int nw_pad,
+                               uint64_t* __restrict__ out) {
+  int qi = blockIdx.x;
+  for (int w = threadIdx.x; w < nw_pad; w += blockDim.x) {
+    uint64_t word = 0;
+    for (int b = 0; b < 64; b++) {
+      int d = w * 64 + b;
+      if (d < dim && q[(size_t)qi * dim + d] >= 0.0f) word |= 1ull << b;
+    }
+    out[(size_t)qi * nw_pad + w] = word;
+  }
+}
+
+}  // namespace
+
+int bq_padded_words(int nw) {
+  for (int p : {2, 4, 8, 16, 32})
+    if (nw <= p) return p;
+  return -1;
+}
+
+int bq_parts(int64_t n, int num_sms) {
+  int64_t p = (int64_t)num_sms * 2;
+  int64_t max_parts = (n + kBqTile - 1) / kBqTile;
+  if (p > max_parts) p = max_parts;
+  return (int)(p < 1 ? 1 : p);
+}
+
+cudaError_t launch_bq_scan(const uint64_t* db, int64_t n, int nw_pad, const uint64_t* qw, int nq,
+                           int parts, const StreamGeom& g, uint64_t* bufs, uint32_t* cnts,
+                           uint64_t* thrs, cudaStream_t st) {
+  switch (nw_pad) {
+    case 2: return launch_nw<2>(db, n, qw, nq, parts, g, bufs, cnts, thrs, st);
+    case 4: return launch_nw<4>(db, n, qw, nq, parts, g, bufs, cnts, thrs, st);
+    case 8: return launch_nw<8>(db, n, qw, nq, parts, g, bufs, cnts, thrs, st);
+    case 16: return launch_nw<16>(db, n, qw, nq, parts, g, bufs, cnts, thrs, st);
+    case 32: return launch_nw<32>(db, n, qw, nq, parts, g, bufs, cnts, thrs, st);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+cudaError_t launch_bq_pack_queries(const float* q, int nq, int dim, int nw_pad, uint64_t* out,
+                                   cudaStream_t st) {
+  if (nq <= 0) return cudaSuccess;
+  bq_pack_kernel<<<nq, 32, 0, st>>>(q, nq, dim, nw_pad, out);
+  return cudaGetLastError();
+}
+
+StreamGeom stream_geom(int K, int slack) {
+  StreamGeom g;
+  g.K = K;
+  int need = (K + slack + 1 + 31) / 32;
+  int R = -1;
+  for (int r : {2, 3, 5, 9, 17, 33})
+    if (r >= need) {
+      R = r;
+      break;
+    }
+  g.R = R;
+  g.C = R > 0 ? 32 * R : 0;
+  return g;
+}
+
+}  // namespace vx

@@ -1,0 +1,421 @@
+// ivfpq.cu -- IVF-PQ search: coarse routing, (query, list) grouping and the ADC list scan.
+//
+// Restates IvfIndex.pqSearch (vectors-ivf/.../IvfIndex.java:539-619):
+//   route:  CentroidIndex.routeWithSpillDistances with gamma = 0 (CentroidIndex.java:89-211),
+//           distances from VectorUtil.batchSquaredL2 / batchDotProduct
+//           (PanamaVectorUtilSupport.java:5353-5397, 5547-5598), evaluated here in the same
+//           lane order; the nprobe nearest lists by (distance asc, list id asc), which is the
+//           set the reference's bounded max-heap keeps (it admits only d < root).
+//   table:  ProductQuantizer.buildADCTable (ProductQuantizer.java:521-544) of the residual
+//           q - c_list (EUCLIDEAN) or of q (dot metrics); for sub-vectors of <= 16 floats the
+//           reference takes the scalar tail: res += diff * diff, two roundings, in order.
+//   scan:   sum = table[0][code[0]] + table[1][code[1]] + ... sequentially in fp32
+//           (IvfIndex.java:581-588); score = -sum (EUCLIDEAN) or q.c + sum.
+// Everything on this path is fixed by the Java source, so scores are bit-identical.
+//
+// Work decomposition.  The nq * nprobe (query, list) pairs are bucketed by list so that
+// consecutive CTAs scan the same list (its codes stay in L2).  A CTA builds one pair's
+// 96 x 256 fp32 table in shared memory, then its 8 warps stream the list's codes (lane = row)
+// through table gathers into warp-owned candidate buffers; the CTA writes the pair's best
+// K keys and a final per-query merge combines the nprobe lists.
+#include "common.cuh"
+#include "exact.cuh"
+#include "ivfpq.h"
+#include "select.cuh"
+
+namespace vx {
+
+namespace {
+
+constexpr int kQG = 8;  // queries per routing block
+
+__device__ __forceinline__ float reduce_add8_local(const float* l) {
+  float even = __fadd_rn(__fadd_rn(l[4], l[0]), __fadd_rn(l[6], l[2]));
+  float odd = __fadd_rn(__fadd_rn(l[5], l[1]), __fadd_rn(l[7], l[3]));
+  return __fadd_rn(even, odd);
+}
+
+// Serial restatements (one thread) of squareDistance / dotProduct over sub-vectors
+// (PanamaVectorUtilSupport.java:208-343).
+__device__ float serial_sqdist(const float* a, const float* b, int len) {
+  float res = 0.0f;
+  int i = 0;
+  if (len > 16) {
+    const int limit = len & ~7;
+    float acc[4][8];
+#pragma unroll
+    for (int u = 0; u < 4; u++)
+#pragma unroll
+      for (int j = 0; j < 8; j++) acc[u][j] = 0.0f;
+    int p = 0;
+    for (; p < limit - 24; p += 32)
+      for (int u = 0; u < 4; u++)
+        for (int j = 0; j < 8; j++) {
+          float d = __fsub_rn(a[p + 8 * u + j], b[p + 8 * u + j]);
+          acc[u][j] = __fmaf_rn(d, d, acc[u][j]);
+        }
+    for (; p < limit; p += 8)
+      for (int j = 0; j < 8; j++) {
+        float d = __fsub_rn(a[p + j], b[p + j]);
+        acc[0][j] = __fmaf_rn(d, d, acc[0][j]);
+      }
+    float s[8];
+    for (int j = 0; j < 8; j++) s[j] = __fadd_rn(__fadd_rn(acc[0][j], acc[1][j]), __fadd_rn(acc[2][j], acc[3][j]));
+    res = __fadd_rn(res, reduce_add8_local(s));
+    i = limit;
+  }
+  for (; i < len; i++) {
+    float d = __fsub_rn(a[i], b[i]);
+    res = __fadd_rn(res, __fmul_rn(d, d));
+  }
+  return res;
+}
+__device__ float serial_dot(const float* a, const float* b, int len) {
+  float res = 0.0f;
+  int i = 0;
+  if (len > 16) {
+    const int limit = len & ~7;
+    float acc[4][8];
+#pragma unroll
+    for (int u = 0; u < 4; u++)
+#pragma unroll
+      for (int j = 0; j < 8; j++) acc[u][j] = 0.0f;
+    int p = 0;
+    for (; p < limit - 24; p += 32)
+      for (int u = 0; u < 4; u++)
+        for (int j = 0; j < 8; j++) acc[u][j] = __fmaf_rn(a[p + 8 * u + j], b[p + 8 * u + j], acc[u][j]);
+    for (; p < limit; p += 8)
+      for (int j = 0; j < 8; j++) acc[0][j] = __fmaf_rn(a[p + j], b[p + j], acc[0][j]);
+    float s[8];
+    for (int j = 0; j < 8; j++) s[j] = __fadd_rn(__fadd_rn(acc[0][j], acc[1][j]), __fadd_rn(acc[2][j], acc[3][j]));
+    res = __fadd_rn(res, reduce_add8_local(s));
+    i = limit;
+  }
+  for (; i < len; i++) res = __fmaf_rn(a[i], b[i], res);
+  return res;
+}
+
+// Distances from kQG queries to every centroid; one thread per centroid row.
+// EUCLIDEAN: matVecSquaredL2; otherwise -matVecDot (queries already normalised for COSINE).
+__global__ void __launch_bounds__(256) route_dist_kernel(const float* __restrict__ queries, int nq,
+                                                         int dim, const float* __restrict__ cent,
+                                                         int nlist, int metric,
+                                                         float* __restrict__ dist) {
+  extern __shared__ float s_q[];  // [kQG][dim]
+  const int q0 = blockIdx.x * kQG;
+  const int nqg = min(kQG, nq - q0);
+  for (int i = threadIdx.x; i < kQG * dim; i += blockDim.x) {
+    const int g = i / dim;
+    s_q[i] = g < nqg ? queries[(size_t)(q0 + g) * dim + (i % dim)] : 0.0f;
+  }
+  __syncthreads();
+  const int group = nlist & ~3;
+  const int limit = dim & ~7;
+  const bool l2 = metric == kEuclidean;
+  for (int c = threadIdx.x; c < nlist; c += blockDim.x) {
+    const float* row = cent + (size_t)c * dim;
+    if (c < group) {
+      float acc[kQG][8];
+#pragma unroll
+      for (int g = 0; g < kQG; g++)
+#pragma unroll
+        for (int j = 0; j < 8; j++) acc[g][j] = 0.0f;
+      for (int i = 0; i < limit; i += 8) {
+        float r[8];
+        if ((dim & 3) == 0) {
+          const float4 r0 = *reinterpret_cast<const float4*>(row + i);
+          const float4 r1 = *reinterpret_cast<const float4*>(row + i + 4);
+          r[0] = r0.x; r[1] = r0.y; r[2] = r0.z; r[3] = r0.w;
+          r[4] = r1.x; r[5] = r1.y; r[6] = r1.z; r[7] = r1.w;
+        } else {
+#pragma unroll
+          for (int j = 0; j < 8; j++) r[j] = row[i + j];
+        }
+#pragma unroll
+        for (int g = 0; g < kQG; g++)
+#pragma unroll
+          for (int j = 0; j < 8; j++) {
+            const float qv = s_q[g * dim + i + j];
+            if (l2) {
+              const float d = __fsub_rn(qv, r[j]);
+              acc[g][j] = __fmaf_rn(d, d, acc[g][j]);
+            } else {
+              acc[g][j] = __fmaf_rn(qv, r[j], acc[g][j]);
+            }
+          }
+      }
+#pragma unroll
+      for (int g = 0; g < kQG; g++) {
+        float s = reduce_add8_local(acc[g]);
+        for (int i = limit; i < dim; i++) {
+          const float qv = s_q[g * dim + i];
+          if (l2) {
+            const float e = __fsub_rn(qv, row[i]);
+            s = __fmaf_rn(e, e, s);
+          } else {
+            s = __fmaf_rn(qv, row[i], s);
+          }
+        }
+        if (g < nqg) dist[(size_t)(q0 + g) * nlist + c] = l2 ? s : -s;
+      }
+    } else {
+      for (int g = 0; g < nqg; g++) {
+        const float s = l2 ? serial_sqdist(s_q + g * dim, row, dim) : serial_dot(s_q + g * dim, row, dim);
+        dist[(size_t)(q0 + g) * nlist + c] = l2 ? s : -s;
+      }
+    }
+  }
+}
+
+// COSINE routing normalises a copy of the query first: l2normalize
+// (PanamaVectorUtilSupport.java:5178-5194).  One warp per query.
+__global__ void l2normalize_kernel(const float* __restrict__ src, int nq, int dim,
+                                   float* __restrict__ dst) {
+  const int lane = threadIdx.x & 31;
+  const int q = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  if (q >= nq) return;
+  const float* v = src + (size_t)q * dim;
+  float* o = dst + (size_t)q * dim;
+  const float dotf = warp_dot(RowF32{v}, RowF32{v}, dim);
+  const double sq = (double)dotf;
+  float inv = 1.0f;
+  bool scale = !(sq == 0.0) && !(fabsf(__fsub_rn((float)sq, 1.0f)) < 1e-5f);
+  if (scale) inv = __fdiv_rn(1.0f, __double2float_rn(__dsqrt_rn(sq)));
+  for (int i = lane; i < dim; i += 32) o[i] = scale ? __fmul_rn(v[i], inv) : v[i];
+}
+
+// nprobe nearest lists per query, ascending distance (ties: lower list id).
+__global__ void __launch_bounds__(256) route_select_kernel(const float* __restrict__ dist, int nlist,
+                                                           int nprobe, int32_t* __restrict__ lists) {
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  const int q = blockIdx.x;
+  uint32_t cap = 1;
+  while (cap < (uint32_t)nlist) cap <<= 1;
+  uint64_t* s_keys = (uint64_t*)smem_raw;
+  uint64_t* s_tmp = s_keys + cap;
+  uint32_t* s_red = (uint32_t*)(s_tmp + cap);
+  uint32_t* s_counter = s_red + 32;
+  for (int c = threadIdx.x; c < nlist; c += blockDim.x)
+    s_keys[c] = make_key(~float_order_bits(dist[(size_t)q * nlist + c]), (uint32_t)c);
+  __syncthreads();
+  uint32_t n = block_keep_top(s_keys, (uint32_t)nlist, (uint32_t)nprobe, s_tmp, s_red, s_counter);
+  block_sort_desc(s_keys, n, cap);
+  for (int i = threadIdx.x; i < nprobe; i += blockDim.x)
+    lists[(size_t)q * nprobe + i] = (uint32_t)i < n ? (int32_t)key_id(s_keys[i]) : -1;
+}
+
+__global__ void pair_hist_kernel(const int32_t* __restrict__ lists, int npairs,
+                                 int32_t* __restrict__ counts) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < npairs && lists[i] >= 0) atomicAdd(&counts[lists[i]], 1);
+}
+
+// Exclusive scan of nlist counts (single block), also resets the scatter cursors.
+__global__ void pair_scan_kernel(const int32_t* __restrict__ counts, int nlist,
+                                 int32_t* __restrict__ offsets, int32_t* __restrict__ cursor) {
+  __shared__ int32_t s_part[1024];
+  const int per = (nlist + blockDim.x - 1) / blockDim.x;
+  const int b = threadIdx.x * per;
+  int32_t sum = 0;
+  for (int i = b; i < b + per && i < nlist; i++) sum += counts[i];
+  s_part[threadIdx.x] = sum;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int32_t run = 0;
+    for (int t = 0; t < (int)blockDim.x; t++) {
+      int32_t v = s_part[t];
+      s_part[t] = run;
+      run += v;
+    }
+  }
+  __syncthreads();
+  int32_t run = s_part[threadIdx.x];
+  for (int i = b; i < b + per && i < nlist; i++) {
+    offsets[i] = run;
+    cursor[i] = run;
+    run += counts[i];
+  }
+  if (threadIdx.x == blockDim.x - 1) offsets[nlist] = run;
+}
+
+__global__ void pair_scatter_kernel(const int32_t* __restrict__ lists, int npairs,
+                                    int32_t* __restrict__ cursor, int32_t* __restrict__ pairs) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < npairs && lists[i] >= 0) pairs[atomicAdd(&cursor[lists[i]], 1)] = i;
+}
+
+// Warp-owned candidate buffer in shared memory: all 32 lanes offer one key each.
+template <int R>
+struct WarpStream {
+  uint64_t* buf;
+  uint32_t cnt;
+  uint64_t thr;
+  __device__ __forceinline__ void offer32(uint64_t key, bool valid, int C, int K) {
+    const int lane = threadIdx.x & 31;
+    const bool pass = valid && key > thr;
+    const unsigned m = __ballot_sync(0xFFFFFFFFu, pass);
+    if (pass) buf[cnt + __popc(m & ((1u << lane) - 1u))] = key;
+    cnt += __popc(m);
+    if (cnt > (uint32_t)(C - 32)) {
+      __syncwarp();
+      warp_compact_one<R>(buf, cnt, (uint32_t)K, thr, cnt);
+      __syncwarp();
+    }
+  }
+};
+
+template <int R>
+__global__ void __launch_bounds__(256) adc_scan_kernel(AdcArgs a) {
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nwarps = blockDim.x >> 5;
+  const int C = 32 * R;
+  float* s_lut = (float*)smem_raw;                            // [M][Ks]
+  float* s_res = s_lut + (size_t)a.M * a.Ks;                  // [dim]
+  uint64_t* s_wbuf = (uint64_t*)(((uintptr_t)(s_res + a.dim) + 15) & ~(uintptr_t)15);  // [nwarps][C]
+  uint64_t* s_merge = s_wbuf + (size_t)nwarps * C;            // [2][mcap]
+  const uint32_t mcap = (uint32_t)(nwarps * a.K);
+  uint32_t* s_red = (uint32_t*)(s_merge + 2 * (size_t)mcap);
+  uint32_t* s_counter = s_red + 32;
+  __shared__ float s_base;
+
+  for (int64_t w = blockIdx.x; w < a.npairs; w += gridDim.x) {
+    const int32_t pair = a.pairs[w];
+    const int q = pair / a.nprobe;
+    const int p = pair % a.nprobe;
+    const int l = a.lists[pair];
+    const float* qv = a.queries + (size_t)q * a.dim;
+    const float* c = a.cent + (size_t)l * a.dim;
+    const bool l2 = a.metric == kEuclidean;
+    __syncthreads();  // previous pair fully consumed the shared buffers
+    for (int i = threadIdx.x; i < a.dim; i += blockDim.x) s_res[i] = l2 ? __fsub_rn(qv[i], c[i]) : qv[i];
+    if (warp == 0) {
+      float base = 0.0f;
+      if (!l2 && a.metric != kCosine) base = warp_dot(RowF32{qv}, RowF32{c}, a.dim);
+      if (lane == 0) s_base = base;
+    }
+    __syncthreads();
+    const int entries = a.M * a.Ks;
+    for (int e = threadIdx.x; e < entries; e += blockDim.x) {
+      const int m = e / a.Ks, cc = e - m * a.Ks;
+      const int sub = a.sub[2 * m], off = a.sub[2 * m + 1];
+      const float* cb = a.codebooks + a.cb_off[m] + (size_t)cc * sub;
+      s_lut[e] = l2 ? serial_sqdist(s_res + off, cb, sub) : serial_dot(s_res + off, cb, sub);
+    }
+    __syncthreads();
+    const float base = s_base;
+    WarpStream<R> ws{s_wbuf + (size_t)warp * C, 0u, 0ull};
+    const int64_t b = a.list_off[l], e = a.list_off[l + 1];
+    for (int64_t r0 = b + (int64_t)warp * 32; r0 < e; r0 += (int64_t)nwarps * 32) {
+      const int64_t r = r0 + lane;
+      const bool valid = r < e;
+      uint64_t key = 0;
+      if (valid) {
+        const uint8_t* code = a.codes + r * (int64_t)a.Mp;
+        float sum = 0.0f;
+        int m = 0;
+        for (; m + 16 <= a.M; m += 16) {
+          const uint4 v = *reinterpret_cast<const uint4*>(code + m);
+          const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+          for (int t = 0; t < 16; t++) {
+            const uint32_t cv = (w4[t >> 2] >> (8 * (t & 3))) & 0xFFu;
+            sum = __fadd_rn(sum, s_lut[(m + t) * a.Ks + cv]);
+          }
+        }
+        for (; m < a.M; m++) sum = __fadd_rn(sum, s_lut[m * a.Ks + code[m]]);
+        const float score = l2 ? -sum : __fadd_rn(base, sum);
+        key = float_key(score, (uint32_t)a.ordinals[r]);
+      }
+      ws.offer32(key, valid, C, a.K);
+    }
+    // Shrink each warp's buffer to K and gather all warps' survivors.
+    __syncwarp();
+    if (ws.cnt > (uint32_t)a.K) warp_compact_one<R>(ws.buf, ws.cnt, (uint32_t)a.K, ws.thr, ws.cnt);
+    __syncwarp();
+    if (lane == 0) s_red[warp] = ws.cnt;
+    __syncthreads();
+    uint32_t at = 0;
+    for (int i = 0; i < warp; i++) at += s_red[i];
+    uint32_t total = 0;
+    for (int i = 0; i < nwarps; i++) total += s_red[i];
+    for (uint32_t i = lane; i < ws.cnt; i += 32) s_merge[at + i] = ws.buf[i];
+    __syncthreads();
+    const uint32_t n = block_keep_top(s_merge, total, (uint32_t)a.K, s_merge + mcap, s_red, s_counter);
+    const size_t sidx = (size_t)p * a.nq + q;
+    for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) a.out[sidx * a.K + i] = s_merge[i];
+    if (threadIdx.x == 0) a.out_cnt[sidx] = n;
+  }
+}
+
+}  // namespace
+
+cudaError_t launch_route(const float* queries, int nq, int dim, const float* cent, int nlist,
+                         int metric, int nprobe, float* qnorm_scratch, float* dist,
+                         int32_t* lists, cudaStream_t st) {
+  if (nq <= 0) return cudaSuccess;
+  const float* qsrc = queries;
+  if (metric == kCosine) {
+    l2normalize_kernel<<<(nq * 32 + 255) / 256, 256, 0, st>>>(queries, nq, dim, qnorm_scratch);
+    qsrc = qnorm_scratch;
+  }
+  const size_t smem = (size_t)kQG * dim * sizeof(float);
+  cudaError_t e = cudaFuncSetAttribute(route_dist_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)smem);
+  if (e != cudaSuccess) return e;
+  route_dist_kernel<<<(nq + kQG - 1) / kQG, 256, smem, st>>>(qsrc, nq, dim, cent, nlist, metric, dist);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  uint32_t cap = 1;
+  while (cap < (uint32_t)nlist) cap <<= 1;
+  const size_t smem2 = (size_t)cap * 16 + 33 * 4 + 16;
+  e = cudaFuncSetAttribute(route_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem2);
+  if (e != cudaSuccess) return e;
+  route_select_kernel<<<nq, 256, smem2, st>>>(dist, nlist, nprobe, lists);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_group_pairs(const int32_t* lists, int npairs, int nlist, int32_t* counts,
+                               int32_t* offsets, int32_t* cursor, int32_t* pairs, cudaStream_t st) {
+  cudaError_t e = cudaMemsetAsync(counts, 0, sizeof(int32_t) * nlist, st);
+  if (e != cudaSuccess) return e;
+  if (npairs <= 0) return cudaSuccess;
+  pair_hist_kernel<<<(npairs + 255) / 256, 256, 0, st>>>(lists, npairs, counts);
+  pair_scan_kernel<<<1, 1024, 0, st>>>(counts, nlist, offsets, cursor);
+  pair_scatter_kernel<<<(npairs + 255) / 256, 256, 0, st>>>(lists, npairs, cursor, pairs);
+  return cudaGetLastError();
+}
+
+size_t adc_smem(int M, int Ks, int dim, int R, int K) {
+  const int nwarps = 8;
+  size_t s = (size_t)M * Ks * 4 + (size_t)dim * 4 + 16;
+  s += (size_t)nwarps * 32 * R * 8;
+  s += 2ull * nwarps * K * 8;
+  s += 33 * 4 + 16;
+  return s;
+}
+
+cudaError_t launch_adc_scan(const AdcArgs& a, int R, int grid, cudaStream_t st) {
+  if (a.npairs <= 0) return cudaSuccess;
+  const size_t smem = adc_smem(a.M, a.Ks, a.dim, R, a.K);
+#define VX_ADC_CASE(RR)                                                                          \
+  case RR: {                                                                                     \
+    cudaError_t e = cudaFuncSetAttribute(adc_scan_kernel<RR>,                                    \
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); \
+    if (e != cudaSuccess) return e;                                                              \
+    adc_scan_kernel<RR><<<grid, 256, smem, st>>>(a);                                             \
+    return cudaGetLastError();                                                                   \
+  }
+  switch (R) {
+    VX_ADC_CASE(2)
+    VX_ADC_CASE(3)
+    VX_ADC_CASE(5)
+    VX_ADC_CASE(9)
+    VX_ADC_CASE(17)
+    VX_ADC_CASE(33)
+    default: return cudaErrorInvalidValue;
+  }
+#undef VX_ADC_CASE
+}
+
+}  // namespace vx

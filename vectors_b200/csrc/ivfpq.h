@@ -1,0 +1,35 @@
+// ivfpq.h -- IVF-PQ routing and ADC scan (ivfpq.cu).
+#pragma once
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace vx {
+
+struct AdcArgs {
+  int nq, dim, nprobe, metric;
+  int M, Ks, Mp;                 // subspaces, centroids per subspace, padded code bytes per row
+  int K;                         // keys kept per (query, list)
+  int64_t npairs;
+  const int32_t* pairs;          // pair indices (q * nprobe + p), grouped by list
+  const int32_t* lists;          // [nq][nprobe] routed list ids
+  const float* queries;          // [nq][dim]
+  const float* cent;             // [nlist][dim]
+  const int64_t* list_off;       // [nlist + 1] CSR offsets into codes / ordinals
+  const int32_t* ordinals;       // [n] ordinal of each list-ordered row
+  const uint8_t* codes;          // [n][Mp] list-ordered PQ codes
+  const float* codebooks;        // concatenated, subspace m at cb_off[m]
+  const int64_t* cb_off;         // [M]
+  const int32_t* sub;            // [M][2] size, offset
+  uint64_t* out;                 // [nprobe][nq][K]
+  uint32_t* out_cnt;             // [nprobe][nq]
+};
+
+cudaError_t launch_route(const float* queries, int nq, int dim, const float* cent, int nlist,
+                         int metric, int nprobe, float* qnorm_scratch, float* dist,
+                         int32_t* lists, cudaStream_t st);
+cudaError_t launch_group_pairs(const int32_t* lists, int npairs, int nlist, int32_t* counts,
+                               int32_t* offsets, int32_t* cursor, int32_t* pairs, cudaStream_t st);
+size_t adc_smem(int M, int Ks, int dim, int R, int K);
+cudaError_t launch_adc_scan(const AdcArgs& a, int R, int grid, cudaStream_t st);
+
+}  // namespace vx

@@ -1,0 +1,76 @@
+// kernels.h -- launch entry points of the scan kernels (internal to libvx.so).
+#pragma once
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace vx {
+
+// SimilarityFunction ordinals (vectors-core/.../SimilarityFunction.java:30-120).
+enum Metric : int { kEuclidean = 0, kDotProduct = 1, kCosine = 2, kMaxInnerProduct = 3 };
+
+enum FinishKind : int { kFinishFloatKey = 0, kFinishHamming = 1 };
+
+// Which reference score an exact re-score reproduces (exact.cuh).
+enum ScoreFlavor : int { kFlavorFlat = 0, kFlavorFp16Quantized = 1, kFlavorIvfRaw = 2 };
+
+// SimilarityFunction.scaleMaxInnerProductScore (SimilarityFunction.java:155-161).
+__host__ __device__ __forceinline__ float scale_mip(float dot) {
+#ifdef __CUDA_ARCH__
+  return dot >= 0.0f ? __fadd_rn(dot, 1.0f) : __fdiv_rn(1.0f, __fsub_rn(1.0f, dot));
+#else
+  return dot >= 0.0f ? dot + 1.0f : 1.0f / (1.0f - dot);
+#endif
+}
+
+// BinaryQuantizedVectors.signBitScoreFunction (BinaryQuantizedVectors.java:88-106).
+__host__ __device__ __forceinline__ float bq_score_device(int metric, int h, int dim) {
+#ifdef __CUDA_ARCH__
+  switch (metric) {
+    case kEuclidean: return __fdiv_rn(1.0f, __fadd_rn(1.0f, __fmul_rn(4.0f, (float)h)));
+    case kMaxInnerProduct: return scale_mip(__fdiv_rn((float)(dim - 2 * h), (float)dim));
+    default: return __fsub_rn(1.0f, __fdiv_rn((float)h, (float)dim));
+  }
+#else
+  switch (metric) {
+    case kEuclidean: return 1.0f / (1.0f + 4.0f * (float)h);
+    case kMaxInnerProduct: return scale_mip((float)(dim - 2 * h) / (float)dim);
+    default: return 1.0f - (float)h / (float)dim;
+  }
+#endif
+}
+
+// Candidate-stream geometry shared by the scan kernels: a stream keeps up to K keys in a
+// buffer of C = 32*R slots; at most `slack` keys are appended between two compaction checks.
+struct StreamGeom {
+  int K;      // keys each stream must keep
+  int R;      // registers per lane used by the warp compaction (C = 32 * R)
+  int C;      // buffer slots per stream
+};
+StreamGeom stream_geom(int K, int slack);
+
+// ---- merge.cu
+cudaError_t launch_merge_streams(const uint64_t* bufs, const uint32_t* cnts, int S, int nq,
+                                 int stride, int C, int K, uint64_t* out_keys, uint32_t* out_cnt,
+                                 cudaStream_t st);
+cudaError_t launch_ids_to_keys(const int32_t* ids, const int32_t* cnt, int nq, int K, uint64_t* keys,
+                               cudaStream_t st);
+cudaError_t launch_min_score(const float* scores, int nq, int k, float min_score, int32_t* counts,
+                             cudaStream_t st);
+cudaError_t launch_finish_keys(const uint64_t* keys, const uint32_t* cnt, int nq, int K, int k_out,
+                               int kind, int metric, int dim, int32_t* ids, float* scores,
+                               int32_t* counts, cudaStream_t st);
+cudaError_t launch_merge_shards(int nshards, const int64_t* offsets, const int32_t* sids,
+                                const float* ssc, const int32_t* scnt, int kin, int nq, int k,
+                                int32_t* ids, float* scores, int32_t* counts, cudaStream_t st);
+
+// ---- bq_scan.cu : sign-bit Hamming scan (BinaryQuantizedVectors.java:81-107)
+// db: [n][nw_pad] 64-bit words; qw: [nq][nw_pad]; writes S = parts streams per query.
+int bq_padded_words(int nw);
+int bq_parts(int64_t n, int num_sms);
+cudaError_t launch_bq_scan(const uint64_t* db, int64_t n, int nw_pad, const uint64_t* qw, int nq,
+                           int parts, const StreamGeom& g, uint64_t* bufs, uint32_t* cnts,
+                           uint64_t* thrs, cudaStream_t st);
+cudaError_t launch_bq_pack_queries(const float* q, int nq, int dim, int nw_pad, uint64_t* out,
+                                   cudaStream_t st);
+
+}  // namespace vx

@@ -1,0 +1,190 @@
+// merge.cu -- per-query merge of candidate streams, key -> (id, score) finishing, and the
+// cross-shard merge (IndexShards.mergeWithOffsets, vectors-db/.../index/IndexShards.java:168-211).
+#include "kernels.h"
+#include "select.cuh"
+
+namespace vx {
+
+// Each block merges the candidate streams of one query into its K best keys, sorted
+// descending.  Stream s of query q holds cnts[s*nq+q] keys at bufs + ((s*nq)+q)*C, where nq
+// is the stream stride (queries beyond the grid are padding and are not merged).
+__global__ void __launch_bounds__(256) merge_streams_kernel(const uint64_t* __restrict__ bufs,
+                                                            const uint32_t* __restrict__ cnts,
+                                                            int S, int nq, int C, int K,
+                                                            uint64_t* __restrict__ out_keys,
+                                                            uint32_t* __restrict__ out_cnt) {
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  const int q = blockIdx.x;
+  const uint32_t cap = (uint32_t)K + (uint32_t)(C > 4096 ? C : 4096);
+  uint64_t* s_keys = (uint64_t*)smem_raw;
+  uint64_t* s_tmp = s_keys + cap;
+  uint32_t* s_red = (uint32_t*)(s_tmp + cap);
+  uint32_t* s_counter = s_red + 32;
+  uint32_t n = 0;
+  for (int s = 0; s < S; s++) {
+    uint32_t c = cnts[(size_t)s * nq + q];
+    if (c == 0) continue;
+    if (n + c > cap) {
+      n = block_keep_top(s_keys, n, (uint32_t)K, s_tmp, s_red, s_counter);
+    }
+    const uint64_t* src = bufs + ((size_t)s * nq + q) * (size_t)C;
+    for (uint32_t i = threadIdx.x; i < c; i += blockDim.x) s_keys[n + i] = src[i];
+    n += c;
+    __syncthreads();
+  }
+  n = block_keep_top(s_keys, n, (uint32_t)K, s_tmp, s_red, s_counter);
+  block_sort_desc(s_keys, n, cap);
+  for (uint32_t i = threadIdx.x; i < (uint32_t)K; i += blockDim.x)
+    out_keys[(size_t)q * K + i] = (i < n) ? s_keys[i] : kEmptyKey;
+  if (threadIdx.x == 0) out_cnt[q] = n;
+}
+
+size_t merge_streams_smem(int C, int K) {
+  size_t cap = (size_t)K + (size_t)(C > 4096 ? C : 4096);
+  return cap * 16 + 33 * 4 + 16;
+}
+
+cudaError_t launch_merge_streams(const uint64_t* bufs, const uint32_t* cnts, int S, int nq,
+                                 int stride, int C, int K, uint64_t* out_keys, uint32_t* out_cnt,
+                                 cudaStream_t st) {
+  if (nq <= 0) return cudaSuccess;
+  size_t smem = merge_streams_smem(C, K);
+  cudaError_t e = cudaFuncSetAttribute(merge_streams_kernel,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  merge_streams_kernel<<<nq, 256, smem, st>>>(bufs, cnts, S, stride, C, K, out_keys, out_cnt);
+  return cudaGetLastError();
+}
+
+// Converts sorted keys to the reference's (ordinal, score) output.  kind selects how the
+// score is recovered: the key's float bits (exact scores), or a Hamming distance mapped
+// through BinaryQuantizedVectors.signBitScoreFunction (BinaryQuantizedVectors.java:88-106).
+__global__ void finish_keys_kernel(const uint64_t* __restrict__ keys, const uint32_t* __restrict__ cnt,
+                                   int nq, int K, int k_out, int kind, int metric, int dim,
+                                   int32_t* __restrict__ ids, float* __restrict__ scores,
+                                   int32_t* __restrict__ counts) {
+  int q = blockIdx.x;
+  int c = (int)cnt[q];
+  if (c > k_out) c = k_out;
+  __syncthreads();
+  for (int i = threadIdx.x; i < k_out; i += blockDim.x) {
+    if (i < c) {
+      uint64_t key = keys[(size_t)q * K + i];
+      ids[(size_t)q * k_out + i] = (int32_t)key_id(key);
+      float s;
+      if (kind == kFinishHamming) {
+        uint32_t h = 0xFFFFFFFFu - key_hi(key);
+        s = bq_score_device(metric, (int)h, dim);
+      } else {
+        s = key_score(key);
+      }
+      scores[(size_t)q * k_out + i] = s;
+    } else {
+      ids[(size_t)q * k_out + i] = -1;
+      scores[(size_t)q * k_out + i] = 0.0f;
+    }
+  }
+  if (threadIdx.x == 0) counts[q] = c;
+}
+
+// Drops the trailing hits scoring below min_score (results are sorted descending), as
+// IvfIndex.pqSearch does with IvfSearchRequest.minScore (IvfIndex.java:592-616).
+__global__ void min_score_kernel(const float* __restrict__ scores, int nq, int k, float min_score,
+                                 int32_t* __restrict__ counts) {
+  const int q = blockIdx.x * blockDim.x + threadIdx.x;
+  if (q >= nq) return;
+  int c = counts[q];
+  while (c > 0 && scores[(size_t)q * k + c - 1] < min_score) c--;
+  counts[q] = c;
+}
+
+cudaError_t launch_min_score(const float* scores, int nq, int k, float min_score, int32_t* counts,
+                             cudaStream_t st) {
+  if (nq <= 0) return cudaSuccess;
+  min_score_kernel<<<(nq + 127) / 128, 128, 0, st>>>(scores, nq, k, min_score, counts);
+  return cudaGetLastError();
+}
+
+// Packs (ordinal, score) outputs into keys (counts may be < K).
+__global__ void ids_to_keys_kernel(const int32_t* __restrict__ ids, const int32_t* __restrict__ cnt,
+                                   int nq, int K, uint64_t* __restrict__ keys) {
+  const int q = blockIdx.x;
+  for (int i = threadIdx.x; i < K; i += blockDim.x)
+    keys[(size_t)q * K + i] = i < cnt[q] ? make_key(0u, (uint32_t)ids[(size_t)q * K + i]) : kEmptyKey;
+}
+
+cudaError_t launch_ids_to_keys(const int32_t* ids, const int32_t* cnt, int nq, int K, uint64_t* keys,
+                               cudaStream_t st) {
+  if (nq <= 0) return cudaSuccess;
+  ids_to_keys_kernel<<<nq, 128, 0, st>>>(ids, cnt, nq, K, keys);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_finish_keys(const uint64_t* keys, const uint32_t* cnt, int nq, int K, int k_out,
+                               int kind, int metric, int dim, int32_t* ids, float* scores,
+                               int32_t* counts, cudaStream_t st) {
+  if (nq <= 0) return cudaSuccess;
+  finish_keys_kernel<<<nq, 128, 0, st>>>(keys, cnt, nq, K, k_out, kind, metric, dim, ids, scores,
+                                         counts);
+  return cudaGetLastError();
+}
+
+// Cross-shard merge: shard s contributes shard_counts[s*nq+q] (ordinal, score) pairs for
+// query q at [(s*nq+q)*kin]; ordinals are shifted by offsets[s].  Output: the k best by
+// (score desc, ordinal asc), the canonical order of TopK.select.
+__global__ void __launch_bounds__(256) merge_shards_kernel(
+    int nshards, const int64_t* __restrict__ offsets, const int32_t* __restrict__ sids,
+    const float* __restrict__ ssc, const int32_t* __restrict__ scnt, int kin, int nq, int k,
+    uint32_t total_cap, int32_t* __restrict__ ids, float* __restrict__ scores,
+    int32_t* __restrict__ counts) {
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  const int q = blockIdx.x;
+  uint64_t* s_keys = (uint64_t*)smem_raw;
+  uint64_t* s_tmp = s_keys + total_cap;
+  uint32_t* s_red = (uint32_t*)(s_tmp + total_cap);
+  uint32_t* s_counter = s_red + 32;
+  if (threadIdx.x == 0) *s_counter = 0;
+  __syncthreads();
+  for (int s = 0; s < nshards; s++) {
+    int c = scnt[(size_t)s * nq + q];
+    for (int i = threadIdx.x; i < c; i += blockDim.x) {
+      size_t at = ((size_t)s * nq + q) * kin + i;
+      uint32_t id = (uint32_t)((int64_t)sids[at] + offsets[s]);
+      s_keys[atomicAdd(s_counter, 1u)] = float_key(ssc[at], id);
+    }
+  }
+  __syncthreads();
+  uint32_t n = *s_counter;
+  __syncthreads();
+  n = block_keep_top(s_keys, n, (uint32_t)k, s_tmp, s_red, s_counter);
+  block_sort_desc(s_keys, n, total_cap);
+  for (int i = threadIdx.x; i < k; i += blockDim.x) {
+    if ((uint32_t)i < n) {
+      ids[(size_t)q * k + i] = (int32_t)key_id(s_keys[i]);
+      scores[(size_t)q * k + i] = key_score(s_keys[i]);
+    } else {
+      ids[(size_t)q * k + i] = -1;
+      scores[(size_t)q * k + i] = 0.0f;
+    }
+  }
+  if (threadIdx.x == 0) counts[q] = (int32_t)n;
+}
+
+cudaError_t launch_merge_shards(int nshards, const int64_t* offsets, const int32_t* sids,
+                                const float* ssc, const int32_t* scnt, int kin, int nq, int k,
+                                int32_t* ids, float* scores, int32_t* counts, cudaStream_t st) {
+  if (nq <= 0) return cudaSuccess;
+  size_t cap = (size_t)nshards * kin;
+  uint32_t p = 1;
+  while (p < cap) p <<= 1;
+  if (p > cap) cap = p;  // bitonic padding room
+  size_t smem = cap * 16 + 33 * 4 + 16;
+  cudaError_t e = cudaFuncSetAttribute(merge_shards_kernel,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  merge_shards_kernel<<<nq, 256, smem, st>>>(nshards, offsets, sids, ssc, scnt, kin, nq, k,
+                                             (uint32_t)cap, ids, scores, counts);
+  return cudaGetLastError();
+}
+
+}  // namespace vx

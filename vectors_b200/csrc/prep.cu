@@ -1,0 +1,226 @@
+// prep.cu -- operand preparation for the scans: fp16 GEMM operands with their norms, the
+// per-query bound on the approximate key error, and the SQ8 query encoder.
+#include <cuda_fp16.h>
+#include "common.cuh"
+#include "prep.h"
+
+namespace vx {
+
+namespace {
+
+__device__ __forceinline__ void atomic_max_pos_float(float* addr, float v) {
+  // non-negative floats order like their bit patterns
+  atomicMax((int*)addr, __float_as_int(v));
+}
+
+// One warp per row: norm in double, then fp16(x / |x|) (or fp16(x) when !unit) into a
+// zero-padded row of Dp halves.
+__global__ void rows_to_f16_kernel(const float* __restrict__ src, int64_t n, int dim,
+                                   int64_t src_stride, int Dp, int unit, __half* __restrict__ dst,
+                                   float* __restrict__ norms, float* __restrict__ norms_sq,
+                                   float* __restrict__ max_norm) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  if (row >= n) return;
+  const float* x = src + row * src_stride;
+  double s = 0.0;
+  for (int i = lane; i < dim; i += 32) s += (double)x[i] * (double)x[i];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xFFFFFFFFu, s, o);
+  const float norm = (float)sqrt(s);
+  const float inv = (unit && norm > 0.0f) ? 1.0f / norm : 1.0f;
+  __half* d = dst + row * (int64_t)Dp;
+  for (int i = lane; i < Dp; i += 32) d[i] = __float2half_rn(i < dim ? x[i] * inv : 0.0f);
+  if (lane == 0) {
+    if (norms) norms[row] = unit ? norm : 1.0f;
+    if (norms_sq) norms_sq[row] = (float)s;
+    if (max_norm) atomic_max_pos_float(max_norm, norm);
+  }
+}
+
+// fp16 rows given in the reference encoding (little-endian binary16, Fp16Quantizer.java:72-85):
+// copy into padded rows and compute norms of the decoded values.
+__global__ void f16_rows_pad_kernel(const __half* __restrict__ src, int64_t n, int dim, int Dp,
+                                    __half* __restrict__ dst, float* __restrict__ norms_sq,
+                                    float* __restrict__ max_norm) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  if (row >= n) return;
+  const __half* x = src + row * (int64_t)dim;
+  double s = 0.0;
+  __half* d = dst + row * (int64_t)Dp;
+  for (int i = lane; i < Dp; i += 32) {
+    __half h = i < dim ? x[i] : __float2half_rn(0.0f);
+    d[i] = h;
+    double v = (double)__half2float(h);
+    s += v * v;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xFFFFFFFFu, s, o);
+  if (lane == 0) {
+    norms_sq[row] = (float)s;
+    atomic_max_pos_float(max_norm, (float)sqrt(s));
+  }
+}
+
+// Bound on |approximate key - exact key| per query (see rescore.cu for the argument).
+// u = 2^-11 is the fp16 unit roundoff; accumulation in the tensor core is bounded by
+// (D+1) 2^-23 of the sum of |products|; the reference's own fp32 rounding by (D+2) 2^-24;
+// the score transform's final rounding by 2^-21 of its magnitude.
+__global__ void margin_kernel(const float* __restrict__ qnorm, int nq, int D, int metric,
+                              int operand_kind, const float* __restrict__ max_norm_ptr,
+                              float* __restrict__ margin) {
+  const int q = blockIdx.x * blockDim.x + threadIdx.x;
+  if (q >= nq) return;
+  const double u = 1.0 / 2048.0;
+  const double xmax = (double)*max_norm_ptr;
+  const double qn = (double)qnorm[q];
+  const double acc = (D + 1) * 0x1.0p-23;
+  const double ref = (D + 2) * 0x1.0p-24;
+  const double sub = sqrt((double)D) * 0x1.0p-24;
+  // relative error of the normalised dot q^.x^ (both operands rounded) or q^.x (rows exact)
+  const double c = (operand_kind == kOperandUnitRows) ? (2 * u + u * u + 0x1.0p-21 + sub + acc)
+                                                      : (u + 0x1.0p-22 + sub + acc);
+  double m;
+  if (metric == 2 /* COSINE */ && operand_kind == kOperandUnitRows) {
+    m = c + ref + 0x1.0p-21;
+  } else if (metric == 0 /* EUCLIDEAN */) {
+    const double big = (qn + xmax) * (qn + xmax);
+    m = 2.0 * qn * xmax * (c + ref) + ref * big + 0x1.0p-21 * (1.0 + big) + 0x1.0p-22 * big;
+  } else {  // DOT_PRODUCT / MAXIMUM_INNER_PRODUCT (and COSINE over fp16-quantized rows)
+    m = (qn > 0.0) ? xmax * (c + ref) + 0x1.0p-21 * (1.0 + qn * xmax) / qn : INFINITY;
+  }
+  if (!(qn > 0.0) && metric != 0) m = INFINITY;
+  margin[q] = (float)(m * 1.0001 + 1e-30);
+}
+
+// SQ8 query encoder: ScalarQuantizer.encodeInt8 / quantizeValue / correctionTerm
+// (ScalarQuantizer.java:243-272), sequential over dimensions, one thread per query, every
+// operation rounded as Java rounds it.  Also returns sum of squared codes for EUCLIDEAN.
+__global__ void sq8_encode_queries_kernel(const float* __restrict__ q, int nq, int dim, int Dp8,
+                                          Sq8Consts k, int8_t* __restrict__ codes,
+                                          float* __restrict__ corr, int32_t* __restrict__ sumsq) {
+  const int qi = blockIdx.x * blockDim.x + threadIdx.x;
+  if (qi >= nq) return;
+  const float* v = q + (size_t)qi * dim;
+  int8_t* out = codes + (size_t)qi * Dp8;
+  float c = 0.0f;
+  int32_t ss = 0;
+  const float half = __fdiv_rn(k.min_q, 2.0f);
+  for (int i = 0; i < dim; i++) {
+    const float x = v[i];
+    // Math.max(minQ, Math.min(maxQ, v)) - minQ
+    float clamped = fminf(k.max_q, x);
+    if (x != x) clamped = x;
+    float lo = fmaxf(k.min_q, clamped);
+    if (clamped != clamped) lo = clamped;
+    const float dxc = __fsub_rn(lo, k.min_q);
+    // Math.round(scale * dxc): nearest, ties toward +infinity; NaN -> 0
+    const float t = __fmul_rn(k.scale, dxc);
+    int32_t qv;
+    if (t != t) {
+      qv = 0;
+    } else {
+      const float f = floorf(t);
+      qv = (int32_t)f + ((__fsub_rn(t, f) >= 0.5f) ? 1 : 0);
+    }
+    qv = qv < 0 ? 0 : (qv > 127 ? 127 : qv);
+    out[i] = (int8_t)qv;
+    ss += qv * qv;
+    const float dx = __fsub_rn(x, k.min_q);
+    const float dxq = __fmul_rn((float)qv, k.alpha);
+    const float t1 = __fmul_rn(k.min_q, __fsub_rn(x, half));
+    const float t2 = __fmul_rn(__fsub_rn(dx, dxq), dxq);
+    c = __fadd_rn(c, __fadd_rn(t1, t2));
+  }
+  for (int i = dim; i < Dp8; i++) out[i] = 0;
+  corr[qi] = c;
+  sumsq[qi] = ss;
+}
+
+// Row codes for SQ8: copy into padded rows and compute sum of squared codes.
+__global__ void sq8_rows_pad_kernel(const int8_t* __restrict__ src, int64_t n, int dim, int Dp8,
+                                    int8_t* __restrict__ dst, int32_t* __restrict__ sumsq) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  if (row >= n) return;
+  int32_t s = 0;
+  for (int i = lane; i < Dp8; i += 32) {
+    int8_t c = i < dim ? src[row * dim + i] : (int8_t)0;
+    dst[row * Dp8 + i] = c;
+    s += (int32_t)c * (int32_t)c;
+  }
+  s = __reduce_add_sync(0xFFFFFFFFu, s);
+  if (lane == 0) sumsq[row] = s;
+}
+
+__global__ void zero_rows_kernel(__half* dst, int64_t first, int64_t last, int Dp) {
+  int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  int64_t total = (last - first) * Dp;
+  if (i < total) dst[first * Dp + i] = __float2half_rn(0.0f);
+}
+
+}  // namespace
+
+cudaError_t launch_rows_to_f16(const float* src, int64_t n, int dim, int64_t src_stride, int Dp,
+                               bool unit, __half* dst, float* norms, float* norms_sq,
+                               float* max_norm, cudaStream_t st) {
+  if (n <= 0) return cudaSuccess;
+  const int64_t threads = n * 32;
+  const int blocks = (int)((threads + 255) / 256);
+  rows_to_f16_kernel<<<blocks, 256, 0, st>>>(src, n, dim, src_stride, Dp, unit ? 1 : 0, dst, norms,
+                                             norms_sq, max_norm);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_f16_rows_pad(const __half* src, int64_t n, int dim, int Dp, __half* dst,
+                                float* norms_sq, float* max_norm, cudaStream_t st) {
+  if (n <= 0) return cudaSuccess;
+  const int blocks = (int)((n * 32 + 255) / 256);
+  f16_rows_pad_kernel<<<blocks, 256, 0, st>>>(src, n, dim, Dp, dst, norms_sq, max_norm);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_zero_f16_rows(__half* dst, int64_t first, int64_t last, int Dp, cudaStream_t st) {
+  if (last <= first) return cudaSuccess;
+  const int64_t total = (last - first) * Dp;
+  zero_rows_kernel<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(dst, first, last, Dp);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_margin(const float* qnorm, int nq, int D, int metric, int operand_kind,
+                          const float* max_norm, float* margin, cudaStream_t st) {
+  if (nq <= 0) return cudaSuccess;
+  margin_kernel<<<(nq + 127) / 128, 128, 0, st>>>(qnorm, nq, D, metric, operand_kind, max_norm,
+                                                 margin);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_sq8_encode_queries(const float* q, int nq, int dim, int Dp8, Sq8Consts k,
+                                      int8_t* codes, float* corr, int32_t* sumsq, cudaStream_t st) {
+  if (nq <= 0) return cudaSuccess;
+  sq8_encode_queries_kernel<<<(nq + 127) / 128, 128, 0, st>>>(q, nq, dim, Dp8, k, codes, corr, sumsq);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_sq8_rows_pad(const int8_t* src, int64_t n, int dim, int Dp8, int8_t* dst,
+                                int32_t* sumsq, cudaStream_t st) {
+  if (n <= 0) return cudaSuccess;
+  const int blocks = (int)((n * 32 + 255) / 256);
+  sq8_rows_pad_kernel<<<blocks, 256, 0, st>>>(src, n, dim, Dp8, dst, sumsq);
+  return cudaGetLastError();
+}
+
+// ScalarQuantizer constructor constants (ScalarQuantizer.java:59-69), INT8 maxValue 127.
+Sq8Consts sq8_consts(float min_q, float max_q) {
+  Sq8Consts k;
+  k.min_q = min_q;
+  k.max_q = max_q;
+  const float range = max_q - min_q;
+  k.scale = (range == 0.0f) ? 0.0f : 127.0f / range;
+  k.alpha = (range == 0.0f) ? 0.0f : range / 127.0f;
+  k.cm = k.alpha * k.alpha;
+  return k;
+}
+
+}  // namespace vx

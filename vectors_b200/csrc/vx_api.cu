@@ -1,0 +1,1293 @@
+// vx_api.cu -- the C ABI of libvx.so (include/vx.h): index handles, device copies, query
+// chunking and the search pipelines built from the scan kernels.
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <atomic>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/vx.h"
+#include "common.cuh"
+#include "gemm_scan.h"
+#include "ivfpq.h"
+#include "kernels.h"
+#include "prep.h"
+#include "rescore.h"
+
+namespace vx {
+namespace {
+
+thread_local std::string g_last_error;
+thread_local int32_t g_fail_next = 0;
+std::atomic<int64_t> g_launches{0};
+
+int fail(int status, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return status;
+}
+
+struct CudaFail {
+  int status;
+};
+
+#define VX_CUDA(expr)                                                                       \
+  do {                                                                                      \
+    cudaError_t _e = (expr);                                                                \
+    if (_e != cudaSuccess) {                                                                \
+      int _s = (_e == cudaErrorMemoryAllocation) ? VX_ERR_OUT_OF_MEMORY : VX_ERR_CUDA;      \
+      fail(_s, "%s failed: %s (%s:%d)", #expr, cudaGetErrorString(_e), __FILE__, __LINE__); \
+      throw CudaFail{_s};                                                                   \
+    }                                                                                       \
+  } while (0)
+
+#define VX_LAUNCH(n, expr)          \
+  do {                              \
+    g_launches.fetch_add(n);        \
+    VX_CUDA(expr);                  \
+  } while (0)
+
+bool take_injected(int* st) {
+  if (g_fail_next != 0) {
+    *st = fail(g_fail_next, "injected failure (vx_debug_fail_next)");
+    g_fail_next = 0;
+    return true;
+  }
+  return false;
+}
+
+int64_t round_up(int64_t v, int64_t m) { return (v + m - 1) / m * m; }
+
+// ------------------------------------------------------------------ driver entry points
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+EncodeTiledFn encode_tiled() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = (EncodeTiledFn)p;
+  });
+  return fn;
+}
+
+// 2-D K-major operand [rows][row_bytes] with a (128-byte x box_rows) box, 128-byte swizzle.
+void make_tmap(CUtensorMap* m, const void* base, CUtensorMapDataType dt, int elem_bytes,
+               int64_t inner_elems, int64_t rows, int box_rows) {
+  EncodeTiledFn fn = encode_tiled();
+  if (!fn) {
+    fail(VX_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+    throw CudaFail{VX_ERR_CUDA};
+  }
+  cuuint64_t dims[2] = {(cuuint64_t)inner_elems, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)(inner_elems * elem_bytes)};
+  cuuint32_t box[2] = {(cuuint32_t)(128 / elem_bytes), (cuuint32_t)box_rows};
+  cuuint32_t es[2] = {1, 1};
+  CUresult r = fn(m, dt, 2, const_cast<void*>(base), dims, strides, box, es,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    fail(VX_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+    throw CudaFail{VX_ERR_CUDA};
+  }
+}
+
+// ------------------------------------------------------------------ scratch
+// Stream-ordered device allocations released (stream-ordered) at scope exit.
+struct Scratch {
+  cudaStream_t st;
+  std::vector<void*> ptrs;
+  explicit Scratch(cudaStream_t s) : st(s) {}
+  template <class T>
+  T* alloc(size_t count) {
+    void* p = nullptr;
+    size_t bytes = std::max<size_t>(count * sizeof(T), 16);
+    VX_CUDA(cudaMallocAsync(&p, bytes, st));
+    ptrs.push_back(p);
+    return (T*)p;
+  }
+  ~Scratch() {
+    for (void* p : ptrs) cudaFreeAsync(p, st);
+  }
+};
+
+size_t scratch_budget() {
+  const char* e = getenv("VX_SCRATCH_BYTES");
+  if (e && *e) return (size_t)strtoull(e, nullptr, 10);
+  return (size_t)1 << 30;
+}
+
+uint64_t wait_timeout_ns() {
+  const char* e = getenv("VX_WAIT_TIMEOUT_MS");
+  if (e && *e) return (uint64_t)strtoull(e, nullptr, 10) * 1000000ull;
+  return 1500ull * 1000000ull;  // 1.5 s per wait
+}
+
+}  // namespace
+}  // namespace vx
+
+using namespace vx;
+
+// ------------------------------------------------------------------ index
+struct vx_index {
+  int kind = 0;
+  int device = 0;
+  int metric = 0;
+  int64_t n = 0;
+  int dim = 0;
+  int num_sms = 148;
+  // fp32 rows (FLAT; optional for the quantized kinds), row stride = dim
+  float* rows32 = nullptr;
+  // fp16 GEMM operand [n][Dp]: unit rows (FLAT) or the stored fp16 rows (FP16)
+  __half* rows16 = nullptr;
+  int Dp = 0;
+  float* rowscale = nullptr;  // |x| (unit rows) or 1 (fp16 rows)
+  float* rowsq = nullptr;     // |x|^2
+  float* max_norm = nullptr;  // device scalar
+  CUtensorMap tm_rows;
+  bool has_tm_rows = false;
+  // SQ8
+  int8_t* codes8 = nullptr;
+  int Dp8 = 0;
+  float* vcorr = nullptr;
+  int32_t* vsq = nullptr;
+  float min_q = 0, max_q = 0;
+  CUtensorMap tm_codes8;
+  // BQ
+  uint64_t* words = nullptr;
+  int nw_pad = 0;
+  // IVF-PQ
+  float* cent = nullptr;
+  int nlist = 0;
+  int64_t* list_off = nullptr;
+  int32_t* ordinals = nullptr;
+  uint8_t* pq_codes = nullptr;
+  int M = 0, Ks = 0, Mp = 0;
+  float* codebooks = nullptr;
+  int64_t* cb_off = nullptr;
+  int32_t* sub = nullptr;
+  int nprobe = 1, rescore = 1;
+  std::vector<void*> owned;
+  // exact-search view of a quantized index (built on first use)
+  vx_index* flat = nullptr;
+  std::mutex lazy_mu;
+};
+
+namespace vx {
+namespace {
+
+template <class T>
+T* dev_alloc(vx_index* ix, size_t count) {
+  void* p = nullptr;
+  VX_CUDA(cudaMalloc(&p, std::max<size_t>(count * sizeof(T), 16)));
+  ix->owned.push_back(p);
+  return (T*)p;
+}
+
+void free_index(vx_index* ix) {
+  if (!ix) return;
+  cudaSetDevice(ix->device);
+  cudaDeviceSynchronize();
+  if (ix->flat) free_index(ix->flat);
+  for (void* p : ix->owned) cudaFree(p);
+  delete ix;
+}
+
+int check_device(int device, int* nsms) {
+  int count = 0;
+  cudaError_t e = cudaGetDeviceCount(&count);
+  if (e != cudaSuccess || count == 0)
+    return fail(VX_ERR_GPU_UNAVAILABLE, "no CUDA device available (%s)",
+                e == cudaSuccess ? "0 devices" : cudaGetErrorString(e));
+  if (device < 0 || device >= count)
+    return fail(VX_ERR_INVALID_ARGUMENT, "device %d out of range [0, %d)", device, count);
+  cudaDeviceProp prop;
+  if (cudaGetDeviceProperties(&prop, device) != cudaSuccess)
+    return fail(VX_ERR_GPU_UNAVAILABLE, "cannot query device %d", device);
+  if (prop.major != 10)
+    return fail(VX_ERR_GPU_UNAVAILABLE, "device %d is sm_%d%d; this library is built for sm_100a",
+                device, prop.major, prop.minor);
+  if (cudaSetDevice(device) != cudaSuccess)
+    return fail(VX_ERR_GPU_UNAVAILABLE, "cannot select device %d", device);
+  *nsms = prop.multiProcessorCount;
+  return VX_OK;
+}
+
+int check_metric(int metric) {
+  if (metric < 0 || metric > 3) return fail(VX_ERR_INVALID_ARGUMENT, "unknown metric %d", metric);
+  return VX_OK;
+}
+
+// Uploads host rows (stride >= dim floats) as a dense [n][dim] device array.
+float* upload_rows32(vx_index* ix, const float* host, int64_t n, int dim, int64_t stride) {
+  float* d = dev_alloc<float>(ix, (size_t)n * dim);
+  if (n > 0)
+    VX_CUDA(cudaMemcpy2D(d, (size_t)dim * 4, host, (size_t)stride * 4, (size_t)dim * 4, (size_t)n,
+                         cudaMemcpyHostToDevice));
+  return d;
+}
+
+// fp16 unit-row GEMM operand from the fp32 rows.
+void build_unit_f16(vx_index* ix) {
+  ix->Dp = (int)round_up(ix->dim, 64);
+  ix->rows16 = dev_alloc<__half>(ix, (size_t)std::max<int64_t>(ix->n, 1) * ix->Dp);
+  ix->rowscale = dev_alloc<float>(ix, (size_t)std::max<int64_t>(ix->n, 1));
+  ix->rowsq = dev_alloc<float>(ix, (size_t)std::max<int64_t>(ix->n, 1));
+  ix->max_norm = dev_alloc<float>(ix, 1);
+  VX_CUDA(cudaMemset(ix->max_norm, 0, 4));
+  VX_LAUNCH(1, launch_rows_to_f16(ix->rows32, ix->n, ix->dim, ix->dim, ix->Dp, true, ix->rows16,
+                                  ix->rowscale, ix->rowsq, ix->max_norm, 0));
+  if (ix->n > 0) {
+    make_tmap(&ix->tm_rows, ix->rows16, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, ix->Dp, ix->n, 256);
+    ix->has_tm_rows = true;
+  }
+  VX_CUDA(cudaDeviceSynchronize());
+}
+
+template <class F>
+int guarded(F&& f) {
+  int st;
+  if (take_injected(&st)) return st;
+  try {
+    return f();
+  } catch (const CudaFail& e) {
+    return e.status;
+  } catch (const std::bad_alloc&) {
+    return fail(VX_ERR_OUT_OF_MEMORY, "host allocation failed");
+  }
+}
+
+int check_device_error(int32_t* d_err, cudaStream_t st) {
+  int32_t h = 0;
+  VX_CUDA(cudaMemcpyAsync(&h, d_err, 4, cudaMemcpyDeviceToHost, st));
+  VX_CUDA(cudaStreamSynchronize(st));
+  if (h == kDevWaitTimeout)
+    return fail(VX_ERR_DEVICE_TIMEOUT, "a device-side wait exceeded its time budget");
+  if (h != 0) return fail(VX_ERR_CUDA, "device error %d", h);
+  return VX_OK;
+}
+
+// ------------------------------------------------------------------ exact fallback
+// Scores every row exactly for the queries in `list` (device indices into q) and writes
+// their results in place.
+void exact_fallback(vx_index* ix, const float* dq, int nq_chunk, int dim, int k, int flavor,
+                    const void* rows, bool rows_f16, int64_t stride, const int32_t* h_list,
+                    int nflag, int32_t* d_ids, float* d_scores, int32_t* d_counts,
+                    cudaStream_t st) {
+  Scratch S(st);
+  const StreamGeom g = stream_geom(k, 32);
+  const int W = exact_scan_warps(ix->num_sms);
+  float* fq = S.alloc<float>((size_t)8 * dim);
+  uint64_t* bufs = S.alloc<uint64_t>((size_t)W * 8 * g.C);
+  uint32_t* cnts = S.alloc<uint32_t>((size_t)W * 8);
+  uint64_t* keys = S.alloc<uint64_t>((size_t)8 * k);
+  uint32_t* kc = S.alloc<uint32_t>(8);
+  int32_t* tids = S.alloc<int32_t>((size_t)8 * k);
+  float* tsc = S.alloc<float>((size_t)8 * k);
+  int32_t* tcnt = S.alloc<int32_t>(8);
+  for (int f0 = 0; f0 < nflag; f0 += 8) {
+    const int nf = std::min(8, nflag - f0);
+    for (int i = 0; i < nf; i++)
+      VX_CUDA(cudaMemcpyAsync(fq + (size_t)i * dim, dq + (size_t)h_list[f0 + i] * dim,
+                              (size_t)dim * 4, cudaMemcpyDeviceToDevice, st));
+    ExactScanArgs a;
+    a.nfq = nf;
+    a.dim = dim;
+    a.K = g.K;
+    a.C = g.C;
+    a.flavor = flavor;
+    a.metric = ix->metric;
+    a.queries = fq;
+    a.rows = rows;
+    a.row_stride = stride;
+    a.n = ix->n;
+    a.bufs = bufs;
+    a.cnts = cnts;
+    VX_LAUNCH(1, launch_exact_scan(a, rows_f16, g.R, ix->num_sms, st));
+    VX_LAUNCH(1, launch_merge_streams(bufs, cnts, W, nf, 8, g.C, k, keys, kc, st));
+    VX_LAUNCH(1, launch_finish_keys(keys, kc, nf, k, k, kFinishFloatKey, ix->metric, dim, tids, tsc,
+                                    tcnt, st));
+    for (int i = 0; i < nf; i++) {
+      const int q = h_list[f0 + i];
+      VX_CUDA(cudaMemcpyAsync(d_ids + (size_t)q * k, tids + (size_t)i * k, (size_t)k * 4,
+                              cudaMemcpyDeviceToDevice, st));
+      VX_CUDA(cudaMemcpyAsync(d_scores + (size_t)q * k, tsc + (size_t)i * k, (size_t)k * 4,
+                              cudaMemcpyDeviceToDevice, st));
+      VX_CUDA(cudaMemcpyAsync(d_counts + q, tcnt + i, 4, cudaMemcpyDeviceToDevice, st));
+    }
+  }
+  VX_CUDA(cudaStreamSynchronize(st));
+}
+
+int candidate_width(int k, int64_t n) {
+  // Approximate candidates per query: enough headroom above k for the margin test to pass on
+  // typical data; queries that need more take the exact fallback.
+  int64_t kc = std::max<int64_t>(32, round_up(2 * (int64_t)k + 16, 32));
+  kc = std::min<int64_t>(kc, 1024);
+  if (n < kc) kc = std::max<int64_t>(n, 1);
+  return (int)kc;
+}
+
+// FLAT / FP16: fp16 tcgen05 approximate pass + exact fp32 re-score (+ exact fallback).
+int search_gemm_exact(vx_index* ix, const float* dq, int nq, int k, int32_t* d_ids,
+                      float* d_scores, int32_t* d_counts, cudaStream_t st) {
+  const bool f16_kind = ix->kind == VX_KIND_FP16;
+  const int flavor = f16_kind ? kFlavorFp16Quantized : kFlavorFlat;
+  const void* rows = f16_kind ? (const void*)ix->rows16 : (const void*)ix->rows32;
+  const int64_t stride = f16_kind ? ix->Dp : ix->dim;
+  const int dim = ix->dim;
+  const int Kc = candidate_width(k, ix->n);
+  const int R = gemm_scan_stream_R(Kc);
+  if (R < 0) return fail(VX_ERR_UNSUPPORTED, "k=%d is larger than this build supports", k);
+  const int C = 32 * R;
+  const int64_t ntiles = (ix->n + 255) / 256;
+  int mode;
+  if (ix->metric == VX_EUCLIDEAN)
+    mode = kEpiF16L2;
+  else if (f16_kind || ix->metric == VX_COSINE)
+    mode = kEpiF16Plain;
+  else
+    mode = kEpiF16Scaled;
+  // query chunk sized by the scratch budget
+  const int G0 = gemm_scan_grid(ntiles, 1 << 20, ix->num_sms);
+  int64_t qch = (int64_t)(scratch_budget() / ((size_t)G0 * (C * 8 + 12)));
+  qch = std::max<int64_t>(128, qch / 128 * 128);
+  Scratch S(st);
+  int32_t* d_err = S.alloc<int32_t>(1);
+  VX_CUDA(cudaMemsetAsync(d_err, 0, 4, st));
+  for (int q0 = 0; q0 < nq; q0 += (int)qch) {
+    const int qc = (int)std::min<int64_t>(qch, nq - q0);
+    const int mblocks = (qc + 127) / 128;
+    const int Qp = mblocks * 128;
+    const int grid = gemm_scan_grid(ntiles, mblocks, ix->num_sms);
+    Scratch T(st);
+    __half* qh = T.alloc<__half>((size_t)Qp * ix->Dp);
+    float* qnorm = T.alloc<float>(qc);
+    float* margin = T.alloc<float>(qc);
+    uint64_t* bufs = T.alloc<uint64_t>((size_t)grid * Qp * C);
+    uint32_t* cnts = T.alloc<uint32_t>((size_t)grid * Qp);
+    uint64_t* thrs = T.alloc<uint64_t>((size_t)grid * Qp);
+    uint64_t* cand = T.alloc<uint64_t>((size_t)qc * Kc);
+    uint32_t* cand_cnt = T.alloc<uint32_t>(qc);
+    int32_t* nflag = T.alloc<int32_t>(1);
+    int32_t* flag_list = T.alloc<int32_t>(qc);
+    const float* dqc = dq + (size_t)q0 * dim;
+    VX_CUDA(cudaMemsetAsync(qh + (size_t)qc * ix->Dp, 0, (size_t)(Qp - qc) * ix->Dp * 2, st));
+    VX_LAUNCH(1, launch_rows_to_f16(dqc, qc, dim, dim, ix->Dp, true, qh, qnorm, nullptr, nullptr, st));
+    VX_LAUNCH(1, launch_margin(qnorm, qc, dim, ix->metric,
+                               f16_kind ? kOperandExactRows : kOperandUnitRows, ix->max_norm, margin,
+                               st));
+    VX_CUDA(cudaMemsetAsync(cnts, 0, (size_t)grid * Qp * 4, st));
+    VX_CUDA(cudaMemsetAsync(thrs, 0, (size_t)grid * Qp * 8, st));
+    VX_CUDA(cudaMemsetAsync(nflag, 0, 4, st));
+    CUtensorMap tmq;
+    make_tmap(&tmq, qh, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, ix->Dp, Qp, 128);
+    ScanArgs a;
+    a.n = ix->n;
+    a.nq = qc;
+    a.num_mblocks = mblocks;
+    a.kchunks = ix->Dp / 64;
+    a.ntiles = ntiles;
+    a.K = Kc;
+    a.C = C;
+    a.bufs = bufs;
+    a.cnts = cnts;
+    a.thrs = thrs;
+    a.err = d_err;
+    a.timeout_ns = wait_timeout_ns();
+    a.epi.xnorm = ix->rowscale;
+    a.epi.rowsq = ix->rowsq;
+    a.epi.qscale = qnorm;
+    a.epi.vcorr = nullptr;
+    a.epi.qsq = nullptr;
+    a.epi.vsq = nullptr;
+    a.epi.cm = 0.0f;
+    VX_LAUNCH(1, launch_gemm_scan(mode, tmq, ix->tm_rows, a, grid, R, st));
+    VX_LAUNCH(1, launch_merge_streams(bufs, cnts, grid, qc, Qp, C, Kc, cand, cand_cnt, st));
+    RescoreArgs r;
+    r.nq = qc;
+    r.dim = dim;
+    r.k = k;
+    r.Kc = Kc;
+    r.flavor = flavor;
+    r.metric = ix->metric;
+    r.queries = dqc;
+    r.rows = rows;
+    r.row_stride = stride;
+    r.cand = cand;
+    r.cand_cnt = cand_cnt;
+    r.check_margin = 1;
+    r.margin = margin;
+    r.id_offset = 0;
+    r.n_rows = ix->n;
+    r.out_ids = d_ids + (size_t)q0 * k;
+    r.out_scores = d_scores + (size_t)q0 * k;
+    r.out_counts = d_counts + q0;
+    r.nflag = nflag;
+    r.flag_list = flag_list;
+    VX_LAUNCH(1, launch_rescore(r, f16_kind, st));
+    int st_err = check_device_error(d_err, st);
+    if (st_err != VX_OK) return st_err;
+    int32_t h_nflag = 0;
+    VX_CUDA(cudaMemcpyAsync(&h_nflag, nflag, 4, cudaMemcpyDeviceToHost, st));
+    VX_CUDA(cudaStreamSynchronize(st));
+    if (h_nflag > 0) {
+      std::vector<int32_t> h_list(h_nflag);
+      VX_CUDA(cudaMemcpyAsync(h_list.data(), flag_list, (size_t)h_nflag * 4, cudaMemcpyDeviceToHost, st));
+      VX_CUDA(cudaStreamSynchronize(st));
+      exact_fallback(ix, dqc, qc, dim, k, flavor, rows, f16_kind, stride, h_list.data(), h_nflag,
+                     d_ids + (size_t)q0 * k, d_scores + (size_t)q0 * k, d_counts + q0, st);
+    }
+  }
+  return VX_OK;
+}
+
+// SQ8 / BQ: exact quantized scores; K best per query (optionally re-scored in fp32).
+int search_quantized_scan(vx_index* ix, const float* dq, int nq, int K, int k_out, bool rescore,
+                          int32_t* d_ids, float* d_scores, int32_t* d_counts, cudaStream_t st) {
+  const int dim = ix->dim;
+  Scratch S(st);
+  int32_t* d_err = S.alloc<int32_t>(1);
+  VX_CUDA(cudaMemsetAsync(d_err, 0, 4, st));
+  if (ix->kind == VX_KIND_SQ8) {
+    const int R = gemm_scan_stream_R(K);
+    if (R < 0) return fail(VX_ERR_UNSUPPORTED, "k=%d is larger than this build supports", K);
+    const int C = 32 * R;
+    const int64_t ntiles = (ix->n + 255) / 256;
+    const int G0 = gemm_scan_grid(ntiles, 1 << 20, ix->num_sms);
+    int64_t qch = (int64_t)(scratch_budget() / ((size_t)G0 * (C * 8 + 12)));
+    qch = std::max<int64_t>(128, qch / 128 * 128);
+    const int mode = ix->metric == VX_EUCLIDEAN ? kEpiSq8L2
+                     : ix->metric == VX_MAXIMUM_INNER_PRODUCT ? kEpiSq8Mip
+                                                              : kEpiSq8Dot;
+    const Sq8Consts kc = sq8_consts(ix->min_q, ix->max_q);
+    for (int q0 = 0; q0 < nq; q0 += (int)qch) {
+      const int qc = (int)std::min<int64_t>(qch, nq - q0);
+      const int mblocks = (qc + 127) / 128;
+      const int Qp = mblocks * 128;
+      const int grid = gemm_scan_grid(ntiles, mblocks, ix->num_sms);
+      Scratch T(st);
+      int8_t* qcodes = T.alloc<int8_t>((size_t)Qp * ix->Dp8);
+      float* qcorr = T.alloc<float>(qc);
+      int32_t* qsq = T.alloc<int32_t>(qc);
+      uint64_t* bufs = T.alloc<uint64_t>((size_t)grid * Qp * C);
+      uint32_t* cnts = T.alloc<uint32_t>((size_t)grid * Qp);
+      uint64_t* thrs = T.alloc<uint64_t>((size_t)grid * Qp);
+      uint64_t* keys = T.alloc<uint64_t>((size_t)qc * K);
+      uint32_t* kcnt = T.alloc<uint32_t>(qc);
+      const float* dqc = dq + (size_t)q0 * dim;
+      VX_CUDA(cudaMemsetAsync(qcodes + (size_t)qc * ix->Dp8, 0, (size_t)(Qp - qc) * ix->Dp8, st));
+      VX_LAUNCH(1, launch_sq8_encode_queries(dqc, qc, dim, ix->Dp8, kc, qcodes, qcorr, qsq, st));
+      VX_CUDA(cudaMemsetAsync(cnts, 0, (size_t)grid * Qp * 4, st));
+      VX_CUDA(cudaMemsetAsync(thrs, 0, (size_t)grid * Qp * 8, st));
+      CUtensorMap tmq;
+      make_tmap(&tmq, qcodes, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, ix->Dp8, Qp, 128);
+      ScanArgs a;
+      a.n = ix->n;
+      a.nq = qc;
+      a.num_mblocks = mblocks;
+      a.kchunks = ix->Dp8 / 128;
+      a.ntiles = ntiles;
+      a.K = K;
+      a.C = C;
+      a.bufs = bufs;
+      a.cnts = cnts;
+      a.thrs = thrs;
+      a.err = d_err;
+      a.timeout_ns = wait_timeout_ns();
+      a.epi.xnorm = nullptr;
+      a.epi.rowsq = nullptr;
+      a.epi.qscale = qcorr;
+      a.epi.vcorr = ix->vcorr;
+      a.epi.qsq = qsq;
+      a.epi.vsq = ix->vsq;
+      a.epi.cm = kc.cm;
+      VX_LAUNCH(1, launch_gemm_scan(mode, tmq, ix->tm_codes8, a, grid, R, st));
+      VX_LAUNCH(1, launch_merge_streams(bufs, cnts, grid, qc, Qp, C, K, keys, kcnt, st));
+      if (rescore) {
+        RescoreArgs r{};
+        r.nq = qc;
+        r.dim = dim;
+        r.k = k_out;
+        r.Kc = K;
+        r.flavor = kFlavorFlat;
+        r.metric = ix->metric;
+        r.queries = dqc;
+        r.rows = ix->rows32;
+        r.row_stride = dim;
+        r.cand = keys;
+        r.cand_cnt = kcnt;
+        r.check_margin = 0;
+        r.n_rows = ix->n;
+        r.out_ids = d_ids + (size_t)q0 * k_out;
+        r.out_scores = d_scores + (size_t)q0 * k_out;
+        r.out_counts = d_counts + q0;
+        r.nflag = T.alloc<int32_t>(1);
+        r.flag_list = T.alloc<int32_t>(qc);
+        VX_LAUNCH(1, launch_rescore(r, false, st));
+      } else {
+        VX_LAUNCH(1, launch_finish_keys(keys, kcnt, qc, K, k_out, kFinishFloatKey, ix->metric, dim,
+                                        d_ids + (size_t)q0 * k_out, d_scores + (size_t)q0 * k_out,
+                                        d_counts + q0, st));
+      }
+    }
+  } else {  // BQ
+    const StreamGeom g = stream_geom(K, 32);
+    if (g.R < 0) return fail(VX_ERR_UNSUPPORTED, "k=%d is larger than this build supports", K);
+    const int parts = bq_parts(ix->n, ix->num_sms);
+    int64_t qch = (int64_t)(scratch_budget() / ((size_t)parts * (g.C * 8 + 12)));
+    qch = std::max<int64_t>(256, qch / 256 * 256);
+    for (int q0 = 0; q0 < nq; q0 += (int)qch) {
+      const int qc = (int)std::min<int64_t>(qch, nq - q0);
+      Scratch T(st);
+      uint64_t* qw = T.alloc<uint64_t>((size_t)qc * ix->nw_pad);
+      uint64_t* bufs = T.alloc<uint64_t>((size_t)parts * qc * g.C);
+      uint32_t* cnts = T.alloc<uint32_t>((size_t)parts * qc);
+      uint64_t* thrs = T.alloc<uint64_t>((size_t)parts * qc);
+      uint64_t* keys = T.alloc<uint64_t>((size_t)qc * K);
+      uint32_t* kcnt = T.alloc<uint32_t>(qc);
+      const float* dqc = dq + (size_t)q0 * dim;
+      VX_LAUNCH(1, launch_bq_pack_queries(dqc, qc, dim, ix->nw_pad, qw, st));
+      VX_CUDA(cudaMemsetAsync(cnts, 0, (size_t)parts * qc * 4, st));
+      VX_CUDA(cudaMemsetAsync(thrs, 0, (size_t)parts * qc * 8, st));
+      VX_LAUNCH(1, launch_bq_scan(ix->words, ix->n, ix->nw_pad, qw, qc, parts, g, bufs, cnts, thrs, st));
+      VX_LAUNCH(1, launch_merge_streams(bufs, cnts, parts, qc, qc, g.C, K, keys, kcnt, st));
+      if (rescore) {
+        RescoreArgs r{};
+        r.nq = qc;
+        r.dim = dim;
+        r.k = k_out;
+        r.Kc = K;
+        r.flavor = kFlavorFlat;
+        r.metric = ix->metric;
+        r.queries = dqc;
+        r.rows = ix->rows32;
+        r.row_stride = dim;
+        r.cand = keys;
+        r.cand_cnt = kcnt;
+        r.check_margin = 0;
+        r.n_rows = ix->n;
+        r.out_ids = d_ids + (size_t)q0 * k_out;
+        r.out_scores = d_scores + (size_t)q0 * k_out;
+        r.out_counts = d_counts + q0;
+        r.nflag = T.alloc<int32_t>(1);
+        r.flag_list = T.alloc<int32_t>(qc);
+        VX_LAUNCH(1, launch_rescore(r, false, st));
+      } else {
+        VX_LAUNCH(1, launch_finish_keys(keys, kcnt, qc, K, k_out, kFinishHamming, ix->metric, dim,
+                                        d_ids + (size_t)q0 * k_out, d_scores + (size_t)q0 * k_out,
+                                        d_counts + q0, st));
+      }
+    }
+  }
+  return check_device_error(d_err, st);
+}
+
+// IVF-PQ: IvfIndex.pqSearch.
+int search_ivfpq(vx_index* ix, const float* dq, int nq, int k, int nprobe, int rescore,
+                 float min_score, int32_t* d_ids, float* d_scores, int32_t* d_counts,
+                 cudaStream_t st) {
+  const int dim = ix->dim;
+  const int probes = std::min(nprobe, ix->nlist);
+  int64_t wide = std::min<int64_t>((int64_t)k * rescore, ix->n);
+  if (wide < 1) wide = 1;
+  const int K = (int)wide;
+  const StreamGeom g = stream_geom(K, 32);
+  if (g.R < 0) return fail(VX_ERR_UNSUPPORTED, "k * rescoreFactor = %d is larger than supported", K);
+  if (rescore > 1 && !ix->rows32)
+    return fail(VX_ERR_UNSUPPORTED, "rescoreFactor > 1 needs the full-precision vectors at build");
+  // chunk queries: distances [qc][nlist] + outputs [nprobe][qc][K]
+  const size_t per_q = (size_t)ix->nlist * 4 + (size_t)probes * (K * 8 + 8) + 64;
+  int64_t qch = std::max<int64_t>(64, (int64_t)(scratch_budget() / per_q));
+  for (int q0 = 0; q0 < nq; q0 += (int)qch) {
+    const int qc = (int)std::min<int64_t>(qch, nq - q0);
+    Scratch T(st);
+    const float* dqc = dq + (size_t)q0 * dim;
+    float* qn = T.alloc<float>((size_t)qc * dim);
+    float* dist = T.alloc<float>((size_t)qc * ix->nlist);
+    int32_t* lists = T.alloc<int32_t>((size_t)qc * probes);
+    int32_t* counts = T.alloc<int32_t>(ix->nlist);
+    int32_t* offsets = T.alloc<int32_t>(ix->nlist + 1);
+    int32_t* cursor = T.alloc<int32_t>(ix->nlist);
+    int32_t* pairs = T.alloc<int32_t>((size_t)qc * probes);
+    uint64_t* out = T.alloc<uint64_t>((size_t)probes * qc * K);
+    uint32_t* out_cnt = T.alloc<uint32_t>((size_t)probes * qc);
+    uint64_t* keys = T.alloc<uint64_t>((size_t)qc * K);
+    uint32_t* kcnt = T.alloc<uint32_t>(qc);
+    VX_LAUNCH(ix->metric == VX_COSINE ? 3 : 2,
+              launch_route(dqc, qc, dim, ix->cent, ix->nlist, ix->metric, probes, qn, dist, lists, st));
+    VX_LAUNCH(3, launch_group_pairs(lists, qc * probes, ix->nlist, counts, offsets, cursor, pairs, st));
+    VX_CUDA(cudaMemsetAsync(out_cnt, 0, (size_t)probes * qc * 4, st));
+    AdcArgs a;
+    a.nq = qc;
+    a.dim = dim;
+    a.nprobe = probes;
+    a.metric = ix->metric;
+    a.M = ix->M;
+    a.Ks = ix->Ks;
+    a.Mp = ix->Mp;
+    a.K = K;
+    a.npairs = (int64_t)qc * probes;
+    a.pairs = pairs;
+    a.lists = lists;
+    a.queries = dqc;
+    a.cent = ix->cent;
+    a.list_off = ix->list_off;
+    a.ordinals = ix->ordinals;
+    a.codes = ix->pq_codes;
+    a.codebooks = ix->codebooks;
+    a.cb_off = ix->cb_off;
+    a.sub = ix->sub;
+    a.out = out;
+    a.out_cnt = out_cnt;
+    const int grid = ix->num_sms * 2;
+    VX_LAUNCH(1, launch_adc_scan(a, g.R, grid, st));
+    VX_LAUNCH(1, launch_merge_streams(out, out_cnt, probes, qc, qc, K, K, keys, kcnt, st));
+    int32_t* oi = d_ids + (size_t)q0 * k;
+    float* os = d_scores + (size_t)q0 * k;
+    int32_t* oc = d_counts + q0;
+    if (rescore == 1) {
+      VX_LAUNCH(1, launch_finish_keys(keys, kcnt, qc, K, k, kFinishFloatKey, ix->metric, dim, oi, os, oc, st));
+    } else {
+      RescoreArgs r{};
+      r.nq = qc;
+      r.dim = dim;
+      r.k = k;
+      r.Kc = K;
+      r.flavor = kFlavorIvfRaw;
+      r.metric = ix->metric;
+      r.queries = dqc;
+      r.rows = ix->rows32;
+      r.row_stride = dim;
+      r.cand = keys;
+      r.cand_cnt = kcnt;
+      r.check_margin = 0;
+      r.n_rows = ix->n;
+      r.out_ids = oi;
+      r.out_scores = os;
+      r.out_counts = oc;
+      r.nflag = T.alloc<int32_t>(1);
+      r.flag_list = T.alloc<int32_t>(qc);
+      VX_LAUNCH(1, launch_rescore(r, false, st));
+    }
+    VX_LAUNCH(1, launch_min_score(os, qc, k, min_score, oc, st));
+  }
+  return VX_OK;
+}
+
+void fill_empty(int nq, int k, int32_t* d_ids, float* d_scores, int32_t* d_counts, cudaStream_t st) {
+  if (nq <= 0) return;
+  VX_CUDA(cudaMemsetAsync(d_counts, 0, (size_t)nq * 4, st));
+  VX_CUDA(cudaMemsetAsync(d_ids, 0xFF, (size_t)nq * k * 4, st));
+  VX_CUDA(cudaMemsetAsync(d_scores, 0, (size_t)nq * k * 4, st));
+}
+
+int validate_search(vx_index* ix, const void* q, int nq, int dim, int k, const void* a,
+                    const void* b, const void* c) {
+  if (!ix) return fail(VX_ERR_NULL_POINTER, "index must not be null");
+  if (!q) return fail(VX_ERR_NULL_POINTER, "queries must not be null");
+  if (!a || !b || !c) return fail(VX_ERR_NULL_POINTER, "output buffers must not be null");
+  if (nq <= 0) return fail(VX_ERR_INVALID_ARGUMENT, "queries must not be empty");
+  if (k <= 0) return fail(VX_ERR_INVALID_ARGUMENT, "k must be positive: %d", k);
+  if (ix->n > 0 && dim != ix->dim)
+    return fail(VX_ERR_INVALID_ARGUMENT, "Query dimension %d does not match index dimension %d", dim,
+                ix->dim);
+  return VX_OK;
+}
+
+// Exact-search view of a quantized index that was built with its fp32 rows: a FLAT index
+// sharing those rows, created on first use (QuantizedFlatScanAdapter's `exact` delegate).
+vx_index* flat_view(vx_index* ix) {
+  std::lock_guard<std::mutex> g(ix->lazy_mu);
+  if (!ix->flat) {
+    vx_index* v = new vx_index();
+    v->kind = VX_KIND_FLAT;
+    v->device = ix->device;
+    v->metric = ix->metric;
+    v->n = ix->n;
+    v->dim = ix->dim;
+    v->num_sms = ix->num_sms;
+    v->rows32 = ix->rows32;  // borrowed; owned by ix
+    try {
+      build_unit_f16(v);
+    } catch (...) {
+      free_index(v);
+      throw;
+    }
+    ix->flat = v;
+  }
+  return ix->flat;
+}
+
+// FP16 two-pass: candidates by the fp16 score function, then exact fp32 re-score.
+int search_fp16_two_pass(vx_index* ix, const float* dq, int nq, int ck, int k, int32_t* d_ids,
+                         float* d_scores, int32_t* d_counts, cudaStream_t st) {
+  Scratch S(st);
+  int32_t* ci = S.alloc<int32_t>((size_t)nq * ck);
+  float* cs = S.alloc<float>((size_t)nq * ck);
+  int32_t* cc = S.alloc<int32_t>(nq);
+  uint64_t* keys = S.alloc<uint64_t>((size_t)nq * ck);
+  int rc = search_gemm_exact(ix, dq, nq, ck, ci, cs, cc, st);
+  if (rc != VX_OK) return rc;
+  VX_LAUNCH(1, launch_ids_to_keys(ci, cc, nq, ck, keys, st));
+  RescoreArgs r{};
+  r.nq = nq;
+  r.dim = ix->dim;
+  r.k = k;
+  r.Kc = ck;
+  r.flavor = kFlavorFlat;
+  r.metric = ix->metric;
+  r.queries = dq;
+  r.rows = ix->rows32;
+  r.row_stride = ix->dim;
+  r.cand = keys;
+  r.cand_cnt = (const uint32_t*)cc;
+  r.check_margin = 0;
+  r.n_rows = ix->n;
+  r.out_ids = d_ids;
+  r.out_scores = d_scores;
+  r.out_counts = d_counts;
+  r.nflag = S.alloc<int32_t>(1);
+  r.flag_list = S.alloc<int32_t>(nq);
+  VX_LAUNCH(1, launch_rescore(r, false, st));
+  return VX_OK;
+}
+
+// Dispatch of IndexSpi.searchBatch semantics on device buffers.
+int search_batch_dev(vx_index* ix, const float* dq, int nq, int dim, int k, int sls, float oqf,
+                     int32_t* d_ids, float* d_scores, int32_t* d_counts, cudaStream_t st) {
+  if (ix->n == 0) {  // empty index -> empty outcomes (FlatScanAdapter.java:117-122)
+    fill_empty(nq, k, d_ids, d_scores, d_counts, st);
+    return VX_OK;
+  }
+  const int kk = (int)std::min<int64_t>(k, ix->n);
+  if (kk < k) fill_empty(nq, k, d_ids, d_scores, d_counts, st);
+  // outputs are written with row stride k; run with kk and re-stride when needed
+  auto run_k = [&](auto&& fn) -> int {
+    if (kk == k) return fn(k, d_ids, d_scores, d_counts);
+    Scratch S(st);
+    int32_t* ti = S.alloc<int32_t>((size_t)nq * kk);
+    float* ts = S.alloc<float>((size_t)nq * kk);
+    int rc = fn(kk, ti, ts, d_counts);
+    if (rc != VX_OK) return rc;
+    VX_CUDA(cudaMemcpy2DAsync(d_ids, (size_t)k * 4, ti, (size_t)kk * 4, (size_t)kk * 4, nq,
+                              cudaMemcpyDeviceToDevice, st));
+    VX_CUDA(cudaMemcpy2DAsync(d_scores, (size_t)k * 4, ts, (size_t)kk * 4, (size_t)kk * 4, nq,
+                              cudaMemcpyDeviceToDevice, st));
+    return VX_OK;
+  };
+  switch (ix->kind) {
+    case VX_KIND_FLAT:
+      return run_k([&](int kq, int32_t* i, float* s, int32_t* c) {
+        return search_gemm_exact(ix, dq, nq, kq, i, s, c, st);
+      });
+    case VX_KIND_FP16:
+    case VX_KIND_SQ8:
+    case VX_KIND_BQ: {
+      if (!ix->rows32)
+        return fail(VX_ERR_UNSUPPORTED,
+                    "searchBatch on a quantized index needs the full-precision vectors at build; "
+                    "use vx_scan_candidates for the compressed scores alone");
+      if (oqf <= 1.0f) {
+        // QuantizedFlatScanAdapter.java:67-69: delegate to the exact flat scan.
+        vx_index* view = flat_view(ix);
+        return run_k([&](int kq, int32_t* i, float* s, int32_t* c) {
+          return search_gemm_exact(view, dq, nq, kq, i, s, c, st);
+        });
+      }
+      // candidateK = min(n, max(k, ceil(k * overQueryFactor)))  (QuantizedFlatScanAdapter.java:71)
+      const int64_t ck = std::min<int64_t>(
+          ix->n, std::max<int64_t>(k, (int64_t)std::ceil((double)((float)k * oqf))));
+      if (ix->kind == VX_KIND_FP16) {
+        return run_k([&](int kq, int32_t* i, float* s, int32_t* c) {
+          return search_fp16_two_pass(ix, dq, nq, (int)ck, kq, i, s, c, st);
+        });
+      }
+      return run_k([&](int kq, int32_t* i, float* s, int32_t* c) {
+        return search_quantized_scan(ix, dq, nq, (int)ck, kq, true, i, s, c, st);
+      });
+    }
+    case VX_KIND_IVFPQ: {
+      // IvfPqAdapter.search (IvfPqAdapter.java:124-158)
+      const int eff = sls > 0 ? sls : ix->nprobe;
+      const bool two = oqf > 1.0f;
+      const int probes = two ? (int)std::min<int64_t>((int64_t)std::ceil((double)((float)eff * oqf)), ix->nlist)
+                             : std::min(eff, ix->nlist);
+      const int rf = two ? std::max(ix->rescore, (int)std::ceil((double)((float)ix->rescore * oqf)))
+                         : ix->rescore;
+      return search_ivfpq(ix, dq, nq, k, probes, rf, -3.4028235e38f, d_ids, d_scores, d_counts, st);
+    }
+    default:
+      return fail(VX_ERR_INVALID_ARGUMENT, "unknown index kind");
+  }
+}
+
+// Host-buffer wrapper: copies queries in, runs on the calling thread's stream, copies out.
+template <class Fn>
+int with_host_buffers(vx_index* ix, const float* queries, int nq, int dim, int k, int32_t* ids,
+                      float* scores, int32_t* counts, Fn&& fn) {
+  VX_CUDA(cudaSetDevice(ix->device));
+  cudaStream_t st = cudaStreamPerThread;
+  int rc;
+  {
+    Scratch S(st);
+    const int qdim = ix->n > 0 ? ix->dim : dim;
+    float* dq = S.alloc<float>((size_t)nq * qdim);
+    int32_t* di = S.alloc<int32_t>((size_t)nq * k);
+    float* ds = S.alloc<float>((size_t)nq * k);
+    int32_t* dc = S.alloc<int32_t>(nq);
+    VX_CUDA(cudaMemcpyAsync(dq, queries, (size_t)nq * qdim * 4, cudaMemcpyHostToDevice, st));
+    rc = fn(dq, di, ds, dc, st);
+    if (rc == VX_OK) {
+      VX_CUDA(cudaMemcpyAsync(ids, di, (size_t)nq * k * 4, cudaMemcpyDeviceToHost, st));
+      VX_CUDA(cudaMemcpyAsync(scores, ds, (size_t)nq * k * 4, cudaMemcpyDeviceToHost, st));
+      VX_CUDA(cudaMemcpyAsync(counts, dc, (size_t)nq * 4, cudaMemcpyDeviceToHost, st));
+    }
+  }
+  VX_CUDA(cudaStreamSynchronize(st));
+  return rc;
+}
+
+}  // namespace
+}  // namespace vx
+
+// ======================================================================== C ABI
+extern "C" {
+
+int vx_abi_version(void) { return VX_ABI_VERSION; }
+
+const char* vx_last_error(void) { return g_last_error.c_str(); }
+
+int vx_debug_fail_next(int32_t status) {
+  g_fail_next = status;
+  return VX_OK;
+}
+
+int vx_kernel_launches(int64_t* count) {
+  if (!count) return fail(VX_ERR_NULL_POINTER, "count must not be null");
+  *count = g_launches.load();
+  return VX_OK;
+}
+
+int vx_device_count(int32_t* count) {
+  return guarded([&]() -> int {
+    if (!count) return fail(VX_ERR_NULL_POINTER, "count must not be null");
+    int c = 0;
+    cudaError_t e = cudaGetDeviceCount(&c);
+    *count = (e == cudaSuccess) ? c : 0;
+    return VX_OK;
+  });
+}
+
+int vx_flat_build(int32_t device, const float* vectors, int64_t n, int32_t dim, int64_t row_stride,
+                  int32_t metric, vx_index** out) {
+  return guarded([&]() -> int {
+    if (!out) return fail(VX_ERR_NULL_POINTER, "out must not be null");
+    *out = nullptr;
+    if (n > 0 && !vectors) return fail(VX_ERR_NULL_POINTER, "vectors must not be null");
+    if (n < 0 || n > INT32_MAX) return fail(VX_ERR_INVALID_ARGUMENT, "bad vector count %lld", (long long)n);
+    if (n > 0 && (dim <= 0 || row_stride < dim))
+      return fail(VX_ERR_INVALID_ARGUMENT, "bad dimension %d / stride %lld", dim, (long long)row_stride);
+    if (int s = check_metric(metric)) return s;
+    int nsms = 0;
+    if (int s = check_device(device, &nsms)) return s;
+    vx_index* ix = new vx_index();
+    ix->kind = VX_KIND_FLAT;
+    ix->device = device;
+    ix->metric = metric;
+    ix->n = n;
+    ix->dim = n > 0 ? dim : 0;
+    ix->num_sms = nsms;
+    try {
+      if (n > 0) {
+        ix->rows32 = upload_rows32(ix, vectors, n, dim, row_stride);
+        build_unit_f16(ix);
+      }
+    } catch (...) {
+      free_index(ix);
+      throw;
+    }
+    *out = ix;
+    return VX_OK;
+  });
+}
+
+int vx_fp16_build(int32_t device, const uint16_t* codes, int64_t n, int32_t dim, int32_t metric,
+                  const float* vectors, int64_t row_stride, vx_index** out) {
+  return guarded([&]() -> int {
+    if (!out) return fail(VX_ERR_NULL_POINTER, "out must not be null");
+    *out = nullptr;
+    if (n > 0 && !codes) return fail(VX_ERR_NULL_POINTER, "codes must not be null");
+    if (n < 0 || n > INT32_MAX) return fail(VX_ERR_INVALID_ARGUMENT, "bad vector count");
+    if (n > 0 && dim <= 0) return fail(VX_ERR_INVALID_ARGUMENT, "bad dimension %d", dim);
+    if (vectors && row_stride < dim) return fail(VX_ERR_INVALID_ARGUMENT, "bad row stride");
+    if (int s = check_metric(metric)) return s;
+    int nsms = 0;
+    if (int s = check_device(device, &nsms)) return s;
+    vx_index* ix = new vx_index();
+    ix->kind = VX_KIND_FP16;
+    ix->device = device;
+    ix->metric = metric;
+    ix->n = n;
+    ix->dim = n > 0 ? dim : 0;
+    ix->num_sms = nsms;
+    try {
+      if (n > 0) {
+        ix->Dp = (int)round_up(dim, 64);
+        __half* raw = nullptr;
+        VX_CUDA(cudaMalloc(&raw, (size_t)n * dim * 2));
+        VX_CUDA(cudaMemcpy(raw, codes, (size_t)n * dim * 2, cudaMemcpyHostToDevice));
+        ix->rows16 = dev_alloc<__half>(ix, (size_t)n * ix->Dp);
+        ix->rowsq = dev_alloc<float>(ix, (size_t)n);
+        ix->rowscale = dev_alloc<float>(ix, (size_t)n);
+        ix->max_norm = dev_alloc<float>(ix, 1);
+        VX_CUDA(cudaMemset(ix->max_norm, 0, 4));
+        std::vector<float> ones((size_t)n, 1.0f);
+        VX_CUDA(cudaMemcpy(ix->rowscale, ones.data(), (size_t)n * 4, cudaMemcpyHostToDevice));
+        VX_LAUNCH(1, launch_f16_rows_pad(raw, n, dim, ix->Dp, ix->rows16, ix->rowsq, ix->max_norm, 0));
+        VX_CUDA(cudaDeviceSynchronize());
+        cudaFree(raw);
+        make_tmap(&ix->tm_rows, ix->rows16, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, ix->Dp, n, 256);
+        ix->has_tm_rows = true;
+        if (vectors) ix->rows32 = upload_rows32(ix, vectors, n, dim, row_stride);
+      }
+    } catch (...) {
+      free_index(ix);
+      throw;
+    }
+    *out = ix;
+    return VX_OK;
+  });
+}
+
+int vx_sq8_build(int32_t device, const int8_t* codes, const float* corrections, int64_t n,
+                 int32_t dim, float min_quantile, float max_quantile, int32_t metric,
+                 const float* vectors, int64_t row_stride, vx_index** out) {
+  return guarded([&]() -> int {
+    if (!out) return fail(VX_ERR_NULL_POINTER, "out must not be null");
+    *out = nullptr;
+    if (n > 0 && (!codes || !corrections)) return fail(VX_ERR_NULL_POINTER, "codes/corrections must not be null");
+    if (n < 0 || n > INT32_MAX) return fail(VX_ERR_INVALID_ARGUMENT, "bad vector count");
+    if (n > 0 && dim <= 0) return fail(VX_ERR_INVALID_ARGUMENT, "bad dimension %d", dim);
+    if (!(min_quantile < max_quantile))
+      return fail(VX_ERR_INVALID_ARGUMENT, "minQuantile must be < maxQuantile: %g >= %g",
+                  (double)min_quantile, (double)max_quantile);
+    if (vectors && row_stride < dim) return fail(VX_ERR_INVALID_ARGUMENT, "bad row stride");
+    if (int s = check_metric(metric)) return s;
+    int nsms = 0;
+    if (int s = check_device(device, &nsms)) return s;
+    vx_index* ix = new vx_index();
+    ix->kind = VX_KIND_SQ8;
+    ix->device = device;
+    ix->metric = metric;
+    ix->n = n;
+    ix->dim = n > 0 ? dim : 0;
+    ix->num_sms = nsms;
+    ix->min_q = min_quantile;
+    ix->max_q = max_quantile;
+    try {
+      if (n > 0) {
+        ix->Dp8 = (int)round_up(dim, 128);
+        int8_t* raw = nullptr;
+        VX_CUDA(cudaMalloc(&raw, (size_t)n * dim));
+        VX_CUDA(cudaMemcpy(raw, codes, (size_t)n * dim, cudaMemcpyHostToDevice));
+        ix->codes8 = dev_alloc<int8_t>(ix, (size_t)n * ix->Dp8);
+        ix->vsq = dev_alloc<int32_t>(ix, (size_t)n);
+        ix->vcorr = dev_alloc<float>(ix, (size_t)n);
+        VX_CUDA(cudaMemcpy(ix->vcorr, corrections, (size_t)n * 4, cudaMemcpyHostToDevice));
+        VX_LAUNCH(1, launch_sq8_rows_pad(raw, n, dim, ix->Dp8, ix->codes8, ix->vsq, 0));
+        VX_CUDA(cudaDeviceSynchronize());
+        cudaFree(raw);
+        make_tmap(&ix->tm_codes8, ix->codes8, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, ix->Dp8, n, 256);
+        if (vectors) ix->rows32 = upload_rows32(ix, vectors, n, dim, row_stride);
+      }
+    } catch (...) {
+      free_index(ix);
+      throw;
+    }
+    *out = ix;
+    return VX_OK;
+  });
+}
+
+int vx_bq_build(int32_t device, const uint64_t* words, int64_t n, int32_t dim, int32_t metric,
+                const float* vectors, int64_t row_stride, vx_index** out) {
+  return guarded([&]() -> int {
+    if (!out) return fail(VX_ERR_NULL_POINTER, "out must not be null");
+    *out = nullptr;
+    if (n > 0 && !words) return fail(VX_ERR_NULL_POINTER, "words must not be null");
+    if (n < 0 || n > INT32_MAX) return fail(VX_ERR_INVALID_ARGUMENT, "bad vector count");
+    if (n > 0 && dim <= 0) return fail(VX_ERR_INVALID_ARGUMENT, "bad dimension %d", dim);
+    const int nw = (dim + 63) / 64;
+    const int nwp = bq_padded_words(nw);
+    if (n > 0 && nwp < 0) return fail(VX_ERR_UNSUPPORTED, "dimension %d exceeds 2048 bits", dim);
+    if (vectors && row_stride < dim) return fail(VX_ERR_INVALID_ARGUMENT, "bad row stride");
+    if (int s = check_metric(metric)) return s;
+    int nsms = 0;
+    if (int s = check_device(device, &nsms)) return s;
+    vx_index* ix = new vx_index();
+    ix->kind = VX_KIND_BQ;
+    ix->device = device;
+    ix->metric = metric;
+    ix->n = n;
+    ix->dim = n > 0 ? dim : 0;
+    ix->num_sms = nsms;
+    ix->nw_pad = nwp;
+    try {
+      if (n > 0) {
+        ix->words = dev_alloc<uint64_t>(ix, (size_t)n * nwp);
+        VX_CUDA(cudaMemset(ix->words, 0, (size_t)n * nwp * 8));
+        VX_CUDA(cudaMemcpy2D(ix->words, (size_t)nwp * 8, words, (size_t)nw * 8, (size_t)nw * 8, (size_t)n,
+                             cudaMemcpyHostToDevice));
+        if (vectors) ix->rows32 = upload_rows32(ix, vectors, n, dim, row_stride);
+      }
+    } catch (...) {
+      free_index(ix);
+      throw;
+    }
+    *out = ix;
+    return VX_OK;
+  });
+}
+
+int vx_ivfpq_build(int32_t device, const float* centroids, int32_t nlist, int32_t dim,
+                   const int64_t* list_offsets, const int32_t* list_ordinals, int32_t m, int32_t ks,
+                   const float* codebooks, const uint8_t* codes, int64_t n, int32_t metric,
+                   const float* vectors, int32_t nprobe, int32_t rescore_factor, vx_index** out) {
+  return guarded([&]() -> int {
+    if (!out) return fail(VX_ERR_NULL_POINTER, "out must not be null");
+    *out = nullptr;
+    if (!centroids || !list_offsets || !codebooks) return fail(VX_ERR_NULL_POINTER, "null IVF-PQ component");
+    if (n > 0 && (!list_ordinals || !codes)) return fail(VX_ERR_NULL_POINTER, "null IVF-PQ component");
+    if (nlist <= 0 || dim <= 0 || n < 0 || n > INT32_MAX)
+      return fail(VX_ERR_INVALID_ARGUMENT, "bad IVF shape nlist=%d dim=%d n=%lld", nlist, dim, (long long)n);
+    if (m <= 0 || m > dim) return fail(VX_ERR_INVALID_ARGUMENT, "numSubspaces must be in [1, dim]: %d", m);
+    if (ks <= 0 || ks > 256) return fail(VX_ERR_INVALID_ARGUMENT, "numClusters must be in [1, 256]: %d", ks);
+    if (nprobe <= 0) return fail(VX_ERR_INVALID_ARGUMENT, "nprobe must be positive: %d", nprobe);
+    if (rescore_factor < 1) return fail(VX_ERR_INVALID_ARGUMENT, "rescoreFactor must be >= 1: %d", rescore_factor);
+    if (int s = check_metric(metric)) return s;
+    if (list_offsets[0] != 0 || list_offsets[nlist] != n)
+      return fail(VX_ERR_INVALID_ARGUMENT, "list offsets must run from 0 to n");
+    for (int l = 0; l < nlist; l++)
+      if (list_offsets[l + 1] < list_offsets[l]) return fail(VX_ERR_INVALID_ARGUMENT, "list offsets must be non-decreasing");
+    for (int64_t i = 0; i < n; i++)
+      if (list_ordinals[i] < 0 || list_ordinals[i] >= n)
+        return fail(VX_ERR_INVALID_ARGUMENT, "list ordinal %d out of range", list_ordinals[i]);
+    int nsms = 0;
+    if (int s = check_device(device, &nsms)) return s;
+    vx_index* ix = new vx_index();
+    ix->kind = VX_KIND_IVFPQ;
+    ix->device = device;
+    ix->metric = metric;
+    ix->n = n;
+    ix->dim = dim;
+    ix->num_sms = nsms;
+    ix->nlist = nlist;
+    ix->M = m;
+    ix->Ks = ks;
+    ix->Mp = (int)round_up(m, 16);
+    ix->nprobe = nprobe;
+    ix->rescore = rescore_factor;
+    try {
+      ix->cent = dev_alloc<float>(ix, (size_t)nlist * dim);
+      VX_CUDA(cudaMemcpy(ix->cent, centroids, (size_t)nlist * dim * 4, cudaMemcpyHostToDevice));
+      ix->list_off = dev_alloc<int64_t>(ix, (size_t)nlist + 1);
+      VX_CUDA(cudaMemcpy(ix->list_off, list_offsets, (size_t)(nlist + 1) * 8, cudaMemcpyHostToDevice));
+      // subspaces (ProductQuantizer.computeSubspaceSizesAndOffsets, ProductQuantizer.java:686-700)
+      std::vector<int32_t> sub(2 * (size_t)m);
+      std::vector<int64_t> cboff(m);
+      int base = dim / m, rem = dim % m, off = 0;
+      int64_t co = 0;
+      for (int i = 0; i < m; i++) {
+        int size = base + (i < rem ? 1 : 0);
+        sub[2 * i] = size;
+        sub[2 * i + 1] = off;
+        cboff[i] = co;
+        off += size;
+        co += (int64_t)ks * size;
+      }
+      ix->sub = dev_alloc<int32_t>(ix, sub.size());
+      VX_CUDA(cudaMemcpy(ix->sub, sub.data(), sub.size() * 4, cudaMemcpyHostToDevice));
+      ix->cb_off = dev_alloc<int64_t>(ix, cboff.size());
+      VX_CUDA(cudaMemcpy(ix->cb_off, cboff.data(), cboff.size() * 8, cudaMemcpyHostToDevice));
+      ix->codebooks = dev_alloc<float>(ix, (size_t)co);
+      VX_CUDA(cudaMemcpy(ix->codebooks, codebooks, (size_t)co * 4, cudaMemcpyHostToDevice));
+      // codes regrouped list-contiguous, rows padded to Mp bytes
+      ix->ordinals = dev_alloc<int32_t>(ix, (size_t)std::max<int64_t>(n, 1));
+      ix->pq_codes = dev_alloc<uint8_t>(ix, (size_t)std::max<int64_t>(n, 1) * ix->Mp);
+      if (n > 0) {
+        VX_CUDA(cudaMemcpy(ix->ordinals, list_ordinals, (size_t)n * 4, cudaMemcpyHostToDevice));
+        std::vector<uint8_t> grouped((size_t)n * ix->Mp, 0);
+        for (int64_t i = 0; i < n; i++)
+          std::memcpy(&grouped[(size_t)i * ix->Mp], codes + (size_t)list_ordinals[i] * m, (size_t)m);
+        VX_CUDA(cudaMemcpy(ix->pq_codes, grouped.data(), grouped.size(), cudaMemcpyHostToDevice));
+      }
+      if (vectors && n > 0) ix->rows32 = upload_rows32(ix, vectors, n, dim, dim);
+    } catch (...) {
+      free_index(ix);
+      throw;
+    }
+    *out = ix;
+    return VX_OK;
+  });
+}
+
+int vx_index_info(const vx_index* ix, int32_t* kind, int64_t* size, int32_t* dim, int32_t* metric) {
+  if (!ix) return fail(VX_ERR_NULL_POINTER, "index must not be null");
+  if (kind) *kind = ix->kind;
+  if (size) *size = ix->n;
+  if (dim) *dim = ix->dim;
+  if (metric) *metric = ix->metric;
+  return VX_OK;
+}
+
+int vx_index_free(vx_index* ix) {
+  return guarded([&]() -> int {
+    free_index(ix);
+    return VX_OK;
+  });
+}
+
+int vx_search_batch_device(vx_index* ix, const float* d_queries, int32_t nq, int32_t dim, int32_t k,
+                           int32_t sls, float oqf, int32_t* d_ids, float* d_scores,
+                           int32_t* d_counts, void* stream) {
+  return guarded([&]() -> int {
+    if (int s = validate_search(ix, d_queries, nq, dim, k, d_ids, d_scores, d_counts)) return s;
+    VX_CUDA(cudaSetDevice(ix->device));
+    return search_batch_dev(ix, d_queries, nq, dim, k, sls, oqf, d_ids, d_scores, d_counts,
+                            (cudaStream_t)stream);
+  });
+}
+
+int vx_search_batch(vx_index* ix, const float* queries, int32_t nq, int32_t dim, int32_t k,
+                    int32_t sls, float oqf, int32_t* ids, float* scores, int32_t* counts) {
+  return guarded([&]() -> int {
+    if (int s = validate_search(ix, queries, nq, dim, k, ids, scores, counts)) return s;
+    return with_host_buffers(ix, queries, nq, dim, k, ids, scores, counts,
+                             [&](float* dq, int32_t* di, float* ds, int32_t* dc, cudaStream_t st) {
+                               return search_batch_dev(ix, dq, nq, dim, k, sls, oqf, di, ds, dc, st);
+                             });
+  });
+}
+
+static int scan_candidates_dev(vx_index* ix, const float* dq, int nq, int dim, int k, int32_t* di,
+                               float* ds, int32_t* dc, cudaStream_t st) {
+  if (ix->kind != VX_KIND_SQ8 && ix->kind != VX_KIND_BQ && ix->kind != VX_KIND_FP16)
+    return fail(VX_ERR_UNSUPPORTED, "candidate scans apply to SQ8, BQ and FP16 indexes");
+  if (ix->n == 0) {
+    fill_empty(nq, k, di, ds, dc, st);
+    return VX_OK;
+  }
+  const int kk = (int)std::min<int64_t>(k, ix->n);
+  if (kk < k) fill_empty(nq, k, di, ds, dc, st);
+  Scratch S(st);
+  int32_t* ti = di;
+  float* ts = ds;
+  if (kk < k) {
+    ti = S.alloc<int32_t>((size_t)nq * kk);
+    ts = S.alloc<float>((size_t)nq * kk);
+  }
+  int rc = (ix->kind == VX_KIND_FP16) ? search_gemm_exact(ix, dq, nq, kk, ti, ts, dc, st)
+                                      : search_quantized_scan(ix, dq, nq, kk, kk, false, ti, ts, dc, st);
+  if (rc != VX_OK) return rc;
+  if (kk < k) {
+    VX_CUDA(cudaMemcpy2DAsync(di, (size_t)k * 4, ti, (size_t)kk * 4, (size_t)kk * 4, nq,
+                              cudaMemcpyDeviceToDevice, st));
+    VX_CUDA(cudaMemcpy2DAsync(ds, (size_t)k * 4, ts, (size_t)kk * 4, (size_t)kk * 4, nq,
+                              cudaMemcpyDeviceToDevice, st));
+  }
+  return VX_OK;
+}
+
+int vx_scan_candidates_device(vx_index* ix, const float* d_queries, int32_t nq, int32_t dim,
+                              int32_t k, int32_t* d_ids, float* d_scores, int32_t* d_counts,
+                              void* stream) {
+  return guarded([&]() -> int {
+    if (int s = validate_search(ix, d_queries, nq, dim, k, d_ids, d_scores, d_counts)) return s;
+    VX_CUDA(cudaSetDevice(ix->device));
+    return scan_candidates_dev(ix, d_queries, nq, dim, k, d_ids, d_scores, d_counts,
+                               (cudaStream_t)stream);
+  });
+}
+
+int vx_scan_candidates(vx_index* ix, const float* queries, int32_t nq, int32_t dim, int32_t k,
+                       int32_t* ids, float* scores, int32_t* counts) {
+  return guarded([&]() -> int {
+    if (int s = validate_search(ix, queries, nq, dim, k, ids, scores, counts)) return s;
+    return with_host_buffers(ix, queries, nq, dim, k, ids, scores, counts,
+                             [&](float* dq, int32_t* di, float* ds, int32_t* dc, cudaStream_t st) {
+                               return scan_candidates_dev(ix, dq, nq, dim, k, di, ds, dc, st);
+                             });
+  });
+}
+
+static int ivfpq_dev(vx_index* ix, const float* dq, int nq, int k, int nprobe, int rf, float min_score,
+                     int32_t* di, float* ds, int32_t* dc, cudaStream_t st) {
+  if (ix->kind != VX_KIND_IVFPQ) return fail(VX_ERR_UNSUPPORTED, "not an IVF-PQ index");
+  if (nprobe < 1) return fail(VX_ERR_INVALID_ARGUMENT, "nprobe must be >= 1, got %d", nprobe);
+  if (rf < 1) return fail(VX_ERR_INVALID_ARGUMENT, "rescoreFactor must be >= 1, got %d", rf);
+  if (ix->n == 0) {
+    fill_empty(nq, k, di, ds, dc, st);
+    return VX_OK;
+  }
+  return search_ivfpq(ix, dq, nq, k, nprobe, rf, min_score, di, ds, dc, st);
+}
+
+int vx_ivfpq_search_device(vx_index* ix, const float* d_queries, int32_t nq, int32_t dim, int32_t k,
+                           int32_t nprobe, int32_t rf, float min_score, int32_t* d_ids,
+                           float* d_scores, int32_t* d_counts, void* stream) {
+  return guarded([&]() -> int {
+    if (int s = validate_search(ix, d_queries, nq, dim, k, d_ids, d_scores, d_counts)) return s;
+    VX_CUDA(cudaSetDevice(ix->device));
+    return ivfpq_dev(ix, d_queries, nq, k, nprobe, rf, min_score, d_ids, d_scores, d_counts,
+                     (cudaStream_t)stream);
+  });
+}
+
+int vx_ivfpq_search(vx_index* ix, const float* queries, int32_t nq, int32_t dim, int32_t k,
+                    int32_t nprobe, int32_t rf, float min_score, int32_t* ids, float* scores,
+                    int32_t* counts) {
+  return guarded([&]() -> int {
+    if (int s = validate_search(ix, queries, nq, dim, k, ids, scores, counts)) return s;
+    return with_host_buffers(ix, queries, nq, dim, k, ids, scores, counts,
+                             [&](float* dq, int32_t* di, float* ds, int32_t* dc, cudaStream_t st) {
+                               return ivfpq_dev(ix, dq, nq, k, nprobe, rf, min_score, di, ds, dc, st);
+                             });
+  });
+}
+
+int vx_merge_shards_device(int32_t device, int32_t nshards, const int64_t* d_offsets,
+                           const int32_t* d_shard_ids, const float* d_shard_scores,
+                           const int32_t* d_shard_counts, int32_t kin, int32_t nq, int32_t k,
+                           int32_t* d_ids, float* d_scores, int32_t* d_counts, void* stream) {
+  return guarded([&]() -> int {
+    if (!d_offsets || !d_shard_ids || !d_shard_scores || !d_shard_counts || !d_ids || !d_scores || !d_counts)
+      return fail(VX_ERR_NULL_POINTER, "null buffer");
+    if (nshards <= 0) return fail(VX_ERR_INVALID_ARGUMENT, "shards must not be empty");
+    if (kin <= 0 || k <= 0 || nq <= 0) return fail(VX_ERR_INVALID_ARGUMENT, "bad merge shape");
+    VX_CUDA(cudaSetDevice(device));
+    VX_LAUNCH(1, launch_merge_shards(nshards, d_offsets, d_shard_ids, d_shard_scores, d_shard_counts,
+                                     kin, nq, k, d_ids, d_scores, d_counts, (cudaStream_t)stream));
+    return VX_OK;
+  });
+}
+
+}  // extern "C"

@@ -1,0 +1,379 @@
+"""Host-side mirror of the reference's index SPI over the libvx.so C ABI.
+
+Names, argument meaning and error behaviour follow
+``vectors-db/src/main/java/com/integrallis/vectors/db/index/IndexSpi.java`` and its scan
+adapters, so a caller of ``FlatScanAdapter`` / ``QuantizedFlatScanAdapter`` / ``IvfPqAdapter``
+/ ``IndexShards`` finds the same contract here, with the scans running on a B200:
+
+* ``build(vectors, metric)``                         IndexSpi.java:43
+* ``search(query, k, search_list_size, oqf)``        IndexSpi.java:62
+* ``search_batch(queries, k, search_list_size, oqf)`` IndexSpi.java:127-152
+* ``size()`` / ``close()``                            IndexSpi.java:155-159
+* ``SearchOutcome(ordinals, scores)``                 IndexSpi.java:162-173
+
+Exceptions: ``IllegalArgumentException`` (bad k, empty batch, dimension mismatch),
+``NullPointerException`` (missing inputs), ``GpuUnavailableException`` (no usable GPU or a
+native failure, as CuVsBruteForceAdapter.java:67-70,86-89), ``UnsupportedOperationException``.
+Results are ordered by (score desc, ordinal asc).
+"""
+from __future__ import annotations
+
+import ctypes as C
+import enum
+import math
+from dataclasses import dataclass, field
+from typing import Optional, Sequence
+
+import numpy as np
+
+from . import _native as N
+
+
+class IllegalArgumentException(ValueError):
+    pass
+
+
+class NullPointerException(TypeError):
+    pass
+
+
+class GpuUnavailableException(RuntimeError):
+    pass
+
+
+class UnsupportedOperationException(NotImplementedError):
+    pass
+
+
+_EXC = {
+    N.VX_ERR_INVALID_ARGUMENT: IllegalArgumentException,
+    N.VX_ERR_NULL_POINTER: NullPointerException,
+    N.VX_ERR_GPU_UNAVAILABLE: GpuUnavailableException,
+    N.VX_ERR_CUDA: GpuUnavailableException,
+    N.VX_ERR_OUT_OF_MEMORY: GpuUnavailableException,
+    N.VX_ERR_UNSUPPORTED: UnsupportedOperationException,
+    N.VX_ERR_DEVICE_TIMEOUT: GpuUnavailableException,
+}
+
+
+def _check(status: int) -> None:
+    if status != N.VX_OK:
+        raise _EXC.get(status, GpuUnavailableException)(N.last_error())
+
+
+class SimilarityFunction(enum.IntEnum):
+    """vectors-core/.../SimilarityFunction.java:30-120 (ordinal order)."""
+
+    EUCLIDEAN = 0
+    DOT_PRODUCT = 1
+    COSINE = 2
+    MAXIMUM_INNER_PRODUCT = 3
+
+
+@dataclass
+class SearchOutcome:
+    """IndexSpi.SearchOutcome: ordinals and scores, descending."""
+
+    ordinals: np.ndarray
+    scores: np.ndarray
+
+    def __post_init__(self):
+        if len(self.ordinals) != len(self.scores):
+            raise IllegalArgumentException(
+                f"ordinals.length ({len(self.ordinals)}) must match scores.length ({len(self.scores)})"
+            )
+
+
+def _ptr(a: Optional[np.ndarray]):
+    return None if a is None else a.ctypes.data_as(C.c_void_p)
+
+
+def _as_matrix(vectors, name: str) -> np.ndarray:
+    if vectors is None:
+        raise NullPointerException(f"{name} must not be null")
+    a = np.ascontiguousarray(np.asarray(vectors, dtype=np.float32))
+    if a.ndim == 1 and a.size == 0:
+        a = a.reshape(0, 0)
+    if a.ndim != 2:
+        raise IllegalArgumentException(f"{name} must be a 2-D array of rows")
+    return a
+
+
+def _outcomes(ids: np.ndarray, scores: np.ndarray, counts: np.ndarray) -> list[SearchOutcome]:
+    return [SearchOutcome(ids[i, : counts[i]].copy(), scores[i, : counts[i]].copy()) for i in range(len(counts))]
+
+
+class _Handle:
+    """Owns one vx_index*."""
+
+    def __init__(self):
+        self.ptr = C.c_void_p()
+
+    def close(self):
+        if self.ptr:
+            N.lib().vx_index_free(self.ptr)
+            self.ptr = C.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class IndexSpi:
+    """Common search plumbing (IndexSpi.java:34-174)."""
+
+    def __init__(self, device: int = 0):
+        self.device = device
+        self._h = _Handle()
+        self._n = 0
+        self._dim = 0
+
+    # -- IndexSpi
+    def size(self) -> int:
+        return self._n
+
+    def close(self) -> None:
+        self._h.close()
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def search(self, query, k: int, search_list_size: int = 0, over_query_factor: float = 1.0) -> SearchOutcome:
+        if query is None:
+            raise NullPointerException("query must not be null")
+        if k <= 0:
+            raise IllegalArgumentException(f"k must be positive: {k}")
+        q = np.asarray(query, dtype=np.float32).reshape(1, -1)
+        return self.search_batch(q, k, search_list_size, over_query_factor)[0]
+
+    def search_batch(self, queries, k: int, search_list_size: int = 0, over_query_factor: float = 1.0) -> list[SearchOutcome]:
+        q = self._queries(queries, k)
+        if self._n == 0:
+            return [SearchOutcome(np.zeros(0, np.int32), np.zeros(0, np.float32)) for _ in range(len(q))]
+        ids, sc, cnt = self._alloc(len(q), k)
+        _check(
+            N.lib().vx_search_batch(
+                self._h.ptr, _ptr(q), len(q), q.shape[1], k, search_list_size, float(over_query_factor),
+                _ptr(ids), _ptr(sc), _ptr(cnt),
+            )
+        )
+        return _outcomes(ids, sc, cnt)
+
+    def search_batch_device(self, queries, k: int, search_list_size: int = 0, over_query_factor: float = 1.0, stream=None):
+        """searchBatch on device tensors (torch, cuda): returns (ids, scores, counts) tensors."""
+        import torch
+
+        q = queries.contiguous()
+        nq = q.shape[0]
+        ids = torch.empty((nq, k), dtype=torch.int32, device=q.device)
+        sc = torch.empty((nq, k), dtype=torch.float32, device=q.device)
+        cnt = torch.empty((nq,), dtype=torch.int32, device=q.device)
+        st = stream if stream is not None else torch.cuda.current_stream(q.device).cuda_stream
+        _check(
+            N.lib().vx_search_batch_device(
+                self._h.ptr, C.c_void_p(q.data_ptr()), nq, q.shape[1], k, search_list_size,
+                float(over_query_factor), C.c_void_p(ids.data_ptr()), C.c_void_p(sc.data_ptr()),
+                C.c_void_p(cnt.data_ptr()), C.c_void_p(st),
+            )
+        )
+        return ids, sc, cnt
+
+    # -- helpers
+    def _queries(self, queries, k: int) -> np.ndarray:
+        if queries is None:
+            raise NullPointerException("queries must not be null")
+        if len(queries) == 0:
+            raise IllegalArgumentException("queries must not be empty")
+        if k <= 0:
+            raise IllegalArgumentException(f"k must be positive: {k}")
+        if self._n == 0:
+            return np.zeros((len(queries), max(1, self._dim)), np.float32)
+        rows = []
+        for i, qi in enumerate(queries):
+            if qi is None:
+                raise NullPointerException(f"queries[{i}] must not be null")
+            a = np.asarray(qi, dtype=np.float32).reshape(-1)
+            if a.shape[0] != self._dim:
+                raise IllegalArgumentException(
+                    f"Query {i} dimension {a.shape[0]} does not match index dimension {self._dim}"
+                )
+            rows.append(a)
+        return np.ascontiguousarray(np.stack(rows))
+
+    @staticmethod
+    def _alloc(nq: int, k: int):
+        return (np.empty((nq, k), np.int32), np.empty((nq, k), np.float32), np.empty((nq,), np.int32))
+
+
+class FlatScanAdapter(IndexSpi):
+    """FlatScanAdapter (FlatScanAdapter.java:35-233): exact scan, searchListSize and
+    overQueryFactor ignored."""
+
+    def build(self, vectors, metric: SimilarityFunction) -> None:
+        if metric is None:
+            raise NullPointerException("metric must not be null")
+        v = _as_matrix(vectors, "vectors")
+        self._h.close()
+        n, dim = v.shape if v.size else (0, 0)
+        _check(N.lib().vx_flat_build(self.device, _ptr(v), n, dim, dim, int(metric), C.byref(self._h.ptr)))
+        self._n, self._dim, self.metric = n, dim, SimilarityFunction(metric)
+
+
+class QuantizedFlatScanAdapter(IndexSpi):
+    """QuantizedFlatScanAdapter (QuantizedFlatScanAdapter.java:27-177) over one of the
+    reference encodings.  ``search_batch`` applies the adapter's contract (overQueryFactor <= 1
+    -> exact scan; otherwise ceil(k * oqf) approximate candidates re-scored exactly), which needs
+    the fp32 rows; ``scan_candidates`` is selectApproximateCandidates alone."""
+
+    def __init__(self, device: int = 0):
+        super().__init__(device)
+        self.kind = None
+
+    def build_sq8(self, codes, corrections, min_quantile: float, max_quantile: float, metric, vectors=None):
+        codes = np.ascontiguousarray(np.asarray(codes, dtype=np.int8))
+        corr = np.ascontiguousarray(np.asarray(corrections, dtype=np.float32))
+        v = None if vectors is None else _as_matrix(vectors, "vectors")
+        n, dim = codes.shape
+        self._h.close()
+        _check(
+            N.lib().vx_sq8_build(self.device, _ptr(codes), _ptr(corr), n, dim, float(min_quantile), float(max_quantile),
+                                 int(metric), _ptr(v), dim, C.byref(self._h.ptr))
+        )
+        self._n, self._dim, self.metric, self.kind = n, dim, SimilarityFunction(metric), "SQ8"
+
+    def build_bq(self, words, dim: int, metric, vectors=None):
+        words = np.ascontiguousarray(np.asarray(words, dtype=np.uint64))
+        v = None if vectors is None else _as_matrix(vectors, "vectors")
+        n = words.shape[0]
+        self._h.close()
+        _check(N.lib().vx_bq_build(self.device, _ptr(words), n, dim, int(metric), _ptr(v), dim, C.byref(self._h.ptr)))
+        self._n, self._dim, self.metric, self.kind = n, dim, SimilarityFunction(metric), "BQ"
+
+    def build_fp16(self, codes, metric, vectors=None):
+        codes = np.ascontiguousarray(np.asarray(codes, dtype=np.uint16))
+        v = None if vectors is None else _as_matrix(vectors, "vectors")
+        n, dim = codes.shape
+        self._h.close()
+        _check(N.lib().vx_fp16_build(self.device, _ptr(codes), n, dim, int(metric), _ptr(v), dim, C.byref(self._h.ptr)))
+        self._n, self._dim, self.metric, self.kind = n, dim, SimilarityFunction(metric), "FP16"
+
+    def build(self, vectors, metric):
+        raise UnsupportedOperationException("QuantizedFlatScanAdapter wraps an already-built flat index")
+
+    def scan_candidates(self, queries, k: int) -> list[SearchOutcome]:
+        q = self._queries(queries, k)
+        if self._n == 0:
+            return [SearchOutcome(np.zeros(0, np.int32), np.zeros(0, np.float32)) for _ in range(len(q))]
+        ids, sc, cnt = self._alloc(len(q), k)
+        _check(N.lib().vx_scan_candidates(self._h.ptr, _ptr(q), len(q), q.shape[1], k, _ptr(ids), _ptr(sc), _ptr(cnt)))
+        return _outcomes(ids, sc, cnt)
+
+    def scan_candidates_device(self, queries, k: int, stream=None):
+        import torch
+
+        q = queries.contiguous()
+        nq = q.shape[0]
+        ids = torch.empty((nq, k), dtype=torch.int32, device=q.device)
+        sc = torch.empty((nq, k), dtype=torch.float32, device=q.device)
+        cnt = torch.empty((nq,), dtype=torch.int32, device=q.device)
+        st = stream if stream is not None else torch.cuda.current_stream(q.device).cuda_stream
+        _check(
+            N.lib().vx_scan_candidates_device(self._h.ptr, C.c_void_p(q.data_ptr()), nq, q.shape[1], k,
+                                              C.c_void_p(ids.data_ptr()), C.c_void_p(sc.data_ptr()),
+                                              C.c_void_p(cnt.data_ptr()), C.c_void_p(st))
+        )
+        return ids, sc, cnt
+
+
+class IvfPqAdapter(IndexSpi):
+    """IvfPqAdapter over a prebuilt IVF-PQ index (IvfIndex.fromPrebuilt, IvfIndex.java:343-351).
+    ``search_batch`` follows IvfPqAdapter.search (IvfPqAdapter.java:124-158); ``ivf_search`` is
+    IvfIndex.search(IvfSearchRequest) (IvfIndex.java:170-171,539-619)."""
+
+    def __init__(self, nprobe: int = 32, rescore_factor: int = 1, device: int = 0):
+        super().__init__(device)
+        if nprobe <= 0:
+            raise IllegalArgumentException(f"nprobe must be positive: {nprobe}")
+        if rescore_factor < 1:
+            raise IllegalArgumentException(f"rescoreFactor must be >= 1: {rescore_factor}")
+        self.nprobe, self.rescore_factor = nprobe, rescore_factor
+
+    def build(self, vectors, metric):
+        raise UnsupportedOperationException("k-means / PQ training is an offline step; use build_prebuilt")
+
+    def build_prebuilt(self, centroids, list_offsets, list_ordinals, codebooks, codes, m: int, ks: int, metric, vectors=None):
+        cent = _as_matrix(centroids, "centroids")
+        off = np.ascontiguousarray(np.asarray(list_offsets, dtype=np.int64))
+        ords = np.ascontiguousarray(np.asarray(list_ordinals, dtype=np.int32))
+        cb = np.ascontiguousarray(np.asarray(codebooks, dtype=np.float32))
+        codes = np.ascontiguousarray(np.asarray(codes, dtype=np.uint8))
+        v = None if vectors is None else _as_matrix(vectors, "vectors")
+        nlist, dim = cent.shape
+        n = codes.shape[0]
+        self._h.close()
+        _check(
+            N.lib().vx_ivfpq_build(self.device, _ptr(cent), nlist, dim, _ptr(off), _ptr(ords), m, ks, _ptr(cb), _ptr(codes),
+                                   n, int(metric), _ptr(v), self.nprobe, self.rescore_factor, C.byref(self._h.ptr))
+        )
+        self._n, self._dim, self.metric = n, dim, SimilarityFunction(metric)
+
+    def ivf_search(self, queries, k: int, nprobe: int, rescore_factor: int = 1, min_score: float = -3.4028235e38):
+        q = self._queries(queries, k)
+        if self._n == 0:
+            return [SearchOutcome(np.zeros(0, np.int32), np.zeros(0, np.float32)) for _ in range(len(q))]
+        ids, sc, cnt = self._alloc(len(q), k)
+        _check(
+            N.lib().vx_ivfpq_search(self._h.ptr, _ptr(q), len(q), q.shape[1], k, nprobe, rescore_factor, float(min_score),
+                                    _ptr(ids), _ptr(sc), _ptr(cnt))
+        )
+        return _outcomes(ids, sc, cnt)
+
+    def ivf_search_device(self, queries, k: int, nprobe: int, rescore_factor: int = 1,
+                          min_score: float = -3.4028235e38, stream=None):
+        import torch
+
+        q = queries.contiguous()
+        nq = q.shape[0]
+        ids = torch.empty((nq, k), dtype=torch.int32, device=q.device)
+        sc = torch.empty((nq, k), dtype=torch.float32, device=q.device)
+        cnt = torch.empty((nq,), dtype=torch.int32, device=q.device)
+        st = stream if stream is not None else torch.cuda.current_stream(q.device).cuda_stream
+        _check(
+            N.lib().vx_ivfpq_search_device(self._h.ptr, C.c_void_p(q.data_ptr()), nq, q.shape[1], k, nprobe,
+                                           rescore_factor, float(min_score), C.c_void_p(ids.data_ptr()),
+                                           C.c_void_p(sc.data_ptr()), C.c_void_p(cnt.data_ptr()), C.c_void_p(st))
+        )
+        return ids, sc, cnt
+
+
+def shard_offsets(n: int, shards: int) -> list[int]:
+    """IndexShards.build ordinal ranges: offsets[i] = n*i/s (IndexShards.java:64-81)."""
+    return [(n * i) // shards for i in range(shards + 1)]
+
+
+def merge_shards_device(shard_ids, shard_scores, shard_counts, offsets, k: int, stream=None):
+    """IndexShards.mergeWithOffsets on device tensors: shard_* are [S, nq, kin] / [S, nq]
+    int32/float32 tensors, offsets an int64 tensor of S shard starts.  Returns (ids, scores,
+    counts) for the k best by (score desc, ordinal asc)."""
+    import torch
+
+    S, nq, kin = shard_ids.shape
+    dev = shard_ids.device
+    ids = torch.empty((nq, k), dtype=torch.int32, device=dev)
+    sc = torch.empty((nq, k), dtype=torch.float32, device=dev)
+    cnt = torch.empty((nq,), dtype=torch.int32, device=dev)
+    st = stream if stream is not None else torch.cuda.current_stream(dev).cuda_stream
+    off = offsets.to(device=dev, dtype=torch.int64).contiguous()
+    _check(
+        N.lib().vx_merge_shards_device(dev.index or 0, S, C.c_void_p(off.data_ptr()), C.c_void_p(shard_ids.contiguous().data_ptr()),
+                                       C.c_void_p(shard_scores.contiguous().data_ptr()),
+                                       C.c_void_p(shard_counts.contiguous().data_ptr()), kin, nq, k,
+                                       C.c_void_p(ids.data_ptr()), C.c_void_p(sc.data_ptr()),
+                                       C.c_void_p(cnt.data_ptr()), C.c_void_p(st))
+    )
+    return ids, sc, cnt
