@@ -1,0 +1,547 @@
+"""Benchmark: queries/sec of the 10M x 768 FLAT (COSINE, fp32, top-10) batch scan, with the
+10M x 768 IVF-PQ (nlist 4096, M=96, nprobe 32, top-10) scan reported beside it.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+
+One process per GPU (torchrun for N > 1).  The database is split into contiguous ordinal
+ranges (IndexShards.build); every rank scans its range for the whole query batch, the
+per-rank top-10 lists are all-gathered over NCCL and merged on the device (IndexShards.
+mergeWithOffsets).  `value` = queries of the batch / step time (max over ranks, CUDA events,
+inputs resident in HBM); `e2e` = the same through the host-buffer C ABI call (queries copied
+in, results copied out inside the timed region).  `--impl reference` times the CPU
+restatement of the reference's Java path (the oracle) on the host cores instead.
+
+Synthetic data: seeded Gaussian mixtures with the reference benchmark's shapes (no dataset is
+needed); both arms draw from the same generator.
+"""
+from __future__ import annotations
+
+import argparse
+import concurrent.futures as cf
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+FLAT = dict(n=10_000_000, dim=768, comps=64, sigma=0.3, nq=10_000, k=10, metric=2)
+IVF = dict(n=10_000_000, dim=768, comps=1024, sigma=0.3, nq=10_000, k=10, nlist=4096, m=96, ks=256,
+           nprobe=32, train=500_000, pq_train=25_000)
+SEED_DB, SEED_Q, SEED_C = 0xC0FFEE01, 0xC0FFEE02, 0xC0FFEE03
+METRIC = "queries/sec, 10M x 768 FLAT COSINE top-10"
+CHUNK = 65536
+
+
+# ------------------------------------------------------------------ synthetic data
+def centres(comps, dim, seed):
+    return np.random.Generator(np.random.PCG64([seed, 0xCE])).standard_normal((comps, dim), dtype=np.float32)
+
+
+def gen_chunk(c, dim, cent, sigma, seed, normalize):
+    rng = np.random.Generator(np.random.PCG64([seed, c]))
+    comp = rng.integers(0, cent.shape[0], size=CHUNK)
+    x = cent[comp]
+    x += sigma * rng.standard_normal((CHUNK, dim), dtype=np.float32)
+    if normalize:
+        x /= np.linalg.norm(x, axis=1, keepdims=True)
+    return x
+
+
+def gen_rows(first, count, dim, cent, sigma, seed, normalize, sink=None, threads=None):
+    """Rows [first, first+count) of the seeded mixture; chunk-seeded, so any slice of the
+    global dataset is identical however it is split.  sink(offset, array) receives pieces."""
+    out = None if sink else np.empty((count, dim), np.float32)
+    c0, c1 = first // CHUNK, (first + count + CHUNK - 1) // CHUNK
+    threads = threads or min(32, os.cpu_count() or 4)
+
+    def work(c):
+        x = gen_chunk(c, dim, cent, sigma, seed, normalize)
+        lo, hi = max(first, c * CHUNK), min(first + count, (c + 1) * CHUNK)
+        return lo - first, x[lo - c * CHUNK: hi - c * CHUNK]
+
+    with cf.ThreadPoolExecutor(threads) as ex:
+        for off, piece in ex.map(work, range(c0, c1)):
+            if sink:
+                sink(off, piece)
+            else:
+                out[off: off + len(piece)] = piece
+    return out
+
+
+# ------------------------------------------------------------------ clocks
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, local_rank):
+        cvd = os.environ.get("CUDA_VISIBLE_DEVICES", "")
+        ids = [s.strip() for s in cvd.split(",") if s.strip()]
+        self.gpu = ids[local_rank] if local_rank < len(ids) else str(local_rank)
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", self.gpu, f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if not self.proc:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx.append(float(f[2]))
+            except ValueError:
+                continue
+            for nm, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ------------------------------------------------------------------ helpers
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return p["hbm_gbs"], p["bf16_tflops"], p["bf16_tflops_sustained"], "measured"
+    except Exception:
+        return 6650.0, 1590.0, 1400.0, "fallback"
+
+
+def cpu_flat_baseline(db_sample, q_sample, total_rows, metric):
+    """The oracle (CPU restatement of FlatScanAdapter.searchBatch) on a bounded sample."""
+    from oracle import oracle as O
+
+    th = os.cpu_count() or 1
+    t = time.perf_counter()
+    O.flat_search(db_sample, q_sample, metric, FLAT["k"], O.REFERENCE_HEAP, th)
+    dt = time.perf_counter() - t
+    qps = len(q_sample) / dt * (len(db_sample) / total_rows)
+    return qps, th, dt
+
+
+# ------------------------------------------------------------------ reference arm
+def run_reference(args, rank):
+    if rank != 0:
+        return 0
+    from oracle import oracle as O
+
+    O.lib()
+    rows = args.ref_rows
+    cent = centres(FLAT["comps"], FLAT["dim"], SEED_C)
+    db = gen_rows(0, rows, FLAT["dim"], cent, FLAT["sigma"], SEED_DB, True)
+    q = gen_rows(0, args.ref_queries, FLAT["dim"], cent, FLAT["sigma"], SEED_Q, True)
+    th = os.cpu_count() or 1
+    for _ in range(args.warmup):
+        O.flat_search(db, q[:4], FLAT["metric"], FLAT["k"], O.REFERENCE_HEAP, th)
+    times = []
+    for _ in range(args.steps):
+        t = time.perf_counter()
+        O.flat_search(db, q, FLAT["metric"], FLAT["k"], O.REFERENCE_HEAP, th)
+        times.append(time.perf_counter() - t)
+    step = sum(times) / len(times)
+    qps = args.ref_queries / step * (rows / FLAT["n"])
+    line = {
+        "impl": "reference",
+        "metric": METRIC,
+        "value": qps,
+        "unit": "queries/s",
+        "n_gpus": args.gpus,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": step * 1e3,
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic",
+        "config": {"workload": "FLAT COSINE fp32, n=10,000,000, dim=768, k=10", "n": FLAT["n"], "dim": FLAT["dim"],
+                   "k": FLAT["k"], "metric": "COSINE"},
+        "cpu_baseline": {"value": qps, "unit": "queries/s", "cores": th, "kind": "port",
+                         "sample": f"{args.ref_queries} queries x {rows:,} rows per step (first rows of the "
+                                   f"10M dataset); QPS scaled by rows/10,000,000"},
+        "e2e": {"value": qps, "unit": "queries/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ------------------------------------------------------------------ our arm
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--n", type=int, default=FLAT["n"])
+    ap.add_argument("--nq", type=int, default=FLAT["nq"])
+    ap.add_argument("--no-ivf", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--ivf-n", type=int, default=IVF["n"])
+    ap.add_argument("--ref-rows", type=int, default=1_000_000)
+    ap.add_argument("--ref-queries", type=int, default=48)
+    args = ap.parse_args()
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        return run_reference(args, rank)
+
+    import torch
+    import torch.distributed as dist
+
+    import vectors_b200 as vx
+    from vectors_b200 import _native as N
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+
+    def max_over_ranks(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    hbm_peak, tc_burst, tc_sustained, peak_kind = peaks()
+    n_total = args.n
+    offs = vx.shard_offsets(n_total, world)
+    lo, hi = offs[rank], offs[rank + 1]
+    dim, k, nq = FLAT["dim"], FLAT["k"], args.nq
+
+    # ---- FLAT data (this rank's ordinal range), generated straight into HBM
+    cent = centres(FLAT["comps"], dim, SEED_C)
+    rows = torch.empty((hi - lo, dim), dtype=torch.float32, device=dev)
+
+    def sink(off, piece):
+        rows[off: off + len(piece)].copy_(torch.from_numpy(np.ascontiguousarray(piece)), non_blocking=False)
+
+    gen_rows(lo, hi - lo, dim, cent, FLAT["sigma"], SEED_DB, True, sink=sink)
+    q_host = gen_rows(0, nq, dim, cent, FLAT["sigma"], SEED_Q, True)
+    q_pinned = torch.from_numpy(q_host).pin_memory()
+    q_dev = q_pinned.to(dev)
+
+    flat = vx.FlatScanAdapter(device=local)
+    flat.build(rows, vx.SimilarityFunction.COSINE)  # device rows: copied device-to-device
+    cpu_sample = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        cpu_sample = rows[: args.ref_rows].cpu().numpy()
+    del rows
+    torch.cuda.empty_cache()
+
+    off_t = torch.tensor(offs[:world], dtype=torch.int64, device=dev)
+
+    def flat_step():
+        ids, sc, cnt = flat.search_batch_device(q_dev, k)
+        if world == 1:
+            return ids, sc, cnt
+        gi = torch.empty((world, nq, k), dtype=torch.int32, device=dev)
+        gs = torch.empty((world, nq, k), dtype=torch.float32, device=dev)
+        gc = torch.empty((world, nq), dtype=torch.int32, device=dev)
+        dist.all_gather_into_tensor(gi, ids)
+        dist.all_gather_into_tensor(gs, sc)
+        dist.all_gather_into_tensor(gc, cnt)
+        return vx.merge_shards_device(gi, gs, gc, off_t, k)
+
+    for _ in range(args.warmup):
+        flat_step()
+    torch.cuda.synchronize()
+    barrier()
+    launches0 = vx.kernel_launches()
+    N.profile_reset()
+    N.profile_enable(True)
+    clocks = ClockSampler(local)
+    clocks.start()
+    torch.cuda.synchronize()
+    barrier()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record()
+    for _ in range(args.steps):
+        out = flat_step()
+    ev1.record()
+    torch.cuda.synchronize()
+    barrier()
+    clk = clocks.stop()
+    N.profile_enable(False)
+    prof = N.profile_read()
+    launches = vx.kernel_launches() - launches0
+    ms = max_over_ranks(ev0.elapsed_time(ev1) / args.steps)
+    qps = nq / (ms / 1e3)
+
+    # roofline of the dominant kernel: the tcgen05 scan (algorithmic flops 2 * nq * rows * dim)
+    g_ms, g_n = prof["gemm_scan"]
+    flops_step = 2.0 * nq * (hi - lo) * dim
+    gemm_ms_step = g_ms / args.steps
+    achieved = flops_step / (gemm_ms_step / 1e3) / 1e12 if gemm_ms_step > 0 else None
+    roofline = {
+        "bound": "tensor",
+        "achieved": achieved,
+        "peak": tc_sustained,
+        "unit": "TFLOP/s",
+        "frac": (achieved / tc_sustained) if achieved else None,
+        "traffic": None,
+        "kernel": "gemm_scan_kernel (tcgen05 kind::f16, fused top-K)",
+        "peak_source": f"{peak_kind} dense bf16/fp16 sustained",
+        "kernel_ms_per_step": gemm_ms_step,
+        "launches_per_step": g_n / args.steps,
+        "breakdown_ms_per_step": {kk: v[0] / args.steps for kk, v in prof.items() if v[1]},
+    }
+    traffic_path = os.path.join(ROOT, "profiles", "flat_gemm_scan_traffic.json")
+    if os.path.exists(traffic_path):
+        with open(traffic_path) as f:
+            tr = json.load(f)
+        roofline["traffic"] = tr.get("bytes_per_launch_full_size")
+
+    # ---- end to end through the host-buffer C ABI (queries in, results out every step)
+    q_np = q_pinned.numpy()
+
+    def e2e_step():
+        res = flat.search_batch(q_np, k)  # H2D queries, scan, D2H results (blocking)
+        if world == 1:
+            return res
+        # shard results meet through the same NCCL all-gather + device merge, then D2H
+        li = torch.full((nq, k), -1, dtype=torch.int32)
+        ls = torch.zeros((nq, k), dtype=torch.float32)
+        lc = torch.zeros((nq,), dtype=torch.int32)
+        for i, o in enumerate(res):
+            c = len(o.ordinals)
+            li[i, :c] = torch.from_numpy(o.ordinals)
+            ls[i, :c] = torch.from_numpy(o.scores)
+            lc[i] = c
+        gi = torch.empty((world, nq, k), dtype=torch.int32, device=dev)
+        gs = torch.empty((world, nq, k), dtype=torch.float32, device=dev)
+        gc = torch.empty((world, nq), dtype=torch.int32, device=dev)
+        dist.all_gather_into_tensor(gi, li.to(dev))
+        dist.all_gather_into_tensor(gs, ls.to(dev))
+        dist.all_gather_into_tensor(gc, lc.to(dev))
+        mi, ms_, mc = vx.merge_shards_device(gi, gs, gc, off_t, k)
+        return mi.cpu(), ms_.cpu(), mc.cpu()
+
+    e2e_step()
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        e2e_step()
+    torch.cuda.synchronize()
+    e2e_s = max_over_ranks((time.perf_counter() - t0) / args.steps)
+    h2d = nq * dim * 4 + (nq * k * 8 + nq * 4 if world > 1 else 0)
+    d2h = (nq * k * 8 + nq * 4) * (2 if world > 1 else 1)
+    e2e = {"value": nq / e2e_s, "unit": "queries/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+           "timing": "host wall clock around the blocking host-buffer call, max over ranks"}
+
+    # ---- CPU baseline (rank 0, N=1): the oracle on a bounded sample
+    cpu = None
+    if cpu_sample is not None:
+        qs = q_host[: args.ref_queries]
+        cqps, cores, dt = cpu_flat_baseline(cpu_sample, qs, n_total, FLAT["metric"])
+        cpu = {"value": cqps, "unit": "queries/s", "cores": cores, "kind": "port",
+               "sample": f"{len(qs)} queries x {len(cpu_sample):,} rows ({dt:.1f} s); QPS scaled by rows/{n_total:,}"}
+    flat.close()
+    torch.cuda.empty_cache()
+
+    # ---- IVF-PQ sub-result
+    ivf = None
+    if not args.no_ivf:
+        ivf = run_ivf(args, rank, world, local, dev, barrier, max_over_ranks, hbm_peak, peak_kind)
+
+    if rank == 0:
+        line = {
+            "metric": METRIC,
+            "value": qps,
+            "unit": "queries/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": ms,
+            "higher_is_better": True,
+            "scaling": "strong",
+            "vs_baseline": None,
+            "dtype": "f16-mma+f32-rescore",
+            "data": "synthetic",
+            "config": {"workload": f"FLAT COSINE fp32, n={n_total:,}, dim={dim}, queries={nq:,}, k={k}",
+                       "n": n_total, "dim": dim, "queries_per_step": nq, "k": k, "metric": "COSINE",
+                       "parallelism": f"row-sharded x{world}, NCCL all-gather + merge",
+                       "l2": "inputs larger than L2 (fp16 scan operand 15.4 GB)"},
+            "roofline": roofline,
+            "cpu_baseline": cpu,
+            "e2e": e2e,
+            "gpu_launches": launches,
+            "clocks": clk,
+            "ivf_pq": ivf,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier(device_ids=[local])
+        dist.destroy_process_group()
+    return 0
+
+
+def run_ivf(args, rank, world, local, dev, barrier, max_over_ranks, hbm_peak, peak_kind):
+    import torch
+    import torch.distributed as dist
+
+    import vectors_b200 as vx
+    from vectors_b200 import _native as N
+
+    P = IVF
+    n, dim, nlist, m, ks = args.ivf_n, P["dim"], P["nlist"], P["m"], P["ks"]
+    offs = vx.shard_offsets(n, world)
+    lo, hi = offs[rank], offs[rank + 1]
+    cent_mix = centres(P["comps"], dim, SEED_C ^ 0x1F)
+    g = torch.Generator(device=dev)
+    g.manual_seed(42)
+    # coarse centroids: k-means (10 Lloyd iterations) on a 500k-row sample, trained on rank 0
+    cent = torch.empty((nlist, dim), dtype=torch.float32, device=dev)
+    if rank == 0:
+        sample = torch.from_numpy(gen_rows(0, min(P["train"], n), dim, cent_mix, P["sigma"], SEED_DB ^ 0x1F, False)).to(dev)
+        cent.copy_(sample[torch.randperm(len(sample), generator=g, device=dev)[:nlist]])
+        for _ in range(10):
+            a = nearest(sample, cent)
+            s = torch.zeros_like(cent).index_add_(0, a, sample)
+            c = torch.bincount(a, minlength=nlist).clamp_min(1).unsqueeze(1).float()
+            cent = torch.where(torch.bincount(a, minlength=nlist).unsqueeze(1) > 0, s / c, cent)
+        del sample
+    if world > 1:
+        dist.broadcast(cent, 0)
+    # this rank's rows, their lists, residuals; PQ codebooks trained on rank 0's residuals
+    rows = torch.from_numpy(gen_rows(lo, hi - lo, dim, cent_mix, P["sigma"], SEED_DB ^ 0x1F, False)).to(dev)
+    assign = nearest(rows, cent)
+    books = torch.empty((m, ks, dim // m), dtype=torch.float32, device=dev)
+    if rank == 0:
+        pick = torch.randperm(len(rows), generator=g, device=dev)[: P["pq_train"]]
+        resid = (rows[pick] - cent[assign[pick]]).view(-1, m, dim // m).transpose(0, 1).contiguous()
+        books.copy_(pq_kmeans(resid, ks, g))
+    if world > 1:
+        dist.broadcast(books, 0)
+    codes = torch.empty((len(rows), m), dtype=torch.uint8, device=dev)
+    for s in range(0, len(rows), 32768):
+        r = (rows[s: s + 32768] - cent[assign[s: s + 32768]]).view(-1, m, dim // m).transpose(0, 1)
+        d = torch.cdist(r, books)  # [m, b, ks]
+        codes[s: s + 32768] = d.argmin(2).transpose(0, 1).to(torch.uint8)
+    order = torch.argsort(assign, stable=True).to(torch.int32)
+    counts = torch.bincount(assign, minlength=nlist)
+    loff = torch.zeros(nlist + 1, dtype=torch.int64, device=dev)
+    loff[1:] = torch.cumsum(counts, 0)
+    del rows
+    a = vx.IvfPqAdapter(nprobe=P["nprobe"], device=local)
+    a.build_prebuilt(cent.cpu().numpy(), loff.cpu().numpy(), order.cpu().numpy(), books.cpu().numpy().reshape(-1),
+                     codes.cpu().numpy(), m, ks, vx.SimilarityFunction.EUCLIDEAN)
+    nq, k = P["nq"], P["k"]
+    qh = gen_rows(0, nq, dim, cent_mix, P["sigma"], SEED_Q ^ 0x1F, False)
+    q = torch.from_numpy(qh).to(dev)
+    # algorithmic bytes: codes + ordinals of every probed list row, per query
+    dq = torch.cdist(q, cent)
+    probed = dq.topk(P["nprobe"], largest=False).indices
+    bytes_step = float(counts[probed].sum().item()) * (m + 4)
+    off_t = torch.tensor(offs[:world], dtype=torch.int64, device=dev)
+
+    def step():
+        ids, sc, cnt = a.ivf_search_device(q, k, P["nprobe"])
+        if world == 1:
+            return ids
+        gi = torch.empty((world, nq, k), dtype=torch.int32, device=dev)
+        gs = torch.empty((world, nq, k), dtype=torch.float32, device=dev)
+        gc = torch.empty((world, nq), dtype=torch.int32, device=dev)
+        dist.all_gather_into_tensor(gi, ids)
+        dist.all_gather_into_tensor(gs, sc)
+        dist.all_gather_into_tensor(gc, cnt)
+        return vx.merge_shards_device(gi, gs, gc, off_t, k)[0]
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    barrier()
+    N.profile_reset()
+    N.profile_enable(True)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    barrier()
+    N.profile_enable(False)
+    prof = N.profile_read()
+    ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
+    adc_ms = prof["adc_scan"][0] / args.steps
+    achieved = bytes_step / (adc_ms / 1e3) / 1e9 if adc_ms > 0 else None
+    a.close()
+    return {
+        "value": nq / (ms / 1e3),
+        "unit": "queries/s",
+        "ms_per_step": ms,
+        "config": {"workload": f"IVF-PQ EUCLIDEAN n={n:,} dim={dim} nlist={nlist} M={m} ks={ks} nprobe={P['nprobe']} "
+                               f"rescore=1 queries={nq:,} k={k}", "train": "torch k-means (10 iters, 500k sample), "
+                               "PQ k-means on 25k residuals"},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
+                     "frac": (achieved / hbm_peak) if achieved else None, "traffic": None,
+                     "kernel": "adc_scan_kernel", "peak_source": f"{peak_kind} HBM copy",
+                     "algorithmic_bytes_per_step": bytes_step,
+                     "breakdown_ms_per_step": {kk: v[0] / args.steps for kk, v in prof.items() if v[1]}},
+    }
+
+
+def nearest(x, c, chunk=131072):
+    import torch
+
+    out = torch.empty(len(x), dtype=torch.int64, device=x.device)
+    cn = (c * c).sum(1)
+    for s in range(0, len(x), chunk):
+        xs = x[s: s + chunk]
+        d = cn.unsqueeze(0) - 2.0 * (xs @ c.T)
+        out[s: s + chunk] = d.argmin(1)
+    return out
+
+
+def pq_kmeans(resid, ks, g, iters=10):
+    """Batched k-means over subspaces: resid [m, npts, sub] -> codebooks [m, ks, sub]."""
+    import torch
+
+    m, npts, sub = resid.shape
+    books = resid[:, torch.randperm(npts, generator=g, device=resid.device)[:ks]].clone()
+    for _ in range(iters):
+        a = torch.cdist(resid, books).argmin(2)  # [m, npts]
+        for j in range(m):
+            s = torch.zeros_like(books[j]).index_add_(0, a[j], resid[j])
+            cnt = torch.bincount(a[j], minlength=ks).unsqueeze(1)
+            books[j] = torch.where(cnt > 0, s / cnt.clamp_min(1).float(), books[j])
+    return books
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -76,12 +76,31 @@ VX_API const char* vx_last_error(void);
 VX_API int vx_device_count(int32_t* count);
 /* Kernels launched by this library since load (cumulative, all threads). */
 VX_API int vx_kernel_launches(int64_t* count);
+/* Per-kernel device timing.  When enabled, the library records CUDA events on the launching
+ * stream around its main kernels; vx_profile_read waits for them and returns the accumulated
+ * device milliseconds and launch count of one slot.  No counterpart in the reference (which
+ * reports only SearchResult.searchTimeNanos, vectors-db/.../SearchResult.java:31). */
+typedef enum vx_profile_slot {
+  VX_PROF_GEMM_SCAN = 0, /* tcgen05 FLAT / FP16 / SQ8 scan */
+  VX_PROF_MERGE = 1,     /* per-query candidate merge */
+  VX_PROF_RESCORE = 2,   /* exact fp32 re-score */
+  VX_PROF_FALLBACK = 3,  /* exact fallback scan */
+  VX_PROF_BQ_SCAN = 4,   /* Hamming scan */
+  VX_PROF_ADC_SCAN = 5,  /* IVF-PQ table build + ADC list scan */
+  VX_PROF_ROUTE = 6,     /* IVF coarse routing */
+  VX_PROF_SLOTS = 8
+} vx_profile_slot;
+VX_API int vx_profile_enable(int32_t on);
+VX_API int vx_profile_read(int32_t slot, double* total_ms, int64_t* launches);
+VX_API int vx_profile_reset(void);
 /* Test hook: the next vx_* call on this host thread fails with `status` before touching the
  * GPU (host-side fault injection; status 0 clears it). */
 VX_API int vx_debug_fail_next(int32_t status);
 
 /* ---- index construction (the handle owns device copies; inputs are not retained) ----- */
-/* FlatScanAdapter.build(float[][] vectors, SimilarityFunction metric)
+/* Input arrays of the build calls may be host or device memory (unified addressing), except
+ * vx_ivfpq_build, whose partitions and codes are regrouped on the host and must be host memory.
+ * FlatScanAdapter.build(float[][] vectors, SimilarityFunction metric)
  * (vectors-db/.../index/FlatScanAdapter.java:42-48).  row_stride in floats (>= dim); use
  * alignUp(dim*4, 64)/4 to read a persistent vectors.bin (MemorySegmentVectors.java:39-45). */
 VX_API int vx_flat_build(int32_t device, const float* vectors, int64_t n, int32_t dim, int64_t row_stride,

@@ -35,6 +35,9 @@ SIGNATURES = {
     "vx_device_count": [_P],
     "vx_kernel_launches": [_P],
     "vx_debug_fail_next": [_I32],
+    "vx_profile_enable": [_I32],
+    "vx_profile_read": [_I32, _P, _P],
+    "vx_profile_reset": [],
     "vx_flat_build": [_I32, _P, _I64, _I32, _I64, _I32, _PP],
     "vx_fp16_build": [_I32, _P, _I64, _I32, _I32, _P, _I64, _PP],
     "vx_sq8_build": [_I32, _P, _P, _I64, _I32, _F32, _F32, _I32, _P, _I64, _PP],
@@ -101,6 +104,35 @@ def device_count() -> int:
     c = C.c_int32(0)
     check(lib().vx_device_count(C.byref(c)))
     return int(c.value)
+
+
+PROFILE_SLOTS = {
+    "gemm_scan": 0,
+    "merge": 1,
+    "rescore": 2,
+    "fallback": 3,
+    "bq_scan": 4,
+    "adc_scan": 5,
+    "route": 6,
+}
+
+
+def profile_enable(on: bool = True) -> None:
+    check(lib().vx_profile_enable(1 if on else 0))
+
+
+def profile_reset() -> None:
+    check(lib().vx_profile_reset())
+
+
+def profile_read() -> dict:
+    """{slot name: (total device ms, launches)} accumulated since the last reset."""
+    out = {}
+    for name, slot in PROFILE_SLOTS.items():
+        ms, n = C.c_double(0), C.c_int64(0)
+        check(lib().vx_profile_read(slot, C.byref(ms), C.byref(n)))
+        out[name] = (ms.value, n.value)
+    return out
 
 
 def kernel_launches() -> int:

@@ -60,6 +60,35 @@ struct CudaFail {
     VX_CUDA(expr);                  \
   } while (0)
 
+// Optional per-kernel device timing: CUDA events recorded on the launching stream around a
+// launch, drained by vx_profile_read.
+struct ProfRec {
+  int slot;
+  cudaEvent_t a, b;
+};
+std::mutex g_prof_mu;
+std::vector<ProfRec> g_prof;
+std::atomic<bool> g_prof_on{false};
+double g_prof_ms[VX_PROF_SLOTS] = {0};
+int64_t g_prof_n[VX_PROF_SLOTS] = {0};
+
+#define VX_TIMED(slot, st, n, expr)                                  \
+  do {                                                               \
+    cudaEvent_t _a = nullptr, _b = nullptr;                          \
+    const bool _on = g_prof_on.load();                               \
+    if (_on) {                                                       \
+      VX_CUDA(cudaEventCreate(&_a));                                 \
+      VX_CUDA(cudaEventCreate(&_b));                                 \
+      VX_CUDA(cudaEventRecord(_a, st));                              \
+    }                                                                \
+    VX_LAUNCH(n, expr);                                              \
+    if (_on) {                                                       \
+      VX_CUDA(cudaEventRecord(_b, st));                              \
+      std::lock_guard<std::mutex> _g(g_prof_mu);                     \
+      g_prof.push_back(ProfRec{slot, _a, _b});                       \
+    }                                                                \
+  } while (0)
+
 bool take_injected(int* st) {
   if (g_fail_next != 0) {
     *st = fail(g_fail_next, "injected failure (vx_debug_fail_next)");
@@ -132,7 +161,7 @@ struct Scratch {
 size_t scratch_budget() {
   const char* e = getenv("VX_SCRATCH_BYTES");
   if (e && *e) return (size_t)strtoull(e, nullptr, 10);
-  return (size_t)1 << 30;
+  return (size_t)2 << 30;
 }
 
 uint64_t wait_timeout_ns() {
@@ -241,7 +270,7 @@ float* upload_rows32(vx_index* ix, const float* host, int64_t n, int dim, int64_
   float* d = dev_alloc<float>(ix, (size_t)n * dim);
   if (n > 0)
     VX_CUDA(cudaMemcpy2D(d, (size_t)dim * 4, host, (size_t)stride * 4, (size_t)dim * 4, (size_t)n,
-                         cudaMemcpyHostToDevice));
+                         cudaMemcpyDefault));
   return d;
 }
 
@@ -321,7 +350,7 @@ void exact_fallback(vx_index* ix, const float* dq, int nq_chunk, int dim, int k,
     a.n = ix->n;
     a.bufs = bufs;
     a.cnts = cnts;
-    VX_LAUNCH(1, launch_exact_scan(a, rows_f16, g.R, ix->num_sms, st));
+    VX_TIMED(VX_PROF_FALLBACK, st, 1, launch_exact_scan(a, rows_f16, g.R, ix->num_sms, st));
     VX_LAUNCH(1, launch_merge_streams(bufs, cnts, W, nf, 8, g.C, k, keys, kc, st));
     VX_LAUNCH(1, launch_finish_keys(keys, kc, nf, k, k, kFinishFloatKey, ix->metric, dim, tids, tsc,
                                     tcnt, st));
@@ -420,8 +449,8 @@ int search_gemm_exact(vx_index* ix, const float* dq, int nq, int k, int32_t* d_i
     a.epi.qsq = nullptr;
     a.epi.vsq = nullptr;
     a.epi.cm = 0.0f;
-    VX_LAUNCH(1, launch_gemm_scan(mode, tmq, ix->tm_rows, a, grid, R, st));
-    VX_LAUNCH(1, launch_merge_streams(bufs, cnts, grid, qc, Qp, C, Kc, cand, cand_cnt, st));
+    VX_TIMED(VX_PROF_GEMM_SCAN, st, 1, launch_gemm_scan(mode, tmq, ix->tm_rows, a, grid, R, st));
+    VX_TIMED(VX_PROF_MERGE, st, 1, launch_merge_streams(bufs, cnts, grid, qc, Qp, C, Kc, cand, cand_cnt, st));
     RescoreArgs r;
     r.nq = qc;
     r.dim = dim;
@@ -443,7 +472,7 @@ int search_gemm_exact(vx_index* ix, const float* dq, int nq, int k, int32_t* d_i
     r.out_counts = d_counts + q0;
     r.nflag = nflag;
     r.flag_list = flag_list;
-    VX_LAUNCH(1, launch_rescore(r, f16_kind, st));
+    VX_TIMED(VX_PROF_RESCORE, st, 1, launch_rescore(r, f16_kind, st));
     int st_err = check_device_error(d_err, st);
     if (st_err != VX_OK) return st_err;
     int32_t h_nflag = 0;
@@ -520,7 +549,7 @@ int search_quantized_scan(vx_index* ix, const float* dq, int nq, int K, int k_ou
       a.epi.qsq = qsq;
       a.epi.vsq = ix->vsq;
       a.epi.cm = kc.cm;
-      VX_LAUNCH(1, launch_gemm_scan(mode, tmq, ix->tm_codes8, a, grid, R, st));
+      VX_TIMED(VX_PROF_GEMM_SCAN, st, 1, launch_gemm_scan(mode, tmq, ix->tm_codes8, a, grid, R, st));
       VX_LAUNCH(1, launch_merge_streams(bufs, cnts, grid, qc, Qp, C, K, keys, kcnt, st));
       if (rescore) {
         RescoreArgs r{};
@@ -568,7 +597,7 @@ int search_quantized_scan(vx_index* ix, const float* dq, int nq, int K, int k_ou
       VX_LAUNCH(1, launch_bq_pack_queries(dqc, qc, dim, ix->nw_pad, qw, st));
       VX_CUDA(cudaMemsetAsync(cnts, 0, (size_t)parts * qc * 4, st));
       VX_CUDA(cudaMemsetAsync(thrs, 0, (size_t)parts * qc * 8, st));
-      VX_LAUNCH(1, launch_bq_scan(ix->words, ix->n, ix->nw_pad, qw, qc, parts, g, bufs, cnts, thrs, st));
+      VX_TIMED(VX_PROF_BQ_SCAN, st, 1, launch_bq_scan(ix->words, ix->n, ix->nw_pad, qw, qc, parts, g, bufs, cnts, thrs, st));
       VX_LAUNCH(1, launch_merge_streams(bufs, cnts, parts, qc, qc, g.C, K, keys, kcnt, st));
       if (rescore) {
         RescoreArgs r{};
@@ -632,8 +661,8 @@ int search_ivfpq(vx_index* ix, const float* dq, int nq, int k, int nprobe, int r
     uint32_t* out_cnt = T.alloc<uint32_t>((size_t)probes * qc);
     uint64_t* keys = T.alloc<uint64_t>((size_t)qc * K);
     uint32_t* kcnt = T.alloc<uint32_t>(qc);
-    VX_LAUNCH(ix->metric == VX_COSINE ? 3 : 2,
-              launch_route(dqc, qc, dim, ix->cent, ix->nlist, ix->metric, probes, qn, dist, lists, st));
+    VX_TIMED(VX_PROF_ROUTE, st, ix->metric == VX_COSINE ? 3 : 2,
+             launch_route(dqc, qc, dim, ix->cent, ix->nlist, ix->metric, probes, qn, dist, lists, st));
     VX_LAUNCH(3, launch_group_pairs(lists, qc * probes, ix->nlist, counts, offsets, cursor, pairs, st));
     VX_CUDA(cudaMemsetAsync(out_cnt, 0, (size_t)probes * qc * 4, st));
     AdcArgs a;
@@ -659,8 +688,8 @@ int search_ivfpq(vx_index* ix, const float* dq, int nq, int k, int nprobe, int r
     a.out = out;
     a.out_cnt = out_cnt;
     const int grid = ix->num_sms * 2;
-    VX_LAUNCH(1, launch_adc_scan(a, g.R, grid, st));
-    VX_LAUNCH(1, launch_merge_streams(out, out_cnt, probes, qc, qc, K, K, keys, kcnt, st));
+    VX_TIMED(VX_PROF_ADC_SCAN, st, 1, launch_adc_scan(a, g.R, grid, st));
+    VX_TIMED(VX_PROF_MERGE, st, 1, launch_merge_streams(out, out_cnt, probes, qc, qc, K, K, keys, kcnt, st));
     int32_t* oi = d_ids + (size_t)q0 * k;
     float* os = d_scores + (size_t)q0 * k;
     int32_t* oc = d_counts + q0;
@@ -887,6 +916,42 @@ int vx_kernel_launches(int64_t* count) {
   return VX_OK;
 }
 
+int vx_profile_enable(int32_t on) {
+  g_prof_on.store(on != 0);
+  return VX_OK;
+}
+
+int vx_profile_read(int32_t slot, double* total_ms, int64_t* launches) {
+  if (slot < 0 || slot >= VX_PROF_SLOTS) return fail(VX_ERR_INVALID_ARGUMENT, "bad profile slot %d", slot);
+  std::vector<ProfRec> recs;
+  {
+    std::lock_guard<std::mutex> g(g_prof_mu);
+    recs.swap(g_prof);
+  }
+  for (auto& r : recs) {
+    float ms = 0.0f;
+    if (cudaEventSynchronize(r.b) == cudaSuccess && cudaEventElapsedTime(&ms, r.a, r.b) == cudaSuccess) {
+      g_prof_ms[r.slot] += ms;
+      g_prof_n[r.slot] += 1;
+    }
+    cudaEventDestroy(r.a);
+    cudaEventDestroy(r.b);
+  }
+  if (total_ms) *total_ms = g_prof_ms[slot];
+  if (launches) *launches = g_prof_n[slot];
+  return VX_OK;
+}
+
+int vx_profile_reset(void) {
+  int64_t dummy;
+  vx_profile_read(0, nullptr, &dummy);
+  for (int i = 0; i < VX_PROF_SLOTS; i++) {
+    g_prof_ms[i] = 0;
+    g_prof_n[i] = 0;
+  }
+  return VX_OK;
+}
+
 int vx_device_count(int32_t* count) {
   return guarded([&]() -> int {
     if (!count) return fail(VX_ERR_NULL_POINTER, "count must not be null");
@@ -954,14 +1019,14 @@ int vx_fp16_build(int32_t device, const uint16_t* codes, int64_t n, int32_t dim,
         ix->Dp = (int)round_up(dim, 64);
         __half* raw = nullptr;
         VX_CUDA(cudaMalloc(&raw, (size_t)n * dim * 2));
-        VX_CUDA(cudaMemcpy(raw, codes, (size_t)n * dim * 2, cudaMemcpyHostToDevice));
+        VX_CUDA(cudaMemcpy(raw, codes, (size_t)n * dim * 2, cudaMemcpyDefault));
         ix->rows16 = dev_alloc<__half>(ix, (size_t)n * ix->Dp);
         ix->rowsq = dev_alloc<float>(ix, (size_t)n);
         ix->rowscale = dev_alloc<float>(ix, (size_t)n);
         ix->max_norm = dev_alloc<float>(ix, 1);
         VX_CUDA(cudaMemset(ix->max_norm, 0, 4));
         std::vector<float> ones((size_t)n, 1.0f);
-        VX_CUDA(cudaMemcpy(ix->rowscale, ones.data(), (size_t)n * 4, cudaMemcpyHostToDevice));
+        VX_CUDA(cudaMemcpy(ix->rowscale, ones.data(), (size_t)n * 4, cudaMemcpyDefault));
         VX_LAUNCH(1, launch_f16_rows_pad(raw, n, dim, ix->Dp, ix->rows16, ix->rowsq, ix->max_norm, 0));
         VX_CUDA(cudaDeviceSynchronize());
         cudaFree(raw);
@@ -1008,11 +1073,11 @@ int vx_sq8_build(int32_t device, const int8_t* codes, const float* corrections, 
         ix->Dp8 = (int)round_up(dim, 128);
         int8_t* raw = nullptr;
         VX_CUDA(cudaMalloc(&raw, (size_t)n * dim));
-        VX_CUDA(cudaMemcpy(raw, codes, (size_t)n * dim, cudaMemcpyHostToDevice));
+        VX_CUDA(cudaMemcpy(raw, codes, (size_t)n * dim, cudaMemcpyDefault));
         ix->codes8 = dev_alloc<int8_t>(ix, (size_t)n * ix->Dp8);
         ix->vsq = dev_alloc<int32_t>(ix, (size_t)n);
         ix->vcorr = dev_alloc<float>(ix, (size_t)n);
-        VX_CUDA(cudaMemcpy(ix->vcorr, corrections, (size_t)n * 4, cudaMemcpyHostToDevice));
+        VX_CUDA(cudaMemcpy(ix->vcorr, corrections, (size_t)n * 4, cudaMemcpyDefault));
         VX_LAUNCH(1, launch_sq8_rows_pad(raw, n, dim, ix->Dp8, ix->codes8, ix->vsq, 0));
         VX_CUDA(cudaDeviceSynchronize());
         cudaFree(raw);
@@ -1056,7 +1121,7 @@ int vx_bq_build(int32_t device, const uint64_t* words, int64_t n, int32_t dim, i
         ix->words = dev_alloc<uint64_t>(ix, (size_t)n * nwp);
         VX_CUDA(cudaMemset(ix->words, 0, (size_t)n * nwp * 8));
         VX_CUDA(cudaMemcpy2D(ix->words, (size_t)nwp * 8, words, (size_t)nw * 8, (size_t)nw * 8, (size_t)n,
-                             cudaMemcpyHostToDevice));
+                             cudaMemcpyDefault));
         if (vectors) ix->rows32 = upload_rows32(ix, vectors, n, dim, row_stride);
       }
     } catch (...) {
@@ -1108,9 +1173,9 @@ int vx_ivfpq_build(int32_t device, const float* centroids, int32_t nlist, int32_
     ix->rescore = rescore_factor;
     try {
       ix->cent = dev_alloc<float>(ix, (size_t)nlist * dim);
-      VX_CUDA(cudaMemcpy(ix->cent, centroids, (size_t)nlist * dim * 4, cudaMemcpyHostToDevice));
+      VX_CUDA(cudaMemcpy(ix->cent, centroids, (size_t)nlist * dim * 4, cudaMemcpyDefault));
       ix->list_off = dev_alloc<int64_t>(ix, (size_t)nlist + 1);
-      VX_CUDA(cudaMemcpy(ix->list_off, list_offsets, (size_t)(nlist + 1) * 8, cudaMemcpyHostToDevice));
+      VX_CUDA(cudaMemcpy(ix->list_off, list_offsets, (size_t)(nlist + 1) * 8, cudaMemcpyDefault));
       // subspaces (ProductQuantizer.computeSubspaceSizesAndOffsets, ProductQuantizer.java:686-700)
       std::vector<int32_t> sub(2 * (size_t)m);
       std::vector<int64_t> cboff(m);
@@ -1125,20 +1190,20 @@ int vx_ivfpq_build(int32_t device, const float* centroids, int32_t nlist, int32_
         co += (int64_t)ks * size;
       }
       ix->sub = dev_alloc<int32_t>(ix, sub.size());
-      VX_CUDA(cudaMemcpy(ix->sub, sub.data(), sub.size() * 4, cudaMemcpyHostToDevice));
+      VX_CUDA(cudaMemcpy(ix->sub, sub.data(), sub.size() * 4, cudaMemcpyDefault));
       ix->cb_off = dev_alloc<int64_t>(ix, cboff.size());
-      VX_CUDA(cudaMemcpy(ix->cb_off, cboff.data(), cboff.size() * 8, cudaMemcpyHostToDevice));
+      VX_CUDA(cudaMemcpy(ix->cb_off, cboff.data(), cboff.size() * 8, cudaMemcpyDefault));
       ix->codebooks = dev_alloc<float>(ix, (size_t)co);
-      VX_CUDA(cudaMemcpy(ix->codebooks, codebooks, (size_t)co * 4, cudaMemcpyHostToDevice));
+      VX_CUDA(cudaMemcpy(ix->codebooks, codebooks, (size_t)co * 4, cudaMemcpyDefault));
       // codes regrouped list-contiguous, rows padded to Mp bytes
       ix->ordinals = dev_alloc<int32_t>(ix, (size_t)std::max<int64_t>(n, 1));
       ix->pq_codes = dev_alloc<uint8_t>(ix, (size_t)std::max<int64_t>(n, 1) * ix->Mp);
       if (n > 0) {
-        VX_CUDA(cudaMemcpy(ix->ordinals, list_ordinals, (size_t)n * 4, cudaMemcpyHostToDevice));
+        VX_CUDA(cudaMemcpy(ix->ordinals, list_ordinals, (size_t)n * 4, cudaMemcpyDefault));
         std::vector<uint8_t> grouped((size_t)n * ix->Mp, 0);
         for (int64_t i = 0; i < n; i++)
           std::memcpy(&grouped[(size_t)i * ix->Mp], codes + (size_t)list_ordinals[i] * m, (size_t)m);
-        VX_CUDA(cudaMemcpy(ix->pq_codes, grouped.data(), grouped.size(), cudaMemcpyHostToDevice));
+        VX_CUDA(cudaMemcpy(ix->pq_codes, grouped.data(), grouped.size(), cudaMemcpyDefault));
       }
       if (vectors && n > 0) ix->rows32 = upload_rows32(ix, vectors, n, dim, dim);
     } catch (...) {

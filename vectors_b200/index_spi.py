@@ -215,12 +215,21 @@ class FlatScanAdapter(IndexSpi):
     overQueryFactor ignored."""
 
     def build(self, vectors, metric: SimilarityFunction) -> None:
+        """vectors: [n][dim] float32 rows (numpy / lists, or a CUDA tensor, copied on device)."""
         if metric is None:
             raise NullPointerException("metric must not be null")
-        v = _as_matrix(vectors, "vectors")
+        if vectors is None:
+            raise NullPointerException("vectors must not be null")
         self._h.close()
-        n, dim = v.shape if v.size else (0, 0)
-        _check(N.lib().vx_flat_build(self.device, _ptr(v), n, dim, dim, int(metric), C.byref(self._h.ptr)))
+        if getattr(vectors, "is_cuda", False):
+            t = vectors.contiguous()
+            n, dim = (t.shape[0], t.shape[1]) if t.numel() else (0, 0)
+            _check(N.lib().vx_flat_build(self.device, C.c_void_p(t.data_ptr()), n, dim, dim, int(metric),
+                                         C.byref(self._h.ptr)))
+        else:
+            v = _as_matrix(vectors, "vectors")
+            n, dim = v.shape if v.size else (0, 0)
+            _check(N.lib().vx_flat_build(self.device, _ptr(v), n, dim, dim, int(metric), C.byref(self._h.ptr)))
         self._n, self._dim, self.metric = n, dim, SimilarityFunction(metric)
 
 
