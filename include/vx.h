@@ -164,6 +164,20 @@ VX_API int vx_ivfpq_search_device(vx_index* index, const float* d_queries, int32
                            int32_t k, int32_t nprobe, int32_t rescore_factor, float min_score,
                            int32_t* d_ids, float* d_scores, int32_t* d_counts, void* stream);
 
+/* No counterpart in the reference.  The sign-bit BQ candidate scan of vx_scan_candidates_device
+ * for callers that must not allocate device memory while searching (a host that reserves its
+ * whole device budget up front and accounts every byte, or a latency-critical loop where an
+ * allocation would block on the allocator or synchronise the device).  Its scratch is a
+ * file-scope 64 MiB device array that every GPU loading the library holds until exit; no
+ * cudaMalloc, cudaFree or pool allocation happens in the call.  The first call on a device
+ * looks the array up with cudaGetSymbolAddress and should come before any stream capture.
+ * All calls on a device share the array: calls that overlap on the GPU race and must be
+ * serialised by the caller.  Batches needing more than 64 MiB of scratch are rejected with
+ * VX_ERR_INVALID_ARGUMENT (split the batch).  Queries and outputs are device buffers. */
+VX_API int vx_bq_scan_candidates_noalloc(vx_index* index, const float* d_queries, int32_t nq,
+                                         int32_t dim, int32_t k, int32_t* d_ids, float* d_scores,
+                                         int32_t* d_counts, void* stream);
+
 /* ---- shards ---------------------------------------------------------------------------- */
 /* IndexShards.mergeWithOffsets (vectors-db/.../index/IndexShards.java:168-211): shard s holds
  * shard_counts[s*nq+q] (ordinal, score) pairs of query q at [(s*nq+q)*kin]; ordinals are

@@ -52,6 +52,7 @@ SIGNATURES = {
     "vx_ivfpq_search": [_P, _P, _I32, _I32, _I32, _I32, _I32, _F32, _P, _P, _P],
     "vx_ivfpq_search_device": [_P, _P, _I32, _I32, _I32, _I32, _I32, _F32, _P, _P, _P, _P],
     "vx_merge_shards_device": [_I32, _I32, _P, _P, _P, _P, _I32, _I32, _I32, _P, _P, _P, _P],
+    "vx_bq_scan_candidates_noalloc": [_P, _P, _I32, _I32, _I32, _P, _P, _P, _P],
 }
 
 _lib = None

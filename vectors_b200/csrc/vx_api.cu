@@ -171,54 +171,16 @@ uint64_t wait_timeout_ns() {
 }
 
 }  // namespace
+
+// Shared with noalloc.cu (internal to the library, not exported).
+int record_failure(int status, const char* msg) { return fail(status, "%s", msg); }
+void add_launches(int n) { g_launches.fetch_add(n); }
+
 }  // namespace vx
 
 using namespace vx;
 
-// ------------------------------------------------------------------ index
-struct vx_index {
-  int kind = 0;
-  int device = 0;
-  int metric = 0;
-  int64_t n = 0;
-  int dim = 0;
-  int num_sms = 148;
-  // fp32 rows (FLAT; optional for the quantized kinds), row stride = dim
-  float* rows32 = nullptr;
-  // fp16 GEMM operand [n][Dp]: unit rows (FLAT) or the stored fp16 rows (FP16)
-  __half* rows16 = nullptr;
-  int Dp = 0;
-  float* rowscale = nullptr;  // |x| (unit rows) or 1 (fp16 rows)
-  float* rowsq = nullptr;     // |x|^2
-  float* max_norm = nullptr;  // device scalar
-  CUtensorMap tm_rows;
-  bool has_tm_rows = false;
-  // SQ8
-  int8_t* codes8 = nullptr;
-  int Dp8 = 0;
-  float* vcorr = nullptr;
-  int32_t* vsq = nullptr;
-  float min_q = 0, max_q = 0;
-  CUtensorMap tm_codes8;
-  // BQ
-  uint64_t* words = nullptr;
-  int nw_pad = 0;
-  // IVF-PQ
-  float* cent = nullptr;
-  int nlist = 0;
-  int64_t* list_off = nullptr;
-  int32_t* ordinals = nullptr;
-  uint8_t* pq_codes = nullptr;
-  int M = 0, Ks = 0, Mp = 0;
-  float* codebooks = nullptr;
-  int64_t* cb_off = nullptr;
-  int32_t* sub = nullptr;
-  int nprobe = 1, rescore = 1;
-  std::vector<void*> owned;
-  // exact-search view of a quantized index (built on first use)
-  vx_index* flat = nullptr;
-  std::mutex lazy_mu;
-};
+#include "index.h"
 
 namespace vx {
 namespace {
