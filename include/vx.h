@@ -88,6 +88,7 @@ typedef enum vx_profile_slot {
   VX_PROF_BQ_SCAN = 4,   /* Hamming scan */
   VX_PROF_ADC_SCAN = 5,  /* IVF-PQ table build + ADC list scan */
   VX_PROF_ROUTE = 6,     /* IVF coarse routing */
+  VX_PROF_PILOT = 7,     /* pilot sweep that seeds the admission floors of the tcgen05 scan */
   VX_PROF_SLOTS = 8
 } vx_profile_slot;
 VX_API int vx_profile_enable(int32_t on);

@@ -45,6 +45,29 @@ def test_flat_matches_oracle(oracle, metric, n, dim, nq, k):
     f.close()
 
 
+@pytest.mark.parametrize("metric", [0, 2])
+def test_flat_large_with_pilot_floors(oracle, metric):
+    # more rows than the pilot sweep, several query blocks: exercises the shared admission
+    # floors and the floor-filtered merge
+    db, q = _data(oracle, 120_000, 96, 300, comps=8)
+    f = vx.FlatScanAdapter()
+    f.build(db, vx.SimilarityFunction(metric))
+    got = f.search_batch(q, 10)
+    ids, sc, cnt = oracle.flat_search(db, q, metric, 10)
+    _check_float(got, ids, sc, cnt, f"flat pilot m={metric}")
+
+
+def test_sq8_large_with_pilot_floors(oracle):
+    db, q = _data(oracle, 120_000, 128, 260, comps=8)
+    lo, hi = oracle.sq8_train(db)
+    codes, corr = oracle.sq8_encode_all(lo, hi, db)
+    a = vx.QuantizedFlatScanAdapter()
+    a.build_sq8(codes, corr, lo, hi, vx.SimilarityFunction.DOT_PRODUCT)
+    got = a.scan_candidates(q, 100)
+    ids, sc, cnt = oracle.sq8_search(codes, corr, lo, hi, q, oracle.DOT_PRODUCT, 100)
+    _check_float(got, ids, sc, cnt, "sq8 pilot", exact_scores=True)
+
+
 def test_flat_single_query_and_small_index(oracle):
     db, q = _data(oracle, 5, 32, 3)
     f = vx.FlatScanAdapter()
@@ -70,6 +93,35 @@ def test_flat_duplicates_take_exact_fallback(oracle):
         got = f.search_batch(q, 20)
         ids, sc, cnt = oracle.flat_search(db, q, metric, 20)
         _check_float(got, ids, sc, cnt, f"flat duplicates m={metric}")
+
+
+@pytest.mark.parametrize("metric", [0, 1, 2])
+def test_flat_near_duplicates_take_second_pass(oracle, metric):
+    # 500 rows within 1e-4 of each other around the queries: the 128-candidate window cannot
+    # prove completeness, the 1000-candidate second pass can
+    rng = np.random.default_rng(1)
+    base = rng.standard_normal((1, 96)).astype(np.float32)
+    near = base + 1e-4 * rng.standard_normal((500, 96)).astype(np.float32)
+    far = rng.standard_normal((4000, 96)).astype(np.float32)
+    db = np.concatenate([far[:2000], near, far[2000:]])
+    q = base + 1e-3 * rng.standard_normal((6, 96)).astype(np.float32)
+    f = vx.FlatScanAdapter()
+    f.build(db, vx.SimilarityFunction(metric))
+    got = f.search_batch(q, 10)
+    ids, sc, cnt = oracle.flat_search(db, q, metric, 10)
+    _check_float(got, ids, sc, cnt, f"flat near-duplicates m={metric}")
+
+
+def test_flat_many_duplicates_exact_fallback(oracle):
+    rng = np.random.default_rng(2)
+    base = rng.standard_normal((1, 64)).astype(np.float32)
+    db = np.concatenate([rng.standard_normal((3000, 64)).astype(np.float32), np.repeat(base, 2500, axis=0)])
+    q = base + 0.01 * rng.standard_normal((3, 64)).astype(np.float32)
+    f = vx.FlatScanAdapter()
+    f.build(db, vx.SimilarityFunction.DOT_PRODUCT)
+    got = f.search_batch(q, 10)
+    ids, sc, cnt = oracle.flat_search(db, q, oracle.DOT_PRODUCT, 10)
+    _check_float(got, ids, sc, cnt, "flat many duplicates")
 
 
 def test_flat_empty_index(oracle):

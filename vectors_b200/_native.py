@@ -115,6 +115,7 @@ PROFILE_SLOTS = {
     "bq_scan": 4,
     "adc_scan": 5,
     "route": 6,
+    "pilot": 7,
 }
 
 

@@ -45,6 +45,26 @@ __device__ __forceinline__ float thr_to_float(uint64_t thr) {
   return thr == 0 ? -INFINITY : key_score(thr);
 }
 
+// Pair p -> (row tile, query block): row-tile-major (consecutive pairs share the database
+// tile) or query-block-major (one CTA sweeps its query block over every row tile).
+__device__ __forceinline__ void tile_of(int64_t p, const ScanArgs& a, int64_t& nt, int& mb) {
+  if (a.m_major) {
+    mb = (int)(p / a.ntiles);
+    nt = p % a.ntiles;
+  } else {
+    nt = p / a.num_mblocks;
+    mb = (int)(p % a.num_mblocks);
+  }
+}
+
+// Raises the stream's threshold to the shared floor (admit keys >= floor).
+__device__ __forceinline__ void apply_floor(const ScanArgs& a, int q, bool active, uint64_t& thr) {
+  if (a.floor && active) {
+    const uint64_t f = __ldcg((const unsigned long long*)a.floor + q);  // other CTAs raise it
+    if (f > 1 && f - 1 > thr) thr = f - 1;
+  }
+}
+
 template <bool kI8, int kMode, int R>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gemm_scan_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -101,8 +121,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       uint32_t used = 0;      // bit s: stage s has had a load issued
       uint32_t last_par = 0;  // bit s: parity of the last phase issued on stage s
       for (int64_t p = p0; p < p1 && !*abort_flag; p++) {
-        const int64_t nt = p / a.num_mblocks;
-        const int mb = (int)(p % a.num_mblocks);
+        int64_t nt;
+        int mb;
+        tile_of(p, a, nt, mb);
         for (int kc = 0; kc < a.kchunks; kc++) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, globaltimer_ns() + a.timeout_ns, abort_flag)) {
             give_up();
@@ -185,8 +206,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const int Qp = a.num_mblocks * BM;
     int64_t t = 0;
     for (int64_t p = p0; p < p1; p++, t++) {
-      const int64_t nt = p / a.num_mblocks;
-      const int mb = (int)(p % a.num_mblocks);
+      int64_t nt;
+      int mb;
+      tile_of(p, a, nt, mb);
       const int acc = (int)(t & 1);
       const uint32_t acc_phase = (uint32_t)((t >> 1) & 1);
       const int64_t col0 = nt * BN;
@@ -225,6 +247,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       st.base = a.bufs + sidx * (size_t)a.C;
       st.cnt = active ? a.cnts[sidx] : 0u;
       st.thr = active ? a.thrs[sidx] : ~0ull;
+      apply_floor(a, q, active, st.thr);
       float tf = active ? thr_to_float(st.thr) : INFINITY;
       float qa = 0.0f;
       int32_t qi = 0;
@@ -277,6 +300,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const bool need = st.cnt > (uint32_t)(a.C - 32);
         if (__any_sync(0xFFFFFFFFu, need)) {
           warp_compact_lanes<R>(need, st.base, st.cnt, st.thr, (uint32_t)a.K);
+          if (need && a.floor && st.cnt == (uint32_t)a.K)
+            atomicMax((unsigned long long*)&a.floor[q], (unsigned long long)st.thr);
+          apply_floor(a, q, active, st.thr);
           tf = active ? thr_to_float(st.thr) : INFINITY;
         }
       }
@@ -297,8 +323,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         uint64_t* base = a.bufs + sidx * (size_t)a.C;
         uint32_t cnt = active ? a.cnts[sidx] : 0u;
         uint64_t thr = active ? a.thrs[sidx] : ~0ull;
-        warp_compact_lanes<R>(cnt > (uint32_t)a.K, base, cnt, thr, (uint32_t)a.K);
-        if (active) a.cnts[sidx] = cnt;
+        const bool need = cnt > (uint32_t)a.K;
+        warp_compact_lanes<R>(need, base, cnt, thr, (uint32_t)a.K);
+        if (active) {
+          a.cnts[sidx] = cnt;
+          a.thrs[sidx] = thr;
+          if (need && a.floor) atomicMax((unsigned long long*)&a.floor[q], (unsigned long long)thr);
+        }
       }
     }
   }

@@ -38,6 +38,9 @@ struct ScanArgs {
   uint64_t* bufs;     // [grid][num_mblocks*128][C]
   uint32_t* cnts;     // [grid][num_mblocks*128]   (zeroed before launch)
   uint64_t* thrs;     // [grid][num_mblocks*128]   (zeroed before launch)
+  int m_major;        // 1: deal (query-block, row-tile) pairs query-block-major (one CTA per block)
+  uint64_t* floor;    // [nq] shared admission floors (nullable): any stream holding K keys
+                      // publishes its K-th key; every stream admits only keys >= floor
   int32_t* err;       // device error word
   uint64_t timeout_ns;
   EpiParams epi;

@@ -23,6 +23,7 @@ struct vx_index {
   float* rowscale = nullptr;  // |x| (unit rows) or 1 (fp16 rows)
   float* rowsq = nullptr;     // |x|^2
   float* max_norm = nullptr;  // device scalar
+  float* max_err = nullptr;   // device scalar: max over rows of |fp16(x/|x|) - x/|x||
   CUtensorMap tm_rows;
   bool has_tm_rows = false;
   // SQ8

@@ -51,9 +51,14 @@ StreamGeom stream_geom(int K, int slack);
 // ---- merge.cu
 cudaError_t launch_merge_streams(const uint64_t* bufs, const uint32_t* cnts, int S, int nq,
                                  int stride, int C, int K, uint64_t* out_keys, uint32_t* out_cnt,
-                                 cudaStream_t st);
+                                 cudaStream_t st, const uint64_t* floor = nullptr);
 cudaError_t launch_ids_to_keys(const int32_t* ids, const int32_t* cnt, int nq, int K, uint64_t* keys,
                                cudaStream_t st);
+cudaError_t launch_gather_rows(const float* src, const int32_t* map, int m, int dim, float* dst,
+                               cudaStream_t st);
+cudaError_t launch_scatter_results(const int32_t* ids, const float* sc, const int32_t* cnt,
+                                   const int32_t* map, int m, int k, int32_t* out_ids, float* out_sc,
+                                   int32_t* out_cnt, cudaStream_t st);
 cudaError_t launch_min_score(const float* scores, int nq, int k, float min_score, int32_t* counts,
                              cudaStream_t st);
 cudaError_t launch_finish_keys(const uint64_t* keys, const uint32_t* cnt, int nq, int K, int k_out,

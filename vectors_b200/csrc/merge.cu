@@ -11,6 +11,7 @@ namespace vx {
 __global__ void __launch_bounds__(256) merge_streams_kernel(const uint64_t* __restrict__ bufs,
                                                             const uint32_t* __restrict__ cnts,
                                                             int S, int nq, int C, int K,
+                                                            const uint64_t* __restrict__ floor,
                                                             uint64_t* __restrict__ out_keys,
                                                             uint32_t* __restrict__ out_cnt) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
@@ -20,16 +21,28 @@ __global__ void __launch_bounds__(256) merge_streams_kernel(const uint64_t* __re
   uint64_t* s_tmp = s_keys + cap;
   uint32_t* s_red = (uint32_t*)(s_tmp + cap);
   uint32_t* s_counter = s_red + 32;
+  __shared__ uint32_t s_n;
+  // Keys below the query's shared floor cannot reach its top K (some stream holds K keys
+  // at or above the floor), so only keys >= floor are gathered.
+  const uint64_t f = floor ? floor[q] : 0ull;
   uint32_t n = 0;
+  if (threadIdx.x == 0) s_n = 0;
+  __syncthreads();
   for (int s = 0; s < S; s++) {
     uint32_t c = cnts[(size_t)s * nq + q];
     if (c == 0) continue;
     if (n + c > cap) {
       n = block_keep_top(s_keys, n, (uint32_t)K, s_tmp, s_red, s_counter);
+      if (threadIdx.x == 0) s_n = n;
+      __syncthreads();
     }
     const uint64_t* src = bufs + ((size_t)s * nq + q) * (size_t)C;
-    for (uint32_t i = threadIdx.x; i < c; i += blockDim.x) s_keys[n + i] = src[i];
-    n += c;
+    for (uint32_t i = threadIdx.x; i < c; i += blockDim.x) {
+      const uint64_t key = src[i];
+      if (key >= f) s_keys[atomicAdd(&s_n, 1u)] = key;
+    }
+    __syncthreads();
+    n = s_n;
     __syncthreads();
   }
   n = block_keep_top(s_keys, n, (uint32_t)K, s_tmp, s_red, s_counter);
@@ -46,13 +59,13 @@ size_t merge_streams_smem(int C, int K) {
 
 cudaError_t launch_merge_streams(const uint64_t* bufs, const uint32_t* cnts, int S, int nq,
                                  int stride, int C, int K, uint64_t* out_keys, uint32_t* out_cnt,
-                                 cudaStream_t st) {
+                                 cudaStream_t st, const uint64_t* floor) {
   if (nq <= 0) return cudaSuccess;
   size_t smem = merge_streams_smem(C, K);
   cudaError_t e = cudaFuncSetAttribute(merge_streams_kernel,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
-  merge_streams_kernel<<<nq, 256, smem, st>>>(bufs, cnts, S, stride, C, K, out_keys, out_cnt);
+  merge_streams_kernel<<<nq, 256, smem, st>>>(bufs, cnts, S, stride, C, K, floor, out_keys, out_cnt);
   return cudaGetLastError();
 }
 
@@ -117,6 +130,46 @@ cudaError_t launch_ids_to_keys(const int32_t* ids, const int32_t* cnt, int nq, i
                                cudaStream_t st) {
   if (nq <= 0) return cudaSuccess;
   ids_to_keys_kernel<<<nq, 128, 0, st>>>(ids, cnt, nq, K, keys);
+  return cudaGetLastError();
+}
+
+// Gathers rows src[map[i]] (dim floats each) into dst[i].
+__global__ void gather_rows_kernel(const float* __restrict__ src, const int32_t* __restrict__ map, int m,
+                                  int dim, float* __restrict__ dst) {
+  const int i = blockIdx.x;
+  if (i >= m) return;
+  const float* s = src + (size_t)map[i] * dim;
+  for (int d = threadIdx.x; d < dim; d += blockDim.x) dst[(size_t)i * dim + d] = s[d];
+}
+
+cudaError_t launch_gather_rows(const float* src, const int32_t* map, int m, int dim, float* dst,
+                               cudaStream_t st) {
+  if (m <= 0) return cudaSuccess;
+  gather_rows_kernel<<<m, 128, 0, st>>>(src, map, m, dim, dst);
+  return cudaGetLastError();
+}
+
+// Writes per-query results computed for a subset back to their places: row i of the subset
+// goes to query map[i].
+__global__ void scatter_results_kernel(const int32_t* __restrict__ ids, const float* __restrict__ sc,
+                                       const int32_t* __restrict__ cnt, const int32_t* __restrict__ map,
+                                       int m, int k, int32_t* __restrict__ out_ids,
+                                       float* __restrict__ out_sc, int32_t* __restrict__ out_cnt) {
+  const int i = blockIdx.x;
+  if (i >= m) return;
+  const int q = map[i];
+  for (int j = threadIdx.x; j < k; j += blockDim.x) {
+    out_ids[(size_t)q * k + j] = ids[(size_t)i * k + j];
+    out_sc[(size_t)q * k + j] = sc[(size_t)i * k + j];
+  }
+  if (threadIdx.x == 0) out_cnt[q] = cnt[i];
+}
+
+cudaError_t launch_scatter_results(const int32_t* ids, const float* sc, const int32_t* cnt,
+                                   const int32_t* map, int m, int k, int32_t* out_ids, float* out_sc,
+                                   int32_t* out_cnt, cudaStream_t st) {
+  if (m <= 0) return cudaSuccess;
+  scatter_results_kernel<<<m, 128, 0, st>>>(ids, sc, cnt, map, m, k, out_ids, out_sc, out_cnt);
   return cudaGetLastError();
 }
 

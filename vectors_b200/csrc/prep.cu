@@ -14,11 +14,14 @@ __device__ __forceinline__ void atomic_max_pos_float(float* addr, float v) {
 }
 
 // One warp per row: norm in double, then fp16(x / |x|) (or fp16(x) when !unit) into a
-// zero-padded row of Dp halves.
+// zero-padded row of Dp halves.  Also the Euclidean norm of the rounding error
+// |fp16(x/|x|) - x/|x||, which bounds the operand's contribution to the approximate key's
+// error by Cauchy-Schwarz (per row into errs, and its maximum into max_err).
 __global__ void rows_to_f16_kernel(const float* __restrict__ src, int64_t n, int dim,
                                    int64_t src_stride, int Dp, int unit, __half* __restrict__ dst,
                                    float* __restrict__ norms, float* __restrict__ norms_sq,
-                                   float* __restrict__ max_norm) {
+                                   float* __restrict__ max_norm, float* __restrict__ errs,
+                                   float* __restrict__ max_err) {
   const int lane = threadIdx.x & 31;
   const int64_t row = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   if (row >= n) return;
@@ -27,14 +30,30 @@ __global__ void rows_to_f16_kernel(const float* __restrict__ src, int64_t n, int
   for (int i = lane; i < dim; i += 32) s += (double)x[i] * (double)x[i];
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xFFFFFFFFu, s, o);
-  const float norm = (float)sqrt(s);
+  const double normd = sqrt(s);
+  const float norm = (float)normd;
   const float inv = (unit && norm > 0.0f) ? 1.0f / norm : 1.0f;
+  const double invd = (unit && normd > 0.0) ? 1.0 / normd : 1.0;
   __half* d = dst + row * (int64_t)Dp;
-  for (int i = lane; i < Dp; i += 32) d[i] = __float2half_rn(i < dim ? x[i] * inv : 0.0f);
+  double e = 0.0;
+  for (int i = lane; i < Dp; i += 32) {
+    const __half h = __float2half_rn(i < dim ? x[i] * inv : 0.0f);
+    d[i] = h;
+    if (i < dim) {
+      const double diff = (double)__half2float(h) - (double)x[i] * invd;
+      e += diff * diff;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) e += __shfl_xor_sync(0xFFFFFFFFu, e, o);
   if (lane == 0) {
     if (norms) norms[row] = unit ? norm : 1.0f;
     if (norms_sq) norms_sq[row] = (float)s;
     if (max_norm) atomic_max_pos_float(max_norm, norm);
+    // rounded up so that the float never understates the double
+    const float ef = __double2float_ru(sqrt(e));
+    if (errs) errs[row] = ef;
+    if (max_err) atomic_max_pos_float(max_err, ef);
   }
 }
 
@@ -64,23 +83,27 @@ __global__ void f16_rows_pad_kernel(const __half* __restrict__ src, int64_t n, i
 }
 
 // Bound on |approximate key - exact key| per query (see rescore.cu for the argument).
-// u = 2^-11 is the fp16 unit roundoff; accumulation in the tensor core is bounded by
-// (D+1) 2^-23 of the sum of |products|; the reference's own fp32 rounding by (D+2) 2^-24;
-// the score transform's final rounding by 2^-21 of its magnitude.
-__global__ void margin_kernel(const float* __restrict__ qnorm, int nq, int D, int metric,
-                              int operand_kind, const float* __restrict__ max_norm_ptr,
-                              float* __restrict__ margin) {
+// With unit vectors q^ = q/|q|, x^ = x/|x| and their fp16 roundings q^ + e_q, x^ + e_x:
+//   |(q^+e_q).(x^+e_x) - q^.x^| <= |e_q| + |e_x| + |e_q||e_x|      (Cauchy-Schwarz),
+// using the measured error norms (qerr per query, rerr_max over all rows; 0 for rows that are
+// stored in fp16 already).  The tensor core's fp32 accumulation adds at most (D+1) 2^-23 of the
+// sum of |products| (<= 1 + |e| terms); the reference's own fp32 evaluation (32 lane partial
+// sums of ~D/32 terms, then a 5-level combine, plus a scalar tail) adds (D/32 + 24) 2^-24; the
+// final score transform's rounding adds 2^-21 of the score scale.
+__global__ void margin_kernel(const float* __restrict__ qnorm, const float* __restrict__ qerr,
+                              int nq, int D, int metric, int operand_kind,
+                              const float* __restrict__ max_norm_ptr,
+                              const float* __restrict__ max_err_ptr, float* __restrict__ margin) {
   const int q = blockIdx.x * blockDim.x + threadIdx.x;
   if (q >= nq) return;
-  const double u = 1.0 / 2048.0;
   const double xmax = (double)*max_norm_ptr;
   const double qn = (double)qnorm[q];
-  const double acc = (D + 1) * 0x1.0p-23;
-  const double ref = (D + 2) * 0x1.0p-24;
-  const double sub = sqrt((double)D) * 0x1.0p-24;
-  // relative error of the normalised dot q^.x^ (both operands rounded) or q^.x (rows exact)
-  const double c = (operand_kind == kOperandUnitRows) ? (2 * u + u * u + 0x1.0p-21 + sub + acc)
-                                                      : (u + 0x1.0p-22 + sub + acc);
+  const double eq = (double)qerr[q];
+  const double ex = (operand_kind == kOperandUnitRows) ? (double)*max_err_ptr : 0.0;
+  const double acc = (D + 1) * 0x1.0p-23 * (1.0 + eq + ex + eq * ex);
+  const double ref = (D / 32 + 24) * 0x1.0p-24;
+  // error of the normalised dot, per unit of |x| (rows stored in fp16 are exact, not unit)
+  const double c = eq + ex + eq * ex + acc;
   double m;
   if (metric == 2 /* COSINE */ && operand_kind == kOperandUnitRows) {
     m = c + ref + 0x1.0p-21;
@@ -164,12 +187,12 @@ __global__ void zero_rows_kernel(__half* dst, int64_t first, int64_t last, int D
 
 cudaError_t launch_rows_to_f16(const float* src, int64_t n, int dim, int64_t src_stride, int Dp,
                                bool unit, __half* dst, float* norms, float* norms_sq,
-                               float* max_norm, cudaStream_t st) {
+                               float* max_norm, cudaStream_t st, float* errs, float* max_err) {
   if (n <= 0) return cudaSuccess;
   const int64_t threads = n * 32;
   const int blocks = (int)((threads + 255) / 256);
   rows_to_f16_kernel<<<blocks, 256, 0, st>>>(src, n, dim, src_stride, Dp, unit ? 1 : 0, dst, norms,
-                                             norms_sq, max_norm);
+                                             norms_sq, max_norm, errs, max_err);
   return cudaGetLastError();
 }
 
@@ -188,11 +211,12 @@ cudaError_t launch_zero_f16_rows(__half* dst, int64_t first, int64_t last, int D
   return cudaGetLastError();
 }
 
-cudaError_t launch_margin(const float* qnorm, int nq, int D, int metric, int operand_kind,
-                          const float* max_norm, float* margin, cudaStream_t st) {
+cudaError_t launch_margin(const float* qnorm, const float* qerr, int nq, int D, int metric,
+                          int operand_kind, const float* max_norm, const float* max_err,
+                          float* margin, cudaStream_t st) {
   if (nq <= 0) return cudaSuccess;
-  margin_kernel<<<(nq + 127) / 128, 128, 0, st>>>(qnorm, nq, D, metric, operand_kind, max_norm,
-                                                 margin);
+  margin_kernel<<<(nq + 127) / 128, 128, 0, st>>>(qnorm, qerr, nq, D, metric, operand_kind,
+                                                 max_norm, max_err, margin);
   return cudaGetLastError();
 }
 

@@ -19,12 +19,14 @@ Sq8Consts sq8_consts(float min_q, float max_q);
 
 cudaError_t launch_rows_to_f16(const float* src, int64_t n, int dim, int64_t src_stride, int Dp,
                                bool unit, __half* dst, float* norms, float* norms_sq,
-                               float* max_norm, cudaStream_t st);
+                               float* max_norm, cudaStream_t st, float* errs = nullptr,
+                               float* max_err = nullptr);
 cudaError_t launch_f16_rows_pad(const __half* src, int64_t n, int dim, int Dp, __half* dst,
                                 float* norms_sq, float* max_norm, cudaStream_t st);
 cudaError_t launch_zero_f16_rows(__half* dst, int64_t first, int64_t last, int Dp, cudaStream_t st);
-cudaError_t launch_margin(const float* qnorm, int nq, int D, int metric, int operand_kind,
-                          const float* max_norm, float* margin, cudaStream_t st);
+cudaError_t launch_margin(const float* qnorm, const float* qerr, int nq, int D, int metric,
+                          int operand_kind, const float* max_norm, const float* max_err,
+                          float* margin, cudaStream_t st);
 cudaError_t launch_sq8_encode_queries(const float* q, int nq, int dim, int Dp8, Sq8Consts k,
                                       int8_t* codes, float* corr, int32_t* sumsq, cudaStream_t st);
 cudaError_t launch_sq8_rows_pad(const int8_t* src, int64_t n, int dim, int Dp8, int8_t* dst,

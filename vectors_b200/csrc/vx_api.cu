@@ -243,9 +243,11 @@ void build_unit_f16(vx_index* ix) {
   ix->rowscale = dev_alloc<float>(ix, (size_t)std::max<int64_t>(ix->n, 1));
   ix->rowsq = dev_alloc<float>(ix, (size_t)std::max<int64_t>(ix->n, 1));
   ix->max_norm = dev_alloc<float>(ix, 1);
+  ix->max_err = dev_alloc<float>(ix, 1);
   VX_CUDA(cudaMemset(ix->max_norm, 0, 4));
+  VX_CUDA(cudaMemset(ix->max_err, 0, 4));
   VX_LAUNCH(1, launch_rows_to_f16(ix->rows32, ix->n, ix->dim, ix->dim, ix->Dp, true, ix->rows16,
-                                  ix->rowscale, ix->rowsq, ix->max_norm, 0));
+                                  ix->rowscale, ix->rowsq, ix->max_norm, 0, nullptr, ix->max_err));
   if (ix->n > 0) {
     make_tmap(&ix->tm_rows, ix->rows16, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, ix->Dp, ix->n, 256);
     ix->has_tm_rows = true;
@@ -328,24 +330,59 @@ void exact_fallback(vx_index* ix, const float* dq, int nq_chunk, int dim, int k,
   VX_CUDA(cudaStreamSynchronize(st));
 }
 
+constexpr int kMaxCandidates = 1000;  // largest window the R=33 stream geometry holds
+
 int candidate_width(int k, int64_t n) {
-  // Approximate candidates per query: enough headroom above k for the margin test to pass on
-  // typical data; queries that need more take the exact fallback.
-  int64_t kc = std::max<int64_t>(32, round_up(2 * (int64_t)k + 16, 32));
-  kc = std::min<int64_t>(kc, 1024);
+  // Approximate candidates per query in the first pass: enough headroom above k for the
+  // completeness test to pass on typical data.  Queries that fail it are re-run with
+  // kMaxCandidates, and only queries failing that too take the exact fallback scan.
+  int64_t kc = std::max<int64_t>(128, round_up(2 * (int64_t)k + 32, 32));
+  kc = std::min<int64_t>(kc, kMaxCandidates);
   if (n < kc) kc = std::max<int64_t>(n, 1);
   return (int)kc;
 }
 
-// FLAT / FP16: fp16 tcgen05 approximate pass + exact fp32 re-score (+ exact fallback).
-int search_gemm_exact(vx_index* ix, const float* dq, int nq, int k, int32_t* d_ids,
-                      float* d_scores, int32_t* d_counts, cudaStream_t st) {
+// Runs the tcgen05 scan for one query chunk and merges each query's streams into its K best
+// keys.  A pilot sweep (each CTA takes one query block over the first kPilotRows rows) first
+// leaves every query with the K-th best key of those rows as its admission floor; during the
+// main scan CTAs also publish the K-th key of every full stream, so floors keep rising and
+// rows below them are never buffered.  The merge then ignores keys under the final floor.
+constexpr int64_t kPilotRows = 32768;
+
+void scan_and_merge(int mode, const CUtensorMap& tmq, const CUtensorMap& tmrows, ScanArgs a,
+                    int grid, int R, int Qp, uint64_t* floor, uint64_t* cand, uint32_t* cand_cnt,
+                    cudaStream_t st) {
+  VX_CUDA(cudaMemsetAsync(floor, 0, (size_t)Qp * 8, st));
+  a.floor = floor;
+  a.m_major = 0;
+  if (a.n > 2 * kPilotRows) {
+    ScanArgs p = a;
+    p.n = kPilotRows;
+    p.ntiles = kPilotRows / 256;
+    p.m_major = 1;
+    const int pgrid = std::min(a.num_mblocks, grid);
+    VX_CUDA(cudaMemsetAsync(a.cnts, 0, (size_t)pgrid * Qp * 4, st));
+    VX_CUDA(cudaMemsetAsync(a.thrs, 0, (size_t)pgrid * Qp * 8, st));
+    VX_TIMED(VX_PROF_PILOT, st, 1, launch_gemm_scan(mode, tmq, tmrows, p, pgrid, R, st));
+  }
+  VX_CUDA(cudaMemsetAsync(a.cnts, 0, (size_t)grid * Qp * 4, st));
+  VX_CUDA(cudaMemsetAsync(a.thrs, 0, (size_t)grid * Qp * 8, st));
+  VX_TIMED(VX_PROF_GEMM_SCAN, st, 1, launch_gemm_scan(mode, tmq, tmrows, a, grid, R, st));
+  VX_TIMED(VX_PROF_MERGE, st, 1,
+           launch_merge_streams(a.bufs, a.cnts, grid, a.nq, Qp, a.C, a.K, cand, cand_cnt, st, floor));
+}
+
+// One approximate pass with Kc candidates per query followed by the exact re-score; queries
+// whose candidate window fails the completeness test are appended to *flagged (indices into
+// dq) and their outputs are left for a later pass.
+int gemm_exact_pass(vx_index* ix, const float* dq, int nq, int k, int Kc, int32_t* d_ids,
+                    float* d_scores, int32_t* d_counts, cudaStream_t st,
+                    std::vector<int32_t>* flagged) {
   const bool f16_kind = ix->kind == VX_KIND_FP16;
   const int flavor = f16_kind ? kFlavorFp16Quantized : kFlavorFlat;
   const void* rows = f16_kind ? (const void*)ix->rows16 : (const void*)ix->rows32;
   const int64_t stride = f16_kind ? ix->Dp : ix->dim;
   const int dim = ix->dim;
-  const int Kc = candidate_width(k, ix->n);
   const int R = gemm_scan_stream_R(Kc);
   if (R < 0) return fail(VX_ERR_UNSUPPORTED, "k=%d is larger than this build supports", k);
   const int C = 32 * R;
@@ -372,22 +409,23 @@ int search_gemm_exact(vx_index* ix, const float* dq, int nq, int k, int32_t* d_i
     Scratch T(st);
     __half* qh = T.alloc<__half>((size_t)Qp * ix->Dp);
     float* qnorm = T.alloc<float>(qc);
+    float* qerr = T.alloc<float>(qc);
     float* margin = T.alloc<float>(qc);
     uint64_t* bufs = T.alloc<uint64_t>((size_t)grid * Qp * C);
     uint32_t* cnts = T.alloc<uint32_t>((size_t)grid * Qp);
     uint64_t* thrs = T.alloc<uint64_t>((size_t)grid * Qp);
+    uint64_t* floor = T.alloc<uint64_t>(Qp);
     uint64_t* cand = T.alloc<uint64_t>((size_t)qc * Kc);
     uint32_t* cand_cnt = T.alloc<uint32_t>(qc);
     int32_t* nflag = T.alloc<int32_t>(1);
     int32_t* flag_list = T.alloc<int32_t>(qc);
     const float* dqc = dq + (size_t)q0 * dim;
     VX_CUDA(cudaMemsetAsync(qh + (size_t)qc * ix->Dp, 0, (size_t)(Qp - qc) * ix->Dp * 2, st));
-    VX_LAUNCH(1, launch_rows_to_f16(dqc, qc, dim, dim, ix->Dp, true, qh, qnorm, nullptr, nullptr, st));
-    VX_LAUNCH(1, launch_margin(qnorm, qc, dim, ix->metric,
-                               f16_kind ? kOperandExactRows : kOperandUnitRows, ix->max_norm, margin,
-                               st));
-    VX_CUDA(cudaMemsetAsync(cnts, 0, (size_t)grid * Qp * 4, st));
-    VX_CUDA(cudaMemsetAsync(thrs, 0, (size_t)grid * Qp * 8, st));
+    VX_LAUNCH(1, launch_rows_to_f16(dqc, qc, dim, dim, ix->Dp, true, qh, qnorm, nullptr, nullptr, st,
+                                    qerr, nullptr));
+    VX_LAUNCH(1, launch_margin(qnorm, qerr, qc, dim, ix->metric,
+                               f16_kind ? kOperandExactRows : kOperandUnitRows, ix->max_norm,
+                               f16_kind ? ix->max_norm : ix->max_err, margin, st));
     VX_CUDA(cudaMemsetAsync(nflag, 0, 4, st));
     CUtensorMap tmq;
     make_tmap(&tmq, qh, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, ix->Dp, Qp, 128);
@@ -411,8 +449,7 @@ int search_gemm_exact(vx_index* ix, const float* dq, int nq, int k, int32_t* d_i
     a.epi.qsq = nullptr;
     a.epi.vsq = nullptr;
     a.epi.cm = 0.0f;
-    VX_TIMED(VX_PROF_GEMM_SCAN, st, 1, launch_gemm_scan(mode, tmq, ix->tm_rows, a, grid, R, st));
-    VX_TIMED(VX_PROF_MERGE, st, 1, launch_merge_streams(bufs, cnts, grid, qc, Qp, C, Kc, cand, cand_cnt, st));
+    scan_and_merge(mode, tmq, ix->tm_rows, a, grid, R, Qp, floor, cand, cand_cnt, st);
     RescoreArgs r;
     r.nq = qc;
     r.dim = dim;
@@ -444,10 +481,49 @@ int search_gemm_exact(vx_index* ix, const float* dq, int nq, int k, int32_t* d_i
       std::vector<int32_t> h_list(h_nflag);
       VX_CUDA(cudaMemcpyAsync(h_list.data(), flag_list, (size_t)h_nflag * 4, cudaMemcpyDeviceToHost, st));
       VX_CUDA(cudaStreamSynchronize(st));
-      exact_fallback(ix, dqc, qc, dim, k, flavor, rows, f16_kind, stride, h_list.data(), h_nflag,
-                     d_ids + (size_t)q0 * k, d_scores + (size_t)q0 * k, d_counts + q0, st);
+      for (int32_t f : h_list) flagged->push_back(q0 + f);
     }
   }
+  return VX_OK;
+}
+
+// FLAT / FP16: fp16 tcgen05 approximate pass + exact fp32 re-score, a wider second pass for
+// the queries whose window was too narrow, and the exact scan for any still unresolved.
+int search_gemm_exact(vx_index* ix, const float* dq, int nq, int k, int32_t* d_ids,
+                      float* d_scores, int32_t* d_counts, cudaStream_t st) {
+  const bool f16_kind = ix->kind == VX_KIND_FP16;
+  const int flavor = f16_kind ? kFlavorFp16Quantized : kFlavorFlat;
+  const void* rows = f16_kind ? (const void*)ix->rows16 : (const void*)ix->rows32;
+  const int64_t stride = f16_kind ? ix->Dp : ix->dim;
+  const int dim = ix->dim;
+  const int Kc1 = candidate_width(k, ix->n);
+  std::vector<int32_t> f1;
+  int rc = gemm_exact_pass(ix, dq, nq, k, Kc1, d_ids, d_scores, d_counts, st, &f1);
+  if (rc != VX_OK || f1.empty()) return rc;
+  std::vector<int32_t> rest;
+  const int Kc2 = (int)std::min<int64_t>(kMaxCandidates, std::max<int64_t>(ix->n, 1));
+  if (Kc2 > Kc1 && Kc2 > k) {
+    const int F = (int)f1.size();
+    Scratch S(st);
+    int32_t* map = S.alloc<int32_t>(F);
+    float* sub = S.alloc<float>((size_t)F * dim);
+    int32_t* ti = S.alloc<int32_t>((size_t)F * k);
+    float* ts = S.alloc<float>((size_t)F * k);
+    int32_t* tc = S.alloc<int32_t>(F);
+    VX_CUDA(cudaMemcpyAsync(map, f1.data(), (size_t)F * 4, cudaMemcpyHostToDevice, st));
+    VX_LAUNCH(1, launch_gather_rows(dq, map, F, dim, sub, st));
+    std::vector<int32_t> f2;
+    rc = gemm_exact_pass(ix, sub, F, k, Kc2, ti, ts, tc, st, &f2);
+    if (rc != VX_OK) return rc;
+    VX_LAUNCH(1, launch_scatter_results(ti, ts, tc, map, F, k, d_ids, d_scores, d_counts, st));
+    for (int32_t i : f2) rest.push_back(f1[i]);
+    VX_CUDA(cudaStreamSynchronize(st));
+  } else {
+    rest = f1;
+  }
+  if (!rest.empty())
+    exact_fallback(ix, dq, nq, dim, k, flavor, rows, f16_kind, stride, rest.data(), (int)rest.size(),
+                   d_ids, d_scores, d_counts, st);
   return VX_OK;
 }
 
@@ -482,13 +558,12 @@ int search_quantized_scan(vx_index* ix, const float* dq, int nq, int K, int k_ou
       uint64_t* bufs = T.alloc<uint64_t>((size_t)grid * Qp * C);
       uint32_t* cnts = T.alloc<uint32_t>((size_t)grid * Qp);
       uint64_t* thrs = T.alloc<uint64_t>((size_t)grid * Qp);
+      uint64_t* floor = T.alloc<uint64_t>(Qp);
       uint64_t* keys = T.alloc<uint64_t>((size_t)qc * K);
       uint32_t* kcnt = T.alloc<uint32_t>(qc);
       const float* dqc = dq + (size_t)q0 * dim;
       VX_CUDA(cudaMemsetAsync(qcodes + (size_t)qc * ix->Dp8, 0, (size_t)(Qp - qc) * ix->Dp8, st));
       VX_LAUNCH(1, launch_sq8_encode_queries(dqc, qc, dim, ix->Dp8, kc, qcodes, qcorr, qsq, st));
-      VX_CUDA(cudaMemsetAsync(cnts, 0, (size_t)grid * Qp * 4, st));
-      VX_CUDA(cudaMemsetAsync(thrs, 0, (size_t)grid * Qp * 8, st));
       CUtensorMap tmq;
       make_tmap(&tmq, qcodes, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, ix->Dp8, Qp, 128);
       ScanArgs a;
@@ -511,8 +586,7 @@ int search_quantized_scan(vx_index* ix, const float* dq, int nq, int K, int k_ou
       a.epi.qsq = qsq;
       a.epi.vsq = ix->vsq;
       a.epi.cm = kc.cm;
-      VX_TIMED(VX_PROF_GEMM_SCAN, st, 1, launch_gemm_scan(mode, tmq, ix->tm_codes8, a, grid, R, st));
-      VX_LAUNCH(1, launch_merge_streams(bufs, cnts, grid, qc, Qp, C, K, keys, kcnt, st));
+      scan_and_merge(mode, tmq, ix->tm_codes8, a, grid, R, Qp, floor, keys, kcnt, st);
       if (rescore) {
         RescoreArgs r{};
         r.nq = qc;
