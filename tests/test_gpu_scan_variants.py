@@ -1,0 +1,22 @@
+"""The 1-CTA tcgen05 scan and the scan without the pilot sweep agree with the oracle too
+(each variant in its own process: the library reads the switches once)."""
+import os
+import subprocess
+import sys
+
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+@pytest.mark.parametrize("env", [{"VX_GEMM_1SM": "1"}, {"VX_SCAN_PILOT": "0"}], ids=["one_cta", "no_pilot"])
+def test_scan_variant_matches_oracle(env):
+    e = dict(os.environ)
+    e.update(env)
+    e["PYTHONPATH"] = ROOT + os.pathsep + e.get("PYTHONPATH", "")
+    r = subprocess.run([sys.executable, os.path.join(ROOT, "tests", "variant_child.py")], env=e,
+                       capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-2000:]
+    assert "variant ok" in r.stdout

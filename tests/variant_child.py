@@ -1,0 +1,38 @@
+"""Child process for test_gpu_scan_variants.py: the scan variant is chosen by environment
+variables that the library reads once per process (VX_GEMM_1SM, VX_SCAN_PILOT), so each
+variant runs in a process of its own.  Exits 0 when FLAT and SQ8 results match the oracle."""
+import sys
+
+import numpy as np
+
+import vectors_b200 as vx
+from oracle import oracle as O
+
+
+def main():
+    db = O.gen_mixture(120_000, 96, 8, 0.3, 0xC0FFEE03, 0xC0FFEE01, True)
+    q = O.gen_mixture(300, 96, 8, 0.3, 0xC0FFEE03, 0xC0FFEE02, True)
+    for metric in (0, 2):
+        f = vx.FlatScanAdapter()
+        f.build(db, vx.SimilarityFunction(metric))
+        got = f.search_batch(q, 10)
+        ids, sc, cnt = O.flat_search(db, q, metric, 10)
+        for i, o in enumerate(got):
+            assert list(o.ordinals) == list(ids[i, : cnt[i]]), f"flat m={metric} query {i}"
+            np.testing.assert_allclose(o.scores, sc[i, : cnt[i]], rtol=1e-4, atol=0)
+        f.close()
+    lo, hi = O.sq8_train(db)
+    codes, corr = O.sq8_encode_all(lo, hi, db)
+    a = vx.QuantizedFlatScanAdapter()
+    a.build_sq8(codes, corr, lo, hi, vx.SimilarityFunction.DOT_PRODUCT)
+    got = a.scan_candidates(q, 100)
+    ids, sc, cnt = O.sq8_search(codes, corr, lo, hi, q, O.DOT_PRODUCT, 100)
+    for i, o in enumerate(got):
+        assert list(o.ordinals) == list(ids[i, : cnt[i]]), f"sq8 query {i}"
+        assert np.array_equal(o.scores, sc[i, : cnt[i]]), f"sq8 query {i} scores"
+    print("variant ok")
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -9,18 +9,22 @@
 //                   exactly into int32, followed by the reference score epilogue
 //                   (ScalarQuantizedVectors.java:82-107), bit-exact.
 //
-// Tiling.  A tile is 128 queries (TMEM lanes) x 256 database rows (TMEM columns), reduced
-// over the padded dimension in 128-byte K chunks (64 fp16 or 128 int8 elements) staged by
-// TMA with 128-byte swizzle through a 4-deep shared-memory ring (48 KB per stage).  Two
-// 256-column fp32/s32 accumulators (all 512 TMEM columns) let the epilogue of tile t overlap
-// the MMAs of tile t+1.  The (row-tile, query-block) pairs are dealt to CTAs in row-major
-// order so that consecutive tiles of one CTA reuse the same database tile from L2 and the
-// database streams from HBM about once per batch.
+// Tiling.  The default variant runs on 2-CTA clusters (tcgen05 cta_group::2): a cluster owns
+// a 256-query x 256-row tile; each CTA stages only its own 128 query rows and 128 database
+// rows of every 128-byte K chunk (64 fp16 / 128 int8 elements) through a 6-deep TMA ring with
+// 128-byte swizzle, i.e. 32 KB of shared memory traffic per SM for 128 x 256 x 64 MACs.  The
+// leader CTA issues the pair MMA; each CTA's TMEM holds its 128 queries x 256 rows in
+// fp32/s32, double buffered (512 columns) so that the epilogue of tile t overlaps the MMAs of
+// tile t+1.  A 1-CTA variant (128 x 256 tiles, 48 KB per stage) is kept for comparison.
+// (row-tile, query-block) pairs are dealt to clusters in row-major order so that consecutive
+// tiles reuse one database tile from L2 and the database streams from HBM about once per batch.
 //
-// Warp roles (192 threads): warp 0 issues TMA, warp 1 owns TMEM and issues tcgen05.mma,
-// warps 2-5 drain TMEM (warp w reads TMEM lanes 32*(w%4)..+31, i.e. one query per thread)
-// and feed each query's candidate stream (common.cuh).  Every wait is bounded in time; on
-// expiry the kernel records kDevWaitTimeout, the roles unwind and TMEM is released.
+// Warp roles (192 threads per CTA): warp 0 issues TMA, warp 1 owns TMEM and (leader only)
+// issues tcgen05.mma, warps 2-5 drain TMEM (warp w reads TMEM lanes 32*(w%4)..+31, i.e. one
+// query per thread) and feed each query's candidate stream (common.cuh).  The two CTAs of a
+// cluster own disjoint queries, so they share one set of streams.  Every wait is bounded in
+// time; on expiry the kernel records kDevWaitTimeout, the roles unwind and TMEM is released.
+// No TMA load uses cluster multicast.
 #include <cuda.h>
 #include "gemm_scan.h"
 #include "sm100.cuh"
@@ -30,23 +34,33 @@ namespace {
 
 using namespace sm100;
 
-constexpr int BM = 128;
-constexpr int BN = 256;
-constexpr int BK_BYTES = 128;
-constexpr int STAGES = 4;
-constexpr int A_BYTES = BM * BK_BYTES;
-constexpr int B_BYTES = BN * BK_BYTES;
-constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr int BN = 256;        // database rows per tile (TMEM columns per accumulator)
+constexpr int BK_BYTES = 128;  // bytes of K per stage row
 constexpr int NUM_THREADS = 192;
 constexpr int TMEM_COLS = 512;
-constexpr size_t SMEM_BYTES = 1024 + (size_t)STAGES * STAGE_BYTES + 4 * 2 * 256 * sizeof(float) + 256;
+constexpr int kStageRowWords = 36;  // per-lane staging row: 32 values + 4 words of padding
+                                    // (16-byte stores of 8 lanes hit 8 distinct bank quads)
+
+template <bool k2Sm>
+struct Geo {
+  static constexpr int kStages = k2Sm ? 6 : 4;
+  static constexpr int kRowsB = k2Sm ? 128 : 256;  // database rows staged per CTA
+  static constexpr int kABytes = 128 * BK_BYTES;    // 128 query rows per CTA
+  static constexpr int kBBytes = kRowsB * BK_BYTES;
+  static constexpr int kStageBytes = kABytes + kBBytes;               // per CTA
+  static constexpr int kTxBytes = k2Sm ? 2 * kStageBytes : kStageBytes;  // on the leader's barrier
+  static constexpr int kQueriesPerTile = k2Sm ? 256 : 128;
+  static constexpr size_t kSmem = 1024 + (size_t)kStages * kStageBytes + 4 * 2 * 256 * sizeof(float) +
+                                  4 * 32 * kStageRowWords * sizeof(uint32_t) + 256;
+  static_assert(kSmem <= 232448, "shared memory above the per-block limit");
+};
 
 __device__ __forceinline__ float thr_to_float(uint64_t thr) {
   return thr == 0 ? -INFINITY : key_score(thr);
 }
 
 // Pair p -> (row tile, query block): row-tile-major (consecutive pairs share the database
-// tile) or query-block-major (one CTA sweeps its query block over every row tile).
+// tile) or query-block-major (one CTA / cluster sweeps its query block over every row tile).
 __device__ __forceinline__ void tile_of(int64_t p, const ScanArgs& a, int64_t& nt, int& mb) {
   if (a.m_major) {
     mb = (int)(p / a.ntiles);
@@ -65,44 +79,155 @@ __device__ __forceinline__ void apply_floor(const ScanArgs& a, int q, bool activ
   }
 }
 
-template <bool kI8, int kMode, int R>
+// Ranking score of one accumulator value in epilogue mode kMode (gemm_scan.h).
+template <int kMode>
+__device__ __forceinline__ float score_of(uint32_t v, int col, const float* s_col, const float* s_col2,
+                                          float qa, int32_t qi, float cm) {
+  if (kMode == kEpiF16Plain) return __uint_as_float(v);
+  if (kMode == kEpiF16Scaled) return __uint_as_float(v) * s_col[col];
+  if (kMode == kEpiF16L2) return fmaf(qa * s_col[col], __uint_as_float(v), -s_col2[col]);
+  if (kMode == kEpiSq8Dot || kMode == kEpiSq8Mip) {
+    // rawDot * constMultiplier + queryCorrection + corrections[ordinal]
+    const float adj = __fadd_rn(__fadd_rn(__fmul_rn(__int2float_rn((int32_t)v), cm), qa), s_col[col]);
+    if (kMode == kEpiSq8Dot) {
+      const float h = __fmul_rn(__fadd_rn(1.0f, adj), 0.5f);  // (1f + adj) / 2f
+      return h >= 0.0f ? h : (h != h ? h : 0.0f);             // Math.max(h, 0f)
+    }
+    return scale_mip(adj);
+  }
+  // kEpiSq8L2: sum (q-v)^2 = sum q^2 + sum v^2 - 2 q.v, exact in int32
+  const int32_t sq = qi + __float_as_int(s_col[col]) - 2 * (int32_t)v;
+  return __fdiv_rn(1.0f, __fadd_rn(1.0f, __fmul_rn(__int2float_rn(sq), cm)));
+}
+
+// Per-lane state of one query's stream during a tile.
+struct TileStream {
+  LaneStream st;
+  float tf;     // score of the admission threshold
+  uint64_t t1;  // best admitted key
+  uint64_t t2;  // second best admitted key
+};
+
+// Slow path of one 32-column group, taken when some lane of the warp may admit a column:
+// builds the lane's pass mask, stages the lane's 32 values in its private shared-memory row
+// (so that the append loop can index them), compacts first when the stream could overflow,
+// then appends the passing columns in ascending order.
+template <int kMode, int R>
+__device__ __forceinline__ void offer_group(const ScanArgs& a, TileStream& ts, int q, bool active,
+                                            const uint32_t (&v)[32], int c0, int limit, int64_t col0,
+                                            const float* s_col, const float* s_col2, float qa, int32_t qi,
+                                            uint32_t* stage_row) {
+  uint32_t pm = 0;
+#pragma unroll
+  for (int j = 0; j < 32; j++)
+    pm |= (score_of<kMode>(v[j], c0 + j, s_col, s_col2, qa, qi, a.epi.cm) >= ts.tf ? 1u : 0u) << j;
+  if (limit < 32) pm &= limit <= 0 ? 0u : (0xFFFFFFFFu >> (32 - limit));  // rows beyond n
+  if (pm) {
+    uint4* d = reinterpret_cast<uint4*>(stage_row);
+#pragma unroll
+    for (int i = 0; i < 8; i++) d[i] = make_uint4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+  }
+  const bool need = ts.st.cnt + (uint32_t)__popc(pm) > (uint32_t)a.C;
+  if (__any_sync(0xFFFFFFFFu, need)) {
+    warp_compact_lanes<R>(need, ts.st.base, ts.st.cnt, ts.st.thr, (uint32_t)a.K);
+    if (need && a.floor && ts.st.cnt == (uint32_t)a.K)
+      atomicMax((unsigned long long*)&a.floor[q], (unsigned long long)ts.st.thr);
+    apply_floor(a, q, active, ts.st.thr);
+    ts.tf = active ? thr_to_float(ts.st.thr) : INFINITY;
+  }
+  while (pm) {
+    const int j = __ffs(pm) - 1;
+    pm &= pm - 1;
+    const int col = c0 + j;
+    const float sc = score_of<kMode>(stage_row[j], col, s_col, s_col2, qa, qi, a.epi.cm);
+    const uint64_t key = float_key(sc, (uint32_t)(col0 + col));
+    if (key > ts.st.thr) {
+      ts.st.base[ts.st.cnt++] = key;
+      if (key > ts.t1) {
+        ts.t2 = ts.t1;
+        ts.t1 = key;
+      } else if (key > ts.t2) {
+        ts.t2 = key;
+      }
+    }
+  }
+}
+
+// Largest score of a 32-column group (pairwise tree: one epilogue warp per scheduler, so the
+// dependency depth matters more than the operation count).
+template <int kMode>
+__device__ __forceinline__ float group_max(const uint32_t (&v)[32], int c0, const float* s_col,
+                                           const float* s_col2, float qa, int32_t qi, float cm) {
+  float m[16];
+#pragma unroll
+  for (int i = 0; i < 16; i++)
+    m[i] = fmaxf(score_of<kMode>(v[2 * i], c0 + 2 * i, s_col, s_col2, qa, qi, cm),
+                 score_of<kMode>(v[2 * i + 1], c0 + 2 * i + 1, s_col, s_col2, qa, qi, cm));
+#pragma unroll
+  for (int w = 8; w >= 1; w >>= 1)
+#pragma unroll
+    for (int i = 0; i < w; i++) m[i] = fmaxf(m[i], m[i + w]);
+  return m[0];
+}
+
+// Pooled-floor check after row tile li (0-based) of a unit's range: right after its first
+// tiles, then every 8th.
+__device__ __forceinline__ bool pool_check_due(int64_t li) {
+  return li < 8 ? (li == 0 || li == 1 || li == 3 || li == 7) : ((li & 7) == 7);
+}
+
+template <bool kI8, int kMode, int R, bool k2Sm>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gemm_scan_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const ScanArgs a) {
+  using G = Geo<k2Sm>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   uint8_t* stages = smem;
-  float* s_cols = (float*)(smem + (size_t)STAGES * STAGE_BYTES);  // [4 warps][2][256]
-  uint64_t* full = (uint64_t*)(s_cols + 4 * 2 * 256);
-  uint64_t* empty = full + STAGES;
-  uint64_t* tfull = empty + STAGES;
+  float* s_cols = (float*)(smem + (size_t)G::kStages * G::kStageBytes);  // [4 warps][2][256]
+  uint32_t* stage_rows = (uint32_t*)(s_cols + 4 * 2 * 256);               // [4 warps][32 lanes][36]
+  uint64_t* full = (uint64_t*)(stage_rows + 4 * 32 * kStageRowWords);
+  uint64_t* empty = full + G::kStages;
+  uint64_t* tfull = empty + G::kStages;
   uint64_t* tempty = tfull + 2;
   uint32_t* tmem_slot = (uint32_t*)(tempty + 2);
   volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = k2Sm ? cluster_ctarank() : 0u;
+  const bool leader = rank == 0;
+  const int unit = k2Sm ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;  // work unit: cluster or CTA
+  const int units = k2Sm ? (int)(gridDim.x >> 1) : (int)gridDim.x;
   const int64_t total = a.ntiles * (int64_t)a.num_mblocks;
-  const int64_t p0 = total * blockIdx.x / gridDim.x;
-  const int64_t p1 = total * (blockIdx.x + 1) / gridDim.x;
+  const int64_t p0 = total * unit / units;
+  const int64_t p1 = total * (unit + 1) / units;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < STAGES; s++) {
+    for (int s = 0; s < G::kStages; s++) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
     for (int b = 0; b < 2; b++) {
       mbar_init(&tfull[b], 1);
-      mbar_init(&tempty[b], 4);
+      mbar_init(&tempty[b], k2Sm ? 8 : 4);  // the epilogue warps of every CTA of the MMA
     }
     *abort_flag = 0;
     fence_mbar_init();
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, TMEM_COLS);
-    tmem_relinquish();
+    if (k2Sm) {
+      tmem_alloc_pair(tmem_slot, TMEM_COLS);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(tmem_slot, TMEM_COLS);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
-  __syncthreads();
+  if (k2Sm)
+    cluster_sync();  // both CTAs' barriers are initialised before any remote arrive
+  else
+    __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
@@ -116,6 +241,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       prefetch_tmap(&tmA);
       prefetch_tmap(&tmB);
       const uint64_t pol_a = policy_evict_last();  // query tiles are re-read by every row tile
+      const uint64_t pol_b = policy_evict_normal();
+      const uint32_t full0 = k2Sm ? mapa_shared(smem_addr(&full[0]), 0) : smem_addr(&full[0]);
       int stage = 0;
       uint32_t phase = 0;
       uint32_t used = 0;      // bit s: stage s has had a load issued
@@ -124,30 +251,40 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         int64_t nt;
         int mb;
         tile_of(p, a, nt, mb);
+        const int32_t ya = mb * G::kQueriesPerTile + (int)rank * 128;
+        const int32_t yb = (int32_t)(nt * BN) + (int)rank * G::kRowsB;
         for (int kc = 0; kc < a.kchunks; kc++) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, globaltimer_ns() + a.timeout_ns, abort_flag)) {
             give_up();
             break;
           }
-          mbar_arrive_expect_tx(&full[stage], STAGE_BYTES);
-          uint8_t* sa = stages + (size_t)stage * STAGE_BYTES;
+          uint8_t* sa = stages + (size_t)stage * G::kStageBytes;
           const int x = kc * (kI8 ? 128 : 64);
-          tma_load_2d_hint(sa, &tmA, &full[stage], x, mb * BM, pol_a);
-          tma_load_2d(sa + A_BYTES, &tmB, &full[stage], x, (int32_t)(nt * BN));
+          if (k2Sm) {
+            // both CTAs' bytes complete on the leader's full barrier
+            if (leader) mbar_arrive_expect_tx(&full[stage], G::kTxBytes);
+            const uint32_t bar = full0 + (uint32_t)(stage * 8);
+            tma_load_2d_pair(sa, &tmA, bar, x, ya, pol_a);
+            tma_load_2d_pair(sa + G::kABytes, &tmB, bar, x, yb, pol_b);
+          } else {
+            mbar_arrive_expect_tx(&full[stage], G::kTxBytes);
+            tma_load_2d_hint(sa, &tmA, &full[stage], x, ya, pol_a);
+            tma_load_2d_hint(sa + G::kABytes, &tmB, &full[stage], x, yb, pol_b);
+          }
           used |= 1u << stage;
           last_par = (last_par & ~(1u << stage)) | (phase << stage);
-          if (++stage == STAGES) {
+          if (++stage == G::kStages) {
             stage = 0;
             phase ^= 1u;
           }
         }
       }
-      if (*abort_flag) {
-        // Let every load already issued land before the CTA's shared memory is released.
+      if (*abort_flag && leader) {
+        // Let every load already issued land before the cluster's shared memory is released.
         const uint64_t until = globaltimer_ns() + a.timeout_ns;
         for (;;) {
           bool all = true;
-          for (int s = 0; s < STAGES; s++)
+          for (int s = 0; s < G::kStages; s++)
             if ((used >> s) & 1u)
               if (!mbar_try_wait(&full[s], (last_par >> s) & 1u)) all = false;
           if (all || globaltimer_ns() > until) break;
@@ -155,8 +292,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       }
     }
   } else if (warp == 1) {
-    if (lane == 0) {
-      const uint32_t idesc = kI8 ? idesc_s8_s32(BM, BN) : idesc_f16_f32(BM, BN);
+    if (lane == 0 && leader) {
+      const uint32_t idesc = kI8 ? idesc_s8_s32(k2Sm ? 256 : 128, BN) : idesc_f16_f32(k2Sm ? 256 : 128, BN);
       int stage = 0;
       uint32_t phase = 0;
       int64_t t = 0;
@@ -177,33 +314,50 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             break;
           }
           tc_fence_after();
-          const uint32_t sa = smem_addr(stages + (size_t)stage * STAGE_BYTES);
+          const uint32_t sa = smem_addr(stages + (size_t)stage * G::kStageBytes);
           const uint64_t da = sw128_kmajor_desc(sa);
-          const uint64_t db = sw128_kmajor_desc(sa + A_BYTES);
+          const uint64_t db = sw128_kmajor_desc(sa + G::kABytes);
 #pragma unroll
           for (int kk = 0; kk < 4; kk++) {
             const uint32_t accum = (kc | kk) != 0 ? 1u : 0u;
-            if (kI8)
-              mma_i8(d, da + 2ull * kk, db + 2ull * kk, idesc, accum);
-            else
-              mma_f16(d, da + 2ull * kk, db + 2ull * kk, idesc, accum);
+            if (k2Sm) {
+              if (kI8)
+                mma_i8_pair(d, da + 2ull * kk, db + 2ull * kk, idesc, accum);
+              else
+                mma_f16_pair(d, da + 2ull * kk, db + 2ull * kk, idesc, accum);
+            } else {
+              if (kI8)
+                mma_i8(d, da + 2ull * kk, db + 2ull * kk, idesc, accum);
+              else
+                mma_f16(d, da + 2ull * kk, db + 2ull * kk, idesc, accum);
+            }
           }
-          mma_commit(&empty[stage]);
-          if (++stage == STAGES) {
+          if (k2Sm)
+            mma_commit_pair_mc(&empty[stage], (uint16_t)0x3);
+          else
+            mma_commit(&empty[stage]);
+          if (++stage == G::kStages) {
             stage = 0;
             phase ^= 1u;
           }
         }
         if (!ok) break;
-        mma_commit(&tfull[acc]);
+        if (k2Sm)
+          mma_commit_pair_mc(&tfull[acc], (uint16_t)0x3);
+        else
+          mma_commit(&tfull[acc]);
       }
     }
   } else {
     // ---------------- epilogue: warps 2..5, one query (TMEM lane) per thread
     const int quarter = warp & 3;
-    const int row_in_block = quarter * 32 + lane;
-    const int etid = threadIdx.x - 64;
-    const int Qp = a.num_mblocks * BM;
+    const int row_in_block = (int)rank * 128 + quarter * 32 + lane;
+    const int Qp = a.num_mblocks * G::kQueriesPerTile;
+    const uint32_t tempty0 = k2Sm ? mapa_shared(smem_addr(&tempty[0]), 0) : smem_addr(&tempty[0]);
+    float* s_col = s_cols + (warp - 2) * 512;  // this warp's private column data
+    float* s_col2 = s_col + 256;
+    uint32_t* stage_row = stage_rows + (warp - 2) * (32 * kStageRowWords) + lane * kStageRowWords;
+    const int64_t nt_first = p0 / a.num_mblocks;  // first row tile of this unit (row-major dealing)
     int64_t t = 0;
     for (int64_t p = p0; p < p1; p++, t++) {
       int64_t nt;
@@ -212,8 +366,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const int acc = (int)(t & 1);
       const uint32_t acc_phase = (uint32_t)((t >> 1) & 1);
       const int64_t col0 = nt * BN;
-      float* s_col = s_cols + (warp - 2) * 512;  // this warp's private column data
-      float* s_col2 = s_col + 256;
       if (kMode != kEpiF16Plain) {
         __syncwarp();
         for (int i = lane; i < BN; i += 32) {
@@ -230,6 +382,24 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
         __syncwarp();
       }
+      const int q = mb * G::kQueriesPerTile + row_in_block;
+      const bool active = q < a.nq;
+      const size_t sidx = (size_t)unit * Qp + (size_t)q;
+      // Stream state does not depend on the accumulator: load it before waiting.
+      TileStream ts;
+      ts.st.base = a.bufs + sidx * (size_t)a.C;
+      ts.st.cnt = active ? a.cnts[sidx] : 0u;
+      ts.st.thr = active ? a.thrs[sidx] : ~0ull;
+      ts.t1 = (a.top1 && active) ? a.top1[sidx] : 0ull;
+      ts.t2 = (a.top1 && active) ? a.top2[sidx] : 0ull;
+      apply_floor(a, q, active, ts.st.thr);
+      float qa = 0.0f;
+      int32_t qi = 0;
+      if (active) {
+        if (kMode == kEpiF16L2) qa = 2.0f * a.epi.qscale[q];  // key = 2|q||x| acc - |x|^2
+        if (kMode == kEpiSq8Dot || kMode == kEpiSq8Mip) qa = a.epi.qscale[q];
+        if (kMode == kEpiSq8L2) qi = a.epi.qsq[q];
+      }
       if (__shfl_sync(0xFFFFFFFFu, *abort_flag, 0)) break;
       {
         bool ok = mbar_wait(&tfull[acc], acc_phase, globaltimer_ns() + a.timeout_ns, abort_flag);
@@ -240,86 +410,55 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
       }
       tc_fence_after();
-      const int q = mb * BM + row_in_block;
-      const bool active = q < a.nq;
-      const size_t sidx = (size_t)blockIdx.x * Qp + (size_t)q;
-      LaneStream st;
-      st.base = a.bufs + sidx * (size_t)a.C;
-      st.cnt = active ? a.cnts[sidx] : 0u;
-      st.thr = active ? a.thrs[sidx] : ~0ull;
-      apply_floor(a, q, active, st.thr);
-      float tf = active ? thr_to_float(st.thr) : INFINITY;
-      float qa = 0.0f;
-      int32_t qi = 0;
-      if (active) {
-        if (kMode == kEpiF16L2) qa = 2.0f * a.epi.qscale[q];  // key = 2|q||x| acc - |x|^2
-        if (kMode == kEpiSq8Dot || kMode == kEpiSq8Mip) qa = a.epi.qscale[q];
-        if (kMode == kEpiSq8L2) qi = a.epi.qsq[q];
-      }
+      ts.tf = active ? thr_to_float(ts.st.thr) : INFINITY;
       const int64_t left = a.n - col0;
       const int valid = left < BN ? (int)left : BN;
       const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * BN);
 #pragma unroll 1
-      for (int ch = 0; ch < BN / 32; ch++) {
+      for (int g = 0; g < BN / 32; g++) {
         uint32_t v[32];
         __syncwarp();
-        tmem_ld_32x32b_x32(taddr + (uint32_t)(ch * 32), v);
+        tmem_ld_32x32b_x32(taddr + (uint32_t)(g * 32), v);
         tmem_ld_wait();
-        if (ch * 32 < valid) {
-#pragma unroll
-          for (int j = 0; j < 32; j++) {
-            const int col = ch * 32 + j;
-            float s;
-            if (kMode == kEpiF16Plain) {
-              s = __uint_as_float(v[j]);
-            } else if (kMode == kEpiF16Scaled) {
-              s = __uint_as_float(v[j]) * s_col[col];
-            } else if (kMode == kEpiF16L2) {
-              s = fmaf(qa * s_col[col], __uint_as_float(v[j]), -s_col2[col]);
-            } else if (kMode == kEpiSq8Dot || kMode == kEpiSq8Mip) {
-              // rawDot * constMultiplier + queryCorrection + corrections[ordinal]
-              const float adj = __fadd_rn(
-                  __fadd_rn(__fmul_rn(__int2float_rn((int32_t)v[j]), a.epi.cm), qa),
-                  s_col[col]);
-              if (kMode == kEpiSq8Dot) {
-                const float h = __fmul_rn(__fadd_rn(1.0f, adj), 0.5f);  // (1f + adj) / 2f
-                s = h >= 0.0f ? h : (h != h ? h : 0.0f);               // Math.max(h, 0f)
-              } else {
-                s = scale_mip(adj);
-              }
-            } else {  // kEpiSq8L2: sum (q-v)^2 = sum q^2 + sum v^2 - 2 q.v, exact in int32
-              const int32_t sq = qi + __float_as_int(s_col[col]) - 2 * (int32_t)v[j];
-              s = __fdiv_rn(1.0f, __fadd_rn(1.0f, __fmul_rn(__int2float_rn(sq), a.epi.cm)));
-            }
-            if (col < valid && s >= tf) {
-              const uint64_t key = float_key(s, (uint32_t)(col0 + col));
-              if (key > st.thr) st.base[st.cnt++] = key;
-            }
-          }
-        }
-        const bool need = st.cnt > (uint32_t)(a.C - 32);
-        if (__any_sync(0xFFFFFFFFu, need)) {
-          warp_compact_lanes<R>(need, st.base, st.cnt, st.thr, (uint32_t)a.K);
-          if (need && a.floor && st.cnt == (uint32_t)a.K)
-            atomicMax((unsigned long long*)&a.floor[q], (unsigned long long)st.thr);
-          apply_floor(a, q, active, st.thr);
-          tf = active ? thr_to_float(st.thr) : INFINITY;
-        }
+        const int c0 = g * 32;
+        const float m = group_max<kMode>(v, c0, s_col, s_col2, qa, qi, a.epi.cm);
+        if (__any_sync(0xFFFFFFFFu, m >= ts.tf))
+          offer_group<kMode, R>(a, ts, q, active, v, c0, valid - c0, col0, s_col, s_col2, qa, qi, stage_row);
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&tempty[acc]);
+      if (lane == 0) {
+        if (k2Sm)
+          mbar_arrive_cluster(tempty0 + (uint32_t)(acc * 8));  // the leader issues the next MMA
+        else
+          mbar_arrive(&tempty[acc]);
+      }
       if (active) {
-        a.cnts[sidx] = st.cnt;
-        a.thrs[sidx] = st.thr;
+        a.cnts[sidx] = ts.st.cnt;
+        a.thrs[sidx] = ts.st.thr;
+        if (a.top1) {
+          a.top1[sidx] = ts.t1;
+          a.top2[sidx] = ts.t2;
+        }
+      }
+      // Pooled floor: propose this stream's j-th best key when enough streams of the query
+      // match it (staggered: each unit checks every 8th row tile).
+      if (a.top1 && pool_check_due(nt - nt_first)) {
+        const uint64_t mine = a.pool_j == 1 ? ts.t1 : ts.t2;
+        const uint64_t* arr = a.pool_j == 1 ? a.top1 : a.top2;
+        __syncwarp();
+        int c = 0;
+        for (int u = 0; u < units; u++) c += __ldcg((const unsigned long long*)arr + (size_t)u * Qp + q) >= mine;
+        if (active && mine != 0 && c >= a.pool_g)
+          atomicMax((unsigned long long*)&a.floor[q], (unsigned long long)mine);
       }
     }
     // Leave every stream this CTA wrote with at most K keys.
     if (!__shfl_sync(0xFFFFFFFFu, *abort_flag, 0)) {
       for (int mb = 0; mb < a.num_mblocks; mb++) {
-        const int q = mb * BM + row_in_block;
+        const int q = mb * G::kQueriesPerTile + row_in_block;
         const bool active = q < a.nq;
-        const size_t sidx = (size_t)blockIdx.x * Qp + (size_t)q;
+        const size_t sidx = (size_t)unit * Qp + (size_t)q;
         uint64_t* base = a.bufs + sidx * (size_t)a.C;
         uint32_t cnt = active ? a.cnts[sidx] : 0u;
         uint64_t thr = active ? a.thrs[sidx] : ~0ull;
@@ -335,61 +474,90 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   }
 
   tc_fence_before();
-  __syncthreads();
+  if (k2Sm)
+    cluster_sync();  // the pair's MMAs, loads and both epilogues are done with TMEM and smem
+  else
+    __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, TMEM_COLS);
+    if (k2Sm)
+      tmem_dealloc_pair(tmem_base, TMEM_COLS);
+    else
+      tmem_dealloc(tmem_base, TMEM_COLS);
   }
 }
 
-template <bool kI8, int kMode>
+template <bool kI8, int kMode, int R, bool k2Sm>
+cudaError_t launch_one(const CUtensorMap& tmA, const CUtensorMap& tmB, const ScanArgs& a, int grid,
+                       cudaStream_t st) {
+  auto kern = gemm_scan_kernel<kI8, kMode, R, k2Sm>;
+  const size_t smem = Geo<k2Sm>::kSmem;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  if (!k2Sm) {
+    kern<<<grid, NUM_THREADS, smem, st>>>(tmA, tmB, a);
+    return cudaGetLastError();
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)grid);
+  cfg.blockDim = dim3(NUM_THREADS);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, tmA, tmB, a);
+}
+
+template <bool kI8, int kMode, bool k2Sm>
 cudaError_t launch_mode(const CUtensorMap& tmA, const CUtensorMap& tmB, const ScanArgs& a, int grid,
                         int R, cudaStream_t st) {
-#define VX_GS_CASE(RR)                                                                         \
-  case RR: {                                                                                   \
-    auto kern = gemm_scan_kernel<kI8, kMode, RR>;                                              \
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,    \
-                                         (int)SMEM_BYTES);                                     \
-    if (e != cudaSuccess) return e;                                                            \
-    kern<<<grid, NUM_THREADS, SMEM_BYTES, st>>>(tmA, tmB, a);                                  \
-    return cudaGetLastError();                                                                 \
-  }
   switch (R) {
-    VX_GS_CASE(3)
-    VX_GS_CASE(5)
-    VX_GS_CASE(9)
-    VX_GS_CASE(17)
-    VX_GS_CASE(33)
+    case 3: return launch_one<kI8, kMode, 3, k2Sm>(tmA, tmB, a, grid, st);
+    case 5: return launch_one<kI8, kMode, 5, k2Sm>(tmA, tmB, a, grid, st);
+    case 9: return launch_one<kI8, kMode, 9, k2Sm>(tmA, tmB, a, grid, st);
+    case 17: return launch_one<kI8, kMode, 17, k2Sm>(tmA, tmB, a, grid, st);
+    case 33: return launch_one<kI8, kMode, 33, k2Sm>(tmA, tmB, a, grid, st);
     default: return cudaErrorInvalidValue;
   }
-#undef VX_GS_CASE
+}
+
+template <bool k2Sm>
+cudaError_t launch_variant(int mode, const CUtensorMap& tmA, const CUtensorMap& tmB, const ScanArgs& a,
+                           int grid, int R, cudaStream_t st) {
+  switch (mode) {
+    case kEpiF16Plain: return launch_mode<false, kEpiF16Plain, k2Sm>(tmA, tmB, a, grid, R, st);
+    case kEpiF16Scaled: return launch_mode<false, kEpiF16Scaled, k2Sm>(tmA, tmB, a, grid, R, st);
+    case kEpiF16L2: return launch_mode<false, kEpiF16L2, k2Sm>(tmA, tmB, a, grid, R, st);
+    case kEpiSq8Dot: return launch_mode<true, kEpiSq8Dot, k2Sm>(tmA, tmB, a, grid, R, st);
+    case kEpiSq8Mip: return launch_mode<true, kEpiSq8Mip, k2Sm>(tmA, tmB, a, grid, R, st);
+    case kEpiSq8L2: return launch_mode<true, kEpiSq8L2, k2Sm>(tmA, tmB, a, grid, R, st);
+    default: return cudaErrorInvalidValue;
+  }
 }
 
 }  // namespace
 
-int gemm_scan_grid(int64_t ntiles, int num_mblocks, int num_sms) {
-  int64_t total = ntiles * (int64_t)num_mblocks;
-  int64_t g = num_sms;
-  if (g > total) g = total;
-  return (int)(g < 1 ? 1 : g);
+int gemm_scan_units(int64_t ntiles, int num_mblocks, int num_sms, bool two_sm) {
+  const int64_t total = ntiles * (int64_t)num_mblocks;
+  int64_t u = two_sm ? num_sms / 2 : num_sms;
+  if (u > total) u = total;
+  return (int)(u < 1 ? 1 : u);
 }
 
 int gemm_scan_stream_R(int K) {
-  StreamGeom g = stream_geom(K, 32);
-  return g.R == 2 ? 3 : g.R;  // the GEMM scan instantiates R in {3,5,9,17,33}
+  StreamGeom g = stream_geom(K, 32);  // at most 32 appends between overflow checks
+  return g.R == 2 ? 3 : g.R;          // the GEMM scan instantiates R in {3,5,9,17,33}
 }
 
 cudaError_t launch_gemm_scan(int mode, const CUtensorMap& tmA, const CUtensorMap& tmB,
-                             const ScanArgs& a, int grid, int R, cudaStream_t st) {
-  switch (mode) {
-    case kEpiF16Plain: return launch_mode<false, kEpiF16Plain>(tmA, tmB, a, grid, R, st);
-    case kEpiF16Scaled: return launch_mode<false, kEpiF16Scaled>(tmA, tmB, a, grid, R, st);
-    case kEpiF16L2: return launch_mode<false, kEpiF16L2>(tmA, tmB, a, grid, R, st);
-    case kEpiSq8Dot: return launch_mode<true, kEpiSq8Dot>(tmA, tmB, a, grid, R, st);
-    case kEpiSq8Mip: return launch_mode<true, kEpiSq8Mip>(tmA, tmB, a, grid, R, st);
-    case kEpiSq8L2: return launch_mode<true, kEpiSq8L2>(tmA, tmB, a, grid, R, st);
-    default: return cudaErrorInvalidValue;
-  }
+                             const ScanArgs& a, int units, int R, bool two_sm, cudaStream_t st) {
+  return two_sm ? launch_variant<true>(mode, tmA, tmB, a, 2 * units, R, st)
+                : launch_variant<false>(mode, tmA, tmB, a, units, R, st);
 }
 
 }  // namespace vx

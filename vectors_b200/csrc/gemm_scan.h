@@ -30,25 +30,38 @@ struct EpiParams {
 struct ScanArgs {
   int64_t n;          // database rows
   int nq;             // queries (rows of the A operand beyond nq are zero padding)
-  int num_mblocks;    // ceil(nq / 128)
+  int num_mblocks;    // ceil(nq / queries per block): 256 for the 2-CTA variant, 128 otherwise
   int kchunks;        // padded row bytes / 128
   int64_t ntiles;     // ceil(n / 256)
   int K;              // keys kept per stream
   int C;              // stream buffer slots (32 * R)
-  uint64_t* bufs;     // [grid][num_mblocks*128][C]
-  uint32_t* cnts;     // [grid][num_mblocks*128]   (zeroed before launch)
-  uint64_t* thrs;     // [grid][num_mblocks*128]   (zeroed before launch)
-  int m_major;        // 1: deal (query-block, row-tile) pairs query-block-major (one CTA per block)
+  uint64_t* bufs;     // [units][Qp][C], Qp = num_mblocks * queries per block
+  uint32_t* cnts;     // [units][Qp]   (zeroed before launch)
+  uint64_t* thrs;     // [units][Qp]   (zeroed before launch)
+  int m_major;        // 1: deal (query-block, row-tile) pairs query-block-major (one unit per block)
   uint64_t* floor;    // [nq] shared admission floors (nullable): any stream holding K keys
                       // publishes its K-th key; every stream admits only keys >= floor
+  // Pooled floors (nullable top1): every stream tracks its two best admitted keys; a stream
+  // whose j-th best key x (j = pool_j in {1, 2}) is matched by the j-th best keys of at least
+  // pool_g streams of the same query (pool_g * pool_j >= K) raises that query's floor to x:
+  // the streams cover disjoint rows, so at least K rows score >= x.
+  uint64_t* top1;     // [units][Qp] best admitted key per stream (zeroed before launch)
+  uint64_t* top2;     // [units][Qp] second best admitted key per stream (zeroed before launch)
+  int pool_j;
+  int pool_g;
   int32_t* err;       // device error word
   uint64_t timeout_ns;
   EpiParams epi;
 };
 
-int gemm_scan_grid(int64_t ntiles, int num_mblocks, int num_sms);
+// A work unit is a 2-CTA cluster (two_sm) or one CTA; each unit owns one candidate stream per
+// query.  The query operand's tensor map has a 128-row box in both variants; the database
+// operand's box is 128 rows with two_sm and 256 rows without.
+constexpr int gemm_scan_query_block(bool two_sm) { return two_sm ? 256 : 128; }
+constexpr int gemm_scan_db_box(bool two_sm) { return two_sm ? 128 : 256; }
+int gemm_scan_units(int64_t ntiles, int num_mblocks, int num_sms, bool two_sm);
 int gemm_scan_stream_R(int K);
 cudaError_t launch_gemm_scan(int mode, const CUtensorMap& tmA, const CUtensorMap& tmB,
-                             const ScanArgs& a, int grid, int R, cudaStream_t st);
+                             const ScanArgs& a, int units, int R, bool two_sm, cudaStream_t st);
 
 }  // namespace vx

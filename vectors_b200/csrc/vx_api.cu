@@ -170,6 +170,25 @@ uint64_t wait_timeout_ns() {
   return 1500ull * 1000000ull;  // 1.5 s per wait
 }
 
+// The pilot sweep before each scan is on unless VX_SCAN_PILOT=0.
+bool use_pilot() {
+  static const bool v = [] {
+    const char* e = getenv("VX_SCAN_PILOT");
+    return !(e && *e == '0');
+  }();
+  return v;
+}
+
+// The tcgen05 scan runs on 2-CTA clusters unless VX_GEMM_1SM=1 selects the 1-CTA variant
+// (read once per process: index tensor maps are built for the variant in use).
+bool gemm_two_sm() {
+  static const bool v = [] {
+    const char* e = getenv("VX_GEMM_1SM");
+    return !(e && *e && *e != '0');
+  }();
+  return v;
+}
+
 }  // namespace
 
 // Shared with noalloc.cu (internal to the library, not exported).
@@ -219,6 +238,13 @@ int check_device(int device, int* nsms) {
   if (cudaSetDevice(device) != cudaSuccess)
     return fail(VX_ERR_GPU_UNAVAILABLE, "cannot select device %d", device);
   *nsms = prop.multiProcessorCount;
+  // Keep the per-search scratch cached in the device's stream-ordered pool between calls
+  // (the default threshold returns it to the driver at every synchronisation).
+  cudaMemPool_t pool;
+  if (cudaDeviceGetDefaultMemPool(&pool, device) == cudaSuccess) {
+    uint64_t keep = UINT64_MAX;
+    cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep);
+  }
   return VX_OK;
 }
 
@@ -249,7 +275,8 @@ void build_unit_f16(vx_index* ix) {
   VX_LAUNCH(1, launch_rows_to_f16(ix->rows32, ix->n, ix->dim, ix->dim, ix->Dp, true, ix->rows16,
                                   ix->rowscale, ix->rowsq, ix->max_norm, 0, nullptr, ix->max_err));
   if (ix->n > 0) {
-    make_tmap(&ix->tm_rows, ix->rows16, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, ix->Dp, ix->n, 256);
+    make_tmap(&ix->tm_rows, ix->rows16, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, ix->Dp, ix->n,
+             gemm_scan_db_box(gemm_two_sm()));
     ix->has_tm_rows = true;
   }
   VX_CUDA(cudaDeviceSynchronize());
@@ -350,26 +377,38 @@ int candidate_width(int k, int64_t n) {
 constexpr int64_t kPilotRows = 32768;
 
 void scan_and_merge(int mode, const CUtensorMap& tmq, const CUtensorMap& tmrows, ScanArgs a,
-                    int grid, int R, int Qp, uint64_t* floor, uint64_t* cand, uint32_t* cand_cnt,
-                    cudaStream_t st) {
+                    int units, int R, int Qp, uint64_t* floor, uint64_t* tops, uint64_t* cand,
+                    uint32_t* cand_cnt, cudaStream_t st) {
+  const bool two_sm = gemm_two_sm();
   VX_CUDA(cudaMemsetAsync(floor, 0, (size_t)Qp * 8, st));
   a.floor = floor;
   a.m_major = 0;
-  if (a.n > 2 * kPilotRows) {
+  // Pooled floors need K <= 2 * (streams per query); each stream then contributes its best
+  // (pool_j = 1) or second best (pool_j = 2) key.
+  a.top1 = a.top2 = nullptr;
+  a.pool_j = a.K <= units ? 1 : (a.K <= 2 * units ? 2 : 0);
+  a.pool_g = a.pool_j ? (a.K + a.pool_j - 1) / a.pool_j : 0;
+  if (a.pool_j && tops) {
+    a.top1 = tops;
+    a.top2 = tops + (size_t)units * Qp;
+    VX_CUDA(cudaMemsetAsync(tops, 0, (size_t)2 * units * Qp * 8, st));
+  }
+  if (a.n > 2 * kPilotRows && use_pilot()) {
     ScanArgs p = a;
+    p.top1 = p.top2 = nullptr;
     p.n = kPilotRows;
     p.ntiles = kPilotRows / 256;
     p.m_major = 1;
-    const int pgrid = std::min(a.num_mblocks, grid);
-    VX_CUDA(cudaMemsetAsync(a.cnts, 0, (size_t)pgrid * Qp * 4, st));
-    VX_CUDA(cudaMemsetAsync(a.thrs, 0, (size_t)pgrid * Qp * 8, st));
-    VX_TIMED(VX_PROF_PILOT, st, 1, launch_gemm_scan(mode, tmq, tmrows, p, pgrid, R, st));
+    const int punits = std::min(a.num_mblocks, units);
+    VX_CUDA(cudaMemsetAsync(a.cnts, 0, (size_t)punits * Qp * 4, st));
+    VX_CUDA(cudaMemsetAsync(a.thrs, 0, (size_t)punits * Qp * 8, st));
+    VX_TIMED(VX_PROF_PILOT, st, 1, launch_gemm_scan(mode, tmq, tmrows, p, punits, R, two_sm, st));
   }
-  VX_CUDA(cudaMemsetAsync(a.cnts, 0, (size_t)grid * Qp * 4, st));
-  VX_CUDA(cudaMemsetAsync(a.thrs, 0, (size_t)grid * Qp * 8, st));
-  VX_TIMED(VX_PROF_GEMM_SCAN, st, 1, launch_gemm_scan(mode, tmq, tmrows, a, grid, R, st));
+  VX_CUDA(cudaMemsetAsync(a.cnts, 0, (size_t)units * Qp * 4, st));
+  VX_CUDA(cudaMemsetAsync(a.thrs, 0, (size_t)units * Qp * 8, st));
+  VX_TIMED(VX_PROF_GEMM_SCAN, st, 1, launch_gemm_scan(mode, tmq, tmrows, a, units, R, two_sm, st));
   VX_TIMED(VX_PROF_MERGE, st, 1,
-           launch_merge_streams(a.bufs, a.cnts, grid, a.nq, Qp, a.C, a.K, cand, cand_cnt, st, floor));
+           launch_merge_streams(a.bufs, a.cnts, units, a.nq, Qp, a.C, a.K, cand, cand_cnt, st, floor));
 }
 
 // One approximate pass with Kc candidates per query followed by the exact re-score; queries
@@ -395,30 +434,40 @@ int gemm_exact_pass(vx_index* ix, const float* dq, int nq, int k, int Kc, int32_
   else
     mode = kEpiF16Scaled;
   // query chunk sized by the scratch budget
-  const int G0 = gemm_scan_grid(ntiles, 1 << 20, ix->num_sms);
-  int64_t qch = (int64_t)(scratch_budget() / ((size_t)G0 * (C * 8 + 12)));
-  qch = std::max<int64_t>(128, qch / 128 * 128);
+  const bool two_sm = gemm_two_sm();
+  const int QB = gemm_scan_query_block(two_sm);
+  const int U0 = gemm_scan_units(ntiles, 1 << 20, ix->num_sms, two_sm);
+  int64_t qch = (int64_t)(scratch_budget() / ((size_t)U0 * (C * 8 + 12)));
+  qch = std::max<int64_t>(QB, qch / QB * QB);
+  // Buffers are sized once for the largest chunk and reused, so repeated calls draw blocks
+  // of one size from the stream-ordered pool.
+  const int qmax = (int)std::min<int64_t>(qch, std::max(nq, 1));
+  const int QpMax = (qmax + QB - 1) / QB * QB;
+  const int unitsMax = gemm_scan_units(ntiles, QpMax / QB, ix->num_sms, two_sm);
+  const int nchunks = (int)((nq + qch - 1) / qch);
   Scratch S(st);
   int32_t* d_err = S.alloc<int32_t>(1);
+  __half* qh = S.alloc<__half>((size_t)QpMax * ix->Dp);
+  float* qnorm = S.alloc<float>(QpMax);
+  float* qerr = S.alloc<float>(QpMax);
+  float* margin = S.alloc<float>(QpMax);
+  uint64_t* bufs = S.alloc<uint64_t>((size_t)unitsMax * QpMax * C);
+  uint32_t* cnts = S.alloc<uint32_t>((size_t)unitsMax * QpMax);
+  uint64_t* thrs = S.alloc<uint64_t>((size_t)unitsMax * QpMax);
+  uint64_t* floor = S.alloc<uint64_t>(QpMax);
+  uint64_t* tops = S.alloc<uint64_t>((size_t)2 * unitsMax * QpMax);
+  uint64_t* cand = S.alloc<uint64_t>((size_t)qmax * Kc);
+  uint32_t* cand_cnt = S.alloc<uint32_t>(qmax);
+  int32_t* nflag = S.alloc<int32_t>(std::max(nchunks, 1));
+  int32_t* flag_list = S.alloc<int32_t>(std::max(nq, 1));
   VX_CUDA(cudaMemsetAsync(d_err, 0, 4, st));
-  for (int q0 = 0; q0 < nq; q0 += (int)qch) {
+  VX_CUDA(cudaMemsetAsync(nflag, 0, (size_t)std::max(nchunks, 1) * 4, st));
+  for (int c = 0; c < nchunks; c++) {
+    const int q0 = (int)(c * qch);
     const int qc = (int)std::min<int64_t>(qch, nq - q0);
-    const int mblocks = (qc + 127) / 128;
-    const int Qp = mblocks * 128;
-    const int grid = gemm_scan_grid(ntiles, mblocks, ix->num_sms);
-    Scratch T(st);
-    __half* qh = T.alloc<__half>((size_t)Qp * ix->Dp);
-    float* qnorm = T.alloc<float>(qc);
-    float* qerr = T.alloc<float>(qc);
-    float* margin = T.alloc<float>(qc);
-    uint64_t* bufs = T.alloc<uint64_t>((size_t)grid * Qp * C);
-    uint32_t* cnts = T.alloc<uint32_t>((size_t)grid * Qp);
-    uint64_t* thrs = T.alloc<uint64_t>((size_t)grid * Qp);
-    uint64_t* floor = T.alloc<uint64_t>(Qp);
-    uint64_t* cand = T.alloc<uint64_t>((size_t)qc * Kc);
-    uint32_t* cand_cnt = T.alloc<uint32_t>(qc);
-    int32_t* nflag = T.alloc<int32_t>(1);
-    int32_t* flag_list = T.alloc<int32_t>(qc);
+    const int mblocks = (qc + QB - 1) / QB;
+    const int Qp = mblocks * QB;
+    const int units = gemm_scan_units(ntiles, mblocks, ix->num_sms, two_sm);
     const float* dqc = dq + (size_t)q0 * dim;
     VX_CUDA(cudaMemsetAsync(qh + (size_t)qc * ix->Dp, 0, (size_t)(Qp - qc) * ix->Dp * 2, st));
     VX_LAUNCH(1, launch_rows_to_f16(dqc, qc, dim, dim, ix->Dp, true, qh, qnorm, nullptr, nullptr, st,
@@ -426,7 +475,6 @@ int gemm_exact_pass(vx_index* ix, const float* dq, int nq, int k, int Kc, int32_
     VX_LAUNCH(1, launch_margin(qnorm, qerr, qc, dim, ix->metric,
                                f16_kind ? kOperandExactRows : kOperandUnitRows, ix->max_norm,
                                f16_kind ? ix->max_norm : ix->max_err, margin, st));
-    VX_CUDA(cudaMemsetAsync(nflag, 0, 4, st));
     CUtensorMap tmq;
     make_tmap(&tmq, qh, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, ix->Dp, Qp, 128);
     ScanArgs a;
@@ -449,7 +497,7 @@ int gemm_exact_pass(vx_index* ix, const float* dq, int nq, int k, int Kc, int32_
     a.epi.qsq = nullptr;
     a.epi.vsq = nullptr;
     a.epi.cm = 0.0f;
-    scan_and_merge(mode, tmq, ix->tm_rows, a, grid, R, Qp, floor, cand, cand_cnt, st);
+    scan_and_merge(mode, tmq, ix->tm_rows, a, units, R, Qp, floor, tops, cand, cand_cnt, st);
     RescoreArgs r;
     r.nq = qc;
     r.dim = dim;
@@ -469,20 +517,22 @@ int gemm_exact_pass(vx_index* ix, const float* dq, int nq, int k, int Kc, int32_
     r.out_ids = d_ids + (size_t)q0 * k;
     r.out_scores = d_scores + (size_t)q0 * k;
     r.out_counts = d_counts + q0;
-    r.nflag = nflag;
-    r.flag_list = flag_list;
+    r.nflag = nflag + c;
+    r.flag_list = flag_list + q0;
     VX_TIMED(VX_PROF_RESCORE, st, 1, launch_rescore(r, f16_kind, st));
-    int st_err = check_device_error(d_err, st);
-    if (st_err != VX_OK) return st_err;
-    int32_t h_nflag = 0;
-    VX_CUDA(cudaMemcpyAsync(&h_nflag, nflag, 4, cudaMemcpyDeviceToHost, st));
+  }
+  int st_err = check_device_error(d_err, st);
+  if (st_err != VX_OK) return st_err;
+  std::vector<int32_t> h_nflag(std::max(nchunks, 1), 0);
+  VX_CUDA(cudaMemcpyAsync(h_nflag.data(), nflag, (size_t)nchunks * 4, cudaMemcpyDeviceToHost, st));
+  VX_CUDA(cudaStreamSynchronize(st));
+  for (int c = 0; c < nchunks; c++) {
+    if (h_nflag[c] <= 0) continue;
+    const int q0 = (int)(c * qch);
+    std::vector<int32_t> h_list(h_nflag[c]);
+    VX_CUDA(cudaMemcpyAsync(h_list.data(), flag_list + q0, (size_t)h_nflag[c] * 4, cudaMemcpyDeviceToHost, st));
     VX_CUDA(cudaStreamSynchronize(st));
-    if (h_nflag > 0) {
-      std::vector<int32_t> h_list(h_nflag);
-      VX_CUDA(cudaMemcpyAsync(h_list.data(), flag_list, (size_t)h_nflag * 4, cudaMemcpyDeviceToHost, st));
-      VX_CUDA(cudaStreamSynchronize(st));
-      for (int32_t f : h_list) flagged->push_back(q0 + f);
-    }
+    for (int32_t f : h_list) flagged->push_back(q0 + f);
   }
   return VX_OK;
 }
@@ -539,28 +589,36 @@ int search_quantized_scan(vx_index* ix, const float* dq, int nq, int K, int k_ou
     if (R < 0) return fail(VX_ERR_UNSUPPORTED, "k=%d is larger than this build supports", K);
     const int C = 32 * R;
     const int64_t ntiles = (ix->n + 255) / 256;
-    const int G0 = gemm_scan_grid(ntiles, 1 << 20, ix->num_sms);
-    int64_t qch = (int64_t)(scratch_budget() / ((size_t)G0 * (C * 8 + 12)));
-    qch = std::max<int64_t>(128, qch / 128 * 128);
+    const bool two_sm = gemm_two_sm();
+    const int QB = gemm_scan_query_block(two_sm);
+    const int U0 = gemm_scan_units(ntiles, 1 << 20, ix->num_sms, two_sm);
+    int64_t qch = (int64_t)(scratch_budget() / ((size_t)U0 * (C * 8 + 12)));
+    qch = std::max<int64_t>(QB, qch / QB * QB);
     const int mode = ix->metric == VX_EUCLIDEAN ? kEpiSq8L2
                      : ix->metric == VX_MAXIMUM_INNER_PRODUCT ? kEpiSq8Mip
                                                               : kEpiSq8Dot;
     const Sq8Consts kc = sq8_consts(ix->min_q, ix->max_q);
+    // sized once for the largest chunk and reused by every chunk
+    const int qmax = (int)std::min<int64_t>(qch, std::max(nq, 1));
+    const int QpMax = (qmax + QB - 1) / QB * QB;
+    const int unitsMax = gemm_scan_units(ntiles, QpMax / QB, ix->num_sms, two_sm);
+    int8_t* qcodes = S.alloc<int8_t>((size_t)QpMax * ix->Dp8);
+    float* qcorr = S.alloc<float>(QpMax);
+    int32_t* qsq = S.alloc<int32_t>(QpMax);
+    uint64_t* bufs = S.alloc<uint64_t>((size_t)unitsMax * QpMax * C);
+    uint32_t* cnts = S.alloc<uint32_t>((size_t)unitsMax * QpMax);
+    uint64_t* thrs = S.alloc<uint64_t>((size_t)unitsMax * QpMax);
+    uint64_t* floor = S.alloc<uint64_t>(QpMax);
+    uint64_t* tops = S.alloc<uint64_t>((size_t)2 * unitsMax * QpMax);
+    uint64_t* keys = S.alloc<uint64_t>((size_t)qmax * K);
+    uint32_t* kcnt = S.alloc<uint32_t>(qmax);
+    int32_t* nflag = S.alloc<int32_t>(1);
+    int32_t* flag_list = S.alloc<int32_t>(qmax);
     for (int q0 = 0; q0 < nq; q0 += (int)qch) {
       const int qc = (int)std::min<int64_t>(qch, nq - q0);
-      const int mblocks = (qc + 127) / 128;
-      const int Qp = mblocks * 128;
-      const int grid = gemm_scan_grid(ntiles, mblocks, ix->num_sms);
-      Scratch T(st);
-      int8_t* qcodes = T.alloc<int8_t>((size_t)Qp * ix->Dp8);
-      float* qcorr = T.alloc<float>(qc);
-      int32_t* qsq = T.alloc<int32_t>(qc);
-      uint64_t* bufs = T.alloc<uint64_t>((size_t)grid * Qp * C);
-      uint32_t* cnts = T.alloc<uint32_t>((size_t)grid * Qp);
-      uint64_t* thrs = T.alloc<uint64_t>((size_t)grid * Qp);
-      uint64_t* floor = T.alloc<uint64_t>(Qp);
-      uint64_t* keys = T.alloc<uint64_t>((size_t)qc * K);
-      uint32_t* kcnt = T.alloc<uint32_t>(qc);
+      const int mblocks = (qc + QB - 1) / QB;
+      const int Qp = mblocks * QB;
+      const int units = gemm_scan_units(ntiles, mblocks, ix->num_sms, two_sm);
       const float* dqc = dq + (size_t)q0 * dim;
       VX_CUDA(cudaMemsetAsync(qcodes + (size_t)qc * ix->Dp8, 0, (size_t)(Qp - qc) * ix->Dp8, st));
       VX_LAUNCH(1, launch_sq8_encode_queries(dqc, qc, dim, ix->Dp8, kc, qcodes, qcorr, qsq, st));
@@ -586,7 +644,7 @@ int search_quantized_scan(vx_index* ix, const float* dq, int nq, int K, int k_ou
       a.epi.qsq = qsq;
       a.epi.vsq = ix->vsq;
       a.epi.cm = kc.cm;
-      scan_and_merge(mode, tmq, ix->tm_codes8, a, grid, R, Qp, floor, keys, kcnt, st);
+      scan_and_merge(mode, tmq, ix->tm_codes8, a, units, R, Qp, floor, tops, keys, kcnt, st);
       if (rescore) {
         RescoreArgs r{};
         r.nq = qc;
@@ -605,8 +663,8 @@ int search_quantized_scan(vx_index* ix, const float* dq, int nq, int K, int k_ou
         r.out_ids = d_ids + (size_t)q0 * k_out;
         r.out_scores = d_scores + (size_t)q0 * k_out;
         r.out_counts = d_counts + q0;
-        r.nflag = T.alloc<int32_t>(1);
-        r.flag_list = T.alloc<int32_t>(qc);
+        r.nflag = nflag;
+        r.flag_list = flag_list;
         VX_LAUNCH(1, launch_rescore(r, false, st));
       } else {
         VX_LAUNCH(1, launch_finish_keys(keys, kcnt, qc, K, k_out, kFinishFloatKey, ix->metric, dim,
@@ -620,15 +678,18 @@ int search_quantized_scan(vx_index* ix, const float* dq, int nq, int K, int k_ou
     const int parts = bq_parts(ix->n, ix->num_sms);
     int64_t qch = (int64_t)(scratch_budget() / ((size_t)parts * (g.C * 8 + 12)));
     qch = std::max<int64_t>(256, qch / 256 * 256);
+    // sized once for the largest chunk and reused by every chunk
+    const int qmax = (int)std::min<int64_t>(qch, std::max(nq, 1));
+    uint64_t* qw = S.alloc<uint64_t>((size_t)qmax * ix->nw_pad);
+    uint64_t* bufs = S.alloc<uint64_t>((size_t)parts * qmax * g.C);
+    uint32_t* cnts = S.alloc<uint32_t>((size_t)parts * qmax);
+    uint64_t* thrs = S.alloc<uint64_t>((size_t)parts * qmax);
+    uint64_t* keys = S.alloc<uint64_t>((size_t)qmax * K);
+    uint32_t* kcnt = S.alloc<uint32_t>(qmax);
+    int32_t* nflag = S.alloc<int32_t>(1);
+    int32_t* flag_list = S.alloc<int32_t>(qmax);
     for (int q0 = 0; q0 < nq; q0 += (int)qch) {
       const int qc = (int)std::min<int64_t>(qch, nq - q0);
-      Scratch T(st);
-      uint64_t* qw = T.alloc<uint64_t>((size_t)qc * ix->nw_pad);
-      uint64_t* bufs = T.alloc<uint64_t>((size_t)parts * qc * g.C);
-      uint32_t* cnts = T.alloc<uint32_t>((size_t)parts * qc);
-      uint64_t* thrs = T.alloc<uint64_t>((size_t)parts * qc);
-      uint64_t* keys = T.alloc<uint64_t>((size_t)qc * K);
-      uint32_t* kcnt = T.alloc<uint32_t>(qc);
       const float* dqc = dq + (size_t)q0 * dim;
       VX_LAUNCH(1, launch_bq_pack_queries(dqc, qc, dim, ix->nw_pad, qw, st));
       VX_CUDA(cudaMemsetAsync(cnts, 0, (size_t)parts * qc * 4, st));
@@ -653,8 +714,8 @@ int search_quantized_scan(vx_index* ix, const float* dq, int nq, int K, int k_ou
         r.out_ids = d_ids + (size_t)q0 * k_out;
         r.out_scores = d_scores + (size_t)q0 * k_out;
         r.out_counts = d_counts + q0;
-        r.nflag = T.alloc<int32_t>(1);
-        r.flag_list = T.alloc<int32_t>(qc);
+        r.nflag = nflag;
+        r.flag_list = flag_list;
         VX_LAUNCH(1, launch_rescore(r, false, st));
       } else {
         VX_LAUNCH(1, launch_finish_keys(keys, kcnt, qc, K, k_out, kFinishHamming, ix->metric, dim,
@@ -1066,7 +1127,8 @@ int vx_fp16_build(int32_t device, const uint16_t* codes, int64_t n, int32_t dim,
         VX_LAUNCH(1, launch_f16_rows_pad(raw, n, dim, ix->Dp, ix->rows16, ix->rowsq, ix->max_norm, 0));
         VX_CUDA(cudaDeviceSynchronize());
         cudaFree(raw);
-        make_tmap(&ix->tm_rows, ix->rows16, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, ix->Dp, n, 256);
+        make_tmap(&ix->tm_rows, ix->rows16, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, ix->Dp, n,
+                 gemm_scan_db_box(gemm_two_sm()));
         ix->has_tm_rows = true;
         if (vectors) ix->rows32 = upload_rows32(ix, vectors, n, dim, row_stride);
       }
@@ -1117,7 +1179,8 @@ int vx_sq8_build(int32_t device, const int8_t* codes, const float* corrections, 
         VX_LAUNCH(1, launch_sq8_rows_pad(raw, n, dim, ix->Dp8, ix->codes8, ix->vsq, 0));
         VX_CUDA(cudaDeviceSynchronize());
         cudaFree(raw);
-        make_tmap(&ix->tm_codes8, ix->codes8, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, ix->Dp8, n, 256);
+        make_tmap(&ix->tm_codes8, ix->codes8, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, ix->Dp8, n,
+                 gemm_scan_db_box(gemm_two_sm()));
         if (vectors) ix->rows32 = upload_rows32(ix, vectors, n, dim, row_stride);
       }
     } catch (...) {
