@@ -331,18 +331,12 @@ def main():
     q_np = q_pinned.numpy()
 
     def e2e_step():
-        res = flat.search_batch(q_np, k)  # H2D queries, scan, D2H results (blocking)
+        # the host-buffer C ABI call: H2D queries, scan, D2H results (blocking)
+        res = flat.search_batch_arrays(q_np, k)
         if world == 1:
             return res
         # shard results meet through the same NCCL all-gather + device merge, then D2H
-        li = torch.full((nq, k), -1, dtype=torch.int32)
-        ls = torch.zeros((nq, k), dtype=torch.float32)
-        lc = torch.zeros((nq,), dtype=torch.int32)
-        for i, o in enumerate(res):
-            c = len(o.ordinals)
-            li[i, :c] = torch.from_numpy(o.ordinals)
-            ls[i, :c] = torch.from_numpy(o.scores)
-            lc[i] = c
+        li, ls, lc = (torch.from_numpy(a) for a in res)
         gi = torch.empty((world, nq, k), dtype=torch.int32, device=dev)
         gs = torch.empty((world, nq, k), dtype=torch.float32, device=dev)
         gc = torch.empty((world, nq), dtype=torch.int32, device=dev)

@@ -254,7 +254,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const int32_t ya = mb * G::kQueriesPerTile + (int)rank * 128;
         const int32_t yb = (int32_t)(nt * BN) + (int)rank * G::kRowsB;
         for (int kc = 0; kc < a.kchunks; kc++) {
-          if (!mbar_wait(&empty[stage], phase ^ 1u, globaltimer_ns() + a.timeout_ns, abort_flag)) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, a.timeout_ns, abort_flag)) {
             give_up();
             break;
           }
@@ -300,7 +300,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       for (int64_t p = p0; p < p1 && !*abort_flag; p++, t++) {
         const int acc = (int)(t & 1);
         const uint32_t acc_phase = (uint32_t)((t >> 1) & 1);
-        if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, globaltimer_ns() + a.timeout_ns, abort_flag)) {
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, a.timeout_ns, abort_flag)) {
           give_up();
           break;
         }
@@ -308,7 +308,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const uint32_t d = tmem_base + (uint32_t)(acc * BN);
         bool ok = true;
         for (int kc = 0; kc < a.kchunks; kc++) {
-          if (!mbar_wait(&full[stage], phase, globaltimer_ns() + a.timeout_ns, abort_flag)) {
+          if (!mbar_wait(&full[stage], phase, a.timeout_ns, abort_flag)) {
             give_up();
             ok = false;
             break;
@@ -402,7 +402,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       }
       if (__shfl_sync(0xFFFFFFFFu, *abort_flag, 0)) break;
       {
-        bool ok = mbar_wait(&tfull[acc], acc_phase, globaltimer_ns() + a.timeout_ns, abort_flag);
+        bool ok = mbar_wait(&tfull[acc], acc_phase, a.timeout_ns, abort_flag);
         ok = __all_sync(0xFFFFFFFFu, ok);
         if (!ok) {
           if (lane == 0) give_up();

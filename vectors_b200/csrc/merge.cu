@@ -5,57 +5,104 @@
 
 namespace vx {
 
+// Shared-memory key slots of the stream merge: the sort window (a power of two) and at
+// least K plus one stream's worth of keys.
+__host__ __device__ __forceinline__ uint32_t merge_cap(int C, int K) {
+  uint32_t need = (uint32_t)K + (uint32_t)(C > 1024 ? C : 1024);
+  return need > 2048u ? need : 2048u;
+}
+
 // Each block merges the candidate streams of one query into its K best keys, sorted
 // descending.  Stream s of query q holds cnts[s*nq+q] keys at bufs + ((s*nq)+q)*C, where nq
 // is the stream stride (queries beyond the grid are padding and are not merged).
-__global__ void __launch_bounds__(256) merge_streams_kernel(const uint64_t* __restrict__ bufs,
-                                                            const uint32_t* __restrict__ cnts,
-                                                            int S, int nq, int C, int K,
-                                                            const uint64_t* __restrict__ floor,
-                                                            uint64_t* __restrict__ out_keys,
-                                                            uint32_t* __restrict__ out_cnt) {
+//
+// Keys below the query's shared floor cannot reach its top K (at least K keys score at or
+// above the floor), so only keys >= floor are gathered.  The stream counts of up to 256
+// streams are read at once and prefix-summed, and their keys are gathered as one flat
+// index range.  The gathered keys are usually a few hundred: they are sorted outright;
+// larger sets are first cut to K by the bitwise K-th search.
+constexpr int kMergeThreads = 256;
+constexpr uint32_t kMergeSortMax = 1024;  // gathered keys sorted without a prior cut
+
+__device__ __forceinline__ uint32_t block_excl_scan_u32(uint32_t v, uint32_t* s_red, uint32_t& total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  uint32_t incl = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t t = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+    if (lane >= o) incl += t;
+  }
+  __syncthreads();
+  if (lane == 31) s_red[warp] = incl;
+  __syncthreads();
+  uint32_t before = 0;
+  total = 0;
+  for (int i = 0; i < nw; i++) {
+    const uint32_t w = s_red[i];
+    before += i < warp ? w : 0u;
+    total += w;
+  }
+  return before + incl - v;
+}
+
+__global__ void __launch_bounds__(kMergeThreads) merge_streams_kernel(const uint64_t* __restrict__ bufs,
+                                                                      const uint32_t* __restrict__ cnts,
+                                                                      int S, int nq, int C, int K,
+                                                                      const uint64_t* __restrict__ floor,
+                                                                      uint64_t* __restrict__ out_keys,
+                                                                      uint32_t* __restrict__ out_cnt) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
   const int q = blockIdx.x;
-  const uint32_t cap = (uint32_t)K + (uint32_t)(C > 4096 ? C : 4096);
+  const uint32_t cap = merge_cap(C, K);
   uint64_t* s_keys = (uint64_t*)smem_raw;
   uint64_t* s_tmp = s_keys + cap;
   uint32_t* s_red = (uint32_t*)(s_tmp + cap);
   uint32_t* s_counter = s_red + 32;
   __shared__ uint32_t s_n;
-  // Keys below the query's shared floor cannot reach its top K (some stream holds K keys
-  // at or above the floor), so only keys >= floor are gathered.
+  __shared__ uint32_t s_off[kMergeThreads + 1];
   const uint64_t f = floor ? floor[q] : 0ull;
   uint32_t n = 0;
   if (threadIdx.x == 0) s_n = 0;
-  __syncthreads();
-  for (int s = 0; s < S; s++) {
-    uint32_t c = cnts[(size_t)s * nq + q];
-    if (c == 0) continue;
-    if (n + c > cap) {
-      n = block_keep_top(s_keys, n, (uint32_t)K, s_tmp, s_red, s_counter);
-      if (threadIdx.x == 0) s_n = n;
+  for (int s0 = 0; s0 < S; s0 += kMergeThreads) {
+    const int ns = min(kMergeThreads, S - s0);
+    const uint32_t c = (int)threadIdx.x < ns ? cnts[(size_t)(s0 + threadIdx.x) * nq + q] : 0u;
+    uint32_t total;
+    const uint32_t excl = block_excl_scan_u32(c, s_red, total);
+    s_off[threadIdx.x] = excl;
+    if (threadIdx.x == 0) s_off[kMergeThreads] = total;
+    __syncthreads();
+    for (uint32_t base = 0; base < total;) {
+      if (n + min(total - base, 1024u) > cap) {  // rare: cut to K before gathering more
+        n = block_keep_top(s_keys, n, (uint32_t)K, s_tmp, s_red, s_counter);
+        if (threadIdx.x == 0) s_n = n;
+        __syncthreads();
+      }
+      const uint32_t take = min(total - base, cap - n);
+      for (uint32_t i = threadIdx.x; i < take; i += blockDim.x) {
+        const uint32_t idx = base + i;
+        int lo = 0, hi = ns - 1;  // last stream whose offset <= idx
+        while (lo < hi) {
+          const int mid = (lo + hi + 1) >> 1;
+          if (s_off[mid] <= idx) lo = mid; else hi = mid - 1;
+        }
+        const uint64_t key = bufs[((size_t)(s0 + lo) * nq + q) * (size_t)C + (idx - s_off[lo])];
+        if (key >= f) s_keys[atomicAdd(&s_n, 1u)] = key;
+      }
+      __syncthreads();
+      n = s_n;
+      base += take;
       __syncthreads();
     }
-    const uint64_t* src = bufs + ((size_t)s * nq + q) * (size_t)C;
-    for (uint32_t i = threadIdx.x; i < c; i += blockDim.x) {
-      const uint64_t key = src[i];
-      if (key >= f) s_keys[atomicAdd(&s_n, 1u)] = key;
-    }
-    __syncthreads();
-    n = s_n;
-    __syncthreads();
   }
-  n = block_keep_top(s_keys, n, (uint32_t)K, s_tmp, s_red, s_counter);
+  if (n > kMergeSortMax) n = block_keep_top(s_keys, n, (uint32_t)K, s_tmp, s_red, s_counter);
   block_sort_desc(s_keys, n, cap);
+  const uint32_t kept = n < (uint32_t)K ? n : (uint32_t)K;
   for (uint32_t i = threadIdx.x; i < (uint32_t)K; i += blockDim.x)
-    out_keys[(size_t)q * K + i] = (i < n) ? s_keys[i] : kEmptyKey;
-  if (threadIdx.x == 0) out_cnt[q] = n;
+    out_keys[(size_t)q * K + i] = (i < kept) ? s_keys[i] : kEmptyKey;
+  if (threadIdx.x == 0) out_cnt[q] = kept;
 }
 
-size_t merge_streams_smem(int C, int K) {
-  size_t cap = (size_t)K + (size_t)(C > 4096 ? C : 4096);
-  return cap * 16 + 33 * 4 + 16;
-}
+size_t merge_streams_smem(int C, int K) { return (size_t)merge_cap(C, K) * 16 + 33 * 4 + 16; }
 
 cudaError_t launch_merge_streams(const uint64_t* bufs, const uint32_t* cnts, int S, int nq,
                                  int stride, int C, int K, uint64_t* out_keys, uint32_t* out_cnt,
@@ -65,7 +112,7 @@ cudaError_t launch_merge_streams(const uint64_t* bufs, const uint32_t* cnts, int
   cudaError_t e = cudaFuncSetAttribute(merge_streams_kernel,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
-  merge_streams_kernel<<<nq, 256, smem, st>>>(bufs, cnts, S, stride, C, K, floor, out_keys, out_cnt);
+  merge_streams_kernel<<<nq, kMergeThreads, smem, st>>>(bufs, cnts, S, stride, C, K, floor, out_keys, out_cnt);
   return cudaGetLastError();
 }
 

@@ -39,15 +39,23 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-// Bounded wait: spins until the phase with `parity` completes, or until `deadline_ns`
-// (globaltimer) passes or another role raised *abort.  Returns false on give-up.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint64_t deadline_ns,
+// Bounded wait: spins until the phase with `parity` completes, or until `timeout_ns` has
+// passed since the wait first spun 256 times, or another role raised *abort.  Returns false
+// on give-up.  The clock is read only by waits that actually spin: the fast path is one
+// try_wait.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint64_t timeout_ns,
                                           volatile int* abort) {
+  if (mbar_try_wait(bar, parity)) return true;
   uint32_t spins = 0;
+  uint64_t deadline = 0;
   while (!mbar_try_wait(bar, parity)) {
     if ((++spins & 255u) == 0) {
       if (*abort) return false;
-      if (globaltimer_ns() > deadline_ns) return false;
+      const uint64_t now = globaltimer_ns();
+      if (deadline == 0)
+        deadline = now + timeout_ns;
+      else if (now > deadline)
+        return false;
     }
   }
   return true;

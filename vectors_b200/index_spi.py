@@ -164,6 +164,24 @@ class IndexSpi:
         )
         return _outcomes(ids, sc, cnt)
 
+    def search_batch_arrays(self, queries, k: int, search_list_size: int = 0, over_query_factor: float = 1.0):
+        """searchBatch through the host-buffer C ABI call, returning the flat result arrays
+        (ids [nq][k], scores [nq][k], counts [nq]) instead of one SearchOutcome per query."""
+        q = self._queries(queries, k)
+        ids, sc, cnt = self._alloc(len(q), k)
+        if self._n == 0:
+            ids.fill(-1)
+            sc.fill(0)
+            cnt.fill(0)
+            return ids, sc, cnt
+        _check(
+            N.lib().vx_search_batch(
+                self._h.ptr, _ptr(q), len(q), q.shape[1], k, search_list_size, float(over_query_factor),
+                _ptr(ids), _ptr(sc), _ptr(cnt),
+            )
+        )
+        return ids, sc, cnt
+
     def search_batch_device(self, queries, k: int, search_list_size: int = 0, over_query_factor: float = 1.0, stream=None):
         """searchBatch on device tensors (torch, cuda): returns (ids, scores, counts) tensors."""
         import torch
@@ -193,6 +211,13 @@ class IndexSpi:
             raise IllegalArgumentException(f"k must be positive: {k}")
         if self._n == 0:
             return np.zeros((len(queries), max(1, self._dim)), np.float32)
+        if isinstance(queries, np.ndarray) and queries.ndim == 2 and queries.dtype == np.float32:
+            # one contiguous [nq][dim] block (pinned or pageable): no per-row copies
+            if queries.shape[1] != self._dim:
+                raise IllegalArgumentException(
+                    f"Query 0 dimension {queries.shape[1]} does not match index dimension {self._dim}"
+                )
+            return np.ascontiguousarray(queries)
         rows = []
         for i, qi in enumerate(queries):
             if qi is None:
