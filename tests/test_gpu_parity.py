@@ -229,6 +229,22 @@ def test_ivfpq_bit_exact(oracle, metric):
     _check_float(got, ids, sc, cnt, f"ivfpq rescore m={metric}")
 
 
+@pytest.mark.parametrize("metric", [0, 1, 2])
+@pytest.mark.parametrize("nlist", [32, 4])
+def test_ivfpq_grouped_bit_exact(oracle, metric, nlist):
+    # 8-dim subspaces, 256 centroids, M a multiple of 16: the grouped ADC kernel (up to four
+    # queries per list, chunked tables); nlist=4 gives lists longer than one row pass
+    db, q, cent, off, ords, cb, codes = _ivf(oracle, n=20000, dim=128, nlist=nlist, m=16)
+    a = vx.IvfPqAdapter(nprobe=4)
+    a.build_prebuilt(cent, off, ords, cb, codes, 16, 256, vx.SimilarityFunction(metric), vectors=db)
+    got = a.ivf_search(q, 10, 4)
+    ids, sc, cnt = oracle.ivfpq_search(cent, off, ords, 16, 256, cb, codes, q, metric, 10, 4)
+    _check_float(got, ids, sc, cnt, f"ivfpq grouped m={metric} nlist={nlist}", exact_scores=True)
+    got = a.ivf_search(q, 10, 4, rescore_factor=4)
+    ids, sc, cnt = oracle.ivfpq_search(cent, off, ords, 16, 256, cb, codes, q, metric, 10, 4, 4, db)
+    _check_float(got, ids, sc, cnt, f"ivfpq grouped rescore m={metric} nlist={nlist}")
+
+
 def test_ivfpq_routing_matches_oracle(oracle):
     db, q, cent, off, ords, cb, codes = _ivf(oracle)
     lids, _ = oracle.route(cent, q, oracle.EUCLIDEAN, 8)

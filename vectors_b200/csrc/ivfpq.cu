@@ -348,6 +348,253 @@ __global__ void __launch_bounds__(256) adc_scan_kernel(AdcArgs a) {
   }
 }
 
+// ---------------------------------------------------------------------------------------
+// Grouped ADC scan (8-dimensional subspaces, 256 centroids, M a multiple of 16).
+//
+// A CTA takes a group of up to four (query, list) pairs that probe the same list.  The
+// subspaces are processed in chunks of 16: for each chunk the CTA builds the four queries'
+// tables, interleaved as table[m][code] = float4(query 0..3) (64 KB), with the codebook row
+// of (m, code) read once for all four queries; then every thread adds the chunk's 16 entries
+// of each of its rows into per-(row, query) running sums held in registers.  Chunks run in
+// subspace order, so each sum is table[0][c0] + table[1][c1] + ... in fp32 exactly as
+// IvfIndex.java:581-588 adds it, and each table entry is ProductQuantizer.buildADCTable's
+// scalar tail for 8-float sub-vectors (ProductQuantizer.java:521-544,
+// PanamaVectorUtilSupport.java:285-296).  One 16-byte shared load serves four queries.
+// Keys go to per-warp, per-query candidate buffers; a query's best key so far over all its
+// lists (its floor, raised by atomicMax) bounds admission in every later group.
+constexpr int kAdcThreads = 256;
+constexpr int kAdcWarps = kAdcThreads / 32;
+constexpr int kMChunk = 16;  // subspaces per table chunk
+constexpr int kRowsPerThread = 12;
+constexpr int kRowsPerPass = kAdcThreads * kRowsPerThread;
+
+__global__ void make_groups_kernel(const int32_t* __restrict__ counts, const int32_t* __restrict__ offsets,
+                                   int nlist, int2* __restrict__ groups, int32_t* __restrict__ ngroups) {
+  __shared__ uint32_t s_red[32];
+  __shared__ int32_t s_carry;
+  if (threadIdx.x == 0) s_carry = 0;
+  __syncthreads();
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  for (int base = 0; base < nlist; base += blockDim.x) {
+    const int l = base + threadIdx.x;
+    const int c = l < nlist ? counts[l] : 0;
+    const int g = (c + kAdcGroupQ - 1) / kAdcGroupQ;
+    int incl = g;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int t = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+      if (lane >= o) incl += t;
+    }
+    if (lane == 31) s_red[warp] = (uint32_t)incl;
+    __syncthreads();
+    int before = s_carry, total = 0;
+    for (int i = 0; i < nw; i++) {
+      before += i < warp ? (int)s_red[i] : 0;
+      total += (int)s_red[i];
+    }
+    const int first = before + incl - g;
+    for (int j = 0; j < g; j++)
+      groups[first + j] = make_int2(offsets[l] + j * kAdcGroupQ, min(kAdcGroupQ, c - j * kAdcGroupQ));
+    __syncthreads();
+    if (threadIdx.x == 0) s_carry += total;
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) *ngroups = s_carry;
+}
+
+// Table entries of subspace m for code c and the group's (up to) four queries.
+template <bool kDot>
+__device__ __forceinline__ float4 group_entry(const float* __restrict__ cb, const float* s_res, int dim, int m) {
+  const float4 b0 = *reinterpret_cast<const float4*>(cb);
+  const float4 b1 = *reinterpret_cast<const float4*>(cb + 4);
+  const float bv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+  float out[kAdcGroupQ];
+#pragma unroll
+  for (int g = 0; g < kAdcGroupQ; g++) {
+    const float4 r0 = *reinterpret_cast<const float4*>(s_res + g * dim + 8 * m);
+    const float4 r1 = *reinterpret_cast<const float4*>(s_res + g * dim + 8 * m + 4);
+    const float rv[8] = {r0.x, r0.y, r0.z, r0.w, r1.x, r1.y, r1.z, r1.w};
+    float res = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+      if (kDot) {
+        res = __fmaf_rn(rv[i], bv[i], res);
+      } else {
+        const float d = __fsub_rn(rv[i], bv[i]);
+        res = __fadd_rn(res, __fmul_rn(d, d));
+      }
+    }
+    out[g] = res;
+  }
+  return make_float4(out[0], out[1], out[2], out[3]);
+}
+
+template <bool kDot, int R>
+__global__ void __launch_bounds__(kAdcThreads, 2) adc_group_kernel(AdcArgs a) {
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  constexpr int C = 32 * R;
+  float4* s_lut = reinterpret_cast<float4*>(smem_raw);                       // [kMChunk][256]
+  float* s_res = reinterpret_cast<float*>(s_lut + kMChunk * 256);            // [4][dim]
+  uint64_t* s_wbuf = reinterpret_cast<uint64_t*>(s_res + kAdcGroupQ * a.dim);  // [warps][4][C]
+  uint64_t* s_mrg = s_wbuf + (size_t)kAdcWarps * kAdcGroupQ * C;              // [4][C]
+  __shared__ uint32_t s_wcnt[kAdcWarps][kAdcGroupQ];
+  __shared__ int s_q[kAdcGroupQ], s_p[kAdcGroupQ];
+  __shared__ float s_base[kAdcGroupQ];
+  __shared__ uint64_t s_floor[kAdcGroupQ];
+  const int ng = *a.ngroups;
+  const int nchunks = a.M / kMChunk;
+  for (int gi = blockIdx.x; gi < ng; gi += gridDim.x) {
+    const int2 grp = a.groups[gi];
+    const int npq = grp.y;  // pairs in this group (1..4)
+    __syncthreads();        // the previous group is finished with every shared buffer
+    if (threadIdx.x < kAdcGroupQ) {
+      const int g = threadIdx.x;
+      int q = -1, p = 0;
+      uint64_t f = 0;
+      if (g < npq) {
+        const int32_t pair = a.pairs[grp.x + g];
+        q = pair / a.nprobe;
+        p = pair - q * a.nprobe;
+        f = a.floor[q];
+      }
+      s_q[g] = q;
+      s_p[g] = p;
+      s_floor[g] = f;
+    }
+    __syncthreads();
+    const int l = a.lists[(size_t)s_q[0] * a.nprobe + s_p[0]];
+    const float* c = a.cent + (size_t)l * a.dim;
+    for (int i = threadIdx.x; i < kAdcGroupQ * a.dim; i += kAdcThreads) {
+      const int g = i / a.dim, d = i - g * a.dim;
+      float v = 0.0f;
+      if (g < npq) {
+        const float qv = a.queries[(size_t)s_q[g] * a.dim + d];
+        v = kDot ? qv : __fsub_rn(qv, c[d]);  // IvfIndex.java:570 residual
+      }
+      s_res[i] = v;
+    }
+    if (kDot && warp < kAdcGroupQ) {
+      float base = 0.0f;
+      if (warp < npq && a.metric != kCosine)
+        base = warp_dot(RowF32{a.queries + (size_t)s_q[warp] * a.dim}, RowF32{c}, a.dim);
+      if (lane == 0) s_base[warp] = base;
+    }
+    // per-warp streams of the group's queries, seeded with the queries' floors
+    uint32_t wcnt[kAdcGroupQ];
+    uint64_t wthr[kAdcGroupQ];
+#pragma unroll
+    for (int g = 0; g < kAdcGroupQ; g++) wcnt[g] = 0;
+    __syncthreads();
+#pragma unroll
+    for (int g = 0; g < kAdcGroupQ; g++) wthr[g] = s_floor[g] > 0 ? s_floor[g] - 1 : 0ull;
+    const int64_t b = a.list_off[l], e = a.list_off[l + 1];
+    for (int64_t pass0 = b; pass0 < e; pass0 += kRowsPerPass) {
+      float ps[kRowsPerThread][kAdcGroupQ];
+#pragma unroll
+      for (int j = 0; j < kRowsPerThread; j++)
+#pragma unroll
+        for (int g = 0; g < kAdcGroupQ; g++) ps[j][g] = 0.0f;
+      for (int ch = 0; ch < nchunks; ch++) {
+        __syncthreads();  // readers of the previous chunk are done
+        {
+          const int code = threadIdx.x;  // 256 threads <-> 256 centroids
+#pragma unroll 1
+          for (int ml = 0; ml < kMChunk; ml++) {
+            const int m = ch * kMChunk + ml;
+            const float* cb = a.codebooks + a.cb_off[m] + (size_t)code * 8;
+            s_lut[ml * 256 + code] = group_entry<kDot>(cb, s_res, a.dim, m);
+          }
+        }
+        __syncthreads();
+#pragma unroll
+        for (int j = 0; j < kRowsPerThread; j++) {
+          const int64_t r = pass0 + threadIdx.x + (int64_t)kAdcThreads * j;
+          if (r < e) {
+            const uint4 cv = *reinterpret_cast<const uint4*>(a.codes + r * (int64_t)a.Mp + ch * kMChunk);
+            const uint32_t w4[4] = {cv.x, cv.y, cv.z, cv.w};
+#pragma unroll
+            for (int ml = 0; ml < kMChunk; ml++) {
+              const uint32_t code = (w4[ml >> 2] >> (8 * (ml & 3))) & 0xFFu;
+              const float4 t = s_lut[ml * 256 + code];
+              ps[j][0] = __fadd_rn(ps[j][0], t.x);
+              ps[j][1] = __fadd_rn(ps[j][1], t.y);
+              ps[j][2] = __fadd_rn(ps[j][2], t.z);
+              ps[j][3] = __fadd_rn(ps[j][3], t.w);
+            }
+          }
+        }
+      }
+      // keys of this pass's rows into the per-warp streams
+#pragma unroll
+      for (int j = 0; j < kRowsPerThread; j++) {
+        const int64_t r = pass0 + threadIdx.x + (int64_t)kAdcThreads * j;
+        const bool in = r < e;
+        const uint32_t ord = in ? (uint32_t)a.ordinals[r] : 0u;
+#pragma unroll
+        for (int g = 0; g < kAdcGroupQ; g++) {
+          const float score = kDot ? __fadd_rn(s_base[g], ps[j][g]) : -ps[j][g];
+          const uint64_t key = float_key(score, ord);
+          const bool pass = in && g < npq && key > wthr[g];
+          const unsigned mk = __ballot_sync(0xFFFFFFFFu, pass);
+          uint64_t* buf = s_wbuf + ((size_t)warp * kAdcGroupQ + g) * C;
+          if (pass) buf[wcnt[g] + __popc(mk & ((1u << lane) - 1u))] = key;
+          wcnt[g] += __popc(mk);
+          if (wcnt[g] > (uint32_t)(C - 32)) {
+            __syncwarp();
+            warp_compact_one<R>(buf, wcnt[g], (uint32_t)a.K, wthr[g], wcnt[g]);
+            __syncwarp();
+          }
+        }
+      }
+    }
+    // each warp shrinks its buffers to K and publishes the counts
+#pragma unroll
+    for (int g = 0; g < kAdcGroupQ; g++) {
+      uint64_t* buf = s_wbuf + ((size_t)warp * kAdcGroupQ + g) * C;
+      __syncwarp();
+      if (wcnt[g] > (uint32_t)a.K) warp_compact_one<R>(buf, wcnt[g], (uint32_t)a.K, wthr[g], wcnt[g]);
+      __syncwarp();
+      if (lane == 0) s_wcnt[warp][g] = wcnt[g];
+    }
+    __syncthreads();
+    // warp g merges query g's buffers (each <= K keys) into its K best; C >= 2K keeps every
+    // append within the buffer
+    if (warp < npq) {
+      const int g = warp;
+      uint64_t* mrg = s_mrg + (size_t)g * C;
+      uint32_t n = 0;
+      uint64_t thr = 0;
+      for (int w = 0; w < kAdcWarps; w++) {
+        const uint32_t cw = s_wcnt[w][g];
+        const uint64_t* src = s_wbuf + ((size_t)w * kAdcGroupQ + g) * C;
+        for (uint32_t i = lane; i < cw; i += 32) mrg[n + i] = src[i];
+        __syncwarp();
+        n += cw;
+        if (n > (uint32_t)(C - a.K)) {
+          warp_compact_one<R>(mrg, n, (uint32_t)a.K, thr, n);
+          __syncwarp();
+        }
+      }
+      if (n > (uint32_t)a.K) {
+        warp_compact_one<R>(mrg, n, (uint32_t)a.K, thr, n);
+        __syncwarp();
+      } else if (n == (uint32_t)a.K) {
+        uint64_t mn = ~0ull;
+        for (uint32_t i = lane; i < n; i += 32) mn = mrg[i] < mn ? mrg[i] : mn;
+        thr = warp_min_u64(mn);
+      }
+      const int q = s_q[g];
+      const size_t sidx = (size_t)s_p[g] * a.nq + q;
+      for (uint32_t i = lane; i < n; i += 32) a.out[sidx * a.K + i] = mrg[i];
+      if (lane == 0) {
+        a.out_cnt[sidx] = n;
+        if (n == (uint32_t)a.K) atomicMax((unsigned long long*)&a.floor[q], (unsigned long long)thr);
+      }
+    }
+  }
+}
+
 }  // namespace
 
 cudaError_t launch_route(const float* queries, int nq, int dim, const float* cent, int nlist,
@@ -416,6 +663,45 @@ cudaError_t launch_adc_scan(const AdcArgs& a, int R, int grid, cudaStream_t st) 
     default: return cudaErrorInvalidValue;
   }
 #undef VX_ADC_CASE
+}
+
+bool adc_group_supported(int M, int Ks, int dim) {
+  return Ks == 256 && M > 0 && M % kMChunk == 0 && dim == 8 * M;
+}
+
+cudaError_t launch_make_groups(const int32_t* counts, const int32_t* offsets, int nlist, int2* groups,
+                               int32_t* ngroups, cudaStream_t st) {
+  make_groups_kernel<<<1, 1024, 0, st>>>(counts, offsets, nlist, groups, ngroups);
+  return cudaGetLastError();
+}
+
+static size_t adc_group_smem(int dim, int R) {
+  return (size_t)kMChunk * 256 * 16 + (size_t)kAdcGroupQ * dim * 4 +
+         (size_t)(kAdcWarps + 1) * kAdcGroupQ * 32 * R * 8;
+}
+
+// R in {2, 3, 5, 9} with 32 R >= 2 K + 1 (each warp buffer and each merge buffer); shared
+// memory 64 KB tables + 4 residuals + 9 * 4 buffers of 32 R keys (<= 159 KB at R = 9).
+cudaError_t launch_adc_group(const AdcArgs& a, int R, int grid, cudaStream_t st) {
+  if (a.npairs <= 0) return cudaSuccess;
+  const size_t smem = adc_group_smem(a.dim, R);
+  const bool dot = a.metric != kEuclidean;
+#define VX_ADCG_CASE(RR)                                                                         \
+  case RR: {                                                                                     \
+    auto kern = dot ? adc_group_kernel<true, RR> : adc_group_kernel<false, RR>;                 \
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); \
+    if (e != cudaSuccess) return e;                                                              \
+    kern<<<grid, kAdcThreads, smem, st>>>(a);                                                    \
+    return cudaGetLastError();                                                                   \
+  }
+  switch (R) {
+    VX_ADCG_CASE(2)
+    VX_ADCG_CASE(3)
+    VX_ADCG_CASE(5)
+    VX_ADCG_CASE(9)
+    default: return cudaErrorInvalidValue;
+  }
+#undef VX_ADCG_CASE
 }
 
 }  // namespace vx

@@ -22,6 +22,10 @@ struct AdcArgs {
   const int32_t* sub;            // [M][2] size, offset
   uint64_t* out;                 // [nprobe][nq][K]
   uint32_t* out_cnt;             // [nprobe][nq]
+  // grouped scan only (adc_group_kernel)
+  const int2* groups;            // (first pair slot, pairs) of up to 4 pairs sharing one list
+  const int32_t* ngroups;        // device count of groups
+  uint64_t* floor;               // [nq] per-query admission floor shared across lists (zeroed)
 };
 
 cudaError_t launch_route(const float* queries, int nq, int dim, const float* cent, int nlist,
@@ -31,5 +35,13 @@ cudaError_t launch_group_pairs(const int32_t* lists, int npairs, int nlist, int3
                                int32_t* offsets, int32_t* cursor, int32_t* pairs, cudaStream_t st);
 size_t adc_smem(int M, int Ks, int dim, int R, int K);
 cudaError_t launch_adc_scan(const AdcArgs& a, int R, int grid, cudaStream_t st);
+
+// Grouped ADC scan for 8-dimensional subspaces with 256 centroids (M a multiple of 16):
+// pairs sharing a list are taken up to four at a time.
+constexpr int kAdcGroupQ = 4;
+bool adc_group_supported(int M, int Ks, int dim);
+cudaError_t launch_make_groups(const int32_t* counts, const int32_t* offsets, int nlist, int2* groups,
+                               int32_t* ngroups, cudaStream_t st);
+cudaError_t launch_adc_group(const AdcArgs& a, int R, int grid, cudaStream_t st);
 
 }  // namespace vx

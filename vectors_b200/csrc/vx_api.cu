@@ -179,6 +179,15 @@ bool use_pilot() {
   return v;
 }
 
+// IVF-PQ scans use the grouped ADC kernel where the shape allows unless VX_ADC_GROUPED=0.
+bool use_adc_group() {
+  static const bool v = [] {
+    const char* e = getenv("VX_ADC_GROUPED");
+    return !(e && *e == '0');
+  }();
+  return v;
+}
+
 // The tcgen05 scan runs on 2-CTA clusters unless VX_GEMM_1SM=1 selects the 1-CTA variant
 // (read once per process: index tensor maps are built for the variant in use).
 bool gemm_two_sm() {
@@ -784,8 +793,25 @@ int search_ivfpq(vx_index* ix, const float* dq, int nq, int k, int nprobe, int r
     a.sub = ix->sub;
     a.out = out;
     a.out_cnt = out_cnt;
+    a.groups = nullptr;
+    a.ngroups = nullptr;
+    a.floor = nullptr;
     const int grid = ix->num_sms * 2;
-    VX_TIMED(VX_PROF_ADC_SCAN, st, 1, launch_adc_scan(a, g.R, grid, st));
+    const StreamGeom gg = stream_geom(K, std::max(32, K));  // group buffers hold >= 2K keys
+    if (use_adc_group() && adc_group_supported(ix->M, ix->Ks, dim) && gg.R > 0 && gg.R <= 9) {
+      const int64_t maxg = (int64_t)qc * probes / kAdcGroupQ + ix->nlist + 1;
+      int2* groups = T.alloc<int2>((size_t)maxg);
+      int32_t* ngroups = T.alloc<int32_t>(1);
+      uint64_t* qfloor = T.alloc<uint64_t>(qc);
+      VX_CUDA(cudaMemsetAsync(qfloor, 0, (size_t)qc * 8, st));
+      VX_LAUNCH(1, launch_make_groups(counts, offsets, ix->nlist, groups, ngroups, st));
+      a.groups = groups;
+      a.ngroups = ngroups;
+      a.floor = qfloor;
+      VX_TIMED(VX_PROF_ADC_SCAN, st, 1, launch_adc_group(a, gg.R, grid, st));
+    } else {
+      VX_TIMED(VX_PROF_ADC_SCAN, st, 1, launch_adc_scan(a, g.R, grid, st));
+    }
     VX_TIMED(VX_PROF_MERGE, st, 1, launch_merge_streams(out, out_cnt, probes, qc, qc, K, K, keys, kcnt, st));
     int32_t* oi = d_ids + (size_t)q0 * k;
     float* os = d_scores + (size_t)q0 * k;
