@@ -204,6 +204,8 @@ def main():
     ap.add_argument("--no-ivf", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--ivf-n", type=int, default=IVF["n"])
+    ap.add_argument("--ivf-nlist", type=int, default=IVF["nlist"], help="smaller cases for profiling keep n/nlist")
+    ap.add_argument("--ivf-nq", type=int, default=IVF["nq"])
     ap.add_argument("--ref-rows", type=int, default=1_000_000)
     ap.add_argument("--ref-queries", type=int, default=48)
     args = ap.parse_args()
@@ -413,7 +415,7 @@ def run_ivf(args, rank, world, local, dev, barrier, max_over_ranks, hbm_peak, pe
     from vectors_b200 import _native as N
 
     P = IVF
-    n, dim, nlist, m, ks = args.ivf_n, P["dim"], P["nlist"], P["m"], P["ks"]
+    n, dim, nlist, m, ks = args.ivf_n, P["dim"], args.ivf_nlist, P["m"], P["ks"]
     offs = vx.shard_offsets(n, world)
     lo, hi = offs[rank], offs[rank + 1]
     cent_mix = centres(P["comps"], dim, SEED_C ^ 0x1F)
@@ -452,10 +454,11 @@ def run_ivf(args, rank, world, local, dev, barrier, max_over_ranks, hbm_peak, pe
     loff = torch.zeros(nlist + 1, dtype=torch.int64, device=dev)
     loff[1:] = torch.cumsum(counts, 0)
     del rows
+    torch.cuda.empty_cache()
     a = vx.IvfPqAdapter(nprobe=P["nprobe"], device=local)
     a.build_prebuilt(cent.cpu().numpy(), loff.cpu().numpy(), order.cpu().numpy(), books.cpu().numpy().reshape(-1),
                      codes.cpu().numpy(), m, ks, vx.SimilarityFunction.EUCLIDEAN)
-    nq, k = P["nq"], P["k"]
+    nq, k = args.ivf_nq, P["k"]
     qh = gen_rows(0, nq, dim, cent_mix, P["sigma"], SEED_Q ^ 0x1F, False)
     q = torch.from_numpy(qh).to(dev)
     # algorithmic bytes: codes + ordinals of every probed list row, per query

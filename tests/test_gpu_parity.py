@@ -217,8 +217,11 @@ def _ivf(oracle, n=20000, dim=64, nlist=64, m=8, ks=256, comps=32):
 
 
 @pytest.mark.parametrize("metric", [0, 1])
-def test_ivfpq_bit_exact(oracle, metric):
-    db, q, cent, off, ords, cb, codes = _ivf(oracle)
+@pytest.mark.parametrize("dim,nlist", [(64, 64), (96, 30)])
+def test_ivfpq_bit_exact(oracle, metric, dim, nlist):
+    # (64, 64): tiled routing; (96, 30): per-row routing (dim not a multiple of 64) with two
+    # centroids outside the 4-row groups, 12-dim subspaces on the general ADC kernel
+    db, q, cent, off, ords, cb, codes = _ivf(oracle, dim=dim, nlist=nlist)
     a = vx.IvfPqAdapter(nprobe=8)
     a.build_prebuilt(cent, off, ords, cb, codes, 8, 256, vx.SimilarityFunction(metric), vectors=db)
     got = a.ivf_search(q, 10, 8)

@@ -95,12 +95,12 @@ __device__ float serial_dot(const float* a, const float* b, int len) {
   return res;
 }
 
-// Distances from kQG queries to every centroid; one thread per centroid row.
+// Distances from kQG queries to centroids [c_begin, nlist); one thread per centroid row.
 // EUCLIDEAN: matVecSquaredL2; otherwise -matVecDot (queries already normalised for COSINE).
 __global__ void __launch_bounds__(256) route_dist_kernel(const float* __restrict__ queries, int nq,
                                                          int dim, const float* __restrict__ cent,
                                                          int nlist, int metric,
-                                                         float* __restrict__ dist) {
+                                                         float* __restrict__ dist, int c_begin) {
   extern __shared__ float s_q[];  // [kQG][dim]
   const int q0 = blockIdx.x * kQG;
   const int nqg = min(kQG, nq - q0);
@@ -112,7 +112,7 @@ __global__ void __launch_bounds__(256) route_dist_kernel(const float* __restrict
   const int group = nlist & ~3;
   const int limit = dim & ~7;
   const bool l2 = metric == kEuclidean;
-  for (int c = threadIdx.x; c < nlist; c += blockDim.x) {
+  for (int c = c_begin + threadIdx.x; c < nlist; c += blockDim.x) {
     const float* row = cent + (size_t)c * dim;
     if (c < group) {
       float acc[kQG][8];
@@ -165,6 +165,82 @@ __global__ void __launch_bounds__(256) route_dist_kernel(const float* __restrict
       }
     }
   }
+}
+
+// Register-tiled form of the same arithmetic for the centroids in 4-row groups when the
+// dimension is a multiple of 64: a block scores 64 queries x 32 centroids, dims staged
+// through shared memory 64 at a time; each thread keeps 4 queries x 2 centroids x the 8
+// accumulator lanes of matVecSquaredL2 / matVecDot (lane j takes dims j, j+8, ... in order,
+// FMA for dot, subtract-then-FMA for L2), then sums the lanes in the reference's order.
+constexpr int kRtQ = 64, kRtC = 32, kRtK = 64, kRtStride = kRtK + 4;
+
+template <bool kL2>
+__global__ void __launch_bounds__(256, 2) route_tile_kernel(const float* __restrict__ queries, int nq, int dim,
+                                                             const float* __restrict__ cent, int ngroup, int nlist,
+                                                             float* __restrict__ dist) {
+  __shared__ __align__(16) float s_q[kRtQ * kRtStride];
+  __shared__ __align__(16) float s_c[kRtC * kRtStride];
+  const int q0 = blockIdx.y * kRtQ, c0 = blockIdx.x * kRtC;
+  const int tq = threadIdx.x >> 4, tc = threadIdx.x & 15;  // queries tq + 16a, centroids tc + 16b
+  float acc[4][2][8];
+#pragma unroll
+  for (int a = 0; a < 4; a++)
+#pragma unroll
+    for (int b = 0; b < 2; b++)
+#pragma unroll
+      for (int j = 0; j < 8; j++) acc[a][b][j] = 0.0f;
+  for (int k0 = 0; k0 < dim; k0 += kRtK) {
+    __syncthreads();
+    for (int i = threadIdx.x; i < kRtQ * (kRtK / 4); i += 256) {
+      const int r = i / (kRtK / 4), v = i % (kRtK / 4);
+      float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (q0 + r < nq) x = *reinterpret_cast<const float4*>(queries + (size_t)(q0 + r) * dim + k0 + 4 * v);
+      *reinterpret_cast<float4*>(s_q + r * kRtStride + 4 * v) = x;
+    }
+    for (int i = threadIdx.x; i < kRtC * (kRtK / 4); i += 256) {
+      const int r = i / (kRtK / 4), v = i % (kRtK / 4);
+      float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (c0 + r < ngroup) x = *reinterpret_cast<const float4*>(cent + (size_t)(c0 + r) * dim + k0 + 4 * v);
+      *reinterpret_cast<float4*>(s_c + r * kRtStride + 4 * v) = x;
+    }
+    __syncthreads();
+#pragma unroll 4
+    for (int kk = 0; kk < kRtK; kk += 4) {
+      float4 qv[4], cv[2];
+#pragma unroll
+      for (int a = 0; a < 4; a++) qv[a] = *reinterpret_cast<const float4*>(s_q + (tq + 16 * a) * kRtStride + kk);
+#pragma unroll
+      for (int b = 0; b < 2; b++) cv[b] = *reinterpret_cast<const float4*>(s_c + (tc + 16 * b) * kRtStride + kk);
+      const int jb = kk & 4;  // accumulator lanes jb..jb+3 take dims kk..kk+3
+#pragma unroll
+      for (int a = 0; a < 4; a++) {
+        const float qa[4] = {qv[a].x, qv[a].y, qv[a].z, qv[a].w};
+#pragma unroll
+        for (int b = 0; b < 2; b++) {
+          const float cb[4] = {cv[b].x, cv[b].y, cv[b].z, cv[b].w};
+#pragma unroll
+          for (int j = 0; j < 4; j++) {
+            if (kL2) {
+              const float d = __fsub_rn(qa[j], cb[j]);
+              acc[a][b][jb + j] = __fmaf_rn(d, d, acc[a][b][jb + j]);
+            } else {
+              acc[a][b][jb + j] = __fmaf_rn(qa[j], cb[j], acc[a][b][jb + j]);
+            }
+          }
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int a = 0; a < 4; a++)
+#pragma unroll
+    for (int b = 0; b < 2; b++) {
+      const int q = q0 + tq + 16 * a, c = c0 + tc + 16 * b;
+      if (q < nq && c < ngroup) {
+        const float sum = reduce_add8_local(acc[a][b]);
+        dist[(size_t)q * nlist + c] = kL2 ? sum : -sum;
+      }
+    }
 }
 
 // COSINE routing normalises a copy of the query first: l2normalize
@@ -597,6 +673,27 @@ __global__ void __launch_bounds__(kAdcThreads, 2) adc_group_kernel(AdcArgs a) {
 
 }  // namespace
 
+// The tiled routing kernel is used where it applies unless VX_ROUTE_TILED=0.
+static bool route_tiled() {
+  static const bool v = [] {
+    const char* e = getenv("VX_ROUTE_TILED");
+    return !(e && *e == '0');
+  }();
+  return v;
+}
+
+static bool route_tile_applies(const float* q, const float* cent, int dim, int nlist) {
+  return route_tiled() && dim % kRtK == 0 && (nlist & ~3) > 0 && ((uintptr_t)q & 15u) == 0 &&
+         ((uintptr_t)cent & 15u) == 0;
+}
+
+int route_launches(const float* queries, int dim, const float* cent, int nlist, int metric) {
+  // l2normalize (COSINE), tiled distances, per-row distances for the rest, selection
+  const bool tiled = route_tile_applies(metric == kCosine ? nullptr : queries, cent, dim, nlist);
+  const bool rest = !tiled || (nlist & 3) != 0;
+  return (metric == kCosine ? 1 : 0) + (tiled ? 1 : 0) + (rest ? 1 : 0) + 1;
+}
+
 cudaError_t launch_route(const float* queries, int nq, int dim, const float* cent, int nlist,
                          int metric, int nprobe, float* qnorm_scratch, float* dist,
                          int32_t* lists, cudaStream_t st) {
@@ -606,13 +703,27 @@ cudaError_t launch_route(const float* queries, int nq, int dim, const float* cen
     l2normalize_kernel<<<(nq * 32 + 255) / 256, 256, 0, st>>>(queries, nq, dim, qnorm_scratch);
     qsrc = qnorm_scratch;
   }
-  const size_t smem = (size_t)kQG * dim * sizeof(float);
-  cudaError_t e = cudaFuncSetAttribute(route_dist_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       (int)smem);
-  if (e != cudaSuccess) return e;
-  route_dist_kernel<<<(nq + kQG - 1) / kQG, 256, smem, st>>>(qsrc, nq, dim, cent, nlist, metric, dist);
-  e = cudaGetLastError();
-  if (e != cudaSuccess) return e;
+  const int group = nlist & ~3;
+  int c_begin = 0;
+  cudaError_t e = cudaSuccess;
+  if (route_tile_applies(qsrc, cent, dim, nlist)) {
+    const dim3 grid((group + kRtC - 1) / kRtC, (nq + kRtQ - 1) / kRtQ);
+    if (metric == kEuclidean)
+      route_tile_kernel<true><<<grid, 256, 0, st>>>(qsrc, nq, dim, cent, group, nlist, dist);
+    else
+      route_tile_kernel<false><<<grid, 256, 0, st>>>(qsrc, nq, dim, cent, group, nlist, dist);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    c_begin = group;
+  }
+  if (c_begin < nlist) {
+    const size_t smem = (size_t)kQG * dim * sizeof(float);
+    e = cudaFuncSetAttribute(route_dist_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    route_dist_kernel<<<(nq + kQG - 1) / kQG, 256, smem, st>>>(qsrc, nq, dim, cent, nlist, metric, dist, c_begin);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+  }
   uint32_t cap = 1;
   while (cap < (uint32_t)nlist) cap <<= 1;
   const size_t smem2 = (size_t)cap * 16 + 33 * 4 + 16;

@@ -31,6 +31,7 @@ struct AdcArgs {
 cudaError_t launch_route(const float* queries, int nq, int dim, const float* cent, int nlist,
                          int metric, int nprobe, float* qnorm_scratch, float* dist,
                          int32_t* lists, cudaStream_t st);
+int route_launches(const float* queries, int dim, const float* cent, int nlist, int metric);
 cudaError_t launch_group_pairs(const int32_t* lists, int npairs, int nlist, int32_t* counts,
                                int32_t* offsets, int32_t* cursor, int32_t* pairs, cudaStream_t st);
 size_t adc_smem(int M, int Ks, int dim, int R, int K);

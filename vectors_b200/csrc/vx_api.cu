@@ -767,7 +767,7 @@ int search_ivfpq(vx_index* ix, const float* dq, int nq, int k, int nprobe, int r
     uint32_t* out_cnt = T.alloc<uint32_t>((size_t)probes * qc);
     uint64_t* keys = T.alloc<uint64_t>((size_t)qc * K);
     uint32_t* kcnt = T.alloc<uint32_t>(qc);
-    VX_TIMED(VX_PROF_ROUTE, st, ix->metric == VX_COSINE ? 3 : 2,
+    VX_TIMED(VX_PROF_ROUTE, st, route_launches(dqc, dim, ix->cent, ix->nlist, ix->metric),
              launch_route(dqc, qc, dim, ix->cent, ix->nlist, ix->metric, probes, qn, dist, lists, st));
     VX_LAUNCH(3, launch_group_pairs(lists, qc * probes, ix->nlist, counts, offsets, cursor, pairs, st));
     VX_CUDA(cudaMemsetAsync(out_cnt, 0, (size_t)probes * qc * 4, st));
