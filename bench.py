@@ -221,6 +221,7 @@ def main():
 
     import vectors_b200 as vx
     from vectors_b200 import _native as N
+    from vectors_b200.sharded import gather_and_merge
 
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
@@ -266,19 +267,12 @@ def main():
     del rows
     torch.cuda.empty_cache()
 
-    off_t = torch.tensor(offs[:world], dtype=torch.int64, device=dev)
 
     def flat_step():
         ids, sc, cnt = flat.search_batch_device(q_dev, k)
         if world == 1:
             return ids, sc, cnt
-        gi = torch.empty((world, nq, k), dtype=torch.int32, device=dev)
-        gs = torch.empty((world, nq, k), dtype=torch.float32, device=dev)
-        gc = torch.empty((world, nq), dtype=torch.int32, device=dev)
-        dist.all_gather_into_tensor(gi, ids)
-        dist.all_gather_into_tensor(gs, sc)
-        dist.all_gather_into_tensor(gc, cnt)
-        return vx.merge_shards_device(gi, gs, gc, off_t, k)
+        return gather_and_merge(ids, sc, cnt, offs, k)
 
     for _ in range(args.warmup):
         flat_step()
@@ -338,14 +332,8 @@ def main():
         if world == 1:
             return res
         # shard results meet through the same NCCL all-gather + device merge, then D2H
-        li, ls, lc = (torch.from_numpy(a) for a in res)
-        gi = torch.empty((world, nq, k), dtype=torch.int32, device=dev)
-        gs = torch.empty((world, nq, k), dtype=torch.float32, device=dev)
-        gc = torch.empty((world, nq), dtype=torch.int32, device=dev)
-        dist.all_gather_into_tensor(gi, li.to(dev))
-        dist.all_gather_into_tensor(gs, ls.to(dev))
-        dist.all_gather_into_tensor(gc, lc.to(dev))
-        mi, ms_, mc = vx.merge_shards_device(gi, gs, gc, off_t, k)
+        li, ls, lc = (torch.from_numpy(a).to(dev) for a in res)
+        mi, ms_, mc = gather_and_merge(li, ls, lc, offs, k)
         return mi.cpu(), ms_.cpu(), mc.cpu()
 
     e2e_step()
@@ -413,6 +401,7 @@ def run_ivf(args, rank, world, local, dev, barrier, max_over_ranks, hbm_peak, pe
 
     import vectors_b200 as vx
     from vectors_b200 import _native as N
+    from vectors_b200.sharded import gather_and_merge
 
     P = IVF
     n, dim, nlist, m, ks = args.ivf_n, P["dim"], args.ivf_nlist, P["m"], P["ks"]
@@ -465,19 +454,12 @@ def run_ivf(args, rank, world, local, dev, barrier, max_over_ranks, hbm_peak, pe
     dq = torch.cdist(q, cent)
     probed = dq.topk(P["nprobe"], largest=False).indices
     bytes_step = float(counts[probed].sum().item()) * (m + 4)
-    off_t = torch.tensor(offs[:world], dtype=torch.int64, device=dev)
 
     def step():
         ids, sc, cnt = a.ivf_search_device(q, k, P["nprobe"])
         if world == 1:
             return ids
-        gi = torch.empty((world, nq, k), dtype=torch.int32, device=dev)
-        gs = torch.empty((world, nq, k), dtype=torch.float32, device=dev)
-        gc = torch.empty((world, nq), dtype=torch.int32, device=dev)
-        dist.all_gather_into_tensor(gi, ids)
-        dist.all_gather_into_tensor(gs, sc)
-        dist.all_gather_into_tensor(gc, cnt)
-        return vx.merge_shards_device(gi, gs, gc, off_t, k)[0]
+        return gather_and_merge(ids, sc, cnt, offs, k)[0]
 
     for _ in range(args.warmup):
         step()

@@ -1,0 +1,62 @@
+"""Row-sharded search over two CPU ranks (gloo): every rank scans its IndexShards range with the
+oracle, vectors_b200.sharded.gather_and_merge all-gathers the per-rank top-k lists and merges
+them with global ordinals; the result must equal the unsharded search on every rank."""
+import os
+import socket
+import tempfile
+
+import numpy as np
+import pytest
+
+SEEDS = (0xC0FFEE03, 0xC0FFEE01, 0xC0FFEE02)
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, n, out_dir):
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    try:
+        from oracle import oracle as O
+        from vectors_b200.index_spi import shard_offsets
+        from vectors_b200.sharded import gather_and_merge, shard_range
+
+        db = O.gen_mixture(n, 64, 8, 0.3, SEEDS[0], SEEDS[1], True)
+        q = O.gen_mixture(9, 64, 8, 0.3, SEEDS[0], SEEDS[2], True)
+        lo, hi = shard_range(n, rank, world)
+        ids, sc, cnt = O.flat_search(db[lo:hi], q, O.COSINE, 10)
+
+        def merge(gi, gs, gc, off, k):
+            r = O.merge_shards(off.numpy(), gi.numpy(), gs.numpy(), gc.numpy(), k)
+            return tuple(torch.from_numpy(np.ascontiguousarray(x)) for x in r)
+
+        mi, ms, mc = gather_and_merge(torch.from_numpy(ids), torch.from_numpy(sc), torch.from_numpy(cnt),
+                                      shard_offsets(n, world), 10, merge=merge)
+        ref_ids, ref_sc, ref_cnt = O.flat_search(db, q, O.COSINE, 10)
+        ok = (np.array_equal(mi.numpy(), ref_ids) and np.array_equal(mc.numpy(), ref_cnt)
+              and np.allclose(ms.numpy(), ref_sc, rtol=1e-6, atol=0))
+        with open(os.path.join(out_dir, f"rank{rank}"), "w") as f:
+            f.write("ok" if ok else "mismatch")
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("n", [3000, 3001])
+def test_two_rank_gloo_sharded_search_matches_unsharded(n):
+    import torch.multiprocessing as mp
+
+    with tempfile.TemporaryDirectory() as d:
+        mp.start_processes(_worker, args=(2, _free_port(), n, d), nprocs=2, join=True, start_method="spawn")
+        for r in range(2):
+            with open(os.path.join(d, f"rank{r}")) as f:
+                assert f.read() == "ok", f"rank {r}"

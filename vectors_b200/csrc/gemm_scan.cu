@@ -386,13 +386,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const bool active = q < a.nq;
       const size_t sidx = (size_t)unit * Qp + (size_t)q;
       // Stream state does not depend on the accumulator: load it before waiting.
+      const bool probe = a.probe != nullptr;
+      const bool live = active && !probe;
       TileStream ts;
       ts.st.base = a.bufs + sidx * (size_t)a.C;
-      ts.st.cnt = active ? a.cnts[sidx] : 0u;
-      ts.st.thr = active ? a.thrs[sidx] : ~0ull;
-      ts.t1 = (a.top1 && active) ? a.top1[sidx] : 0ull;
-      ts.t2 = (a.top1 && active) ? a.top2[sidx] : 0ull;
-      apply_floor(a, q, active, ts.st.thr);
+      ts.st.cnt = live ? a.cnts[sidx] : 0u;
+      ts.st.thr = live ? a.thrs[sidx] : ~0ull;
+      ts.t1 = (a.top1 && live) ? a.top1[sidx] : 0ull;
+      ts.t2 = (a.top1 && live) ? a.top2[sidx] : 0ull;
+      apply_floor(a, q, live, ts.st.thr);
       float qa = 0.0f;
       int32_t qi = 0;
       if (active) {
@@ -422,6 +424,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         tmem_ld_wait();
         const int c0 = g * 32;
         const float m = group_max<kMode>(v, c0, s_col, s_col2, qa, qi, a.epi.cm);
+        if (probe) {
+          if (active && c0 < valid) a.probe[(size_t)q * a.probe_groups + (size_t)((col0 + c0) >> 5)] = m;
+          continue;
+        }
         if (__any_sync(0xFFFFFFFFu, m >= ts.tf))
           offer_group<kMode, R>(a, ts, q, active, v, c0, valid - c0, col0, s_col, s_col2, qa, qi, stage_row);
       }
@@ -433,7 +439,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         else
           mbar_arrive(&tempty[acc]);
       }
-      if (active) {
+      if (live) {
         a.cnts[sidx] = ts.st.cnt;
         a.thrs[sidx] = ts.st.thr;
         if (a.top1) {
@@ -454,7 +460,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       }
     }
     // Leave every stream this CTA wrote with at most K keys.
-    if (!__shfl_sync(0xFFFFFFFFu, *abort_flag, 0)) {
+    if (!a.probe && !__shfl_sync(0xFFFFFFFFu, *abort_flag, 0)) {
       for (int mb = 0; mb < a.num_mblocks; mb++) {
         const int q = mb * G::kQueriesPerTile + row_in_block;
         const bool active = q < a.nq;

@@ -49,6 +49,10 @@ struct ScanArgs {
   uint64_t* top2;     // [units][Qp] second best admitted key per stream (zeroed before launch)
   int pool_j;
   int pool_g;
+  // Probe mode (nullable): the epilogue writes each query's largest score of every 32-row
+  // group to probe[q][row / 32] (probe_groups per query) and keeps no candidate streams.
+  float* probe;
+  int probe_groups;
   int32_t* err;       // device error word
   uint64_t timeout_ns;
   EpiParams epi;

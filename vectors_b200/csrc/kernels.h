@@ -52,6 +52,7 @@ StreamGeom stream_geom(int K, int slack);
 cudaError_t launch_merge_streams(const uint64_t* bufs, const uint32_t* cnts, int S, int nq,
                                  int stride, int C, int K, uint64_t* out_keys, uint32_t* out_cnt,
                                  cudaStream_t st, const uint64_t* floor = nullptr);
+cudaError_t launch_probe_floor(const float* probe, int nq, int G, int K, uint64_t* floor, cudaStream_t st);
 cudaError_t launch_ids_to_keys(const int32_t* ids, const int32_t* cnt, int nq, int K, uint64_t* keys,
                                cudaStream_t st);
 cudaError_t launch_gather_rows(const float* src, const int32_t* map, int m, int dim, float* dst,

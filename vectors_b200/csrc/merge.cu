@@ -116,6 +116,33 @@ cudaError_t launch_merge_streams(const uint64_t* bufs, const uint32_t* cnts, int
   return cudaGetLastError();
 }
 
+// Admission floors from a probe sweep: probe[q][g] is query q's largest score over the g-th
+// group of 32 rows, so the K-th largest group maximum x is reached by K distinct rows and the
+// query's K-th best key is at least (bits(x), any id).  One warp per query, bitwise search
+// for the K-th largest of the G order-preserving score bits.
+__global__ void probe_floor_kernel(const float* __restrict__ probe, int nq, int G, int K,
+                                   uint64_t* __restrict__ floor) {
+  const int q = (int)((blockIdx.x * (size_t)blockDim.x + threadIdx.x) >> 5);
+  const int lane = threadIdx.x & 31;
+  if (q >= nq) return;
+  const float* row = probe + (size_t)q * G;
+  uint32_t t = 0;
+  for (int b = 31; b >= 0; b--) {
+    const uint32_t cand = t | (1u << b);
+    uint32_t c = 0;
+    for (int i = lane; i < G; i += 32) c += float_order_bits(row[i]) >= cand ? 1u : 0u;
+    c = __reduce_add_sync(0xFFFFFFFFu, c);
+    if (c >= (uint32_t)K) t = cand;
+  }
+  if (lane == 0) floor[q] = (G >= K && t > 0) ? ((uint64_t)t << 32) : 0ull;
+}
+
+cudaError_t launch_probe_floor(const float* probe, int nq, int G, int K, uint64_t* floor, cudaStream_t st) {
+  if (nq <= 0) return cudaSuccess;
+  probe_floor_kernel<<<(nq * 32 + 255) / 256, 256, 0, st>>>(probe, nq, G, K, floor);
+  return cudaGetLastError();
+}
+
 // Converts sorted keys to the reference's (ordinal, score) output.  kind selects how the
 // score is recovered: the key's float bits (exact scores), or a Hamming distance mapped
 // through BinaryQuantizedVectors.signBitScoreFunction (BinaryQuantizedVectors.java:88-106).

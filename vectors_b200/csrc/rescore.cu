@@ -40,6 +40,7 @@ __global__ void __launch_bounds__(256) rescore_kernel(RescoreArgs a) {
   uint32_t* s_red = (uint32_t*)(s_tmp + cap);
   uint32_t* s_counter = s_red + 32;
   __shared__ int s_complete;
+  __shared__ uint32_t s_nres;
 
   const uint32_t c = a.cand_cnt[q];
   const uint64_t* cand = a.cand + (size_t)q * a.Kc;
@@ -56,6 +57,7 @@ __global__ void __launch_bounds__(256) rescore_kernel(RescoreArgs a) {
       complete = false;
     }
     s_complete = complete ? 1 : 0;
+    s_nres = c;
     if (!complete) {
       int slot = atomicAdd(a.nflag, 1);
       a.flag_list[slot] = q;
@@ -63,17 +65,29 @@ __global__ void __launch_bounds__(256) rescore_kernel(RescoreArgs a) {
   }
   __syncthreads();
   if (!s_complete) return;
+  // Candidates are sorted by approximate key.  With a margin, one whose approximate score is
+  // below A_k - 2m has an exact key below every one of the k best approximate candidates'
+  // exact keys, so only the prefix at or above A_k - 2m needs the exact score.
+  if (a.check_margin && c > (uint32_t)a.k && a.n_rows > (int64_t)a.Kc) {
+    const float cut = key_score(cand[a.k - 1]) - 2.0f * (a.margin ? a.margin[q] : 0.0f);
+    for (uint32_t i = (uint32_t)a.k + threadIdx.x; i < c; i += blockDim.x)
+      if (key_score(cand[i]) < cut && !(key_score(cand[i - 1]) < cut)) s_nres = i;  // first below
+    __syncthreads();
+  }
+  const uint32_t nres = s_nres;
 
   RowF32 qrow{a.queries + (size_t)q * a.dim};
-  for (uint32_t i = warp; i < c; i += blockDim.x / 32) {
+  for (uint32_t i = warp; i < nres; i += blockDim.x / 32) {
     const uint32_t id = key_id(cand[i]);
     RowT x = row_at<RowT>(a.rows, (int64_t)id, a.row_stride);
     const float s = warp_exact_score(a.flavor, a.metric, qrow, x, a.dim);
     if (lane == 0) s_keys[i] = float_key(s, id + a.id_offset);
   }
   __syncthreads();
-  uint32_t n = block_keep_top(s_keys, c, (uint32_t)a.k, s_tmp, s_red, s_counter);
+  uint32_t n = nres;
+  if (nres > 256) n = block_keep_top(s_keys, nres, (uint32_t)a.k, s_tmp, s_red, s_counter);
   block_sort_desc(s_keys, n, cap);
+  if (n > (uint32_t)a.k) n = (uint32_t)a.k;
   // Fp16QuantizedVectors clamps DOT/COSINE scores at 0: if the cut falls on a clamped score,
   // rows tied at 0 are ranked by ordinal alone, which the approximate key cannot see.
   if (a.check_margin && a.flavor == kFlavorFp16Quantized && a.metric != kEuclidean &&

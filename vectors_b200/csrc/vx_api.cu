@@ -379,19 +379,29 @@ int candidate_width(int k, int64_t n) {
 }
 
 // Runs the tcgen05 scan for one query chunk and merges each query's streams into its K best
-// keys.  A pilot sweep (each CTA takes one query block over the first kPilotRows rows) first
-// leaves every query with the K-th best key of those rows as its admission floor; during the
-// main scan CTAs also publish the K-th key of every full stream, so floors keep rising and
-// rows below them are never buffered.  The merge then ignores keys under the final floor.
+// keys.  A probe sweep over the first kPilotRows rows (the same kernel keeping no streams,
+// only each query's maximum per 32-row group) seeds every query's admission floor with the
+// K-th largest group maximum; during the main scan, full streams publish their K-th keys and
+// pooled floors rise further, so rows below them are never buffered.  The merge then ignores
+// keys under the final floor.
 constexpr int64_t kPilotRows = 32768;
 
+cudaError_t launch_probe_sweep(int mode, const CUtensorMap& tmq, const CUtensorMap& tmrows, const ScanArgs& p,
+                               int units, int R, bool two_sm, uint64_t* floor, int K, cudaStream_t st) {
+  cudaError_t e = launch_gemm_scan(mode, tmq, tmrows, p, units, R, two_sm, st);
+  if (e == cudaSuccess) e = launch_probe_floor(p.probe, p.nq, p.probe_groups, K, floor, st);
+  return e;
+}
+
 void scan_and_merge(int mode, const CUtensorMap& tmq, const CUtensorMap& tmrows, ScanArgs a,
-                    int units, int R, int Qp, uint64_t* floor, uint64_t* tops, uint64_t* cand,
-                    uint32_t* cand_cnt, cudaStream_t st) {
+                    int units, int R, int Qp, uint64_t* floor, uint64_t* tops, float* probe,
+                    uint64_t* cand, uint32_t* cand_cnt, cudaStream_t st) {
   const bool two_sm = gemm_two_sm();
   VX_CUDA(cudaMemsetAsync(floor, 0, (size_t)Qp * 8, st));
   a.floor = floor;
   a.m_major = 0;
+  a.probe = nullptr;
+  a.probe_groups = 0;
   // Pooled floors need K <= 2 * (streams per query); each stream then contributes its best
   // (pool_j = 1) or second best (pool_j = 2) key.
   a.top1 = a.top2 = nullptr;
@@ -402,16 +412,17 @@ void scan_and_merge(int mode, const CUtensorMap& tmq, const CUtensorMap& tmrows,
     a.top2 = tops + (size_t)units * Qp;
     VX_CUDA(cudaMemsetAsync(tops, 0, (size_t)2 * units * Qp * 8, st));
   }
-  if (a.n > 2 * kPilotRows && use_pilot()) {
+  if (probe && a.n > 2 * kPilotRows && a.K <= kPilotRows / 32 && use_pilot()) {
+    // probe sweep over the first kPilotRows rows: group maxima only, then the floors
     ScanArgs p = a;
-    p.top1 = p.top2 = nullptr;
     p.n = kPilotRows;
     p.ntiles = kPilotRows / 256;
-    p.m_major = 1;
-    const int punits = std::min(a.num_mblocks, units);
-    VX_CUDA(cudaMemsetAsync(a.cnts, 0, (size_t)punits * Qp * 4, st));
-    VX_CUDA(cudaMemsetAsync(a.thrs, 0, (size_t)punits * Qp * 8, st));
-    VX_TIMED(VX_PROF_PILOT, st, 1, launch_gemm_scan(mode, tmq, tmrows, p, punits, R, two_sm, st));
+    p.top1 = p.top2 = nullptr;
+    p.floor = nullptr;
+    p.probe = probe;
+    p.probe_groups = (int)(kPilotRows / 32);
+    const int punits = (int)std::min<int64_t>((int64_t)p.ntiles * a.num_mblocks, units);
+    VX_TIMED(VX_PROF_PILOT, st, 2, launch_probe_sweep(mode, tmq, tmrows, p, punits, R, two_sm, floor, a.K, st));
   }
   VX_CUDA(cudaMemsetAsync(a.cnts, 0, (size_t)units * Qp * 4, st));
   VX_CUDA(cudaMemsetAsync(a.thrs, 0, (size_t)units * Qp * 8, st));
@@ -465,6 +476,7 @@ int gemm_exact_pass(vx_index* ix, const float* dq, int nq, int k, int Kc, int32_
   uint64_t* thrs = S.alloc<uint64_t>((size_t)unitsMax * QpMax);
   uint64_t* floor = S.alloc<uint64_t>(QpMax);
   uint64_t* tops = S.alloc<uint64_t>((size_t)2 * unitsMax * QpMax);
+  float* probe = S.alloc<float>((size_t)QpMax * (kPilotRows / 32));
   uint64_t* cand = S.alloc<uint64_t>((size_t)qmax * Kc);
   uint32_t* cand_cnt = S.alloc<uint32_t>(qmax);
   int32_t* nflag = S.alloc<int32_t>(std::max(nchunks, 1));
@@ -506,7 +518,7 @@ int gemm_exact_pass(vx_index* ix, const float* dq, int nq, int k, int Kc, int32_
     a.epi.qsq = nullptr;
     a.epi.vsq = nullptr;
     a.epi.cm = 0.0f;
-    scan_and_merge(mode, tmq, ix->tm_rows, a, units, R, Qp, floor, tops, cand, cand_cnt, st);
+    scan_and_merge(mode, tmq, ix->tm_rows, a, units, R, Qp, floor, tops, probe, cand, cand_cnt, st);
     RescoreArgs r;
     r.nq = qc;
     r.dim = dim;
@@ -619,6 +631,7 @@ int search_quantized_scan(vx_index* ix, const float* dq, int nq, int K, int k_ou
     uint64_t* thrs = S.alloc<uint64_t>((size_t)unitsMax * QpMax);
     uint64_t* floor = S.alloc<uint64_t>(QpMax);
     uint64_t* tops = S.alloc<uint64_t>((size_t)2 * unitsMax * QpMax);
+    float* probe = S.alloc<float>((size_t)QpMax * (kPilotRows / 32));
     uint64_t* keys = S.alloc<uint64_t>((size_t)qmax * K);
     uint32_t* kcnt = S.alloc<uint32_t>(qmax);
     int32_t* nflag = S.alloc<int32_t>(1);
@@ -653,7 +666,7 @@ int search_quantized_scan(vx_index* ix, const float* dq, int nq, int K, int k_ou
       a.epi.qsq = qsq;
       a.epi.vsq = ix->vsq;
       a.epi.cm = kc.cm;
-      scan_and_merge(mode, tmq, ix->tm_codes8, a, units, R, Qp, floor, tops, keys, kcnt, st);
+      scan_and_merge(mode, tmq, ix->tm_codes8, a, units, R, Qp, floor, tops, probe, keys, kcnt, st);
       if (rescore) {
         RescoreArgs r{};
         r.nq = qc;

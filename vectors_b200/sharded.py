@@ -1,0 +1,51 @@
+"""Row-sharded search across ranks (one process per GPU).
+
+The database is split into contiguous ordinal ranges exactly as IndexShards.build does
+(vectors-db/.../index/IndexShards.java:64-81); every rank scans its range for the whole query
+batch and returns its local top-k with shard-local ordinals.  The only exchange is those
+per-rank lists: they are all-gathered over the process group (NCCL on GPUs) and merged on
+every rank into the global top-k, ordinals offset by each shard's start, as
+IndexShards.mergeWithOffsets does (IndexShards.java:168-211) but in the canonical
+(score desc, ordinal asc) order.
+"""
+from __future__ import annotations
+
+from typing import Callable, Optional, Sequence
+
+from .index_spi import merge_shards_device, shard_offsets
+
+__all__ = ["shard_range", "gather_and_merge"]
+
+
+def shard_range(n: int, rank: int, world: int) -> tuple[int, int]:
+    """Ordinal range [lo, hi) of `rank`'s shard."""
+    offs = shard_offsets(n, world)
+    return offs[rank], offs[rank + 1]
+
+
+def gather_and_merge(local_ids, local_scores, local_counts, offsets: Sequence[int], k: int,
+                     group=None, merge: Optional[Callable] = None):
+    """All-gathers every rank's (ids [nq][kin], scores [nq][kin], counts [nq]) tensors and
+    merges them into the global top-k.  `offsets` holds each shard's first ordinal; `merge`
+    defaults to the device merge (vx_merge_shards_device) and is called as
+    merge(ids [S][nq][kin], scores [S][nq][kin], counts [S][nq], offsets tensor, k).
+    Every rank takes the same collective steps and returns the same merged result."""
+    import torch
+    import torch.distributed as dist
+
+    world = dist.get_world_size(group)
+    nq, kin = local_ids.shape
+    dev = local_ids.device
+    gi = torch.empty((world, nq, kin), dtype=torch.int32, device=dev)
+    gs = torch.empty((world, nq, kin), dtype=torch.float32, device=dev)
+    gc = torch.empty((world, nq), dtype=torch.int32, device=dev)
+    if dev.type == "cuda":
+        dist.all_gather_into_tensor(gi, local_ids.contiguous(), group=group)
+        dist.all_gather_into_tensor(gs, local_scores.contiguous(), group=group)
+        dist.all_gather_into_tensor(gc, local_counts.contiguous(), group=group)
+    else:  # gloo has no all_gather_into_tensor on every build: gather into per-rank views
+        dist.all_gather(list(gi.unbind(0)), local_ids.contiguous(), group=group)
+        dist.all_gather(list(gs.unbind(0)), local_scores.contiguous(), group=group)
+        dist.all_gather(list(gc.unbind(0)), local_counts.contiguous(), group=group)
+    off = torch.tensor(list(offsets)[:world], dtype=torch.int64, device=dev)
+    return (merge or merge_shards_device)(gi, gs, gc, off, k)
