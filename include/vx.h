@@ -128,7 +128,9 @@ VX_API int vx_bq_build(int32_t device, const uint64_t* words, int64_t n, int32_t
  * concatenated per subspace (ProductQuantizer.codebooks(), subspace sizes from
  * computeSubspaceSizesAndOffsets, ProductQuantizer.java:686-700), no global centroid; codes
  * [n][m] in ordinal order (IvfIndex.java:59).  nprobe / rescore_factor are the adapter's
- * defaults (IvfPqAdapter.java:84-109); vectors (optional) enable rescore_factor > 1. */
+ * defaults (IvfPqAdapter.java:84-109); vectors (optional) enable rescore_factor > 1.  The lists
+ * may hold a subset of the n coded rows (list_offsets[nlist] <= n): a list-sharded index keeps
+ * only its own lists, with global ordinals. */
 VX_API int vx_ivfpq_build(int32_t device, const float* centroids, int32_t nlist, int32_t dim,
                    const int64_t* list_offsets, const int32_t* list_ordinals, int32_t m, int32_t ks,
                    const float* codebooks, const uint8_t* codes, int64_t n, int32_t metric,
@@ -164,6 +166,19 @@ VX_API int vx_ivfpq_search(vx_index* index, const float* queries, int32_t nq, in
 VX_API int vx_ivfpq_search_device(vx_index* index, const float* d_queries, int32_t nq, int32_t dim,
                            int32_t k, int32_t nprobe, int32_t rescore_factor, float min_score,
                            int32_t* d_ids, float* d_scores, int32_t* d_counts, void* stream);
+/* The two halves of vx_ivfpq_search_device, for row-sharded search where every GPU holds the
+ * same centroids: CentroidIndex.routeWithSpillDistances with gamma = 0 (CentroidIndex.java:89-211,
+ * the routing step of IvfIndex.pqSearch, IvfIndex.java:545-547) writes the min(nprobe, nlist)
+ * nearest lists of each query to d_lists [nq][min(nprobe, nlist)], ascending distance, ties by
+ * lower list id; the routed search then scans those lists (ids outside [-1, nlist) are
+ * rejected with VX_ERR_INVALID_ARGUMENT, -1 means no list).  Routing a slice of the queries on
+ * each GPU and exchanging the lists gives the same results as routing everything everywhere. */
+VX_API int vx_ivf_route_device(vx_index* index, const float* d_queries, int32_t nq, int32_t dim,
+                        int32_t nprobe, int32_t* d_lists, void* stream);
+VX_API int vx_ivfpq_search_routed_device(vx_index* index, const float* d_queries, int32_t nq, int32_t dim,
+                                  int32_t k, int32_t nprobe, int32_t rescore_factor, float min_score,
+                                  const int32_t* d_lists, int32_t* d_ids, float* d_scores,
+                                  int32_t* d_counts, void* stream);
 
 /* No counterpart in the reference.  The sign-bit BQ candidate scan of vx_scan_candidates_device
  * for callers that must not allocate device memory while searching (a host that reserves its

@@ -248,6 +248,64 @@ def test_ivfpq_grouped_bit_exact(oracle, metric, nlist):
     _check_float(got, ids, sc, cnt, f"ivfpq grouped rescore m={metric} nlist={nlist}")
 
 
+@pytest.mark.parametrize("metric", [0, 1, 2])
+@pytest.mark.parametrize("dim,nlist", [(64, 64), (96, 30)])
+def test_ivf_route_device_matches_oracle_and_routed_search(oracle, metric, dim, nlist):
+    import torch
+
+    db, q, cent, off, ords, cb, codes = _ivf(oracle, dim=dim, nlist=nlist)
+    a = vx.IvfPqAdapter(nprobe=8)
+    a.build_prebuilt(cent, off, ords, cb, codes, 8, 256, vx.SimilarityFunction(metric))
+    qd = torch.from_numpy(q).cuda()
+    lists = a.route_device(qd, 8)
+    torch.cuda.synchronize()
+    ref, _ = oracle.route(cent, q, metric, 8)
+    assert np.array_equal(lists.cpu().numpy(), ref), "routing differs from the oracle"
+    # routed search over the same lists == the one-call search
+    i1, s1, c1 = a.ivf_search_device(qd, 10, 8)
+    i2, s2, c2 = a.ivf_search_routed_device(qd, 10, 8, lists)
+    torch.cuda.synchronize()
+    assert torch.equal(i1, i2) and torch.equal(s1, s2) and torch.equal(c1, c2)
+    bad = lists.clone()
+    bad[0, 0] = nlist + 5
+    with pytest.raises(vx.IllegalArgumentException):
+        a.ivf_search_routed_device(qd, 10, 8, bad)
+
+
+@pytest.mark.parametrize("m,dim", [(16, 128), (8, 96)])
+def test_ivfpq_list_sharded_equals_unsharded(oracle, m, dim):
+    # two indexes holding the even / odd lists (global ordinals, the other lists empty), searched
+    # with the same routed lists and merged with zero offsets == the unsharded index; covers
+    # both ADC kernels and the skipping of lists without rows
+    import torch
+
+    db, q, cent, off, ords, cb, codes = _ivf(oracle, dim=dim, nlist=32, m=m)
+    full = vx.IvfPqAdapter(nprobe=8)
+    full.build_prebuilt(cent, off, ords, cb, codes, m, 256, vx.SimilarityFunction.EUCLIDEAN)
+    qd = torch.from_numpy(q).cuda()
+    lists = full.route_device(qd, 8)
+    ref = full.ivf_search_device(qd, 10, 8)
+    parts = []
+    for r in range(2):
+        own = [l for l in range(32) if l % 2 == r]
+        sizes = np.zeros(32, np.int64)
+        order = []
+        for l in own:
+            sizes[l] = off[l + 1] - off[l]
+            order.append(ords[off[l]:off[l + 1]])
+        loff = np.zeros(33, np.int64)
+        loff[1:] = np.cumsum(sizes)
+        a = vx.IvfPqAdapter(nprobe=8)
+        a.build_prebuilt(cent, loff, np.concatenate(order), cb, codes, m, 256, vx.SimilarityFunction.EUCLIDEAN)
+        parts.append(a.ivf_search_routed_device(qd, 10, 8, lists))
+    ids = torch.stack([p_[0] for p_ in parts])
+    sc = torch.stack([p_[1] for p_ in parts])
+    cnt = torch.stack([p_[2] for p_ in parts])
+    mi, ms, mc = vx.merge_shards_device(ids, sc, cnt, torch.zeros(2, dtype=torch.int64), 10)
+    torch.cuda.synchronize()
+    assert torch.equal(mi, ref[0]) and torch.equal(ms, ref[1]) and torch.equal(mc, ref[2])
+
+
 def test_ivfpq_routing_matches_oracle(oracle):
     db, q, cent, off, ords, cb, codes = _ivf(oracle)
     lids, _ = oracle.route(cent, q, oracle.EUCLIDEAN, 8)

@@ -60,3 +60,78 @@ def test_two_rank_gloo_sharded_search_matches_unsharded(n):
         for r in range(2):
             with open(os.path.join(d, f"rank{r}")) as f:
                 assert f.read() == "ok", f"rank {r}"
+
+
+def _rows_worker(rank, world, port, total, out_dir):
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    try:
+        from vectors_b200.sharded import gather_rows, shard_range
+
+        full = torch.arange(total * 3, dtype=torch.int32).reshape(total, 3)
+        lo, hi = shard_range(total, rank, world)
+        got = gather_rows(full[lo:hi].clone(), total)
+        with open(os.path.join(out_dir, f"rank{rank}"), "w") as f:
+            f.write("ok" if torch.equal(got, full) else "mismatch")
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("total", [7, 8])
+def test_two_rank_gloo_gather_rows(total):
+    # the routed-list exchange of ivf_search_sharded: uneven query slices padded for the collective
+    import torch.multiprocessing as mp
+
+    with tempfile.TemporaryDirectory() as d:
+        mp.start_processes(_rows_worker, args=(2, _free_port(), total, d), nprocs=2, join=True, start_method="spawn")
+        for r in range(2):
+            with open(os.path.join(d, f"rank{r}")) as f:
+                assert f.read() == "ok", f"rank {r}"
+
+
+def _qshard_worker(rank, world, port, nq, out_dir):
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    try:
+        from oracle import oracle as O
+        from vectors_b200.sharded import search_query_sharded
+
+        db = O.gen_mixture(2000, 48, 8, 0.3, SEEDS[0], SEEDS[1], True)
+        q = O.gen_mixture(nq, 48, 8, 0.3, SEEDS[0], SEEDS[2], True)
+
+        def search(qs):
+            ids, sc, cnt = O.flat_search(db, qs.numpy(), O.DOT_PRODUCT, 7)
+            return torch.from_numpy(ids), torch.from_numpy(sc), torch.from_numpy(cnt)
+
+        mi, ms, mc = search_query_sharded(search, torch.from_numpy(q))
+        ref = O.flat_search(db, q, O.DOT_PRODUCT, 7)
+        ok = (np.array_equal(mi.numpy(), ref[0]) and np.array_equal(ms.numpy(), ref[1])
+              and np.array_equal(mc.numpy(), ref[2]))
+        with open(os.path.join(out_dir, f"rank{rank}"), "w") as f:
+            f.write("ok" if ok else "mismatch")
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("nq", [9, 10])
+def test_two_rank_gloo_query_sharded_search(nq):
+    # the replicated-index mode of the IVF-PQ benchmark: queries split, results all-gathered
+    import torch.multiprocessing as mp
+
+    with tempfile.TemporaryDirectory() as d:
+        mp.start_processes(_qshard_worker, args=(2, _free_port(), nq, d), nprocs=2, join=True, start_method="spawn")
+        for r in range(2):
+            with open(os.path.join(d, f"rank{r}")) as f:
+                assert f.read() == "ok", f"rank {r}"

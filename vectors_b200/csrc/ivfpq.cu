@@ -280,10 +280,28 @@ __global__ void __launch_bounds__(256) route_select_kernel(const float* __restri
     lists[(size_t)q * nprobe + i] = (uint32_t)i < n ? (int32_t)key_id(s_keys[i]) : -1;
 }
 
-__global__ void pair_hist_kernel(const int32_t* __restrict__ lists, int npairs,
-                                 int32_t* __restrict__ counts) {
+// Copies caller-routed list ids, replacing ids outside [-1, nlist) by -1 and counting them.
+__global__ void copy_lists_kernel(const int32_t* __restrict__ src, int n, int nlist, int32_t* __restrict__ dst,
+                                  int32_t* __restrict__ bad) {
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i < npairs && lists[i] >= 0) atomicAdd(&counts[lists[i]], 1);
+  if (i >= n) return;
+  const int32_t l = src[i];
+  const bool ok = l >= -1 && l < nlist;
+  dst[i] = ok ? l : -1;
+  if (!ok) atomicAdd(bad, 1);
+}
+
+// A pair takes part when its list is routed (id >= 0) and holds rows on this device (a
+// list-sharded index keeps only its own lists' rows).
+__device__ __forceinline__ bool pair_live(const int32_t* lists, const int64_t* list_off, int i) {
+  const int32_t l = lists[i];
+  return l >= 0 && list_off[l + 1] > list_off[l];
+}
+
+__global__ void pair_hist_kernel(const int32_t* __restrict__ lists, const int64_t* __restrict__ list_off,
+                                 int npairs, int32_t* __restrict__ counts) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < npairs && pair_live(lists, list_off, i)) atomicAdd(&counts[lists[i]], 1);
 }
 
 // Exclusive scan of nlist counts (single block), also resets the scatter cursors.
@@ -314,10 +332,10 @@ __global__ void pair_scan_kernel(const int32_t* __restrict__ counts, int nlist,
   if (threadIdx.x == blockDim.x - 1) offsets[nlist] = run;
 }
 
-__global__ void pair_scatter_kernel(const int32_t* __restrict__ lists, int npairs,
-                                    int32_t* __restrict__ cursor, int32_t* __restrict__ pairs) {
+__global__ void pair_scatter_kernel(const int32_t* __restrict__ lists, const int64_t* __restrict__ list_off,
+                                    int npairs, int32_t* __restrict__ cursor, int32_t* __restrict__ pairs) {
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i < npairs && lists[i] >= 0) pairs[atomicAdd(&cursor[lists[i]], 1)] = i;
+  if (i < npairs && pair_live(lists, list_off, i)) pairs[atomicAdd(&cursor[lists[i]], 1)] = i;
 }
 
 // Warp-owned candidate buffer in shared memory: all 32 lanes offer one key each.
@@ -355,7 +373,8 @@ __global__ void __launch_bounds__(256) adc_scan_kernel(AdcArgs a) {
   uint32_t* s_counter = s_red + 32;
   __shared__ float s_base;
 
-  for (int64_t w = blockIdx.x; w < a.npairs; w += gridDim.x) {
+  const int64_t live = *a.pair_count;  // pairs grouped by list (routed, non-empty lists)
+  for (int64_t w = blockIdx.x; w < live; w += gridDim.x) {
     const int32_t pair = a.pairs[w];
     const int q = pair / a.nprobe;
     const int p = pair % a.nprobe;
@@ -733,14 +752,21 @@ cudaError_t launch_route(const float* queries, int nq, int dim, const float* cen
   return cudaGetLastError();
 }
 
-cudaError_t launch_group_pairs(const int32_t* lists, int npairs, int nlist, int32_t* counts,
-                               int32_t* offsets, int32_t* cursor, int32_t* pairs, cudaStream_t st) {
+cudaError_t launch_copy_lists(const int32_t* src, int n, int nlist, int32_t* dst, int32_t* bad, cudaStream_t st) {
+  if (n <= 0) return cudaSuccess;
+  copy_lists_kernel<<<(n + 255) / 256, 256, 0, st>>>(src, n, nlist, dst, bad);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_group_pairs(const int32_t* lists, const int64_t* list_off, int npairs, int nlist,
+                               int32_t* counts, int32_t* offsets, int32_t* cursor, int32_t* pairs,
+                               cudaStream_t st) {
   cudaError_t e = cudaMemsetAsync(counts, 0, sizeof(int32_t) * nlist, st);
   if (e != cudaSuccess) return e;
   if (npairs <= 0) return cudaSuccess;
-  pair_hist_kernel<<<(npairs + 255) / 256, 256, 0, st>>>(lists, npairs, counts);
+  pair_hist_kernel<<<(npairs + 255) / 256, 256, 0, st>>>(lists, list_off, npairs, counts);
   pair_scan_kernel<<<1, 1024, 0, st>>>(counts, nlist, offsets, cursor);
-  pair_scatter_kernel<<<(npairs + 255) / 256, 256, 0, st>>>(lists, npairs, cursor, pairs);
+  pair_scatter_kernel<<<(npairs + 255) / 256, 256, 0, st>>>(lists, list_off, npairs, cursor, pairs);
   return cudaGetLastError();
 }
 

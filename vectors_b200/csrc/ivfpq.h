@@ -9,8 +9,9 @@ struct AdcArgs {
   int nq, dim, nprobe, metric;
   int M, Ks, Mp;                 // subspaces, centroids per subspace, padded code bytes per row
   int K;                         // keys kept per (query, list)
-  int64_t npairs;
+  int64_t npairs;                // routed pairs (nq * nprobe)
   const int32_t* pairs;          // pair indices (q * nprobe + p), grouped by list
+  const int32_t* pair_count;     // device count of the grouped pairs
   const int32_t* lists;          // [nq][nprobe] routed list ids
   const float* queries;          // [nq][dim]
   const float* cent;             // [nlist][dim]
@@ -31,9 +32,13 @@ struct AdcArgs {
 cudaError_t launch_route(const float* queries, int nq, int dim, const float* cent, int nlist,
                          int metric, int nprobe, float* qnorm_scratch, float* dist,
                          int32_t* lists, cudaStream_t st);
+cudaError_t launch_copy_lists(const int32_t* src, int n, int nlist, int32_t* dst, int32_t* bad, cudaStream_t st);
 int route_launches(const float* queries, int dim, const float* cent, int nlist, int metric);
-cudaError_t launch_group_pairs(const int32_t* lists, int npairs, int nlist, int32_t* counts,
-                               int32_t* offsets, int32_t* cursor, int32_t* pairs, cudaStream_t st);
+// Buckets the (query, probe) pairs by list: only routed pairs (list id >= 0) whose list holds
+// rows on this device; offsets[nlist] is the number of such pairs.
+cudaError_t launch_group_pairs(const int32_t* lists, const int64_t* list_off, int npairs, int nlist,
+                               int32_t* counts, int32_t* offsets, int32_t* cursor, int32_t* pairs,
+                               cudaStream_t st);
 size_t adc_smem(int M, int Ks, int dim, int R, int K);
 cudaError_t launch_adc_scan(const AdcArgs& a, int R, int grid, cudaStream_t st);
 

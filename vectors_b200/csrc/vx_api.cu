@@ -752,7 +752,7 @@ int search_quantized_scan(vx_index* ix, const float* dq, int nq, int K, int k_ou
 // IVF-PQ: IvfIndex.pqSearch.
 int search_ivfpq(vx_index* ix, const float* dq, int nq, int k, int nprobe, int rescore,
                  float min_score, int32_t* d_ids, float* d_scores, int32_t* d_counts,
-                 cudaStream_t st) {
+                 cudaStream_t st, const int32_t* given_lists = nullptr) {
   const int dim = ix->dim;
   const int probes = std::min(nprobe, ix->nlist);
   int64_t wide = std::min<int64_t>((int64_t)k * rescore, ix->n);
@@ -765,6 +765,9 @@ int search_ivfpq(vx_index* ix, const float* dq, int nq, int k, int nprobe, int r
   // chunk queries: distances [qc][nlist] + outputs [nprobe][qc][K]
   const size_t per_q = (size_t)ix->nlist * 4 + (size_t)probes * (K * 8 + 8) + 64;
   int64_t qch = std::max<int64_t>(64, (int64_t)(scratch_budget() / per_q));
+  Scratch S(st);
+  int32_t* d_bad = S.alloc<int32_t>(1);
+  VX_CUDA(cudaMemsetAsync(d_bad, 0, 4, st));
   for (int q0 = 0; q0 < nq; q0 += (int)qch) {
     const int qc = (int)std::min<int64_t>(qch, nq - q0);
     Scratch T(st);
@@ -780,9 +783,14 @@ int search_ivfpq(vx_index* ix, const float* dq, int nq, int k, int nprobe, int r
     uint32_t* out_cnt = T.alloc<uint32_t>((size_t)probes * qc);
     uint64_t* keys = T.alloc<uint64_t>((size_t)qc * K);
     uint32_t* kcnt = T.alloc<uint32_t>(qc);
-    VX_TIMED(VX_PROF_ROUTE, st, route_launches(dqc, dim, ix->cent, ix->nlist, ix->metric),
-             launch_route(dqc, qc, dim, ix->cent, ix->nlist, ix->metric, probes, qn, dist, lists, st));
-    VX_LAUNCH(3, launch_group_pairs(lists, qc * probes, ix->nlist, counts, offsets, cursor, pairs, st));
+    if (given_lists) {
+      // routed beforehand (possibly by another rank): checked copy, ids outside the index -> -1
+      VX_LAUNCH(1, launch_copy_lists(given_lists + (size_t)q0 * probes, qc * probes, ix->nlist, lists, d_bad, st));
+    } else {
+      VX_TIMED(VX_PROF_ROUTE, st, route_launches(dqc, dim, ix->cent, ix->nlist, ix->metric),
+               launch_route(dqc, qc, dim, ix->cent, ix->nlist, ix->metric, probes, qn, dist, lists, st));
+    }
+    VX_LAUNCH(3, launch_group_pairs(lists, ix->list_off, qc * probes, ix->nlist, counts, offsets, cursor, pairs, st));
     VX_CUDA(cudaMemsetAsync(out_cnt, 0, (size_t)probes * qc * 4, st));
     AdcArgs a;
     a.nq = qc;
@@ -795,6 +803,7 @@ int search_ivfpq(vx_index* ix, const float* dq, int nq, int k, int nprobe, int r
     a.K = K;
     a.npairs = (int64_t)qc * probes;
     a.pairs = pairs;
+    a.pair_count = offsets + ix->nlist;
     a.lists = lists;
     a.queries = dqc;
     a.cent = ix->cent;
@@ -854,6 +863,31 @@ int search_ivfpq(vx_index* ix, const float* dq, int nq, int k, int nprobe, int r
       VX_LAUNCH(1, launch_rescore(r, false, st));
     }
     VX_LAUNCH(1, launch_min_score(os, qc, k, min_score, oc, st));
+  }
+  if (given_lists) {
+    int32_t h_bad = 0;
+    VX_CUDA(cudaMemcpyAsync(&h_bad, d_bad, 4, cudaMemcpyDeviceToHost, st));
+    VX_CUDA(cudaStreamSynchronize(st));
+    if (h_bad) return fail(VX_ERR_INVALID_ARGUMENT, "%d routed list ids are outside [-1, nlist)", h_bad);
+  }
+  return VX_OK;
+}
+
+// CentroidIndex routing alone: the min(nprobe, nlist) nearest lists of every query.
+int route_ivf(vx_index* ix, const float* dq, int nq, int nprobe, int32_t* d_lists, cudaStream_t st) {
+  const int dim = ix->dim;
+  const int probes = std::min(nprobe, ix->nlist);
+  const size_t per_q = (size_t)ix->nlist * 4 + (size_t)dim * 4 + 64;
+  const int64_t qch = std::max<int64_t>(64, (int64_t)(scratch_budget() / per_q));
+  for (int q0 = 0; q0 < nq; q0 += (int)qch) {
+    const int qc = (int)std::min<int64_t>(qch, nq - q0);
+    Scratch T(st);
+    const float* dqc = dq + (size_t)q0 * dim;
+    float* qn = T.alloc<float>((size_t)qc * dim);
+    float* dist = T.alloc<float>((size_t)qc * ix->nlist);
+    VX_TIMED(VX_PROF_ROUTE, st, route_launches(dqc, dim, ix->cent, ix->nlist, ix->metric),
+             launch_route(dqc, qc, dim, ix->cent, ix->nlist, ix->metric, probes, qn, dist,
+                          d_lists + (size_t)q0 * probes, st));
   }
   return VX_OK;
 }
@@ -1287,11 +1321,15 @@ int vx_ivfpq_build(int32_t device, const float* centroids, int32_t nlist, int32_
     if (nprobe <= 0) return fail(VX_ERR_INVALID_ARGUMENT, "nprobe must be positive: %d", nprobe);
     if (rescore_factor < 1) return fail(VX_ERR_INVALID_ARGUMENT, "rescoreFactor must be >= 1: %d", rescore_factor);
     if (int s = check_metric(metric)) return s;
-    if (list_offsets[0] != 0 || list_offsets[nlist] != n)
-      return fail(VX_ERR_INVALID_ARGUMENT, "list offsets must run from 0 to n");
+    // The lists may hold a subset of the n coded rows (a list-sharded index keeps only its
+    // own lists): offsets run from 0 to nl <= n, ordinals index the codes.
+    const int64_t nl = list_offsets[nlist];
+    if (list_offsets[0] != 0 || nl < 0 || nl > n)
+      return fail(VX_ERR_INVALID_ARGUMENT, "list offsets must run from 0 to at most n");
     for (int l = 0; l < nlist; l++)
       if (list_offsets[l + 1] < list_offsets[l]) return fail(VX_ERR_INVALID_ARGUMENT, "list offsets must be non-decreasing");
-    for (int64_t i = 0; i < n; i++)
+    if (nl > 0 && !list_ordinals) return fail(VX_ERR_NULL_POINTER, "null IVF-PQ component");
+    for (int64_t i = 0; i < nl; i++)
       if (list_ordinals[i] < 0 || list_ordinals[i] >= n)
         return fail(VX_ERR_INVALID_ARGUMENT, "list ordinal %d out of range", list_ordinals[i]);
     int nsms = 0;
@@ -1334,12 +1372,12 @@ int vx_ivfpq_build(int32_t device, const float* centroids, int32_t nlist, int32_
       ix->codebooks = dev_alloc<float>(ix, (size_t)co);
       VX_CUDA(cudaMemcpy(ix->codebooks, codebooks, (size_t)co * 4, cudaMemcpyDefault));
       // codes regrouped list-contiguous, rows padded to Mp bytes
-      ix->ordinals = dev_alloc<int32_t>(ix, (size_t)std::max<int64_t>(n, 1));
-      ix->pq_codes = dev_alloc<uint8_t>(ix, (size_t)std::max<int64_t>(n, 1) * ix->Mp);
-      if (n > 0) {
-        VX_CUDA(cudaMemcpy(ix->ordinals, list_ordinals, (size_t)n * 4, cudaMemcpyDefault));
-        std::vector<uint8_t> grouped((size_t)n * ix->Mp, 0);
-        for (int64_t i = 0; i < n; i++)
+      ix->ordinals = dev_alloc<int32_t>(ix, (size_t)std::max<int64_t>(nl, 1));
+      ix->pq_codes = dev_alloc<uint8_t>(ix, (size_t)std::max<int64_t>(nl, 1) * ix->Mp);
+      if (nl > 0) {
+        VX_CUDA(cudaMemcpy(ix->ordinals, list_ordinals, (size_t)nl * 4, cudaMemcpyDefault));
+        std::vector<uint8_t> grouped((size_t)nl * ix->Mp, 0);
+        for (int64_t i = 0; i < nl; i++)
           std::memcpy(&grouped[(size_t)i * ix->Mp], codes + (size_t)list_ordinals[i] * m, (size_t)m);
         VX_CUDA(cudaMemcpy(ix->pq_codes, grouped.data(), grouped.size(), cudaMemcpyDefault));
       }
@@ -1462,6 +1500,40 @@ int vx_ivfpq_search_device(vx_index* ix, const float* d_queries, int32_t nq, int
     VX_CUDA(cudaSetDevice(ix->device));
     return ivfpq_dev(ix, d_queries, nq, k, nprobe, rf, min_score, d_ids, d_scores, d_counts,
                      (cudaStream_t)stream);
+  });
+}
+
+int vx_ivf_route_device(vx_index* ix, const float* d_queries, int32_t nq, int32_t dim, int32_t nprobe,
+                        int32_t* d_lists, void* stream) {
+  return guarded([&]() -> int {
+    if (!ix) return fail(VX_ERR_NULL_POINTER, "index must not be null");
+    if (!d_queries || !d_lists) return fail(VX_ERR_NULL_POINTER, "null buffer");
+    if (ix->kind != VX_KIND_IVFPQ) return fail(VX_ERR_UNSUPPORTED, "not an IVF-PQ index");
+    if (nq <= 0) return fail(VX_ERR_INVALID_ARGUMENT, "queries must not be empty");
+    if (dim != ix->dim)
+      return fail(VX_ERR_INVALID_ARGUMENT, "Query dimension %d does not match index dimension %d", dim, ix->dim);
+    if (nprobe < 1) return fail(VX_ERR_INVALID_ARGUMENT, "nprobe must be >= 1, got %d", nprobe);
+    VX_CUDA(cudaSetDevice(ix->device));
+    return route_ivf(ix, d_queries, nq, nprobe, d_lists, (cudaStream_t)stream);
+  });
+}
+
+int vx_ivfpq_search_routed_device(vx_index* ix, const float* d_queries, int32_t nq, int32_t dim, int32_t k,
+                                  int32_t nprobe, int32_t rf, float min_score, const int32_t* d_lists,
+                                  int32_t* d_ids, float* d_scores, int32_t* d_counts, void* stream) {
+  return guarded([&]() -> int {
+    if (int s = validate_search(ix, d_queries, nq, dim, k, d_ids, d_scores, d_counts)) return s;
+    if (!d_lists) return fail(VX_ERR_NULL_POINTER, "lists must not be null");
+    if (ix->kind != VX_KIND_IVFPQ) return fail(VX_ERR_UNSUPPORTED, "not an IVF-PQ index");
+    if (nprobe < 1) return fail(VX_ERR_INVALID_ARGUMENT, "nprobe must be >= 1, got %d", nprobe);
+    if (rf < 1) return fail(VX_ERR_INVALID_ARGUMENT, "rescoreFactor must be >= 1, got %d", rf);
+    VX_CUDA(cudaSetDevice(ix->device));
+    const cudaStream_t st = (cudaStream_t)stream;
+    if (ix->n == 0) {
+      fill_empty(nq, k, d_ids, d_scores, d_counts, st);
+      return VX_OK;
+    }
+    return search_ivfpq(ix, d_queries, nq, k, nprobe, rf, min_score, d_ids, d_scores, d_counts, st, d_lists);
   });
 }
 

@@ -355,6 +355,7 @@ class IvfPqAdapter(IndexSpi):
                                    n, int(metric), _ptr(v), self.nprobe, self.rescore_factor, C.byref(self._h.ptr))
         )
         self._n, self._dim, self.metric = n, dim, SimilarityFunction(metric)
+        self._nlist = nlist
 
     def ivf_search(self, queries, k: int, nprobe: int, rescore_factor: int = 1, min_score: float = -3.4028235e38):
         q = self._queries(queries, k)
@@ -381,6 +382,42 @@ class IvfPqAdapter(IndexSpi):
             N.lib().vx_ivfpq_search_device(self._h.ptr, C.c_void_p(q.data_ptr()), nq, q.shape[1], k, nprobe,
                                            rescore_factor, float(min_score), C.c_void_p(ids.data_ptr()),
                                            C.c_void_p(sc.data_ptr()), C.c_void_p(cnt.data_ptr()), C.c_void_p(st))
+        )
+        return ids, sc, cnt
+
+    def route_device(self, queries, nprobe: int, stream=None):
+        """The routing step of pqSearch alone (CentroidIndex.routeWithSpillDistances, gamma 0):
+        an int32 [nq][min(nprobe, nlist)] tensor of list ids, nearest first."""
+        import torch
+
+        q = queries.contiguous()
+        nq = q.shape[0]
+        lists = torch.empty((nq, max(1, min(nprobe, self._nlist))), dtype=torch.int32, device=q.device)
+        st = stream if stream is not None else torch.cuda.current_stream(q.device).cuda_stream
+        _check(N.lib().vx_ivf_route_device(self._h.ptr, C.c_void_p(q.data_ptr()), nq, q.shape[1], nprobe,
+                                           C.c_void_p(lists.data_ptr()), C.c_void_p(st)))
+        return lists
+
+    def ivf_search_routed_device(self, queries, k: int, nprobe: int, lists, rescore_factor: int = 1,
+                                 min_score: float = -3.4028235e38, stream=None):
+        """pqSearch over lists routed beforehand (route_device, on any GPU holding the same
+        centroids): same results as ivf_search_device with the same lists."""
+        import torch
+
+        q = queries.contiguous()
+        lst = lists.contiguous()
+        nq = q.shape[0]
+        if lst.dtype != torch.int32 or lst.shape[0] != nq or lst.shape[1] != min(nprobe, self._nlist):
+            raise IllegalArgumentException("lists must be an int32 [nq][min(nprobe, nlist)] tensor")
+        ids = torch.empty((nq, k), dtype=torch.int32, device=q.device)
+        sc = torch.empty((nq, k), dtype=torch.float32, device=q.device)
+        cnt = torch.empty((nq,), dtype=torch.int32, device=q.device)
+        st = stream if stream is not None else torch.cuda.current_stream(q.device).cuda_stream
+        _check(
+            N.lib().vx_ivfpq_search_routed_device(self._h.ptr, C.c_void_p(q.data_ptr()), nq, q.shape[1], k, nprobe,
+                                                  rescore_factor, float(min_score), C.c_void_p(lst.data_ptr()),
+                                                  C.c_void_p(ids.data_ptr()), C.c_void_p(sc.data_ptr()),
+                                                  C.c_void_p(cnt.data_ptr()), C.c_void_p(st))
         )
         return ids, sc, cnt
 

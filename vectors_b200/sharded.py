@@ -14,7 +14,7 @@ from typing import Callable, Optional, Sequence
 
 from .index_spi import merge_shards_device, shard_offsets
 
-__all__ = ["shard_range", "gather_and_merge"]
+__all__ = ["shard_range", "gather_and_merge", "gather_rows", "ivf_search_sharded", "search_query_sharded"]
 
 
 def shard_range(n: int, rank: int, world: int) -> tuple[int, int]:
@@ -49,3 +49,51 @@ def gather_and_merge(local_ids, local_scores, local_counts, offsets: Sequence[in
         dist.all_gather(list(gc.unbind(0)), local_counts.contiguous(), group=group)
     off = torch.tensor(list(offsets)[:world], dtype=torch.int64, device=dev)
     return (merge or merge_shards_device)(gi, gs, gc, off, k)
+
+
+def gather_rows(local, total: int, group=None):
+    """All-gathers a row slice: rank r holds rows [total*r/W, total*(r+1)/W) of a
+    [total][...] tensor; every rank returns the whole tensor (slices padded to equal size
+    for the collective)."""
+    import torch
+    import torch.distributed as dist
+
+    world = dist.get_world_size(group)
+    offs = shard_offsets(total, world)
+    width = max(offs[i + 1] - offs[i] for i in range(world))
+    pad = torch.zeros((width,) + tuple(local.shape[1:]), dtype=local.dtype, device=local.device)
+    pad[: local.shape[0]] = local
+    out = torch.empty((world, width) + tuple(local.shape[1:]), dtype=local.dtype, device=local.device)
+    if local.device.type == "cuda":
+        dist.all_gather_into_tensor(out, pad, group=group)
+    else:
+        dist.all_gather(list(out.unbind(0)), pad, group=group)
+    return torch.cat([out[i, : offs[i + 1] - offs[i]] for i in range(world)], 0)
+
+
+def ivf_search_sharded(adapter, queries, k: int, nprobe: int, offsets: Sequence[int], group=None,
+                       rescore_factor: int = 1):
+    """IVF-PQ search over row-sharded indexes that share the centroids: each rank routes its
+    slice of the queries, the routed lists are all-gathered, every rank scans its own rows for
+    the whole batch, and the per-rank top-k lists are merged (gather_and_merge)."""
+    import torch.distributed as dist
+
+    rank, world = dist.get_rank(group), dist.get_world_size(group)
+    lo, hi = shard_range(queries.shape[0], rank, world)
+    lists = gather_rows(adapter.route_device(queries[lo:hi], nprobe), queries.shape[0], group)
+    ids, sc, cnt = adapter.ivf_search_routed_device(queries, k, nprobe, lists, rescore_factor)
+    return gather_and_merge(ids, sc, cnt, offsets, k, group)
+
+
+def search_query_sharded(search, queries, group=None):
+    """Query-parallel search over an index replicated on every rank (the IVF-PQ index of 10M
+    rows is about 1 GB): rank r answers queries [nq*r/W, nq*(r+1)/W) with search(slice) ->
+    (ids, scores, counts) and the slices are all-gathered, so every rank returns the whole
+    batch.  No table build or list scan is duplicated and the load is balanced by the queries."""
+    import torch.distributed as dist
+
+    rank, world = dist.get_rank(group), dist.get_world_size(group)
+    nq = queries.shape[0]
+    lo, hi = shard_range(nq, rank, world)
+    ids, sc, cnt = search(queries[lo:hi])
+    return gather_rows(ids, nq, group), gather_rows(sc, nq, group), gather_rows(cnt, nq, group)
