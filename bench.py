@@ -202,6 +202,7 @@ def main():
     ap.add_argument("--n", type=int, default=FLAT["n"])
     ap.add_argument("--nq", type=int, default=FLAT["nq"])
     ap.add_argument("--no-ivf", action="store_true")
+    ap.add_argument("--no-quant", action="store_true", help="skip the SQ8 and BQ scan legs")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--ivf-n", type=int, default=IVF["n"])
     ap.add_argument("--ivf-nlist", type=int, default=IVF["nlist"], help="smaller cases for profiling keep n/nlist")
@@ -363,6 +364,12 @@ def main():
     if not args.no_ivf:
         ivf = run_ivf(args, rank, world, local, dev, barrier, max_over_ranks, hbm_peak, peak_kind)
 
+    # ---- SQ8 and BQ candidate scans (selectApproximateCandidates, k = 100)
+    sq8 = bq = None
+    if not args.no_quant:
+        sq8 = run_sq8(args, rank, world, local, dev, barrier, max_over_ranks, tc_sustained, peak_kind)
+        bq = run_bq(args, rank, world, local, dev, barrier, max_over_ranks, tc_sustained, peak_kind)
+
     if rank == 0:
         line = {
             "metric": METRIC,
@@ -387,6 +394,8 @@ def main():
             "gpu_launches": launches,
             "clocks": clk,
             "ivf_pq": ivf,
+            "sq8": sq8,
+            "bq": bq,
         }
         print(json.dumps(line), flush=True)
     if world > 1:
@@ -510,6 +519,157 @@ def run_ivf(args, rank, world, local, dev, barrier, max_over_ranks, hbm_peak, pe
                      "sharding": "index replicated, queries split across ranks" if world > 1 else "single GPU",
                      "breakdown_ms_per_step": {kk: v[0] / args.steps for kk, v in prof.items() if v[1]},
                      "per_rank": per_rank},
+    }
+
+
+SQ8 = dict(n=1_000_000, dim=768, comps=64, sigma=0.3, nq=10_000, k=100)
+BQ = dict(n=10_000_000, dim=1024, comps=256, sigma=0.5, nq=10_000, k=100)
+
+
+def _timed_scan(args, world, dev, barrier, max_over_ranks, step, slot):
+    """Warm-up, then K timed steps (CUDA events on the current stream, max over ranks) and the
+    library's per-kernel time of `slot` per step."""
+    import torch
+
+    from vectors_b200 import _native as N
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    barrier()
+    N.profile_reset()
+    N.profile_enable(True)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    barrier()
+    N.profile_enable(False)
+    prof = N.profile_read()
+    ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
+    kms = max_over_ranks(prof[slot][0] / args.steps)
+    return ms, kms, {kk: v[0] / args.steps for kk, v in prof.items() if v[1]}
+
+
+def run_sq8(args, rank, world, local, dev, barrier, max_over_ranks, tc_sustained, peak_kind):
+    """SQ8 DOT candidate scan, 1M x 768, 10k queries, k = 100: the int8 tcgen05 scan (exact
+    int32 dot + the reference's score epilogue) over this rank's rows."""
+    import torch
+
+    import vectors_b200 as vx
+    from vectors_b200.sharded import gather_and_merge
+
+    P = SQ8
+    n, dim, nq, k = P["n"], P["dim"], P["nq"], P["k"]
+    offs = vx.shard_offsets(n, world)
+    lo, hi = offs[rank], offs[rank + 1]
+    cent = centres(P["comps"], dim, SEED_C ^ 0x5A)
+    x = torch.from_numpy(gen_rows(lo, hi - lo, dim, cent, P["sigma"], SEED_DB ^ 0x5A, True)).to(dev)
+    # ScalarQuantizer encoding (global quantile pair, codes 0..127, per-row correction), as data
+    # preparation on the device; the quantile pair comes from rank 0's first 25k rows
+    qs = torch.quantile(x[:25_000].flatten()[:16_000_000], torch.tensor([0.005, 0.995], device=dev))
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.broadcast(qs, 0)
+    mn, mx = float(qs[0]), float(qs[1])
+    scale, alpha = 127.0 / (mx - mn), (mx - mn) / 127.0
+    qc = torch.clamp(torch.round(scale * (torch.clamp(x, mn, mx) - mn)), 0, 127)
+    corr = (mn * (x - mn / 2) + ((x - mn) - qc * alpha) * (qc * alpha)).sum(1)
+    codes = qc.to(torch.int8).cpu().numpy()
+    del x, qc
+    torch.cuda.empty_cache()
+    a = vx.QuantizedFlatScanAdapter(device=local)
+    a.build_sq8(codes, corr.cpu().numpy(), mn, mx, vx.SimilarityFunction.DOT_PRODUCT)
+    q = torch.from_numpy(gen_rows(0, nq, dim, cent, P["sigma"], SEED_Q ^ 0x5A, True)).to(dev)
+
+    def step():
+        ids, sc, cnt = a.scan_candidates_device(q, k)
+        return ids if world == 1 else gather_and_merge(ids, sc, cnt, offs, k)[0]
+
+    ms, kms, br = _timed_scan(args, world, dev, barrier, max_over_ranks, step, "gemm_scan")
+    a.close()
+    ops = 2.0 * nq * (hi - lo) * dim  # int8 multiply-adds x 2 on this rank
+    achieved = ops / (kms / 1e3) / 1e12 if kms > 0 else None
+    peak = 2.0 * tc_sustained
+    return {
+        "value": nq / (ms / 1e3), "unit": "queries/s", "ms_per_step": ms,
+        "config": {"workload": f"SQ8 DOT candidate scan n={n:,} dim={dim} queries={nq:,} k={k}",
+                   "encoding": "ScalarQuantizer global quantile pair, codes 0..127 (the reference's SQ8)"},
+        "roofline": {"bound": "tensor (int8)", "achieved": achieved, "peak": peak, "unit": "TOP/s",
+                     "frac": (achieved / peak) if achieved else None, "traffic": None,
+                     "kernel": "gemm_scan_kernel (tcgen05 kind::i8, fused top-K)", "per": "GPU",
+                     "peak_source": f"2 x {peak_kind} dense bf16 sustained (int8 MMA runs at twice the bf16 rate)",
+                     "breakdown_ms_per_step": br},
+    }
+
+
+def run_bq(args, rank, world, local, dev, barrier, max_over_ranks, tc_sustained, peak_kind):
+    """BQ (sign-bit) Hamming candidate scan, 10M x 1024 bits, 10k queries, k = 100."""
+    import torch
+
+    import vectors_b200 as vx
+    from vectors_b200.sharded import gather_and_merge
+
+    P = BQ
+    n, dim, nq, k = P["n"], P["dim"], P["nq"], P["k"]
+    offs = vx.shard_offsets(n, world)
+    lo, hi = offs[rank], offs[rank + 1]
+    g = torch.Generator(device=dev)
+    g.manual_seed(0xB0 + 0)  # the same centres on every rank
+    cent = torch.randn((P["comps"], dim), generator=g, device=dev)
+    weights = (1 << torch.arange(64, device=dev, dtype=torch.int64))
+
+    def pack(x):  # BinaryQuantizer.packBits + bytesToLongs: bit j of word w = x[64w + j] >= 0
+        b = (x >= 0).view(x.shape[0], dim // 64, 64).to(torch.int64)
+        return (b * weights).sum(2)
+
+    words = torch.empty((hi - lo, dim // 64), dtype=torch.int64, device=dev)
+    for s0 in range(lo, hi, 1 << 18):
+        s1 = min(hi, s0 + (1 << 18))
+        gc = torch.Generator(device=dev)
+        gc.manual_seed(0xB1 * 1_000_003 + s0)  # chunk-seeded: identical however rows are split
+        comp = torch.randint(0, P["comps"], (s1 - s0,), generator=gc, device=dev)
+        x = cent[comp] + P["sigma"] * torch.randn((s1 - s0, dim), generator=gc, device=dev)
+        words[s0 - lo: s1 - lo] = pack(x)
+    gq = torch.Generator(device=dev)
+    gq.manual_seed(0xB2)
+    comp = torch.randint(0, P["comps"], (nq,), generator=gq, device=dev)
+    q = cent[comp] + P["sigma"] * torch.randn((nq, dim), generator=gq, device=dev)
+    a = vx.QuantizedFlatScanAdapter(device=local)
+    a.build_bq(words.cpu().numpy().view(np.uint64), dim, vx.SimilarityFunction.DOT_PRODUCT)
+    del words
+    torch.cuda.empty_cache()
+
+    def step():
+        ids, sc, cnt = a.scan_candidates_device(q, k)
+        return ids if world == 1 else gather_and_merge(ids, sc, cnt, offs, k)[0]
+
+    ms, kms, br = _timed_scan(args, world, dev, barrier, max_over_ranks, step, "gemm_scan")
+    a.close()
+    rows = hi - lo
+    if br.get("gemm_scan"):
+        # tensor-core path: +-1 int8 operands, dot = D - 2h, exact int32 (2 ops per bit pair)
+        dp8 = (dim + 127) // 128 * 128
+        achieved = 2.0 * nq * rows * dp8 / (kms / 1e3) / 1e12 if kms > 0 else None
+        peak = 2.0 * tc_sustained
+        roof = {"bound": "tensor (int8)", "achieved": achieved, "peak": peak, "unit": "TOP/s",
+                "frac": (achieved / peak) if achieved else None,
+                "kernel": "gemm_scan_kernel (tcgen05 kind::i8 on +-1 expanded bits, Hamming epilogue)",
+                "peak_source": f"2 x {peak_kind} dense bf16 sustained (int8 MMA runs at twice the bf16 rate)"}
+    else:
+        # popcount path (VX_BQ_TENSOR_BYTES below the operand size): XOR + popc + add per word
+        bms = br.get("bq_scan", 0.0)
+        achieved = nq * rows * (dim // 64) / (bms / 1e3) / 1e12 if bms > 0 else None
+        roof = {"bound": "integer pipe (xor + popc)", "achieved": achieved, "unit": "T word-compares/s",
+                "peak": None, "frac": None, "kernel": "bq_scan_kernel"}
+    roof.update({"per": "GPU", "traffic": None, "breakdown_ms_per_step": br})
+    return {
+        "value": nq / (ms / 1e3), "unit": "queries/s", "ms_per_step": ms,
+        "config": {"workload": f"BQ sign-bit Hamming candidate scan n={n:,} x {dim} bits queries={nq:,} k={k}"},
+        "roofline": roof,
     }
 
 

@@ -1,5 +1,5 @@
-"""The 1-CTA tcgen05 scan and the scan without the pilot sweep agree with the oracle too
-(each variant in its own process: the library reads the switches once)."""
+"""The 1-CTA tcgen05 scan, the scan without the pilot sweep and the popcount BQ scan agree with
+the oracle too (each variant in its own process: the library reads the switches once)."""
 import os
 import subprocess
 import sys
@@ -11,7 +11,8 @@ pytestmark = pytest.mark.gpu
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 
-@pytest.mark.parametrize("env", [{"VX_GEMM_1SM": "1"}, {"VX_SCAN_PILOT": "0"}], ids=["one_cta", "no_pilot"])
+@pytest.mark.parametrize("env", [{"VX_GEMM_1SM": "1"}, {"VX_SCAN_PILOT": "0"}, {"VX_BQ_TENSOR_BYTES": "0"}],
+                         ids=["one_cta", "no_pilot", "bq_popcount"])
 def test_scan_variant_matches_oracle(env):
     e = dict(os.environ)
     e.update(env)

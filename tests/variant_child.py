@@ -1,6 +1,7 @@
 """Child process for test_gpu_scan_variants.py: the scan variant is chosen by environment
-variables that the library reads once per process (VX_GEMM_1SM, VX_SCAN_PILOT), so each
-variant runs in a process of its own.  Exits 0 when FLAT and SQ8 results match the oracle."""
+variables that the library reads once per process (VX_GEMM_1SM, VX_SCAN_PILOT,
+VX_BQ_TENSOR_BYTES), so each variant runs in a process of its own.  Exits 0 when FLAT, SQ8 and
+BQ results match the oracle."""
 import sys
 
 import numpy as np
@@ -30,6 +31,14 @@ def main():
     for i, o in enumerate(got):
         assert list(o.ordinals) == list(ids[i, : cnt[i]]), f"sq8 query {i}"
         assert np.array_equal(o.scores, sc[i, : cnt[i]]), f"sq8 query {i} scores"
+    words = O.bq_encode_all(db)
+    b = vx.QuantizedFlatScanAdapter()
+    b.build_bq(words, 96, vx.SimilarityFunction.DOT_PRODUCT)
+    got = b.scan_candidates(q, 100)
+    ids, sc, cnt = O.bq_search(words, 96, q, O.DOT_PRODUCT, 100)
+    for i, o in enumerate(got):
+        assert list(o.ordinals) == list(ids[i, : cnt[i]]), f"bq query {i}"
+        assert np.array_equal(o.scores, sc[i, : cnt[i]]), f"bq query {i} scores"
     print("variant ok")
     return 0
 

@@ -95,6 +95,10 @@ __device__ __forceinline__ float score_of(uint32_t v, int col, const float* s_co
     }
     return scale_mip(adj);
   }
+  if (kMode == kEpiBqHamming) {
+    // +-1 operands: dot = (agreeing bits) - (differing bits) = D - 2h; qi carries D
+    return -(float)((qi - (int32_t)v) >> 1);
+  }
   // kEpiSq8L2: sum (q-v)^2 = sum q^2 + sum v^2 - 2 q.v, exact in int32
   const int32_t sq = qi + __float_as_int(s_col[col]) - 2 * (int32_t)v;
   return __fdiv_rn(1.0f, __fadd_rn(1.0f, __fmul_rn(__int2float_rn(sq), cm)));
@@ -366,7 +370,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const int acc = (int)(t & 1);
       const uint32_t acc_phase = (uint32_t)((t >> 1) & 1);
       const int64_t col0 = nt * BN;
-      if (kMode != kEpiF16Plain) {
+      if (kMode != kEpiF16Plain && kMode != kEpiBqHamming) {
         __syncwarp();
         for (int i = lane; i < BN; i += 32) {
           const int64_t row = col0 + i;
@@ -402,6 +406,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         if (kMode == kEpiSq8Dot || kMode == kEpiSq8Mip) qa = a.epi.qscale[q];
         if (kMode == kEpiSq8L2) qi = a.epi.qsq[q];
       }
+      if (kMode == kEpiBqHamming) qi = a.epi.bits;
       if (__shfl_sync(0xFFFFFFFFu, *abort_flag, 0)) break;
       {
         bool ok = mbar_wait(&tfull[acc], acc_phase, a.timeout_ns, abort_flag);
@@ -542,6 +547,7 @@ cudaError_t launch_variant(int mode, const CUtensorMap& tmA, const CUtensorMap& 
     case kEpiSq8Dot: return launch_mode<true, kEpiSq8Dot, k2Sm>(tmA, tmB, a, grid, R, st);
     case kEpiSq8Mip: return launch_mode<true, kEpiSq8Mip, k2Sm>(tmA, tmB, a, grid, R, st);
     case kEpiSq8L2: return launch_mode<true, kEpiSq8L2, k2Sm>(tmA, tmB, a, grid, R, st);
+    case kEpiBqHamming: return launch_mode<true, kEpiBqHamming, k2Sm>(tmA, tmB, a, grid, R, st);
     default: return cudaErrorInvalidValue;
   }
 }

@@ -15,6 +15,7 @@ enum EpiMode : int {
   kEpiSq8Dot = 3,     // ScalarQuantizedVectors DOT/COSINE score (exact)
   kEpiSq8Mip = 4,     // ScalarQuantizedVectors MAXIMUM_INNER_PRODUCT score (exact)
   kEpiSq8L2 = 5,      // ScalarQuantizedVectors EUCLIDEAN score (exact)
+  kEpiBqHamming = 6,  // sign-bit BQ on +-1 int8 operands: h = (D - dot) / 2, ranked by -h (exact)
 };
 
 struct EpiParams {
@@ -25,6 +26,7 @@ struct EpiParams {
   const int32_t* qsq;   // [nq] SQ8 sum of squared query codes
   const int32_t* vsq;   // [n] SQ8 sum of squared row codes
   float cm;             // SQ8 constMultiplier = alpha^2
+  int32_t bits;         // BQ dimension D (bits per vector)
 };
 
 struct ScanArgs {

@@ -8,7 +8,11 @@ namespace vx {
 // SimilarityFunction ordinals (vectors-core/.../SimilarityFunction.java:30-120).
 enum Metric : int { kEuclidean = 0, kDotProduct = 1, kCosine = 2, kMaxInnerProduct = 3 };
 
-enum FinishKind : int { kFinishFloatKey = 0, kFinishHamming = 1 };
+enum FinishKind : int {
+  kFinishFloatKey = 0,    // key high word = order bits of the reference score
+  kFinishHamming = 1,     // key high word = 0xFFFFFFFF - Hamming distance
+  kFinishNegHamming = 2,  // key high word = order bits of -(Hamming distance) (tensor BQ scan)
+};
 
 // Which reference score an exact re-score reproduces (exact.cuh).
 enum ScoreFlavor : int { kFlavorFlat = 0, kFlavorFp16Quantized = 1, kFlavorIvfRaw = 2 };

@@ -162,6 +162,8 @@ __global__ void finish_keys_kernel(const uint64_t* __restrict__ keys, const uint
       if (kind == kFinishHamming) {
         uint32_t h = 0xFFFFFFFFu - key_hi(key);
         s = bq_score_device(metric, (int)h, dim);
+      } else if (kind == kFinishNegHamming) {
+        s = bq_score_device(metric, (int)(-key_score(key)), dim);
       } else {
         s = key_score(key);
       }

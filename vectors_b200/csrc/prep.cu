@@ -247,4 +247,48 @@ Sq8Consts sq8_consts(float min_q, float max_q) {
   return k;
 }
 
+// One thread per 4 output bytes of a row (Dp8 is a multiple of 128, so of 4).
+__global__ void bq_words_to_i8_kernel(const uint64_t* __restrict__ words, int64_t n, int nwp, int dim,
+                                      int Dp8, int8_t* __restrict__ dst) {
+  const int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  const int per_row = Dp8 / 4;
+  if (t >= n * per_row) return;
+  const int64_t r = t / per_row;
+  const int c0 = (int)(t - r * per_row) * 4;
+  uint32_t out = 0;
+#pragma unroll
+  for (int j = 0; j < 4; j++) {
+    const int c = c0 + j;
+    int8_t v = 0;
+    if (c < dim) v = ((words[r * nwp + (c >> 6)] >> (c & 63)) & 1ull) ? (int8_t)1 : (int8_t)-1;
+    out |= (uint32_t)(uint8_t)v << (8 * j);
+  }
+  reinterpret_cast<uint32_t*>(dst + r * Dp8)[c0 / 4] = out;
+}
+
+__global__ void bq_queries_to_i8_kernel(const float* __restrict__ q, int nq, int dim, int Dp8,
+                                        int8_t* __restrict__ dst) {
+  const int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (t >= (int64_t)nq * Dp8) return;
+  const int64_t r = t / Dp8;
+  const int c = (int)(t - r * Dp8);
+  // BinaryQuantizer.packBits: bit = v >= 0 (NaN -> 0)
+  dst[t] = c < dim ? (q[r * dim + c] >= 0.0f ? (int8_t)1 : (int8_t)-1) : (int8_t)0;
+}
+
+cudaError_t launch_bq_words_to_i8(const uint64_t* words, int64_t n, int nwp, int dim, int Dp8, int8_t* dst,
+                                  cudaStream_t st) {
+  if (n <= 0) return cudaSuccess;
+  const int64_t total = n * (Dp8 / 4);
+  bq_words_to_i8_kernel<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(words, n, nwp, dim, Dp8, dst);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_bq_queries_to_i8(const float* q, int nq, int dim, int Dp8, int8_t* dst, cudaStream_t st) {
+  if (nq <= 0) return cudaSuccess;
+  const int64_t total = (int64_t)nq * Dp8;
+  bq_queries_to_i8_kernel<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(q, nq, dim, Dp8, dst);
+  return cudaGetLastError();
+}
+
 }  // namespace vx

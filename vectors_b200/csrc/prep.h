@@ -29,6 +29,11 @@ cudaError_t launch_margin(const float* qnorm, const float* qerr, int nq, int D, 
                           float* margin, cudaStream_t st);
 cudaError_t launch_sq8_encode_queries(const float* q, int nq, int dim, int Dp8, Sq8Consts k,
                                       int8_t* codes, float* corr, int32_t* sumsq, cudaStream_t st);
+// Sign-bit BQ as +-1 int8 operands for the tensor-core Hamming scan: bit set (v >= 0) -> +1,
+// clear -> -1, dims [dim, Dp8) -> 0.  Rows from packed words [n][nwp]; queries from fp32.
+cudaError_t launch_bq_words_to_i8(const uint64_t* words, int64_t n, int nwp, int dim, int Dp8, int8_t* dst,
+                                  cudaStream_t st);
+cudaError_t launch_bq_queries_to_i8(const float* q, int nq, int dim, int Dp8, int8_t* dst, cudaStream_t st);
 cudaError_t launch_sq8_rows_pad(const int8_t* src, int64_t n, int dim, int Dp8, int8_t* dst,
                                 int32_t* sumsq, cudaStream_t st);
 

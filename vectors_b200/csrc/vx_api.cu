@@ -179,6 +179,16 @@ bool use_pilot() {
   return v;
 }
 
+// BQ indexes also keep a +-1 int8 copy of the bits (8x the storage) for the tensor-core
+// Hamming scan while it fits VX_BQ_TENSOR_BYTES (default 64 GiB; 0 keeps the popcount scan).
+uint64_t bq_tensor_budget() {
+  static const uint64_t v = [] {
+    const char* e = getenv("VX_BQ_TENSOR_BYTES");
+    return (e && *e) ? (uint64_t)strtoull(e, nullptr, 10) : (uint64_t)64 << 30;
+  }();
+  return v;
+}
+
 // IVF-PQ scans use the grouped ADC kernel where the shape allows unless VX_ADC_GROUPED=0.
 bool use_adc_group() {
   static const bool v = [] {
@@ -518,6 +528,7 @@ int gemm_exact_pass(vx_index* ix, const float* dq, int nq, int k, int Kc, int32_
     a.epi.qsq = nullptr;
     a.epi.vsq = nullptr;
     a.epi.cm = 0.0f;
+    a.epi.bits = 0;
     scan_and_merge(mode, tmq, ix->tm_rows, a, units, R, Qp, floor, tops, probe, cand, cand_cnt, st);
     RescoreArgs r;
     r.nq = qc;
@@ -605,7 +616,8 @@ int search_quantized_scan(vx_index* ix, const float* dq, int nq, int K, int k_ou
   Scratch S(st);
   int32_t* d_err = S.alloc<int32_t>(1);
   VX_CUDA(cudaMemsetAsync(d_err, 0, 4, st));
-  if (ix->kind == VX_KIND_SQ8) {
+  if (ix->kind == VX_KIND_SQ8 || (ix->kind == VX_KIND_BQ && ix->codes8)) {
+    const bool bq = ix->kind == VX_KIND_BQ;  // +-1 operands, Hamming epilogue
     const int R = gemm_scan_stream_R(K);
     if (R < 0) return fail(VX_ERR_UNSUPPORTED, "k=%d is larger than this build supports", K);
     const int C = 32 * R;
@@ -615,10 +627,11 @@ int search_quantized_scan(vx_index* ix, const float* dq, int nq, int K, int k_ou
     const int U0 = gemm_scan_units(ntiles, 1 << 20, ix->num_sms, two_sm);
     int64_t qch = (int64_t)(scratch_budget() / ((size_t)U0 * (C * 8 + 12)));
     qch = std::max<int64_t>(QB, qch / QB * QB);
-    const int mode = ix->metric == VX_EUCLIDEAN ? kEpiSq8L2
+    const int mode = bq ? kEpiBqHamming
+                     : ix->metric == VX_EUCLIDEAN ? kEpiSq8L2
                      : ix->metric == VX_MAXIMUM_INNER_PRODUCT ? kEpiSq8Mip
                                                               : kEpiSq8Dot;
-    const Sq8Consts kc = sq8_consts(ix->min_q, ix->max_q);
+    const Sq8Consts kc = bq ? Sq8Consts{0.f, 0.f, 0.f, 0.f, 0.f} : sq8_consts(ix->min_q, ix->max_q);
     // sized once for the largest chunk and reused by every chunk
     const int qmax = (int)std::min<int64_t>(qch, std::max(nq, 1));
     const int QpMax = (qmax + QB - 1) / QB * QB;
@@ -643,7 +656,10 @@ int search_quantized_scan(vx_index* ix, const float* dq, int nq, int K, int k_ou
       const int units = gemm_scan_units(ntiles, mblocks, ix->num_sms, two_sm);
       const float* dqc = dq + (size_t)q0 * dim;
       VX_CUDA(cudaMemsetAsync(qcodes + (size_t)qc * ix->Dp8, 0, (size_t)(Qp - qc) * ix->Dp8, st));
-      VX_LAUNCH(1, launch_sq8_encode_queries(dqc, qc, dim, ix->Dp8, kc, qcodes, qcorr, qsq, st));
+      if (bq)
+        VX_LAUNCH(1, launch_bq_queries_to_i8(dqc, qc, dim, ix->Dp8, qcodes, st));
+      else
+        VX_LAUNCH(1, launch_sq8_encode_queries(dqc, qc, dim, ix->Dp8, kc, qcodes, qcorr, qsq, st));
       CUtensorMap tmq;
       make_tmap(&tmq, qcodes, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, ix->Dp8, Qp, 128);
       ScanArgs a;
@@ -666,6 +682,7 @@ int search_quantized_scan(vx_index* ix, const float* dq, int nq, int K, int k_ou
       a.epi.qsq = qsq;
       a.epi.vsq = ix->vsq;
       a.epi.cm = kc.cm;
+      a.epi.bits = dim;
       scan_and_merge(mode, tmq, ix->tm_codes8, a, units, R, Qp, floor, tops, probe, keys, kcnt, st);
       if (rescore) {
         RescoreArgs r{};
@@ -689,7 +706,8 @@ int search_quantized_scan(vx_index* ix, const float* dq, int nq, int K, int k_ou
         r.flag_list = flag_list;
         VX_LAUNCH(1, launch_rescore(r, false, st));
       } else {
-        VX_LAUNCH(1, launch_finish_keys(keys, kcnt, qc, K, k_out, kFinishFloatKey, ix->metric, dim,
+        VX_LAUNCH(1, launch_finish_keys(keys, kcnt, qc, K, k_out, bq ? kFinishNegHamming : kFinishFloatKey,
+                                        ix->metric, dim,
                                         d_ids + (size_t)q0 * k_out, d_scores + (size_t)q0 * k_out,
                                         d_counts + q0, st));
       }
@@ -1294,6 +1312,16 @@ int vx_bq_build(int32_t device, const uint64_t* words, int64_t n, int32_t dim, i
         VX_CUDA(cudaMemset(ix->words, 0, (size_t)n * nwp * 8));
         VX_CUDA(cudaMemcpy2D(ix->words, (size_t)nwp * 8, words, (size_t)nw * 8, (size_t)nw * 8, (size_t)n,
                              cudaMemcpyDefault));
+        // +-1 int8 operand for the tensor-core Hamming scan (8 bytes per bit of storage)
+        const int Dp8 = (int)round_up(dim, 128);
+        if (bq_tensor_budget() >= (uint64_t)n * Dp8) {
+          ix->Dp8 = Dp8;
+          ix->codes8 = dev_alloc<int8_t>(ix, (size_t)n * Dp8);
+          VX_LAUNCH(1, launch_bq_words_to_i8(ix->words, n, nwp, dim, Dp8, ix->codes8, 0));
+          VX_CUDA(cudaDeviceSynchronize());
+          make_tmap(&ix->tm_codes8, ix->codes8, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, Dp8, n,
+                    gemm_scan_db_box(gemm_two_sm()));
+        }
         if (vectors) ix->rows32 = upload_rows32(ix, vectors, n, dim, row_stride);
       }
     } catch (...) {
