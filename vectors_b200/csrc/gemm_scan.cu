@@ -158,20 +158,69 @@ __device__ __forceinline__ void offer_group(const ScanArgs& a, TileStream& ts, i
 }
 
 // Largest score of a 32-column group (pairwise tree: one epilogue warp per scheduler, so the
-// dependency depth matters more than the operation count).
-template <int kMode>
-__device__ __forceinline__ float group_max(const uint32_t (&v)[32], int c0, const float* s_col,
-                                           const float* s_col2, float qa, int32_t qi, float cm) {
-  float m[16];
+// dependency depth matters more than the operation count).  The integer modes take the
+// extreme of the cheapest exact inner quantity (BQ: the raw dot; SQ8: adj or the integer
+// squared distance) and apply the score's monotone tail once; the result is exact.
+__device__ __forceinline__ int32_t imax_tree32(const uint32_t (&v)[32]) {
+  int32_t m[16];
 #pragma unroll
-  for (int i = 0; i < 16; i++)
-    m[i] = fmaxf(score_of<kMode>(v[2 * i], c0 + 2 * i, s_col, s_col2, qa, qi, cm),
-                 score_of<kMode>(v[2 * i + 1], c0 + 2 * i + 1, s_col, s_col2, qa, qi, cm));
+  for (int i = 0; i < 16; i++) m[i] = max((int32_t)v[2 * i], (int32_t)v[2 * i + 1]);
 #pragma unroll
   for (int w = 8; w >= 1; w >>= 1)
 #pragma unroll
-    for (int i = 0; i < w; i++) m[i] = fmaxf(m[i], m[i + w]);
+    for (int i = 0; i < w; i++) m[i] = max(m[i], m[i + w]);
   return m[0];
+}
+
+template <int kMode>
+__device__ __forceinline__ float group_max(const uint32_t (&v)[32], int c0, const float* s_col,
+                                           const float* s_col2, float qa, int32_t qi, const EpiParams& e) {
+  if constexpr (kMode == kEpiBqHamming) {
+    return score_of<kMode>((uint32_t)imax_tree32(v), 0, s_col, s_col2, qa, qi, e.cm);
+  } else if constexpr (kMode == kEpiSq8Dot || kMode == kEpiSq8Mip) {
+    // exact: the largest adj = raw * cm + queryCorrection + correction, then the monotone tail
+    float m[16];
+#pragma unroll
+    for (int i = 0; i < 16; i++) {
+      const float a0 = __fadd_rn(__fadd_rn(__fmul_rn(__int2float_rn((int32_t)v[2 * i]), e.cm), qa), s_col[c0 + 2 * i]);
+      const float a1 =
+          __fadd_rn(__fadd_rn(__fmul_rn(__int2float_rn((int32_t)v[2 * i + 1]), e.cm), qa), s_col[c0 + 2 * i + 1]);
+      m[i] = fmaxf(a0, a1);
+    }
+#pragma unroll
+    for (int w = 8; w >= 1; w >>= 1)
+#pragma unroll
+      for (int i = 0; i < w; i++) m[i] = fmaxf(m[i], m[i + w]);
+    const float adj = m[0];
+    if (kMode == kEpiSq8Dot) {
+      const float h = __fmul_rn(__fadd_rn(1.0f, adj), 0.5f);
+      return h >= 0.0f ? h : (h != h ? h : 0.0f);
+    }
+    return scale_mip(adj);
+  } else if constexpr (kMode == kEpiSq8L2) {
+    // exact: the smallest integer squared distance, then the monotone tail
+    int32_t m[16];
+#pragma unroll
+    for (int i = 0; i < 16; i++)
+      m[i] = min(qi + __float_as_int(s_col[c0 + 2 * i]) - 2 * (int32_t)v[2 * i],
+                 qi + __float_as_int(s_col[c0 + 2 * i + 1]) - 2 * (int32_t)v[2 * i + 1]);
+#pragma unroll
+    for (int w = 8; w >= 1; w >>= 1)
+#pragma unroll
+      for (int i = 0; i < w; i++) m[i] = min(m[i], m[i + w]);
+    return __fdiv_rn(1.0f, __fadd_rn(1.0f, __fmul_rn(__int2float_rn(m[0]), e.cm)));
+  } else {
+    float m[16];
+#pragma unroll
+    for (int i = 0; i < 16; i++)
+      m[i] = fmaxf(score_of<kMode>(v[2 * i], c0 + 2 * i, s_col, s_col2, qa, qi, e.cm),
+                   score_of<kMode>(v[2 * i + 1], c0 + 2 * i + 1, s_col, s_col2, qa, qi, e.cm));
+#pragma unroll
+    for (int w = 8; w >= 1; w >>= 1)
+#pragma unroll
+      for (int i = 0; i < w; i++) m[i] = fmaxf(m[i], m[i + w]);
+    return m[0];
+  }
 }
 
 // Pooled-floor check after row tile li (0-based) of a unit's range: right after its first
@@ -423,14 +472,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * BN);
 #pragma unroll 1
       for (int g = 0; g < BN / 32; g++) {
+        const int c0 = g * 32;
+        if (c0 >= valid) break;  // groups past the last row (tile-uniform)
         uint32_t v[32];
         __syncwarp();
         tmem_ld_32x32b_x32(taddr + (uint32_t)(g * 32), v);
         tmem_ld_wait();
-        const int c0 = g * 32;
-        const float m = group_max<kMode>(v, c0, s_col, s_col2, qa, qi, a.epi.cm);
-        if (probe) {
-          if (active && c0 < valid) a.probe[(size_t)q * a.probe_groups + (size_t)((col0 + c0) >> 5)] = m;
+        const float m = group_max<kMode>(v, c0, s_col, s_col2, qa, qi, a.epi);
+        if (probe) {  // exact group maxima: the floor needs scores that rows reach
+          if (active) a.probe[(size_t)q * a.probe_groups + (size_t)((col0 + c0) >> 5)] = m;
           continue;
         }
         if (__any_sync(0xFFFFFFFFu, m >= ts.tf))
