@@ -365,10 +365,11 @@ def main():
         ivf = run_ivf(args, rank, world, local, dev, barrier, max_over_ranks, hbm_peak, peak_kind)
 
     # ---- SQ8 and BQ candidate scans (selectApproximateCandidates, k = 100)
-    sq8 = bq = None
+    sq8 = bq = fp16 = None
     if not args.no_quant:
         sq8 = run_sq8(args, rank, world, local, dev, barrier, max_over_ranks, tc_sustained, peak_kind)
         bq = run_bq(args, rank, world, local, dev, barrier, max_over_ranks, tc_sustained, peak_kind)
+        fp16 = run_fp16(args, rank, world, local, dev, barrier, max_over_ranks, tc_sustained, peak_kind)
 
     if rank == 0:
         line = {
@@ -396,6 +397,7 @@ def main():
             "ivf_pq": ivf,
             "sq8": sq8,
             "bq": bq,
+            "fp16": fp16,
         }
         print(json.dumps(line), flush=True)
     if world > 1:
@@ -524,6 +526,7 @@ def run_ivf(args, rank, world, local, dev, barrier, max_over_ranks, hbm_peak, pe
 
 SQ8 = dict(n=1_000_000, dim=768, comps=64, sigma=0.3, nq=10_000, k=100)
 BQ = dict(n=10_000_000, dim=1024, comps=256, sigma=0.5, nq=10_000, k=100)
+FP16 = dict(n_per_gpu=12_500_000, dim=768, comps=4096, sigma=0.3, nq=4096, k=100)
 
 
 def _timed_scan(args, world, dev, barrier, max_over_ranks, step, slot):
@@ -670,6 +673,59 @@ def run_bq(args, rank, world, local, dev, barrier, max_over_ranks, tc_sustained,
         "value": nq / (ms / 1e3), "unit": "queries/s", "ms_per_step": ms,
         "config": {"workload": f"BQ sign-bit Hamming candidate scan n={n:,} x {dim} bits queries={nq:,} k={k}"},
         "roofline": roof,
+    }
+
+
+def run_fp16(args, rank, world, local, dev, barrier, max_over_ranks, tc_sustained, peak_kind):
+    """FP16 DOT candidate scan at the 100M x 768 configuration's per-GPU share: 12.5M stored
+    binary16 rows per GPU (100M at 8 GPUs), 4,096 fp32 queries, k = 100; per-GPU top-k merged.
+    Rows are generated on the device (4,096-component mixture, L2-normalised, rounded to fp16)."""
+    import torch
+
+    import vectors_b200 as vx
+    from vectors_b200.sharded import gather_and_merge
+
+    P = FP16
+    per, dim, nq, k = P["n_per_gpu"], P["dim"], P["nq"], P["k"]
+    offs = [per * r for r in range(world + 1)]
+    g = torch.Generator(device=dev)
+    g.manual_seed(0xF16)  # the same centres on every rank
+    cent = torch.randn((P["comps"], dim), generator=g, device=dev)
+    rows = torch.empty((per, dim), dtype=torch.float16, device=dev)
+    for s0 in range(0, per, 1 << 20):
+        s1 = min(per, s0 + (1 << 20))
+        gc = torch.Generator(device=dev)
+        gc.manual_seed(0xF17 * 1_000_003 + offs[rank] + s0)
+        comp = torch.randint(0, P["comps"], (s1 - s0,), generator=gc, device=dev)
+        x = cent[comp] + P["sigma"] * torch.randn((s1 - s0, dim), generator=gc, device=dev)
+        rows[s0:s1] = (x / x.norm(dim=1, keepdim=True)).half()
+    gq = torch.Generator(device=dev)
+    gq.manual_seed(0xF18)
+    comp = torch.randint(0, P["comps"], (nq,), generator=gq, device=dev)
+    q = cent[comp] + P["sigma"] * torch.randn((nq, dim), generator=gq, device=dev)
+    q = q / q.norm(dim=1, keepdim=True)
+    a = vx.QuantizedFlatScanAdapter(device=local)
+    a.build_fp16(rows, vx.SimilarityFunction.DOT_PRODUCT)
+    del rows, cent
+    torch.cuda.empty_cache()
+
+    def step():
+        ids, sc, cnt = a.scan_candidates_device(q, k)
+        return ids if world == 1 else gather_and_merge(ids, sc, cnt, offs, k)[0]
+
+    ms, kms, br = _timed_scan(args, world, dev, barrier, max_over_ranks, step, "gemm_scan")
+    a.close()
+    flops = 2.0 * nq * per * dim
+    achieved = flops / (kms / 1e3) / 1e12 if kms > 0 else None
+    return {
+        "value": nq / (ms / 1e3), "unit": "queries/s", "ms_per_step": ms, "scaling": "weak",
+        "config": {"workload": f"FP16 DOT candidate scan, {per:,} x {dim} binary16 rows per GPU "
+                               f"({per * world:,} in total), {nq:,} fp32 queries, k={k}",
+                   "queries": "fp32, as Fp16QuantizedVectors scores them (fp16 operand pass + exact re-score)"},
+        "roofline": {"bound": "tensor (fp16)", "achieved": achieved, "peak": tc_sustained, "unit": "TFLOP/s",
+                     "frac": (achieved / tc_sustained) if achieved else None, "traffic": None, "per": "GPU",
+                     "kernel": "gemm_scan_kernel (tcgen05 kind::f16, fused top-K)",
+                     "peak_source": f"{peak_kind} dense bf16/fp16 sustained", "breakdown_ms_per_step": br},
     }
 
 

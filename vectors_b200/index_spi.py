@@ -289,11 +289,21 @@ class QuantizedFlatScanAdapter(IndexSpi):
         self._n, self._dim, self.metric, self.kind = n, dim, SimilarityFunction(metric), "BQ"
 
     def build_fp16(self, codes, metric, vectors=None):
-        codes = np.ascontiguousarray(np.asarray(codes, dtype=np.uint16))
+        """codes: [n][dim] binary16 bit patterns (numpy uint16, or a CUDA float16 / int16 tensor,
+        copied on the device)."""
         v = None if vectors is None else _as_matrix(vectors, "vectors")
-        n, dim = codes.shape
         self._h.close()
-        _check(N.lib().vx_fp16_build(self.device, _ptr(codes), n, dim, int(metric), _ptr(v), dim, C.byref(self._h.ptr)))
+        if getattr(codes, "is_cuda", False):
+            t = codes.contiguous()
+            if t.element_size() != 2:
+                raise IllegalArgumentException("fp16 codes must be 2-byte elements")
+            n, dim = t.shape
+            ptr = C.c_void_p(t.data_ptr())
+        else:
+            arr = np.ascontiguousarray(np.asarray(codes, dtype=np.uint16))
+            n, dim = arr.shape
+            ptr = _ptr(arr)
+        _check(N.lib().vx_fp16_build(self.device, ptr, n, dim, int(metric), _ptr(v), dim, C.byref(self._h.ptr)))
         self._n, self._dim, self.metric, self.kind = n, dim, SimilarityFunction(metric), "FP16"
 
     def build(self, vectors, metric):
