@@ -161,7 +161,7 @@ struct Scratch {
 size_t scratch_budget() {
   const char* e = getenv("VX_SCRATCH_BYTES");
   if (e && *e) return (size_t)strtoull(e, nullptr, 10);
-  return (size_t)2 << 30;
+  return (size_t)6 << 30;
 }
 
 uint64_t wait_timeout_ns() {
