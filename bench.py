@@ -202,13 +202,16 @@ def main():
     ap.add_argument("--n", type=int, default=FLAT["n"])
     ap.add_argument("--nq", type=int, default=FLAT["nq"])
     ap.add_argument("--no-ivf", action="store_true")
-    ap.add_argument("--no-quant", action="store_true", help="skip the SQ8 and BQ scan legs")
+    ap.add_argument("--no-quant", action="store_true", help="skip the SQ8, BQ and FP16 scan legs")
+    ap.add_argument("--sq8-n", type=int, default=SQ8["n"], help="smaller cases for profiling")
+    ap.add_argument("--bq-n", type=int, default=BQ["n"])
+    ap.add_argument("--fp16-n", type=int, default=FP16["n_per_gpu"], help="rows per GPU")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--ivf-n", type=int, default=IVF["n"])
     ap.add_argument("--ivf-nlist", type=int, default=IVF["nlist"], help="smaller cases for profiling keep n/nlist")
     ap.add_argument("--ivf-nq", type=int, default=IVF["nq"])
     ap.add_argument("--ref-rows", type=int, default=1_000_000)
-    ap.add_argument("--ref-queries", type=int, default=48)
+    ap.add_argument("--ref-queries", type=int, default=256)
     args = ap.parse_args()
 
     rank = int(os.environ.get("RANK", "0"))
@@ -565,7 +568,7 @@ def run_sq8(args, rank, world, local, dev, barrier, max_over_ranks, tc_sustained
     from vectors_b200.sharded import gather_and_merge
 
     P = SQ8
-    n, dim, nq, k = P["n"], P["dim"], P["nq"], P["k"]
+    n, dim, nq, k = args.sq8_n, P["dim"], P["nq"], P["k"]
     offs = vx.shard_offsets(n, world)
     lo, hi = offs[rank], offs[rank + 1]
     cent = centres(P["comps"], dim, SEED_C ^ 0x5A)
@@ -617,7 +620,7 @@ def run_bq(args, rank, world, local, dev, barrier, max_over_ranks, tc_sustained,
     from vectors_b200.sharded import gather_and_merge
 
     P = BQ
-    n, dim, nq, k = P["n"], P["dim"], P["nq"], P["k"]
+    n, dim, nq, k = args.bq_n, P["dim"], P["nq"], P["k"]
     offs = vx.shard_offsets(n, world)
     lo, hi = offs[rank], offs[rank + 1]
     g = torch.Generator(device=dev)
@@ -686,7 +689,7 @@ def run_fp16(args, rank, world, local, dev, barrier, max_over_ranks, tc_sustaine
     from vectors_b200.sharded import gather_and_merge
 
     P = FP16
-    per, dim, nq, k = P["n_per_gpu"], P["dim"], P["nq"], P["k"]
+    per, dim, nq, k = args.fp16_n, P["dim"], P["nq"], P["k"]
     offs = [per * r for r in range(world + 1)]
     g = torch.Generator(device=dev)
     g.manual_seed(0xF16)  # the same centres on every rank

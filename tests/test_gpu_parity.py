@@ -68,6 +68,37 @@ def test_sq8_large_with_pilot_floors(oracle):
     _check_float(got, ids, sc, cnt, "sq8 pilot", exact_scores=True)
 
 
+@pytest.mark.parametrize("metric", [0, 2])
+def test_flat_wide_rows(oracle, metric):
+    # 1536 dims: 24 K chunks per tile
+    db, q = _data(oracle, 4000, 1536, 20, normalize=(metric != 3))
+    f = vx.FlatScanAdapter()
+    f.build(db, vx.SimilarityFunction(metric))
+    got = f.search_batch(q, 10)
+    ids, sc, cnt = oracle.flat_search(db, q, metric, 10)
+    _check_float(got, ids, sc, cnt, f"flat 1536 m={metric}")
+
+
+def test_k_larger_than_index(oracle):
+    # every row is returned, in canonical order, for FLAT, SQ8 and BQ
+    db, q = _data(oracle, 50, 64, 7)
+    f = vx.FlatScanAdapter()
+    f.build(db, vx.SimilarityFunction.COSINE)
+    ids, sc, cnt = oracle.flat_search(db, q, oracle.COSINE, 100)
+    _check_float(f.search_batch(q, 100), ids, sc, cnt, "flat k > n")
+    lo, hi = oracle.sq8_train(db)
+    codes, corr = oracle.sq8_encode_all(lo, hi, db)
+    a = vx.QuantizedFlatScanAdapter()
+    a.build_sq8(codes, corr, lo, hi, vx.SimilarityFunction.DOT_PRODUCT)
+    ids, sc, cnt = oracle.sq8_search(codes, corr, lo, hi, q, oracle.DOT_PRODUCT, 100)
+    _check_float(a.scan_candidates(q, 100), ids, sc, cnt, "sq8 k > n", exact_scores=True)
+    words = oracle.bq_encode_all(db)
+    b = vx.QuantizedFlatScanAdapter()
+    b.build_bq(words, 64, vx.SimilarityFunction.EUCLIDEAN)
+    ids, sc, cnt = oracle.bq_search(words, 64, q, oracle.EUCLIDEAN, 100)
+    _check_float(b.scan_candidates(q, 100), ids, sc, cnt, "bq k > n", exact_scores=True)
+
+
 def test_flat_single_query_and_small_index(oracle):
     db, q = _data(oracle, 5, 32, 3)
     f = vx.FlatScanAdapter()

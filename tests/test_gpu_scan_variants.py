@@ -1,5 +1,6 @@
-"""The 1-CTA tcgen05 scan, the scan without the pilot sweep and the popcount BQ scan agree with
-the oracle too (each variant in its own process: the library reads the switches once)."""
+"""The 1-CTA tcgen05 scan, the scan without the pilot sweep, the popcount BQ scan and searches
+split into several query chunks (small scratch budget) agree with the oracle too (each variant
+in its own process: the library reads the switches once)."""
 import os
 import subprocess
 import sys
@@ -11,8 +12,9 @@ pytestmark = pytest.mark.gpu
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 
-@pytest.mark.parametrize("env", [{"VX_GEMM_1SM": "1"}, {"VX_SCAN_PILOT": "0"}, {"VX_BQ_TENSOR_BYTES": "0"}],
-                         ids=["one_cta", "no_pilot", "bq_popcount"])
+@pytest.mark.parametrize("env", [{"VX_GEMM_1SM": "1"}, {"VX_SCAN_PILOT": "0"}, {"VX_BQ_TENSOR_BYTES": "0"},
+                                 {"VX_SCRATCH_BYTES": "50000000"}],
+                         ids=["one_cta", "no_pilot", "bq_popcount", "query_chunks"])
 def test_scan_variant_matches_oracle(env):
     e = dict(os.environ)
     e.update(env)
