@@ -174,12 +174,42 @@ __global__ void __launch_bounds__(256) route_dist_kernel(const float* __restrict
 // FMA for dot, subtract-then-FMA for L2), then sums the lanes in the reference's order.
 constexpr int kRtQ = 64, kRtC = 32, kRtK = 64, kRtStride = kRtK + 4;
 
+// 16-byte asynchronous global -> shared copy; src_bytes 0 writes zeros (rows past the end).
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* src, uint32_t src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"((uint32_t)__cvta_generic_to_shared(smem_dst)),
+               "l"(src), "r"(src_bytes)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int kPending>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(kPending) : "memory");
+}
+
+// Stages one 64-dim chunk of the block's 64 query rows and 32 centroid rows.
+__device__ __forceinline__ void route_stage(float* s_q, float* s_c, const float* __restrict__ queries, int nq,
+                                            const float* __restrict__ cent, int ngroup, int dim, int q0, int c0,
+                                            int k0) {
+  for (int i = threadIdx.x; i < (kRtQ + kRtC) * (kRtK / 4); i += 256) {
+    const int r = i / (kRtK / 4), v = i % (kRtK / 4);
+    if (r < kRtQ) {
+      const bool in = q0 + r < nq;
+      cp_async16(s_q + r * kRtStride + 4 * v, queries + (in ? (size_t)(q0 + r) * dim + k0 + 4 * v : 0), in ? 16u : 0u);
+    } else {
+      const int rc = r - kRtQ;
+      const bool in = c0 + rc < ngroup;
+      cp_async16(s_c + rc * kRtStride + 4 * v, cent + (in ? (size_t)(c0 + rc) * dim + k0 + 4 * v : 0), in ? 16u : 0u);
+    }
+  }
+  cp_async_commit();
+}
+
 template <bool kL2>
 __global__ void __launch_bounds__(256, 2) route_tile_kernel(const float* __restrict__ queries, int nq, int dim,
                                                              const float* __restrict__ cent, int ngroup, int nlist,
                                                              float* __restrict__ dist) {
-  __shared__ __align__(16) float s_q[kRtQ * kRtStride];
-  __shared__ __align__(16) float s_c[kRtC * kRtStride];
+  extern __shared__ __align__(16) float s_route[];  // 2 x ([64][68] queries, [32][68] centroids)
+  constexpr int kStage = (kRtQ + kRtC) * kRtStride;
   const int q0 = blockIdx.y * kRtQ, c0 = blockIdx.x * kRtC;
   const int tq = threadIdx.x >> 4, tc = threadIdx.x & 15;  // queries tq + 16a, centroids tc + 16b
   float acc[4][2][8];
@@ -189,21 +219,20 @@ __global__ void __launch_bounds__(256, 2) route_tile_kernel(const float* __restr
     for (int b = 0; b < 2; b++)
 #pragma unroll
       for (int j = 0; j < 8; j++) acc[a][b][j] = 0.0f;
+  route_stage(s_route, s_route + kRtQ * kRtStride, queries, nq, cent, ngroup, dim, q0, c0, 0);
+  int buf = 0;
   for (int k0 = 0; k0 < dim; k0 += kRtK) {
-    __syncthreads();
-    for (int i = threadIdx.x; i < kRtQ * (kRtK / 4); i += 256) {
-      const int r = i / (kRtK / 4), v = i % (kRtK / 4);
-      float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (q0 + r < nq) x = *reinterpret_cast<const float4*>(queries + (size_t)(q0 + r) * dim + k0 + 4 * v);
-      *reinterpret_cast<float4*>(s_q + r * kRtStride + 4 * v) = x;
-    }
-    for (int i = threadIdx.x; i < kRtC * (kRtK / 4); i += 256) {
-      const int r = i / (kRtK / 4), v = i % (kRtK / 4);
-      float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (c0 + r < ngroup) x = *reinterpret_cast<const float4*>(cent + (size_t)(c0 + r) * dim + k0 + 4 * v);
-      *reinterpret_cast<float4*>(s_c + r * kRtStride + 4 * v) = x;
+    // the next chunk streams in while this one is scored (double buffer)
+    if (k0 + kRtK < dim) {
+      float* nb = s_route + (buf ^ 1) * kStage;
+      route_stage(nb, nb + kRtQ * kRtStride, queries, nq, cent, ngroup, dim, q0, c0, k0 + kRtK);
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
     }
     __syncthreads();
+    const float* s_q = s_route + buf * kStage;
+    const float* s_c = s_q + kRtQ * kRtStride;
 #pragma unroll 4
     for (int kk = 0; kk < kRtK; kk += 4) {
       float4 qv[4], cv[2];
@@ -230,6 +259,8 @@ __global__ void __launch_bounds__(256, 2) route_tile_kernel(const float* __restr
         }
       }
     }
+    __syncthreads();  // every warp is done with this buffer before it is refilled
+    buf ^= 1;
   }
 #pragma unroll
   for (int a = 0; a < 4; a++)
@@ -727,10 +758,11 @@ cudaError_t launch_route(const float* queries, int nq, int dim, const float* cen
   cudaError_t e = cudaSuccess;
   if (route_tile_applies(qsrc, cent, dim, nlist)) {
     const dim3 grid((group + kRtC - 1) / kRtC, (nq + kRtQ - 1) / kRtQ);
-    if (metric == kEuclidean)
-      route_tile_kernel<true><<<grid, 256, 0, st>>>(qsrc, nq, dim, cent, group, nlist, dist);
-    else
-      route_tile_kernel<false><<<grid, 256, 0, st>>>(qsrc, nq, dim, cent, group, nlist, dist);
+    const size_t rsmem = (size_t)2 * (kRtQ + kRtC) * kRtStride * sizeof(float);
+    auto kern = metric == kEuclidean ? route_tile_kernel<true> : route_tile_kernel<false>;
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)rsmem);
+    if (e != cudaSuccess) return e;
+    kern<<<grid, 256, rsmem, st>>>(qsrc, nq, dim, cent, group, nlist, dist);
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     c_begin = group;
