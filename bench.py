@@ -77,51 +77,92 @@ def gen_rows(first, count, dim, cent, sigma, seed, normalize, sink=None, threads
 
 # ------------------------------------------------------------------ clocks
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+    """SM clocks, power and throttle reasons of this rank's GPU sampled during the timed region.
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    Reads NVML in a background thread of this process (50 ms period; the same counters
+    nvidia-smi's clocks / clocks_event_reasons fields report); an external nvidia-smi poller is
+    the fallback when NVML is missing.  Only one rank samples: several pollers on one box stall
+    kernel launches measurably."""
 
-    def __init__(self, local_rank):
+    REASONS = (("hw_slowdown", "nvmlClocksEventReasonHwSlowdown"),
+               ("hw_thermal_slowdown", "nvmlClocksEventReasonHwThermalSlowdown"),
+               ("sw_thermal_slowdown", "nvmlClocksEventReasonSwThermalSlowdown"),
+               ("sw_power_cap", "nvmlClocksEventReasonSwPowerCap"))
+
+    def __init__(self, local_rank, enabled=True):
         cvd = os.environ.get("CUDA_VISIBLE_DEVICES", "")
         ids = [s.strip() for s in cvd.split(",") if s.strip()]
         self.gpu = ids[local_rank] if local_rank < len(ids) else str(local_rank)
+        self.enabled = enabled
+        self.samples = []
+        self.max_mhz = None
+        self.thread = None
         self.proc = None
+        self.stop_evt = None
 
     def start(self):
+        if not self.enabled:
+            return
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", "-i", self.gpu, f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200"],
-                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-        except OSError:
-            self.proc = None
+            import threading
+
+            import pynvml as nv
+
+            nv.nvmlInit()
+            h = nv.nvmlDeviceGetHandleByIndex(int(self.gpu))
+            self.max_mhz = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+            masks = [(name, getattr(nv, attr)) for name, attr in self.REASONS]
+            self.stop_evt = threading.Event()
+
+            def run():
+                while not self.stop_evt.is_set():
+                    try:
+                        mhz = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+                        bits = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+                        self.samples.append((mhz, [nm for nm, m in masks if bits & m]))
+                    except Exception:
+                        pass
+                    self.stop_evt.wait(0.05)
+
+            self.thread = threading.Thread(target=run, daemon=True)
+            self.thread.start()
+        except Exception:
+            try:
+                self.proc = subprocess.Popen(
+                    ["nvidia-smi", "-i", self.gpu, "--query-gpu=clocks.sm,clocks.max.sm,clocks_event_reasons.hw_slowdown,"
+                     "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+                     "clocks_event_reasons.sw_power_cap", "--format=csv,noheader,nounits", "-lms", "100"],
+                    stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            except OSError:
+                self.proc = None
 
     def stop(self):
-        if not self.proc:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        self.proc.terminate()
-        try:
-            out, _ = self.proc.communicate(timeout=5)
-        except subprocess.TimeoutExpired:
-            self.proc.kill()
-            out, _ = self.proc.communicate()
-        sm, mx, reasons = [], [], set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in out.strip().splitlines():
-            f = [x.strip() for x in line.split(",")]
-            if len(f) < 9:
-                continue
+        if not self.enabled:
+            return None
+        if self.thread is not None:
+            self.stop_evt.set()
+            self.thread.join(timeout=2)
+        elif self.proc is not None:
+            self.proc.terminate()
             try:
-                sm.append(float(f[1]))
-                mx.append(float(f[2]))
-            except ValueError:
-                continue
-            for nm, v in zip(names, f[5:9]):
-                if v.lower() == "active":
-                    reasons.add(nm)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": sorted(reasons), "samples": len(sm)}
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            names = [nm for nm, _ in self.REASONS]
+            for line in out.strip().splitlines():
+                f = [x.strip() for x in line.split(",")]
+                try:
+                    self.max_mhz = float(f[1])
+                    self.samples.append((float(f[0]), [nm for nm, v in zip(names, f[2:6]) if v.lower() == "active"]))
+                except (ValueError, IndexError):
+                    continue
+        else:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no NVML / nvidia-smi"]}
+        sm = [m for m, _ in self.samples]
+        reasons = sorted({r for _, rs in self.samples for r in rs})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": self.max_mhz,
+                "reasons": reasons, "samples": len(sm), "source": "NVML (rank 0's GPU)" if self.thread else "nvidia-smi"}
 
 
 # ------------------------------------------------------------------ helpers
@@ -285,7 +326,7 @@ def main():
     launches0 = vx.kernel_launches()
     N.profile_reset()
     N.profile_enable(True)
-    clocks = ClockSampler(local)
+    clocks = ClockSampler(local, enabled=(rank == 0))
     clocks.start()
     torch.cuda.synchronize()
     barrier()
@@ -300,8 +341,15 @@ def main():
     N.profile_enable(False)
     prof = N.profile_read()
     launches = vx.kernel_launches() - launches0
-    ms = max_over_ranks(ev0.elapsed_time(ev1) / args.steps)
+    ms_local = ev0.elapsed_time(ev1) / args.steps
+    ms = max_over_ranks(ms_local)
     qps = nq / (ms / 1e3)
+    per_rank = None
+    if world > 1:  # each rank's step time and scan time: load balance of the row shards
+        t = torch.tensor([ms_local, prof["gemm_scan"][0] / args.steps], dtype=torch.float64, device=dev)
+        g_ = torch.empty((world, 2), dtype=torch.float64, device=dev)
+        dist.all_gather_into_tensor(g_, t)
+        per_rank = {"step_ms": g_[:, 0].tolist(), "gemm_scan_ms": g_[:, 1].tolist()}
 
     # roofline of the dominant kernel: the tcgen05 scan (algorithmic flops 2 * nq * rows * dim)
     g_ms, g_n = prof["gemm_scan"]
@@ -320,6 +368,7 @@ def main():
         "kernel_ms_per_step": gemm_ms_step,
         "launches_per_step": g_n / args.steps,
         "breakdown_ms_per_step": {kk: v[0] / args.steps for kk, v in prof.items() if v[1]},
+        "per_rank": per_rank,
     }
     traffic_path = os.path.join(ROOT, "profiles", "flat_gemm_scan_traffic.json")
     if os.path.exists(traffic_path):
