@@ -337,6 +337,34 @@ def test_ivfpq_list_sharded_equals_unsharded(oracle, m, dim):
     assert torch.equal(mi, ref[0]) and torch.equal(ms, ref[1]) and torch.equal(mc, ref[2])
 
 
+def test_ivfpq_balanced_masks_equal_unsharded(oracle):
+    # the replicated-index balanced mode of vectors_b200.sharded.ivf_search_balanced, two ranks
+    # emulated on one GPU: lists dealt by assign_lists, each rank scans only its lists' pairs
+    import torch
+
+    from vectors_b200.sharded import assign_lists
+
+    db, q, cent, off, ords, cb, codes = _ivf(oracle, dim=128, nlist=32, m=16)
+    a = vx.IvfPqAdapter(nprobe=8)
+    a.build_prebuilt(cent, off, ords, cb, codes, 16, 256, vx.SimilarityFunction.EUCLIDEAN)
+    qd = torch.from_numpy(q).cuda()
+    ref = a.ivf_search_device(qd, 10, 8)
+    lists = a.route_device(qd, 8)
+    flat = lists.reshape(-1).long()
+    rows = torch.from_numpy(np.diff(off)).cuda()
+    owner = assign_lists(torch.bincount(flat, minlength=32), rows, 2)
+    parts = []
+    for r in range(2):
+        mine = torch.where(owner[lists.long()] == r, lists, torch.full_like(lists, -1))
+        parts.append(a.ivf_search_routed_device(qd, 10, 8, mine))
+    ids = torch.stack([p_[0] for p_ in parts])
+    sc = torch.stack([p_[1] for p_ in parts])
+    cnt = torch.stack([p_[2] for p_ in parts])
+    mi, ms, mc = vx.merge_shards_device(ids, sc, cnt, torch.zeros(2, dtype=torch.int64), 10)
+    torch.cuda.synchronize()
+    assert torch.equal(mi, ref[0]) and torch.equal(ms, ref[1]) and torch.equal(mc, ref[2])
+
+
 def test_ivfpq_routing_matches_oracle(oracle):
     db, q, cent, off, ords, cb, codes = _ivf(oracle)
     lids, _ = oracle.route(cent, q, oracle.EUCLIDEAN, 8)

@@ -135,3 +135,21 @@ def test_two_rank_gloo_query_sharded_search(nq):
         for r in range(2):
             with open(os.path.join(d, f"rank{r}")) as f:
                 assert f.read() == "ok", f"rank {r}"
+
+
+@pytest.mark.parametrize("world", [2, 3, 8])
+def test_assign_lists_deals_every_list_once_and_balances(world):
+    import torch
+
+    from vectors_b200.sharded import assign_lists
+
+    g = torch.Generator().manual_seed(world)
+    pairs = torch.randint(0, 300, (4096,), generator=g)
+    rows = torch.randint(10, 20000, (4096,), generator=g)
+    owner = assign_lists(pairs, rows, world)
+    assert owner.shape == (4096,) and int(owner.min()) >= 0 and int(owner.max()) < world
+    assert torch.equal(owner, assign_lists(pairs.clone(), rows.clone(), world))  # deterministic
+    work = pairs.double() * (rows.double() + 600)
+    loads = torch.zeros(world, dtype=torch.float64).index_add_(0, owner, work)
+    # within one list's work of the mean
+    assert float(loads.max() - loads.mean()) <= float(work.max())

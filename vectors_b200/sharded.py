@@ -14,7 +14,8 @@ from typing import Callable, Optional, Sequence
 
 from .index_spi import merge_shards_device, shard_offsets
 
-__all__ = ["shard_range", "gather_and_merge", "gather_rows", "ivf_search_sharded", "search_query_sharded"]
+__all__ = ["shard_range", "gather_and_merge", "gather_rows", "ivf_search_sharded", "search_query_sharded",
+           "assign_lists", "ivf_search_balanced"]
 
 
 def shard_range(n: int, rank: int, world: int) -> tuple[int, int]:
@@ -97,3 +98,44 @@ def search_query_sharded(search, queries, group=None):
     lo, hi = shard_range(nq, rank, world)
     ids, sc, cnt = search(queries[lo:hi])
     return gather_rows(ids, nq, group), gather_rows(sc, nq, group), gather_rows(cnt, nq, group)
+
+
+def assign_lists(pairs_per_list, list_rows, world: int, table_rows: int = 600):
+    """Deals lists to ranks for one routed batch: work(l) = pairs(l) * (rows(l) + table_rows)
+    (the table build of a pair costs about as much as scanning `table_rows` rows); lists sorted
+    by work (ties by id) are dealt in snake order 0..W-1, W-1..0, ... -- a longest-first deal
+    that keeps the ranks within about one list's work of each other.  Deterministic, so every
+    rank computes the same owners from the same inputs.  Returns owner[l] (int64)."""
+    import torch
+
+    work = pairs_per_list.to(torch.float64) * (list_rows.to(torch.float64) + table_rows)
+    nl = work.shape[0]
+    # sort by (work desc, id asc): stable sort on -work keeps ids ascending within ties
+    order = torch.sort(-work, stable=True).indices
+    pos = torch.arange(nl, device=work.device)
+    rnd, r = pos // world, pos % world
+    snake = torch.where(rnd % 2 == 0, r, world - 1 - r)
+    owner = torch.empty(nl, dtype=torch.int64, device=work.device)
+    owner[order] = snake
+    return owner
+
+
+def ivf_search_balanced(adapter, queries, k: int, nprobe: int, list_rows, group=None, rescore_factor: int = 1):
+    """IVF-PQ search over an index replicated on every rank, balanced by list: each rank routes
+    its slice of the queries, the routed lists are all-gathered, lists are dealt to ranks by
+    their work in this batch (assign_lists), and each rank scans every query's pairs on its own
+    lists -- full four-query table groups, no table built twice -- before the per-rank top-k
+    lists are merged.  `list_rows` is a device tensor of the lists' row counts."""
+    import torch
+    import torch.distributed as dist
+
+    rank, world = dist.get_rank(group), dist.get_world_size(group)
+    nq = queries.shape[0]
+    lo, hi = shard_range(nq, rank, world)
+    lists = gather_rows(adapter.route_device(queries[lo:hi], nprobe), nq, group)
+    flat = lists.reshape(-1).long()
+    pairs = torch.bincount(flat[flat >= 0], minlength=list_rows.shape[0])
+    owner = assign_lists(pairs, list_rows, world)
+    mine = torch.where((lists >= 0) & (owner[lists.clamp_min(0).long()] == rank), lists, torch.full_like(lists, -1))
+    ids, sc, cnt = adapter.ivf_search_routed_device(queries, k, nprobe, mine, rescore_factor)
+    return gather_and_merge(ids, sc, cnt, [0] * (world + 1), k, group)
