@@ -464,7 +464,7 @@ def run_ivf(args, rank, world, local, dev, barrier, max_over_ranks, hbm_peak, pe
 
     import vectors_b200 as vx
     from vectors_b200 import _native as N
-    from vectors_b200.sharded import gather_rows, ivf_search_balanced
+    from vectors_b200.sharded import gather_rows, search_query_sharded
 
     P = IVF
     n, dim, nlist, m, ks = args.ivf_n, P["dim"], args.ivf_nlist, P["m"], P["ks"]
@@ -513,7 +513,6 @@ def run_ivf(args, rank, world, local, dev, barrier, max_over_ranks, hbm_peak, pe
     order = torch.argsort(assign, stable=True).to(torch.int32)
     codes_h = codes.cpu().numpy()
     own = torch.bincount(assign, minlength=nlist)
-    list_rows = own
     loff = torch.zeros(nlist + 1, dtype=torch.int64, device=dev)
     loff[1:] = torch.cumsum(own, 0)
     a = vx.IvfPqAdapter(nprobe=P["nprobe"], device=local)
@@ -530,8 +529,10 @@ def run_ivf(args, rank, world, local, dev, barrier, max_over_ranks, hbm_peak, pe
     def step():
         if world == 1:
             return a.ivf_search_device(q, k, P["nprobe"])[0]
-        # replicated index: route query slices, deal lists to ranks by their work, merge
-        return ivf_search_balanced(a, q, k, P["nprobe"], list_rows)[0]
+        # replicated index: each rank answers its slice of the queries; results all-gathered
+        # (dealing whole lists to ranks is unbalanced on this data: two hub lists carry more
+        # than an eighth of the work at 8 GPUs)
+        return search_query_sharded(lambda qs: a.ivf_search_device(qs, k, P["nprobe"]), q)[0]
 
     for _ in range(args.warmup):
         step()
@@ -552,7 +553,7 @@ def run_ivf(args, rank, world, local, dev, barrier, max_over_ranks, hbm_peak, pe
     adc_local = prof["adc_scan"][0] / args.steps
     adc_ms = max_over_ranks(adc_local)
     per_rank = None
-    if world > 1:  # load balance of the list deal: each rank's scan time
+    if world > 1:  # load balance of the query split: each rank's scan time
         t = torch.tensor([adc_local], dtype=torch.float64, device=dev)
         g_ = torch.empty((world, 1), dtype=torch.float64, device=dev)
         dist.all_gather_into_tensor(g_, t)
@@ -571,8 +572,7 @@ def run_ivf(args, rank, world, local, dev, barrier, max_over_ranks, hbm_peak, pe
                      "frac": (achieved / hbm_peak) if achieved else None, "traffic": None,
                      "kernel": "adc_group_kernel (grouped ADC list scan)", "peak_source": f"{peak_kind} HBM copy",
                      "algorithmic_bytes_per_step": bytes_step, "per": "GPU",
-                     "sharding": "index replicated; queries routed in slices, lists dealt to ranks by work"
-                     if world > 1 else "single GPU",
+                     "sharding": "index replicated, queries split across ranks" if world > 1 else "single GPU",
                      "breakdown_ms_per_step": {kk: v[0] / args.steps for kk, v in prof.items() if v[1]},
                      "per_rank": per_rank},
     }

@@ -125,7 +125,10 @@ def ivf_search_balanced(adapter, queries, k: int, nprobe: int, list_rows, group=
     its slice of the queries, the routed lists are all-gathered, lists are dealt to ranks by
     their work in this batch (assign_lists), and each rank scans every query's pairs on its own
     lists -- full four-query table groups, no table built twice -- before the per-rank top-k
-    lists are merged.  `list_rows` is a device tensor of the lists' row counts."""
+    lists are merged.  `list_rows` is a device tensor of the lists' row counts.  A list is never
+    split, so a batch whose work concentrates in a few lists (centroids near every query, as
+    in high-dimensional Gaussian mixtures) stays unbalanced; search_query_sharded is the robust
+    choice there."""
     import torch
     import torch.distributed as dist
 
