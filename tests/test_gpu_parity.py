@@ -280,6 +280,24 @@ def test_ivfpq_grouped_bit_exact(oracle, metric, nlist):
 
 
 @pytest.mark.parametrize("metric", [0, 1, 2])
+def test_ivfpq_many_queries_per_list_bit_exact(oracle, metric):
+    # 400 queries x 8 probes over 16 lists: ~200 pairs per list, so ~50 four-query groups
+    # scan each list one after another and every query's floor is carried across its eight
+    # lists; rescore 2 and 4 widen the kept candidates (K = 20, 40).
+    db, _, cent, off, ords, cb, codes = _ivf(oracle, n=20000, dim=128, nlist=16, m=16)
+    q = oracle.gen_mixture(400, 128, 32, 0.3, SEED_C, SEED_Q + 7, False)
+    a = vx.IvfPqAdapter(nprobe=8)
+    a.build_prebuilt(cent, off, ords, cb, codes, 16, 256, vx.SimilarityFunction(metric), vectors=db)
+    got = a.ivf_search(q, 10, 8)
+    ids, sc, cnt = oracle.ivfpq_search(cent, off, ords, 16, 256, cb, codes, q, metric, 10, 8)
+    _check_float(got, ids, sc, cnt, f"ivfpq many m={metric}", exact_scores=True)
+    for rf in (2, 4):
+        got = a.ivf_search(q, 10, 8, rescore_factor=rf)
+        ids, sc, cnt = oracle.ivfpq_search(cent, off, ords, 16, 256, cb, codes, q, metric, 10, 8, rf, db)
+        _check_float(got, ids, sc, cnt, f"ivfpq many rescore {rf} m={metric}")
+
+
+@pytest.mark.parametrize("metric", [0, 1, 2])
 @pytest.mark.parametrize("dim,nlist", [(64, 64), (96, 30)])
 def test_ivf_route_device_matches_oracle_and_routed_search(oracle, metric, dim, nlist):
     import torch

@@ -1,6 +1,7 @@
-"""The 1-CTA tcgen05 scan, the scan without the pilot sweep, the popcount BQ scan and searches
-split into several query chunks (small scratch budget) agree with the oracle too (each variant
-in its own process: the library reads the switches once)."""
+"""The 1-CTA tcgen05 scan, the scan without the pilot sweep, the popcount BQ scan, searches
+split into several query chunks (small scratch budget) and the IVF-PQ scan with one table per
+(query, list) pair agree with the oracle too (each variant in its own process: the library
+reads the switches once)."""
 import os
 import subprocess
 import sys
@@ -20,6 +21,17 @@ def test_scan_variant_matches_oracle(env):
     e.update(env)
     e["PYTHONPATH"] = ROOT + os.pathsep + e.get("PYTHONPATH", "")
     r = subprocess.run([sys.executable, os.path.join(ROOT, "tests", "variant_child.py")], env=e,
+                       capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-2000:]
+    assert "variant ok" in r.stdout
+
+
+@pytest.mark.parametrize("env", [{"VX_ADC_GROUPED": "0"}], ids=["per_pair_tables"])
+def test_adc_variant_matches_oracle(env):
+    e = dict(os.environ)
+    e.update(env)
+    e["PYTHONPATH"] = ROOT + os.pathsep + e.get("PYTHONPATH", "")
+    r = subprocess.run([sys.executable, os.path.join(ROOT, "tests", "variant_child.py"), "ivf"], env=e,
                        capture_output=True, text=True, timeout=600)
     assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-2000:]
     assert "variant ok" in r.stdout

@@ -1,7 +1,8 @@
 """Child process for test_gpu_scan_variants.py: the scan variant is chosen by environment
 variables that the library reads once per process (VX_GEMM_1SM, VX_SCAN_PILOT,
-VX_BQ_TENSOR_BYTES), so each variant runs in a process of its own.  Exits 0 when FLAT, SQ8 and
-BQ results match the oracle."""
+VX_BQ_TENSOR_BYTES, VX_ADC_GROUPED), so each variant runs in a process of its own.
+Exits 0 when FLAT, SQ8 and BQ results (or, with the argument "ivf", IVF-PQ results) match the
+oracle."""
 import sys
 
 import numpy as np
@@ -10,7 +11,32 @@ import vectors_b200 as vx
 from oracle import oracle as O
 
 
+def ivf():
+    """IVF-PQ (8-dim subspaces, 256 centroids): the ADC scan variants."""
+    db = O.gen_mixture(20_000, 128, 32, 0.3, 0xC0FFEE03, 0xC0FFEE01, False)
+    q = O.gen_mixture(300, 128, 32, 0.3, 0xC0FFEE03, 0xC0FFEE02, False)
+    cent = O.kmeans_train(db[:5000], 8, 10, 42)
+    assign = O.kmeans_assign(db, cent)
+    off, ords = O.build_ivf_lists(assign, 8)
+    resid = db - cent[assign]
+    cb = O.pq_train(resid, 16, 256)
+    codes = O.pq_encode_all(resid, 16, 256, cb)
+    for metric in (0, 1):
+        a = vx.IvfPqAdapter(nprobe=4)
+        a.build_prebuilt(cent, off, ords, cb, codes, 16, 256, vx.SimilarityFunction(metric), vectors=db)
+        got = a.ivf_search(q, 10, 4)
+        ids, sc, cnt = O.ivfpq_search(cent, off, ords, 16, 256, cb, codes, q, metric, 10, 4)
+        for i, o in enumerate(got):
+            assert list(o.ordinals) == list(ids[i, : cnt[i]]), f"ivfpq m={metric} query {i}"
+            assert np.array_equal(o.scores, sc[i, : cnt[i]]), f"ivfpq m={metric} query {i} scores"
+        a.close()
+    print("variant ok")
+    return 0
+
+
 def main():
+    if sys.argv[1:] == ["ivf"]:
+        return ivf()
     db = O.gen_mixture(120_000, 96, 8, 0.3, 0xC0FFEE03, 0xC0FFEE01, True)
     q = O.gen_mixture(300, 96, 8, 0.3, 0xC0FFEE03, 0xC0FFEE02, True)
     for metric in (0, 2):
