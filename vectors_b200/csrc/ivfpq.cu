@@ -204,6 +204,25 @@ __device__ __forceinline__ void route_stage(float* s_q, float* s_c, const float*
   cp_async_commit();
 }
 
+// Packed pairs of fp32 lanes: each lane of sub / fma.rn.f32x2 is the IEEE single-precision
+// operation with round-to-nearest, so a pair of accumulator lanes updated together gets the
+// same bits as two scalar updates.
+__device__ __forceinline__ uint64_t f2_sub(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ float2 f2_unpack(uint64_t v) {
+  float2 r;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(v));
+  return r;
+}
+
 template <bool kL2>
 __global__ void __launch_bounds__(256, 2) route_tile_kernel(const float* __restrict__ queries, int nq, int dim,
                                                              const float* __restrict__ cent, int ngroup, int nlist,
@@ -212,13 +231,13 @@ __global__ void __launch_bounds__(256, 2) route_tile_kernel(const float* __restr
   constexpr int kStage = (kRtQ + kRtC) * kRtStride;
   const int q0 = blockIdx.y * kRtQ, c0 = blockIdx.x * kRtC;
   const int tq = threadIdx.x >> 4, tc = threadIdx.x & 15;  // queries tq + 16a, centroids tc + 16b
-  float acc[4][2][8];
+  uint64_t acc[4][2][4];  // accumulator lanes (2p, 2p + 1) packed in acc[a][b][p]
 #pragma unroll
   for (int a = 0; a < 4; a++)
 #pragma unroll
     for (int b = 0; b < 2; b++)
 #pragma unroll
-      for (int j = 0; j < 8; j++) acc[a][b][j] = 0.0f;
+      for (int p = 0; p < 4; p++) acc[a][b][p] = 0ull;
   route_stage(s_route, s_route + kRtQ * kRtStride, queries, nq, cent, ngroup, dim, q0, c0, 0);
   int buf = 0;
   for (int k0 = 0; k0 < dim; k0 += kRtK) {
@@ -235,26 +254,23 @@ __global__ void __launch_bounds__(256, 2) route_tile_kernel(const float* __restr
     const float* s_c = s_q + kRtQ * kRtStride;
 #pragma unroll 4
     for (int kk = 0; kk < kRtK; kk += 4) {
-      float4 qv[4], cv[2];
+      ulonglong2 qv[4], cv[2];  // dims (kk, kk + 1) and (kk + 2, kk + 3) as packed pairs
 #pragma unroll
-      for (int a = 0; a < 4; a++) qv[a] = *reinterpret_cast<const float4*>(s_q + (tq + 16 * a) * kRtStride + kk);
+      for (int a = 0; a < 4; a++) qv[a] = *reinterpret_cast<const ulonglong2*>(s_q + (tq + 16 * a) * kRtStride + kk);
 #pragma unroll
-      for (int b = 0; b < 2; b++) cv[b] = *reinterpret_cast<const float4*>(s_c + (tc + 16 * b) * kRtStride + kk);
-      const int jb = kk & 4;  // accumulator lanes jb..jb+3 take dims kk..kk+3
+      for (int b = 0; b < 2; b++) cv[b] = *reinterpret_cast<const ulonglong2*>(s_c + (tc + 16 * b) * kRtStride + kk);
+      const int pb = (kk & 4) >> 1;  // accumulator lanes 2 pb .. 2 pb + 3 take dims kk .. kk + 3
 #pragma unroll
       for (int a = 0; a < 4; a++) {
-        const float qa[4] = {qv[a].x, qv[a].y, qv[a].z, qv[a].w};
 #pragma unroll
         for (int b = 0; b < 2; b++) {
-          const float cb[4] = {cv[b].x, cv[b].y, cv[b].z, cv[b].w};
-#pragma unroll
-          for (int j = 0; j < 4; j++) {
-            if (kL2) {
-              const float d = __fsub_rn(qa[j], cb[j]);
-              acc[a][b][jb + j] = __fmaf_rn(d, d, acc[a][b][jb + j]);
-            } else {
-              acc[a][b][jb + j] = __fmaf_rn(qa[j], cb[j], acc[a][b][jb + j]);
-            }
+          if (kL2) {
+            const uint64_t d0 = f2_sub(qv[a].x, cv[b].x), d1 = f2_sub(qv[a].y, cv[b].y);
+            acc[a][b][pb] = f2_fma(d0, d0, acc[a][b][pb]);
+            acc[a][b][pb + 1] = f2_fma(d1, d1, acc[a][b][pb + 1]);
+          } else {
+            acc[a][b][pb] = f2_fma(qv[a].x, cv[b].x, acc[a][b][pb]);
+            acc[a][b][pb + 1] = f2_fma(qv[a].y, cv[b].y, acc[a][b][pb + 1]);
           }
         }
       }
@@ -268,7 +284,14 @@ __global__ void __launch_bounds__(256, 2) route_tile_kernel(const float* __restr
     for (int b = 0; b < 2; b++) {
       const int q = q0 + tq + 16 * a, c = c0 + tc + 16 * b;
       if (q < nq && c < ngroup) {
-        const float sum = reduce_add8_local(acc[a][b]);
+        float lanes[8];
+#pragma unroll
+        for (int p = 0; p < 4; p++) {
+          const float2 v = f2_unpack(acc[a][b][p]);
+          lanes[2 * p] = v.x;
+          lanes[2 * p + 1] = v.y;
+        }
+        const float sum = reduce_add8_local(lanes);
         dist[(size_t)q * nlist + c] = kL2 ? sum : -sum;
       }
     }
