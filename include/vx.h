@@ -47,7 +47,9 @@ typedef enum vx_status {
   VX_ERR_CUDA = 4,             /* GpuUnavailableException wrapping a native failure (:86-89,117-119) */
   VX_ERR_OUT_OF_MEMORY = 5,
   VX_ERR_UNSUPPORTED = 6,      /* UnsupportedOperationException */
-  VX_ERR_DEVICE_TIMEOUT = 7    /* a bounded device-side wait expired; the context stays usable */
+  VX_ERR_DEVICE_TIMEOUT = 7,   /* a bounded device-side wait expired; the context stays usable */
+  VX_ERR_FORMAT = 8            /* java.io.IOException: a quantized.bin / graph.bin that does not decode
+                                  (QuantizedVectorsCodec.java:131-192) */
 } vx_status;
 
 /* SimilarityFunction ordinals (vectors-core/.../SimilarityFunction.java:30-120). */
@@ -135,6 +137,33 @@ VX_API int vx_ivfpq_build(int32_t device, const float* centroids, int32_t nlist,
                    const int64_t* list_offsets, const int32_t* list_ordinals, int32_t m, int32_t ks,
                    const float* codebooks, const uint8_t* codes, int64_t n, int32_t metric,
                    const float* vectors, int32_t nprobe, int32_t rescore_factor, vx_index** out);
+/* ---- persistent files (host memory; the bytes are not retained) --------------------------
+ * quantized.bin as written by QuantizedVectorsCodec.encode and read by .decode
+ * (vectors-db/.../storage/QuantizedVectorsCodec.java:91-192): little-endian, header magic 'VQTZ'
+ * (FileFormat.java:77), version 1, QuantizerKind ordinal, dimension, vectorCount.  SQ8 (:224-296),
+ * BQ SIGN_BIT (:425-518) and FP16 (:194-221) payloads build the index vx_sq8_build /
+ * vx_bq_build / vx_fp16_build would; SQ4, PQ, BQ BBQ, RABITQ, NVQ, TURBOQUANT and EXTENDED_RABITQ
+ * return VX_ERR_UNSUPPORTED.  The collection's metric is not stored in the file.  vectors
+ * (optional) are the fp32 rows for the two-pass rescore, e.g. a mapped vectors.bin with
+ * row_stride = alignUp(dim*4, 64)/4.  Malformed bytes return VX_ERR_FORMAT with the decoder's
+ * message. */
+VX_API int vx_quantized_bin_info(const uint8_t* bytes, int64_t len, int32_t* kind_ordinal, int32_t* dim,
+                                 int64_t* count);
+VX_API int vx_quantized_bin_build(int32_t device, const uint8_t* bytes, int64_t len, int32_t metric,
+                                  const float* vectors, int64_t row_stride, vx_index** out);
+/* graph.bin of an IVF_PQ generation: the bytes of IvfIndex.encode (vectors-ivf/.../IvfIndex.java:
+ * 354-400; decode :408-442, PQ trailer :450-500) around BuoyIndex.encode (BuoyIndex.java:130-167),
+ * big-endian as java.nio.ByteBuffer and java.io.DataOutputStream write them; read by
+ * VectorCollectionImpl.openIvfPqAdapter (VectorCollectionImpl.java:703-718).  Builds the index
+ * vx_ivfpq_build would from the centroids, partitions, codebooks and ordinal-ordered codes.
+ * metric -1 takes the routing metric recorded in the file; another metric must equal it.
+ * IVF-flat files (no PQ trailer) and PQ with a global centroid return VX_ERR_UNSUPPORTED;
+ * HARMONY key dimensions are read and ignored (IvfIndex.pqSearch does not use them). */
+VX_API int vx_ivf_graph_info(const uint8_t* bytes, int64_t len, int32_t* nlist, int32_t* dim, int64_t* count,
+                             int32_t* m, int32_t* metric);
+VX_API int vx_ivf_graph_build(int32_t device, const uint8_t* bytes, int64_t len, int32_t metric,
+                              const float* vectors, int64_t row_stride, int32_t nprobe, int32_t rescore_factor,
+                              vx_index** out);
 /* IndexSpi.size() and the index's shape. */
 VX_API int vx_index_info(const vx_index* index, int32_t* kind, int64_t* size, int32_t* dim,
                   int32_t* metric);

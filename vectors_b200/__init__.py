@@ -8,6 +8,7 @@ from ._native import VxError, device_count, kernel_launches, lib  # noqa: F401
 from .index_spi import (  # noqa: F401
     FlatScanAdapter,
     GpuUnavailableException,
+    IOException,
     IllegalArgumentException,
     IndexSpi,
     IvfPqAdapter,
@@ -16,7 +17,9 @@ from .index_spi import (  # noqa: F401
     SearchOutcome,
     SimilarityFunction,
     UnsupportedOperationException,
+    ivf_graph_info,
     merge_shards_device,
+    quantized_bin_info,
     shard_offsets,
 )
 
@@ -31,6 +34,9 @@ __all__ = [
     "NullPointerException",
     "GpuUnavailableException",
     "UnsupportedOperationException",
+    "IOException",
+    "quantized_bin_info",
+    "ivf_graph_info",
     "merge_shards_device",
     "shard_offsets",
     "device_count",

@@ -1,0 +1,20 @@
+// internal.h -- library-internal entry points shared between translation units of libvx.so
+// (hidden: the library is built with -fvisibility=hidden and these carry no VX_API).
+#pragma once
+#include <cstdint>
+
+#include "../../include/vx.h"
+
+namespace vx {
+
+// Records `msg` for vx_last_error() and returns `status` (vx_api.cu).
+int record_failure(int status, const char* msg);
+
+// vx_ivfpq_build with the full-precision rows `row_stride` floats apart (vx_api.cu).
+int ivfpq_build_strided(int32_t device, const float* centroids, int32_t nlist, int32_t dim,
+                        const int64_t* list_offsets, const int32_t* list_ordinals, int32_t m, int32_t ks,
+                        const float* codebooks, const uint8_t* codes, int64_t n, int32_t metric,
+                        const float* vectors, int64_t row_stride, int32_t nprobe, int32_t rescore_factor,
+                        vx_index** out);
+
+}  // namespace vx

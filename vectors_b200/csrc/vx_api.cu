@@ -18,6 +18,7 @@
 #include "../../include/vx.h"
 #include "common.cuh"
 #include "gemm_scan.h"
+#include "internal.h"
 #include "ivfpq.h"
 #include "kernels.h"
 #include "prep.h"
@@ -1337,6 +1338,19 @@ int vx_ivfpq_build(int32_t device, const float* centroids, int32_t nlist, int32_
                    const int64_t* list_offsets, const int32_t* list_ordinals, int32_t m, int32_t ks,
                    const float* codebooks, const uint8_t* codes, int64_t n, int32_t metric,
                    const float* vectors, int32_t nprobe, int32_t rescore_factor, vx_index** out) {
+  return vx::ivfpq_build_strided(device, centroids, nlist, dim, list_offsets, list_ordinals, m, ks, codebooks,
+                                 codes, n, metric, vectors, dim, nprobe, rescore_factor, out);
+}
+
+}  // extern "C"
+
+namespace vx {
+// vx_ivfpq_build with full-precision rows `row_stride` floats apart (a vectors.bin mapping).
+int ivfpq_build_strided(int32_t device, const float* centroids, int32_t nlist, int32_t dim,
+                        const int64_t* list_offsets, const int32_t* list_ordinals, int32_t m, int32_t ks,
+                        const float* codebooks, const uint8_t* codes, int64_t n, int32_t metric,
+                        const float* vectors, int64_t row_stride, int32_t nprobe, int32_t rescore_factor,
+                        vx_index** out) {
   return guarded([&]() -> int {
     if (!out) return fail(VX_ERR_NULL_POINTER, "out must not be null");
     *out = nullptr;
@@ -1348,6 +1362,8 @@ int vx_ivfpq_build(int32_t device, const float* centroids, int32_t nlist, int32_
     if (ks <= 0 || ks > 256) return fail(VX_ERR_INVALID_ARGUMENT, "numClusters must be in [1, 256]: %d", ks);
     if (nprobe <= 0) return fail(VX_ERR_INVALID_ARGUMENT, "nprobe must be positive: %d", nprobe);
     if (rescore_factor < 1) return fail(VX_ERR_INVALID_ARGUMENT, "rescoreFactor must be >= 1: %d", rescore_factor);
+    if (vectors && row_stride < dim)
+      return fail(VX_ERR_INVALID_ARGUMENT, "row_stride %lld < dimension %d", (long long)row_stride, dim);
     if (int s = check_metric(metric)) return s;
     // The lists may hold a subset of the n coded rows (a list-sharded index keeps only its
     // own lists): offsets run from 0 to nl <= n, ordinals index the codes.
@@ -1409,7 +1425,7 @@ int vx_ivfpq_build(int32_t device, const float* centroids, int32_t nlist, int32_
           std::memcpy(&grouped[(size_t)i * ix->Mp], codes + (size_t)list_ordinals[i] * m, (size_t)m);
         VX_CUDA(cudaMemcpy(ix->pq_codes, grouped.data(), grouped.size(), cudaMemcpyDefault));
       }
-      if (vectors && n > 0) ix->rows32 = upload_rows32(ix, vectors, n, dim, dim);
+      if (vectors && n > 0) ix->rows32 = upload_rows32(ix, vectors, n, dim, row_stride);
     } catch (...) {
       free_index(ix);
       throw;
@@ -1418,6 +1434,9 @@ int vx_ivfpq_build(int32_t device, const float* centroids, int32_t nlist, int32_
     return VX_OK;
   });
 }
+}  // namespace vx
+
+extern "C" {
 
 int vx_index_info(const vx_index* ix, int32_t* kind, int64_t* size, int32_t* dim, int32_t* metric) {
   if (!ix) return fail(VX_ERR_NULL_POINTER, "index must not be null");

@@ -20,6 +20,7 @@ from __future__ import annotations
 
 import ctypes as C
 import enum
+import os
 import math
 from dataclasses import dataclass, field
 from typing import Optional, Sequence
@@ -45,6 +46,10 @@ class UnsupportedOperationException(NotImplementedError):
     pass
 
 
+class IOException(OSError):
+    """java.io.IOException: a quantized.bin / graph.bin that does not decode."""
+
+
 _EXC = {
     N.VX_ERR_INVALID_ARGUMENT: IllegalArgumentException,
     N.VX_ERR_NULL_POINTER: NullPointerException,
@@ -53,6 +58,7 @@ _EXC = {
     N.VX_ERR_OUT_OF_MEMORY: GpuUnavailableException,
     N.VX_ERR_UNSUPPORTED: UnsupportedOperationException,
     N.VX_ERR_DEVICE_TIMEOUT: GpuUnavailableException,
+    N.VX_ERR_FORMAT: IOException,
 }
 
 
@@ -97,6 +103,51 @@ def _as_matrix(vectors, name: str) -> np.ndarray:
     if a.ndim != 2:
         raise IllegalArgumentException(f"{name} must be a 2-D array of rows")
     return a
+
+
+def _file_bytes(data) -> np.ndarray:
+    """The bytes of a persistent file: a path, bytes-like, or a uint8 array (e.g. np.memmap)."""
+    if isinstance(data, (str, os.PathLike)):
+        return np.fromfile(data, dtype=np.uint8)
+    if data is None:
+        raise NullPointerException("bytes must not be null")
+    if isinstance(data, np.ndarray):
+        return np.ascontiguousarray(data.reshape(-1).view(np.uint8))
+    return np.frombuffer(data, dtype=np.uint8)
+
+
+def _strided_rows(vectors, dim: int):
+    """(array, row stride in floats) for fp32 rows that may sit further apart than dim floats, as
+    in a mapped vectors.bin viewed as np.memmap(path, np.float32).reshape(n, stride)[:, :dim]."""
+    if vectors is None:
+        return None, dim
+    a = np.asarray(vectors, dtype=np.float32)
+    if a.ndim != 2 or a.shape[1] != dim:
+        raise IllegalArgumentException(f"vectors must be [n][{dim}] float32 rows")
+    if a.strides[1] == 4 and a.strides[0] % 4 == 0 and a.strides[0] >= 4 * dim:
+        return a, a.strides[0] // 4
+    a = np.ascontiguousarray(a)
+    return a, dim
+
+
+def quantized_bin_info(data) -> tuple[int, int, int]:
+    """(QuantizerKind ordinal, dimension, vectorCount) of a quantized.bin, validated the way
+    QuantizedVectorsCodec.decode validates it (no GPU needed).  Raises IOException for malformed
+    bytes and UnsupportedOperationException for kinds this library does not serve."""
+    b = _file_bytes(data)
+    kind, dim, cnt = C.c_int32(), C.c_int32(), C.c_int64()
+    _check(N.lib().vx_quantized_bin_info(_ptr(b), b.size, C.byref(kind), C.byref(dim), C.byref(cnt)))
+    return kind.value, dim.value, cnt.value
+
+
+def ivf_graph_info(data) -> dict:
+    """Shape of an IVF_PQ graph.bin (IvfIndex.encode) validated as IvfIndex.decode reads it."""
+    b = _file_bytes(data)
+    nlist, dim, cnt, m, metric = C.c_int32(), C.c_int32(), C.c_int64(), C.c_int32(), C.c_int32()
+    _check(N.lib().vx_ivf_graph_info(_ptr(b), b.size, C.byref(nlist), C.byref(dim), C.byref(cnt), C.byref(m),
+                                     C.byref(metric)))
+    return {"nlist": nlist.value, "dim": dim.value, "count": cnt.value, "m": m.value,
+            "metric": SimilarityFunction(metric.value)}
 
 
 def _outcomes(ids: np.ndarray, scores: np.ndarray, counts: np.ndarray) -> list[SearchOutcome]:
@@ -306,6 +357,19 @@ class QuantizedFlatScanAdapter(IndexSpi):
         _check(N.lib().vx_fp16_build(self.device, ptr, n, dim, int(metric), _ptr(v), dim, C.byref(self._h.ptr)))
         self._n, self._dim, self.metric, self.kind = n, dim, SimilarityFunction(metric), "FP16"
 
+    def load_quantized_bin(self, data, metric, vectors=None):
+        """Opens a persistent quantized.bin (QuantizedVectorsCodec.decode) as this adapter's index:
+        SQ8, BQ SIGN_BIT or FP16.  ``vectors`` are the fp32 rows for the two-pass rescore (a mapped
+        vectors.bin view with its 64-byte row stride is taken as is)."""
+        b = _file_bytes(data)
+        kind, dim, n = quantized_bin_info(b)
+        v, stride = _strided_rows(vectors, dim)
+        self._h.close()
+        _check(N.lib().vx_quantized_bin_build(self.device, _ptr(b), b.size, int(metric), _ptr(v), stride,
+                                              C.byref(self._h.ptr)))
+        self._n, self._dim, self.metric = n, dim, SimilarityFunction(metric)
+        self.kind = {1: "SQ8", 4: "BQ", 8: "FP16"}[kind]
+
     def build(self, vectors, metric):
         raise UnsupportedOperationException("QuantizedFlatScanAdapter wraps an already-built flat index")
 
@@ -366,6 +430,21 @@ class IvfPqAdapter(IndexSpi):
         )
         self._n, self._dim, self.metric = n, dim, SimilarityFunction(metric)
         self._nlist = nlist
+
+    def load_graph_bin(self, data, metric=None, vectors=None):
+        """Opens an IVF_PQ generation's graph.bin (IvfIndex.decode, as
+        VectorCollectionImpl.openIvfPqAdapter does): centroids, partitions, PQ codebooks and codes.
+        ``metric`` None takes the routing metric recorded in the file; ``vectors`` (fp32 rows, e.g.
+        a mapped vectors.bin view) enable rescore_factor > 1."""
+        b = _file_bytes(data)
+        info = ivf_graph_info(b)
+        v, stride = _strided_rows(vectors, info["dim"])
+        self._h.close()
+        _check(N.lib().vx_ivf_graph_build(self.device, _ptr(b), b.size, -1 if metric is None else int(metric), _ptr(v),
+                                          stride, self.nprobe, self.rescore_factor, C.byref(self._h.ptr)))
+        self._n, self._dim = info["count"], info["dim"]
+        self.metric = info["metric"] if metric is None else SimilarityFunction(metric)
+        self._nlist = info["nlist"]
 
     def ivf_search(self, queries, k: int, nprobe: int, rescore_factor: int = 1, min_score: float = -3.4028235e38):
         q = self._queries(queries, k)
