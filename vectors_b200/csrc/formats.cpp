@@ -231,8 +231,9 @@ int parse_ivf(const uint8_t* bytes, int64_t len, IvfFile& f) {
     const int32_t size = c.i32();
     if (size < 0) return failf(VX_ERR_FORMAT, "graph.bin partition %d has negative size %d", p, size);
     if (c.remaining() / 4 < (uint64_t)size + 1) return underflow("partition ordinals");
-    f.ordinals.reserve(f.ordinals.size() + (size_t)size);
-    for (int32_t i = 0; i < size; i++) f.ordinals.push_back(c.i32());
+    const size_t at = f.ordinals.size();
+    f.ordinals.resize(at + (size_t)size);  // grows geometrically (an exact reserve per partition would not)
+    for (int32_t i = 0; i < size; i++) f.ordinals[at + (size_t)i] = c.i32();
     f.offsets[(size_t)p + 1] = f.offsets[(size_t)p] + size;
     const int32_t kd = c.i32();  // HARMONY key dimensions (0 = none): not used by pqSearch
     if (kd < 0 || c.remaining() / 4 < (uint64_t)kd) return underflow("partition key dimensions");
