@@ -244,6 +244,8 @@ def main():
     ap.add_argument("--nq", type=int, default=FLAT["nq"])
     ap.add_argument("--no-ivf", action="store_true")
     ap.add_argument("--no-quant", action="store_true", help="skip the SQ8, BQ and FP16 scan legs")
+    ap.add_argument("--no-ivfflat", action="store_true", help="skip the IVF-flat leg")
+    ap.add_argument("--ivfflat-n", type=int, default=IVFFLAT["n"])
     ap.add_argument("--sq8-n", type=int, default=SQ8["n"], help="smaller cases for profiling")
     ap.add_argument("--bq-n", type=int, default=BQ["n"])
     ap.add_argument("--fp16-n", type=int, default=FP16["n_per_gpu"], help="rows per GPU")
@@ -416,6 +418,10 @@ def main():
     if not args.no_ivf:
         ivf = run_ivf(args, rank, world, local, dev, barrier, max_over_ranks, hbm_peak, peak_kind)
 
+    ivfflat = None
+    if not args.no_ivf and not args.no_ivfflat:
+        ivfflat = run_ivfflat(args, rank, world, local, dev, barrier, max_over_ranks, peak_kind)
+
     # ---- SQ8 and BQ candidate scans (selectApproximateCandidates, k = 100)
     sq8 = bq = fp16 = None
     if not args.no_quant:
@@ -447,6 +453,7 @@ def main():
             "gpu_launches": launches,
             "clocks": clk,
             "ivf_pq": ivf,
+            "ivf_flat": ivfflat,
             "sq8": sq8,
             "bq": bq,
             "fp16": fp16,
@@ -579,6 +586,7 @@ def run_ivf(args, rank, world, local, dev, barrier, max_over_ranks, hbm_peak, pe
 
 
 SQ8 = dict(n=1_000_000, dim=768, comps=64, sigma=0.3, nq=10_000, k=100)
+IVFFLAT = dict(n=1_000_000, dim=768, comps=256, sigma=0.3, nq=10_000, k=10, nlist=1024, nprobe=32, train=200_000)
 BQ = dict(n=10_000_000, dim=1024, comps=256, sigma=0.5, nq=10_000, k=100)
 FP16 = dict(n_per_gpu=12_500_000, dim=768, comps=4096, sigma=0.3, nq=4096, k=100)
 
@@ -608,6 +616,79 @@ def _timed_scan(args, world, dev, barrier, max_over_ranks, step, slot):
     ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
     kms = max_over_ranks(prof[slot][0] / args.steps)
     return ms, kms, {kk: v[0] / args.steps for kk, v in prof.items() if v[1]}
+
+
+def run_ivfflat(args, rank, world, local, dev, barrier, max_over_ranks, peak_kind):
+    """IVF-flat (IvfIndex.search without PQ), 1M x 768 EUCLIDEAN, nlist 1024, nprobe 32, 10k
+    queries, top-10: routing, then the exact list scan in the reference's batched fp32 order
+    (CUDA cores: the scores must be the reference's to the bit).  The index is replicated and
+    the queries split across ranks, as for IVF-PQ."""
+    import torch
+
+    import vectors_b200 as vx
+    from vectors_b200.sharded import search_query_sharded
+
+    P = IVFFLAT
+    n, dim, nlist, nq, k = args.ivfflat_n, P["dim"], P["nlist"], P["nq"], P["k"]
+    cent_mix = centres(P["comps"], dim, SEED_C ^ 0x2E)
+    rows = torch.from_numpy(gen_rows(0, n, dim, cent_mix, P["sigma"], SEED_DB ^ 0x2E, False)).to(dev)
+    g = torch.Generator(device=dev)
+    g.manual_seed(7)
+    sample = rows[torch.randperm(n, generator=g, device=dev)[: P["train"]]]
+    cent = sample[:nlist].clone()
+    for _ in range(10):
+        a_ = nearest(sample, cent)
+        s_ = torch.zeros_like(cent).index_add_(0, a_, sample)
+        c_ = torch.bincount(a_, minlength=nlist)
+        cent = torch.where(c_.unsqueeze(1) > 0, s_ / c_.clamp_min(1).unsqueeze(1).float(), cent)
+    del sample
+    assign = nearest(rows, cent)
+    counts = torch.bincount(assign, minlength=nlist)
+    order = torch.argsort(assign, stable=True).to(torch.int32)
+    loff = torch.zeros(nlist + 1, dtype=torch.int64, device=dev)
+    loff[1:] = torch.cumsum(counts, 0)
+    a = vx.IvfFlatAdapter(nprobe=P["nprobe"], device=local)
+    a.build_prebuilt(cent.cpu().numpy(), loff.cpu().numpy(), order.cpu().numpy(), rows, vx.SimilarityFunction.EUCLIDEAN)
+    qh = gen_rows(0, nq, dim, cent_mix, P["sigma"], SEED_Q ^ 0x2E, False)
+    q = torch.from_numpy(qh).to(dev)
+    probed = torch.cdist(q, cent).topk(P["nprobe"], largest=False).indices
+    pair_rows = float(counts[probed].sum().item())
+
+    def step():
+        if world == 1:
+            return a.ivf_search_device(q, k, P["nprobe"])[0]
+        return search_query_sharded(lambda qs: a.ivf_search_device(qs, k, P["nprobe"]), q)[0]
+
+    ms, kms, br = _timed_scan(args, world, dev, barrier, max_over_ranks, step, "adc_scan")
+    ops = 2.0 * pair_rows * dim / world  # subtract + fused multiply-add per (query, row, dim)
+    achieved = ops / (kms / 1e3) / 1e12 if kms > 0 else None
+    peak = 148 * 128 * 1.965e9 / 1e12  # fp32 lanes x max SM clock, as instructions
+    cpu = None
+    if rank == 0 and not args.no_cpu:
+        from oracle import oracle as O
+
+        th = os.cpu_count() or 1
+        qs = qh[:64]
+        t = time.perf_counter()
+        O.ivfflat_search(cent.cpu().numpy(), loff.cpu().numpy(), order.cpu().numpy(), rows.cpu().numpy(), qs, 0, k,
+                         P["nprobe"], O.REFERENCE_HEAP, th)
+        dt = time.perf_counter() - t
+        cpu = {"value": len(qs) / dt, "unit": "queries/s", "cores": th, "kind": "port",
+               "sample": f"{len(qs)} queries over the same index ({dt:.1f} s)"}
+    a.close()
+    del rows
+    torch.cuda.empty_cache()
+    return {
+        "value": nq / (ms / 1e3), "unit": "queries/s", "ms_per_step": ms,
+        "config": {"workload": f"IVF-flat EUCLIDEAN n={n:,} dim={dim} nlist={nlist} nprobe={P['nprobe']} "
+                               f"queries={nq:,} k={k}", "train": "torch k-means (10 iters, 200k sample)"},
+        "roofline": {"bound": "fp32 CUDA cores (exact batched order)", "achieved": achieved, "peak": peak,
+                     "unit": "T fp32 ops/s", "frac": (achieved / peak) if achieved else None, "traffic": None,
+                     "kernel": "flat_list_kernel (IVF-flat list scan)", "per": "GPU",
+                     "peak_source": "nominal: 148 SMs x 128 fp32 lanes x 1.965 GHz",
+                     "pair_rows_per_step": pair_rows, "breakdown_ms_per_step": br},
+        "cpu_baseline": cpu,
+    }
 
 
 def run_sq8(args, rank, world, local, dev, barrier, max_over_ranks, tc_sustained, peak_kind):

@@ -65,7 +65,8 @@ typedef enum vx_index_kind {
   VX_KIND_FP16 = 1,  /* QuantizerKind.FP16 -> QuantizedFlatScanAdapter(Fp16QuantizedVectors) */
   VX_KIND_SQ8 = 2,   /* QuantizerKind.SQ8  -> QuantizedFlatScanAdapter(ScalarQuantizedVectors) */
   VX_KIND_BQ = 3,    /* QuantizerKind.BQ (SIGN_BIT) -> QuantizedFlatScanAdapter(BinaryQuantizedVectors) */
-  VX_KIND_IVFPQ = 4  /* IndexType.IVF_PQ -> IvfPqAdapter / IvfIndex.pqSearch                 */
+  VX_KIND_IVFPQ = 4, /* IndexType.IVF_PQ -> IvfPqAdapter / IvfIndex.pqSearch                 */
+  VX_KIND_IVFFLAT = 5 /* IndexType.IVF_FLAT -> IvfFlatAdapter / IvfIndex.search (no PQ)       */
 } vx_index_kind;
 
 typedef struct vx_index vx_index;
@@ -137,6 +138,15 @@ VX_API int vx_ivfpq_build(int32_t device, const float* centroids, int32_t nlist,
                    const int64_t* list_offsets, const int32_t* list_ordinals, int32_t m, int32_t ks,
                    const float* codebooks, const uint8_t* codes, int64_t n, int32_t metric,
                    const float* vectors, int32_t nprobe, int32_t rescore_factor, vx_index** out);
+/* IvfIndex without PQ (IndexType.IVF_FLAT: IvfFlatAdapter.java:30-150, IvfIndex.search
+ * :170-289): centroids and partitions as for vx_ivfpq_build, and the fp32 rows [n] row_stride
+ * floats apart (host or device; a mapped vectors.bin with alignUp(dim*4, 64)/4).
+ * vx_search_batch follows IvfFlatAdapter.search (searchListSize overrides nprobe,
+ * overQueryFactor > 1 widens the probes); vx_ivfpq_search* run IvfIndex.search's flat list scan
+ * (their rescore_factor is ignored: the scan is exact) for k <= 96. */
+VX_API int vx_ivfflat_build(int32_t device, const float* centroids, int32_t nlist, int32_t dim,
+                            const int64_t* list_offsets, const int32_t* list_ordinals, const float* vectors,
+                            int64_t n, int64_t row_stride, int32_t metric, int32_t nprobe, vx_index** out);
 /* ---- persistent files (host memory; the bytes are not retained) --------------------------
  * quantized.bin as written by QuantizedVectorsCodec.encode and read by .decode
  * (vectors-db/.../storage/QuantizedVectorsCodec.java:91-192): little-endian, header magic 'VQTZ'
@@ -151,19 +161,22 @@ VX_API int vx_quantized_bin_info(const uint8_t* bytes, int64_t len, int32_t* kin
                                  int64_t* count);
 VX_API int vx_quantized_bin_build(int32_t device, const uint8_t* bytes, int64_t len, int32_t metric,
                                   const float* vectors, int64_t row_stride, vx_index** out);
-/* graph.bin of an IVF_PQ generation: the bytes of IvfIndex.encode (vectors-ivf/.../IvfIndex.java:
- * 354-400; decode :408-442, PQ trailer :450-500) around BuoyIndex.encode (BuoyIndex.java:130-167),
- * big-endian as java.nio.ByteBuffer and java.io.DataOutputStream write them; read by
- * VectorCollectionImpl.openIvfPqAdapter (VectorCollectionImpl.java:703-718).  Builds the index
- * vx_ivfpq_build would from the centroids, partitions, codebooks and ordinal-ordered codes.
- * metric -1 takes the routing metric recorded in the file; another metric must equal it.
- * IVF-flat files (no PQ trailer) and PQ with a global centroid return VX_ERR_UNSUPPORTED;
- * HARMONY key dimensions are read and ignored (IvfIndex.pqSearch does not use them). */
+/* graph.bin of an IVF_PQ or IVF_FLAT generation: the bytes of IvfIndex.encode
+ * (vectors-ivf/.../IvfIndex.java:354-400; decode :408-442, PQ trailer :450-500) around
+ * BuoyIndex.encode (BuoyIndex.java:130-167), big-endian as java.nio.ByteBuffer and
+ * java.io.DataOutputStream write them; read by VectorCollectionImpl.openIvfFlatAdapter /
+ * openIvfPqAdapter (VectorCollectionImpl.java:684-718).  With a PQ trailer it builds the index
+ * vx_ivfpq_build would (vectors, optional, enable rescore_factor > 1 and must number the codes);
+ * without one, the index vx_ivfflat_build would from the caller's vectors (required, as
+ * IvfIndex.decode takes them).  metric -1 takes the routing metric recorded in the file; another
+ * metric must equal it.  PQ with a global centroid or non-standard subspaces returns
+ * VX_ERR_UNSUPPORTED; HARMONY key dimensions are read and not used.  vx_ivf_graph_info reports
+ * m = 0 and count = the partitioned rows for an IVF-flat file. */
 VX_API int vx_ivf_graph_info(const uint8_t* bytes, int64_t len, int32_t* nlist, int32_t* dim, int64_t* count,
                              int32_t* m, int32_t* metric);
 VX_API int vx_ivf_graph_build(int32_t device, const uint8_t* bytes, int64_t len, int32_t metric,
-                              const float* vectors, int64_t row_stride, int32_t nprobe, int32_t rescore_factor,
-                              vx_index** out);
+                              const float* vectors, int64_t vector_count, int64_t row_stride, int32_t nprobe,
+                              int32_t rescore_factor, vx_index** out);
 /* IndexSpi.size() and the index's shape. */
 VX_API int vx_index_info(const vx_index* index, int32_t* kind, int64_t* size, int32_t* dim,
                   int32_t* metric);

@@ -79,6 +79,7 @@ def lib() -> C.CDLL:
             "vo_quantized_two_pass_search": (None, [i32, p, p, f32, f32, p, i64, i32, i32, p, i32, i32, f32, i32, i32, p, p, p]),
             "vo_route": (None, [p, i32, i32, i32, p, i32, i32, i32, i32, p, p]),
             "vo_ivfpq_search": (None, [p, i32, i32, p, p, i32, i32, p, p, i64, i32, p, i32, i32, i32, i32, p, i32, i32, p, p, p]),
+            "vo_ivfflat_search": (None, [p, i32, i32, p, p, p, i64, i32, p, i32, i32, i32, i32, i32, p, p, p]),
             "vo_merge_shards": (None, [i32, p, p, p, p, i32, i32, i32, i32, p, p, p]),
             "vo_topk_select": (i32, [p, i32, i32, p]),
         }
@@ -330,6 +331,17 @@ def ivfpq_search(centroids, list_offsets, list_ordinals, m, ks, codebooks, codes
     lib().vo_ivfpq_search(P(c), c.shape[0], c.shape[1], P(off), P(ords), m, ks, P(f32(codebooks)), P(codes),
                           codes.shape[0], metric, P(q), q.shape[0], k, nprobe, rescore, P(v), policy,
                           nthreads or threads(), P(ids), P(sc), P(cnt))
+    return ids, sc, cnt
+
+
+def ivfflat_search(centroids, list_offsets, list_ordinals, vectors, queries, metric, k, nprobe, policy=CANONICAL,
+                   nthreads=None):
+    c, q, v = f32(centroids), f32(queries), f32(vectors)
+    off = np.ascontiguousarray(list_offsets, np.int64)
+    ords = np.ascontiguousarray(list_ordinals, np.int32)
+    ids, sc, cnt = _outs(q.shape[0], k)
+    lib().vo_ivfflat_search(P(c), c.shape[0], c.shape[1], P(off), P(ords), P(v), v.shape[0], metric, P(q), q.shape[0],
+                            k, nprobe, policy, nthreads or threads(), P(ids), P(sc), P(cnt))
     return ids, sc, cnt
 
 

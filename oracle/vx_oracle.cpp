@@ -1191,6 +1191,68 @@ void vo_ivfpq_search(const float* cent, int32_t nlist, int32_t dim, const int64_
     }
   });
 }
+// IvfIndex.search without PQ (IvfIndex.java:170-226): route, then every probed cluster's
+// ordinals in batches of BATCH_ROWS = 64 through batchSquaredL2 / batchDotProduct
+// (scanPartitionBulk, :244-277 -- matVecSquaredL2 / matVecDot over the batch: groups of four
+// rows on the 8-lane accumulators, the batch's last count % 4 rows through squareDistance /
+// dotProduct); score -d (EUCLIDEAN), dot (DOT_PRODUCT, MAXIMUM_INNER_PRODUCT) or
+// (float)(dot / sqrt((double)|q|^2 * (double)|v|^2)) with both norms from dotProduct (COSINE,
+// computeNormsSq :83-89); scores < minScore (-Float.MAX_VALUE) skipped; TopKHeap of k.
+// Not restated: the triangle-inequality early exit (:190-200) and the HARMONY key-dimension
+// path (:207-212, scanPartitionWithHarmony :279-289); both only skip clusters / rows that the
+// bound shows cannot enter the top k.
+void vo_ivfflat_search(const float* cent, int32_t nlist, int32_t dim, const int64_t* loff, const int32_t* lord,
+                       const float* vectors, int64_t n, int32_t metric, const float* queries, int32_t nq,
+                       int32_t k, int32_t nprobe, int32_t policy, int32_t nthreads, int32_t* ids, float* scores,
+                       int32_t* counts) {
+  (void)n;
+  int probes = std::min(nprobe, nlist);
+  std::vector<int32_t> lids((size_t)nq * probes);
+  std::vector<float> ld((size_t)nq * probes);
+  vo_route(cent, nlist, dim, metric, queries, nq, probes, policy, nthreads, lids.data(), ld.data());
+  const bool euclid = metric == VO_EUCLIDEAN, cosine = metric == VO_COSINE;
+  parallel_for(nq, nthreads, [&](int64_t lo, int64_t hi) {
+    std::vector<float> batch((size_t)64 * dim), out(64);
+    for (int64_t q = lo; q < hi; q++) {
+      const float* qq = queries + q * dim;
+      const float qn = cosine ? vo_dot(qq, qq, dim) : 0.0f;
+      RefHeap rh(k);
+      CanonTopK ch(k);
+      for (int p = 0; p < probes; p++) {
+        int cid = lids[(size_t)q * probes + p];
+        int64_t b = loff[cid], e = loff[cid + 1];
+        for (int64_t s0 = b; s0 < e; s0 += 64) {
+          const int cnt = (int)std::min<int64_t>(64, e - s0);
+          for (int j = 0; j < cnt; j++)
+            std::memcpy(&batch[(size_t)j * dim], vectors + (int64_t)lord[s0 + j] * dim, sizeof(float) * dim);
+          if (euclid) vo_mat_vec_square_l2(qq, batch.data(), cnt, dim, out.data());
+          else vo_mat_vec_dot(qq, batch.data(), cnt, dim, out.data());
+          for (int j = 0; j < cnt; j++) {
+            const int32_t o = lord[s0 + j];
+            float sc;
+            if (euclid) {
+              sc = -out[j];
+            } else if (cosine) {
+              const float* v = vectors + (int64_t)o * dim;
+              sc = (float)(out[j] / std::sqrt((double)qn * (double)vo_dot(v, v, dim)));
+            } else {
+              sc = out[j];
+            }
+            if (sc < -3.4028235e38f) continue;
+            if (policy == VO_POLICY_REFERENCE_HEAP) {
+              if (rh.size < rh.cap) rh.offer(o, sc);
+              else if (sc > rh.sc[0]) rh.offer(o, sc);
+            } else {
+              ch.offer(o, sc);
+            }
+          }
+        }
+      }
+      counts[q] = policy == VO_POLICY_REFERENCE_HEAP ? rh.drain(ids + q * k, scores + q * k)
+                                                     : ch.drain(ids + q * k, scores + q * k);
+    }
+  });
+}
 // IndexShards.mergeWithOffsets (IndexShards.java:168-211).
 void vo_merge_shards(int32_t ns, const int64_t* offsets, const int32_t* sids, const float* ssc,
                      const int32_t* scnt, int32_t kin, int32_t nq, int32_t k, int32_t policy,

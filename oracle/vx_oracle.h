@@ -142,7 +142,11 @@ void vo_ivfpq_search(const float* centroids, int32_t nlist, int32_t dim, const i
                      const int32_t* list_ordinals, int32_t m, int32_t ks, const float* codebooks,
                      const uint8_t* codes /* [n][m], ordinal order */, int64_t n, int32_t metric,
                      const float* queries, int32_t nq, int32_t k, int32_t nprobe,
-                     int32_t rescore_factor, const float* vectors /* for rescore; may be NULL */,
+                     int32_t rescore_factor, const float* vectors /* for rescore;
+void vo_ivfflat_search(const float* centroids, int32_t nlist, int32_t dim, const int64_t* list_offsets,
+                       const int32_t* list_ordinals, const float* vectors, int64_t n, int32_t metric,
+                       const float* queries, int32_t nq, int32_t k, int32_t nprobe, int32_t policy,
+                       int32_t nthreads, int32_t* ids, float* scores, int32_t* counts); may be NULL */,
                      int32_t policy, int32_t nthreads, int32_t* ids, float* scores,
                      int32_t* counts);
 /* IndexShards.mergeWithOffsets (IndexShards.java:168-211); policy 0 = reference partial

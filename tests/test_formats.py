@@ -121,12 +121,17 @@ def test_ivf_graph_rejections():
     for cut in (3, 40, len(good) // 2, len(good) - 1):
         with pytest.raises(vx.IOException, match="truncated"):
             vx.ivf_graph_info(good[:cut])
-    # IVF-flat (pqFlag 0, or the flag byte absent as in files older than IVF-PQ)
+    # IVF-flat (pqFlag 0, or the flag byte absent as in files older than IVF-PQ): m = 0
     flat = F.ivf_graph_bin(cent, off, ords, 0, pq=None)
-    with pytest.raises(vx.UnsupportedOperationException, match="IVF-flat"):
-        vx.ivf_graph_info(flat)
-    with pytest.raises(vx.UnsupportedOperationException, match="IVF-flat"):
-        vx.ivf_graph_info(flat[:-1])
+    assert vx.ivf_graph_info(flat) == {"nlist": 6, "dim": 32, "count": 200, "m": 0,
+                                       "metric": vx.SimilarityFunction.EUCLIDEAN}
+    assert vx.ivf_graph_info(flat[:-1])["m"] == 0
+    arr = np.frombuffer(flat, np.uint8)
+    out = C.c_void_p()
+    assert N.lib().vx_ivf_graph_build(0, arr.ctypes.data, arr.size, -1, None, 0, 0, 8, 1, C.byref(out)) == \
+        N.VX_ERR_NULL_POINTER  # IVF-flat needs the vectors
+    with pytest.raises(vx.NullPointerException):
+        vx.IvfFlatAdapter().load_graph_bin(flat)
     # an unknown flag byte is IvfIndex.decode's IllegalArgumentException
     at = len(flat) - 1
     with pytest.raises(vx.IllegalArgumentException, match="pqFlag"):
@@ -148,7 +153,7 @@ def test_ivf_graph_rejections():
         vx.ivf_graph_info(good[:at] + struct.pack(">i", 5) + good[at + 4:])
     out = C.c_void_p()
     arr = np.frombuffer(good[:40], np.uint8)
-    assert N.lib().vx_ivf_graph_build(0, arr.ctypes.data, arr.size, -1, None, 0, 8, 1, C.byref(out)) == N.VX_ERR_FORMAT
+    assert N.lib().vx_ivf_graph_build(0, arr.ctypes.data, arr.size, -1, None, 0, 0, 8, 1, C.byref(out)) == N.VX_ERR_FORMAT
 
 
 def test_strided_rows_view():

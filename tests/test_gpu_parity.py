@@ -297,6 +297,43 @@ def test_ivfpq_many_queries_per_list_bit_exact(oracle, metric):
         _check_float(got, ids, sc, cnt, f"ivfpq many rescore {rf} m={metric}")
 
 
+# ------------------------------------------------------------------ IVF-flat
+@pytest.mark.parametrize("metric", [0, 1, 2, 3])
+@pytest.mark.parametrize("dim,nq,k", [(128, 400, 10), (96, 50, 50), (100, 40, 10), (7, 30, 5)])
+def test_ivfflat_matches_oracle(oracle, metric, dim, nq, k):
+    # dims: whole 64-dim chunks, a zero-padded last chunk, 4 dims after the 8-lane part, no
+    # lane part at all; 400 queries x 8 probes over 16 lists puts several 64-query groups on
+    # each list; every list ends in a batch whose count % 4 rows take the scalar functions
+    n, nlist = 9000, 16
+    db = oracle.gen_mixture(n, dim, 12, 0.3, SEED_C, SEED_DB, metric == 2)
+    q = oracle.gen_mixture(nq, dim, 12, 0.3, SEED_C, SEED_Q, metric == 2)
+    cent = oracle.kmeans_train(db[:3000], nlist, 8, 42)
+    off, ords = oracle.build_ivf_lists(oracle.kmeans_assign(db, cent), nlist)
+    a = vx.IvfFlatAdapter(nprobe=8)
+    a.build_prebuilt(cent, off, ords, db, vx.SimilarityFunction(metric))
+    got = a.ivf_search(q, k, 8)
+    ids, sc, cnt = oracle.ivfflat_search(cent, off, ords, db, q, metric, k, 8)
+    for i, o in enumerate(got):
+        c = cnt[i]
+        assert list(o.ordinals) == list(ids[i, :c]), f"ivfflat m={metric} dim={dim} query {i}"
+        if metric == 2:
+            np.testing.assert_allclose(o.scores, sc[i, :c], rtol=1e-6, atol=0)
+        else:
+            assert np.array_equal(o.scores, sc[i, :c]), f"ivfflat m={metric} dim={dim} query {i} scores"
+    # IndexSpi.searchBatch: the adapter's nprobe, and overQueryFactor widening the probes
+    _same_outcomes(a.search_batch(q, k), got, "ivfflat searchBatch")
+    wide = oracle.ivfflat_search(cent, off, ords, db, q, metric, k, 12)
+    got2 = a.search_batch(q, k, over_query_factor=1.5)
+    for i, o in enumerate(got2):
+        assert list(o.ordinals) == list(wide[0][i, : wide[2][i]]), f"ivfflat oqf query {i}"
+    a.close()
+
+
+def _same_outcomes(x, y, tag):
+    for i, (u, v) in enumerate(zip(x, y)):
+        assert np.array_equal(u.ordinals, v.ordinals) and np.array_equal(u.scores, v.scores), f"{tag} query {i}"
+
+
 @pytest.mark.parametrize("metric", [0, 1, 2])
 @pytest.mark.parametrize("dim,nlist", [(64, 64), (96, 30)])
 def test_ivf_route_device_matches_oracle_and_routed_search(oracle, metric, dim, nlist):

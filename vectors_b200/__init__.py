@@ -11,6 +11,7 @@ from .index_spi import (  # noqa: F401
     IOException,
     IllegalArgumentException,
     IndexSpi,
+    IvfFlatAdapter,
     IvfPqAdapter,
     NullPointerException,
     QuantizedFlatScanAdapter,
@@ -27,6 +28,7 @@ __all__ = [
     "FlatScanAdapter",
     "QuantizedFlatScanAdapter",
     "IvfPqAdapter",
+    "IvfFlatAdapter",
     "IndexSpi",
     "SearchOutcome",
     "SimilarityFunction",

@@ -22,7 +22,7 @@ VX_ERR_UNSUPPORTED = 6
 VX_ERR_DEVICE_TIMEOUT = 7
 VX_ERR_FORMAT = 8
 
-VX_KIND_FLAT, VX_KIND_FP16, VX_KIND_SQ8, VX_KIND_BQ, VX_KIND_IVFPQ = range(5)
+VX_KIND_FLAT, VX_KIND_FP16, VX_KIND_SQ8, VX_KIND_BQ, VX_KIND_IVFPQ, VX_KIND_IVFFLAT = range(6)
 
 _P = C.c_void_p
 _I32 = C.c_int32
@@ -47,7 +47,8 @@ SIGNATURES = {
     "vx_quantized_bin_info": [_P, _I64, _P, _P, _P],
     "vx_quantized_bin_build": [_I32, _P, _I64, _I32, _P, _I64, _PP],
     "vx_ivf_graph_info": [_P, _I64, _P, _P, _P, _P, _P],
-    "vx_ivf_graph_build": [_I32, _P, _I64, _I32, _P, _I64, _I32, _I32, _PP],
+    "vx_ivf_graph_build": [_I32, _P, _I64, _I32, _P, _I64, _I64, _I32, _I32, _PP],
+    "vx_ivfflat_build": [_I32, _P, _I32, _I32, _P, _P, _P, _I64, _I64, _I32, _I32, _PP],
     "vx_index_info": [_P, _P, _P, _P, _P],
     "vx_index_free": [_P],
     "vx_search_batch": [_P, _P, _I32, _I32, _I32, _I32, _F32, _P, _P, _P],

@@ -283,7 +283,7 @@ int parse_ivf(const uint8_t* bytes, int64_t len, IvfFile& f) {
 }
 
 int unsupported_ivf(const IvfFile& f) {
-  if (!f.pq) return failf(VX_ERR_UNSUPPORTED, "graph.bin holds an IVF-flat index (no PQ trailer); IVF_PQ is served here");
+  if (!f.pq) return VX_OK;  // IVF-flat
   if (f.global_centroid) return failf(VX_ERR_UNSUPPORTED, "graph.bin PQ with a global centroid is not served here");
   if (!f.subspaces_standard)
     return failf(VX_ERR_UNSUPPORTED, "graph.bin PQ subspaces differ from computeSubspaceSizesAndOffsets");
@@ -361,15 +361,16 @@ int vx_ivf_graph_info(const uint8_t* bytes, int64_t len, int32_t* nlist, int32_t
     if (int s = parse_ivf(bytes, len, f)) return s;
     if (nlist) *nlist = f.nlist;
     if (dim) *dim = f.dim;
-    if (count) *count = f.count;
-    if (m) *m = f.m;
+    if (count) *count = f.pq ? (int64_t)f.count : (int64_t)f.ordinals.size();
+    if (m) *m = f.pq ? f.m : 0;
     if (metric) *metric = f.metric;
     return unsupported_ivf(f);
   });
 }
 
 int vx_ivf_graph_build(int32_t device, const uint8_t* bytes, int64_t len, int32_t metric, const float* vectors,
-                       int64_t row_stride, int32_t nprobe, int32_t rescore_factor, vx_index** out) {
+                       int64_t vector_count, int64_t row_stride, int32_t nprobe, int32_t rescore_factor,
+                       vx_index** out) {
   return guarded_parse([&]() -> int {
     if (!out) return failf(VX_ERR_NULL_POINTER, "out must not be null");
     *out = nullptr;
@@ -380,6 +381,14 @@ int vx_ivf_graph_build(int32_t device, const uint8_t* bytes, int64_t len, int32_
     if (metric != f.metric)
       return failf(VX_ERR_UNSUPPORTED, "graph.bin routes by %s; the index metric %d differs", kMetricNames[f.metric],
                    metric);
+    if (!f.pq) {  // IVF-flat: IvfIndex.decode scores the caller's vectors
+      if (!vectors) return failf(VX_ERR_NULL_POINTER, "an IVF-flat graph.bin needs the vectors");
+      return vx_ivfflat_build(device, f.centroids.data(), f.nlist, f.dim, f.offsets.data(),
+                              f.ordinals.empty() ? nullptr : f.ordinals.data(), vectors, vector_count, row_stride,
+                              metric, nprobe, out);
+    }
+    if (vectors && vector_count != f.count)
+      return failf(VX_ERR_INVALID_ARGUMENT, "%lld vectors for %d PQ codes", (long long)vector_count, f.count);
     return ivfpq_build_strided(device, f.centroids.data(), f.nlist, f.dim, f.offsets.data(),
                                f.ordinals.empty() ? nullptr : f.ordinals.data(), f.m, f.ks, f.codebooks.data(),
                                f.count ? f.codes : nullptr, f.count, metric, vectors,

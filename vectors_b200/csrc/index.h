@@ -47,6 +47,10 @@ struct vx_index {
   int64_t* cb_off = nullptr;
   int32_t* sub = nullptr;
   int nprobe = 1, rescore = 1;
+  // IVF-flat: list-ordered rows zero-padded to Dp floats, their dotProduct(v, v) (COSINE)
+  float* flat_rows = nullptr;
+  float* flat_norms = nullptr;
+  int Dp_flat = 0;
   std::vector<void*> owned;
   // exact-search view of a quantized index (built on first use)
   vx_index* flat = nullptr;

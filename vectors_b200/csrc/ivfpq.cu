@@ -18,6 +18,8 @@
 // 96 x 256 fp32 table in shared memory, then its 8 warps stream the list's codes (lane = row)
 // through table gathers into warp-owned candidate buffers; the CTA writes the pair's best
 // K keys and a final per-query merge combines the nprobe lists.
+#include <algorithm>
+
 #include "common.cuh"
 #include "exact.cuh"
 #include "ivfpq.h"
@@ -518,7 +520,7 @@ constexpr int kRowsPerThread = 12;
 constexpr int kRowsPerPass = kAdcThreads * kRowsPerThread;
 
 __global__ void make_groups_kernel(const int32_t* __restrict__ counts, const int32_t* __restrict__ offsets,
-                                   int nlist, int2* __restrict__ groups, int32_t* __restrict__ ngroups) {
+                                   int nlist, int wmax, int2* __restrict__ groups, int32_t* __restrict__ ngroups) {
   __shared__ uint32_t s_red[32];
   __shared__ int32_t s_carry;
   if (threadIdx.x == 0) s_carry = 0;
@@ -527,7 +529,7 @@ __global__ void make_groups_kernel(const int32_t* __restrict__ counts, const int
   for (int base = 0; base < nlist; base += blockDim.x) {
     const int l = base + threadIdx.x;
     const int c = l < nlist ? counts[l] : 0;
-    const int g = (c + kAdcGroupQ - 1) / kAdcGroupQ;
+    const int g = (c + wmax - 1) / wmax;
     int incl = g;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
@@ -542,8 +544,7 @@ __global__ void make_groups_kernel(const int32_t* __restrict__ counts, const int
       total += (int)s_red[i];
     }
     const int first = before + incl - g;
-    for (int j = 0; j < g; j++)
-      groups[first + j] = make_int2(offsets[l] + j * kAdcGroupQ, min(kAdcGroupQ, c - j * kAdcGroupQ));
+    for (int j = 0; j < g; j++) groups[first + j] = make_int2(offsets[l] + j * wmax, min(wmax, c - j * wmax));
     __syncthreads();
     if (threadIdx.x == 0) s_carry += total;
     __syncthreads();
@@ -744,6 +745,260 @@ __global__ void __launch_bounds__(kAdcThreads, 2) adc_group_kernel(AdcArgs a) {
   }
 }
 
+
+// ---------------------------------------------------------------------------------------
+// IVF-flat list scan: IvfIndex.search without PQ (IvfIndex.java:170-226) scores a probed
+// cluster's rows in batches of BATCH_ROWS = 64 through VectorUtil.batchSquaredL2 /
+// batchDotProduct (scanPartitionBulk, :244-277).  Inside a batch the rows in groups of four
+// take matVecSquaredL2 / matVecDot's arithmetic -- eight lane accumulators (lane j: dims j,
+// j + 8, ... below dim & ~7, subtract-then-FMA or FMA), summed as reduce_add8_local, then the
+// remaining dims folded in with FMA -- exactly route_tile_kernel's arithmetic; the batch's last
+// count % 4 rows go through squareDistance / dotProduct instead (flat_tail_kernel).  Score:
+// -d (EUCLIDEAN), dot (DOT_PRODUCT, MAXIMUM_INNER_PRODUCT) or
+// (float)(dot / sqrt((double)|q|^2 * (double)|v|^2)) (COSINE, norms by dotProduct).
+//
+// One CTA takes up to 64 (query, list) pairs of one list: 32-row tiles of the list against the
+// group's queries, dims staged 64 at a time (cp.async, double buffer, zero past dim & ~7);
+// per-query candidate buffers in shared memory, shrunk to K between tiles; a query's best K
+// over earlier lists (its floor) bounds admission, as in the ADC scan.
+// ---------------------------------------------------------------------------------------
+constexpr int kFlGroup = kRtQ;  // pairs per group (64)
+
+// Rows [n][dim] (stride src_stride, optionally gathered through map) -> [n][Dp], zero padded.
+__global__ void pad_rows_kernel(const float* __restrict__ src, int64_t n, int dim, int64_t src_stride,
+                                const int32_t* __restrict__ map, int Dp, float* __restrict__ dst) {
+  const int64_t total = n * (int64_t)Dp;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / Dp;
+    const int d = (int)(i - r * Dp);
+    const int64_t s = map ? (int64_t)map[r] : r;
+    dst[i] = d < dim ? src[s * src_stride + d] : 0.0f;
+  }
+}
+
+// dotProduct(v, v) (PanamaVectorUtilSupport.java:204-230) of every padded row; one warp a row.
+__global__ void row_norms_kernel(const float* __restrict__ rows, int64_t n, int dim, int Dp, float* __restrict__ out) {
+  const int lane = threadIdx.x & 31;
+  const int64_t w = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  if (w >= n) return;
+  const float* v = rows + w * Dp;
+  const float d = warp_dot(RowF32{v}, RowF32{v}, dim);
+  if (lane == 0) out[w] = d;
+}
+
+// The last batch's trailing count % 4 rows of every live pair's list, scored with
+// squareDistance / dotProduct (raw: distance or dot); one warp per (pair slot, row).
+template <bool kL2>
+__global__ void flat_tail_kernel(FlatListArgs a) {
+  const int lane = threadIdx.x & 31;
+  const int64_t w = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  const int64_t slot = w / 3;
+  const int t = (int)(w - slot * 3);
+  if (slot >= *a.pair_count) return;
+  const int32_t pair = a.pairs[slot];
+  const int q = pair / a.nprobe;
+  const int l = a.lists[pair];
+  const int64_t b = a.list_off[l];
+  const int n = (int)(a.list_off[l + 1] - b);
+  const int last = ((n - 1) / 64) * 64;
+  const int r = last + ((n - last) & ~3) + t;
+  if (r >= n) return;
+  const float* qv = a.queries + (size_t)q * a.Dp;
+  const float* x = a.rows + (size_t)(b + r) * a.Dp;
+  const float s = kL2 ? warp_sqdist(RowF32{qv}, RowF32{x}, a.dim) : warp_dot(RowF32{qv}, RowF32{x}, a.dim);
+  if (lane == 0) a.tail[slot * 3 + t] = s;
+}
+
+// Stages dims [k0, k0 + 64) of the group's queries and of rows r0 .. r0 + 31 of the list.
+__device__ __forceinline__ void flat_stage(float* s_q, float* s_c, const FlatListArgs& a, const int* s_query,
+                                           int npq, const float* rows, int r0, int n, int k0, int limit) {
+  for (int i = threadIdx.x; i < (kRtQ + kRtC) * (kRtK / 4); i += 256) {
+    const int r = i / (kRtK / 4), v = i % (kRtK / 4);
+    const int d = k0 + 4 * v;
+    if (r < kRtQ) {
+      const bool in = r < npq && d < limit;
+      cp_async16(s_q + r * kRtStride + 4 * v, a.queries + (in ? (size_t)s_query[r] * a.Dp + d : 0), in ? 16u : 0u);
+    } else {
+      const int rc = r - kRtQ;
+      const bool in = r0 + rc < n && d < limit;
+      cp_async16(s_c + rc * kRtStride + 4 * v, rows + (in ? (size_t)(r0 + rc) * a.Dp + d : 0), in ? 16u : 0u);
+    }
+  }
+  cp_async_commit();
+}
+
+template <bool kL2, int R>
+__global__ void __launch_bounds__(256, 2) flat_list_kernel(FlatListArgs a) {
+  extern __shared__ __align__(16) float s_flat[];
+  constexpr int kStage = (kRtQ + kRtC) * kRtStride;
+  constexpr int C = 32 * R;  // key slots per query; a tile adds at most 32
+  uint64_t* keys = reinterpret_cast<uint64_t*>(s_flat + 2 * kStage);  // [64][C]
+  __shared__ int s_query[kFlGroup], s_probe[kFlGroup], s_slot[kFlGroup];
+  __shared__ float s_qn[kFlGroup];
+  __shared__ uint64_t s_thr[kFlGroup];
+  __shared__ uint32_t s_cnt[kFlGroup];
+  const int tq = threadIdx.x >> 4, tc = threadIdx.x & 15;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const bool cosine = a.metric == kCosine;
+  const int ng = *a.ngroups;
+  const int limit = a.dim & ~7;
+  for (int gi = blockIdx.x; gi < ng; gi += gridDim.x) {
+    const int2 grp = a.groups[gi];
+    const int npq = grp.y;
+    __syncthreads();  // the previous group is done with every shared buffer
+    if (threadIdx.x < kFlGroup) {
+      const int g = threadIdx.x;
+      int q = 0, p = 0;
+      uint64_t f = 0;
+      if (g < npq) {
+        const int32_t pair = a.pairs[grp.x + g];
+        q = pair / a.nprobe;
+        p = pair - q * a.nprobe;
+        f = a.floor[q];
+      }
+      s_query[g] = q;
+      s_probe[g] = p;
+      s_slot[g] = grp.x + g;
+      s_qn[g] = (g < npq && cosine) ? a.qnorm[q] : 0.0f;
+      s_thr[g] = f > 0 ? f - 1 : 0ull;  // keys >= the query's floor stay admissible
+      s_cnt[g] = 0;
+    }
+    __syncthreads();
+    const int l = a.lists[(size_t)s_query[0] * a.nprobe + s_probe[0]];
+    const int64_t b = a.list_off[l];
+    const int n = (int)(a.list_off[l + 1] - b);
+    const int last = ((n - 1) / 64) * 64;
+    const int tail_begin = last + ((n - last) & ~3);
+    const float* rows = a.rows + (size_t)b * a.Dp;
+    for (int r0 = 0; r0 < n; r0 += kRtC) {
+      uint64_t acc[4][2][4];  // accumulator lanes (2p, 2p + 1) packed in acc[.][.][p]
+#pragma unroll
+      for (int u = 0; u < 4; u++)
+#pragma unroll
+        for (int v = 0; v < 2; v++)
+#pragma unroll
+          for (int p = 0; p < 4; p++) acc[u][v][p] = 0ull;
+      if (limit > 0) {
+        flat_stage(s_flat, s_flat + kRtQ * kRtStride, a, s_query, npq, rows, r0, n, 0, limit);
+        int buf = 0;
+        for (int k0 = 0; k0 < limit; k0 += kRtK) {
+          if (k0 + kRtK < limit) {
+            float* nb = s_flat + (buf ^ 1) * kStage;
+            flat_stage(nb, nb + kRtQ * kRtStride, a, s_query, npq, rows, r0, n, k0 + kRtK, limit);
+            cp_async_wait<1>();
+          } else {
+            cp_async_wait<0>();
+          }
+          __syncthreads();
+          const float* sq = s_flat + buf * kStage;
+          const float* sc = sq + kRtQ * kRtStride;
+#pragma unroll 4
+          for (int kk = 0; kk < kRtK; kk += 4) {
+            ulonglong2 qv[4], cv[2];
+#pragma unroll
+            for (int u = 0; u < 4; u++) qv[u] = *reinterpret_cast<const ulonglong2*>(sq + (tq + 16 * u) * kRtStride + kk);
+#pragma unroll
+            for (int v = 0; v < 2; v++) cv[v] = *reinterpret_cast<const ulonglong2*>(sc + (tc + 16 * v) * kRtStride + kk);
+            const int pb = (kk & 4) >> 1;
+#pragma unroll
+            for (int u = 0; u < 4; u++)
+#pragma unroll
+              for (int v = 0; v < 2; v++) {
+                if (kL2) {
+                  const uint64_t d0 = f2_sub(qv[u].x, cv[v].x), d1 = f2_sub(qv[u].y, cv[v].y);
+                  acc[u][v][pb] = f2_fma(d0, d0, acc[u][v][pb]);
+                  acc[u][v][pb + 1] = f2_fma(d1, d1, acc[u][v][pb + 1]);
+                } else {
+                  acc[u][v][pb] = f2_fma(qv[u].x, cv[v].x, acc[u][v][pb]);
+                  acc[u][v][pb + 1] = f2_fma(qv[u].y, cv[v].y, acc[u][v][pb + 1]);
+                }
+              }
+          }
+          __syncthreads();  // every warp is done with this buffer before it is refilled
+          buf ^= 1;
+        }
+      }
+      // this tile's keys into the per-query buffers
+#pragma unroll
+      for (int u = 0; u < 4; u++)
+#pragma unroll
+        for (int v = 0; v < 2; v++) {
+          const int g = tq + 16 * u, rr = r0 + tc + 16 * v;
+          if (g < npq && rr < n) {
+            float s;
+            if (rr >= tail_begin) {
+              s = a.tail[(size_t)s_slot[g] * 3 + (rr - tail_begin)];
+            } else {
+              float lanes[8];
+#pragma unroll
+              for (int p = 0; p < 4; p++) {
+                const float2 x = f2_unpack(acc[u][v][p]);
+                lanes[2 * p] = x.x;
+                lanes[2 * p + 1] = x.y;
+              }
+              s = reduce_add8_local(lanes);
+              const float* qv = a.queries + (size_t)s_query[g] * a.Dp;
+              const float* xv = rows + (size_t)rr * a.Dp;
+              for (int i = limit; i < a.dim; i++) {
+                if (kL2) {
+                  const float e = __fsub_rn(qv[i], xv[i]);
+                  s = __fmaf_rn(e, e, s);
+                } else {
+                  s = __fmaf_rn(qv[i], xv[i], s);
+                }
+              }
+            }
+            float score;
+            if (kL2) {
+              score = -s;
+            } else if (cosine) {
+              score = (float)((double)s / sqrt((double)s_qn[g] * (double)a.rnorm[b + rr]));
+            } else {
+              score = s;
+            }
+            const uint64_t key = float_key(score, (uint32_t)a.ordinals[b + rr]);
+            if (key > s_thr[g]) keys[(size_t)g * C + atomicAdd(&s_cnt[g], 1u)] = key;
+          }
+        }
+      __syncthreads();
+      // buffers that another tile could overflow shrink to their K best
+      for (int g = warp; g < npq; g += 8) {
+        const uint32_t c = s_cnt[g];
+        if (c > (uint32_t)(C - kRtC)) {
+          uint64_t t;
+          uint32_t nc;
+          warp_compact_one<R>(keys + (size_t)g * C, c, (uint32_t)a.K, t, nc);
+          if (lane == 0) {
+            s_thr[g] = t;
+            s_cnt[g] = nc;
+          }
+        }
+      }
+      __syncthreads();
+    }
+    // each query's K best of this list to its (probe, query) slot; its floor rises
+    for (int g = warp; g < npq; g += 8) {
+      uint32_t c = s_cnt[g];
+      uint64_t t = 0;
+      uint64_t* kb = keys + (size_t)g * C;
+      if (c > (uint32_t)a.K) {
+        warp_compact_one<R>(kb, c, (uint32_t)a.K, t, c);
+      } else if (c == (uint32_t)a.K) {
+        uint64_t mn = ~0ull;
+        for (uint32_t i = lane; i < c; i += 32) mn = kb[i] < mn ? kb[i] : mn;
+        t = warp_min_u64(mn);
+      }
+      const int q = s_query[g];
+      const size_t sidx = (size_t)s_probe[g] * a.nq + q;
+      for (uint32_t i = lane; i < c; i += 32) a.out[sidx * a.K + i] = kb[i];
+      if (lane == 0) {
+        a.out_cnt[sidx] = c;
+        if (c == (uint32_t)a.K) atomicMax((unsigned long long*)&a.floor[q], (unsigned long long)t);
+      }
+    }
+  }
+}
+
 }  // namespace
 
 // The tiled routing kernel is used where it applies unless VX_ROUTE_TILED=0.
@@ -861,9 +1116,46 @@ bool adc_group_supported(int M, int Ks, int dim) {
   return Ks == 256 && M > 0 && M % kMChunk == 0 && dim == 8 * M;
 }
 
-cudaError_t launch_make_groups(const int32_t* counts, const int32_t* offsets, int nlist, int2* groups,
+cudaError_t launch_make_groups(const int32_t* counts, const int32_t* offsets, int nlist, int wmax, int2* groups,
                                int32_t* ngroups, cudaStream_t st) {
-  make_groups_kernel<<<1, 1024, 0, st>>>(counts, offsets, nlist, groups, ngroups);
+  if (wmax < 1) return cudaErrorInvalidValue;
+  make_groups_kernel<<<1, 1024, 0, st>>>(counts, offsets, nlist, wmax, groups, ngroups);
+  return cudaGetLastError();
+}
+
+bool flat_list_supported(int K) { return K >= 1 && K <= 4 * 32 - kRtC; }
+
+cudaError_t launch_pad_rows(const float* src, int64_t n, int dim, int64_t src_stride, const int32_t* map, int Dp,
+                            float* dst, cudaStream_t st) {
+  if (n <= 0) return cudaSuccess;
+  const int64_t total = n * (int64_t)Dp;
+  const int grid = (int)std::min<int64_t>((total + 255) / 256, 148 * 32);
+  pad_rows_kernel<<<grid, 256, 0, st>>>(src, n, dim, src_stride, map, Dp, dst);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_row_norms(const float* rows, int64_t n, int dim, int Dp, float* out, cudaStream_t st) {
+  if (n <= 0) return cudaSuccess;
+  row_norms_kernel<<<(unsigned)((n * 32 + 255) / 256), 256, 0, st>>>(rows, n, dim, Dp, out);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_flat_list(const FlatListArgs& a, int64_t pair_slots, int grid, cudaStream_t st) {
+  if (pair_slots <= 0) return cudaSuccess;
+  const bool l2 = a.metric == kEuclidean;
+  const int64_t warps = pair_slots * 3;
+  const unsigned tgrid = (unsigned)((warps * 32 + 255) / 256);
+  if (l2) flat_tail_kernel<true><<<tgrid, 256, 0, st>>>(a);
+  else flat_tail_kernel<false><<<tgrid, 256, 0, st>>>(a);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  const int R = a.K <= 2 * 32 - kRtC ? 2 : 4;
+  const size_t smem = (size_t)2 * (kRtQ + kRtC) * kRtStride * sizeof(float) + (size_t)kFlGroup * 32 * R * 8;
+  auto kern = l2 ? (R == 2 ? flat_list_kernel<true, 2> : flat_list_kernel<true, 4>)
+                 : (R == 2 ? flat_list_kernel<false, 2> : flat_list_kernel<false, 4>);
+  e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  kern<<<grid, 256, smem, st>>>(a);
   return cudaGetLastError();
 }
 

@@ -46,8 +46,37 @@ cudaError_t launch_adc_scan(const AdcArgs& a, int R, int grid, cudaStream_t st);
 // pairs sharing a list are taken up to four at a time.
 constexpr int kAdcGroupQ = 4;
 bool adc_group_supported(int M, int Ks, int dim);
-cudaError_t launch_make_groups(const int32_t* counts, const int32_t* offsets, int nlist, int2* groups,
+// Groups of up to `wmax` consecutive pairs of one list: groups[i] = (first pair slot, pairs).
+cudaError_t launch_make_groups(const int32_t* counts, const int32_t* offsets, int nlist, int wmax, int2* groups,
                                int32_t* ngroups, cudaStream_t st);
 cudaError_t launch_adc_group(const AdcArgs& a, int R, int grid, cudaStream_t st);
+
+// IVF-flat list scan (IvfIndex.search without PQ): pairs grouped by list, up to 64 per group.
+struct FlatListArgs {
+  int nq, dim, Dp, nprobe, metric, K;
+  const int32_t* pairs;       // pair indices (q * nprobe + p), grouped by list
+  const int32_t* pair_count;  // device count of the grouped pairs
+  const int2* groups;         // (first pair slot, pairs) of up to 64 pairs sharing one list
+  const int32_t* ngroups;
+  const int32_t* lists;       // [nq][nprobe] routed list ids
+  const float* queries;       // [nq][Dp] zero-padded copy
+  const float* qnorm;         // [nq] dotProduct(q, q) (COSINE)
+  const int64_t* list_off;    // [nlist + 1]
+  const int32_t* ordinals;    // [n] ordinal of each list-ordered row
+  const float* rows;          // [n][Dp] list-ordered rows, zero-padded
+  const float* rnorm;         // [n] dotProduct(v, v) of the list-ordered rows (COSINE)
+  float* tail;                // [pairs][3] raw scores of each list's last-batch trailing rows
+  uint64_t* out;              // [nprobe][nq][K]
+  uint32_t* out_cnt;          // [nprobe][nq]
+  uint64_t* floor;            // [nq] per-query admission floor across lists (zeroed)
+};
+constexpr int kFlatGroup = 64;
+// Keys kept per (query, list) that the scan supports: K <= 96.
+bool flat_list_supported(int K);
+cudaError_t launch_pad_rows(const float* src, int64_t n, int dim, int64_t src_stride, const int32_t* map, int Dp,
+                            float* dst, cudaStream_t st);
+cudaError_t launch_row_norms(const float* rows, int64_t n, int dim, int Dp, float* out, cudaStream_t st);
+// flat_tail_kernel then flat_list_kernel (2 launches)
+cudaError_t launch_flat_list(const FlatListArgs& a, int64_t pair_slots, int grid, cudaStream_t st);
 
 }  // namespace vx

@@ -769,9 +769,98 @@ int search_quantized_scan(vx_index* ix, const float* dq, int nq, int K, int k_ou
 }
 
 // IVF-PQ: IvfIndex.pqSearch.
+// IVF-flat: IvfIndex.search without PQ (IvfIndex.java:170-226).  Routing as for IVF-PQ, then
+// the (query, list) pairs grouped by list (up to 64 per group) through the flat list scan, the
+// per-list best K merged per query.
+int search_ivfflat(vx_index* ix, const float* dq, int nq, int k, int nprobe, float min_score, int32_t* d_ids,
+                   float* d_scores, int32_t* d_counts, cudaStream_t st, const int32_t* given_lists) {
+  const int dim = ix->dim, Dp = ix->Dp_flat;
+  const int probes = std::min(nprobe, ix->nlist);
+  const int K = (int)std::max<int64_t>(1, std::min<int64_t>(k, ix->n));
+  if (!flat_list_supported(K)) return fail(VX_ERR_UNSUPPORTED, "k = %d is larger than the IVF-flat scan keeps (96)", K);
+  const size_t per_q = (size_t)ix->nlist * 4 + (size_t)Dp * 4 + (size_t)probes * (K * 8 + 8 + 12) + 64;
+  const int64_t qch = std::max<int64_t>(64, (int64_t)(scratch_budget() / per_q));
+  Scratch S(st);
+  int32_t* d_bad = S.alloc<int32_t>(1);
+  VX_CUDA(cudaMemsetAsync(d_bad, 0, 4, st));
+  for (int q0 = 0; q0 < nq; q0 += (int)qch) {
+    const int qc = (int)std::min<int64_t>(qch, nq - q0);
+    Scratch T(st);
+    const float* dqc = dq + (size_t)q0 * dim;
+    float* qn = T.alloc<float>((size_t)qc * dim);
+    float* dist = T.alloc<float>((size_t)qc * ix->nlist);
+    int32_t* lists = T.alloc<int32_t>((size_t)qc * probes);
+    int32_t* counts = T.alloc<int32_t>(ix->nlist);
+    int32_t* offsets = T.alloc<int32_t>(ix->nlist + 1);
+    int32_t* cursor = T.alloc<int32_t>(ix->nlist);
+    int32_t* pairs = T.alloc<int32_t>((size_t)qc * probes);
+    float* qpad = T.alloc<float>((size_t)qc * Dp);
+    float* qnorm = T.alloc<float>(qc);
+    float* tail = T.alloc<float>((size_t)qc * probes * 3);
+    uint64_t* out = T.alloc<uint64_t>((size_t)probes * qc * K);
+    uint32_t* out_cnt = T.alloc<uint32_t>((size_t)probes * qc);
+    uint64_t* keys = T.alloc<uint64_t>((size_t)qc * K);
+    uint32_t* kcnt = T.alloc<uint32_t>(qc);
+    const int64_t maxg = (int64_t)qc * probes / kFlatGroup + ix->nlist + 1;
+    int2* groups = T.alloc<int2>((size_t)maxg);
+    int32_t* ngroups = T.alloc<int32_t>(1);
+    uint64_t* qfloor = T.alloc<uint64_t>(qc);
+    if (given_lists) {
+      VX_LAUNCH(1, launch_copy_lists(given_lists + (size_t)q0 * probes, qc * probes, ix->nlist, lists, d_bad, st));
+    } else {
+      VX_TIMED(VX_PROF_ROUTE, st, route_launches(dqc, dim, ix->cent, ix->nlist, ix->metric),
+               launch_route(dqc, qc, dim, ix->cent, ix->nlist, ix->metric, probes, qn, dist, lists, st));
+    }
+    VX_LAUNCH(1, launch_pad_rows(dqc, qc, dim, dim, nullptr, Dp, qpad, st));
+    if (ix->metric == VX_COSINE) VX_LAUNCH(1, launch_row_norms(qpad, qc, dim, Dp, qnorm, st));
+    VX_LAUNCH(3, launch_group_pairs(lists, ix->list_off, qc * probes, ix->nlist, counts, offsets, cursor, pairs, st));
+    VX_CUDA(cudaMemsetAsync(out_cnt, 0, (size_t)probes * qc * 4, st));
+    VX_CUDA(cudaMemsetAsync(qfloor, 0, (size_t)qc * 8, st));
+    VX_LAUNCH(1, launch_make_groups(counts, offsets, ix->nlist, kFlatGroup, groups, ngroups, st));
+    FlatListArgs a{};
+    a.nq = qc;
+    a.dim = dim;
+    a.Dp = Dp;
+    a.nprobe = probes;
+    a.metric = ix->metric;
+    a.K = K;
+    a.pairs = pairs;
+    a.pair_count = offsets + ix->nlist;
+    a.groups = groups;
+    a.ngroups = ngroups;
+    a.lists = lists;
+    a.queries = qpad;
+    a.qnorm = qnorm;
+    a.list_off = ix->list_off;
+    a.ordinals = ix->ordinals;
+    a.rows = ix->flat_rows;
+    a.rnorm = ix->flat_norms;
+    a.tail = tail;
+    a.out = out;
+    a.out_cnt = out_cnt;
+    a.floor = qfloor;
+    VX_TIMED(VX_PROF_ADC_SCAN, st, 2, launch_flat_list(a, (int64_t)qc * probes, ix->num_sms * 2, st));
+    VX_TIMED(VX_PROF_MERGE, st, 1, launch_merge_streams(out, out_cnt, probes, qc, qc, K, K, keys, kcnt, st));
+    int32_t* oi = d_ids + (size_t)q0 * k;
+    float* os = d_scores + (size_t)q0 * k;
+    int32_t* oc = d_counts + q0;
+    VX_LAUNCH(1, launch_finish_keys(keys, kcnt, qc, K, k, kFinishFloatKey, ix->metric, dim, oi, os, oc, st));
+    VX_LAUNCH(1, launch_min_score(os, qc, k, min_score, oc, st));
+  }
+  if (given_lists) {
+    int32_t h_bad = 0;
+    VX_CUDA(cudaMemcpyAsync(&h_bad, d_bad, 4, cudaMemcpyDeviceToHost, st));
+    VX_CUDA(cudaStreamSynchronize(st));
+    if (h_bad) return fail(VX_ERR_INVALID_ARGUMENT, "%d routed list ids are outside [-1, nlist)", h_bad);
+  }
+  return VX_OK;
+}
+
 int search_ivfpq(vx_index* ix, const float* dq, int nq, int k, int nprobe, int rescore,
                  float min_score, int32_t* d_ids, float* d_scores, int32_t* d_counts,
                  cudaStream_t st, const int32_t* given_lists = nullptr) {
+  if (ix->kind == VX_KIND_IVFFLAT)  // IvfIndex.search takes the flat scan when there is no PQ
+    return search_ivfflat(ix, dq, nq, k, nprobe, min_score, d_ids, d_scores, d_counts, st, given_lists);
   const int dim = ix->dim;
   const int probes = std::min(nprobe, ix->nlist);
   int64_t wide = std::min<int64_t>((int64_t)k * rescore, ix->n);
@@ -845,7 +934,7 @@ int search_ivfpq(vx_index* ix, const float* dq, int nq, int k, int nprobe, int r
       int32_t* ngroups = T.alloc<int32_t>(1);
       uint64_t* qfloor = T.alloc<uint64_t>(qc);
       VX_CUDA(cudaMemsetAsync(qfloor, 0, (size_t)qc * 8, st));
-      VX_LAUNCH(1, launch_make_groups(counts, offsets, ix->nlist, groups, ngroups, st));
+      VX_LAUNCH(1, launch_make_groups(counts, offsets, ix->nlist, kAdcGroupQ, groups, ngroups, st));
       a.groups = groups;
       a.ngroups = ngroups;
       a.floor = qfloor;
@@ -1052,6 +1141,14 @@ int search_batch_dev(vx_index* ix, const float* dq, int nq, int dim, int k, int 
       const int rf = two ? std::max(ix->rescore, (int)std::ceil((double)((float)ix->rescore * oqf)))
                          : ix->rescore;
       return search_ivfpq(ix, dq, nq, k, probes, rf, -3.4028235e38f, d_ids, d_scores, d_counts, st);
+    }
+    case VX_KIND_IVFFLAT: {
+      // IvfFlatAdapter.search (IvfFlatAdapter.java:102-140): the candidateK = ceil(k * oqf)
+      // hits trimmed to k are the k best of the widened probe set
+      const int eff = sls > 0 ? sls : ix->nprobe;
+      const int probes = oqf > 1.0f ? (int)std::min<int64_t>((int64_t)std::ceil((double)((float)eff * oqf)), ix->nlist)
+                                    : std::min(eff, ix->nlist);
+      return search_ivfflat(ix, dq, nq, k, probes, -3.4028235e38f, d_ids, d_scores, d_counts, st, nullptr);
     }
     default:
       return fail(VX_ERR_INVALID_ARGUMENT, "unknown index kind");
@@ -1438,6 +1535,72 @@ int ivfpq_build_strided(int32_t device, const float* centroids, int32_t nlist, i
 
 extern "C" {
 
+int vx_ivfflat_build(int32_t device, const float* centroids, int32_t nlist, int32_t dim, const int64_t* list_offsets,
+                     const int32_t* list_ordinals, const float* vectors, int64_t n, int64_t row_stride, int32_t metric,
+                     int32_t nprobe, vx_index** out) {
+  return guarded([&]() -> int {
+    if (!out) return fail(VX_ERR_NULL_POINTER, "out must not be null");
+    *out = nullptr;
+    if (!centroids || !list_offsets) return fail(VX_ERR_NULL_POINTER, "null IVF component");
+    if (n > 0 && (!list_ordinals || !vectors)) return fail(VX_ERR_NULL_POINTER, "null IVF component");
+    if (nlist <= 0 || dim <= 0 || n < 0 || n > INT32_MAX)
+      return fail(VX_ERR_INVALID_ARGUMENT, "bad IVF shape nlist=%d dim=%d n=%lld", nlist, dim, (long long)n);
+    if (vectors && row_stride < dim)
+      return fail(VX_ERR_INVALID_ARGUMENT, "row_stride %lld < dimension %d", (long long)row_stride, dim);
+    if (nprobe <= 0) return fail(VX_ERR_INVALID_ARGUMENT, "nprobe must be positive: %d", nprobe);
+    if (int s = check_metric(metric)) return s;
+    const int64_t nl = list_offsets[nlist];
+    if (list_offsets[0] != 0 || nl < 0 || nl > n)
+      return fail(VX_ERR_INVALID_ARGUMENT, "list offsets must run from 0 to at most n");
+    for (int l = 0; l < nlist; l++)
+      if (list_offsets[l + 1] < list_offsets[l]) return fail(VX_ERR_INVALID_ARGUMENT, "list offsets must be non-decreasing");
+    for (int64_t i = 0; i < nl; i++)
+      if (list_ordinals[i] < 0 || list_ordinals[i] >= n)
+        return fail(VX_ERR_INVALID_ARGUMENT, "list ordinal %d out of range", list_ordinals[i]);
+    int nsms = 0;
+    if (int s = check_device(device, &nsms)) return s;
+    vx_index* ix = new vx_index();
+    ix->kind = VX_KIND_IVFFLAT;
+    ix->device = device;
+    ix->metric = metric;
+    ix->n = n;
+    ix->dim = dim;
+    ix->num_sms = nsms;
+    ix->nlist = nlist;
+    ix->nprobe = nprobe;
+    ix->Dp_flat = (int)round_up(dim, 4);
+    try {
+      ix->cent = dev_alloc<float>(ix, (size_t)nlist * dim);
+      VX_CUDA(cudaMemcpy(ix->cent, centroids, (size_t)nlist * dim * 4, cudaMemcpyDefault));
+      ix->list_off = dev_alloc<int64_t>(ix, (size_t)nlist + 1);
+      VX_CUDA(cudaMemcpy(ix->list_off, list_offsets, (size_t)(nlist + 1) * 8, cudaMemcpyDefault));
+      ix->ordinals = dev_alloc<int32_t>(ix, (size_t)std::max<int64_t>(nl, 1));
+      ix->flat_rows = dev_alloc<float>(ix, (size_t)std::max<int64_t>(nl, 1) * ix->Dp_flat);
+      if (metric == VX_COSINE) ix->flat_norms = dev_alloc<float>(ix, (size_t)std::max<int64_t>(nl, 1));
+      if (nl > 0) {
+        VX_CUDA(cudaMemcpy(ix->ordinals, list_ordinals, (size_t)nl * 4, cudaMemcpyDefault));
+        // the rows as dense [n][dim] on the device, then gathered into list order, padded
+        float* dense = nullptr;
+        VX_CUDA(cudaMalloc(&dense, (size_t)n * dim * 4));
+        cudaError_t e = cudaMemcpy2D(dense, (size_t)dim * 4, vectors, (size_t)row_stride * 4, (size_t)dim * 4,
+                                     (size_t)n, cudaMemcpyDefault);
+        if (e == cudaSuccess) e = launch_pad_rows(dense, nl, dim, dim, ix->ordinals, ix->Dp_flat, ix->flat_rows, 0);
+        if (e == cudaSuccess) e = cudaDeviceSynchronize();
+        cudaFree(dense);
+        VX_CUDA(e);
+        g_launches.fetch_add(1);
+        if (ix->flat_norms) VX_LAUNCH(1, launch_row_norms(ix->flat_rows, nl, dim, ix->Dp_flat, ix->flat_norms, 0));
+        VX_CUDA(cudaDeviceSynchronize());
+      }
+    } catch (...) {
+      free_index(ix);
+      throw;
+    }
+    *out = ix;
+    return VX_OK;
+  });
+}
+
 int vx_index_info(const vx_index* ix, int32_t* kind, int64_t* size, int32_t* dim, int32_t* metric) {
   if (!ix) return fail(VX_ERR_NULL_POINTER, "index must not be null");
   if (kind) *kind = ix->kind;
@@ -1529,7 +1692,7 @@ int vx_scan_candidates(vx_index* ix, const float* queries, int32_t nq, int32_t d
 
 static int ivfpq_dev(vx_index* ix, const float* dq, int nq, int k, int nprobe, int rf, float min_score,
                      int32_t* di, float* ds, int32_t* dc, cudaStream_t st) {
-  if (ix->kind != VX_KIND_IVFPQ) return fail(VX_ERR_UNSUPPORTED, "not an IVF-PQ index");
+  if (ix->kind != VX_KIND_IVFPQ && ix->kind != VX_KIND_IVFFLAT) return fail(VX_ERR_UNSUPPORTED, "not an IVF index");
   if (nprobe < 1) return fail(VX_ERR_INVALID_ARGUMENT, "nprobe must be >= 1, got %d", nprobe);
   if (rf < 1) return fail(VX_ERR_INVALID_ARGUMENT, "rescoreFactor must be >= 1, got %d", rf);
   if (ix->n == 0) {
@@ -1555,7 +1718,7 @@ int vx_ivf_route_device(vx_index* ix, const float* d_queries, int32_t nq, int32_
   return guarded([&]() -> int {
     if (!ix) return fail(VX_ERR_NULL_POINTER, "index must not be null");
     if (!d_queries || !d_lists) return fail(VX_ERR_NULL_POINTER, "null buffer");
-    if (ix->kind != VX_KIND_IVFPQ) return fail(VX_ERR_UNSUPPORTED, "not an IVF-PQ index");
+    if (ix->kind != VX_KIND_IVFPQ && ix->kind != VX_KIND_IVFFLAT) return fail(VX_ERR_UNSUPPORTED, "not an IVF index");
     if (nq <= 0) return fail(VX_ERR_INVALID_ARGUMENT, "queries must not be empty");
     if (dim != ix->dim)
       return fail(VX_ERR_INVALID_ARGUMENT, "Query dimension %d does not match index dimension %d", dim, ix->dim);
@@ -1571,7 +1734,7 @@ int vx_ivfpq_search_routed_device(vx_index* ix, const float* d_queries, int32_t 
   return guarded([&]() -> int {
     if (int s = validate_search(ix, d_queries, nq, dim, k, d_ids, d_scores, d_counts)) return s;
     if (!d_lists) return fail(VX_ERR_NULL_POINTER, "lists must not be null");
-    if (ix->kind != VX_KIND_IVFPQ) return fail(VX_ERR_UNSUPPORTED, "not an IVF-PQ index");
+    if (ix->kind != VX_KIND_IVFPQ && ix->kind != VX_KIND_IVFFLAT) return fail(VX_ERR_UNSUPPORTED, "not an IVF index");
     if (nprobe < 1) return fail(VX_ERR_INVALID_ARGUMENT, "nprobe must be >= 1, got %d", nprobe);
     if (rf < 1) return fail(VX_ERR_INVALID_ARGUMENT, "rescoreFactor must be >= 1, got %d", rf);
     VX_CUDA(cudaSetDevice(ix->device));

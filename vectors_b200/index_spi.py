@@ -441,8 +441,9 @@ class IvfPqAdapter(IndexSpi):
         v, stride = _strided_rows(vectors, info["dim"])
         self._h.close()
         _check(N.lib().vx_ivf_graph_build(self.device, _ptr(b), b.size, -1 if metric is None else int(metric), _ptr(v),
-                                          stride, self.nprobe, self.rescore_factor, C.byref(self._h.ptr)))
-        self._n, self._dim = info["count"], info["dim"]
+                                          0 if v is None else v.shape[0], stride, self.nprobe, self.rescore_factor,
+                                          C.byref(self._h.ptr)))
+        self._n, self._dim = (info["count"] if v is None or info["m"] else v.shape[0]), info["dim"]
         self.metric = info["metric"] if metric is None else SimilarityFunction(metric)
         self._nlist = info["nlist"]
 
@@ -509,6 +510,43 @@ class IvfPqAdapter(IndexSpi):
                                                   C.c_void_p(cnt.data_ptr()), C.c_void_p(st))
         )
         return ids, sc, cnt
+
+
+class IvfFlatAdapter(IvfPqAdapter):
+    """IvfFlatAdapter over a prebuilt IVF index without PQ (IvfIndex.fromPrebuilt /
+    IvfIndex.decode, IvfIndex.java:330-351,408-442).  ``search_batch`` follows
+    IvfFlatAdapter.search (IvfFlatAdapter.java:102-140); ``ivf_search`` is IvfIndex.search's flat
+    list scan (IvfIndex.java:170-289); the routing helpers are those of the IVF-PQ adapter."""
+
+    def __init__(self, nprobe: int = 32, device: int = 0):
+        super().__init__(nprobe=nprobe, rescore_factor=1, device=device)
+
+    def build_prebuilt(self, centroids, list_offsets, list_ordinals, vectors, metric):
+        cent = _as_matrix(centroids, "centroids")
+        off = np.ascontiguousarray(np.asarray(list_offsets, dtype=np.int64))
+        ords = np.ascontiguousarray(np.asarray(list_ordinals, dtype=np.int32))
+        nlist, dim = cent.shape
+        if getattr(vectors, "is_cuda", False):
+            t = vectors
+            if t.dtype != __import__("torch").float32 or t.dim() != 2 or t.stride(1) != 1:
+                raise IllegalArgumentException("vectors must be [n][dim] float32 rows")
+            n, ptr, stride = t.shape[0], C.c_void_p(t.data_ptr()), t.stride(0)
+        else:
+            v, stride = _strided_rows(vectors, dim)
+            n, ptr = v.shape[0], _ptr(v)
+        self._h.close()
+        _check(N.lib().vx_ivfflat_build(self.device, _ptr(cent), nlist, dim, _ptr(off), _ptr(ords), ptr, n, stride,
+                                        int(metric), self.nprobe, C.byref(self._h.ptr)))
+        self._n, self._dim, self.metric = n, dim, SimilarityFunction(metric)
+        self._nlist = nlist
+
+    def load_graph_bin(self, data, metric=None, vectors=None):
+        """Opens an IVF_FLAT generation's graph.bin (VectorCollectionImpl.openIvfFlatAdapter):
+        centroids and partitions from the file, rows from ``vectors`` (required; e.g. a mapped
+        vectors.bin view)."""
+        if vectors is None:
+            raise NullPointerException("an IVF-flat graph.bin needs the vectors")
+        super().load_graph_bin(data, metric=metric, vectors=vectors)
 
 
 def shard_offsets(n: int, shards: int) -> list[int]:
