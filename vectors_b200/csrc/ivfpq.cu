@@ -519,16 +519,19 @@ constexpr int kMChunk = 16;  // subspaces per table chunk
 constexpr int kRowsPerThread = 12;
 constexpr int kRowsPerPass = kAdcThreads * kRowsPerThread;
 
+// Lists in `order` (null: by id), each cut into groups of up to wmax consecutive pairs.
 __global__ void make_groups_kernel(const int32_t* __restrict__ counts, const int32_t* __restrict__ offsets,
-                                   int nlist, int wmax, int2* __restrict__ groups, int32_t* __restrict__ ngroups) {
+                                   const int32_t* __restrict__ order, int nlist, int wmax, int2* __restrict__ groups,
+                                   int32_t* __restrict__ ngroups) {
   __shared__ uint32_t s_red[32];
   __shared__ int32_t s_carry;
   if (threadIdx.x == 0) s_carry = 0;
   __syncthreads();
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
   for (int base = 0; base < nlist; base += blockDim.x) {
-    const int l = base + threadIdx.x;
-    const int c = l < nlist ? counts[l] : 0;
+    const int i = base + threadIdx.x;
+    const int l = i < nlist ? (order ? order[i] : i) : 0;
+    const int c = i < nlist ? counts[l] : 0;
     const int g = (c + wmax - 1) / wmax;
     int incl = g;
 #pragma unroll
@@ -592,12 +595,17 @@ __global__ void __launch_bounds__(kAdcThreads, 2) adc_group_kernel(AdcArgs a) {
   __shared__ int s_q[kAdcGroupQ], s_p[kAdcGroupQ];
   __shared__ float s_base[kAdcGroupQ];
   __shared__ uint64_t s_floor[kAdcGroupQ];
-  const int ng = *a.ngroups;
+  __shared__ int s_gi;
+  const int ng = a.ngroups[0];
   const int nchunks = a.M / kMChunk;
-  for (int gi = blockIdx.x; gi < ng; gi += gridDim.x) {
+  for (;;) {
+    __syncthreads();  // the previous group is finished with every shared buffer (and s_gi)
+    if (threadIdx.x == 0) s_gi = atomicAdd(a.ngroups + 1, 1);  // longest lists first
+    __syncthreads();
+    const int gi = s_gi;
+    if (gi >= ng) break;
     const int2 grp = a.groups[gi];
     const int npq = grp.y;  // pairs in this group (1..4)
-    __syncthreads();        // the previous group is finished with every shared buffer
     if (threadIdx.x < kAdcGroupQ) {
       const int g = threadIdx.x;
       int q = -1, p = 0;
@@ -840,12 +848,17 @@ __global__ void __launch_bounds__(256, 2) flat_list_kernel(FlatListArgs a) {
   const int tq = threadIdx.x >> 4, tc = threadIdx.x & 15;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const bool cosine = a.metric == kCosine;
-  const int ng = *a.ngroups;
+  __shared__ int s_gi;
+  const int ng = a.ngroups[0];
   const int limit = a.dim & ~7;
-  for (int gi = blockIdx.x; gi < ng; gi += gridDim.x) {
+  for (;;) {
+    __syncthreads();  // the previous group is done with every shared buffer (and s_gi)
+    if (threadIdx.x == 0) s_gi = atomicAdd(a.ngroups + 1, 1);  // longest lists first
+    __syncthreads();
+    const int gi = s_gi;
+    if (gi >= ng) break;
     const int2 grp = a.groups[gi];
     const int npq = grp.y;
-    __syncthreads();  // the previous group is done with every shared buffer
     if (threadIdx.x < kFlGroup) {
       const int g = threadIdx.x;
       int q = 0, p = 0;
@@ -1116,10 +1129,13 @@ bool adc_group_supported(int M, int Ks, int dim) {
   return Ks == 256 && M > 0 && M % kMChunk == 0 && dim == 8 * M;
 }
 
-cudaError_t launch_make_groups(const int32_t* counts, const int32_t* offsets, int nlist, int wmax, int2* groups,
-                               int32_t* ngroups, cudaStream_t st) {
+cudaError_t launch_make_groups(const int32_t* counts, const int32_t* offsets, const int32_t* order, int nlist,
+                               int wmax, int2* groups, int32_t* ngroups, cudaStream_t st) {
   if (wmax < 1) return cudaErrorInvalidValue;
-  make_groups_kernel<<<1, 1024, 0, st>>>(counts, offsets, nlist, wmax, groups, ngroups);
+  // ngroups[1] is the dispenser the scan kernels take groups from
+  cudaError_t e = cudaMemsetAsync(ngroups + 1, 0, sizeof(int32_t), st);
+  if (e != cudaSuccess) return e;
+  make_groups_kernel<<<1, 1024, 0, st>>>(counts, offsets, order, nlist, wmax, groups, ngroups);
   return cudaGetLastError();
 }
 

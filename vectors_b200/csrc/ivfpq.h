@@ -25,7 +25,7 @@ struct AdcArgs {
   uint32_t* out_cnt;             // [nprobe][nq]
   // grouped scan only (adc_group_kernel)
   const int2* groups;            // (first pair slot, pairs) of up to 4 pairs sharing one list
-  const int32_t* ngroups;        // device count of groups
+  int32_t* ngroups;              // [0] device count of groups, [1] the group dispenser
   uint64_t* floor;               // [nq] per-query admission floor shared across lists (zeroed)
 };
 
@@ -46,9 +46,11 @@ cudaError_t launch_adc_scan(const AdcArgs& a, int R, int grid, cudaStream_t st);
 // pairs sharing a list are taken up to four at a time.
 constexpr int kAdcGroupQ = 4;
 bool adc_group_supported(int M, int Ks, int dim);
-// Groups of up to `wmax` consecutive pairs of one list: groups[i] = (first pair slot, pairs).
-cudaError_t launch_make_groups(const int32_t* counts, const int32_t* offsets, int nlist, int wmax, int2* groups,
-                               int32_t* ngroups, cudaStream_t st);
+// Groups of up to `wmax` consecutive pairs of one list: groups[i] = (first pair slot, pairs),
+// lists taken in `order` (null: by id; longest first balances the scans).  ngroups[0] is the
+// count and ngroups[1] the dispenser the grouped scans take groups from (zeroed here).
+cudaError_t launch_make_groups(const int32_t* counts, const int32_t* offsets, const int32_t* order, int nlist,
+                               int wmax, int2* groups, int32_t* ngroups, cudaStream_t st);
 cudaError_t launch_adc_group(const AdcArgs& a, int R, int grid, cudaStream_t st);
 
 // IVF-flat list scan (IvfIndex.search without PQ): pairs grouped by list, up to 64 per group.
@@ -57,7 +59,7 @@ struct FlatListArgs {
   const int32_t* pairs;       // pair indices (q * nprobe + p), grouped by list
   const int32_t* pair_count;  // device count of the grouped pairs
   const int2* groups;         // (first pair slot, pairs) of up to 64 pairs sharing one list
-  const int32_t* ngroups;
+  int32_t* ngroups;           // [0] count, [1] dispenser
   const int32_t* lists;       // [nq][nprobe] routed list ids
   const float* queries;       // [nq][Dp] zero-padded copy
   const float* qnorm;         // [nq] dotProduct(q, q) (COSINE)

@@ -282,6 +282,19 @@ float* upload_rows32(vx_index* ix, const float* host, int64_t n, int dim, int64_
   return d;
 }
 
+// IVF list ids ordered by row count, longest first (ties by id): grouped scans hand out the
+// groups of long lists first, so the last groups to finish are short.
+int32_t* upload_list_order(vx_index* ix, const int64_t* list_offsets, int nlist) {
+  std::vector<int32_t> order(nlist);
+  for (int l = 0; l < nlist; l++) order[l] = l;
+  std::stable_sort(order.begin(), order.end(), [&](int32_t x, int32_t y) {
+    return list_offsets[x + 1] - list_offsets[x] > list_offsets[y + 1] - list_offsets[y];
+  });
+  int32_t* d = dev_alloc<int32_t>(ix, (size_t)nlist);
+  VX_CUDA(cudaMemcpy(d, order.data(), (size_t)nlist * 4, cudaMemcpyHostToDevice));
+  return d;
+}
+
 // fp16 unit-row GEMM operand from the fp32 rows.
 void build_unit_f16(vx_index* ix) {
   ix->Dp = (int)round_up(ix->dim, 64);
@@ -803,7 +816,7 @@ int search_ivfflat(vx_index* ix, const float* dq, int nq, int k, int nprobe, flo
     uint32_t* kcnt = T.alloc<uint32_t>(qc);
     const int64_t maxg = (int64_t)qc * probes / kFlatGroup + ix->nlist + 1;
     int2* groups = T.alloc<int2>((size_t)maxg);
-    int32_t* ngroups = T.alloc<int32_t>(1);
+    int32_t* ngroups = T.alloc<int32_t>(2);  // count, dispenser
     uint64_t* qfloor = T.alloc<uint64_t>(qc);
     if (given_lists) {
       VX_LAUNCH(1, launch_copy_lists(given_lists + (size_t)q0 * probes, qc * probes, ix->nlist, lists, d_bad, st));
@@ -816,7 +829,7 @@ int search_ivfflat(vx_index* ix, const float* dq, int nq, int k, int nprobe, flo
     VX_LAUNCH(3, launch_group_pairs(lists, ix->list_off, qc * probes, ix->nlist, counts, offsets, cursor, pairs, st));
     VX_CUDA(cudaMemsetAsync(out_cnt, 0, (size_t)probes * qc * 4, st));
     VX_CUDA(cudaMemsetAsync(qfloor, 0, (size_t)qc * 8, st));
-    VX_LAUNCH(1, launch_make_groups(counts, offsets, ix->nlist, kFlatGroup, groups, ngroups, st));
+    VX_LAUNCH(1, launch_make_groups(counts, offsets, ix->list_order, ix->nlist, kFlatGroup, groups, ngroups, st));
     FlatListArgs a{};
     a.nq = qc;
     a.dim = dim;
@@ -931,10 +944,10 @@ int search_ivfpq(vx_index* ix, const float* dq, int nq, int k, int nprobe, int r
     if (use_adc_group() && adc_group_supported(ix->M, ix->Ks, dim) && gg.R > 0 && gg.R <= 9) {
       const int64_t maxg = (int64_t)qc * probes / kAdcGroupQ + ix->nlist + 1;
       int2* groups = T.alloc<int2>((size_t)maxg);
-      int32_t* ngroups = T.alloc<int32_t>(1);
+      int32_t* ngroups = T.alloc<int32_t>(2);  // count, dispenser
       uint64_t* qfloor = T.alloc<uint64_t>(qc);
       VX_CUDA(cudaMemsetAsync(qfloor, 0, (size_t)qc * 8, st));
-      VX_LAUNCH(1, launch_make_groups(counts, offsets, ix->nlist, kAdcGroupQ, groups, ngroups, st));
+      VX_LAUNCH(1, launch_make_groups(counts, offsets, ix->list_order, ix->nlist, kAdcGroupQ, groups, ngroups, st));
       a.groups = groups;
       a.ngroups = ngroups;
       a.floor = qfloor;
@@ -1493,6 +1506,7 @@ int ivfpq_build_strided(int32_t device, const float* centroids, int32_t nlist, i
       VX_CUDA(cudaMemcpy(ix->cent, centroids, (size_t)nlist * dim * 4, cudaMemcpyDefault));
       ix->list_off = dev_alloc<int64_t>(ix, (size_t)nlist + 1);
       VX_CUDA(cudaMemcpy(ix->list_off, list_offsets, (size_t)(nlist + 1) * 8, cudaMemcpyDefault));
+      ix->list_order = upload_list_order(ix, list_offsets, nlist);
       // subspaces (ProductQuantizer.computeSubspaceSizesAndOffsets, ProductQuantizer.java:686-700)
       std::vector<int32_t> sub(2 * (size_t)m);
       std::vector<int64_t> cboff(m);
@@ -1574,6 +1588,7 @@ int vx_ivfflat_build(int32_t device, const float* centroids, int32_t nlist, int3
       VX_CUDA(cudaMemcpy(ix->cent, centroids, (size_t)nlist * dim * 4, cudaMemcpyDefault));
       ix->list_off = dev_alloc<int64_t>(ix, (size_t)nlist + 1);
       VX_CUDA(cudaMemcpy(ix->list_off, list_offsets, (size_t)(nlist + 1) * 8, cudaMemcpyDefault));
+      ix->list_order = upload_list_order(ix, list_offsets, nlist);
       ix->ordinals = dev_alloc<int32_t>(ix, (size_t)std::max<int64_t>(nl, 1));
       ix->flat_rows = dev_alloc<float>(ix, (size_t)std::max<int64_t>(nl, 1) * ix->Dp_flat);
       if (metric == VX_COSINE) ix->flat_norms = dev_alloc<float>(ix, (size_t)std::max<int64_t>(nl, 1));
