@@ -66,7 +66,8 @@ typedef enum vx_index_kind {
   VX_KIND_SQ8 = 2,   /* QuantizerKind.SQ8  -> QuantizedFlatScanAdapter(ScalarQuantizedVectors) */
   VX_KIND_BQ = 3,    /* QuantizerKind.BQ (SIGN_BIT) -> QuantizedFlatScanAdapter(BinaryQuantizedVectors) */
   VX_KIND_IVFPQ = 4, /* IndexType.IVF_PQ -> IvfPqAdapter / IvfIndex.pqSearch                 */
-  VX_KIND_IVFFLAT = 5 /* IndexType.IVF_FLAT -> IvfFlatAdapter / IvfIndex.search (no PQ)       */
+  VX_KIND_IVFFLAT = 5, /* IndexType.IVF_FLAT -> IvfFlatAdapter / IvfIndex.search (no PQ)      */
+  VX_KIND_SQ4 = 6      /* QuantizerKind.SQ4 -> QuantizedFlatScanAdapter(ScalarQuantizedVectors INT4) */
 } vx_index_kind;
 
 typedef struct vx_index vx_index;
@@ -121,6 +122,14 @@ VX_API int vx_fp16_build(int32_t device, const uint16_t* codes, int64_t n, int32
 VX_API int vx_sq8_build(int32_t device, const int8_t* codes, const float* corrections, int64_t n,
                  int32_t dim, float min_quantile, float max_quantile, int32_t metric,
                  const float* vectors, int64_t row_stride, vx_index** out);
+/* ScalarQuantizedVectors INT4 (ScalarQuantizedVectors.java:110-140, ScalarQuantizer.java:285-351):
+ * packed codes [n][ceil(dim/2)] (low nibble = even dimension, high nibble = odd), per-row
+ * corrections, the quantiles.  Scored as scoreFunctionInt4 does: the codes unpacked one per
+ * byte (0..15), the exact int32 dot or squared distance, then the INT8 formulas with
+ * maxValue 15. */
+VX_API int vx_sq4_build(int32_t device, const uint8_t* packed, const float* corrections, int64_t n,
+                        int32_t dim, float min_quantile, float max_quantile, int32_t metric,
+                        const float* vectors, int64_t row_stride, vx_index** out);
 /* BinaryQuantizedVectors SIGN_BIT (BinaryQuantizedVectors.java:40-107): words [n][ceil(dim/64)]
  * as produced by BinaryQuantizer.packBits + bytesToLongs (BinaryQuantizer.java:207-232). */
 VX_API int vx_bq_build(int32_t device, const uint64_t* words, int64_t n, int32_t dim, int32_t metric,
@@ -150,10 +159,10 @@ VX_API int vx_ivfflat_build(int32_t device, const float* centroids, int32_t nlis
 /* ---- persistent files (host memory; the bytes are not retained) --------------------------
  * quantized.bin as written by QuantizedVectorsCodec.encode and read by .decode
  * (vectors-db/.../storage/QuantizedVectorsCodec.java:91-192): little-endian, header magic 'VQTZ'
- * (FileFormat.java:77), version 1, QuantizerKind ordinal, dimension, vectorCount.  SQ8 (:224-296),
- * BQ SIGN_BIT (:425-518) and FP16 (:194-221) payloads build the index vx_sq8_build /
- * vx_bq_build / vx_fp16_build would; SQ4, PQ, BQ BBQ, RABITQ, NVQ, TURBOQUANT and EXTENDED_RABITQ
- * return VX_ERR_UNSUPPORTED.  The collection's metric is not stored in the file.  vectors
+ * (FileFormat.java:77), version 1, QuantizerKind ordinal, dimension, vectorCount.  SQ8 / SQ4
+ * (:224-296), BQ SIGN_BIT (:425-518) and FP16 (:194-221) payloads build the index vx_sq8_build /
+ * vx_sq4_build / vx_bq_build / vx_fp16_build would; PQ, BQ BBQ, RABITQ, NVQ, TURBOQUANT and
+ * EXTENDED_RABITQ return VX_ERR_UNSUPPORTED.  The collection's metric is not stored in the file.  vectors
  * (optional) are the fp32 rows for the two-pass rescore, e.g. a mapped vectors.bin with
  * row_stride = alignUp(dim*4, 64)/4.  Malformed bytes return VX_ERR_FORMAT with the decoder's
  * message. */

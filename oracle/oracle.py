@@ -74,6 +74,8 @@ def lib() -> C.CDLL:
             "vo_pq_encode_all": (None, [p, i64, i32, i32, i32, p, p, i32]),
             "vo_flat_search": (None, [p, i64, i32, i32, p, i32, i32, i32, i32, p, p, p]),
             "vo_sq8_search": (None, [p, p, i64, i32, f32, f32, i32, p, i32, i32, i32, i32, p, p, p]),
+            "vo_sq_search": (None, [p, p, i64, i32, f32, f32, i32, i32, p, i32, i32, i32, i32, p, p, p]),
+            "vo_sq_encode_all": (None, [f32, f32, i32, p, i64, i32, p, p, i32]),
             "vo_bq_search": (None, [p, i64, i32, i32, p, i32, i32, i32, i32, p, p, p]),
             "vo_fp16_search": (None, [p, i64, i32, i32, p, i32, i32, i32, i32, p, p, p]),
             "vo_quantized_two_pass_search": (None, [i32, p, p, f32, f32, p, i64, i32, i32, p, i32, i32, f32, i32, i32, p, p, p]),
@@ -271,6 +273,45 @@ def flat_search(db, queries, metric, k, policy=CANONICAL, nthreads=None):
     ids, sc, cnt = _outs(q.shape[0], k)
     lib().vo_flat_search(P(db), db.shape[0], q.shape[1], metric, P(q), q.shape[0], k, policy,
                          nthreads or threads(), P(ids), P(sc), P(cnt))
+    return ids, sc, cnt
+
+
+def sq4_encode_all(min_q, max_q, data):
+    """ScalarQuantizer INT4 encode (ScalarQuantizer.java:285-301): packed [n][ceil(dim/2)] codes,
+    low nibble = even dimension, and the per-row corrections."""
+    d = f32(data)
+    n, dim = d.shape
+    codes = np.empty(d.shape, np.int8)
+    corr = np.empty(n, np.float32)
+    lib().vo_sq_encode_all(min_q, max_q, 15, P(d), n, dim, P(codes), P(corr), threads())
+    return sq4_pack(codes), corr
+
+
+def sq4_pack(codes):
+    c = np.asarray(codes, np.uint8)
+    n, dim = c.shape
+    out = np.zeros((n, (dim + 1) // 2), np.uint8)
+    out[:, :] = c[:, 0::2] & 0x0F
+    out[:, : dim // 2] |= (c[:, 1::2] & 0x0F) << 4
+    return out
+
+
+def sq4_unpack(packed, dim):
+    """unpackInt4 (ScalarQuantizer.java:330-336)."""
+    p = np.asarray(packed, np.uint8)
+    out = np.empty((p.shape[0], dim), np.int8)
+    out[:, 0::2] = (p & 0x0F)[:, : (dim + 1) // 2]
+    out[:, 1::2] = ((p >> 4) & 0x0F)[:, : dim // 2]
+    return out
+
+
+def sq4_search(packed, corr, dim, min_q, max_q, queries, metric, k, policy=CANONICAL, nthreads=None):
+    codes = np.ascontiguousarray(sq4_unpack(packed, dim))
+    corr = f32(corr)
+    q = f32(queries)
+    ids, sc, cnt = _outs(q.shape[0], k)
+    lib().vo_sq_search(P(codes), P(corr), codes.shape[0], dim, min_q, max_q, 15, metric, P(q), q.shape[0], k, policy,
+                       nthreads or threads(), P(ids), P(sc), P(cnt))
     return ids, sc, cnt
 
 

@@ -534,26 +534,30 @@ void vo_sq8_train(const float* data, int64_t n, int32_t dim, float ci, float* mi
 }
 struct Sq8Params {
   float min_q, max_q, scale, alpha, cm;
+  int max_value;
 };
-// ScalarQuantizer constructor (ScalarQuantizer.java:59-69), INT8 maxValue = 127 (ScalarBits.java:30).
-static Sq8Params sq8_params(float min_q, float max_q) {
+// ScalarQuantizer constructor (ScalarQuantizer.java:59-69): maxValue 127 for INT8, 15 for INT4
+// (ScalarBits.java:30-33).
+static Sq8Params sq8_params(float min_q, float max_q, int max_value = 127) {
   Sq8Params p;
   p.min_q = min_q;
   p.max_q = max_q;
+  p.max_value = max_value;
   float range = max_q - min_q;
-  p.scale = (range == 0.0f) ? 0.0f : (float)127 / range;
-  p.alpha = (range == 0.0f) ? 0.0f : range / (float)127;
+  p.scale = (range == 0.0f) ? 0.0f : (float)max_value / range;
+  p.alpha = (range == 0.0f) ? 0.0f : range / (float)max_value;
   p.cm = p.alpha * p.alpha;
   return p;
 }
-// encodeInt8 / quantizeValue / correctionTerm (ScalarQuantizer.java:243-272).
-float vo_sq8_encode(float min_q, float max_q, const float* v, int32_t dim, int8_t* dst) {
-  Sq8Params p = sq8_params(min_q, max_q);
+// encodeInt8 / encodeInt4Unpacked / quantizeValue / correctionTerm (ScalarQuantizer.java:243-272,
+// 343-351): one code per byte (0..maxValue).
+float vo_sq_encode(float min_q, float max_q, int32_t max_value, const float* v, int32_t dim, int8_t* dst) {
+  Sq8Params p = sq8_params(min_q, max_q, max_value);
   float corr = 0.0f;
   for (int i = 0; i < dim; i++) {
     float dxc = java_max(p.min_q, java_min(p.max_q, v[i])) - p.min_q;
     int32_t q = java_round(p.scale * dxc);
-    q = std::max(0, std::min(127, q));
+    q = std::max(0, std::min(p.max_value, q));
     dst[i] = (int8_t)q;
     float dx = v[i] - p.min_q;
     float dxq = (float)q * p.alpha;
@@ -564,10 +568,14 @@ float vo_sq8_encode(float min_q, float max_q, const float* v, int32_t dim, int8_
   }
   return corr;
 }
-// scoreFunctionInt8 (ScalarQuantizedVectors.java:82-107).
-float vo_sq8_score(int32_t metric, float min_q, float max_q, const int8_t* qc, float qcorr,
-                   const int8_t* vc, float vcorr, int32_t dim) {
-  Sq8Params p = sq8_params(min_q, max_q);
+float vo_sq8_encode(float min_q, float max_q, const float* v, int32_t dim, int8_t* dst) {
+  return vo_sq_encode(min_q, max_q, 127, v, dim, dst);
+}
+// scoreFunctionInt8 / scoreFunctionInt4 (ScalarQuantizedVectors.java:82-140): the INT4 codes
+// unpacked one per byte, the same formulas with the INT4 constants.
+float vo_sq_score(int32_t metric, float min_q, float max_q, int32_t max_value, const int8_t* qc, float qcorr,
+                  const int8_t* vc, float vcorr, int32_t dim) {
+  Sq8Params p = sq8_params(min_q, max_q, max_value);
   if (metric == VO_EUCLIDEAN) {
     int32_t sq = vo_byte_square_distance(qc, vc, dim);
     float adj = (float)sq * p.cm;
@@ -577,6 +585,10 @@ float vo_sq8_score(int32_t metric, float min_q, float max_q, const int8_t* qc, f
   float adj = (float)raw * p.cm + qcorr + vcorr;
   if (metric == VO_MAXIMUM_INNER_PRODUCT) return vo_scale_mip(adj);
   return java_max((1.0f + adj) / 2.0f, 0.0f);
+}
+float vo_sq8_score(int32_t metric, float min_q, float max_q, const int8_t* qc, float qcorr,
+                   const int8_t* vc, float vcorr, int32_t dim) {
+  return vo_sq_score(metric, min_q, max_q, 127, qc, qcorr, vc, vcorr, dim);
 }
 
 // ---------------------------------------------------------------- BQ (sign bit)
@@ -921,20 +933,32 @@ void vo_flat_search(const float* db, int64_t n, int32_t dim, int32_t metric, con
 }
 // QuantizedFlatScanAdapter.selectApproximateCandidates over ScalarQuantizedVectors
 // (QuantizedFlatScanAdapter.java:97-113, ScalarQuantizedVectors.java:82-107).
+void vo_sq_search(const int8_t* codes, const float* corr, int64_t n, int32_t dim, float min_q, float max_q,
+                  int32_t max_value, int32_t metric, const float* queries, int32_t nq, int32_t k, int32_t policy,
+                  int32_t nthreads, int32_t* ids, float* scores, int32_t* counts) {
+  std::vector<int8_t> qc((size_t)nq * dim);
+  std::vector<float> qcorr(nq);
+  for (int q = 0; q < nq; q++)
+    qcorr[q] = vo_sq_encode(min_q, max_q, max_value, queries + (int64_t)q * dim, dim, &qc[(size_t)q * dim]);
+  scan_topk(n, nq, k, policy, nthreads,
+            [&](int64_t q, int64_t r) {
+              return vo_sq_score(metric, min_q, max_q, max_value, &qc[(size_t)q * dim], qcorr[q], codes + r * dim,
+                                 corr[r], dim);
+            },
+            ids, scores, counts);
+}
 void vo_sq8_search(const int8_t* codes, const float* corr, int64_t n, int32_t dim, float min_q,
                    float max_q, int32_t metric, const float* queries, int32_t nq, int32_t k,
                    int32_t policy, int32_t nthreads, int32_t* ids, float* scores,
                    int32_t* counts) {
-  std::vector<int8_t> qc((size_t)nq * dim);
-  std::vector<float> qcorr(nq);
-  for (int q = 0; q < nq; q++)
-    qcorr[q] = vo_sq8_encode(min_q, max_q, queries + (int64_t)q * dim, dim, &qc[(size_t)q * dim]);
-  scan_topk(n, nq, k, policy, nthreads,
-            [&](int64_t q, int64_t r) {
-              return vo_sq8_score(metric, min_q, max_q, &qc[(size_t)q * dim], qcorr[q],
-                                  codes + r * dim, corr[r], dim);
-            },
-            ids, scores, counts);
+  vo_sq_search(codes, corr, n, dim, min_q, max_q, 127, metric, queries, nq, k, policy, nthreads, ids, scores, counts);
+}
+void vo_sq_encode_all(float min_q, float max_q, int32_t max_value, const float* data, int64_t n, int32_t dim,
+                      int8_t* codes, float* corrections, int32_t nthreads) {
+  parallel_for(n, nthreads, [&](int64_t lo, int64_t hi) {
+    for (int64_t i = lo; i < hi; i++)
+      corrections[i] = vo_sq_encode(min_q, max_q, max_value, data + i * dim, dim, codes + i * dim);
+  });
 }
 void vo_bq_search(const uint64_t* words, int64_t n, int32_t dim, int32_t metric,
                   const float* queries, int32_t nq, int32_t k, int32_t policy, int32_t nthreads,

@@ -120,6 +120,14 @@ void vo_sq8_search(const int8_t* codes, const float* corrections, int64_t n, int
                    float min_q, float max_q, int32_t metric, const float* queries, int32_t nq,
                    int32_t k, int32_t policy, int32_t nthreads, int32_t* ids, float* scores,
                    int32_t* counts);
+float vo_sq_encode(float min_q, float max_q, int32_t max_value, const float* v, int32_t dim, int8_t* dst);
+float vo_sq_score(int32_t metric, float min_q, float max_q, int32_t max_value, const int8_t* qc, float qcorr,
+                  const int8_t* vc, float vcorr, int32_t dim);
+void vo_sq_search(const int8_t* codes, const float* corr, int64_t n, int32_t dim, float min_q, float max_q,
+                  int32_t max_value, int32_t metric, const float* queries, int32_t nq, int32_t k, int32_t policy,
+                  int32_t nthreads, int32_t* ids, float* scores, int32_t* counts);
+void vo_sq_encode_all(float min_q, float max_q, int32_t max_value, const float* data, int64_t n, int32_t dim,
+                      int8_t* codes, float* corrections, int32_t nthreads);
 void vo_bq_search(const uint64_t* words, int64_t n, int32_t dim, int32_t metric,
                   const float* queries, int32_t nq, int32_t k, int32_t policy, int32_t nthreads,
                   int32_t* ids, float* scores, int32_t* counts);

@@ -69,8 +69,9 @@ def test_quantized_rejections_mirror_the_codec(mutate, word):
 
 def test_quantized_kinds_not_served():
     packed = np.zeros((5, 6), np.uint8)
-    with pytest.raises(vx.UnsupportedOperationException, match="SQ4"):
-        vx.quantized_bin_info(F.quantized_bin_sq4(packed, np.zeros(5, np.float32), 12, 0.0, 1.0))
+    assert vx.quantized_bin_info(F.quantized_bin_sq4(packed, np.zeros(5, np.float32), 12, 0.0, 1.0)) == (F.SQ4, 12, 5)
+    with pytest.raises(vx.IOException, match="SQ vector data"):  # ceil(13/2) = 7 bytes a row expected
+        vx.quantized_bin_info(F.quantized_bin_sq4(packed, np.zeros(5, np.float32), 13, 0.0, 1.0))
     words = np.zeros((4, 1), np.uint64)
     with pytest.raises(vx.UnsupportedOperationException, match="BBQ"):
         vx.quantized_bin_info(F.quantized_bin_bq(words, 64, np.zeros(64, np.float32), np.zeros((4, 3), np.float32)))
@@ -166,3 +167,16 @@ def test_strided_rows_view():
     assert stride == 8 and v.dtype == np.float32
     with pytest.raises(vx.IllegalArgumentException):
         _strided_rows(np.ones((4, 7), np.float32), 8)
+
+
+def test_sq4_nibble_layout(oracle):
+    # encodeInt4 / unpackInt4 (ScalarQuantizer.java:285-336): low nibble = even dimension
+    codes = np.array([[1, 2, 3], [15, 0, 7]], np.int8)
+    packed = oracle.sq4_pack(codes)
+    assert packed.tolist() == [[0x21, 0x03], [0x0F, 0x07]]
+    assert np.array_equal(oracle.sq4_unpack(packed, 3), codes)
+    db = oracle.gen_mixture(300, 9, 4, 0.3, 5, 6, True)
+    lo, hi = oracle.sq8_train(db)
+    p4, c4 = oracle.sq4_encode_all(lo, hi, db)
+    u = oracle.sq4_unpack(p4, 9)
+    assert u.min() >= 0 and u.max() <= 15 and u.max() == 15

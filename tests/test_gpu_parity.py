@@ -297,6 +297,26 @@ def test_ivfpq_many_queries_per_list_bit_exact(oracle, metric):
         _check_float(got, ids, sc, cnt, f"ivfpq many rescore {rf} m={metric}")
 
 
+# ------------------------------------------------------------------ SQ4
+@pytest.mark.parametrize("metric", [0, 1, 2, 3])
+@pytest.mark.parametrize("n,dim,nq,k", [(6000, 768, 40, 100), (2500, 101, 65, 10)])
+def test_sq4_bit_exact(oracle, metric, n, dim, nq, k):
+    # ScalarQuantizedVectors INT4: nibble codes unpacked to bytes, the exact int8 tensor scan
+    # with the INT4 constants (maxValue 15); odd dim leaves the last byte's high nibble unused
+    db, q = _data(oracle, n, dim, nq, normalize=(metric != 3))
+    lo, hi = oracle.sq8_train(db)
+    packed, corr = oracle.sq4_encode_all(lo, hi, db)
+    a = vx.QuantizedFlatScanAdapter()
+    a.build_sq4(packed, corr, dim, lo, hi, vx.SimilarityFunction(metric), vectors=db)
+    got = a.scan_candidates(q, k)
+    ids, sc, cnt = oracle.sq4_search(packed, corr, dim, lo, hi, q, metric, k)
+    _check_float(got, ids, sc, cnt, f"sq4 m={metric} dim={dim}", exact_scores=True)
+    # the two-pass contract (candidates re-scored in fp32) on top of the SQ4 scan
+    two = a.search_batch(q, 10, over_query_factor=4.0)
+    assert all(len(o.ordinals) == min(10, n) for o in two)
+    a.close()
+
+
 # ------------------------------------------------------------------ IVF-flat
 @pytest.mark.parametrize("metric", [0, 1, 2, 3])
 @pytest.mark.parametrize("dim,nq,k", [(128, 400, 10), (96, 50, 50), (100, 40, 10), (7, 30, 5)])

@@ -160,8 +160,8 @@ int parse_quantized(const uint8_t* bytes, int64_t len, QuantizedFile& f) {
 int unsupported_kind(const QuantizedFile& f) {
   if (f.kind == kBq && f.bq_mode == 1)
     return failf(VX_ERR_UNSUPPORTED, "quantized.bin BQ in BBQ mode is not served here (SIGN_BIT is)");
-  if (f.kind != kSq8 && f.kind != kBq && f.kind != kFp16)
-    return failf(VX_ERR_UNSUPPORTED, "quantized.bin kind %s is not served here (SQ8, BQ SIGN_BIT and FP16 are)",
+  if (f.kind != kSq8 && f.kind != kSq4 && f.kind != kBq && f.kind != kFp16)
+    return failf(VX_ERR_UNSUPPORTED, "quantized.bin kind %s is not served here (SQ8, SQ4, BQ SIGN_BIT and FP16 are)",
                  kKindNames[f.kind]);
   return VX_OK;
 }
@@ -340,6 +340,19 @@ int vx_quantized_bin_build(int32_t device, const uint8_t* bytes, int64_t len, in
         std::memcpy(&corr[i], r + d, 4);  // little-endian float, as the host
       }
       return vx_sq8_build(device, codes.data(), corr.data(), (int64_t)n, f.dim, f.min_q, f.max_q, metric, vectors,
+                          row_stride, out);
+    }
+    if (f.kind == kSq4) {
+      // records are (ceil(dim/2) packed bytes, correction)
+      const size_t nb = (d + 1) / 2;
+      std::vector<uint8_t> packed(n * nb);
+      std::vector<float> corr(n);
+      for (size_t i = 0; i < n; i++) {
+        const uint8_t* r = data + i * (nb + 4);
+        std::memcpy(&packed[i * nb], r, nb);
+        std::memcpy(&corr[i], r + nb, 4);
+      }
+      return vx_sq4_build(device, packed.data(), corr.data(), (int64_t)n, f.dim, f.min_q, f.max_q, metric, vectors,
                           row_stride, out);
     }
     if (f.kind == kBq) {

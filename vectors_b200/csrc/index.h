@@ -32,6 +32,7 @@ struct vx_index {
   float* vcorr = nullptr;
   int32_t* vsq = nullptr;
   float min_q = 0, max_q = 0;
+  int sq_max = 127;  // ScalarBits.maxValue(): 127 SQ8, 15 SQ4 (codes unpacked one per byte)
   CUtensorMap tm_codes8;
   // BQ
   uint64_t* words = nullptr;

@@ -17,4 +17,9 @@ int ivfpq_build_strided(int32_t device, const float* centroids, int32_t nlist, i
                         const float* vectors, int64_t row_stride, int32_t nprobe, int32_t rescore_factor,
                         vx_index** out);
 
+// ScalarQuantizedVectors index with codes one per byte, maxValue 127 (SQ8) or 15 (SQ4) (vx_api.cu).
+int sq_build(int32_t device, const int8_t* codes, const float* corrections, int64_t n, int32_t dim,
+             float min_quantile, float max_quantile, int max_value, int32_t metric, const float* vectors,
+             int64_t row_stride, vx_index** out);
+
 }  // namespace vx

@@ -117,8 +117,8 @@ __global__ void margin_kernel(const float* __restrict__ qnorm, const float* __re
   margin[q] = (float)(m * 1.0001 + 1e-30);
 }
 
-// SQ8 query encoder: ScalarQuantizer.encodeInt8 / quantizeValue / correctionTerm
-// (ScalarQuantizer.java:243-272), sequential over dimensions, one thread per query, every
+// SQ8 / SQ4 query encoder: ScalarQuantizer.encodeInt8 / encodeInt4Unpacked / quantizeValue /
+// correctionTerm (ScalarQuantizer.java:243-272,343-351), sequential over dimensions, one thread per query, every
 // operation rounded as Java rounds it.  Also returns sum of squared codes for EUCLIDEAN.
 __global__ void sq8_encode_queries_kernel(const float* __restrict__ q, int nq, int dim, int Dp8,
                                           Sq8Consts k, int8_t* __restrict__ codes,
@@ -147,7 +147,7 @@ __global__ void sq8_encode_queries_kernel(const float* __restrict__ q, int nq, i
       const float f = floorf(t);
       qv = (int32_t)f + ((__fsub_rn(t, f) >= 0.5f) ? 1 : 0);
     }
-    qv = qv < 0 ? 0 : (qv > 127 ? 127 : qv);
+    qv = qv < 0 ? 0 : (qv > k.max_value ? k.max_value : qv);
     out[i] = (int8_t)qv;
     ss += qv * qv;
     const float dx = __fsub_rn(x, k.min_q);
@@ -235,14 +235,16 @@ cudaError_t launch_sq8_rows_pad(const int8_t* src, int64_t n, int dim, int Dp8, 
   return cudaGetLastError();
 }
 
-// ScalarQuantizer constructor constants (ScalarQuantizer.java:59-69), INT8 maxValue 127.
-Sq8Consts sq8_consts(float min_q, float max_q) {
+// ScalarQuantizer constructor constants (ScalarQuantizer.java:59-69): maxValue 127 for INT8,
+// 15 for INT4 (ScalarBits.java:30-33); the int is promoted to float as in Java.
+Sq8Consts sq8_consts(float min_q, float max_q, int max_value) {
   Sq8Consts k;
   k.min_q = min_q;
   k.max_q = max_q;
+  k.max_value = max_value;
   const float range = max_q - min_q;
-  k.scale = (range == 0.0f) ? 0.0f : 127.0f / range;
-  k.alpha = (range == 0.0f) ? 0.0f : range / 127.0f;
+  k.scale = (range == 0.0f) ? 0.0f : (float)max_value / range;
+  k.alpha = (range == 0.0f) ? 0.0f : range / (float)max_value;
   k.cm = k.alpha * k.alpha;
   return k;
 }

@@ -14,8 +14,9 @@ enum OperandKind : int {
 
 struct Sq8Consts {
   float min_q, max_q, scale, alpha, cm;
+  int max_value;  // ScalarBits.maxValue(): 127 (INT8) or 15 (INT4)
 };
-Sq8Consts sq8_consts(float min_q, float max_q);
+Sq8Consts sq8_consts(float min_q, float max_q, int max_value = 127);
 
 cudaError_t launch_rows_to_f16(const float* src, int64_t n, int dim, int64_t src_stride, int Dp,
                                bool unit, __half* dst, float* norms, float* norms_sq,

@@ -630,7 +630,7 @@ int search_quantized_scan(vx_index* ix, const float* dq, int nq, int K, int k_ou
   Scratch S(st);
   int32_t* d_err = S.alloc<int32_t>(1);
   VX_CUDA(cudaMemsetAsync(d_err, 0, 4, st));
-  if (ix->kind == VX_KIND_SQ8 || (ix->kind == VX_KIND_BQ && ix->codes8)) {
+  if (ix->kind == VX_KIND_SQ8 || ix->kind == VX_KIND_SQ4 || (ix->kind == VX_KIND_BQ && ix->codes8)) {
     const bool bq = ix->kind == VX_KIND_BQ;  // +-1 operands, Hamming epilogue
     const int R = gemm_scan_stream_R(K);
     if (R < 0) return fail(VX_ERR_UNSUPPORTED, "k=%d is larger than this build supports", K);
@@ -645,7 +645,7 @@ int search_quantized_scan(vx_index* ix, const float* dq, int nq, int K, int k_ou
                      : ix->metric == VX_EUCLIDEAN ? kEpiSq8L2
                      : ix->metric == VX_MAXIMUM_INNER_PRODUCT ? kEpiSq8Mip
                                                               : kEpiSq8Dot;
-    const Sq8Consts kc = bq ? Sq8Consts{0.f, 0.f, 0.f, 0.f, 0.f} : sq8_consts(ix->min_q, ix->max_q);
+    const Sq8Consts kc = bq ? Sq8Consts{0.f, 0.f, 0.f, 0.f, 0.f} : sq8_consts(ix->min_q, ix->max_q, ix->sq_max);
     // sized once for the largest chunk and reused by every chunk
     const int qmax = (int)std::min<int64_t>(qch, std::max(nq, 1));
     const int QpMax = (qmax + QB - 1) / QB * QB;
@@ -1121,6 +1121,7 @@ int search_batch_dev(vx_index* ix, const float* dq, int nq, int dim, int k, int 
       });
     case VX_KIND_FP16:
     case VX_KIND_SQ8:
+    case VX_KIND_SQ4:
     case VX_KIND_BQ: {
       if (!ix->rows32)
         return fail(VX_ERR_UNSUPPORTED,
@@ -1346,6 +1347,50 @@ int vx_fp16_build(int32_t device, const uint16_t* codes, int64_t n, int32_t dim,
 int vx_sq8_build(int32_t device, const int8_t* codes, const float* corrections, int64_t n,
                  int32_t dim, float min_quantile, float max_quantile, int32_t metric,
                  const float* vectors, int64_t row_stride, vx_index** out) {
+  return vx::sq_build(device, codes, corrections, n, dim, min_quantile, max_quantile, 127, metric, vectors,
+                      row_stride, out);
+}
+
+int vx_sq4_build(int32_t device, const uint8_t* packed, const float* corrections, int64_t n, int32_t dim,
+                 float min_quantile, float max_quantile, int32_t metric, const float* vectors, int64_t row_stride,
+                 vx_index** out) {
+  return guarded([&]() -> int {
+    if (!out) return fail(VX_ERR_NULL_POINTER, "out must not be null");
+    *out = nullptr;
+    if (n > 0 && (!packed || !corrections)) return fail(VX_ERR_NULL_POINTER, "codes/corrections must not be null");
+    if (n < 0 || n > INT32_MAX) return fail(VX_ERR_INVALID_ARGUMENT, "bad vector count");
+    if (n > 0 && dim <= 0) return fail(VX_ERR_INVALID_ARGUMENT, "bad dimension %d", dim);
+    // unpackInt4 (ScalarQuantizer.java:330-336): low nibble = even dimension, high = odd
+    const size_t nb = ((size_t)dim + 1) / 2;
+    std::vector<uint8_t> host_packed;
+    const uint8_t* src = packed;
+    if (n > 0) {
+      cudaPointerAttributes attr{};
+      if (cudaPointerGetAttributes(&attr, packed) == cudaSuccess && attr.type == cudaMemoryTypeDevice) {
+        host_packed.resize((size_t)n * nb);
+        VX_CUDA(cudaMemcpy(host_packed.data(), packed, host_packed.size(), cudaMemcpyDeviceToHost));
+        src = host_packed.data();
+      }
+      cudaGetLastError();
+    }
+    std::vector<int8_t> codes((size_t)std::max<int64_t>(n, 0) * (size_t)std::max(dim, 0));
+    for (int64_t r = 0; r < n; r++)
+      for (int i = 0; i < dim; i++) {
+        const uint8_t b = src[(size_t)r * nb + (i >> 1)];
+        codes[(size_t)r * dim + i] = (int8_t)((i & 1) ? (b >> 4) & 0x0F : b & 0x0F);
+      }
+    return vx::sq_build(device, codes.data(), corrections, n, dim, min_quantile, max_quantile, 15, metric,
+                        vectors, row_stride, out);
+  });
+}
+
+}  // extern "C"
+
+namespace vx {
+// ScalarQuantizedVectors with codes one per byte, maxValue 127 (SQ8) or 15 (SQ4 unpacked).
+int sq_build(int32_t device, const int8_t* codes, const float* corrections, int64_t n, int32_t dim,
+             float min_quantile, float max_quantile, int max_value, int32_t metric, const float* vectors,
+             int64_t row_stride, vx_index** out) {
   return guarded([&]() -> int {
     if (!out) return fail(VX_ERR_NULL_POINTER, "out must not be null");
     *out = nullptr;
@@ -1360,7 +1405,8 @@ int vx_sq8_build(int32_t device, const int8_t* codes, const float* corrections, 
     int nsms = 0;
     if (int s = check_device(device, &nsms)) return s;
     vx_index* ix = new vx_index();
-    ix->kind = VX_KIND_SQ8;
+    ix->kind = max_value == 15 ? VX_KIND_SQ4 : VX_KIND_SQ8;
+    ix->sq_max = max_value;
     ix->device = device;
     ix->metric = metric;
     ix->n = n;
@@ -1393,6 +1439,9 @@ int vx_sq8_build(int32_t device, const int8_t* codes, const float* corrections, 
     return VX_OK;
   });
 }
+}  // namespace vx
+
+extern "C" {
 
 int vx_bq_build(int32_t device, const uint64_t* words, int64_t n, int32_t dim, int32_t metric,
                 const float* vectors, int64_t row_stride, vx_index** out) {
@@ -1656,7 +1705,7 @@ int vx_search_batch(vx_index* ix, const float* queries, int32_t nq, int32_t dim,
 
 static int scan_candidates_dev(vx_index* ix, const float* dq, int nq, int dim, int k, int32_t* di,
                                float* ds, int32_t* dc, cudaStream_t st) {
-  if (ix->kind != VX_KIND_SQ8 && ix->kind != VX_KIND_BQ && ix->kind != VX_KIND_FP16)
+  if (ix->kind != VX_KIND_SQ8 && ix->kind != VX_KIND_SQ4 && ix->kind != VX_KIND_BQ && ix->kind != VX_KIND_FP16)
     return fail(VX_ERR_UNSUPPORTED, "candidate scans apply to SQ8, BQ and FP16 indexes");
   if (ix->n == 0) {
     fill_empty(nq, k, di, ds, dc, st);

@@ -331,6 +331,21 @@ class QuantizedFlatScanAdapter(IndexSpi):
         )
         self._n, self._dim, self.metric, self.kind = n, dim, SimilarityFunction(metric), "SQ8"
 
+    def build_sq4(self, packed, corrections, dim: int, min_quantile: float, max_quantile: float, metric, vectors=None):
+        """ScalarQuantizedVectors INT4: packed [n][ceil(dim/2)] codes, low nibble = even dimension."""
+        packed = np.ascontiguousarray(np.asarray(packed, dtype=np.uint8))
+        corr = np.ascontiguousarray(np.asarray(corrections, dtype=np.float32))
+        v = None if vectors is None else _as_matrix(vectors, "vectors")
+        n = packed.shape[0]
+        if packed.ndim != 2 or packed.shape[1] != (dim + 1) // 2:
+            raise IllegalArgumentException(f"packed codes must be [n][{(dim + 1) // 2}]")
+        self._h.close()
+        _check(
+            N.lib().vx_sq4_build(self.device, _ptr(packed), _ptr(corr), n, dim, float(min_quantile), float(max_quantile),
+                                 int(metric), _ptr(v), dim, C.byref(self._h.ptr))
+        )
+        self._n, self._dim, self.metric, self.kind = n, dim, SimilarityFunction(metric), "SQ4"
+
     def build_bq(self, words, dim: int, metric, vectors=None):
         words = np.ascontiguousarray(np.asarray(words, dtype=np.uint64))
         v = None if vectors is None else _as_matrix(vectors, "vectors")
@@ -359,7 +374,7 @@ class QuantizedFlatScanAdapter(IndexSpi):
 
     def load_quantized_bin(self, data, metric, vectors=None):
         """Opens a persistent quantized.bin (QuantizedVectorsCodec.decode) as this adapter's index:
-        SQ8, BQ SIGN_BIT or FP16.  ``vectors`` are the fp32 rows for the two-pass rescore (a mapped
+        SQ8, SQ4, BQ SIGN_BIT or FP16.  ``vectors`` are the fp32 rows for the two-pass rescore (a mapped
         vectors.bin view with its 64-byte row stride is taken as is)."""
         b = _file_bytes(data)
         kind, dim, n = quantized_bin_info(b)
@@ -368,7 +383,7 @@ class QuantizedFlatScanAdapter(IndexSpi):
         _check(N.lib().vx_quantized_bin_build(self.device, _ptr(b), b.size, int(metric), _ptr(v), stride,
                                               C.byref(self._h.ptr)))
         self._n, self._dim, self.metric = n, dim, SimilarityFunction(metric)
-        self.kind = {1: "SQ8", 4: "BQ", 8: "FP16"}[kind]
+        self.kind = {1: "SQ8", 2: "SQ4", 4: "BQ", 8: "FP16"}[kind]
 
     def build(self, vectors, metric):
         raise UnsupportedOperationException("QuantizedFlatScanAdapter wraps an already-built flat index")
