@@ -67,7 +67,8 @@ typedef enum vx_index_kind {
   VX_KIND_BQ = 3,    /* QuantizerKind.BQ (SIGN_BIT) -> QuantizedFlatScanAdapter(BinaryQuantizedVectors) */
   VX_KIND_IVFPQ = 4, /* IndexType.IVF_PQ -> IvfPqAdapter / IvfIndex.pqSearch                 */
   VX_KIND_IVFFLAT = 5, /* IndexType.IVF_FLAT -> IvfFlatAdapter / IvfIndex.search (no PQ)      */
-  VX_KIND_SQ4 = 6      /* QuantizerKind.SQ4 -> QuantizedFlatScanAdapter(ScalarQuantizedVectors INT4) */
+  VX_KIND_SQ4 = 6,     /* QuantizerKind.SQ4 -> QuantizedFlatScanAdapter(ScalarQuantizedVectors INT4) */
+  VX_KIND_BBQ = 7      /* QuantizerKind.BQ, BinaryMode.BBQ -> QuantizedFlatScanAdapter(BinaryQuantizedVectors) */
 } vx_index_kind;
 
 typedef struct vx_index vx_index;
@@ -134,6 +135,14 @@ VX_API int vx_sq4_build(int32_t device, const uint8_t* packed, const float* corr
  * as produced by BinaryQuantizer.packBits + bytesToLongs (BinaryQuantizer.java:207-232). */
 VX_API int vx_bq_build(int32_t device, const uint64_t* words, int64_t n, int32_t dim, int32_t metric,
                 const float* vectors, int64_t row_stride, vx_index** out);
+/* BinaryQuantizedVectors BBQ (BinaryQuantizedVectors.java:110-275, BinaryQuantizer.java:199-270):
+ * words [n][ceil(dim/64)] of the centroid-relative sign bits, corrections [n][3] =
+ * (|v - c|^2, vl, width), the centroid [dim].  Scored as bbqScoreFunction does: the query
+ * centred and quantised to 4 bits, rawAsymDot from its 4 bit planes (exact), computeBbqDot and
+ * the metric's transform in the Java float order.  dim <= 1024. */
+VX_API int vx_bbq_build(int32_t device, const uint64_t* words, const float* corrections, const float* centroid,
+                        int64_t n, int32_t dim, int32_t metric, const float* vectors, int64_t row_stride,
+                        vx_index** out);
 /* IvfIndex.fromPrebuilt(buoy, partitions, vectors, metric, pq, codes)
  * (vectors-ivf/.../IvfIndex.java:343-351): centroids [nlist][dim]; partitions as CSR
  * (list_offsets[nlist+1], list_ordinals); PQ with m subspaces of ks centroids, codebooks
@@ -160,9 +169,9 @@ VX_API int vx_ivfflat_build(int32_t device, const float* centroids, int32_t nlis
  * quantized.bin as written by QuantizedVectorsCodec.encode and read by .decode
  * (vectors-db/.../storage/QuantizedVectorsCodec.java:91-192): little-endian, header magic 'VQTZ'
  * (FileFormat.java:77), version 1, QuantizerKind ordinal, dimension, vectorCount.  SQ8 / SQ4
- * (:224-296), BQ SIGN_BIT (:425-518) and FP16 (:194-221) payloads build the index vx_sq8_build /
- * vx_sq4_build / vx_bq_build / vx_fp16_build would; PQ, BQ BBQ, RABITQ, NVQ, TURBOQUANT and
- * EXTENDED_RABITQ return VX_ERR_UNSUPPORTED.  The collection's metric is not stored in the file.  vectors
+ * (:224-296), BQ SIGN_BIT and BBQ (:425-518) and FP16 (:194-221) payloads build the index
+ * vx_sq8_build / vx_sq4_build / vx_bq_build / vx_bbq_build / vx_fp16_build would; PQ, RABITQ, NVQ,
+ * TURBOQUANT and EXTENDED_RABITQ return VX_ERR_UNSUPPORTED.  The collection's metric is not stored in the file.  vectors
  * (optional) are the fp32 rows for the two-pass rescore, e.g. a mapped vectors.bin with
  * row_stride = alignUp(dim*4, 64)/4.  Malformed bytes return VX_ERR_FORMAT with the decoder's
  * message. */

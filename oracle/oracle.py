@@ -76,6 +76,8 @@ def lib() -> C.CDLL:
             "vo_sq8_search": (None, [p, p, i64, i32, f32, f32, i32, p, i32, i32, i32, i32, p, p, p]),
             "vo_sq_search": (None, [p, p, i64, i32, f32, f32, i32, i32, p, i32, i32, i32, i32, p, p, p]),
             "vo_sq_encode_all": (None, [f32, f32, i32, p, i64, i32, p, p, i32]),
+            "vo_bbq_encode_all": (None, [p, p, i64, i32, p, p, i32]),
+            "vo_bbq_search": (None, [p, p, p, i64, i32, i32, p, i32, i32, i32, i32, p, p, p]),
             "vo_bq_search": (None, [p, i64, i32, i32, p, i32, i32, i32, i32, p, p, p]),
             "vo_fp16_search": (None, [p, i64, i32, i32, p, i32, i32, i32, i32, p, p, p]),
             "vo_quantized_two_pass_search": (None, [i32, p, p, f32, f32, p, i64, i32, i32, p, i32, i32, f32, i32, i32, p, p, p]),
@@ -312,6 +314,25 @@ def sq4_search(packed, corr, dim, min_q, max_q, queries, metric, k, policy=CANON
     ids, sc, cnt = _outs(q.shape[0], k)
     lib().vo_sq_search(P(codes), P(corr), codes.shape[0], dim, min_q, max_q, 15, metric, P(q), q.shape[0], k, policy,
                        nthreads or threads(), P(ids), P(sc), P(cnt))
+    return ids, sc, cnt
+
+
+def bbq_encode_all(data, centroid):
+    """BinaryQuantizer BBQ encode given the centroid: words [n][ceil(dim/64)], corrections [n][3]."""
+    d, c = f32(data), f32(centroid)
+    n, dim = d.shape
+    words = np.empty((n, (dim + 63) // 64), np.uint64)
+    corr = np.empty((n, 3), np.float32)
+    lib().vo_bbq_encode_all(P(d), P(c), n, dim, P(words), P(corr), threads())
+    return words, corr
+
+
+def bbq_search(words, corr, centroid, dim, queries, metric, k, policy=CANONICAL, nthreads=None):
+    words = np.ascontiguousarray(words, np.uint64)
+    corr, c, q = f32(corr), f32(centroid), f32(queries)
+    ids, sc, cnt = _outs(q.shape[0], k)
+    lib().vo_bbq_search(P(words), P(corr), P(c), words.shape[0], dim, metric, P(q), q.shape[0], k, policy,
+                        nthreads or threads(), P(ids), P(sc), P(cnt))
     return ids, sc, cnt
 
 

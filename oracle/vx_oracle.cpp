@@ -908,6 +908,103 @@ void vo_bq_encode_all(const float* data, int64_t n, int32_t dim, uint64_t* words
     for (int64_t i = lo; i < hi; i++) vo_bq_encode(data + i * dim, dim, words + i * nw);
   });
 }
+// BBQ encode: packBits with the centroid (distToC = sum (v - c)^2 in order) and
+// computeCorrections (BinaryQuantizer.java:207-270): corr = (distToC, vl = min, width = max - min).
+void vo_bbq_encode_all(const float* data, const float* cent, int64_t n, int32_t dim, uint64_t* words, float* corr,
+                       int32_t nthreads) {
+  int nw = (dim + 63) >> 6;
+  parallel_for(n, nthreads, [&](int64_t lo, int64_t hi) {
+    for (int64_t i = lo; i < hi; i++) {
+      const float* v = data + i * dim;
+      uint64_t* w = words + i * nw;
+      for (int j = 0; j < nw; j++) w[j] = 0;
+      float dist = 0.0f, mn = INFINITY, mx = -INFINITY;
+      for (int d = 0; d < dim; d++) {
+        float c = v[d] - cent[d];
+        dist += c * c;
+        if (c >= 0) w[d >> 6] |= 1ULL << (d & 63);
+      }
+      for (int d = 0; d < dim; d++) {
+        float c = v[d] - cent[d];
+        if (c < mn) mn = c;
+        if (c > mx) mx = c;
+      }
+      corr[i * 3] = dist;
+      corr[i * 3 + 1] = mn;
+      corr[i * 3 + 2] = mx - mn;
+    }
+  });
+}
+// bbqScoreFunction / computeBbqDot / asymmetricDot / extractBitPlanes
+// (BinaryQuantizedVectors.java:110-275).
+void vo_bbq_search(const uint64_t* words, const float* corr, const float* cent, int64_t n, int32_t dim,
+                   int32_t metric, const float* queries, int32_t nq, int32_t k, int32_t policy, int32_t nthreads,
+                   int32_t* ids, float* scores, int32_t* counts) {
+  const int nw = (dim + 63) >> 6;
+  struct Q {
+    float qmin, w15, nsq, norm;
+    int32_t qsum;
+  };
+  std::vector<Q> qs(nq);
+  std::vector<uint64_t> planes((size_t)nq * 4 * nw, 0);
+  for (int q = 0; q < nq; q++) {
+    const float* v = queries + (int64_t)q * dim;
+    std::vector<float> c(dim);
+    for (int d = 0; d < dim; d++) c[d] = v[d] - cent[d];  // VectorUtil.subInPlace
+    float nsq = 0.0f, mn = INFINITY, mx = -INFINITY;
+    for (int d = 0; d < dim; d++) {
+      nsq += c[d] * c[d];
+      if (c[d] < mn) mn = c[d];
+      if (c[d] > mx) mx = c[d];
+    }
+    const float width = mx - mn;
+    const float norm = (float)std::sqrt((double)nsq);
+    const float scale = width > 0 ? 15.0f / width : 0.0f;
+    int32_t qsum = 0;
+    uint64_t* pl = &planes[(size_t)q * 4 * nw];
+    for (int d = 0; d < dim; d++) {
+      int32_t qv = java_round((c[d] - mn) * scale);
+      qv = std::max(0, std::min(15, qv));
+      qsum += qv;
+      for (int b = 0; b < 4; b++)
+        if ((qv >> b) & 1) pl[(size_t)b * nw + (d >> 6)] |= 1ULL << (d & 63);
+    }
+    qs[q] = Q{mn, width / 15.0f, nsq, norm, qsum};
+  }
+  scan_topk(n, nq, k, policy, nthreads,
+            [&](int64_t q, int64_t r) {
+              const Q& qi = qs[q];
+              const uint64_t* w = words + r * nw;
+              const uint64_t* pl = &planes[(size_t)q * 4 * nw];
+              int32_t raw = 0, pop = 0;
+              for (int b = 0; b < 4; b++) {
+                int32_t ps = 0;
+                for (int j = 0; j < nw; j++) ps += __builtin_popcountll(w[j] & pl[(size_t)b * nw + j]);
+                raw += ps << b;
+              }
+              for (int j = 0; j < nw; j++) pop += __builtin_popcountll(w[j]);
+              const float dist = corr[r * 3], vl = corr[r * 3 + 1], width = corr[r * 3 + 2];
+              const float approx = qi.qmin * (vl * (float)dim + width * (float)pop) +
+                                   qi.w15 * (vl * (float)qi.qsum + width * (float)raw);
+              switch (metric) {
+                case VO_EUCLIDEAN: {
+                  float adj = qi.nsq + dist - 2.0f * approx;
+                  return 1.0f / (1.0f + java_max(adj, 0.0f));
+                }
+                case VO_COSINE: {
+                  float vn = (float)std::sqrt((double)dist);
+                  if (qi.norm == 0.0f || vn == 0.0f) return 0.0f;
+                  float cosv = approx / (qi.norm * vn);
+                  return java_max((1.0f + cosv) / 2.0f, 0.0f);
+                }
+                case VO_MAXIMUM_INNER_PRODUCT:
+                  return vo_scale_mip(approx);
+                default:
+                  return java_max((1.0f + approx) / 2.0f, 0.0f);
+              }
+            },
+            ids, scores, counts);
+}
 void vo_fp16_encode_all(const float* data, int64_t n, int32_t dim, uint16_t* codes, int32_t nthreads) {
   parallel_for(n * dim, nthreads, [&](int64_t lo, int64_t hi) {
     for (int64_t i = lo; i < hi; i++) codes[i] = vo_f32_to_f16(data[i]);

@@ -131,6 +131,11 @@ void vo_sq_encode_all(float min_q, float max_q, int32_t max_value, const float* 
 void vo_bq_search(const uint64_t* words, int64_t n, int32_t dim, int32_t metric,
                   const float* queries, int32_t nq, int32_t k, int32_t policy, int32_t nthreads,
                   int32_t* ids, float* scores, int32_t* counts);
+void vo_bbq_encode_all(const float* data, const float* cent, int64_t n, int32_t dim, uint64_t* words, float* corr,
+                       int32_t nthreads);
+void vo_bbq_search(const uint64_t* words, const float* corr, const float* cent, int64_t n, int32_t dim,
+                   int32_t metric, const float* queries, int32_t nq, int32_t k, int32_t policy, int32_t nthreads,
+                   int32_t* ids, float* scores, int32_t* counts);
 void vo_fp16_search(const uint16_t* codes, int64_t n, int32_t dim, int32_t metric,
                     const float* queries, int32_t nq, int32_t k, int32_t policy, int32_t nthreads,
                     int32_t* ids, float* scores, int32_t* counts);

@@ -73,8 +73,11 @@ def test_quantized_kinds_not_served():
     with pytest.raises(vx.IOException, match="SQ vector data"):  # ceil(13/2) = 7 bytes a row expected
         vx.quantized_bin_info(F.quantized_bin_sq4(packed, np.zeros(5, np.float32), 13, 0.0, 1.0))
     words = np.zeros((4, 1), np.uint64)
+    assert vx.quantized_bin_info(F.quantized_bin_bq(words, 64, np.zeros(64, np.float32),
+                                                    np.zeros((4, 3), np.float32))) == (F.BQ, 64, 4)
+    big = np.zeros((2, 17), np.uint64)  # BBQ beyond 1024 dimensions is refused
     with pytest.raises(vx.UnsupportedOperationException, match="BBQ"):
-        vx.quantized_bin_info(F.quantized_bin_bq(words, 64, np.zeros(64, np.float32), np.zeros((4, 3), np.float32)))
+        vx.quantized_bin_info(F.quantized_bin_bq(big, 1050, np.zeros(1050, np.float32), np.zeros((2, 3), np.float32)))
     # a PQ payload: the header is validated, the kind is refused
     pq = struct.pack("<iiiii", F.MAGIC_QUANTIZED, 1, F.PQ, 16, 3)
     with pytest.raises(vx.UnsupportedOperationException, match="PQ"):

@@ -39,6 +39,8 @@ def test_quantized_bin_opens_the_same_index(oracle, metric):
     codes, corr = oracle.sq8_encode_all(lo, hi, db)
     packed4, corr4 = oracle.sq4_encode_all(lo, hi, db)
     words = oracle.bq_encode_all(db)
+    cent = db.mean(0).astype(np.float32)
+    bwords, bcorr = oracle.bbq_encode_all(db, cent)
     f16 = oracle.fp16_encode_all(db)
     cases = [
         ("SQ8", lambda a: a.build_sq8(codes, corr, lo, hi, vx.SimilarityFunction(metric), vectors=db),
@@ -46,6 +48,8 @@ def test_quantized_bin_opens_the_same_index(oracle, metric):
         ("SQ4", lambda a: a.build_sq4(packed4, corr4, dim, lo, hi, vx.SimilarityFunction(metric), vectors=db),
          F.quantized_bin_sq4(packed4, corr4, dim, lo, hi)),
         ("BQ", lambda a: a.build_bq(words, dim, vx.SimilarityFunction(metric), vectors=db), F.quantized_bin_bq(words, dim)),
+        ("BBQ", lambda a: a.build_bbq(bwords, bcorr, cent, dim, vx.SimilarityFunction(metric), vectors=db),
+         F.quantized_bin_bq(bwords, dim, cent, bcorr)),
         ("FP16", lambda a: a.build_fp16(f16, vx.SimilarityFunction(metric), vectors=db), F.quantized_bin_fp16(f16)),
     ]
     for kind, build, blob in cases:

@@ -317,6 +317,25 @@ def test_sq4_bit_exact(oracle, metric, n, dim, nq, k):
     a.close()
 
 
+# ------------------------------------------------------------------ BBQ
+@pytest.mark.parametrize("metric", [0, 1, 2, 3])
+@pytest.mark.parametrize("n,dim,nq,k", [(6000, 768, 40, 100), (2500, 100, 65, 10), (1000, 1024, 20, 5)])
+def test_bbq_bit_exact(oracle, metric, n, dim, nq, k):
+    # BinaryQuantizedVectors BBQ: 4-bit query planes against centroid-relative sign bits, the
+    # exact asymmetric popcount dot, computeBbqDot and the metric transform in Java's order
+    db, q = _data(oracle, n, dim, nq, normalize=(metric == 2))
+    cent = db.mean(0).astype(np.float32)
+    words, corr = oracle.bbq_encode_all(db, cent)
+    a = vx.QuantizedFlatScanAdapter()
+    a.build_bbq(words, corr, cent, dim, vx.SimilarityFunction(metric), vectors=db)
+    got = a.scan_candidates(q, k)
+    ids, sc, cnt = oracle.bbq_search(words, corr, cent, dim, q, metric, k)
+    _check_float(got, ids, sc, cnt, f"bbq m={metric} dim={dim}", exact_scores=True)
+    two = a.search_batch(q, 5, over_query_factor=4.0)
+    assert all(len(o.ordinals) == 5 for o in two)
+    a.close()
+
+
 # ------------------------------------------------------------------ IVF-flat
 @pytest.mark.parametrize("metric", [0, 1, 2, 3])
 @pytest.mark.parametrize("dim,nq,k", [(128, 400, 10), (96, 50, 50), (100, 40, 10), (7, 30, 5)])

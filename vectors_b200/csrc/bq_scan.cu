@@ -152,6 +152,225 @@ __global__ void bq_pack_kernel(const float* __restrict__ q, int nq, int dim, int
   }
 }
 
+
+// ---------------------------------------------------------------------------------------
+// BBQ (BinaryMode.BBQ): BinaryQuantizedVectors.bbqScoreFunction, computeBbqDot and
+// asymmetricDot (vectors-quantization/.../BinaryQuantizedVectors.java:110-275).  Rows are
+// centroid-relative sign bits with corrections (|v - c|^2, vl = min(v - c), width = max - min);
+// the query is centred, quantised to 4 bits over its own [min, max] and split into 4 bit
+// planes.  rawAsymDot = sum_b popcount(bits & plane_b) << b is exact; the score follows the
+// Java float expression operation by operation (no fused multiply-add).
+// ---------------------------------------------------------------------------------------
+// One thread per query: the two sequential passes of bbqScoreFunction's query set-up.
+__global__ void bbq_prep_queries_kernel(const float* __restrict__ q, int nq, int dim, const float* __restrict__ cent,
+                                        int nw_pad, uint64_t* __restrict__ planes, BbqQuery* __restrict__ info) {
+  const int qi = blockIdx.x * blockDim.x + threadIdx.x;
+  if (qi >= nq) return;
+  const float* v = q + (size_t)qi * dim;
+  float nsq = 0.0f, mn = __int_as_float(0x7f800000), mx = __int_as_float(0xff800000);
+  for (int d = 0; d < dim; d++) {
+    const float c = __fsub_rn(v[d], cent[d]);  // VectorUtil.subInPlace
+    nsq = __fadd_rn(nsq, __fmul_rn(c, c));
+    if (c < mn) mn = c;
+    if (c > mx) mx = c;
+  }
+  const float width = __fsub_rn(mx, mn);
+  const float scale = width > 0.0f ? __fdiv_rn(15.0f, width) : 0.0f;
+  int32_t qsum = 0;
+  uint64_t* pl = planes + (size_t)qi * 4 * nw_pad;
+  for (int w = 0; w < nw_pad; w++) {
+    uint64_t b0 = 0, b1 = 0, b2 = 0, b3 = 0;
+    for (int j = 0; j < 64; j++) {
+      const int d = w * 64 + j;
+      if (d >= dim) break;
+      const float c = __fsub_rn(v[d], cent[d]);
+      // Math.round: nearest, ties toward +infinity; NaN -> 0
+      const float t = __fmul_rn(__fsub_rn(c, mn), scale);
+      int32_t qv = 0;
+      if (t == t) {
+        const float f = floorf(t);
+        qv = (int32_t)f + ((__fsub_rn(t, f) >= 0.5f) ? 1 : 0);
+      }
+      qv = qv < 0 ? 0 : (qv > 15 ? 15 : qv);
+      qsum += qv;
+      const uint64_t bit = 1ull << j;
+      if (qv & 1) b0 |= bit;
+      if (qv & 2) b1 |= bit;
+      if (qv & 4) b2 |= bit;
+      if (qv & 8) b3 |= bit;
+    }
+    pl[w] = b0;
+    pl[nw_pad + w] = b1;
+    pl[2 * nw_pad + w] = b2;
+    pl[3 * nw_pad + w] = b3;
+  }
+  BbqQuery o;
+  o.qmin = mn;
+  o.w15 = __fdiv_rn(width, 15.0f);
+  o.nsq = nsq;
+  o.norm = (float)sqrt((double)nsq);
+  o.qsum = qsum;
+  info[qi] = o;
+}
+
+// Score of one (query, row): computeBbqDot then the metric's transform (:155-225).
+__device__ __forceinline__ float bbq_score(int metric, const BbqQuery& qi, float4 ri, int32_t raw, int dim) {
+  const float dist_c = ri.x, vl = ri.y, width = ri.z;
+  const int32_t pop = __float_as_int(ri.w);
+  const float s1 = __fadd_rn(__fmul_rn(vl, (float)dim), __fmul_rn(width, (float)pop));
+  const float s2 = __fadd_rn(__fmul_rn(vl, (float)qi.qsum), __fmul_rn(width, (float)raw));
+  const float approx = __fadd_rn(__fmul_rn(qi.qmin, s1), __fmul_rn(qi.w15, s2));
+  switch (metric) {
+    case kEuclidean: {
+      const float adj = __fsub_rn(__fadd_rn(qi.nsq, dist_c), __fmul_rn(2.0f, approx));
+      return __fdiv_rn(1.0f, __fadd_rn(1.0f, adj > 0.0f ? adj : 0.0f));
+    }
+    case kCosine: {
+      const float vn = (float)sqrt((double)dist_c);
+      if (qi.norm == 0.0f || vn == 0.0f) return 0.0f;
+      const float cosv = __fdiv_rn(approx, __fmul_rn(qi.norm, vn));
+      const float s = __fdiv_rn(__fadd_rn(1.0f, cosv), 2.0f);
+      return s > 0.0f ? s : 0.0f;
+    }
+    case kMaxInnerProduct:
+      return scale_mip(approx);
+    default: {
+      const float s = __fdiv_rn(__fadd_rn(1.0f, approx), 2.0f);
+      return s > 0.0f ? s : 0.0f;
+    }
+  }
+}
+
+template <int NW, int R>
+__global__ void __launch_bounds__(kBqThreads, 1)  // the 4 query planes stay in registers
+    bbq_scan_kernel(const uint64_t* __restrict__ db, const float4* __restrict__ rowinfo, int64_t n, int dim,
+                    int metric, const uint64_t* __restrict__ planes, const BbqQuery* __restrict__ qinfo, int nq,
+                    int64_t rows_per_part, int K, int C, uint64_t* __restrict__ bufs, uint32_t* __restrict__ cnts,
+                    uint64_t* __restrict__ thrs) {
+  extern __shared__ __align__(16) uint64_t s_tile[];  // [2][kBqTile * NW] words, then [2][kBqTile] float4
+  float4* s_info = reinterpret_cast<float4*>(s_tile + 2 * kBqTile * NW);
+  const int part = blockIdx.x;
+  const int64_t r0 = (int64_t)part * rows_per_part;
+  int64_t r1 = r0 + rows_per_part;
+  if (r1 > n) r1 = n;
+  const int64_t nrows = r1 > r0 ? r1 - r0 : 0;
+  const int ntiles = (int)((nrows + kBqTile - 1) / kBqTile);
+  constexpr int kChunks = kBqTile * NW / 2;
+
+  auto stage = [&](int t) {
+    uint64_t* dst = s_tile + (t & 1) * (kBqTile * NW);
+    float4* idst = s_info + (t & 1) * kBqTile;
+    const int64_t base_row = r0 + (int64_t)t * kBqTile;
+    for (int c = threadIdx.x; c < kChunks + kBqTile; c += kBqThreads) {
+      if (c < kChunks) {
+        const int row = c / (NW / 2);
+        const bool valid = (base_row + row) < r1;
+        cp_async16(dst + c * 2, valid ? db + base_row * NW + (int64_t)c * 2 : db, valid);
+      } else {
+        const int row = c - kChunks;
+        const bool valid = (base_row + row) < r1;
+        cp_async16(idst + row, valid ? rowinfo + base_row + row : rowinfo, valid);
+      }
+    }
+  };
+
+  if (ntiles > 0) stage(0);
+  cp_async_commit();
+  for (int t = 0; t < ntiles; t++) {
+    if (t + 1 < ntiles) stage(t + 1);
+    cp_async_commit();
+    cp_async_wait1();
+    __syncthreads();
+    const uint64_t* T = s_tile + (t & 1) * (kBqTile * NW);
+    const float4* I = s_info + (t & 1) * kBqTile;
+    const int64_t base_row = r0 + (int64_t)t * kBqTile;
+    const int rows = (int)((r1 - base_row) < kBqTile ? (r1 - base_row) : kBqTile);
+    for (int qb = 0; qb < nq; qb += kBqThreads) {
+      const int q = qb + threadIdx.x;
+      const bool active = q < nq;
+      uint64_t qp[4][NW];
+#pragma unroll
+      for (int b = 0; b < 4; b++)
+#pragma unroll
+        for (int w = 0; w < NW; w++) qp[b][w] = active ? planes[((size_t)q * 4 + b) * NW + w] : 0ull;
+      const BbqQuery qi = active ? qinfo[q] : BbqQuery{};
+      const size_t sidx = (size_t)part * nq + (active ? q : 0);
+      LaneStream st;
+      st.base = bufs + sidx * (size_t)C;
+      st.cnt = active ? cnts[sidx] : 0u;
+      st.thr = active ? thrs[sidx] : ~0ull;
+      for (int rr = 0; rr < rows; rr += 32) {
+        const int re = (rr + 32 < rows) ? rr + 32 : rows;
+        for (int r = rr; r < re; r++) {
+          const uint64_t* row = T + r * NW;
+          int32_t raw = 0;
+#pragma unroll
+          for (int b = 0; b < 4; b++) {
+            int32_t s = 0;
+#pragma unroll
+            for (int w = 0; w < NW; w++) s += __popcll(row[w] & qp[b][w]);
+            raw += s << b;
+          }
+          if (active) st.offer(float_key(bbq_score(metric, qi, I[r], raw, dim), (uint32_t)(base_row + r)));
+        }
+        warp_compact_lanes<R>(st.cnt > (uint32_t)(C - 32), st.base, st.cnt, st.thr, (uint32_t)K);
+      }
+      if (active) {
+        cnts[sidx] = st.cnt;
+        thrs[sidx] = st.thr;
+      }
+    }
+    __syncthreads();
+  }
+  for (int qb = 0; qb < nq; qb += kBqThreads) {
+    const int q = qb + threadIdx.x;
+    const bool active = q < nq;
+    const size_t sidx = (size_t)part * nq + (active ? q : 0);
+    uint64_t* base = bufs + sidx * (size_t)C;
+    uint32_t cnt = active ? cnts[sidx] : 0u;
+    uint64_t thr = active ? thrs[sidx] : ~0ull;
+    warp_compact_lanes<R>(cnt > (uint32_t)K, base, cnt, thr, (uint32_t)K);
+    if (active) cnts[sidx] = cnt;
+  }
+}
+
+// Per-row staging record: (|v - c|^2, vl, width, popcount of the bits as int bits).
+__global__ void bbq_rowinfo_kernel(const uint64_t* __restrict__ words, int nw, int nw_pad, const float* __restrict__ corr,
+                                   int64_t n, float4* __restrict__ out) {
+  const int64_t r = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (r >= n) return;
+  int32_t pop = 0;
+  for (int w = 0; w < nw; w++) pop += __popcll(words[r * nw_pad + w]);  // BitCounts.popcount
+  out[r] = make_float4(corr[r * 3], corr[r * 3 + 1], corr[r * 3 + 2], __int_as_float(pop));
+}
+
+template <int NW>
+cudaError_t launch_bbq_nw(const uint64_t* db, const float4* rowinfo, int64_t n, int dim, int metric,
+                          const uint64_t* planes, const BbqQuery* qinfo, int nq, int parts, const StreamGeom& g,
+                          uint64_t* bufs, uint32_t* cnts, uint64_t* thrs, cudaStream_t st) {
+  const int64_t rows_per_part = (n + parts - 1) / parts;
+  const size_t smem = 2ull * kBqTile * NW * sizeof(uint64_t) + 2ull * kBqTile * sizeof(float4);
+#define VX_BBQ_CASE(RR)                                                                             \
+  case RR: {                                                                                        \
+    auto kern = bbq_scan_kernel<NW, RR>;                                                            \
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); \
+    if (e != cudaSuccess) return e;                                                                 \
+    kern<<<parts, kBqThreads, smem, st>>>(db, rowinfo, n, dim, metric, planes, qinfo, nq, rows_per_part, g.K, g.C, \
+                                          bufs, cnts, thrs);                                        \
+    return cudaGetLastError();                                                                      \
+  }
+  switch (g.R) {
+    VX_BBQ_CASE(2)
+    VX_BBQ_CASE(3)
+    VX_BBQ_CASE(5)
+    VX_BBQ_CASE(9)
+    VX_BBQ_CASE(17)
+    VX_BBQ_CASE(33)
+    default: return cudaErrorInvalidValue;
+  }
+#undef VX_BBQ_CASE
+}
+
 }  // namespace
 
 int bq_padded_words(int nw) {
@@ -176,6 +395,34 @@ cudaError_t launch_bq_scan(const uint64_t* db, int64_t n, int nw_pad, const uint
     case 8: return launch_nw<8>(db, n, qw, nq, parts, g, bufs, cnts, thrs, st);
     case 16: return launch_nw<16>(db, n, qw, nq, parts, g, bufs, cnts, thrs, st);
     case 32: return launch_nw<32>(db, n, qw, nq, parts, g, bufs, cnts, thrs, st);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+cudaError_t launch_bbq_prep_queries(const float* q, int nq, int dim, const float* centroid, int nw_pad,
+                                    uint64_t* planes, BbqQuery* info, cudaStream_t st) {
+  if (nq <= 0) return cudaSuccess;
+  bbq_prep_queries_kernel<<<(nq + 127) / 128, 128, 0, st>>>(q, nq, dim, centroid, nw_pad, planes, info);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_bbq_rowinfo(const uint64_t* words, int nw, int nw_pad, const float* corr, int64_t n, float4* out,
+                               cudaStream_t st) {
+  if (n <= 0) return cudaSuccess;
+  bbq_rowinfo_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(words, nw, nw_pad, corr, n, out);
+  return cudaGetLastError();
+}
+
+bool bbq_supported(int nw_pad) { return nw_pad >= 2 && nw_pad <= 16; }
+
+cudaError_t launch_bbq_scan(const uint64_t* db, const float4* rowinfo, int64_t n, int nw_pad, int dim, int metric,
+                            const uint64_t* planes, const BbqQuery* qinfo, int nq, int parts, const StreamGeom& g,
+                            uint64_t* bufs, uint32_t* cnts, uint64_t* thrs, cudaStream_t st) {
+  switch (nw_pad) {
+    case 2: return launch_bbq_nw<2>(db, rowinfo, n, dim, metric, planes, qinfo, nq, parts, g, bufs, cnts, thrs, st);
+    case 4: return launch_bbq_nw<4>(db, rowinfo, n, dim, metric, planes, qinfo, nq, parts, g, bufs, cnts, thrs, st);
+    case 8: return launch_bbq_nw<8>(db, rowinfo, n, dim, metric, planes, qinfo, nq, parts, g, bufs, cnts, thrs, st);
+    case 16: return launch_bbq_nw<16>(db, rowinfo, n, dim, metric, planes, qinfo, nq, parts, g, bufs, cnts, thrs, st);
     default: return cudaErrorInvalidValue;
   }
 }

@@ -158,8 +158,8 @@ int parse_quantized(const uint8_t* bytes, int64_t len, QuantizedFile& f) {
 }
 
 int unsupported_kind(const QuantizedFile& f) {
-  if (f.kind == kBq && f.bq_mode == 1)
-    return failf(VX_ERR_UNSUPPORTED, "quantized.bin BQ in BBQ mode is not served here (SIGN_BIT is)");
+  if (f.kind == kBq && f.bq_mode == 1 && f.dim > 1024)
+    return failf(VX_ERR_UNSUPPORTED, "quantized.bin BQ in BBQ mode is served up to 1024 dimensions, not %d", f.dim);
   if (f.kind != kSq8 && f.kind != kSq4 && f.kind != kBq && f.kind != kFp16)
     return failf(VX_ERR_UNSUPPORTED, "quantized.bin kind %s is not served here (SQ8, SQ4, BQ SIGN_BIT and FP16 are)",
                  kKindNames[f.kind]);
@@ -353,6 +353,21 @@ int vx_quantized_bin_build(int32_t device, const uint8_t* bytes, int64_t len, in
         std::memcpy(&corr[i], r + nb, 4);
       }
       return vx_sq4_build(device, packed.data(), corr.data(), (int64_t)n, f.dim, f.min_q, f.max_q, metric, vectors,
+                          row_stride, out);
+    }
+    if (f.kind == kBq && f.bq_mode == 1) {
+      // BBQ: the centroid after the mode ordinal, then (words, 3 corrections) per vector
+      const size_t nw = (d + 63) / 64;
+      std::vector<float> cent(d);
+      std::memcpy(cent.data(), bytes + kQuantizedHeader + 4, d * 4);
+      std::vector<uint64_t> words(n * nw);
+      std::vector<float> corr(n * 3);
+      for (size_t i = 0; i < n; i++) {
+        const uint8_t* r = data + i * (nw * 8 + 12);
+        std::memcpy(&words[i * nw], r, nw * 8);
+        std::memcpy(&corr[i * 3], r + nw * 8, 12);
+      }
+      return vx_bbq_build(device, words.data(), corr.data(), cent.data(), (int64_t)n, f.dim, metric, vectors,
                           row_stride, out);
     }
     if (f.kind == kBq) {

@@ -37,6 +37,9 @@ struct vx_index {
   // BQ
   uint64_t* words = nullptr;
   int nw_pad = 0;
+  // BBQ: the quantizer's centroid, per-row (|v - c|^2, vl, width, popcount) records
+  float* bbq_centroid = nullptr;
+  float4* bbq_rows = nullptr;
   // IVF-PQ
   float* cent = nullptr;
   int nlist = 0;

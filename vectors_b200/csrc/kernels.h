@@ -83,4 +83,19 @@ cudaError_t launch_bq_scan(const uint64_t* db, int64_t n, int nw_pad, const uint
 cudaError_t launch_bq_pack_queries(const float* q, int nq, int dim, int nw_pad, uint64_t* out,
                                    cudaStream_t st);
 
+// BBQ (BinaryQuantizedVectors.java:110-275): per-query terms of bbqScoreFunction, 4 bit planes
+// [nq][4][nw_pad] of the 4-bit query; per-row (|v - c|^2, vl, width, popcount) records.
+struct BbqQuery {
+  float qmin, w15, nsq, norm;  // queryMin, queryWidth / 15, queryNormSq, queryNorm
+  int32_t qsum, pad0, pad1, pad2;
+};
+bool bbq_supported(int nw_pad);  // up to 1024 dimensions
+cudaError_t launch_bbq_prep_queries(const float* q, int nq, int dim, const float* centroid, int nw_pad,
+                                    uint64_t* planes, BbqQuery* info, cudaStream_t st);
+cudaError_t launch_bbq_rowinfo(const uint64_t* words, int nw, int nw_pad, const float* corr, int64_t n, float4* out,
+                               cudaStream_t st);
+cudaError_t launch_bbq_scan(const uint64_t* db, const float4* rowinfo, int64_t n, int nw_pad, int dim, int metric,
+                            const uint64_t* planes, const BbqQuery* qinfo, int nq, int parts, const StreamGeom& g,
+                            uint64_t* bufs, uint32_t* cnts, uint64_t* thrs, cudaStream_t st);
+
 }  // namespace vx

@@ -734,7 +734,9 @@ int search_quantized_scan(vx_index* ix, const float* dq, int nq, int K, int k_ou
     qch = std::max<int64_t>(256, qch / 256 * 256);
     // sized once for the largest chunk and reused by every chunk
     const int qmax = (int)std::min<int64_t>(qch, std::max(nq, 1));
-    uint64_t* qw = S.alloc<uint64_t>((size_t)qmax * ix->nw_pad);
+    const bool bbq = ix->kind == VX_KIND_BBQ;
+    uint64_t* qw = S.alloc<uint64_t>((size_t)qmax * ix->nw_pad * (bbq ? 4 : 1));
+    BbqQuery* qinfo = bbq ? S.alloc<BbqQuery>(qmax) : nullptr;
     uint64_t* bufs = S.alloc<uint64_t>((size_t)parts * qmax * g.C);
     uint32_t* cnts = S.alloc<uint32_t>((size_t)parts * qmax);
     uint64_t* thrs = S.alloc<uint64_t>((size_t)parts * qmax);
@@ -745,10 +747,18 @@ int search_quantized_scan(vx_index* ix, const float* dq, int nq, int K, int k_ou
     for (int q0 = 0; q0 < nq; q0 += (int)qch) {
       const int qc = (int)std::min<int64_t>(qch, nq - q0);
       const float* dqc = dq + (size_t)q0 * dim;
-      VX_LAUNCH(1, launch_bq_pack_queries(dqc, qc, dim, ix->nw_pad, qw, st));
       VX_CUDA(cudaMemsetAsync(cnts, 0, (size_t)parts * qc * 4, st));
       VX_CUDA(cudaMemsetAsync(thrs, 0, (size_t)parts * qc * 8, st));
-      VX_TIMED(VX_PROF_BQ_SCAN, st, 1, launch_bq_scan(ix->words, ix->n, ix->nw_pad, qw, qc, parts, g, bufs, cnts, thrs, st));
+      if (bbq) {
+        VX_LAUNCH(1, launch_bbq_prep_queries(dqc, qc, dim, ix->bbq_centroid, ix->nw_pad, qw, qinfo, st));
+        VX_TIMED(VX_PROF_BQ_SCAN, st, 1,
+                 launch_bbq_scan(ix->words, ix->bbq_rows, ix->n, ix->nw_pad, dim, ix->metric, qw, qinfo, qc, parts, g,
+                                 bufs, cnts, thrs, st));
+      } else {
+        VX_LAUNCH(1, launch_bq_pack_queries(dqc, qc, dim, ix->nw_pad, qw, st));
+        VX_TIMED(VX_PROF_BQ_SCAN, st, 1,
+                 launch_bq_scan(ix->words, ix->n, ix->nw_pad, qw, qc, parts, g, bufs, cnts, thrs, st));
+      }
       VX_LAUNCH(1, launch_merge_streams(bufs, cnts, parts, qc, qc, g.C, K, keys, kcnt, st));
       if (rescore) {
         RescoreArgs r{};
@@ -772,7 +782,7 @@ int search_quantized_scan(vx_index* ix, const float* dq, int nq, int K, int k_ou
         r.flag_list = flag_list;
         VX_LAUNCH(1, launch_rescore(r, false, st));
       } else {
-        VX_LAUNCH(1, launch_finish_keys(keys, kcnt, qc, K, k_out, kFinishHamming, ix->metric, dim,
+        VX_LAUNCH(1, launch_finish_keys(keys, kcnt, qc, K, k_out, bbq ? kFinishFloatKey : kFinishHamming, ix->metric, dim,
                                         d_ids + (size_t)q0 * k_out, d_scores + (size_t)q0 * k_out,
                                         d_counts + q0, st));
       }
@@ -1122,7 +1132,8 @@ int search_batch_dev(vx_index* ix, const float* dq, int nq, int dim, int k, int 
     case VX_KIND_FP16:
     case VX_KIND_SQ8:
     case VX_KIND_SQ4:
-    case VX_KIND_BQ: {
+    case VX_KIND_BQ:
+    case VX_KIND_BBQ: {
       if (!ix->rows32)
         return fail(VX_ERR_UNSUPPORTED,
                     "searchBatch on a quantized index needs the full-precision vectors at build; "
@@ -1443,6 +1454,58 @@ int sq_build(int32_t device, const int8_t* codes, const float* corrections, int6
 
 extern "C" {
 
+int vx_bbq_build(int32_t device, const uint64_t* words, const float* corrections, const float* centroid, int64_t n,
+                 int32_t dim, int32_t metric, const float* vectors, int64_t row_stride, vx_index** out) {
+  return guarded([&]() -> int {
+    if (!out) return fail(VX_ERR_NULL_POINTER, "out must not be null");
+    *out = nullptr;
+    if (!centroid) return fail(VX_ERR_NULL_POINTER, "centroid must not be null");
+    if (n > 0 && (!words || !corrections)) return fail(VX_ERR_NULL_POINTER, "words/corrections must not be null");
+    if (n < 0 || n > INT32_MAX) return fail(VX_ERR_INVALID_ARGUMENT, "bad vector count");
+    if (dim <= 0) return fail(VX_ERR_INVALID_ARGUMENT, "bad dimension %d", dim);
+    const int nw = (dim + 63) / 64;
+    const int nwp = bq_padded_words(nw);
+    if (nwp < 0 || !bbq_supported(nwp)) return fail(VX_ERR_UNSUPPORTED, "BBQ dimension %d exceeds 1024", dim);
+    if (vectors && row_stride < dim) return fail(VX_ERR_INVALID_ARGUMENT, "bad row stride");
+    if (int s = check_metric(metric)) return s;
+    int nsms = 0;
+    if (int s = check_device(device, &nsms)) return s;
+    vx_index* ix = new vx_index();
+    ix->kind = VX_KIND_BBQ;
+    ix->device = device;
+    ix->metric = metric;
+    ix->n = n;
+    ix->dim = dim;
+    ix->num_sms = nsms;
+    ix->nw_pad = nwp;
+    try {
+      ix->bbq_centroid = dev_alloc<float>(ix, (size_t)dim);
+      VX_CUDA(cudaMemcpy(ix->bbq_centroid, centroid, (size_t)dim * 4, cudaMemcpyDefault));
+      if (n > 0) {
+        ix->words = dev_alloc<uint64_t>(ix, (size_t)n * nwp);
+        VX_CUDA(cudaMemset(ix->words, 0, (size_t)n * nwp * 8));
+        VX_CUDA(cudaMemcpy2D(ix->words, (size_t)nwp * 8, words, (size_t)nw * 8, (size_t)nw * 8, (size_t)n,
+                             cudaMemcpyDefault));
+        float* corr = nullptr;
+        VX_CUDA(cudaMalloc(&corr, (size_t)n * 12));
+        cudaError_t e = cudaMemcpy(corr, corrections, (size_t)n * 12, cudaMemcpyDefault);
+        ix->bbq_rows = dev_alloc<float4>(ix, (size_t)n);
+        if (e == cudaSuccess) e = launch_bbq_rowinfo(ix->words, nw, nwp, corr, n, ix->bbq_rows, 0);
+        if (e == cudaSuccess) e = cudaDeviceSynchronize();
+        cudaFree(corr);
+        VX_CUDA(e);
+        g_launches.fetch_add(1);
+        if (vectors) ix->rows32 = upload_rows32(ix, vectors, n, dim, row_stride);
+      }
+    } catch (...) {
+      free_index(ix);
+      throw;
+    }
+    *out = ix;
+    return VX_OK;
+  });
+}
+
 int vx_bq_build(int32_t device, const uint64_t* words, int64_t n, int32_t dim, int32_t metric,
                 const float* vectors, int64_t row_stride, vx_index** out) {
   return guarded([&]() -> int {
@@ -1705,7 +1768,8 @@ int vx_search_batch(vx_index* ix, const float* queries, int32_t nq, int32_t dim,
 
 static int scan_candidates_dev(vx_index* ix, const float* dq, int nq, int dim, int k, int32_t* di,
                                float* ds, int32_t* dc, cudaStream_t st) {
-  if (ix->kind != VX_KIND_SQ8 && ix->kind != VX_KIND_SQ4 && ix->kind != VX_KIND_BQ && ix->kind != VX_KIND_FP16)
+  if (ix->kind != VX_KIND_SQ8 && ix->kind != VX_KIND_SQ4 && ix->kind != VX_KIND_BQ && ix->kind != VX_KIND_BBQ &&
+      ix->kind != VX_KIND_FP16)
     return fail(VX_ERR_UNSUPPORTED, "candidate scans apply to SQ8, BQ and FP16 indexes");
   if (ix->n == 0) {
     fill_empty(nq, k, di, ds, dc, st);

@@ -354,6 +354,21 @@ class QuantizedFlatScanAdapter(IndexSpi):
         _check(N.lib().vx_bq_build(self.device, _ptr(words), n, dim, int(metric), _ptr(v), dim, C.byref(self._h.ptr)))
         self._n, self._dim, self.metric, self.kind = n, dim, SimilarityFunction(metric), "BQ"
 
+    def build_bbq(self, words, corrections, centroid, dim: int, metric, vectors=None):
+        """BinaryQuantizedVectors in BBQ mode: centroid-relative sign bits [n][ceil(dim/64)],
+        corrections [n][3] = (|v - c|^2, vl, width), the quantizer's centroid."""
+        words = np.ascontiguousarray(np.asarray(words, dtype=np.uint64))
+        corr = np.ascontiguousarray(np.asarray(corrections, dtype=np.float32))
+        cent = np.ascontiguousarray(np.asarray(centroid, dtype=np.float32))
+        v = None if vectors is None else _as_matrix(vectors, "vectors")
+        n = words.shape[0]
+        if corr.shape != (n, 3) or cent.shape != (dim,):
+            raise IllegalArgumentException("corrections must be [n][3] and the centroid [dim]")
+        self._h.close()
+        _check(N.lib().vx_bbq_build(self.device, _ptr(words), _ptr(corr), _ptr(cent), n, dim, int(metric), _ptr(v), dim,
+                                    C.byref(self._h.ptr)))
+        self._n, self._dim, self.metric, self.kind = n, dim, SimilarityFunction(metric), "BBQ"
+
     def build_fp16(self, codes, metric, vectors=None):
         """codes: [n][dim] binary16 bit patterns (numpy uint16, or a CUDA float16 / int16 tensor,
         copied on the device)."""
@@ -374,7 +389,7 @@ class QuantizedFlatScanAdapter(IndexSpi):
 
     def load_quantized_bin(self, data, metric, vectors=None):
         """Opens a persistent quantized.bin (QuantizedVectorsCodec.decode) as this adapter's index:
-        SQ8, SQ4, BQ SIGN_BIT or FP16.  ``vectors`` are the fp32 rows for the two-pass rescore (a mapped
+        SQ8, SQ4, BQ (SIGN_BIT or BBQ) or FP16.  ``vectors`` are the fp32 rows for the two-pass rescore (a mapped
         vectors.bin view with its 64-byte row stride is taken as is)."""
         b = _file_bytes(data)
         kind, dim, n = quantized_bin_info(b)
@@ -384,6 +399,11 @@ class QuantizedFlatScanAdapter(IndexSpi):
                                               C.byref(self._h.ptr)))
         self._n, self._dim, self.metric = n, dim, SimilarityFunction(metric)
         self.kind = {1: "SQ8", 2: "SQ4", 4: "BQ", 8: "FP16"}[kind]
+        if kind == 4:  # SIGN_BIT or BBQ: the index knows
+            built = C.c_int32()
+            _check(N.lib().vx_index_info(self._h.ptr, C.byref(built), None, None, None))
+            if built.value == N.VX_KIND_BBQ:
+                self.kind = "BBQ"
 
     def build(self, vectors, metric):
         raise UnsupportedOperationException("QuantizedFlatScanAdapter wraps an already-built flat index")
