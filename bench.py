@@ -248,6 +248,7 @@ def main():
     ap.add_argument("--ivfflat-n", type=int, default=IVFFLAT["n"])
     ap.add_argument("--sq8-n", type=int, default=SQ8["n"], help="smaller cases for profiling")
     ap.add_argument("--bq-n", type=int, default=BQ["n"])
+    ap.add_argument("--bbq-n", type=int, default=1_000_000, help="rows per GPU of the BBQ scan")
     ap.add_argument("--fp16-n", type=int, default=FP16["n_per_gpu"], help="rows per GPU")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--ivf-n", type=int, default=IVF["n"])
@@ -765,6 +766,11 @@ def run_bq(args, rank, world, local, dev, barrier, max_over_ranks, tc_sustained,
         return (b * weights).sum(2)
 
     words = torch.empty((hi - lo, dim // 64), dtype=torch.int64, device=dev)
+    # BBQ on this rank's first rows: centroid-relative bits and (|v - c|^2, vl, width)
+    nb = min(hi - lo, args.bbq_n)
+    bbq_c = cent.mean(0)
+    bbq_words = torch.empty((nb, dim // 64), dtype=torch.int64, device=dev)
+    bbq_corr = torch.empty((nb, 3), dtype=torch.float32, device=dev)
     for s0 in range(lo, hi, 1 << 18):
         s1 = min(hi, s0 + (1 << 18))
         gc = torch.Generator(device=dev)
@@ -772,6 +778,13 @@ def run_bq(args, rank, world, local, dev, barrier, max_over_ranks, tc_sustained,
         comp = torch.randint(0, P["comps"], (s1 - s0,), generator=gc, device=dev)
         x = cent[comp] + P["sigma"] * torch.randn((s1 - s0, dim), generator=gc, device=dev)
         words[s0 - lo: s1 - lo] = pack(x)
+        if s0 - lo < nb:
+            e = min(s1 - lo, nb) - (s0 - lo)
+            xc = x[:e] - bbq_c
+            bbq_words[s0 - lo: s0 - lo + e] = pack(xc)
+            bbq_corr[s0 - lo: s0 - lo + e, 0] = (xc * xc).sum(1)
+            bbq_corr[s0 - lo: s0 - lo + e, 1] = xc.min(1).values
+            bbq_corr[s0 - lo: s0 - lo + e, 2] = xc.max(1).values - xc.min(1).values
     gq = torch.Generator(device=dev)
     gq.manual_seed(0xB2)
     comp = torch.randint(0, P["comps"], (nq,), generator=gq, device=dev)
@@ -804,10 +817,31 @@ def run_bq(args, rank, world, local, dev, barrier, max_over_ranks, tc_sustained,
         roof = {"bound": "integer pipe (xor + popc)", "achieved": achieved, "unit": "T word-compares/s",
                 "peak": None, "frac": None, "kernel": "bq_scan_kernel"}
     roof.update({"per": "GPU", "traffic": None, "breakdown_ms_per_step": br})
+    # BBQ (BinaryMode.BBQ): 4-bit query planes against the sign bits, popcount kernel
+    b = vx.QuantizedFlatScanAdapter(device=local)
+    b.build_bbq(bbq_words.cpu().numpy().view(np.uint64), bbq_corr.cpu().numpy(), bbq_c.cpu().numpy(), dim,
+                vx.SimilarityFunction.DOT_PRODUCT)
+    del bbq_words, bbq_corr
+
+    def bstep():
+        ids, sc, cnt = b.scan_candidates_device(q, k)
+        return ids if world == 1 else gather_and_merge(ids, sc, cnt, offs, k)[0]
+
+    bms_step, bkms, bbr = _timed_scan(args, world, dev, barrier, max_over_ranks, bstep, "bq_scan")
+    b.close()
+    bwork = 4.0 * nq * nb * (dim // 64)  # AND + popcount of a 64-bit word per plane
+    bach = bwork / (bkms / 1e3) / 1e12 if bkms > 0 else None
+    bbq = {"value": nq / (bms_step / 1e3), "unit": "queries/s", "ms_per_step": bms_step,
+           "config": {"workload": f"BBQ candidate scan n={nb * world:,} x {dim} bits (4-bit queries) "
+                                  f"queries={nq:,} k={k}"},
+           "roofline": {"bound": "integer pipe (and + popc)", "achieved": bach, "unit": "T word-plane ops/s",
+                        "peak": None, "frac": None, "kernel": "bbq_scan_kernel", "per": "GPU",
+                        "breakdown_ms_per_step": bbr}}
     return {
         "value": nq / (ms / 1e3), "unit": "queries/s", "ms_per_step": ms,
         "config": {"workload": f"BQ sign-bit Hamming candidate scan n={n:,} x {dim} bits queries={nq:,} k={k}"},
         "roofline": roof,
+        "bbq": bbq,
     }
 
 
