@@ -213,6 +213,38 @@ __global__ void bbq_prep_queries_kernel(const float* __restrict__ q, int nq, int
   info[qi] = o;
 }
 
+// Carry-save adder of three words: l holds the bitwise sum, h the carries (weight 2).
+__device__ __forceinline__ void csa(uint64_t& h, uint64_t& l, uint64_t a, uint64_t b, uint64_t c) {
+  const uint64_t u = a ^ b;
+  h = (a & b) | (u & c);
+  l = u ^ c;
+}
+
+// sum_w popcount(x[w] & p[w]) over 16 words through a Harley-Seal carry-save tree: the words are
+// added bitwise into ones / twos / fours / eights / sixteens (cheap logic operations), so five
+// popcounts replace sixteen on the slow population-count pipe; the integer is the same.
+__device__ __forceinline__ int32_t popc_and16(const uint64_t* x, const uint64_t (&p)[16]) {
+  uint64_t ones = 0, twos = 0, fours = 0, eights = 0, sixteens;
+  uint64_t twos_a, twos_b, fours_a, fours_b, eights_a, eights_b;
+  csa(twos_a, ones, ones, x[0] & p[0], x[1] & p[1]);
+  csa(twos_b, ones, ones, x[2] & p[2], x[3] & p[3]);
+  csa(fours_a, twos, twos, twos_a, twos_b);
+  csa(twos_a, ones, ones, x[4] & p[4], x[5] & p[5]);
+  csa(twos_b, ones, ones, x[6] & p[6], x[7] & p[7]);
+  csa(fours_b, twos, twos, twos_a, twos_b);
+  csa(eights_a, fours, fours, fours_a, fours_b);
+  csa(twos_a, ones, ones, x[8] & p[8], x[9] & p[9]);
+  csa(twos_b, ones, ones, x[10] & p[10], x[11] & p[11]);
+  csa(fours_a, twos, twos, twos_a, twos_b);
+  csa(twos_a, ones, ones, x[12] & p[12], x[13] & p[13]);
+  csa(twos_b, ones, ones, x[14] & p[14], x[15] & p[15]);
+  csa(fours_b, twos, twos, twos_a, twos_b);
+  csa(eights_b, fours, fours, fours_a, fours_b);
+  csa(sixteens, eights, eights, eights_a, eights_b);
+  return 16 * __popcll(sixteens) + 8 * __popcll(eights) + 4 * __popcll(fours) + 2 * __popcll(twos) +
+         __popcll(ones);
+}
+
 // Score of one (query, row): computeBbqDot then the metric's transform (:155-225).
 __device__ __forceinline__ float bbq_score(int metric, const BbqQuery& qi, float4 ri, int32_t raw, int dim) {
   const float dist_c = ri.x, vl = ri.y, width = ri.z;
@@ -229,13 +261,13 @@ __device__ __forceinline__ float bbq_score(int metric, const BbqQuery& qi, float
       const float vn = (float)sqrt((double)dist_c);
       if (qi.norm == 0.0f || vn == 0.0f) return 0.0f;
       const float cosv = __fdiv_rn(approx, __fmul_rn(qi.norm, vn));
-      const float s = __fdiv_rn(__fadd_rn(1.0f, cosv), 2.0f);
+      const float s = __fmul_rn(__fadd_rn(1.0f, cosv), 0.5f);  // x / 2f, the same rounding
       return s > 0.0f ? s : 0.0f;
     }
     case kMaxInnerProduct:
       return scale_mip(approx);
     default: {
-      const float s = __fdiv_rn(__fadd_rn(1.0f, approx), 2.0f);
+      const float s = __fmul_rn(__fadd_rn(1.0f, approx), 0.5f);  // (1f + approxDot) / 2f
       return s > 0.0f ? s : 0.0f;
     }
   }
@@ -274,31 +306,34 @@ __global__ void __launch_bounds__(kBqThreads, 1)  // the 4 query planes stay in 
     }
   };
 
-  if (ntiles > 0) stage(0);
-  cp_async_commit();
-  for (int t = 0; t < ntiles; t++) {
-    if (t + 1 < ntiles) stage(t + 1);
+  // Query chunks outermost: a thread keeps its query's planes and stream in registers while the
+  // part's rows stream past (re-reading the rows per chunk is cheaper than the planes per tile).
+  for (int qb = 0; qb < nq; qb += kBqThreads) {
+    const int q = qb + threadIdx.x;
+    const bool active = q < nq;
+    uint64_t qp[4][NW];
+#pragma unroll
+    for (int b = 0; b < 4; b++)
+#pragma unroll
+      for (int w = 0; w < NW; w++) qp[b][w] = active ? planes[((size_t)q * 4 + b) * NW + w] : 0ull;
+    const BbqQuery qi = active ? qinfo[q] : BbqQuery{};
+    const size_t sidx = (size_t)part * nq + (active ? q : 0);
+    LaneStream st;
+    st.base = bufs + sidx * (size_t)C;
+    st.cnt = 0u;
+    st.thr = active ? 0ull : ~0ull;
+    __syncthreads();  // the previous chunk is done with both staging buffers
+    if (ntiles > 0) stage(0);
     cp_async_commit();
-    cp_async_wait1();
-    __syncthreads();
-    const uint64_t* T = s_tile + (t & 1) * (kBqTile * NW);
-    const float4* I = s_info + (t & 1) * kBqTile;
-    const int64_t base_row = r0 + (int64_t)t * kBqTile;
-    const int rows = (int)((r1 - base_row) < kBqTile ? (r1 - base_row) : kBqTile);
-    for (int qb = 0; qb < nq; qb += kBqThreads) {
-      const int q = qb + threadIdx.x;
-      const bool active = q < nq;
-      uint64_t qp[4][NW];
-#pragma unroll
-      for (int b = 0; b < 4; b++)
-#pragma unroll
-        for (int w = 0; w < NW; w++) qp[b][w] = active ? planes[((size_t)q * 4 + b) * NW + w] : 0ull;
-      const BbqQuery qi = active ? qinfo[q] : BbqQuery{};
-      const size_t sidx = (size_t)part * nq + (active ? q : 0);
-      LaneStream st;
-      st.base = bufs + sidx * (size_t)C;
-      st.cnt = active ? cnts[sidx] : 0u;
-      st.thr = active ? thrs[sidx] : ~0ull;
+    for (int t = 0; t < ntiles; t++) {
+      if (t + 1 < ntiles) stage(t + 1);
+      cp_async_commit();
+      cp_async_wait1();
+      __syncthreads();
+      const uint64_t* T = s_tile + (t & 1) * (kBqTile * NW);
+      const float4* I = s_info + (t & 1) * kBqTile;
+      const int64_t base_row = r0 + (int64_t)t * kBqTile;
+      const int rows = (int)((r1 - base_row) < kBqTile ? (r1 - base_row) : kBqTile);
       for (int rr = 0; rr < rows; rr += 32) {
         const int re = (rr + 32 < rows) ? rr + 32 : rows;
         for (int r = rr; r < re; r++) {
@@ -306,31 +341,26 @@ __global__ void __launch_bounds__(kBqThreads, 1)  // the 4 query planes stay in 
           int32_t raw = 0;
 #pragma unroll
           for (int b = 0; b < 4; b++) {
-            int32_t s = 0;
+            int32_t sb = 0;
+            if constexpr (NW == 16) {
+              sb = popc_and16(row, qp[b]);
+            } else {
 #pragma unroll
-            for (int w = 0; w < NW; w++) s += __popcll(row[w] & qp[b][w]);
-            raw += s << b;
+              for (int w = 0; w < NW; w++) sb += __popcll(row[w] & qp[b][w]);
+            }
+            raw += sb << b;
           }
           if (active) st.offer(float_key(bbq_score(metric, qi, I[r], raw, dim), (uint32_t)(base_row + r)));
         }
         warp_compact_lanes<R>(st.cnt > (uint32_t)(C - 32), st.base, st.cnt, st.thr, (uint32_t)K);
       }
-      if (active) {
-        cnts[sidx] = st.cnt;
-        thrs[sidx] = st.thr;
-      }
+      __syncthreads();  // every thread is done with this buffer before it is refilled
     }
-    __syncthreads();
-  }
-  for (int qb = 0; qb < nq; qb += kBqThreads) {
-    const int q = qb + threadIdx.x;
-    const bool active = q < nq;
-    const size_t sidx = (size_t)part * nq + (active ? q : 0);
-    uint64_t* base = bufs + sidx * (size_t)C;
-    uint32_t cnt = active ? cnts[sidx] : 0u;
-    uint64_t thr = active ? thrs[sidx] : ~0ull;
-    warp_compact_lanes<R>(cnt > (uint32_t)K, base, cnt, thr, (uint32_t)K);
-    if (active) cnts[sidx] = cnt;
+    warp_compact_lanes<R>(st.cnt > (uint32_t)K, st.base, st.cnt, st.thr, (uint32_t)K);
+    if (active) {
+      cnts[sidx] = st.cnt;
+      thrs[sidx] = st.thr;
+    }
   }
 }
 
