@@ -665,7 +665,7 @@ def run_ivfflat(args, rank, world, local, dev, barrier, max_over_ranks, peak_kin
     achieved = ops / (kms / 1e3) / 1e12 if kms > 0 else None
     peak = 148 * 128 * 1.965e9 / 1e12  # fp32 lanes x max SM clock, as instructions
     cpu = None
-    if rank == 0 and not args.no_cpu:
+    if rank == 0 and world == 1 and not args.no_cpu:  # the CPU baseline is a 1-GPU figure
         from oracle import oracle as O
 
         th = os.cpu_count() or 1
