@@ -835,6 +835,34 @@ __device__ __forceinline__ void flat_stage(float* s_q, float* s_c, const FlatLis
   cp_async_commit();
 }
 
+// One staged 64-dim chunk into the accumulators of the first NU 16-query slices (the rest of
+// the group's 64 slots hold no pair), routing's 8-lane batched arithmetic on packed lane pairs.
+template <bool kL2, int NU>
+__device__ __forceinline__ void flat_chunk(const float* sq, const float* sc, int tq, int tc, uint64_t (&acc)[4][2][4]) {
+#pragma unroll 4
+  for (int kk = 0; kk < kRtK; kk += 4) {
+    ulonglong2 qv[NU], cv[2];
+#pragma unroll
+    for (int u = 0; u < NU; u++) qv[u] = *reinterpret_cast<const ulonglong2*>(sq + (tq + 16 * u) * kRtStride + kk);
+#pragma unroll
+    for (int v = 0; v < 2; v++) cv[v] = *reinterpret_cast<const ulonglong2*>(sc + (tc + 16 * v) * kRtStride + kk);
+    const int pb = (kk & 4) >> 1;
+#pragma unroll
+    for (int u = 0; u < NU; u++)
+#pragma unroll
+      for (int v = 0; v < 2; v++) {
+        if (kL2) {
+          const uint64_t d0 = f2_sub(qv[u].x, cv[v].x), d1 = f2_sub(qv[u].y, cv[v].y);
+          acc[u][v][pb] = f2_fma(d0, d0, acc[u][v][pb]);
+          acc[u][v][pb + 1] = f2_fma(d1, d1, acc[u][v][pb + 1]);
+        } else {
+          acc[u][v][pb] = f2_fma(qv[u].x, cv[v].x, acc[u][v][pb]);
+          acc[u][v][pb + 1] = f2_fma(qv[u].y, cv[v].y, acc[u][v][pb + 1]);
+        }
+      }
+  }
+}
+
 template <bool kL2, int R>
 __global__ void __launch_bounds__(256, 2) flat_list_kernel(FlatListArgs a) {
   extern __shared__ __align__(16) float s_flat[];
@@ -883,6 +911,7 @@ __global__ void __launch_bounds__(256, 2) flat_list_kernel(FlatListArgs a) {
     const int last = ((n - 1) / 64) * 64;
     const int tail_begin = last + ((n - last) & ~3);
     const float* rows = a.rows + (size_t)b * a.Dp;
+    const int nu = npq > 48 ? 4 : (npq + 15) / 16;  // 16-query slices holding pairs
     for (int r0 = 0; r0 < n; r0 += kRtC) {
       uint64_t acc[4][2][4];  // accumulator lanes (2p, 2p + 1) packed in acc[.][.][p]
 #pragma unroll
@@ -905,27 +934,17 @@ __global__ void __launch_bounds__(256, 2) flat_list_kernel(FlatListArgs a) {
           __syncthreads();
           const float* sq = s_flat + buf * kStage;
           const float* sc = sq + kRtQ * kRtStride;
-#pragma unroll 4
-          for (int kk = 0; kk < kRtK; kk += 4) {
-            ulonglong2 qv[4], cv[2];
-#pragma unroll
-            for (int u = 0; u < 4; u++) qv[u] = *reinterpret_cast<const ulonglong2*>(sq + (tq + 16 * u) * kRtStride + kk);
-#pragma unroll
-            for (int v = 0; v < 2; v++) cv[v] = *reinterpret_cast<const ulonglong2*>(sc + (tc + 16 * v) * kRtStride + kk);
-            const int pb = (kk & 4) >> 1;
-#pragma unroll
-            for (int u = 0; u < 4; u++)
-#pragma unroll
-              for (int v = 0; v < 2; v++) {
-                if (kL2) {
-                  const uint64_t d0 = f2_sub(qv[u].x, cv[v].x), d1 = f2_sub(qv[u].y, cv[v].y);
-                  acc[u][v][pb] = f2_fma(d0, d0, acc[u][v][pb]);
-                  acc[u][v][pb + 1] = f2_fma(d1, d1, acc[u][v][pb + 1]);
-                } else {
-                  acc[u][v][pb] = f2_fma(qv[u].x, cv[v].x, acc[u][v][pb]);
-                  acc[u][v][pb + 1] = f2_fma(qv[u].y, cv[v].y, acc[u][v][pb + 1]);
-                }
-              }
+          // only the 16-query slices that hold pairs of this group (the same for every thread);
+          // the dot-product instances keep all four (the extra variants would spill there)
+          if constexpr (kL2) {
+            switch (nu) {
+              case 1: flat_chunk<kL2, 1>(sq, sc, tq, tc, acc); break;
+              case 2: flat_chunk<kL2, 2>(sq, sc, tq, tc, acc); break;
+              case 3: flat_chunk<kL2, 3>(sq, sc, tq, tc, acc); break;
+              default: flat_chunk<kL2, 4>(sq, sc, tq, tc, acc); break;
+            }
+          } else {
+            flat_chunk<kL2, 4>(sq, sc, tq, tc, acc);
           }
           __syncthreads();  // every warp is done with this buffer before it is refilled
           buf ^= 1;
