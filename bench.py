@@ -817,7 +817,8 @@ def run_bq(args, rank, world, local, dev, barrier, max_over_ranks, tc_sustained,
         roof = {"bound": "integer pipe (xor + popc)", "achieved": achieved, "unit": "T word-compares/s",
                 "peak": None, "frac": None, "kernel": "bq_scan_kernel"}
     roof.update({"per": "GPU", "traffic": None, "breakdown_ms_per_step": br})
-    # BBQ (BinaryMode.BBQ): 4-bit query planes against the sign bits, popcount kernel
+    # BBQ (BinaryMode.BBQ): 4-bit queries against the centroid-relative sign bits; rawAsymDot on
+    # the int8 tensor cores (0/1 rows x 4-bit codes), or the popcount kernel without the operand
     b = vx.QuantizedFlatScanAdapter(device=local)
     b.build_bbq(bbq_words.cpu().numpy().view(np.uint64), bbq_corr.cpu().numpy(), bbq_c.cpu().numpy(), dim,
                 vx.SimilarityFunction.DOT_PRODUCT)
@@ -827,16 +828,27 @@ def run_bq(args, rank, world, local, dev, barrier, max_over_ranks, tc_sustained,
         ids, sc, cnt = b.scan_candidates_device(q, k)
         return ids if world == 1 else gather_and_merge(ids, sc, cnt, offs, k)[0]
 
-    bms_step, bkms, bbr = _timed_scan(args, world, dev, barrier, max_over_ranks, bstep, "bq_scan")
+    bms_step, bkms, bbr = _timed_scan(args, world, dev, barrier, max_over_ranks, bstep, "gemm_scan")
     b.close()
-    bwork = 4.0 * nq * nb * (dim // 64)  # AND + popcount of a 64-bit word per plane
-    bach = bwork / (bkms / 1e3) / 1e12 if bkms > 0 else None
+    if bbr.get("gemm_scan"):
+        dp8 = (dim + 127) // 128 * 128
+        bach = 2.0 * nq * nb * dp8 / (bkms / 1e3) / 1e12 if bkms > 0 else None
+        bpeak = 2.0 * tc_sustained
+        broof = {"bound": "tensor (int8)", "achieved": bach, "peak": bpeak, "unit": "TOP/s",
+                 "frac": (bach / bpeak) if bach else None,
+                 "kernel": "gemm_scan_kernel (tcgen05 kind::i8 on 0/1 bits x 4-bit codes, BBQ epilogue)",
+                 "peak_source": f"2 x {peak_kind} dense bf16 sustained (int8 MMA runs at twice the bf16 rate)"}
+    else:
+        bkms = bbr.get("bq_scan", 0.0)
+        bwork = 4.0 * nq * nb * (dim // 64)  # AND + popcount of a 64-bit word per plane
+        bach = bwork / (bkms / 1e3) / 1e12 if bkms > 0 else None
+        broof = {"bound": "integer pipe (and + popc)", "achieved": bach, "unit": "T word-plane ops/s",
+                 "peak": None, "frac": None, "kernel": "bbq_scan_kernel"}
+    broof.update({"per": "GPU", "breakdown_ms_per_step": bbr})
     bbq = {"value": nq / (bms_step / 1e3), "unit": "queries/s", "ms_per_step": bms_step,
            "config": {"workload": f"BBQ candidate scan n={nb * world:,} x {dim} bits (4-bit queries) "
                                   f"queries={nq:,} k={k}"},
-           "roofline": {"bound": "integer pipe (and + popc)", "achieved": bach, "unit": "T word-plane ops/s",
-                        "peak": None, "frac": None, "kernel": "bbq_scan_kernel", "per": "GPU",
-                        "breakdown_ms_per_step": bbr}}
+           "roofline": broof}
     return {
         "value": nq / (ms / 1e3), "unit": "queries/s", "ms_per_step": ms,
         "config": {"workload": f"BQ sign-bit Hamming candidate scan n={n:,} x {dim} bits queries={nq:,} k={k}"},

@@ -319,10 +319,12 @@ def test_sq4_bit_exact(oracle, metric, n, dim, nq, k):
 
 # ------------------------------------------------------------------ BBQ
 @pytest.mark.parametrize("metric", [0, 1, 2, 3])
-@pytest.mark.parametrize("n,dim,nq,k", [(6000, 768, 40, 100), (2500, 100, 65, 10), (1000, 1024, 20, 5)])
+@pytest.mark.parametrize("n,dim,nq,k", [(6000, 768, 40, 100), (2500, 100, 65, 10), (1000, 1024, 20, 5),
+                                        (90000, 256, 300, 100)])
 def test_bbq_bit_exact(oracle, metric, n, dim, nq, k):
-    # BinaryQuantizedVectors BBQ: 4-bit query planes against centroid-relative sign bits, the
-    # exact asymmetric popcount dot, computeBbqDot and the metric transform in Java's order
+    # BinaryQuantizedVectors BBQ: 4-bit query codes against centroid-relative sign bits, the
+    # exact asymmetric dot (int8 tensor cores), computeBbqDot and the metric transform in Java's
+    # order; 90,000 rows also take the pilot sweep's floors and several row tiles per unit
     db, q = _data(oracle, n, dim, nq, normalize=(metric == 2))
     cent = db.mean(0).astype(np.float32)
     words, corr = oracle.bbq_encode_all(db, cent)

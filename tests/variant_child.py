@@ -1,8 +1,8 @@
 """Child process for test_gpu_scan_variants.py: the scan variant is chosen by environment
 variables that the library reads once per process (VX_GEMM_1SM, VX_SCAN_PILOT,
 VX_BQ_TENSOR_BYTES, VX_ADC_GROUPED), so each variant runs in a process of its own.
-Exits 0 when FLAT, SQ8 and BQ results (or, with the argument "ivf", IVF-PQ results) match the
-oracle."""
+Exits 0 when FLAT, SQ8, BQ and BBQ results (or, with the argument "ivf", IVF-PQ results) match
+the oracle."""
 import sys
 
 import numpy as np
@@ -65,6 +65,17 @@ def main():
     for i, o in enumerate(got):
         assert list(o.ordinals) == list(ids[i, : cnt[i]]), f"bq query {i}"
         assert np.array_equal(o.scores, sc[i, : cnt[i]]), f"bq query {i} scores"
+    cent = db.mean(0).astype(np.float32)
+    bw, bc = O.bbq_encode_all(db, cent)
+    for metric in (0, 2):
+        b = vx.QuantizedFlatScanAdapter()
+        b.build_bbq(bw, bc, cent, 96, vx.SimilarityFunction(metric))
+        got = b.scan_candidates(q, 100)
+        ids, sc, cnt = O.bbq_search(bw, bc, cent, 96, q, metric, 100)
+        for i, o in enumerate(got):
+            assert list(o.ordinals) == list(ids[i, : cnt[i]]), f"bbq m={metric} query {i}"
+            assert np.array_equal(o.scores, sc[i, : cnt[i]]), f"bbq m={metric} query {i} scores"
+        b.close()
     print("variant ok")
     return 0
 

@@ -13,6 +13,7 @@
 // thread owns one query (its words live in registers) and scores each staged row against
 // it.  The database is read from HBM once per batch; the binding roof is the integer/popc
 // pipe.
+#include "bbq.cuh"
 #include "common.cuh"
 #include "kernels.h"
 
@@ -249,27 +250,12 @@ __device__ __forceinline__ int32_t popc_and16(const uint64_t* x, const uint64_t 
 __device__ __forceinline__ float bbq_score(int metric, const BbqQuery& qi, float4 ri, int32_t raw, int dim) {
   const float dist_c = ri.x, vl = ri.y, width = ri.z;
   const int32_t pop = __float_as_int(ri.w);
-  const float s1 = __fadd_rn(__fmul_rn(vl, (float)dim), __fmul_rn(width, (float)pop));
-  const float s2 = __fadd_rn(__fmul_rn(vl, (float)qi.qsum), __fmul_rn(width, (float)raw));
-  const float approx = __fadd_rn(__fmul_rn(qi.qmin, s1), __fmul_rn(qi.w15, s2));
+  const float approx = bbq_approx(qi.qmin, qi.w15, (float)qi.qsum, vl, width, bbq_row_term(vl, width, dim, pop), raw);
   switch (metric) {
-    case kEuclidean: {
-      const float adj = __fsub_rn(__fadd_rn(qi.nsq, dist_c), __fmul_rn(2.0f, approx));
-      return __fdiv_rn(1.0f, __fadd_rn(1.0f, adj > 0.0f ? adj : 0.0f));
-    }
-    case kCosine: {
-      const float vn = (float)sqrt((double)dist_c);
-      if (qi.norm == 0.0f || vn == 0.0f) return 0.0f;
-      const float cosv = __fdiv_rn(approx, __fmul_rn(qi.norm, vn));
-      const float s = __fmul_rn(__fadd_rn(1.0f, cosv), 0.5f);  // x / 2f, the same rounding
-      return s > 0.0f ? s : 0.0f;
-    }
-    case kMaxInnerProduct:
-      return scale_mip(approx);
-    default: {
-      const float s = __fmul_rn(__fadd_rn(1.0f, approx), 0.5f);  // (1f + approxDot) / 2f
-      return s > 0.0f ? s : 0.0f;
-    }
+    case kEuclidean: return bbq_l2_score(bbq_l2_adj(approx, qi.nsq, dist_c));
+    case kCosine: return bbq_cos_score(approx, qi.norm, bbq_vnorm(dist_c));
+    case kMaxInnerProduct: return scale_mip(approx);
+    default: return bbq_dot_score(approx);
   }
 }
 
@@ -374,6 +360,42 @@ __global__ void bbq_rowinfo_kernel(const uint64_t* __restrict__ words, int nw, i
   out[r] = make_float4(corr[r * 3], corr[r * 3 + 1], corr[r * 3 + 2], __int_as_float(pop));
 }
 
+// Per-row epilogue record of the int8 tensor-core BBQ scan: (vl, width, vl * D + width * pop,
+// |v - c| for COSINE or |v - c|^2 otherwise), from the (|v - c|^2, vl, width, pop) record.
+__global__ void bbq_epi_rows_kernel(const float4* __restrict__ info, int64_t n, int dim, int metric,
+                                    float4* __restrict__ out) {
+  const int64_t r = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (r >= n) return;
+  const float4 i = info[r];
+  const float s1 = bbq_row_term(i.y, i.z, dim, __float_as_int(i.w));
+  out[r] = make_float4(i.y, i.z, s1, metric == kCosine ? bbq_vnorm(i.x) : i.x);
+}
+
+// The 4-bit query codes as int8 (the A operand of rawAsymDot on the tensor cores) from the bit
+// planes [nq][4][nw_pad]; one thread per 4 bytes of a row, dims [dim, Dp8) -> 0.
+__global__ void bbq_planes_to_i8_kernel(const uint64_t* __restrict__ planes, int nq, int dim, int nw_pad, int Dp8,
+                                        int8_t* __restrict__ dst) {
+  const int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  const int per_row = Dp8 / 4;
+  if (t >= (int64_t)nq * per_row) return;
+  const int64_t r = t / per_row;
+  const int c0 = (int)(t - r * per_row) * 4;
+  const uint64_t* pl = planes + r * 4 * nw_pad;
+  uint32_t out = 0;
+#pragma unroll
+  for (int j = 0; j < 4; j++) {
+    const int c = c0 + j;
+    uint32_t v = 0;
+    if (c < dim) {
+      const int w = c >> 6, b = c & 63;
+#pragma unroll
+      for (int p = 0; p < 4; p++) v |= (uint32_t)((pl[p * nw_pad + w] >> b) & 1ull) << p;
+    }
+    out |= v << (8 * j);
+  }
+  reinterpret_cast<uint32_t*>(dst + r * Dp8)[c0 / 4] = out;
+}
+
 template <int NW>
 cudaError_t launch_bbq_nw(const uint64_t* db, const float4* rowinfo, int64_t n, int dim, int metric,
                           const uint64_t* planes, const BbqQuery* qinfo, int nq, int parts, const StreamGeom& g,
@@ -440,6 +462,20 @@ cudaError_t launch_bbq_rowinfo(const uint64_t* words, int nw, int nw_pad, const 
                                cudaStream_t st) {
   if (n <= 0) return cudaSuccess;
   bbq_rowinfo_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(words, nw, nw_pad, corr, n, out);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_bbq_epi_rows(const float4* info, int64_t n, int dim, int metric, float4* out, cudaStream_t st) {
+  if (n <= 0) return cudaSuccess;
+  bbq_epi_rows_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(info, n, dim, metric, out);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_bbq_planes_to_i8(const uint64_t* planes, int nq, int dim, int nw_pad, int Dp8, int8_t* dst,
+                                    cudaStream_t st) {
+  if (nq <= 0) return cudaSuccess;
+  const int64_t total = (int64_t)nq * (Dp8 / 4);
+  bbq_planes_to_i8_kernel<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(planes, nq, dim, nw_pad, Dp8, dst);
   return cudaGetLastError();
 }
 

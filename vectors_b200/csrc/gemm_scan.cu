@@ -7,12 +7,15 @@
 //                   (vectors-db/.../index/FlatScanAdapter.java:51-175).
 //   * kind::i8   -- the SQ8 scan: 7-bit codes (ScalarQuantizer.java:243-272) multiplied
 //                   exactly into int32, followed by the reference score epilogue
-//                   (ScalarQuantizedVectors.java:82-107), bit-exact.
+//                   (ScalarQuantizedVectors.java:82-107), bit-exact.  The same pipeline serves
+//                   sign-bit BQ (+-1 operands, Hamming epilogue) and BBQ (0/1 row bits x 4-bit
+//                   query codes = rawAsymDot, BinaryQuantizedVectors.java:110-275, epilogue in
+//                   bbq.cuh).
 //
 // Tiling.  The default variant runs on 2-CTA clusters (tcgen05 cta_group::2): a cluster owns
 // a 256-query x 256-row tile; each CTA stages only its own 128 query rows and 128 database
-// rows of every 128-byte K chunk (64 fp16 / 128 int8 elements) through a 6-deep TMA ring with
-// 128-byte swizzle, i.e. 32 KB of shared memory traffic per SM for 128 x 256 x 64 MACs.  The
+// rows of every 128-byte K chunk (64 fp16 / 128 int8 elements) through a 6-deep TMA ring (5-deep
+// for BBQ, whose per-row epilogue records take four words instead of two) with 128-byte swizzle, i.e. 32 KB of shared memory traffic per SM for 128 x 256 x 64 MACs.  The
 // leader CTA issues the pair MMA; each CTA's TMEM holds its 128 queries x 256 rows in
 // fp32/s32, double buffered (512 columns) so that the epilogue of tile t overlaps the MMAs of
 // tile t+1.  A 1-CTA variant (128 x 256 tiles, 48 KB per stage) is kept for comparison.
@@ -26,6 +29,7 @@
 // time; on expiry the kernel records kDevWaitTimeout, the roles unwind and TMEM is released.
 // No TMA load uses cluster multicast.
 #include <cuda.h>
+#include "bbq.cuh"
 #include "gemm_scan.h"
 #include "sm100.cuh"
 
@@ -41,16 +45,20 @@ constexpr int TMEM_COLS = 512;
 constexpr int kStageRowWords = 36;  // per-lane staging row: 32 values + 4 words of padding
                                     // (16-byte stores of 8 lanes hit 8 distinct bank quads)
 
-template <bool k2Sm>
+// Per-row float arrays the epilogue stages for each tile: two (row scale, |x|^2 or the SQ8
+// terms), four for BBQ.
+__host__ __device__ constexpr int cols_of(int mode) { return epi_is_bbq(mode) ? 4 : 2; }
+
+template <bool k2Sm, int kCols>
 struct Geo {
-  static constexpr int kStages = k2Sm ? 6 : 4;
+  static constexpr int kStages = k2Sm ? (kCols > 2 ? 5 : 6) : (kCols > 2 ? 3 : 4);
   static constexpr int kRowsB = k2Sm ? 128 : 256;  // database rows staged per CTA
   static constexpr int kABytes = 128 * BK_BYTES;    // 128 query rows per CTA
   static constexpr int kBBytes = kRowsB * BK_BYTES;
   static constexpr int kStageBytes = kABytes + kBBytes;               // per CTA
   static constexpr int kTxBytes = k2Sm ? 2 * kStageBytes : kStageBytes;  // on the leader's barrier
   static constexpr int kQueriesPerTile = k2Sm ? 256 : 128;
-  static constexpr size_t kSmem = 1024 + (size_t)kStages * kStageBytes + 4 * 2 * 256 * sizeof(float) +
+  static constexpr size_t kSmem = 1024 + (size_t)kStages * kStageBytes + 4 * kCols * 256 * sizeof(float) +
                                   4 * 32 * kStageRowWords * sizeof(uint32_t) + 256;
   static_assert(kSmem <= 232448, "shared memory above the per-block limit");
 };
@@ -80,10 +88,21 @@ __device__ __forceinline__ void apply_floor(const ScanArgs& a, int q, bool activ
 }
 
 // Ranking score of one accumulator value in epilogue mode kMode (gemm_scan.h).
+// BBQ: computeBbqDot of one accumulator value (rawAsymDot) against the staged row record
+// s_col[col] = vl, s_col[256 + col] = width, s_col[512 + col] = vl * D + width * pop; qb holds
+// the lane's query (queryMin, queryWidth / 15, querySum, queryNormSq or queryNorm).
+__device__ __forceinline__ float bbq_approx_at(uint32_t v, int col, const float* s_col, const float4& qb) {
+  return bbq_approx(qb.x, qb.y, qb.z, s_col[col], s_col[256 + col], s_col[512 + col], (int32_t)v);
+}
+
 template <int kMode>
 __device__ __forceinline__ float score_of(uint32_t v, int col, const float* s_col, const float* s_col2,
-                                          float qa, int32_t qi, float cm) {
+                                          float qa, int32_t qi, float cm, const float4& qb) {
   if (kMode == kEpiF16Plain) return __uint_as_float(v);
+  if (kMode == kEpiBbqDot) return bbq_dot_score(bbq_approx_at(v, col, s_col, qb));
+  if (kMode == kEpiBbqMip) return scale_mip(bbq_approx_at(v, col, s_col, qb));
+  if (kMode == kEpiBbqL2) return bbq_l2_score(bbq_l2_adj(bbq_approx_at(v, col, s_col, qb), qb.w, s_col[768 + col]));
+  if (kMode == kEpiBbqCos) return bbq_cos_score(bbq_approx_at(v, col, s_col, qb), qb.w, s_col[768 + col]);
   if (kMode == kEpiF16Scaled) return __uint_as_float(v) * s_col[col];
   if (kMode == kEpiF16L2) return fmaf(qa * s_col[col], __uint_as_float(v), -s_col2[col]);
   if (kMode == kEpiSq8Dot || kMode == kEpiSq8Mip) {
@@ -120,11 +139,11 @@ template <int kMode, int R>
 __device__ __forceinline__ void offer_group(const ScanArgs& a, TileStream& ts, int q, bool active,
                                             const uint32_t (&v)[32], int c0, int limit, int64_t col0,
                                             const float* s_col, const float* s_col2, float qa, int32_t qi,
-                                            uint32_t* stage_row) {
+                                            const float4& qb, uint32_t* stage_row) {
   uint32_t pm = 0;
 #pragma unroll
   for (int j = 0; j < 32; j++)
-    pm |= (score_of<kMode>(v[j], c0 + j, s_col, s_col2, qa, qi, a.epi.cm) >= ts.tf ? 1u : 0u) << j;
+    pm |= (score_of<kMode>(v[j], c0 + j, s_col, s_col2, qa, qi, a.epi.cm, qb) >= ts.tf ? 1u : 0u) << j;
   if (limit < 32) pm &= limit <= 0 ? 0u : (0xFFFFFFFFu >> (32 - limit));  // rows beyond n
   if (pm) {
     uint4* d = reinterpret_cast<uint4*>(stage_row);
@@ -143,7 +162,7 @@ __device__ __forceinline__ void offer_group(const ScanArgs& a, TileStream& ts, i
     const int j = __ffs(pm) - 1;
     pm &= pm - 1;
     const int col = c0 + j;
-    const float sc = score_of<kMode>(stage_row[j], col, s_col, s_col2, qa, qi, a.epi.cm);
+    const float sc = score_of<kMode>(stage_row[j], col, s_col, s_col2, qa, qi, a.epi.cm, qb);
     const uint64_t key = float_key(sc, (uint32_t)(col0 + col));
     if (key > ts.st.thr) {
       ts.st.base[ts.st.cnt++] = key;
@@ -174,9 +193,34 @@ __device__ __forceinline__ int32_t imax_tree32(const uint32_t (&v)[32]) {
 
 template <int kMode>
 __device__ __forceinline__ float group_max(const uint32_t (&v)[32], int c0, const float* s_col,
-                                           const float* s_col2, float qa, int32_t qi, const EpiParams& e) {
+                                           const float* s_col2, float qa, int32_t qi, const EpiParams& e,
+                                           const float4& qb) {
   if constexpr (kMode == kEpiBqHamming) {
-    return score_of<kMode>((uint32_t)imax_tree32(v), 0, s_col, s_col2, qa, qi, e.cm);
+    return score_of<kMode>((uint32_t)imax_tree32(v), 0, s_col, s_col2, qa, qi, e.cm, qb);
+  } else if constexpr (kMode == kEpiBbqDot || kMode == kEpiBbqMip) {
+    // exact: the largest computeBbqDot, then the non-decreasing tail
+    float m[16];
+#pragma unroll
+    for (int i = 0; i < 16; i++)
+      m[i] = fmaxf(bbq_approx_at(v[2 * i], c0 + 2 * i, s_col, qb), bbq_approx_at(v[2 * i + 1], c0 + 2 * i + 1, s_col, qb));
+#pragma unroll
+    for (int w = 8; w >= 1; w >>= 1)
+#pragma unroll
+      for (int i = 0; i < w; i++) m[i] = fmaxf(m[i], m[i + w]);
+    return kMode == kEpiBbqDot ? bbq_dot_score(m[0]) : scale_mip(m[0]);
+  } else if constexpr (kMode == kEpiBbqL2) {
+    // exact: the smallest clamped distance term (never NaN), then the non-increasing tail
+    float m[16];
+#pragma unroll
+    for (int i = 0; i < 16; i++)
+      m[i] = fminf(bbq_l2_adj(bbq_approx_at(v[2 * i], c0 + 2 * i, s_col, qb), qb.w, s_col[768 + c0 + 2 * i]),
+                   bbq_l2_adj(bbq_approx_at(v[2 * i + 1], c0 + 2 * i + 1, s_col, qb), qb.w,
+                              s_col[768 + c0 + 2 * i + 1]));
+#pragma unroll
+    for (int w = 8; w >= 1; w >>= 1)
+#pragma unroll
+      for (int i = 0; i < w; i++) m[i] = fminf(m[i], m[i + w]);
+    return bbq_l2_score(m[0]);
   } else if constexpr (kMode == kEpiSq8Dot || kMode == kEpiSq8Mip) {
     // exact: the largest adj = raw * cm + queryCorrection + correction, then the monotone tail
     float m[16];
@@ -213,8 +257,8 @@ __device__ __forceinline__ float group_max(const uint32_t (&v)[32], int c0, cons
     float m[16];
 #pragma unroll
     for (int i = 0; i < 16; i++)
-      m[i] = fmaxf(score_of<kMode>(v[2 * i], c0 + 2 * i, s_col, s_col2, qa, qi, e.cm),
-                   score_of<kMode>(v[2 * i + 1], c0 + 2 * i + 1, s_col, s_col2, qa, qi, e.cm));
+      m[i] = fmaxf(score_of<kMode>(v[2 * i], c0 + 2 * i, s_col, s_col2, qa, qi, e.cm, qb),
+                   score_of<kMode>(v[2 * i + 1], c0 + 2 * i + 1, s_col, s_col2, qa, qi, e.cm, qb));
 #pragma unroll
     for (int w = 8; w >= 1; w >>= 1)
 #pragma unroll
@@ -233,12 +277,12 @@ template <bool kI8, int kMode, int R, bool k2Sm>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gemm_scan_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const ScanArgs a) {
-  using G = Geo<k2Sm>;
+  using G = Geo<k2Sm, cols_of(kMode)>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   uint8_t* stages = smem;
-  float* s_cols = (float*)(smem + (size_t)G::kStages * G::kStageBytes);  // [4 warps][2][256]
-  uint32_t* stage_rows = (uint32_t*)(s_cols + 4 * 2 * 256);               // [4 warps][32 lanes][36]
+  float* s_cols = (float*)(smem + (size_t)G::kStages * G::kStageBytes);  // [4 warps][kCols][256]
+  uint32_t* stage_rows = (uint32_t*)(s_cols + 4 * cols_of(kMode) * 256);  // [4 warps][32 lanes][36]
   uint64_t* full = (uint64_t*)(stage_rows + 4 * 32 * kStageRowWords);
   uint64_t* empty = full + G::kStages;
   uint64_t* tfull = empty + G::kStages;
@@ -407,7 +451,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const int row_in_block = (int)rank * 128 + quarter * 32 + lane;
     const int Qp = a.num_mblocks * G::kQueriesPerTile;
     const uint32_t tempty0 = k2Sm ? mapa_shared(smem_addr(&tempty[0]), 0) : smem_addr(&tempty[0]);
-    float* s_col = s_cols + (warp - 2) * 512;  // this warp's private column data
+    float* s_col = s_cols + (warp - 2) * (cols_of(kMode) * 256);  // this warp's private column data
     float* s_col2 = s_col + 256;
     uint32_t* stage_row = stage_rows + (warp - 2) * (32 * kStageRowWords) + lane * kStageRowWords;
     const int64_t nt_first = p0 / a.num_mblocks;  // first row tile of this unit (row-major dealing)
@@ -429,6 +473,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             if (kMode == kEpiF16L2) s_col2[i] = in ? a.epi.rowsq[row] : 0.0f;
           } else if (kMode == kEpiSq8Dot || kMode == kEpiSq8Mip) {
             s_col[i] = in ? a.epi.vcorr[row] : 0.0f;
+          } else if (epi_is_bbq(kMode)) {
+            const float4 r = in ? a.epi.bbq_rows[row] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            s_col[i] = r.x;
+            s_col[256 + i] = r.y;
+            s_col[512 + i] = r.z;
+            s_col[768 + i] = r.w;
           } else {  // kEpiSq8L2
             s_col[i] = __int_as_float(in ? a.epi.vsq[row] : 0);
           }
@@ -456,6 +506,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         if (kMode == kEpiSq8L2) qi = a.epi.qsq[q];
       }
       if (kMode == kEpiBqHamming) qi = a.epi.bits;
+      float4 qb = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+      if (epi_is_bbq(kMode) && active) {
+        const BbqQuery b = a.epi.bbq_q[q];
+        qb = make_float4(b.qmin, b.w15, (float)b.qsum, kMode == kEpiBbqL2 ? b.nsq : b.norm);
+      }
       if (__shfl_sync(0xFFFFFFFFu, *abort_flag, 0)) break;
       {
         bool ok = mbar_wait(&tfull[acc], acc_phase, a.timeout_ns, abort_flag);
@@ -478,13 +533,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         __syncwarp();
         tmem_ld_32x32b_x32(taddr + (uint32_t)(g * 32), v);
         tmem_ld_wait();
-        const float m = group_max<kMode>(v, c0, s_col, s_col2, qa, qi, a.epi);
+        const float m = group_max<kMode>(v, c0, s_col, s_col2, qa, qi, a.epi, qb);
         if (probe) {  // exact group maxima: the floor needs scores that rows reach
           if (active) a.probe[(size_t)q * a.probe_groups + (size_t)((col0 + c0) >> 5)] = m;
           continue;
         }
         if (__any_sync(0xFFFFFFFFu, m >= ts.tf))
-          offer_group<kMode, R>(a, ts, q, active, v, c0, valid - c0, col0, s_col, s_col2, qa, qi, stage_row);
+          offer_group<kMode, R>(a, ts, q, active, v, c0, valid - c0, col0, s_col, s_col2, qa, qi, qb, stage_row);
       }
       tc_fence_before();
       __syncwarp();
@@ -552,7 +607,7 @@ template <bool kI8, int kMode, int R, bool k2Sm>
 cudaError_t launch_one(const CUtensorMap& tmA, const CUtensorMap& tmB, const ScanArgs& a, int grid,
                        cudaStream_t st) {
   auto kern = gemm_scan_kernel<kI8, kMode, R, k2Sm>;
-  const size_t smem = Geo<k2Sm>::kSmem;
+  const size_t smem = Geo<k2Sm, cols_of(kMode)>::kSmem;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   if (!k2Sm) {
@@ -598,6 +653,10 @@ cudaError_t launch_variant(int mode, const CUtensorMap& tmA, const CUtensorMap& 
     case kEpiSq8Mip: return launch_mode<true, kEpiSq8Mip, k2Sm>(tmA, tmB, a, grid, R, st);
     case kEpiSq8L2: return launch_mode<true, kEpiSq8L2, k2Sm>(tmA, tmB, a, grid, R, st);
     case kEpiBqHamming: return launch_mode<true, kEpiBqHamming, k2Sm>(tmA, tmB, a, grid, R, st);
+    case kEpiBbqDot: return launch_mode<true, kEpiBbqDot, k2Sm>(tmA, tmB, a, grid, R, st);
+    case kEpiBbqMip: return launch_mode<true, kEpiBbqMip, k2Sm>(tmA, tmB, a, grid, R, st);
+    case kEpiBbqL2: return launch_mode<true, kEpiBbqL2, k2Sm>(tmA, tmB, a, grid, R, st);
+    case kEpiBbqCos: return launch_mode<true, kEpiBbqCos, k2Sm>(tmA, tmB, a, grid, R, st);
     default: return cudaErrorInvalidValue;
   }
 }

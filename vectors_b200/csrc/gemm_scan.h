@@ -16,7 +16,15 @@ enum EpiMode : int {
   kEpiSq8Mip = 4,     // ScalarQuantizedVectors MAXIMUM_INNER_PRODUCT score (exact)
   kEpiSq8L2 = 5,      // ScalarQuantizedVectors EUCLIDEAN score (exact)
   kEpiBqHamming = 6,  // sign-bit BQ on +-1 int8 operands: h = (D - dot) / 2, ranked by -h (exact)
+  // BBQ on 0/1 row bits x 4-bit query codes: the int32 accumulator is rawAsymDot exactly; the
+  // epilogue applies computeBbqDot and the metric's transform (bbq.cuh), bit-exact
+  kEpiBbqDot = 7,     // DOT_PRODUCT
+  kEpiBbqMip = 8,     // MAXIMUM_INNER_PRODUCT
+  kEpiBbqL2 = 9,      // EUCLIDEAN
+  kEpiBbqCos = 10,    // COSINE
 };
+
+__host__ __device__ constexpr bool epi_is_bbq(int mode) { return mode >= kEpiBbqDot && mode <= kEpiBbqCos; }
 
 struct EpiParams {
   const float* xnorm;   // [n] row scale: |x| for unit rows, 1 for stored fp16 rows
@@ -27,6 +35,8 @@ struct EpiParams {
   const int32_t* vsq;   // [n] SQ8 sum of squared row codes
   float cm;             // SQ8 constMultiplier = alpha^2
   int32_t bits;         // BQ dimension D (bits per vector)
+  const float4* bbq_rows;   // [n] BBQ (vl, width, vl * D + width * pop, |v - c| or |v - c|^2)
+  const BbqQuery* bbq_q;    // [nq] BBQ per-query terms
 };
 
 struct ScanArgs {

@@ -40,6 +40,9 @@ struct vx_index {
   // BBQ: the quantizer's centroid, per-row (|v - c|^2, vl, width, popcount) records
   float* bbq_centroid = nullptr;
   float4* bbq_rows = nullptr;
+  // BBQ on the int8 tensor-core scan (with codes8 = the 0/1 bits): per-row epilogue records
+  // (vl, width, vl * D + width * pop, |v - c| for COSINE or |v - c|^2)
+  float4* bbq_epi = nullptr;
   // IVF-PQ
   float* cent = nullptr;
   int nlist = 0;

@@ -94,6 +94,11 @@ cudaError_t launch_bbq_prep_queries(const float* q, int nq, int dim, const float
                                     uint64_t* planes, BbqQuery* info, cudaStream_t st);
 cudaError_t launch_bbq_rowinfo(const uint64_t* words, int nw, int nw_pad, const float* corr, int64_t n, float4* out,
                                cudaStream_t st);
+// int8 tensor-core BBQ scan (gemm_scan.cu, kEpiBbq*): per-row (vl, width, vl * D + width * pop,
+// |v - c| (COSINE) or |v - c|^2) records, and the 4-bit query codes as int8 rows of Dp8 bytes.
+cudaError_t launch_bbq_epi_rows(const float4* info, int64_t n, int dim, int metric, float4* out, cudaStream_t st);
+cudaError_t launch_bbq_planes_to_i8(const uint64_t* planes, int nq, int dim, int nw_pad, int Dp8, int8_t* dst,
+                                    cudaStream_t st);
 cudaError_t launch_bbq_scan(const uint64_t* db, const float4* rowinfo, int64_t n, int nw_pad, int dim, int metric,
                             const uint64_t* planes, const BbqQuery* qinfo, int nq, int parts, const StreamGeom& g,
                             uint64_t* bufs, uint32_t* cnts, uint64_t* thrs, cudaStream_t st);

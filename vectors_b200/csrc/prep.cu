@@ -251,7 +251,7 @@ Sq8Consts sq8_consts(float min_q, float max_q, int max_value) {
 
 // One thread per 4 output bytes of a row (Dp8 is a multiple of 128, so of 4).
 __global__ void bq_words_to_i8_kernel(const uint64_t* __restrict__ words, int64_t n, int nwp, int dim,
-                                      int Dp8, int8_t* __restrict__ dst) {
+                                      int Dp8, int8_t clear, int8_t* __restrict__ dst) {
   const int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
   const int per_row = Dp8 / 4;
   if (t >= n * per_row) return;
@@ -262,7 +262,7 @@ __global__ void bq_words_to_i8_kernel(const uint64_t* __restrict__ words, int64_
   for (int j = 0; j < 4; j++) {
     const int c = c0 + j;
     int8_t v = 0;
-    if (c < dim) v = ((words[r * nwp + (c >> 6)] >> (c & 63)) & 1ull) ? (int8_t)1 : (int8_t)-1;
+    if (c < dim) v = ((words[r * nwp + (c >> 6)] >> (c & 63)) & 1ull) ? (int8_t)1 : clear;
     out |= (uint32_t)(uint8_t)v << (8 * j);
   }
   reinterpret_cast<uint32_t*>(dst + r * Dp8)[c0 / 4] = out;
@@ -279,10 +279,11 @@ __global__ void bq_queries_to_i8_kernel(const float* __restrict__ q, int nq, int
 }
 
 cudaError_t launch_bq_words_to_i8(const uint64_t* words, int64_t n, int nwp, int dim, int Dp8, int8_t* dst,
-                                  cudaStream_t st) {
+                                  cudaStream_t st, bool zero_one) {
   if (n <= 0) return cudaSuccess;
   const int64_t total = n * (Dp8 / 4);
-  bq_words_to_i8_kernel<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(words, n, nwp, dim, Dp8, dst);
+  bq_words_to_i8_kernel<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(words, n, nwp, dim, Dp8,
+                                                                         zero_one ? (int8_t)0 : (int8_t)-1, dst);
   return cudaGetLastError();
 }
 

@@ -32,8 +32,9 @@ cudaError_t launch_sq8_encode_queries(const float* q, int nq, int dim, int Dp8, 
                                       int8_t* codes, float* corr, int32_t* sumsq, cudaStream_t st);
 // Sign-bit BQ as +-1 int8 operands for the tensor-core Hamming scan: bit set (v >= 0) -> +1,
 // clear -> -1, dims [dim, Dp8) -> 0.  Rows from packed words [n][nwp]; queries from fp32.
+// With zero_one the clear bits become 0 instead (BBQ rows: the 0/1 operand of rawAsymDot).
 cudaError_t launch_bq_words_to_i8(const uint64_t* words, int64_t n, int nwp, int dim, int Dp8, int8_t* dst,
-                                  cudaStream_t st);
+                                  cudaStream_t st, bool zero_one = false);
 cudaError_t launch_bq_queries_to_i8(const float* q, int nq, int dim, int Dp8, int8_t* dst, cudaStream_t st);
 cudaError_t launch_sq8_rows_pad(const int8_t* src, int64_t n, int dim, int Dp8, int8_t* dst,
                                 int32_t* sumsq, cudaStream_t st);

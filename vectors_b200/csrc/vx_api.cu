@@ -623,15 +623,19 @@ int search_gemm_exact(vx_index* ix, const float* dq, int nq, int k, int32_t* d_i
   return VX_OK;
 }
 
-// SQ8 / BQ: exact quantized scores; K best per query (optionally re-scored in fp32).
+// SQ8 / SQ4 / BQ / BBQ: exact quantized scores; K best per query (optionally re-scored in fp32).
+// The int8 tensor-core scan serves every kind whose rows have an int8 operand (codes8); BQ and
+// BBQ indexes built without one (VX_BQ_TENSOR_BYTES below their size) take the popcount scans.
 int search_quantized_scan(vx_index* ix, const float* dq, int nq, int K, int k_out, bool rescore,
                           int32_t* d_ids, float* d_scores, int32_t* d_counts, cudaStream_t st) {
   const int dim = ix->dim;
   Scratch S(st);
   int32_t* d_err = S.alloc<int32_t>(1);
   VX_CUDA(cudaMemsetAsync(d_err, 0, 4, st));
-  if (ix->kind == VX_KIND_SQ8 || ix->kind == VX_KIND_SQ4 || (ix->kind == VX_KIND_BQ && ix->codes8)) {
-    const bool bq = ix->kind == VX_KIND_BQ;  // +-1 operands, Hamming epilogue
+  if (ix->kind == VX_KIND_SQ8 || ix->kind == VX_KIND_SQ4 ||
+      ((ix->kind == VX_KIND_BQ || ix->kind == VX_KIND_BBQ) && ix->codes8)) {
+    const bool bq = ix->kind == VX_KIND_BQ;    // +-1 operands, Hamming epilogue
+    const bool bbq = ix->kind == VX_KIND_BBQ;  // 0/1 rows x 4-bit query codes, BBQ epilogue
     const int R = gemm_scan_stream_R(K);
     if (R < 0) return fail(VX_ERR_UNSUPPORTED, "k=%d is larger than this build supports", K);
     const int C = 32 * R;
@@ -642,10 +646,15 @@ int search_quantized_scan(vx_index* ix, const float* dq, int nq, int K, int k_ou
     int64_t qch = (int64_t)(scratch_budget() / ((size_t)U0 * (C * 8 + 12)));
     qch = std::max<int64_t>(QB, qch / QB * QB);
     const int mode = bq ? kEpiBqHamming
+                     : bbq ? (ix->metric == VX_EUCLIDEAN ? kEpiBbqL2
+                              : ix->metric == VX_MAXIMUM_INNER_PRODUCT ? kEpiBbqMip
+                              : ix->metric == VX_COSINE ? kEpiBbqCos
+                                                        : kEpiBbqDot)
                      : ix->metric == VX_EUCLIDEAN ? kEpiSq8L2
                      : ix->metric == VX_MAXIMUM_INNER_PRODUCT ? kEpiSq8Mip
                                                               : kEpiSq8Dot;
-    const Sq8Consts kc = bq ? Sq8Consts{0.f, 0.f, 0.f, 0.f, 0.f} : sq8_consts(ix->min_q, ix->max_q, ix->sq_max);
+    const Sq8Consts kc =
+        (bq || bbq) ? Sq8Consts{0.f, 0.f, 0.f, 0.f, 0.f} : sq8_consts(ix->min_q, ix->max_q, ix->sq_max);
     // sized once for the largest chunk and reused by every chunk
     const int qmax = (int)std::min<int64_t>(qch, std::max(nq, 1));
     const int QpMax = (qmax + QB - 1) / QB * QB;
@@ -653,6 +662,8 @@ int search_quantized_scan(vx_index* ix, const float* dq, int nq, int K, int k_ou
     int8_t* qcodes = S.alloc<int8_t>((size_t)QpMax * ix->Dp8);
     float* qcorr = S.alloc<float>(QpMax);
     int32_t* qsq = S.alloc<int32_t>(QpMax);
+    uint64_t* qplanes = bbq ? S.alloc<uint64_t>((size_t)qmax * 4 * ix->nw_pad) : nullptr;
+    BbqQuery* qinfo = bbq ? S.alloc<BbqQuery>(QpMax) : nullptr;
     uint64_t* bufs = S.alloc<uint64_t>((size_t)unitsMax * QpMax * C);
     uint32_t* cnts = S.alloc<uint32_t>((size_t)unitsMax * QpMax);
     uint64_t* thrs = S.alloc<uint64_t>((size_t)unitsMax * QpMax);
@@ -670,10 +681,14 @@ int search_quantized_scan(vx_index* ix, const float* dq, int nq, int K, int k_ou
       const int units = gemm_scan_units(ntiles, mblocks, ix->num_sms, two_sm);
       const float* dqc = dq + (size_t)q0 * dim;
       VX_CUDA(cudaMemsetAsync(qcodes + (size_t)qc * ix->Dp8, 0, (size_t)(Qp - qc) * ix->Dp8, st));
-      if (bq)
+      if (bq) {
         VX_LAUNCH(1, launch_bq_queries_to_i8(dqc, qc, dim, ix->Dp8, qcodes, st));
-      else
+      } else if (bbq) {
+        VX_LAUNCH(1, launch_bbq_prep_queries(dqc, qc, dim, ix->bbq_centroid, ix->nw_pad, qplanes, qinfo, st));
+        VX_LAUNCH(1, launch_bbq_planes_to_i8(qplanes, qc, dim, ix->nw_pad, ix->Dp8, qcodes, st));
+      } else {
         VX_LAUNCH(1, launch_sq8_encode_queries(dqc, qc, dim, ix->Dp8, kc, qcodes, qcorr, qsq, st));
+      }
       CUtensorMap tmq;
       make_tmap(&tmq, qcodes, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, ix->Dp8, Qp, 128);
       ScanArgs a;
@@ -697,6 +712,8 @@ int search_quantized_scan(vx_index* ix, const float* dq, int nq, int K, int k_ou
       a.epi.vsq = ix->vsq;
       a.epi.cm = kc.cm;
       a.epi.bits = dim;
+      a.epi.bbq_rows = ix->bbq_epi;
+      a.epi.bbq_q = qinfo;
       scan_and_merge(mode, tmq, ix->tm_codes8, a, units, R, Qp, floor, tops, probe, keys, kcnt, st);
       if (rescore) {
         RescoreArgs r{};
@@ -1495,6 +1512,18 @@ int vx_bbq_build(int32_t device, const uint64_t* words, const float* corrections
         cudaFree(corr);
         VX_CUDA(e);
         g_launches.fetch_add(1);
+        // 0/1 int8 operand and epilogue records for the tensor-core scan (8 bytes per bit)
+        const int Dp8 = (int)round_up(dim, 128);
+        if (bq_tensor_budget() >= (uint64_t)n * Dp8) {
+          ix->Dp8 = Dp8;
+          ix->codes8 = dev_alloc<int8_t>(ix, (size_t)n * Dp8);
+          ix->bbq_epi = dev_alloc<float4>(ix, (size_t)n);
+          VX_LAUNCH(1, launch_bq_words_to_i8(ix->words, n, nwp, dim, Dp8, ix->codes8, 0, true));
+          VX_LAUNCH(1, launch_bbq_epi_rows(ix->bbq_rows, n, dim, metric, ix->bbq_epi, 0));
+          VX_CUDA(cudaDeviceSynchronize());
+          make_tmap(&ix->tm_codes8, ix->codes8, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, Dp8, n,
+                    gemm_scan_db_box(gemm_two_sm()));
+        }
         if (vectors) ix->rows32 = upload_rows32(ix, vectors, n, dim, row_stride);
       }
     } catch (...) {
