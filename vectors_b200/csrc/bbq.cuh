@@ -17,11 +17,17 @@ __device__ __forceinline__ float bbq_row_term(float vl, float width, int dim, in
 }
 
 // computeBbqDot from the query's (queryMin, queryWidth / 15, querySum), the row's (vl, width,
-// row term) and rawAsymDot.
+// row term) and rawAsymDot as a float (exact: |raw| <= 15 * 1024).
 __device__ __forceinline__ float bbq_approx(float qmin, float w15, float qsum, float vl, float width, float s1,
-                                            int32_t raw) {
-  const float s2 = __fadd_rn(__fmul_rn(vl, qsum), __fmul_rn(width, (float)raw));
+                                            float raw) {
+  const float s2 = __fadd_rn(__fmul_rn(vl, qsum), __fmul_rn(width, raw));
   return __fadd_rn(__fmul_rn(qmin, s1), __fmul_rn(w15, s2));
+}
+
+// (float) raw for 0 <= raw < 2^23 without the conversion unit: 2^23 + raw has raw as its
+// mantissa, and subtracting 2^23 is exact.
+__device__ __forceinline__ float bbq_raw_to_float(int32_t raw) {
+  return __fsub_rn(__int_as_float(0x4B000000 | raw), 8388608.0f);
 }
 
 // EUCLIDEAN: max(queryNormSq + |v - c|^2 - 2 approx, 0) (NaN -> 0); the score is 1 / (1 + that),

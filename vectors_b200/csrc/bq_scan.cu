@@ -250,7 +250,8 @@ __device__ __forceinline__ int32_t popc_and16(const uint64_t* x, const uint64_t 
 __device__ __forceinline__ float bbq_score(int metric, const BbqQuery& qi, float4 ri, int32_t raw, int dim) {
   const float dist_c = ri.x, vl = ri.y, width = ri.z;
   const int32_t pop = __float_as_int(ri.w);
-  const float approx = bbq_approx(qi.qmin, qi.w15, (float)qi.qsum, vl, width, bbq_row_term(vl, width, dim, pop), raw);
+  const float approx =
+      bbq_approx(qi.qmin, qi.w15, (float)qi.qsum, vl, width, bbq_row_term(vl, width, dim, pop), (float)raw);
   switch (metric) {
     case kEuclidean: return bbq_l2_score(bbq_l2_adj(approx, qi.nsq, dist_c));
     case kCosine: return bbq_cos_score(approx, qi.norm, bbq_vnorm(dist_c));
