@@ -24,12 +24,6 @@ __device__ __forceinline__ float bbq_approx(float qmin, float w15, float qsum, f
   return __fadd_rn(__fmul_rn(qmin, s1), __fmul_rn(w15, s2));
 }
 
-// (float) raw for 0 <= raw < 2^23 without the conversion unit: 2^23 + raw has raw as its
-// mantissa, and subtracting 2^23 is exact.
-__device__ __forceinline__ float bbq_raw_to_float(int32_t raw) {
-  return __fsub_rn(__int_as_float(0x4B000000 | raw), 8388608.0f);
-}
-
 // EUCLIDEAN: max(queryNormSq + |v - c|^2 - 2 approx, 0) (NaN -> 0); the score is 1 / (1 + that),
 // non-increasing in it.
 __device__ __forceinline__ float bbq_l2_adj(float approx, float nsq, float dist_c) {

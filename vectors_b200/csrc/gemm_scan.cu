@@ -45,8 +45,8 @@ constexpr int TMEM_COLS = 512;
 constexpr int kStageRowWords = 36;  // per-lane staging row: 32 values + 4 words of padding
                                     // (16-byte stores of 8 lanes hit 8 distinct bank quads)
 
-// Per-row floats the epilogue stages for each tile: two arrays (row scale, |x|^2 or the SQ8
-// terms), or one four-float record per row for BBQ.
+// Per-row float arrays the epilogue stages for each tile: two (row scale, |x|^2 or the SQ8
+// terms), four for BBQ.
 __host__ __device__ constexpr int cols_of(int mode) { return epi_is_bbq(mode) ? 4 : 2; }
 
 template <bool k2Sm, int kCols>
@@ -88,31 +88,23 @@ __device__ __forceinline__ void apply_floor(const ScanArgs& a, int q, bool activ
 }
 
 // Ranking score of one accumulator value in epilogue mode kMode (gemm_scan.h).
-// BBQ: the staged row record of column col, (vl, width, vl * D + width * pop, |v - c| or
-// |v - c|^2), one 16-byte load that every lane shares; computeBbqDot of one accumulator value
-// (rawAsymDot, 0 <= raw <= 15 * 1024) against it.  qb holds the lane's query (queryMin,
-// queryWidth / 15, querySum, queryNormSq or queryNorm).
-__device__ __forceinline__ float4 bbq_rec(const float* s_col, int col) {
-  return reinterpret_cast<const float4*>(s_col)[col];
-}
-__device__ __forceinline__ float bbq_approx_rec(uint32_t v, const float4& r, const float4& qb) {
-  return bbq_approx(qb.x, qb.y, qb.z, r.x, r.y, r.z, bbq_raw_to_float((int32_t)v));
+// BBQ: computeBbqDot of one accumulator value (rawAsymDot) against the staged row record
+// s_col[col] = vl, s_col[256 + col] = width, s_col[512 + col] = vl * D + width * pop
+// (s_col[768 + col] = |v - c| or |v - c|^2); qb holds the lane's query (queryMin,
+// queryWidth / 15, querySum, queryNormSq or queryNorm).  Neither a 16-byte record load per
+// column nor an integer-to-float by the 2^23 bias (LOP3 + FADD) made the scan faster.
+__device__ __forceinline__ float bbq_approx_at(uint32_t v, int col, const float* s_col, const float4& qb) {
+  return bbq_approx(qb.x, qb.y, qb.z, s_col[col], s_col[256 + col], s_col[512 + col], __int2float_rn((int32_t)v));
 }
 
 template <int kMode>
 __device__ __forceinline__ float score_of(uint32_t v, int col, const float* s_col, const float* s_col2,
                                           float qa, int32_t qi, float cm, const float4& qb) {
   if (kMode == kEpiF16Plain) return __uint_as_float(v);
-  if (kMode == kEpiBbqDot) return bbq_dot_score(bbq_approx_rec(v, bbq_rec(s_col, col), qb));
-  if (kMode == kEpiBbqMip) return scale_mip(bbq_approx_rec(v, bbq_rec(s_col, col), qb));
-  if (kMode == kEpiBbqL2) {
-    const float4 r = bbq_rec(s_col, col);
-    return bbq_l2_score(bbq_l2_adj(bbq_approx_rec(v, r, qb), qb.w, r.w));
-  }
-  if (kMode == kEpiBbqCos) {
-    const float4 r = bbq_rec(s_col, col);
-    return bbq_cos_score(bbq_approx_rec(v, r, qb), qb.w, r.w);
-  }
+  if (kMode == kEpiBbqDot) return bbq_dot_score(bbq_approx_at(v, col, s_col, qb));
+  if (kMode == kEpiBbqMip) return scale_mip(bbq_approx_at(v, col, s_col, qb));
+  if (kMode == kEpiBbqL2) return bbq_l2_score(bbq_l2_adj(bbq_approx_at(v, col, s_col, qb), qb.w, s_col[768 + col]));
+  if (kMode == kEpiBbqCos) return bbq_cos_score(bbq_approx_at(v, col, s_col, qb), qb.w, s_col[768 + col]);
   if (kMode == kEpiF16Scaled) return __uint_as_float(v) * s_col[col];
   if (kMode == kEpiF16L2) return fmaf(qa * s_col[col], __uint_as_float(v), -s_col2[col]);
   if (kMode == kEpiSq8Dot || kMode == kEpiSq8Mip) {
@@ -212,8 +204,7 @@ __device__ __forceinline__ float group_max(const uint32_t (&v)[32], int c0, cons
     float m[16];
 #pragma unroll
     for (int i = 0; i < 16; i++)
-      m[i] = fmaxf(bbq_approx_rec(v[2 * i], bbq_rec(s_col, c0 + 2 * i), qb),
-                   bbq_approx_rec(v[2 * i + 1], bbq_rec(s_col, c0 + 2 * i + 1), qb));
+      m[i] = fmaxf(bbq_approx_at(v[2 * i], c0 + 2 * i, s_col, qb), bbq_approx_at(v[2 * i + 1], c0 + 2 * i + 1, s_col, qb));
 #pragma unroll
     for (int w = 8; w >= 1; w >>= 1)
 #pragma unroll
@@ -223,11 +214,10 @@ __device__ __forceinline__ float group_max(const uint32_t (&v)[32], int c0, cons
     // exact: the smallest clamped distance term (never NaN), then the non-increasing tail
     float m[16];
 #pragma unroll
-    for (int i = 0; i < 16; i++) {
-      const float4 r0 = bbq_rec(s_col, c0 + 2 * i), r1 = bbq_rec(s_col, c0 + 2 * i + 1);
-      m[i] = fminf(bbq_l2_adj(bbq_approx_rec(v[2 * i], r0, qb), qb.w, r0.w),
-                   bbq_l2_adj(bbq_approx_rec(v[2 * i + 1], r1, qb), qb.w, r1.w));
-    }
+    for (int i = 0; i < 16; i++)
+      m[i] = fminf(bbq_l2_adj(bbq_approx_at(v[2 * i], c0 + 2 * i, s_col, qb), qb.w, s_col[768 + c0 + 2 * i]),
+                   bbq_l2_adj(bbq_approx_at(v[2 * i + 1], c0 + 2 * i + 1, s_col, qb), qb.w,
+                              s_col[768 + c0 + 2 * i + 1]));
 #pragma unroll
     for (int w = 8; w >= 1; w >>= 1)
 #pragma unroll
@@ -486,7 +476,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           } else if (kMode == kEpiSq8Dot || kMode == kEpiSq8Mip) {
             s_col[i] = in ? a.epi.vcorr[row] : 0.0f;
           } else if (epi_is_bbq(kMode)) {
-            reinterpret_cast<float4*>(s_col)[i] = in ? a.epi.bbq_rows[row] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            const float4 r = in ? a.epi.bbq_rows[row] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            s_col[i] = r.x;
+            s_col[256 + i] = r.y;
+            s_col[512 + i] = r.z;
+            s_col[768 + i] = r.w;
           } else {  // kEpiSq8L2
             s_col[i] = __int_as_float(in ? a.epi.vsq[row] : 0);
           }
