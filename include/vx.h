@@ -138,7 +138,9 @@ VX_API int vx_bq_build(int32_t device, const uint64_t* words, int64_t n, int32_t
 /* BinaryQuantizedVectors BBQ (BinaryQuantizedVectors.java:110-275, BinaryQuantizer.java:199-270):
  * words [n][ceil(dim/64)] of the centroid-relative sign bits, corrections [n][3] =
  * (|v - c|^2, vl, width), the centroid [dim].  Scored as bbqScoreFunction does: the query
- * centred and quantised to 4 bits, rawAsymDot from its 4 bit planes (exact), computeBbqDot and
+ * centred and quantised to 4 bits, rawAsymDot exactly (the 4-bit codes times a 0/1 int8 copy of
+ * the bits on the int8 tensor cores, 8 bytes of device memory per stored bit, within the
+ * VX_BQ_TENSOR_BYTES budget; above it, popcounts of the query's 4 bit planes), computeBbqDot and
  * the metric's transform in the Java float order.  dim <= 1024. */
 VX_API int vx_bbq_build(int32_t device, const uint64_t* words, const float* corrections, const float* centroid,
                         int64_t n, int32_t dim, int32_t metric, const float* vectors, int64_t row_stride,
