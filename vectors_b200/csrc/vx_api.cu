@@ -232,6 +232,22 @@ T* dev_alloc(vx_index* ix, size_t count) {
   return (T*)p;
 }
 
+// A build's temporary device buffer, released when it leaves scope (the error path included).
+template <class T>
+struct DevTemp {
+  T* p = nullptr;
+  explicit DevTemp(size_t count) {
+    void* q = nullptr;
+    VX_CUDA(cudaMalloc(&q, std::max<size_t>(count * sizeof(T), 16)));
+    p = (T*)q;
+  }
+  ~DevTemp() {
+    if (p) cudaFree(p);
+  }
+  DevTemp(const DevTemp&) = delete;
+  DevTemp& operator=(const DevTemp&) = delete;
+};
+
 void free_index(vx_index* ix) {
   if (!ix) return;
   cudaSetDevice(ix->device);
@@ -1345,8 +1361,8 @@ int vx_fp16_build(int32_t device, const uint16_t* codes, int64_t n, int32_t dim,
     try {
       if (n > 0) {
         ix->Dp = (int)round_up(dim, 64);
-        __half* raw = nullptr;
-        VX_CUDA(cudaMalloc(&raw, (size_t)n * dim * 2));
+        DevTemp<__half> raw_buf((size_t)n * dim);
+        __half* raw = raw_buf.p;
         VX_CUDA(cudaMemcpy(raw, codes, (size_t)n * dim * 2, cudaMemcpyDefault));
         ix->rows16 = dev_alloc<__half>(ix, (size_t)n * ix->Dp);
         ix->rowsq = dev_alloc<float>(ix, (size_t)n);
@@ -1357,7 +1373,6 @@ int vx_fp16_build(int32_t device, const uint16_t* codes, int64_t n, int32_t dim,
         VX_CUDA(cudaMemcpy(ix->rowscale, ones.data(), (size_t)n * 4, cudaMemcpyDefault));
         VX_LAUNCH(1, launch_f16_rows_pad(raw, n, dim, ix->Dp, ix->rows16, ix->rowsq, ix->max_norm, 0));
         VX_CUDA(cudaDeviceSynchronize());
-        cudaFree(raw);
         make_tmap(&ix->tm_rows, ix->rows16, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, ix->Dp, n,
                  gemm_scan_db_box(gemm_two_sm()));
         ix->has_tm_rows = true;
@@ -1445,8 +1460,8 @@ int sq_build(int32_t device, const int8_t* codes, const float* corrections, int6
     try {
       if (n > 0) {
         ix->Dp8 = (int)round_up(dim, 128);
-        int8_t* raw = nullptr;
-        VX_CUDA(cudaMalloc(&raw, (size_t)n * dim));
+        DevTemp<int8_t> raw_buf((size_t)n * dim);
+        int8_t* raw = raw_buf.p;
         VX_CUDA(cudaMemcpy(raw, codes, (size_t)n * dim, cudaMemcpyDefault));
         ix->codes8 = dev_alloc<int8_t>(ix, (size_t)n * ix->Dp8);
         ix->vsq = dev_alloc<int32_t>(ix, (size_t)n);
@@ -1454,7 +1469,6 @@ int sq_build(int32_t device, const int8_t* codes, const float* corrections, int6
         VX_CUDA(cudaMemcpy(ix->vcorr, corrections, (size_t)n * 4, cudaMemcpyDefault));
         VX_LAUNCH(1, launch_sq8_rows_pad(raw, n, dim, ix->Dp8, ix->codes8, ix->vsq, 0));
         VX_CUDA(cudaDeviceSynchronize());
-        cudaFree(raw);
         make_tmap(&ix->tm_codes8, ix->codes8, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, ix->Dp8, n,
                  gemm_scan_db_box(gemm_two_sm()));
         if (vectors) ix->rows32 = upload_rows32(ix, vectors, n, dim, row_stride);
@@ -1503,15 +1517,11 @@ int vx_bbq_build(int32_t device, const uint64_t* words, const float* corrections
         VX_CUDA(cudaMemset(ix->words, 0, (size_t)n * nwp * 8));
         VX_CUDA(cudaMemcpy2D(ix->words, (size_t)nwp * 8, words, (size_t)nw * 8, (size_t)nw * 8, (size_t)n,
                              cudaMemcpyDefault));
-        float* corr = nullptr;
-        VX_CUDA(cudaMalloc(&corr, (size_t)n * 12));
-        cudaError_t e = cudaMemcpy(corr, corrections, (size_t)n * 12, cudaMemcpyDefault);
+        DevTemp<float> corr((size_t)n * 3);
+        VX_CUDA(cudaMemcpy(corr.p, corrections, (size_t)n * 12, cudaMemcpyDefault));
         ix->bbq_rows = dev_alloc<float4>(ix, (size_t)n);
-        if (e == cudaSuccess) e = launch_bbq_rowinfo(ix->words, nw, nwp, corr, n, ix->bbq_rows, 0);
-        if (e == cudaSuccess) e = cudaDeviceSynchronize();
-        cudaFree(corr);
-        VX_CUDA(e);
-        g_launches.fetch_add(1);
+        VX_LAUNCH(1, launch_bbq_rowinfo(ix->words, nw, nwp, corr.p, n, ix->bbq_rows, 0));
+        VX_CUDA(cudaDeviceSynchronize());
         // 0/1 int8 operand and epilogue records for the tensor-core scan (8 bytes per bit)
         const int Dp8 = (int)round_up(dim, 128);
         if (bq_tensor_budget() >= (uint64_t)n * Dp8) {
@@ -1736,15 +1746,11 @@ int vx_ivfflat_build(int32_t device, const float* centroids, int32_t nlist, int3
       if (nl > 0) {
         VX_CUDA(cudaMemcpy(ix->ordinals, list_ordinals, (size_t)nl * 4, cudaMemcpyDefault));
         // the rows as dense [n][dim] on the device, then gathered into list order, padded
-        float* dense = nullptr;
-        VX_CUDA(cudaMalloc(&dense, (size_t)n * dim * 4));
-        cudaError_t e = cudaMemcpy2D(dense, (size_t)dim * 4, vectors, (size_t)row_stride * 4, (size_t)dim * 4,
-                                     (size_t)n, cudaMemcpyDefault);
-        if (e == cudaSuccess) e = launch_pad_rows(dense, nl, dim, dim, ix->ordinals, ix->Dp_flat, ix->flat_rows, 0);
-        if (e == cudaSuccess) e = cudaDeviceSynchronize();
-        cudaFree(dense);
-        VX_CUDA(e);
-        g_launches.fetch_add(1);
+        DevTemp<float> dense((size_t)n * dim);
+        VX_CUDA(cudaMemcpy2D(dense.p, (size_t)dim * 4, vectors, (size_t)row_stride * 4, (size_t)dim * 4, (size_t)n,
+                             cudaMemcpyDefault));
+        VX_LAUNCH(1, launch_pad_rows(dense.p, nl, dim, dim, ix->ordinals, ix->Dp_flat, ix->flat_rows, 0));
+        VX_CUDA(cudaDeviceSynchronize());
         if (ix->flat_norms) VX_LAUNCH(1, launch_row_norms(ix->flat_rows, nl, dim, ix->Dp_flat, ix->flat_norms, 0));
         VX_CUDA(cudaDeviceSynchronize());
       }
