@@ -180,6 +180,15 @@ bool use_pilot() {
   return v;
 }
 
+// Pooled admission floors (ScanArgs::top1) unless VX_SCAN_POOL=0.
+bool use_pool() {
+  static const bool v = [] {
+    const char* e = getenv("VX_SCAN_POOL");
+    return !(e && *e == '0');
+  }();
+  return v;
+}
+
 // BQ indexes also keep a +-1 int8 copy of the bits (8x the storage) for the tensor-core
 // Hamming scan while it fits VX_BQ_TENSOR_BYTES (default 64 GiB; 0 keeps the popcount scan).
 uint64_t bq_tensor_budget() {
@@ -447,7 +456,7 @@ void scan_and_merge(int mode, const CUtensorMap& tmq, const CUtensorMap& tmrows,
   a.top1 = a.top2 = nullptr;
   a.pool_j = a.K <= units ? 1 : (a.K <= 2 * units ? 2 : 0);
   a.pool_g = a.pool_j ? (a.K + a.pool_j - 1) / a.pool_j : 0;
-  if (a.pool_j && tops) {
+  if (a.pool_j && tops && use_pool()) {
     a.top1 = tops;
     a.top2 = tops + (size_t)units * Qp;
     VX_CUDA(cudaMemsetAsync(tops, 0, (size_t)2 * units * Qp * 8, st));
