@@ -1,7 +1,7 @@
-"""The 1-CTA tcgen05 scan, the scan without the pilot sweep, the popcount BQ scan, searches
-split into several query chunks (small scratch budget) and the IVF-PQ scan with one table per
-(query, list) pair agree with the oracle too (each variant in its own process: the library
-reads the switches once)."""
+"""The 1-CTA tcgen05 scan, the scan without the pilot sweep or without pooled floors, the
+popcount BQ / BBQ scans, searches split into several query chunks (small scratch budget) and the
+IVF-PQ scan with one table per (query, list) pair agree with the oracle too (each variant in
+its own process: the library reads the switches once)."""
 import os
 import subprocess
 import sys
@@ -14,8 +14,8 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 
 @pytest.mark.parametrize("env", [{"VX_GEMM_1SM": "1"}, {"VX_SCAN_PILOT": "0"}, {"VX_BQ_TENSOR_BYTES": "0"},
-                                 {"VX_SCRATCH_BYTES": "50000000"}],
-                         ids=["one_cta", "no_pilot", "bq_popcount", "query_chunks"])
+                                 {"VX_SCRATCH_BYTES": "50000000"}, {"VX_SCAN_POOL": "0"}],
+                         ids=["one_cta", "no_pilot", "bq_popcount", "query_chunks", "no_pooled_floors"])
 def test_scan_variant_matches_oracle(env):
     e = dict(os.environ)
     e.update(env)

@@ -1,5 +1,5 @@
 """Child process for test_gpu_scan_variants.py: the scan variant is chosen by environment
-variables that the library reads once per process (VX_GEMM_1SM, VX_SCAN_PILOT,
+variables that the library reads once per process (VX_GEMM_1SM, VX_SCAN_PILOT, VX_SCAN_POOL,
 VX_BQ_TENSOR_BYTES, VX_ADC_GROUPED), so each variant runs in a process of its own.
 Exits 0 when FLAT, SQ8, BQ and BBQ results (or, with the argument "ivf", IVF-PQ results) match
 the oracle."""
