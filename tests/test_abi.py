@@ -80,6 +80,31 @@ def test_argument_validation_before_gpu():
         vx.SearchOutcome(np.zeros(2, np.int32), np.zeros(3, np.float32))
 
 
+def test_quantized_builds_reject_mismatched_shapes():
+    # the C entry points read n x width elements of each array: a mismatch must raise before
+    # the library is called (no GPU needed), as a Java array of the wrong length would
+    import vectors_b200 as vx
+
+    a = vx.QuantizedFlatScanAdapter()
+    dot = vx.SimilarityFunction.DOT_PRODUCT
+    codes = np.zeros((5, 8), np.int8)
+    with pytest.raises(vx.IllegalArgumentException, match="corrections"):
+        a.build_sq8(codes, np.zeros(4, np.float32), -1.0, 1.0, dot)
+    with pytest.raises(vx.IllegalArgumentException, match="vectors"):
+        a.build_sq8(codes, np.zeros(5, np.float32), -1.0, 1.0, dot, vectors=np.zeros((5, 7), np.float32))
+    with pytest.raises(vx.IllegalArgumentException, match="corrections"):
+        a.build_sq4(np.zeros((5, 4), np.uint8), np.zeros(6, np.float32), 8, -1.0, 1.0, dot)
+    with pytest.raises(vx.IllegalArgumentException, match="words"):
+        a.build_bq(np.zeros((5, 1), np.uint64), 100, dot)
+    with pytest.raises(vx.IllegalArgumentException, match="vectors"):
+        a.build_bq(np.zeros((5, 2), np.uint64), 100, dot, vectors=np.zeros((4, 100), np.float32))
+    with pytest.raises(vx.IllegalArgumentException, match="words"):
+        a.build_bbq(np.zeros((5, 3), np.uint64), np.zeros((5, 3), np.float32), np.zeros(100, np.float32), 100, dot)
+    with pytest.raises(vx.IllegalArgumentException, match="vectors"):
+        a.build_fp16(np.zeros((5, 8), np.uint16), dot, vectors=np.zeros((5, 9), np.float32))
+    assert a.size() == 0
+
+
 def test_null_pointer_status_from_c():
     import ctypes as C
 

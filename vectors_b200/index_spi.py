@@ -105,6 +105,19 @@ def _as_matrix(vectors, name: str) -> np.ndarray:
     return a
 
 
+def _expect_shape(a: np.ndarray, shape, name: str) -> None:
+    """The C entry points read exactly this many elements; a Java array of another length
+    would have thrown, so a mismatch is an IllegalArgumentException, never a short read."""
+    if a.shape != tuple(shape):
+        raise IllegalArgumentException(f"{name} must be {list(shape)}, got {list(a.shape)}")
+
+
+def _expect_rows(v, n: int, dim: int) -> None:
+    """Optional fp32 rows (two-pass rescore) must match the encoded index: [n][dim]."""
+    if v is not None:
+        _expect_shape(v, (n, dim), "vectors")
+
+
 def _file_bytes(data) -> np.ndarray:
     """The bytes of a persistent file: a path, bytes-like, or a uint8 array (e.g. np.memmap)."""
     if isinstance(data, (str, os.PathLike)):
@@ -323,7 +336,11 @@ class QuantizedFlatScanAdapter(IndexSpi):
         codes = np.ascontiguousarray(np.asarray(codes, dtype=np.int8))
         corr = np.ascontiguousarray(np.asarray(corrections, dtype=np.float32))
         v = None if vectors is None else _as_matrix(vectors, "vectors")
+        if codes.ndim != 2:
+            raise IllegalArgumentException("codes must be [n][dim]")
         n, dim = codes.shape
+        _expect_shape(corr, (n,), "corrections")
+        _expect_rows(v, n, dim)
         self._h.close()
         _check(
             N.lib().vx_sq8_build(self.device, _ptr(codes), _ptr(corr), n, dim, float(min_quantile), float(max_quantile),
@@ -339,6 +356,8 @@ class QuantizedFlatScanAdapter(IndexSpi):
         n = packed.shape[0]
         if packed.ndim != 2 or packed.shape[1] != (dim + 1) // 2:
             raise IllegalArgumentException(f"packed codes must be [n][{(dim + 1) // 2}]")
+        _expect_shape(corr, (n,), "corrections")
+        _expect_rows(v, n, dim)
         self._h.close()
         _check(
             N.lib().vx_sq4_build(self.device, _ptr(packed), _ptr(corr), n, dim, float(min_quantile), float(max_quantile),
@@ -350,6 +369,8 @@ class QuantizedFlatScanAdapter(IndexSpi):
         words = np.ascontiguousarray(np.asarray(words, dtype=np.uint64))
         v = None if vectors is None else _as_matrix(vectors, "vectors")
         n = words.shape[0]
+        _expect_shape(words, (n, (dim + 63) // 64), "words")
+        _expect_rows(v, n, dim)
         self._h.close()
         _check(N.lib().vx_bq_build(self.device, _ptr(words), n, dim, int(metric), _ptr(v), dim, C.byref(self._h.ptr)))
         self._n, self._dim, self.metric, self.kind = n, dim, SimilarityFunction(metric), "BQ"
@@ -364,6 +385,8 @@ class QuantizedFlatScanAdapter(IndexSpi):
         n = words.shape[0]
         if corr.shape != (n, 3) or cent.shape != (dim,):
             raise IllegalArgumentException("corrections must be [n][3] and the centroid [dim]")
+        _expect_shape(words, (n, (dim + 63) // 64), "words")
+        _expect_rows(v, n, dim)
         self._h.close()
         _check(N.lib().vx_bbq_build(self.device, _ptr(words), _ptr(corr), _ptr(cent), n, dim, int(metric), _ptr(v), dim,
                                     C.byref(self._h.ptr)))
@@ -373,7 +396,6 @@ class QuantizedFlatScanAdapter(IndexSpi):
         """codes: [n][dim] binary16 bit patterns (numpy uint16, or a CUDA float16 / int16 tensor,
         copied on the device)."""
         v = None if vectors is None else _as_matrix(vectors, "vectors")
-        self._h.close()
         if getattr(codes, "is_cuda", False):
             t = codes.contiguous()
             if t.element_size() != 2:
@@ -382,8 +404,12 @@ class QuantizedFlatScanAdapter(IndexSpi):
             ptr = C.c_void_p(t.data_ptr())
         else:
             arr = np.ascontiguousarray(np.asarray(codes, dtype=np.uint16))
+            if arr.ndim != 2:
+                raise IllegalArgumentException("codes must be [n][dim]")
             n, dim = arr.shape
             ptr = _ptr(arr)
+        _expect_rows(v, n, dim)
+        self._h.close()
         _check(N.lib().vx_fp16_build(self.device, ptr, n, dim, int(metric), _ptr(v), dim, C.byref(self._h.ptr)))
         self._n, self._dim, self.metric, self.kind = n, dim, SimilarityFunction(metric), "FP16"
 
