@@ -105,6 +105,31 @@ def test_quantized_builds_reject_mismatched_shapes():
     assert a.size() == 0
 
 
+def test_ivf_builds_reject_mismatched_shapes():
+    import vectors_b200 as vx
+
+    cent = np.zeros((4, 16), np.float32)
+    off = np.array([0, 2, 3, 5, 6], np.int64)
+    ords = np.arange(6, dtype=np.int32)
+    cb = np.zeros(256 * 16, np.float32)
+    codes = np.zeros((6, 2), np.uint8)
+    l2 = vx.SimilarityFunction.EUCLIDEAN
+    p = vx.IvfPqAdapter()
+    with pytest.raises(vx.IllegalArgumentException, match="list_offsets"):
+        p.build_prebuilt(cent, off[:4], ords, cb, codes, 2, 256, l2)
+    with pytest.raises(vx.IllegalArgumentException, match="list_ordinals"):
+        p.build_prebuilt(cent, off, ords[:5], cb, codes, 2, 256, l2)
+    with pytest.raises(vx.IllegalArgumentException, match="codes"):
+        p.build_prebuilt(cent, off, ords, cb, codes[:, :1], 2, 256, l2)
+    with pytest.raises(vx.IllegalArgumentException, match="codebooks"):
+        p.build_prebuilt(cent, off, ords, cb[:100], codes, 2, 256, l2)
+    with pytest.raises(vx.IllegalArgumentException, match="vectors"):
+        p.build_prebuilt(cent, off, ords, cb, codes, 2, 256, l2, vectors=np.zeros((5, 16), np.float32))
+    f = vx.IvfFlatAdapter()
+    with pytest.raises(vx.IllegalArgumentException, match="list_ordinals"):
+        f.build_prebuilt(cent, off, ords[:4], np.zeros((6, 16), np.float32), l2)
+
+
 def test_null_pointer_status_from_c():
     import ctypes as C
 

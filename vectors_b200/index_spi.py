@@ -118,6 +118,15 @@ def _expect_rows(v, n: int, dim: int) -> None:
         _expect_shape(v, (n, dim), "vectors")
 
 
+def _expect_partitions(off: np.ndarray, ords: np.ndarray, nlist: int) -> None:
+    """CSR partitions: nlist + 1 offsets, as many ordinals as the last offset says."""
+    _expect_shape(off, (nlist + 1,), "list_offsets")
+    total = int(off[-1]) if off.size else 0
+    if ords.ndim != 1 or ords.shape[0] != total:
+        raise IllegalArgumentException(f"list_ordinals must hold list_offsets[nlist] = {total} ordinals, "
+                                       f"got {list(ords.shape)}")
+
+
 def _file_bytes(data) -> np.ndarray:
     """The bytes of a persistent file: a path, bytes-like, or a uint8 array (e.g. np.memmap)."""
     if isinstance(data, (str, os.PathLike)):
@@ -483,7 +492,13 @@ class IvfPqAdapter(IndexSpi):
         codes = np.ascontiguousarray(np.asarray(codes, dtype=np.uint8))
         v = None if vectors is None else _as_matrix(vectors, "vectors")
         nlist, dim = cent.shape
+        _expect_partitions(off, ords, nlist)
+        if codes.ndim != 2 or codes.shape[1] != m:
+            raise IllegalArgumentException(f"codes must be [n][{m}]")
         n = codes.shape[0]
+        if cb.size != ks * dim:
+            raise IllegalArgumentException(f"codebooks must hold ks * dim = {ks * dim} floats, got {cb.size}")
+        _expect_rows(v, n, dim)
         self._h.close()
         _check(
             N.lib().vx_ivfpq_build(self.device, _ptr(cent), nlist, dim, _ptr(off), _ptr(ords), m, ks, _ptr(cb), _ptr(codes),
@@ -587,6 +602,7 @@ class IvfFlatAdapter(IvfPqAdapter):
         off = np.ascontiguousarray(np.asarray(list_offsets, dtype=np.int64))
         ords = np.ascontiguousarray(np.asarray(list_ordinals, dtype=np.int32))
         nlist, dim = cent.shape
+        _expect_partitions(off, ords, nlist)
         if getattr(vectors, "is_cuda", False):
             t = vectors
             if t.dtype != __import__("torch").float32 or t.dim() != 2 or t.stride(1) != 1:
