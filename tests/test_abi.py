@@ -76,6 +76,11 @@ def test_argument_validation_before_gpu():
         f.search(None, 3)
     out = f.search_batch([[1.0, 2.0], [3.0, 4.0]], 3)
     assert len(out) == 2 and all(len(o.ordinals) == 0 for o in out)
+    # the SPI's default overloads: multi-start and predicate searches delegate to search
+    assert len(f.search([1.0, 2.0], 3, 0, 1.0, 4).ordinals) == 0
+    assert len(f.search_with_predicate([1.0, 2.0], 3, 0, 1.0, lambda o: o % 2 == 0).ordinals) == 0
+    with pytest.raises(vx.IllegalArgumentException):
+        f.search_with_predicate([1.0, 2.0], 0, 0, 1.0, lambda o: True)
     with pytest.raises(vx.IllegalArgumentException):
         vx.SearchOutcome(np.zeros(2, np.int32), np.zeros(3, np.float32))
 

@@ -216,13 +216,23 @@ class IndexSpi:
     def __exit__(self, *exc):
         self.close()
 
-    def search(self, query, k: int, search_list_size: int = 0, over_query_factor: float = 1.0) -> SearchOutcome:
+    def search(self, query, k: int, search_list_size: int = 0, over_query_factor: float = 1.0,
+               search_multi_start: int = 1) -> SearchOutcome:
+        """IndexSpi.search; the five-argument overload's searchMultiStart is ignored, as its
+        default does for every brute-force and IVF backend (IndexSpi.java:82-86)."""
         if query is None:
             raise NullPointerException("query must not be null")
         if k <= 0:
             raise IllegalArgumentException(f"k must be positive: {k}")
         q = np.asarray(query, dtype=np.float32).reshape(1, -1)
         return self.search_batch(q, k, search_list_size, over_query_factor)[0]
+
+    def search_with_predicate(self, query, k: int, search_list_size: int, over_query_factor: float,
+                              predicate) -> SearchOutcome:
+        """IndexSpi.searchWithPredicate (IndexSpi.java:103-107): the scan backends keep the default,
+        which ignores the predicate and searches; the caller post-filters the outcome
+        (VectorCollectionImpl.search widens k by filterExpansion for that)."""
+        return self.search(query, k, search_list_size, over_query_factor)
 
     def search_batch(self, queries, k: int, search_list_size: int = 0, over_query_factor: float = 1.0) -> list[SearchOutcome]:
         q = self._queries(queries, k)
