@@ -4,6 +4,8 @@ published algorithms.  CPU only.
 Sources (reference project paths):
   VectorUtilSupportTest.java:423-438,464-476  byte dot / L2 / Hamming known values
   BinaryQuantizerTest.java:55-75,484-532       sign-bit packing, zero -> 1, long packing
+  BinaryQuantizerTest.java:150-227             BBQ: bits of v - centroid, (|v-c|^2, vl, width)
+  ScalarQuantizerTest.java:606-631             INT4: packed size, nibble layout
   TopKTest.java:55-135                         canonical top-k, ties by ordinal, infinities, NaN
   IndexSpiSearchBatchTest.java:47-93           batch == sequential
   QuantizedFlatScanAdapter.java:59-95          two-pass contract
@@ -20,6 +22,37 @@ GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
 def test_byte_kernels_known_values(oracle):
     assert oracle.byte_dot([1, 2, 3, 4], [5, 6, 7, 8]) == 70
     assert oracle.byte_square_distance([1, 2, 3], [4, 6, 8]) == 50
+
+
+def test_sq4_nibble_layout_and_size(oracle):
+    # fromQuantiles(4, INT4, 0, 15): {0, 5, 10, 15} sit on the levels; low nibble = even dimension
+    packed, _ = oracle.sq4_encode_all(0.0, 15.0, np.array([[0.0, 5.0, 10.0, 15.0]], np.float32))
+    assert packed.shape == (1, 2)
+    assert int(packed[0, 0]) & 0x0F == 0 and int(packed[0, 0]) >> 4 == 5
+    assert int(packed[0, 1]) & 0x0F == 10 and int(packed[0, 1]) >> 4 == 15
+    # ceil(129 / 2) = 65 bytes per vector
+    packed, _ = oracle.sq4_encode_all(-1.0, 1.0, np.zeros((1, 129), np.float32))
+    assert packed.shape == (1, 65)
+
+
+def test_bbq_centres_before_the_sign_bit(oracle):
+    # centroid [3, -3]: [2, -2] -> [-1, 1] -> bits 0b10; [4, -4] -> [1, -1] -> bits 0b01
+    v = np.array([[2.0, -2.0], [4.0, -4.0]], np.float32)
+    words, corr = oracle.bbq_encode_all(v, np.array([3.0, -3.0], np.float32))
+    assert int(words[0, 0]) == 0x02 and int(words[1, 0]) == 0x01
+    # corrections (|v - c|^2, min centred component, max - min)
+    assert corr.tolist() == [[2.0, -1.0, 2.0], [2.0, -1.0, 2.0]]
+
+
+def test_bbq_corrections_follow_their_definitions(oracle):
+    rng = np.random.default_rng(42)
+    v = rng.standard_normal((50, 64)).astype(np.float32)
+    c = v.mean(0).astype(np.float32)
+    _, corr = oracle.bbq_encode_all(v, c)
+    x = v - c
+    np.testing.assert_allclose(corr[:, 0], (x.astype(np.float64) ** 2).sum(1), rtol=0, atol=1e-3)
+    assert np.array_equal(corr[:, 1], x.min(1))
+    assert np.array_equal(corr[:, 2], x.max(1) - x.min(1))
 
 
 def test_hamming_known_values(oracle):
