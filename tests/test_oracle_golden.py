@@ -6,6 +6,7 @@ Sources (reference project paths):
   BinaryQuantizerTest.java:55-75,484-532       sign-bit packing, zero -> 1, long packing
   BinaryQuantizerTest.java:150-227             BBQ: bits of v - centroid, (|v-c|^2, vl, width)
   ScalarQuantizerTest.java:606-631             INT4: packed size, nibble layout
+  IvfIndexIntegrationTest.java:113-135         probing every list finds the brute-force neighbours
   TopKTest.java:55-135                         canonical top-k, ties by ordinal, infinities, NaN
   IndexSpiSearchBatchTest.java:47-93           batch == sequential
   QuantizedFlatScanAdapter.java:59-95          two-pass contract
@@ -216,3 +217,18 @@ def test_golden_fixtures(oracle):
 
     now = compute(oracle)
     assert now == g
+
+
+@pytest.mark.parametrize("metric", [0, 1, 2])
+def test_ivfflat_probing_every_list_is_the_flat_scan(oracle, metric):
+    # nprobe = nlist visits every row, so IvfIndex.search returns the FlatScanAdapter neighbours
+    # (scores differ in scale: -distance / dot / cosine against SimilarityFunction.compare)
+    n, dim, nlist, k = 3000, 24, 8, 10
+    db = oracle.gen_mixture(n, dim, 6, 0.3, 0xC0FFEE03, 0xC0FFEE01, False)
+    q = oracle.gen_mixture(40, dim, 6, 0.3, 0xC0FFEE03, 0xC0FFEE02, False)
+    cent = oracle.kmeans_train(db[:1000], nlist, 8, 42)
+    off, ords = oracle.build_ivf_lists(oracle.kmeans_assign(db, cent), nlist)
+    i1, _, c1 = oracle.ivfflat_search(cent, off, ords, db, q, metric, k, nlist)
+    i2, _, c2 = oracle.flat_search(db, q, metric, k)
+    for j in range(len(q)):
+        assert list(i1[j, : c1[j]]) == list(i2[j, : c2[j]]), j
