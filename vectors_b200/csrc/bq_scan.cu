@@ -12,7 +12,9 @@
 // range of rows (a "part") and streams it through shared memory in 128-row tiles; every
 // thread owns one query (its words live in registers) and scores each staged row against
 // it.  The database is read from HBM once per batch; the binding roof is the integer/popc
-// pipe.
+// pipe.  These popcount scans serve BQ and BBQ indexes built without the int8 operand of the
+// tensor-core scan (gemm_scan.cu), and vx_bq_scan_candidates_noalloc; the file also holds the
+// BBQ query preparation and the per-row records both BBQ scans read.
 #include "bbq.cuh"
 #include "common.cuh"
 #include "kernels.h"
