@@ -105,7 +105,8 @@ VX_API int vx_debug_fail_next(int32_t status);
 
 /* ---- index construction (the handle owns device copies; inputs are not retained) ----- */
 /* Input arrays of the build calls may be host or device memory (unified addressing), except
- * vx_ivfpq_build, whose partitions and codes are regrouped on the host and must be host memory.
+ * the partitions (list_offsets, list_ordinals) of vx_ivfpq_build and vx_ivfflat_build and the
+ * codes of vx_ivfpq_build, which are validated or regrouped on the host and must be host memory.
  * FlatScanAdapter.build(float[][] vectors, SimilarityFunction metric)
  * (vectors-db/.../index/FlatScanAdapter.java:42-48).  row_stride in floats (>= dim); use
  * alignUp(dim*4, 64)/4 to read a persistent vectors.bin (MemorySegmentVectors.java:39-45). */
