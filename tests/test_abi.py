@@ -144,3 +144,37 @@ def test_null_pointer_status_from_c():
     assert st in (N.VX_ERR_NULL_POINTER, N.VX_ERR_GPU_UNAVAILABLE)
     assert N.lib().vx_device_count(None) == N.VX_ERR_NULL_POINTER
     assert "null" in N.last_error()
+
+
+def test_build_argument_statuses_before_the_gpu():
+    # shape, pointer and range checks of the newer build calls run before any device work, so
+    # these statuses hold with or without a GPU
+    import ctypes as C
+
+    import vectors_b200._native as N
+
+    L = N.lib()
+    out = C.c_void_p()
+    f = np.zeros(64, np.float32)
+    w = np.zeros(64, np.uint64)
+    p = lambda a: a.ctypes.data_as(C.c_void_p)  # noqa: E731
+    # BBQ: centroid required; more than 1024 dimensions unsupported
+    assert L.vx_bbq_build(0, p(w), p(f), None, 1, 64, 1, None, 64, C.byref(out)) == N.VX_ERR_NULL_POINTER
+    assert L.vx_bbq_build(0, p(w), p(f), p(f), 1, 2000, 1, None, 2000, C.byref(out)) == N.VX_ERR_UNSUPPORTED
+    assert "1024" in N.last_error()
+    assert L.vx_bbq_build(0, p(w), p(f), p(f), 1, 0, 1, None, 0, C.byref(out)) == N.VX_ERR_INVALID_ARGUMENT
+    # SQ4: codes required for a non-empty index
+    assert L.vx_sq4_build(0, None, p(f), 4, 8, -1.0, 1.0, 1, None, 8, C.byref(out)) == N.VX_ERR_NULL_POINTER
+    # IVF-flat: partitions validated on the host
+    cent = np.zeros((2, 4), np.float32)
+    rows = np.zeros((3, 4), np.float32)
+    ords = np.array([0, 1, 2], np.int32)
+    bad_start = np.array([1, 2, 3], np.int64)
+    assert L.vx_ivfflat_build(0, p(cent), 2, 4, p(bad_start), p(ords), p(rows), 3, 4, 0, 1,
+                              C.byref(out)) == N.VX_ERR_INVALID_ARGUMENT
+    bad_ord = np.array([0, 5, 2], np.int32)
+    off = np.array([0, 2, 3], np.int64)
+    assert L.vx_ivfflat_build(0, p(cent), 2, 4, p(off), p(bad_ord), p(rows), 3, 4, 0, 1,
+                              C.byref(out)) == N.VX_ERR_INVALID_ARGUMENT
+    assert "out of range" in N.last_error()
+    assert not out.value
