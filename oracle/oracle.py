@@ -84,6 +84,9 @@ def lib() -> C.CDLL:
             "vo_route": (None, [p, i32, i32, i32, p, i32, i32, i32, i32, p, p]),
             "vo_ivfpq_search": (None, [p, i32, i32, p, p, i32, i32, p, p, i64, i32, p, i32, i32, i32, i32, p, i32, i32, p, p, p]),
             "vo_ivfflat_search": (None, [p, i32, i32, p, p, p, i64, i32, p, i32, i32, i32, i32, i32, p, p, p]),
+            "vo_ivfflat_search_early_exit": (None, [p, i32, i32, p, p, p, i64, i32, p, p, i32, i32, i32, i32, i32, p, p,
+                                                    p]),
+            "vo_ivf_radii": (None, [p, i32, i32, p, p, p, p]),
             "vo_merge_shards": (None, [i32, p, p, p, p, i32, i32, i32, i32, p, p, p]),
             "vo_topk_select": (i32, [p, i32, i32, p]),
         }
@@ -404,6 +407,29 @@ def ivfflat_search(centroids, list_offsets, list_ordinals, vectors, queries, met
     ids, sc, cnt = _outs(q.shape[0], k)
     lib().vo_ivfflat_search(P(c), c.shape[0], c.shape[1], P(off), P(ords), P(v), v.shape[0], metric, P(q), q.shape[0],
                             k, nprobe, policy, nthreads or threads(), P(ids), P(sc), P(cnt))
+    return ids, sc, cnt
+
+
+def ivf_radii(centroids, list_offsets, list_ordinals, vectors):
+    """BuoyIndex.computeRadii over CSR partitions: the largest member distance per cluster."""
+    c, v = f32(centroids), f32(vectors)
+    off = np.ascontiguousarray(list_offsets, np.int64)
+    ords = np.ascontiguousarray(list_ordinals, np.int32)
+    out = np.empty(c.shape[0], np.float32)
+    lib().vo_ivf_radii(P(c), c.shape[0], c.shape[1], P(off), P(ords), P(v), P(out))
+    return out
+
+
+def ivfflat_search_early_exit(centroids, list_offsets, list_ordinals, vectors, radii, queries, metric, k, nprobe,
+                              policy=CANONICAL, nthreads=None):
+    """IvfIndex.search with the reference's EUCLIDEAN early exit against the given radii."""
+    c, q, v, r = f32(centroids), f32(queries), f32(vectors), f32(radii)
+    off = np.ascontiguousarray(list_offsets, np.int64)
+    ords = np.ascontiguousarray(list_ordinals, np.int32)
+    ids, sc, cnt = _outs(q.shape[0], k)
+    lib().vo_ivfflat_search_early_exit(P(c), c.shape[0], c.shape[1], P(off), P(ords), P(v), v.shape[0], metric, P(r),
+                                       P(q), q.shape[0], k, nprobe, policy, nthreads or threads(), P(ids), P(sc),
+                                       P(cnt))
     return ids, sc, cnt
 
 

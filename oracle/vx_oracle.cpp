@@ -1319,14 +1319,17 @@ void vo_ivfpq_search(const float* cent, int32_t nlist, int32_t dim, const int64_
 // dotProduct); score -d (EUCLIDEAN), dot (DOT_PRODUCT, MAXIMUM_INNER_PRODUCT) or
 // (float)(dot / sqrt((double)|q|^2 * (double)|v|^2)) with both norms from dotProduct (COSINE,
 // computeNormsSq :83-89); scores < minScore (-Float.MAX_VALUE) skipped; TopKHeap of k.
-// Not restated: the triangle-inequality early exit (:190-200) and the HARMONY key-dimension
-// path (:207-212, scanPartitionWithHarmony :279-289); both only skip clusters / rows that the
-// bound shows cannot enter the top k.
-void vo_ivfflat_search(const float* cent, int32_t nlist, int32_t dim, const int64_t* loff, const int32_t* lord,
-                       const float* vectors, int64_t n, int32_t metric, const float* queries, int32_t nq,
-                       int32_t k, int32_t nprobe, int32_t policy, int32_t nthreads, int32_t* ids, float* scores,
-                       int32_t* counts) {
-  (void)n;
+// The EUCLIDEAN triangle-inequality early exit (:190-200) is restated by
+// vo_ivfflat_search_early_exit (radii given): once the heap is full, the first cluster in route
+// order whose bound (max(0, (float) sqrt(centroid distance) - radius))^2 reaches the heap's
+// worst distance ends the scan, and every later cluster is skipped with it -- including one whose
+// larger radius leaves a smaller bound, so it can miss a closer row that scanning every probed
+// cluster (vo_ivfflat_search) finds.  Not restated: the HARMONY key-dimension path (:207-212,
+// scanPartitionWithHarmony :279-289) of partitions built with key dimensions.
+static void ivfflat_search(const float* cent, int32_t nlist, int32_t dim, const int64_t* loff, const int32_t* lord,
+                           const float* vectors, int32_t metric, const float* radii, const float* queries,
+                           int32_t nq, int32_t k, int32_t nprobe, int32_t policy, int32_t nthreads, int32_t* ids,
+                           float* scores, int32_t* counts) {
   int probes = std::min(nprobe, nlist);
   std::vector<int32_t> lids((size_t)nq * probes);
   std::vector<float> ld((size_t)nq * probes);
@@ -1341,6 +1344,19 @@ void vo_ivfflat_search(const float* cent, int32_t nlist, int32_t dim, const int6
       CanonTopK ch(k);
       for (int p = 0; p < probes; p++) {
         int cid = lids[(size_t)q * probes + p];
+        if (euclid && radii) {
+          const bool ref = policy == VO_POLICY_REFERENCE_HEAP;
+          const bool full = ref ? rh.size == rh.cap : (int)ch.v.size() == ch.cap;
+          if (full) {
+            const float worst = ref ? rh.sc[0] : ch.v.front().first;
+            const float centroid_l2 = (float)std::sqrt((double)ld[(size_t)q * probes + p]);
+            const float lb = centroid_l2 - radii[cid];
+            if (lb > 0.0f) {
+              const float lb_sq = lb * lb;
+              if (lb_sq >= -worst) break;  // route order is ascending: no later cluster is scanned
+            }
+          }
+        }
         int64_t b = loff[cid], e = loff[cid + 1];
         for (int64_t s0 = b; s0 < e; s0 += 64) {
           const int cnt = (int)std::min<int64_t>(64, e - s0);
@@ -1373,6 +1389,41 @@ void vo_ivfflat_search(const float* cent, int32_t nlist, int32_t dim, const int6
                                                      : ch.drain(ids + q * k, scores + q * k);
     }
   });
+}
+void vo_ivfflat_search(const float* cent, int32_t nlist, int32_t dim, const int64_t* loff, const int32_t* lord,
+                       const float* vectors, int64_t n, int32_t metric, const float* queries, int32_t nq,
+                       int32_t k, int32_t nprobe, int32_t policy, int32_t nthreads, int32_t* ids, float* scores,
+                       int32_t* counts) {
+  (void)n;
+  ivfflat_search(cent, nlist, dim, loff, lord, vectors, metric, nullptr, queries, nq, k, nprobe, policy, nthreads,
+                 ids, scores, counts);
+}
+void vo_ivfflat_search_early_exit(const float* cent, int32_t nlist, int32_t dim, const int64_t* loff,
+                                  const int32_t* lord, const float* vectors, int64_t n, int32_t metric,
+                                  const float* radii, const float* queries, int32_t nq, int32_t k, int32_t nprobe,
+                                  int32_t policy, int32_t nthreads, int32_t* ids, float* scores, int32_t* counts) {
+  (void)n;
+  ivfflat_search(cent, nlist, dim, loff, lord, vectors, metric, radii, queries, nq, k, nprobe, policy, nthreads,
+                 ids, scores, counts);
+}
+// BuoyIndex.computeRadii / euclideanDist (BuoyIndex.java:175-183,220-227).
+void vo_ivf_radii(const float* cent, int32_t nlist, int32_t dim, const int64_t* loff, const int32_t* lord,
+                  const float* vectors, float* radii) {
+  for (int l = 0; l < nlist; l++) {
+    float r = 0.0f;
+    const float* c = cent + (size_t)l * dim;
+    for (int64_t i = loff[l]; i < loff[l + 1]; i++) {
+      const float* v = vectors + (int64_t)lord[i] * dim;
+      float sum = 0.0f;
+      for (int d = 0; d < dim; d++) {
+        const float x = v[d] - c[d];
+        sum += x * x;
+      }
+      const float dist = (float)std::sqrt((double)sum);
+      if (dist > r) r = dist;
+    }
+    radii[l] = r;
+  }
 }
 // IndexShards.mergeWithOffsets (IndexShards.java:168-211).
 void vo_merge_shards(int32_t ns, const int64_t* offsets, const int32_t* sids, const float* ssc,

@@ -155,13 +155,26 @@ void vo_ivfpq_search(const float* centroids, int32_t nlist, int32_t dim, const i
                      const int32_t* list_ordinals, int32_t m, int32_t ks, const float* codebooks,
                      const uint8_t* codes /* [n][m], ordinal order */, int64_t n, int32_t metric,
                      const float* queries, int32_t nq, int32_t k, int32_t nprobe,
-                     int32_t rescore_factor, const float* vectors /* for rescore;
+                     int32_t rescore_factor, const float* vectors /* for rescore; may be NULL */,
+                     int32_t policy, int32_t nthreads, int32_t* ids, float* scores,
+                     int32_t* counts);
+/* IvfIndex.search without PQ (IvfIndex.java:170-277), every probed cluster scanned */
 void vo_ivfflat_search(const float* centroids, int32_t nlist, int32_t dim, const int64_t* list_offsets,
                        const int32_t* list_ordinals, const float* vectors, int64_t n, int32_t metric,
                        const float* queries, int32_t nq, int32_t k, int32_t nprobe, int32_t policy,
-                       int32_t nthreads, int32_t* ids, float* scores, int32_t* counts); may be NULL */,
-                     int32_t policy, int32_t nthreads, int32_t* ids, float* scores,
-                     int32_t* counts);
+                       int32_t nthreads, int32_t* ids, float* scores, int32_t* counts);
+/* The same with the reference's EUCLIDEAN triangle-inequality early exit (IvfIndex.java:190-200)
+ * against per-cluster radii (BuoyIndex.clusterRadii); other metrics ignore radii. */
+void vo_ivfflat_search_early_exit(const float* centroids, int32_t nlist, int32_t dim,
+                                  const int64_t* list_offsets, const int32_t* list_ordinals,
+                                  const float* vectors, int64_t n, int32_t metric, const float* radii,
+                                  const float* queries, int32_t nq, int32_t k, int32_t nprobe,
+                                  int32_t policy, int32_t nthreads, int32_t* ids, float* scores,
+                                  int32_t* counts);
+/* BuoyIndex.computeRadii (BuoyIndex.java:175-183): per cluster, the largest
+ * (float) sqrt(sum of (v - c)^2) over its members (sequential float sum); 0 for empty lists. */
+void vo_ivf_radii(const float* centroids, int32_t nlist, int32_t dim, const int64_t* list_offsets,
+                  const int32_t* list_ordinals, const float* vectors, float* radii);
 /* IndexShards.mergeWithOffsets (IndexShards.java:168-211); policy 0 = reference partial
  * selection sort (earlier shard wins ties), 1 = canonical. */
 void vo_merge_shards(int32_t nshards, const int64_t* offsets, const int32_t* shard_ids,

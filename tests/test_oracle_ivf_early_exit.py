@@ -1,0 +1,49 @@
+"""IvfIndex.search's EUCLIDEAN early exit (IvfIndex.java:190-200) against per-cluster radii
+(BuoyIndex.computeRadii, BuoyIndex.java:175-183), restated by the oracle.  The GPU scans every
+probed list; these CPU tests pin (1) that the reference's break can skip a closer row held by a
+later, wider cluster, and (2) that on the inputs of the IVF-flat GPU parity tests the break
+changes no result, so parity with the scan-all oracle there is parity with the reference."""
+import numpy as np
+import pytest
+
+SEED_C, SEED_DB, SEED_Q = 0xC0FFEE03, 0xC0FFEE01, 0xC0FFEE02
+
+
+def test_radii_are_the_largest_member_distance(oracle):
+    cent = np.array([[2, 0], [-2.5, 0], [0, 3]], np.float32)
+    rows = np.array([[2, 0], [-2.5, 0], [0, 3], [0, 1.1]], np.float32)
+    off = np.array([0, 1, 2, 4], np.int64)
+    ords = np.array([0, 1, 2, 3], np.int32)
+    assert oracle.ivf_radii(cent, off, ords, rows).tolist() == [0.0, 0.0, np.float32(1.9)]
+
+
+def test_break_skips_a_closer_row_in_a_wider_later_cluster(oracle):
+    # route order for q = 0: cluster 0 (d^2 4), 1 (6.25), 2 (9).  After cluster 0 the heap (k = 1)
+    # holds d^2 = 4; cluster 1's bound 2.5^2 >= 4 ends the scan, so cluster 2's row at d^2 1.21
+    # (bound (3 - 1.9)^2 = 1.21 < 4) is never seen
+    cent = np.array([[2, 0], [-2.5, 0], [0, 3]], np.float32)
+    rows = np.array([[2, 0], [-2.5, 0], [0, 3], [0, 1.1]], np.float32)
+    off = np.array([0, 1, 2, 4], np.int64)
+    ords = np.array([0, 1, 2, 3], np.int32)
+    q = np.zeros((1, 2), np.float32)
+    radii = oracle.ivf_radii(cent, off, ords, rows)
+    ids, sc, _ = oracle.ivfflat_search_early_exit(cent, off, ords, rows, radii, q, oracle.EUCLIDEAN, 1, 3)
+    assert ids[0, 0] == 0 and sc[0, 0] == -4.0
+    ids, sc, _ = oracle.ivfflat_search(cent, off, ords, rows, q, oracle.EUCLIDEAN, 1, 3)
+    assert ids[0, 0] == 3 and sc[0, 0] == np.float32(-1.21)
+
+
+@pytest.mark.parametrize("dim,nq,k", [(128, 400, 10), (96, 50, 50), (100, 40, 10), (7, 30, 5)])
+def test_break_changes_nothing_on_the_gpu_parity_inputs(oracle, dim, nq, k):
+    # the inputs of test_ivfflat_matches_oracle (EUCLIDEAN): 9,000 rows, 16 lists, 8 probes
+    n, nlist = 9000, 16
+    db = oracle.gen_mixture(n, dim, 12, 0.3, SEED_C, SEED_DB, False)
+    q = oracle.gen_mixture(nq, dim, 12, 0.3, SEED_C, SEED_Q, False)
+    cent = oracle.kmeans_train(db[:3000], nlist, 8, 42)
+    off, ords = oracle.build_ivf_lists(oracle.kmeans_assign(db, cent), nlist)
+    radii = oracle.ivf_radii(cent, off, ords, db)
+    a = oracle.ivfflat_search(cent, off, ords, db, q, oracle.EUCLIDEAN, k, 8)
+    b = oracle.ivfflat_search_early_exit(cent, off, ords, db, radii, q, oracle.EUCLIDEAN, k, 8)
+    for j in range(nq):
+        assert list(a[0][j, : a[2][j]]) == list(b[0][j, : b[2][j]]), j
+        assert np.array_equal(a[1][j, : a[2][j]], b[1][j, : b[2][j]]), j
