@@ -263,7 +263,7 @@ def test_ivfpq_bit_exact(oracle, metric, dim, nlist):
     _check_float(got, ids, sc, cnt, f"ivfpq rescore m={metric}")
 
 
-@pytest.mark.parametrize("metric", [0, 1, 2])
+@pytest.mark.parametrize("metric", [0, 1, 2, 3])
 @pytest.mark.parametrize("nlist", [32, 4])
 def test_ivfpq_grouped_bit_exact(oracle, metric, nlist):
     # 8-dim subspaces, 256 centroids, M a multiple of 16: the grouped ADC kernel (up to four
