@@ -47,3 +47,61 @@ def test_break_changes_nothing_on_the_gpu_parity_inputs(oracle, dim, nq, k):
     for j in range(nq):
         assert list(a[0][j, : a[2][j]]) == list(b[0][j, : b[2][j]]), j
         assert np.array_equal(a[1][j, : a[2][j]], b[1][j, : b[2][j]]), j
+
+
+def _ordered_merge(oracle, cent, off, ords, db, radii, q, k, nprobe):
+    """The early exit from per-list results: each probed list's own top-k (scored alone, in the
+    same batch order), merged in route order with the bound checked before each list -- the heap
+    after i lists is the k best of those lists' top-k."""
+    lids, dists = oracle.route(cent, q, oracle.EUCLIDEAN, nprobe)
+    out = []
+    for j in range(len(q)):
+        kept = []  # (score, id)
+        for p in range(nprobe):
+            cid = int(lids[j, p])
+            if len(kept) == k:
+                worst = kept[-1][0]
+                lb = np.float32(np.float32(np.sqrt(np.float64(dists[j, p]))) - radii[cid])
+                if lb > 0 and np.float32(lb * lb) >= -worst:
+                    break
+            b, e = int(off[cid]), int(off[cid + 1])
+            if e == b:
+                continue
+            one = np.array([0, e - b], np.int64)
+            ids, sc, cnt = oracle.ivfflat_search(cent[cid:cid + 1], one, ords[b:e], db, q[j:j + 1],
+                                                 oracle.EUCLIDEAN, k, 1)
+            kept += [(sc[0, i], int(ids[0, i])) for i in range(cnt[0])]
+            kept = sorted(kept, key=lambda t: (-t[0], t[1]))[:k]
+        out.append(kept)
+    return out
+
+
+@pytest.mark.parametrize("case", ["two_dims", "wide_late_clusters"])
+def test_ordered_merge_of_list_top_k_reproduces_the_break(oracle, case):
+    if case == "two_dims":
+        cent = np.array([[2, 0], [-2.5, 0], [0, 3]], np.float32)
+        db = np.array([[2, 0], [-2.5, 0], [0, 3], [0, 1.1]], np.float32)
+        off = np.array([0, 1, 2, 4], np.int64)
+        ords = np.array([0, 1, 2, 3], np.int32)
+        q = np.zeros((1, 2), np.float32)
+        k, nprobe = 1, 3
+    else:
+        # 2-D clusters of very different spreads, rows kept in the cluster that generated them:
+        # wide clusters late in route order hold rows the break skips (most queries change)
+        rng = np.random.default_rng(0)
+        cent = (10.0 * rng.standard_normal((8, 2))).astype(np.float32)
+        sig = np.array([0.2, 0.2, 0.3, 0.3, 0.5, 4.0, 6.0, 8.0], np.float32)
+        assign = rng.integers(0, 8, 2000)
+        db = (cent[assign] + sig[assign, None] * rng.standard_normal((2000, 2))).astype(np.float32)
+        off, ords = oracle.build_ivf_lists(assign.astype(np.int32), 8)
+        q = (10.0 * rng.standard_normal((60, 2))).astype(np.float32)
+        k, nprobe = 5, 8
+    radii = oracle.ivf_radii(cent, off, ords, db)
+    want = oracle.ivfflat_search_early_exit(cent, off, ords, db, radii, q, oracle.EUCLIDEAN, k, nprobe)
+    if case == "wide_late_clusters":
+        every = oracle.ivfflat_search(cent, off, ords, db, q, oracle.EUCLIDEAN, k, nprobe)
+        assert sum(not np.array_equal(every[0][j], want[0][j]) for j in range(len(q))) > len(q) // 4
+    got = _ordered_merge(oracle, cent, off, ords, db, radii, q, k, nprobe)
+    for j in range(len(q)):
+        assert [i for _, i in got[j]] == list(want[0][j, : want[2][j]]), j
+        assert [s for s, _ in got[j]] == list(want[1][j, : want[2][j]]), j
