@@ -87,6 +87,7 @@ def lib() -> C.CDLL:
             "vo_ivfflat_search_early_exit": (None, [p, i32, i32, p, p, p, i64, i32, p, p, i32, i32, i32, i32, i32, p, p,
                                                     p]),
             "vo_ivf_radii": (None, [p, i32, i32, p, p, p, p]),
+            "vo_route_spill": (None, [p, i32, i32, i32, p, i32, i32, f32, p, i32, p, p, p]),
             "vo_merge_shards": (None, [i32, p, p, p, p, i32, i32, i32, i32, p, p, p]),
             "vo_topk_select": (i32, [p, i32, i32, p]),
         }
@@ -383,6 +384,19 @@ def route(centroids, queries, metric, nprobe, policy=CANONICAL, nthreads=None):
     lib().vo_route(P(c), c.shape[0], c.shape[1], metric, P(q), q.shape[0], nprobe, policy, nthreads or threads(),
                    P(lids), P(dists))
     return lids, dists
+
+
+def route_spill(centroids, queries, metric, nprobe, gamma, spill_targets, nthreads=None):
+    """routeWithSpillDistances with SOAR spill: per query the lists (primaries ascending, then
+    spill targets) and their distances, trimmed to each query's count."""
+    c, q = f32(centroids), f32(queries)
+    sp = np.ascontiguousarray(spill_targets, np.int32)
+    lids = np.empty((q.shape[0], 2 * nprobe), np.int32)
+    dists = np.empty((q.shape[0], 2 * nprobe), np.float32)
+    cnt = np.empty(q.shape[0], np.int32)
+    lib().vo_route_spill(P(c), c.shape[0], c.shape[1], metric, P(q), q.shape[0], nprobe, float(gamma), P(sp),
+                         nthreads or threads(), P(lids), P(dists), P(cnt))
+    return [(lids[i, : cnt[i]], dists[i, : cnt[i]]) for i in range(q.shape[0])]
 
 
 def ivfpq_search(centroids, list_offsets, list_ordinals, m, ks, codebooks, codes, queries, metric, k, nprobe,

@@ -1137,6 +1137,22 @@ void vo_quantized_two_pass_search(int32_t kind, const void* qdata, const float* 
   });
 }
 // CentroidIndex.routeWithSpillDistances, gamma == 0 (CentroidIndex.java:89-211).
+// CentroidIndex.computeDistances (CentroidIndex.java:196-211): squared L2 (EUCLIDEAN), negated
+// cosine via the l2-normalised query (COSINE), negated dot (dot-style metrics).
+static void route_distances(const float* cent, int32_t nlist, int32_t dim, int32_t metric, const float* qq,
+                            float* d, float* qn) {
+  if (metric == VO_EUCLIDEAN) {
+    vo_mat_vec_square_l2(qq, cent, nlist, dim, d);
+  } else if (metric == VO_COSINE) {
+    std::memcpy(qn, qq, sizeof(float) * dim);
+    vo_l2normalize(qn, dim);
+    vo_mat_vec_dot(qn, cent, nlist, dim, d);
+    for (int i = 0; i < nlist; i++) d[i] = -d[i];
+  } else {
+    vo_mat_vec_dot(qq, cent, nlist, dim, d);
+    for (int i = 0; i < nlist; i++) d[i] = -d[i];
+  }
+}
 void vo_route(const float* cent, int32_t nlist, int32_t dim, int32_t metric, const float* queries,
               int32_t nq, int32_t nprobe, int32_t policy, int32_t nthreads, int32_t* list_ids,
               float* dists) {
@@ -1147,17 +1163,7 @@ void vo_route(const float* cent, int32_t nlist, int32_t dim, int32_t metric, con
     std::vector<float> tds(probes);
     for (int64_t q = lo; q < hi; q++) {
       const float* qq = queries + q * dim;
-      if (metric == VO_EUCLIDEAN) {
-        vo_mat_vec_square_l2(qq, cent, nlist, dim, d.data());
-      } else if (metric == VO_COSINE) {
-        std::memcpy(qn.data(), qq, sizeof(float) * dim);
-        vo_l2normalize(qn.data(), dim);
-        vo_mat_vec_dot(qn.data(), cent, nlist, dim, d.data());
-        for (int i = 0; i < nlist; i++) d[i] = -d[i];
-      } else {
-        vo_mat_vec_dot(qq, cent, nlist, dim, d.data());
-        for (int i = 0; i < nlist; i++) d[i] = -d[i];
-      }
+      route_distances(cent, nlist, dim, metric, qq, d.data(), qn.data());
       int32_t* oi = list_ids + q * nprobe;
       float* od = dists + q * nprobe;
       if (policy == VO_POLICY_CANONICAL) {
@@ -1218,6 +1224,60 @@ void vo_route(const float* cent, int32_t nlist, int32_t dim, int32_t metric, con
         oi[i] = tid[i];
         od[i] = tds[i];
       }
+    }
+  });
+}
+// CentroidIndex.routeWithSpillDistances with gamma > 0 (CentroidIndex.java:89-187,213-220): the
+// nprobe nearest in ascending order (reference heap, as vo_route), then, walking them in that
+// order while a primary's distance is within spillBoundary(nearest, gamma), each one's spill
+// target when it is a valid list not yet included, appended with its own distance.
+// spillBoundary: nearest * (1 + gamma) for EUCLIDEAN; otherwise -(s - |s| * gamma) with
+// s = -nearest.  Writes up to 2 * nprobe lists per query and their count.
+void vo_route_spill(const float* cent, int32_t nlist, int32_t dim, int32_t metric, const float* queries,
+                    int32_t nq, int32_t nprobe, float gamma, const int32_t* spill_targets, int32_t nthreads,
+                    int32_t* list_ids, float* dists, int32_t* counts) {
+  const int probes = std::min(nprobe, nlist);
+  const int width = 2 * nprobe;
+  std::vector<int32_t> prim((size_t)nq * probes);
+  std::vector<float> pd((size_t)nq * probes);
+  vo_route(cent, nlist, dim, metric, queries, nq, probes, VO_POLICY_REFERENCE_HEAP, nthreads, prim.data(), pd.data());
+  parallel_for(nq, nthreads, [&](int64_t lo, int64_t hi) {
+    std::vector<float> d(nlist), qn(dim);
+    std::vector<char> included(nlist);
+    for (int64_t q = lo; q < hi; q++) {
+      route_distances(cent, nlist, dim, metric, queries + q * dim, d.data(), qn.data());
+      std::fill(included.begin(), included.end(), 0);
+      int32_t* oi = list_ids + q * width;
+      float* od = dists + q * width;
+      int count = 0;
+      for (int r = 0; r < probes; r++) {
+        oi[count] = prim[(size_t)q * probes + r];
+        od[count] = pd[(size_t)q * probes + r];
+        included[oi[count]] = 1;
+        count++;
+      }
+      if (gamma > 0.0f && spill_targets && count > 0) {
+        const float nearest = pd[(size_t)q * probes];
+        float boundary;
+        if (metric == VO_EUCLIDEAN) {
+          boundary = nearest * (1.0f + gamma);
+        } else {
+          const float ns = -nearest;
+          const float thr = ns - std::fabs(ns) * gamma;
+          boundary = -thr;
+        }
+        for (int r = 0; r < probes; r++) {
+          if (pd[(size_t)q * probes + r] > boundary) break;
+          const int32_t sp = spill_targets[prim[(size_t)q * probes + r]];
+          if (sp >= 0 && sp < nlist && !included[sp]) {
+            oi[count] = sp;
+            od[count] = d[sp];
+            included[sp] = 1;
+            count++;
+          }
+        }
+      }
+      counts[q] = count;
     }
   });
 }

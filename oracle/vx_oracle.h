@@ -150,6 +150,12 @@ void vo_quantized_two_pass_search(int32_t kind, const void* qdata, const float* 
 void vo_route(const float* centroids, int32_t nlist, int32_t dim, int32_t metric,
               const float* queries, int32_t nq, int32_t nprobe, int32_t policy, int32_t nthreads,
               int32_t* list_ids /* [nq][nprobe] */, float* dists);
+/* CentroidIndex.routeWithSpillDistances with SOAR spill (gamma > 0): up to 2*nprobe lists per
+ * query in list_ids / dists [nq][2*nprobe], their number in counts[nq] */
+void vo_route_spill(const float* centroids, int32_t nlist, int32_t dim, int32_t metric,
+                    const float* queries, int32_t nq, int32_t nprobe, float gamma,
+                    const int32_t* spill_targets, int32_t nthreads, int32_t* list_ids, float* dists,
+                    int32_t* counts);
 /* IvfIndex.pqSearch (IvfIndex.java:539-619); lists are CSR: list_offsets[nlist+1], list_ordinals */
 void vo_ivfpq_search(const float* centroids, int32_t nlist, int32_t dim, const int64_t* list_offsets,
                      const int32_t* list_ordinals, int32_t m, int32_t ks, const float* codebooks,
