@@ -414,21 +414,32 @@ def main():
     flat.close()
     torch.cuda.empty_cache()
 
+    def leg(fn, *a):
+        # One GPU: a failed secondary leg is reported in its slot and the line still prints.
+        # Several ranks: the exception propagates (a rank that skipped a leg's collectives
+        # would leave the others waiting in them).
+        if world > 1:
+            return fn(*a)
+        try:
+            return fn(*a)
+        except Exception as e:
+            return {"error": f"{type(e).__name__}: {e}"[:500]}
+
     # ---- IVF-PQ sub-result
     ivf = None
     if not args.no_ivf:
-        ivf = run_ivf(args, rank, world, local, dev, barrier, max_over_ranks, hbm_peak, peak_kind)
+        ivf = leg(run_ivf, args, rank, world, local, dev, barrier, max_over_ranks, hbm_peak, peak_kind)
 
     ivfflat = None
     if not args.no_ivf and not args.no_ivfflat:
-        ivfflat = run_ivfflat(args, rank, world, local, dev, barrier, max_over_ranks, peak_kind)
+        ivfflat = leg(run_ivfflat, args, rank, world, local, dev, barrier, max_over_ranks, peak_kind)
 
     # ---- SQ8 and BQ candidate scans (selectApproximateCandidates, k = 100)
     sq8 = bq = fp16 = None
     if not args.no_quant:
-        sq8 = run_sq8(args, rank, world, local, dev, barrier, max_over_ranks, tc_sustained, peak_kind)
-        bq = run_bq(args, rank, world, local, dev, barrier, max_over_ranks, tc_sustained, peak_kind)
-        fp16 = run_fp16(args, rank, world, local, dev, barrier, max_over_ranks, tc_sustained, peak_kind)
+        sq8 = leg(run_sq8, args, rank, world, local, dev, barrier, max_over_ranks, tc_sustained, peak_kind)
+        bq = leg(run_bq, args, rank, world, local, dev, barrier, max_over_ranks, tc_sustained, peak_kind)
+        fp16 = leg(run_fp16, args, rank, world, local, dev, barrier, max_over_ranks, tc_sustained, peak_kind)
 
     if rank == 0:
         line = {
