@@ -46,6 +46,24 @@ def compute(O):
     pq = O.pq_encode_all(resid, 12, 16, cb2)
     ids, sc, cnt = O.ivfpq_search(cent, off, ords, 12, 16, cb2, pq, q, O.EUCLIDEAN, 10, 4)
     out["ivfpq_0"] = {"ids": ids.tolist(), "scores": _bits(sc)}
+    # routing, the IVF-flat batched scan, the cluster radii, SQ4 and BBQ
+    for metric in range(4):
+        lids, dists = O.route(cent, q, metric, 5)
+        out[f"route_{metric}"] = {"ids": lids.tolist(), "dists": _bits(dists)}
+        ids, sc, cnt = O.ivfflat_search(cent, off, ords, db, q, metric, 10, 4)
+        out[f"ivfflat_{metric}"] = {"ids": ids.tolist(), "scores": _bits(sc), "counts": cnt.tolist()}
+    out["ivf_radii"] = _bits(O.ivf_radii(cent, off, ords, db))
+    packed, corr4 = O.sq4_encode_all(lo, hi, db)
+    out["sq4_corr_head"] = _bits(corr4[:16])
+    for metric in range(2):
+        ids, sc, cnt = O.sq4_search(packed, corr4, 96, lo, hi, q, metric, 10)
+        out[f"sq4_{metric}"] = {"ids": ids.tolist(), "scores": _bits(sc)}
+    c0 = db.mean(0).astype(np.float32)
+    bw, bc = O.bbq_encode_all(db, c0)
+    out["bbq_corr_head"] = _bits(bc[:8])
+    for metric in range(4):
+        ids, sc, cnt = O.bbq_search(bw, bc, c0, 96, q, metric, 10)
+        out[f"bbq_{metric}"] = {"ids": ids.tolist(), "scores": _bits(sc)}
     return out
 
 
