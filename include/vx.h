@@ -247,12 +247,16 @@ VX_API int vx_ivfpq_search_routed_device(vx_index* index, const float* d_queries
  * for callers that must not allocate device memory while searching (a host that reserves its
  * whole device budget up front and accounts every byte, or a latency-critical loop where an
  * allocation would block on the allocator or synchronise the device).  Its scratch is a
- * file-scope 64 MiB device array that every GPU loading the library holds until exit; no
- * cudaMalloc, cudaFree or pool allocation happens in the call.  The first call on a device
- * looks the array up with cudaGetSymbolAddress and should come before any stream capture.
+ * file-scope 64 MiB device array; no cudaMalloc, cudaFree or pool allocation happens in the
+ * call.  With CUDA's default lazy module loading the array is placed on a device by the first
+ * vx_bq_build there (which looks it up with cudaGetSymbolAddress), not when the library is
+ * loaded, and stays until the process exits; with CUDA_MODULE_LOADING=EAGER every context
+ * holds it from load.  If that placement failed, the call returns VX_ERR_OUT_OF_MEMORY.
  * All calls on a device share the array: calls that overlap on the GPU race and must be
  * serialised by the caller.  Batches needing more than 64 MiB of scratch are rejected with
- * VX_ERR_INVALID_ARGUMENT (split the batch).  Queries and outputs are device buffers. */
+ * VX_ERR_INVALID_ARGUMENT and a message giving the largest batch that fits for the index and
+ * k (about 175 queries at k = 100 on a large index; split the batch).  Queries and outputs are
+ * device buffers. */
 VX_API int vx_bq_scan_candidates_noalloc(vx_index* index, const float* d_queries, int32_t nq,
                                          int32_t dim, int32_t k, int32_t* d_ids, float* d_scores,
                                          int32_t* d_counts, void* stream);

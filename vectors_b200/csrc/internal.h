@@ -10,6 +10,14 @@ namespace vx {
 // Records `msg` for vx_last_error() and returns `status` (vx_api.cu).
 int record_failure(int status, const char* msg);
 
+// Runs an entry point's body as every vx_* call does: host-side injected failures first, then
+// CUDA and host-allocation failures mapped to a status (vx_api.cu).
+int run_guarded(int (*body)(void*), void* ctx);
+
+// Places the no-allocation scan's static scratch on `device` (the current device) and caches
+// its address; called by vx_bq_build (noalloc.cu).
+void noalloc_prepare(int device);
+
 // vx_ivfpq_build with the full-precision rows `row_stride` floats apart (vx_api.cu).
 int ivfpq_build_strided(int32_t device, const float* centroids, int32_t nlist, int32_t dim,
                         const int64_t* list_offsets, const int32_t* list_ordinals, int32_t m, int32_t ks,

@@ -353,6 +353,14 @@ int guarded(F&& f) {
   }
 }
 
+}  // namespace
+
+int run_guarded(int (*body)(void*), void* ctx) {
+  return guarded([&]() -> int { return body(ctx); });
+}
+
+namespace {
+
 int check_device_error(int32_t* d_err, cudaStream_t st) {
   int32_t h = 0;
   VX_CUDA(cudaMemcpyAsync(&h, d_err, 4, cudaMemcpyDeviceToHost, st));
@@ -1599,6 +1607,9 @@ int vx_bq_build(int32_t device, const uint64_t* words, int64_t n, int32_t dim, i
       free_index(ix);
       throw;
     }
+    // The no-allocation BQ scan's static scratch is placed on this device here, at build time,
+    // so that vx_bq_scan_candidates_noalloc never loads a module (and with it 64 MiB) itself.
+    noalloc_prepare(device);
     *out = ix;
     return VX_OK;
   });
