@@ -81,9 +81,12 @@ def lib() -> C.CDLL:
             "vo_bq_search": (None, [p, i64, i32, i32, p, i32, i32, i32, i32, p, p, p]),
             "vo_fp16_search": (None, [p, i64, i32, i32, p, i32, i32, i32, i32, p, p, p]),
             "vo_quantized_two_pass_search": (None, [i32, p, p, f32, f32, p, i64, i32, i32, p, i32, i32, f32, i32, i32, p, p, p]),
+            "vo_rescore_candidates": (None, [p, i32, i32, p, i32, p, i32, p, i32, i32, i32, p, p, p]),
             "vo_route": (None, [p, i32, i32, i32, p, i32, i32, i32, i32, p, p]),
             "vo_ivfpq_search": (None, [p, i32, i32, p, p, i32, i32, p, p, i64, i32, p, i32, i32, i32, i32, p, i32, i32, p, p, p]),
             "vo_ivfflat_search": (None, [p, i32, i32, p, p, p, i64, i32, p, i32, i32, i32, i32, i32, p, p, p]),
+            "vo_ivfpq_search_spill": (None, [p, i32, i32, p, p, i32, i32, p, p, i64, i32, p, i32, i32, i32, f32, p, i32, p, i32, p, p, p]),
+            "vo_ivfflat_search_spill": (None, [p, i32, i32, p, p, p, i32, p, p, i32, i32, i32, f32, p, i32, p, p, p]),
             "vo_ivfflat_search_early_exit": (None, [p, i32, i32, p, p, p, i64, i32, p, p, i32, i32, i32, i32, i32, p, p,
                                                     p]),
             "vo_ivf_radii": (None, [p, i32, i32, p, p, p, p]),
@@ -377,6 +380,22 @@ def quantized_two_pass(kind, qdata, qcorr, min_q, max_q, db, queries, metric, k,
     return ids, sc, cnt
 
 
+def rescore_candidates(db, queries, metric, cand_ids, cand_counts, k, policy=CANONICAL, nthreads=None):
+    """The two-pass search's exact second pass over given candidates (e.g. an SQ4 or BBQ scan's)."""
+    db, q = f32(db), f32(queries)
+    cid = np.ascontiguousarray(cand_ids, np.int32)
+    cc = np.ascontiguousarray(cand_counts, np.int32)
+    ids, sc, cnt = _outs(q.shape[0], k)
+    lib().vo_rescore_candidates(P(db), q.shape[1], metric, P(q), q.shape[0], P(cid), cid.shape[1], P(cc), k, policy,
+                                nthreads or threads(), P(ids), P(sc), P(cnt))
+    return ids, sc, cnt
+
+
+def candidate_k(k, oqf):
+    """QuantizedFlatScanAdapter's candidateK = max(k, ceil(k * overQueryFactor)) (float product)."""
+    return max(k, int(np.ceil(np.float64(np.float32(k) * np.float32(oqf)))))
+
+
 def route(centroids, queries, metric, nprobe, policy=CANONICAL, nthreads=None):
     c, q = f32(centroids), f32(queries)
     lids = np.empty((q.shape[0], nprobe), np.int32)
@@ -421,6 +440,37 @@ def ivfflat_search(centroids, list_offsets, list_ordinals, vectors, queries, met
     ids, sc, cnt = _outs(q.shape[0], k)
     lib().vo_ivfflat_search(P(c), c.shape[0], c.shape[1], P(off), P(ords), P(v), v.shape[0], metric, P(q), q.shape[0],
                             k, nprobe, policy, nthreads or threads(), P(ids), P(sc), P(cnt))
+    return ids, sc, cnt
+
+
+def ivfpq_search_spill(centroids, list_offsets, list_ordinals, m, ks, codebooks, codes, queries, metric, k, nprobe,
+                       gamma, spill_targets, rescore=1, vectors=None, nthreads=None):
+    """IvfIndex.pqSearch with SOAR spill routing (gamma > 0), canonical ranking."""
+    c, q = f32(centroids), f32(queries)
+    off = np.ascontiguousarray(list_offsets, np.int64)
+    ords = np.ascontiguousarray(list_ordinals, np.int32)
+    codes = np.ascontiguousarray(codes, np.uint8)
+    sp = np.ascontiguousarray(spill_targets, np.int32)
+    v = None if vectors is None else f32(vectors)
+    ids, sc, cnt = _outs(q.shape[0], k)
+    lib().vo_ivfpq_search_spill(P(c), c.shape[0], c.shape[1], P(off), P(ords), m, ks, P(f32(codebooks)), P(codes),
+                                codes.shape[0], metric, P(q), q.shape[0], k, nprobe, float(gamma), P(sp), rescore, P(v),
+                                nthreads or threads(), P(ids), P(sc), P(cnt))
+    return ids, sc, cnt
+
+
+def ivfflat_search_full(centroids, list_offsets, list_ordinals, vectors, radii, queries, metric, k, nprobe, gamma=0.0,
+                        spill_targets=None, nthreads=None):
+    """IvfIndex.search without PQ as the reference runs it: SOAR spill routing (gamma > 0) and,
+    for EUCLIDEAN, the early exit against `radii` (None: every probed list scanned)."""
+    c, q, v = f32(centroids), f32(queries), f32(vectors)
+    off = np.ascontiguousarray(list_offsets, np.int64)
+    ords = np.ascontiguousarray(list_ordinals, np.int32)
+    r = None if radii is None else f32(radii)
+    sp = None if spill_targets is None else np.ascontiguousarray(spill_targets, np.int32)
+    ids, sc, cnt = _outs(q.shape[0], k)
+    lib().vo_ivfflat_search_spill(P(c), c.shape[0], c.shape[1], P(off), P(ords), P(v), metric, P(r), P(q), q.shape[0],
+                                  k, nprobe, float(gamma), P(sp), nthreads or threads(), P(ids), P(sc), P(cnt))
     return ids, sc, cnt
 
 

@@ -1113,6 +1113,14 @@ void vo_quantized_two_pass_search(int32_t kind, const void* qdata, const float* 
   else
     vo_fp16_search((const uint16_t*)qdata, n, dim, metric, queries, nq, (int32_t)ck, policy,
                    nthreads, cid.data(), csc.data(), cnt.data());
+  vo_rescore_candidates(db, dim, metric, queries, nq, cid.data(), (int32_t)ck, cnt.data(), k, policy, nthreads, ids,
+                        scores, counts);
+}
+// The exact second pass of QuantizedFlatScanAdapter.search (QuantizedFlatScanAdapter.java:79-94):
+// every candidate re-scored with the full-precision SimilarityFunction.compare, k best kept.
+void vo_rescore_candidates(const float* db, int32_t dim, int32_t metric, const float* queries, int32_t nq,
+                           const int32_t* cid, int32_t stride, const int32_t* cnt, int32_t k, int32_t policy,
+                           int32_t nthreads, int32_t* ids, float* scores, int32_t* counts) {
   parallel_for(nq, nthreads, [&](int64_t lo, int64_t hi) {
     for (int64_t q = lo; q < hi; q++) {
       int c = cnt[q];
@@ -1121,14 +1129,14 @@ void vo_quantized_two_pass_search(int32_t kind, const void* qdata, const float* 
       if (policy == VO_POLICY_REFERENCE_HEAP) {
         RefHeap h(std::max(kk, 1));
         for (int i = 0; i < c; i++) {
-          int32_t o = cid[q * ck + i];
+          int32_t o = cid[q * stride + i];
           h.offer(o, vo_compare(metric, qq, db + (int64_t)o * dim, dim));
         }
         counts[q] = kk > 0 ? h.drain(ids + q * k, scores + q * k) : 0;
       } else {
         CanonTopK h(std::max(kk, 1));
         for (int i = 0; i < c; i++) {
-          int32_t o = cid[q * ck + i];
+          int32_t o = cid[q * stride + i];
           h.offer(o, vo_compare(metric, qq, db + (int64_t)o * dim, dim));
         }
         counts[q] = kk > 0 ? h.drain(ids + q * k, scores + q * k) : 0;
@@ -1282,16 +1290,42 @@ void vo_route_spill(const float* cent, int32_t nlist, int32_t dim, int32_t metri
   });
 }
 // IvfIndex.pqSearch (IvfIndex.java:539-619) with TopKHeap semantics (TopKHeap.java:60-95).
-void vo_ivfpq_search(const float* cent, int32_t nlist, int32_t dim, const int64_t* loff,
-                     const int32_t* lord, int32_t m, int32_t ks, const float* cb,
-                     const uint8_t* codes, int64_t n, int32_t metric, const float* queries,
-                     int32_t nq, int32_t k, int32_t nprobe, int32_t rescore, const float* vectors,
-                     int32_t policy, int32_t nthreads, int32_t* ids, float* scores,
-                     int32_t* counts) {
-  int probes = std::min(nprobe, nlist);
-  std::vector<int32_t> lids((size_t)nq * probes);
-  std::vector<float> ld((size_t)nq * probes);
-  vo_route(cent, nlist, dim, metric, queries, nq, probes, policy, nthreads, lids.data(), ld.data());
+// The probed clusters of every query, in the order IvfIndex visits them: the min(nprobe, nlist)
+// nearest (CentroidIndex.routeWithSpillDistances, ascending), then with gamma > 0 and spill
+// targets the SOAR additions (vo_route_spill).  width slots per query, cnt[q] of them used.
+struct IvfRoute {
+  int width = 0;
+  std::vector<int32_t> lids, cnt;
+  std::vector<float> ld;
+};
+static IvfRoute ivf_route(const float* cent, int32_t nlist, int32_t dim, int32_t metric, const float* queries,
+                          int32_t nq, int32_t nprobe, float gamma, const int32_t* spill, int32_t policy,
+                          int32_t nthreads) {
+  IvfRoute r;
+  const int probes = std::min(nprobe, nlist);
+  if (gamma > 0.0f && spill) {
+    r.width = 2 * nprobe;
+    r.lids.assign((size_t)nq * r.width, -1);
+    r.ld.assign((size_t)nq * r.width, 0.0f);
+    r.cnt.assign(nq, 0);
+    vo_route_spill(cent, nlist, dim, metric, queries, nq, nprobe, gamma, spill, nthreads, r.lids.data(), r.ld.data(),
+                   r.cnt.data());
+  } else {
+    r.width = probes;
+    r.lids.resize((size_t)nq * probes);
+    r.ld.resize((size_t)nq * probes);
+    r.cnt.assign(nq, probes);
+    vo_route(cent, nlist, dim, metric, queries, nq, probes, policy, nthreads, r.lids.data(), r.ld.data());
+  }
+  return r;
+}
+
+static void ivfpq_search(const float* cent, int32_t nlist, int32_t dim, const int64_t* loff, const int32_t* lord,
+                         int32_t m, int32_t ks, const float* cb, const uint8_t* codes, int64_t n, int32_t metric,
+                         const float* queries, int32_t nq, int32_t k, int32_t nprobe, float gamma,
+                         const int32_t* spill, int32_t rescore, const float* vectors, int32_t policy,
+                         int32_t nthreads, int32_t* ids, float* scores, int32_t* counts) {
+  const IvfRoute route = ivf_route(cent, nlist, dim, metric, queries, nq, nprobe, gamma, spill, policy, nthreads);
   int64_t wide = std::min<int64_t>((int64_t)k * rescore, n);
   if (wide < 1) wide = 1;
   bool euclid = metric == VO_EUCLIDEAN;
@@ -1312,8 +1346,8 @@ void vo_ivfpq_search(const float* cent, int32_t nlist, int32_t dim, const int64_
           ch.offer(o, s);
         }
       };
-      for (int p = 0; p < probes; p++) {
-        int cid = lids[(size_t)q * probes + p];
+      for (int p = 0; p < route.cnt[q]; p++) {
+        int cid = route.lids[(size_t)q * route.width + p];
         int64_t b = loff[cid], e = loff[cid + 1];
         if (b == e) continue;
         const float* c = cent + (size_t)cid * dim;
@@ -1372,6 +1406,25 @@ void vo_ivfpq_search(const float* cent, int32_t nlist, int32_t dim, const int64_
     }
   });
 }
+void vo_ivfpq_search(const float* cent, int32_t nlist, int32_t dim, const int64_t* loff,
+                     const int32_t* lord, int32_t m, int32_t ks, const float* cb,
+                     const uint8_t* codes, int64_t n, int32_t metric, const float* queries,
+                     int32_t nq, int32_t k, int32_t nprobe, int32_t rescore, const float* vectors,
+                     int32_t policy, int32_t nthreads, int32_t* ids, float* scores,
+                     int32_t* counts) {
+  ivfpq_search(cent, nlist, dim, loff, lord, m, ks, cb, codes, n, metric, queries, nq, k, nprobe, 0.0f, nullptr,
+               rescore, vectors, policy, nthreads, ids, scores, counts);
+}
+// IvfIndex.pqSearch with IvfSearchRequest.gamma > 0: the clusters of routeWithSpillDistances,
+// SOAR spill targets appended (IvfIndex.java:545-547, CentroidIndex.java:168-187).
+void vo_ivfpq_search_spill(const float* cent, int32_t nlist, int32_t dim, const int64_t* loff, const int32_t* lord,
+                           int32_t m, int32_t ks, const float* cb, const uint8_t* codes, int64_t n, int32_t metric,
+                           const float* queries, int32_t nq, int32_t k, int32_t nprobe, float gamma,
+                           const int32_t* spill_targets, int32_t rescore, const float* vectors, int32_t nthreads,
+                           int32_t* ids, float* scores, int32_t* counts) {
+  ivfpq_search(cent, nlist, dim, loff, lord, m, ks, cb, codes, n, metric, queries, nq, k, nprobe, gamma,
+               spill_targets, rescore, vectors, VO_POLICY_CANONICAL, nthreads, ids, scores, counts);
+}
 // IvfIndex.search without PQ (IvfIndex.java:170-226): route, then every probed cluster's
 // ordinals in batches of BATCH_ROWS = 64 through batchSquaredL2 / batchDotProduct
 // (scanPartitionBulk, :244-277 -- matVecSquaredL2 / matVecDot over the batch: groups of four
@@ -1388,12 +1441,9 @@ void vo_ivfpq_search(const float* cent, int32_t nlist, int32_t dim, const int64_
 // scanPartitionWithHarmony :279-289) of partitions built with key dimensions.
 static void ivfflat_search(const float* cent, int32_t nlist, int32_t dim, const int64_t* loff, const int32_t* lord,
                            const float* vectors, int32_t metric, const float* radii, const float* queries,
-                           int32_t nq, int32_t k, int32_t nprobe, int32_t policy, int32_t nthreads, int32_t* ids,
-                           float* scores, int32_t* counts) {
-  int probes = std::min(nprobe, nlist);
-  std::vector<int32_t> lids((size_t)nq * probes);
-  std::vector<float> ld((size_t)nq * probes);
-  vo_route(cent, nlist, dim, metric, queries, nq, probes, policy, nthreads, lids.data(), ld.data());
+                           int32_t nq, int32_t k, int32_t nprobe, float gamma, const int32_t* spill, int32_t policy,
+                           int32_t nthreads, int32_t* ids, float* scores, int32_t* counts) {
+  const IvfRoute route = ivf_route(cent, nlist, dim, metric, queries, nq, nprobe, gamma, spill, policy, nthreads);
   const bool euclid = metric == VO_EUCLIDEAN, cosine = metric == VO_COSINE;
   parallel_for(nq, nthreads, [&](int64_t lo, int64_t hi) {
     std::vector<float> batch((size_t)64 * dim), out(64);
@@ -1402,14 +1452,14 @@ static void ivfflat_search(const float* cent, int32_t nlist, int32_t dim, const 
       const float qn = cosine ? vo_dot(qq, qq, dim) : 0.0f;
       RefHeap rh(k);
       CanonTopK ch(k);
-      for (int p = 0; p < probes; p++) {
-        int cid = lids[(size_t)q * probes + p];
+      for (int p = 0; p < route.cnt[q]; p++) {
+        int cid = route.lids[(size_t)q * route.width + p];
         if (euclid && radii) {
           const bool ref = policy == VO_POLICY_REFERENCE_HEAP;
           const bool full = ref ? rh.size == rh.cap : (int)ch.v.size() == ch.cap;
           if (full) {
             const float worst = ref ? rh.sc[0] : ch.v.front().first;
-            const float centroid_l2 = (float)std::sqrt((double)ld[(size_t)q * probes + p]);
+            const float centroid_l2 = (float)std::sqrt((double)route.ld[(size_t)q * route.width + p]);
             const float lb = centroid_l2 - radii[cid];
             if (lb > 0.0f) {
               const float lb_sq = lb * lb;
@@ -1455,16 +1505,25 @@ void vo_ivfflat_search(const float* cent, int32_t nlist, int32_t dim, const int6
                        int32_t k, int32_t nprobe, int32_t policy, int32_t nthreads, int32_t* ids, float* scores,
                        int32_t* counts) {
   (void)n;
-  ivfflat_search(cent, nlist, dim, loff, lord, vectors, metric, nullptr, queries, nq, k, nprobe, policy, nthreads,
-                 ids, scores, counts);
+  ivfflat_search(cent, nlist, dim, loff, lord, vectors, metric, nullptr, queries, nq, k, nprobe, 0.0f, nullptr,
+                 policy, nthreads, ids, scores, counts);
 }
 void vo_ivfflat_search_early_exit(const float* cent, int32_t nlist, int32_t dim, const int64_t* loff,
                                   const int32_t* lord, const float* vectors, int64_t n, int32_t metric,
                                   const float* radii, const float* queries, int32_t nq, int32_t k, int32_t nprobe,
                                   int32_t policy, int32_t nthreads, int32_t* ids, float* scores, int32_t* counts) {
   (void)n;
-  ivfflat_search(cent, nlist, dim, loff, lord, vectors, metric, radii, queries, nq, k, nprobe, policy, nthreads,
-                 ids, scores, counts);
+  ivfflat_search(cent, nlist, dim, loff, lord, vectors, metric, radii, queries, nq, k, nprobe, 0.0f, nullptr,
+                 policy, nthreads, ids, scores, counts);
+}
+// IvfIndex.search (no PQ) as the reference runs it in full: clusters of routeWithSpillDistances
+// (SOAR spill targets appended when gamma > 0), and for EUCLIDEAN the early exit against radii.
+void vo_ivfflat_search_spill(const float* cent, int32_t nlist, int32_t dim, const int64_t* loff, const int32_t* lord,
+                             const float* vectors, int32_t metric, const float* radii, const float* queries,
+                             int32_t nq, int32_t k, int32_t nprobe, float gamma, const int32_t* spill_targets,
+                             int32_t nthreads, int32_t* ids, float* scores, int32_t* counts) {
+  ivfflat_search(cent, nlist, dim, loff, lord, vectors, metric, radii, queries, nq, k, nprobe, gamma, spill_targets,
+                 VO_POLICY_CANONICAL, nthreads, ids, scores, counts);
 }
 // BuoyIndex.computeRadii / euclideanDist (BuoyIndex.java:175-183,220-227).
 void vo_ivf_radii(const float* cent, int32_t nlist, int32_t dim, const int64_t* loff, const int32_t* lord,

@@ -146,6 +146,11 @@ void vo_quantized_two_pass_search(int32_t kind, const void* qdata, const float* 
                                   int32_t dim, int32_t metric, const float* queries, int32_t nq,
                                   int32_t k, float over_query_factor, int32_t policy,
                                   int32_t nthreads, int32_t* ids, float* scores, int32_t* counts);
+/* The exact second pass alone (QuantizedFlatScanAdapter.java:79-94): candidates cid[q*stride ..
+ * + cnt[q]) re-scored with SimilarityFunction.compare on the fp32 rows, k best kept. */
+void vo_rescore_candidates(const float* db, int32_t dim, int32_t metric, const float* queries, int32_t nq,
+                           const int32_t* cid, int32_t stride, const int32_t* cnt, int32_t k, int32_t policy,
+                           int32_t nthreads, int32_t* ids, float* scores, int32_t* counts);
 /* IVF routing (CentroidIndex.routeWithSpillDistances with gamma == 0) */
 void vo_route(const float* centroids, int32_t nlist, int32_t dim, int32_t metric,
               const float* queries, int32_t nq, int32_t nprobe, int32_t policy, int32_t nthreads,
@@ -171,6 +176,20 @@ void vo_ivfflat_search(const float* centroids, int32_t nlist, int32_t dim, const
                        int32_t nthreads, int32_t* ids, float* scores, int32_t* counts);
 /* The same with the reference's EUCLIDEAN triangle-inequality early exit (IvfIndex.java:190-200)
  * against per-cluster radii (BuoyIndex.clusterRadii); other metrics ignore radii. */
+/* IvfIndex.pqSearch with gamma > 0: clusters of routeWithSpillDistances, SOAR spill targets
+ * (spill_targets[nlist], -1 = none) appended (canonical ranking). */
+void vo_ivfpq_search_spill(const float* centroids, int32_t nlist, int32_t dim, const int64_t* list_offsets,
+                           const int32_t* list_ordinals, int32_t m, int32_t ks, const float* codebooks,
+                           const uint8_t* codes, int64_t n, int32_t metric, const float* queries, int32_t nq,
+                           int32_t k, int32_t nprobe, float gamma, const int32_t* spill_targets, int32_t rescore,
+                           const float* vectors, int32_t nthreads, int32_t* ids, float* scores, int32_t* counts);
+/* IvfIndex.search without PQ in full: SOAR spill routing (gamma > 0), and for EUCLIDEAN the
+ * early exit against radii (NULL radii: every probed cluster scanned) (canonical ranking). */
+void vo_ivfflat_search_spill(const float* centroids, int32_t nlist, int32_t dim, const int64_t* list_offsets,
+                             const int32_t* list_ordinals, const float* vectors, int32_t metric, const float* radii,
+                             const float* queries, int32_t nq, int32_t k, int32_t nprobe, float gamma,
+                             const int32_t* spill_targets, int32_t nthreads, int32_t* ids, float* scores,
+                             int32_t* counts);
 void vo_ivfflat_search_early_exit(const float* centroids, int32_t nlist, int32_t dim,
                                   const int64_t* list_offsets, const int32_t* list_ordinals,
                                   const float* vectors, int64_t n, int32_t metric, const float* radii,

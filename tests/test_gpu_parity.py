@@ -223,7 +223,7 @@ def test_bq_all_equal_rows_ties_by_ordinal(oracle):
 
 
 # ------------------------------------------------------------------ FP16
-@pytest.mark.parametrize("metric", [0, 1, 3])
+@pytest.mark.parametrize("metric", [0, 1, 2, 3])
 def test_fp16_candidates_match_oracle(oracle, metric):
     db, q = _data(oracle, 6000, 256, 50, normalize=(metric != 3))
     codes = oracle.fp16_encode_all(db)
@@ -313,7 +313,9 @@ def test_sq4_bit_exact(oracle, metric, n, dim, nq, k):
     _check_float(got, ids, sc, cnt, f"sq4 m={metric} dim={dim}", exact_scores=True)
     # the two-pass contract (candidates re-scored in fp32) on top of the SQ4 scan
     two = a.search_batch(q, 10, over_query_factor=4.0)
-    assert all(len(o.ordinals) == min(10, n) for o in two)
+    ci, cs, cc = oracle.sq4_search(packed, corr, dim, lo, hi, q, metric, oracle.candidate_k(10, 4.0))
+    ids, sc, cnt = oracle.rescore_candidates(db, q, metric, ci, cc, 10)
+    _check_float(two, ids, sc, cnt, f"sq4 two-pass m={metric} dim={dim}")
     a.close()
 
 
@@ -334,7 +336,9 @@ def test_bbq_bit_exact(oracle, metric, n, dim, nq, k):
     ids, sc, cnt = oracle.bbq_search(words, corr, cent, dim, q, metric, k)
     _check_float(got, ids, sc, cnt, f"bbq m={metric} dim={dim}", exact_scores=True)
     two = a.search_batch(q, 5, over_query_factor=4.0)
-    assert all(len(o.ordinals) == 5 for o in two)
+    ci, cs, cc = oracle.bbq_search(words, corr, cent, dim, q, metric, oracle.candidate_k(5, 4.0))
+    ids, sc, cnt = oracle.rescore_candidates(db, q, metric, ci, cc, 5)
+    _check_float(two, ids, sc, cnt, f"bbq two-pass m={metric} dim={dim}")
     a.close()
 
 
@@ -490,3 +494,43 @@ def test_merge_shards_device(oracle):
     ref = oracle.flat_search(db, q, oracle.COSINE, 10)
     assert np.array_equal(mi.cpu().numpy(), ref[0])
     np.testing.assert_allclose(ms.cpu().numpy(), ref[1], rtol=REL)
+
+
+# ------------------------------------------------------------------ threading
+def test_concurrent_searches_equal_serial(oracle):
+    # an index is safe for concurrent searches from several host threads (the facade's read
+    # lock, FlatScanAdapter.java:31-33): two threads searching one FLAT and one SQ8 index at
+    # once return what the same calls return one after another
+    import threading
+
+    db, q = _data(oracle, 40_000, 256, 300)
+    f = vx.FlatScanAdapter()
+    f.build(db, vx.SimilarityFunction.COSINE)
+    lo, hi = oracle.sq8_train(db)
+    codes, corr = oracle.sq8_encode_all(lo, hi, db)
+    s = vx.QuantizedFlatScanAdapter()
+    s.build_sq8(codes, corr, lo, hi, vx.SimilarityFunction.DOT_PRODUCT, vectors=db)
+    calls = [lambda i=i: f.search_batch(q[i::2], 10) for i in range(2)]
+    calls += [lambda i=i: s.search_batch(q[i::2], 10, 0, 4.0) for i in range(2)]
+    serial = [c() for c in calls]
+    results = [[None] * len(calls) for _ in range(3)]
+    errors = []
+
+    def run(rep, j):
+        try:
+            results[rep][j] = calls[j]()
+        except Exception as e:  # pragma: no cover - reported below
+            errors.append(e)
+
+    for rep in range(3):
+        threads = [threading.Thread(target=run, args=(rep, j)) for j in range(len(calls))]
+        for t in threads:
+            t.start()
+        for t in threads:
+            t.join()
+    assert not errors, errors
+    for rep in range(3):
+        for j in range(len(calls)):
+            _same_outcomes(results[rep][j], serial[j], f"concurrent rep {rep} call {j}")
+    f.close()
+    s.close()
