@@ -198,6 +198,21 @@ VX_API int vx_ivf_graph_info(const uint8_t* bytes, int64_t len, int32_t* nlist, 
 VX_API int vx_ivf_graph_build(int32_t device, const uint8_t* bytes, int64_t len, int32_t metric,
                               const float* vectors, int64_t vector_count, int64_t row_stride, int32_t nprobe,
                               int32_t rescore_factor, vx_index** out);
+/* The BuoyIndex state an IVF index routes with beyond its centroids (IvfIndex.fromPrebuilt takes
+ * a BuoyIndex; vectors-ivf/.../BuoyIndex.java:130-167): radii [nlist], the largest distance from
+ * each centroid to a row of its cluster (BuoyIndex.clusterRadii), and SOAR spill targets [nlist]
+ * (BuoyIndex.spillTargets, -1 = none).  NULL leaves that part unchanged.  vx_ivfflat_build
+ * computes the radii from its partitions as BuoyIndex.computeRadii does (:175-183); graph.bin
+ * builds take both from the file.  The IVF-flat EUCLIDEAN search stops early with them as
+ * IvfIndex.search does (IvfIndex.java:190-205).  Must not overlap searches on the index. */
+VX_API int vx_ivf_set_buoy(vx_index* index, const float* radii, const int32_t* spill_targets);
+/* The adapter's SOAR spill ratio at search time (IvfPqAdapter / IvfFlatAdapter gamma,
+ * IvfSearchRequest.gamma >= 0, IvfSearchRequest.java:40; default 0 = no spill).  With gamma > 0
+ * and spill targets set, vx_search_batch and vx_ivfpq_search* route with
+ * CentroidIndex.routeWithSpillDistances' additions (CentroidIndex.java:155-187).  The routed
+ * entry points (vx_ivf_route_device, vx_ivfpq_search_routed_device) route and scan without spill
+ * and without the early exit.  Must not overlap searches on the index. */
+VX_API int vx_ivf_set_gamma(vx_index* index, float gamma);
 /* IndexSpi.size() and the index's shape. */
 VX_API int vx_index_info(const vx_index* index, int32_t* kind, int64_t* size, int32_t* dim,
                   int32_t* metric);

@@ -96,12 +96,12 @@ def buoy_bytes(centroids, metric: int, spill=None, sizes=None, radii=None) -> by
 
 
 def ivf_graph_bin(centroids, list_offsets, list_ordinals, metric: int, pq=None, key_dims=None,
-                  sizes=None, radii=None) -> bytes:
+                  sizes=None, radii=None, spill=None) -> bytes:
     """IvfIndex.encode: [buoyLen][buoy] [k] k x ([ordCount][ordinals][keyDimCount][keyDims])
     [pqFlag] [PQ trailer].  pq = dict(m, ks, codebooks (concatenated per subspace), codes
     [n][m] in ordinal order, anisotropic (float), global_centroid (optional), subs (optional
     [m][2] sizes/offsets; default computeSubspaceSizesAndOffsets)); None writes pqFlag 0."""
-    buoy = buoy_bytes(centroids, metric, sizes=sizes, radii=radii)
+    buoy = buoy_bytes(centroids, metric, spill=spill, sizes=sizes, radii=radii)
     k, dim = np.asarray(centroids).shape
     off = np.asarray(list_offsets, np.int64)
     ords = np.asarray(list_ordinals, ">i4")

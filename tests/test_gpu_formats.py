@@ -101,14 +101,16 @@ def test_ivf_flat_graph_bin_opens_the_same_index(oracle, metric):
     q = oracle.gen_mixture(50, dim, 16, 0.3, SEED_C, SEED_Q, metric == 2)
     cent = oracle.kmeans_train(db[:3000], 20, 8, 42)
     off, ords = oracle.build_ivf_lists(oracle.kmeans_assign(db, cent), 20)
-    blob = F.ivf_graph_bin(cent, off, ords, metric, pq=None, key_dims=[[1, 2]] + [None] * 19)
+    # the buoy's radii as BuoyIndex.computeRadii leaves them (the EUCLIDEAN early exit reads them)
+    radii = oracle.ivf_radii(cent, off, ords, db)
+    blob = F.ivf_graph_bin(cent, off, ords, metric, pq=None, key_dims=[[1, 2]] + [None] * 19, radii=radii)
     got = vx.IvfFlatAdapter(nprobe=5)
     got.load_graph_bin(blob, vectors=_vectors_bin_view(db))
     assert got.size() == 8000
     ref = vx.IvfFlatAdapter(nprobe=5)
     ref.build_prebuilt(cent, off, ords, db, vx.SimilarityFunction(metric))
     _same(got.ivf_search(q, 10, 5), ref.ivf_search(q, 10, 5), f"ivf-flat graph.bin m={metric}")
-    ids, sc, cnt = oracle.ivfflat_search(cent, off, ords, db, q, metric, 10, 5)
+    ids, sc, cnt = oracle.ivfflat_search_full(cent, off, ords, db, radii, q, metric, 10, 5)
     for i, o in enumerate(got.search_batch(q, 10)):
         assert list(o.ordinals) == list(ids[i, : cnt[i]]), f"ivf-flat graph.bin m={metric} query {i}"
     got.close()

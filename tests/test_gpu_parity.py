@@ -357,7 +357,9 @@ def test_ivfflat_matches_oracle(oracle, metric, dim, nq, k):
     a = vx.IvfFlatAdapter(nprobe=8)
     a.build_prebuilt(cent, off, ords, db, vx.SimilarityFunction(metric))
     got = a.ivf_search(q, k, 8)
-    ids, sc, cnt = oracle.ivfflat_search(cent, off, ords, db, q, metric, k, 8)
+    # the reference's search in full: EUCLIDEAN stops early against the partitions' radii
+    radii = oracle.ivf_radii(cent, off, ords, db)
+    ids, sc, cnt = oracle.ivfflat_search_full(cent, off, ords, db, radii, q, metric, k, 8)
     for i, o in enumerate(got):
         c = cnt[i]
         assert list(o.ordinals) == list(ids[i, :c]), f"ivfflat m={metric} dim={dim} query {i}"
@@ -367,10 +369,11 @@ def test_ivfflat_matches_oracle(oracle, metric, dim, nq, k):
             assert np.array_equal(o.scores, sc[i, :c]), f"ivfflat m={metric} dim={dim} query {i} scores"
     # IndexSpi.searchBatch: the adapter's nprobe, and overQueryFactor widening the probes
     _same_outcomes(a.search_batch(q, k), got, "ivfflat searchBatch")
-    wide = oracle.ivfflat_search(cent, off, ords, db, q, metric, k, 12)
+    # IvfFlatAdapter.search: candidateK = ceil(k * 1.5) hits from ceil(8 * 1.5) probes, trimmed to k
+    wide = oracle.ivfflat_search_full(cent, off, ords, db, radii, q, metric, oracle.candidate_k(k, 1.5), 12)
     got2 = a.search_batch(q, k, over_query_factor=1.5)
     for i, o in enumerate(got2):
-        assert list(o.ordinals) == list(wide[0][i, : wide[2][i]]), f"ivfflat oqf query {i}"
+        assert list(o.ordinals) == list(wide[0][i, : min(k, wide[2][i])]), f"ivfflat oqf query {i}"
     a.close()
 
 

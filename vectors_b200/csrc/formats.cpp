@@ -170,6 +170,8 @@ int unsupported_kind(const QuantizedFile& f) {
 struct IvfFile {
   int32_t nlist = 0, dim = 0, metric = -1;
   std::vector<float> centroids;       // [nlist][dim]
+  std::vector<int32_t> spill;         // [nlist] SOAR spill targets (-1: none)
+  std::vector<float> radii;           // [nlist] cluster radii (the EUCLIDEAN early exit)
   std::vector<int64_t> offsets;       // [nlist + 1]
   std::vector<int32_t> ordinals;      // partitions, concatenated
   bool pq = false;
@@ -206,7 +208,11 @@ int parse_buoy(Cursor& c, IvfFile& f) {
   if (c.remaining() / 4 < k * d + 3 * k) return underflow("the buoy vectors");
   f.centroids.resize(k * d);
   for (uint64_t i = 0; i < k * d; i++) f.centroids[i] = c.f32();
-  c.pos += 3 * k * 4;  // spill targets, cluster sizes, radii: not used by the search
+  f.spill.resize(k);
+  for (uint64_t i = 0; i < k; i++) f.spill[i] = c.i32();
+  c.pos += k * 4;  // cluster sizes: not used by the search
+  f.radii.resize(k);
+  for (uint64_t i = 0; i < k; i++) f.radii[i] = c.f32();
   return VX_OK;
 }
 
@@ -409,18 +415,28 @@ int vx_ivf_graph_build(int32_t device, const uint8_t* bytes, int64_t len, int32_
     if (metric != f.metric)
       return failf(VX_ERR_UNSUPPORTED, "graph.bin routes by %s; the index metric %d differs", kMetricNames[f.metric],
                    metric);
+    int st;
     if (!f.pq) {  // IVF-flat: IvfIndex.decode scores the caller's vectors
       if (!vectors) return failf(VX_ERR_NULL_POINTER, "an IVF-flat graph.bin needs the vectors");
-      return vx_ivfflat_build(device, f.centroids.data(), f.nlist, f.dim, f.offsets.data(),
-                              f.ordinals.empty() ? nullptr : f.ordinals.data(), vectors, vector_count, row_stride,
-                              metric, nprobe, out);
-    }
-    if (vectors && vector_count != f.count)
-      return failf(VX_ERR_INVALID_ARGUMENT, "%lld vectors for %d PQ codes", (long long)vector_count, f.count);
-    return ivfpq_build_strided(device, f.centroids.data(), f.nlist, f.dim, f.offsets.data(),
+      st = vx_ivfflat_build(device, f.centroids.data(), f.nlist, f.dim, f.offsets.data(),
+                            f.ordinals.empty() ? nullptr : f.ordinals.data(), vectors, vector_count, row_stride,
+                            metric, nprobe, out);
+    } else {
+      if (vectors && vector_count != f.count)
+        return failf(VX_ERR_INVALID_ARGUMENT, "%lld vectors for %d PQ codes", (long long)vector_count, f.count);
+      st = ivfpq_build_strided(device, f.centroids.data(), f.nlist, f.dim, f.offsets.data(),
                                f.ordinals.empty() ? nullptr : f.ordinals.data(), f.m, f.ks, f.codebooks.data(),
                                f.count ? f.codes : nullptr, f.count, metric, vectors,
                                vectors ? row_stride : f.dim, nprobe, rescore_factor, out);
+    }
+    if (st != VX_OK) return st;
+    // the buoy's own radii and spill targets, as IvfIndex.decode restores them (BuoyIndex.decode)
+    st = vx_ivf_set_buoy(*out, f.radii.data(), f.spill.data());
+    if (st != VX_OK) {
+      vx_index_free(*out);
+      *out = nullptr;
+    }
+    return st;
   });
 }
 

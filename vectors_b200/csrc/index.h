@@ -55,6 +55,11 @@ struct vx_index {
   int64_t* cb_off = nullptr;
   int32_t* sub = nullptr;
   int nprobe = 1, rescore = 1;
+  // BuoyIndex state (IVF-PQ and IVF-flat): cluster radii (the EUCLIDEAN early exit of the flat
+  // list scan), SOAR spill targets (null: none) and the adapter's search-time gamma
+  float* radii = nullptr;
+  int32_t* spill = nullptr;
+  float gamma = 0.0f;
   // IVF-flat: list-ordered rows zero-padded to Dp floats, their dotProduct(v, v) (COSINE)
   float* flat_rows = nullptr;
   float* flat_norms = nullptr;

@@ -895,7 +895,7 @@ __global__ void __launch_bounds__(256, 2) flat_list_kernel(FlatListArgs a) {
         const int32_t pair = a.pairs[grp.x + g];
         q = pair / a.nprobe;
         p = pair - q * a.nprobe;
-        f = a.floor[q];
+        f = a.floor ? a.floor[q] : 0ull;
       }
       s_query[g] = q;
       s_probe[g] = p;
@@ -1025,15 +1025,206 @@ __global__ void __launch_bounds__(256, 2) flat_list_kernel(FlatListArgs a) {
       for (uint32_t i = lane; i < c; i += 32) a.out[sidx * a.K + i] = kb[i];
       if (lane == 0) {
         a.out_cnt[sidx] = c;
-        if (c == (uint32_t)a.K) atomicMax((unsigned long long*)&a.floor[q], (unsigned long long)t);
+        if (a.floor && c == (uint32_t)a.K) atomicMax((unsigned long long*)&a.floor[q], (unsigned long long)t);
       }
     }
   }
 }
 
+// ---------------------------------------------------------------------------------------
+// SOAR spill expansion (CentroidIndex.routeWithSpillDistances, CentroidIndex.java:155-187 and
+// spillBoundary :213-220).  After the primary probes (ascending distance), with gamma > 0 the
+// spill target of each primary within the boundary -- nearest * (1 + gamma) for EUCLIDEAN,
+// else the negated (nearest score - |nearest score| * gamma) -- is appended at its own
+// distance, unless it is out of range or already listed; the walk stops at the first primary
+// beyond the boundary.  Also writes each listed cluster's routing distance (the early exit's
+// input).  One thread per query; slots past the query's count hold -1.
+// ---------------------------------------------------------------------------------------
+__global__ void route_expand_kernel(const int32_t* __restrict__ lists, int nq, int probes,
+                                    const float* __restrict__ dist, int nlist, int euclid, float gamma,
+                                    const int32_t* __restrict__ spill, int width, int32_t* __restrict__ out_lists,
+                                    float* __restrict__ out_dist) {
+  const int q = blockIdx.x * blockDim.x + threadIdx.x;
+  if (q >= nq) return;
+  const int32_t* pl = lists + (size_t)q * probes;
+  const float* dq = dist + (size_t)q * nlist;
+  int32_t* ol = out_lists + (size_t)q * width;
+  float* od = out_dist + (size_t)q * width;
+  int count = 0;
+  for (int r = 0; r < probes; r++) {
+    const int32_t l = pl[r];
+    ol[count] = l;
+    od[count] = l >= 0 ? dq[l] : 0.0f;
+    count++;
+  }
+  if (gamma > 0.0f && spill && probes > 0 && pl[0] >= 0) {
+    const float nearest = dq[pl[0]];
+    float boundary;
+    if (euclid) {
+      boundary = __fmul_rn(nearest, __fadd_rn(1.0f, gamma));
+    } else {
+      const float ns = -nearest;
+      boundary = -__fsub_rn(ns, __fmul_rn(fabsf(ns), gamma));
+    }
+    for (int r = 0; r < probes && count < width; r++) {
+      const int32_t l = pl[r];
+      if (l < 0 || dq[l] > boundary) break;
+      const int32_t sp = spill[l];
+      if (sp < 0 || sp >= nlist) continue;
+      bool seen = false;
+      for (int i = 0; i < count; i++) seen |= ol[i] == sp;
+      if (seen) continue;
+      ol[count] = sp;
+      od[count] = dq[sp];
+      count++;
+    }
+  }
+  for (int i = count; i < width; i++) {
+    ol[i] = -1;
+    od[i] = 0.0f;
+  }
+}
+
+// BuoyIndex.computeRadii / euclideanDist (BuoyIndex.java:175-183,220-227): the largest
+// distance from a cluster's centroid to its rows, each distance a sequential fp32 sum of
+// (v - c)^2 (no fused multiply-add) and (float) Math.sqrt of it.  One thread per list-ordered
+// row; the maximum by integer atomicMax on the non-negative float bits (radii zeroed).
+__global__ void list_radii_kernel(const float* __restrict__ rows, int64_t n, int dim, int Dp,
+                                  const int64_t* __restrict__ list_off, int nlist, const float* __restrict__ cent,
+                                  float* __restrict__ radii) {
+  const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  int lo = 0, hi = nlist - 1;  // the list holding row i: the last l with list_off[l] <= i
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (list_off[mid] <= i) lo = mid;
+    else hi = mid - 1;
+  }
+  const float* v = rows + i * Dp;
+  const float* c = cent + (size_t)lo * dim;
+  float sum = 0.0f;
+  for (int d = 0; d < dim; d++) {
+    const float e = __fsub_rn(v[d], c[d]);
+    sum = __fadd_rn(sum, __fmul_rn(e, e));
+  }
+  const float r = (float)sqrt((double)sum);
+  atomicMax(reinterpret_cast<int*>(radii + lo), __float_as_int(r));
+}
+
+// IvfIndex.search's EUCLIDEAN early exit (IvfIndex.java:190-205) over the per-(probe, query)
+// results of the list scan (each list's own best K, no floors shared across lists): one warp
+// per query walks its listed clusters in route order, keeping the K best keys seen (the
+// TopKHeap of k); once it holds K, a cluster whose bound (max(0, (float) sqrt(centroid
+// distance) - radius))^2 reaches the K-th best distance ends the walk, and every later cluster
+// is skipped with it.  Keys scoring below min_score are not offered (scanPartitionBulk's
+// minScore test comes before heap.offer).  Other metrics (no early exit): every listed cluster
+// is merged.  The kept keys are written sorted descending.
+constexpr int kExitWarps = 8;
+constexpr int kExitR = 8;  // 256 key slots per warp >= 2 K (K <= 128)
+
+__global__ void __launch_bounds__(kExitWarps * 32) ivf_early_exit_kernel(
+    const uint64_t* __restrict__ out, const uint32_t* __restrict__ out_cnt, int nq, int width, int K,
+    const int32_t* __restrict__ lists, const float* __restrict__ ldist, const float* __restrict__ radii, int euclid,
+    uint64_t min_key, uint64_t* __restrict__ keys, uint32_t* __restrict__ kcnt) {
+  __shared__ uint64_t s_buf[kExitWarps][32 * kExitR];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int q = blockIdx.x * kExitWarps + warp;
+  if (q >= nq) return;
+  uint64_t* buf = s_buf[warp];
+  uint32_t n = 0;
+  uint64_t worst = 0;  // the K-th best key once n == K
+  for (int p = 0; p < width; p++) {
+    const int32_t cid = lists[(size_t)q * width + p];
+    if (cid < 0) break;
+    if (euclid && n == (uint32_t)K) {
+      const float worst_score = key_score(worst);
+      const float cl2 = (float)sqrt((double)ldist[(size_t)q * width + p]);
+      const float lb = __fsub_rn(cl2, radii[cid]);
+      if (lb > 0.0f && __fmul_rn(lb, lb) >= -worst_score) break;
+    }
+    const size_t slot = (size_t)p * nq + q;
+    const uint32_t c = out_cnt[slot];
+    const uint64_t* src = out + slot * K;
+    for (uint32_t i0 = 0; i0 < c; i0 += 32) {
+      const uint32_t i = i0 + lane;
+      const uint64_t key = i < c ? src[i] : kEmptyKey;
+      const bool keep = i < c && key >= min_key;
+      const uint32_t m = __ballot_sync(0xFFFFFFFFu, keep);
+      if (keep) buf[n + __popc(m & ((1u << lane) - 1u))] = key;
+      n += __popc(m);
+    }
+    __syncwarp();
+    if (n > (uint32_t)K) {
+      uint64_t t;
+      uint32_t nc;
+      warp_compact_one<kExitR>(buf, n, (uint32_t)K, t, nc);
+      n = nc;
+      worst = t;
+    } else if (n == (uint32_t)K) {
+      uint64_t mn = ~0ull;
+      for (uint32_t i = lane; i < n; i += 32) mn = buf[i] < mn ? buf[i] : mn;
+      worst = warp_min_u64(mn);
+    }
+    __syncwarp();
+  }
+  // sorted descending (bitonic over the next power of two, empty keys as padding)
+  uint32_t p2 = 1;
+  while (p2 < n) p2 <<= 1;
+  for (uint32_t i = n + lane; i < p2; i += 32) buf[i] = kEmptyKey;
+  for (uint32_t size = 2; size <= p2; size <<= 1)
+    for (uint32_t stride = size >> 1; stride > 0; stride >>= 1) {
+      __syncwarp();
+      for (uint32_t i = lane; i < p2 / 2; i += 32) {
+        const uint32_t lo = 2 * i - (i & (stride - 1)), hi = lo + stride;
+        const bool desc = (lo & size) == 0;
+        const uint64_t x = buf[lo], y = buf[hi];
+        if ((x < y) == desc) {
+          buf[lo] = y;
+          buf[hi] = x;
+        }
+      }
+    }
+  __syncwarp();
+  for (uint32_t i = lane; i < n; i += 32) keys[(size_t)q * K + i] = buf[i];
+  if (lane == 0) kcnt[q] = n;
+}
+
 }  // namespace
 
+cudaError_t launch_route_expand(const int32_t* lists, int nq, int probes, const float* dist, int nlist, int metric,
+                                float gamma, const int32_t* spill, int width, int32_t* out_lists, float* out_dist,
+                                cudaStream_t st) {
+  if (nq <= 0) return cudaSuccess;
+  route_expand_kernel<<<(nq + 127) / 128, 128, 0, st>>>(lists, nq, probes, dist, nlist, metric == kEuclidean ? 1 : 0,
+                                                         gamma, spill, width, out_lists, out_dist);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_list_radii(const float* rows, int64_t n, int dim, int Dp, const int64_t* list_off, int nlist,
+                              const float* cent, float* radii, cudaStream_t st) {
+  cudaError_t e = cudaMemsetAsync(radii, 0, sizeof(float) * nlist, st);
+  if (e != cudaSuccess || n <= 0) return e;
+  list_radii_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(rows, n, dim, Dp, list_off, nlist, cent, radii);
+  return cudaGetLastError();
+}
+
+bool early_exit_supported(int K) { return K >= 1 && 2 * K <= 32 * kExitR; }
+
+cudaError_t launch_ivf_early_exit(const uint64_t* out, const uint32_t* out_cnt, int nq, int width, int K,
+                                  const int32_t* lists, const float* ldist, const float* radii, int metric,
+                                  float min_score, uint64_t* keys, uint32_t* kcnt, cudaStream_t st) {
+  if (nq <= 0) return cudaSuccess;
+  if (!early_exit_supported(K)) return cudaErrorInvalidValue;
+  // keys scoring >= min_score are those >= (order bits of min_score) << 32; -0.0 == 0.0 as in Java
+  const float m = min_score == 0.0f ? -0.0f : min_score;
+  const uint64_t min_key = (uint64_t)float_order_bits(m) << 32;
+  ivf_early_exit_kernel<<<(nq + kExitWarps - 1) / kExitWarps, kExitWarps * 32, 0, st>>>(
+      out, out_cnt, nq, width, K, lists, ldist, radii, metric == kEuclidean ? 1 : 0, min_key, keys, kcnt);
+  return cudaGetLastError();
+}
+
 // The tiled routing kernel is used where it applies unless VX_ROUTE_TILED=0.
+
 static bool route_tiled() {
   static const bool v = [] {
     const char* e = getenv("VX_ROUTE_TILED");

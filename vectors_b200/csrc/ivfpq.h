@@ -70,7 +70,8 @@ struct FlatListArgs {
   float* tail;                // [pairs][3] raw scores of each list's last-batch trailing rows
   uint64_t* out;              // [nprobe][nq][K]
   uint32_t* out_cnt;          // [nprobe][nq]
-  uint64_t* floor;            // [nq] per-query admission floor across lists (zeroed)
+  uint64_t* floor;            // [nq] per-query admission floor across lists (zeroed); null: each
+                              // (query, list) keeps its own best K (the early exit's input)
 };
 constexpr int kFlatGroup = 64;
 // Keys kept per (query, list) that the scan supports: K <= 96.
@@ -80,5 +81,21 @@ cudaError_t launch_pad_rows(const float* src, int64_t n, int dim, int64_t src_st
 cudaError_t launch_row_norms(const float* rows, int64_t n, int dim, int Dp, float* out, cudaStream_t st);
 // flat_tail_kernel then flat_list_kernel (2 launches)
 cudaError_t launch_flat_list(const FlatListArgs& a, int64_t pair_slots, int grid, cudaStream_t st);
+
+// CentroidIndex.routeWithSpillDistances' SOAR additions: lists [nq][probes] (ascending) and the
+// routing distances [nq][nlist] -> out_lists / out_dist [nq][width] (primaries, then spill
+// targets when gamma > 0 and spill is set, -1 past the count) with each cluster's distance.
+cudaError_t launch_route_expand(const int32_t* lists, int nq, int probes, const float* dist, int nlist, int metric,
+                                float gamma, const int32_t* spill, int width, int32_t* out_lists, float* out_dist,
+                                cudaStream_t st);
+// BuoyIndex.computeRadii over the list-ordered rows [n][Dp] (radii [nlist], overwritten).
+cudaError_t launch_list_radii(const float* rows, int64_t n, int dim, int Dp, const int64_t* list_off, int nlist,
+                              const float* cent, float* radii, cudaStream_t st);
+// The per-(probe, query) list results merged per query in route order, with IvfIndex.search's
+// EUCLIDEAN early exit (other metrics: a plain merge); keys [nq][K] sorted descending, kcnt [nq].
+bool early_exit_supported(int K);
+cudaError_t launch_ivf_early_exit(const uint64_t* out, const uint32_t* out_cnt, int nq, int width, int K,
+                                  const int32_t* lists, const float* ldist, const float* radii, int metric,
+                                  float min_score, uint64_t* keys, uint32_t* kcnt, cudaStream_t st);
 
 }  // namespace vx

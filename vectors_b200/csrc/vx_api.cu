@@ -845,13 +845,21 @@ int search_quantized_scan(vx_index* ix, const float* dq, int nq, int K, int k_ou
 // IVF-flat: IvfIndex.search without PQ (IvfIndex.java:170-226).  Routing as for IVF-PQ, then
 // the (query, list) pairs grouped by list (up to 64 per group) through the flat list scan, the
 // per-list best K merged per query.
-int search_ivfflat(vx_index* ix, const float* dq, int nq, int k, int nprobe, float min_score, int32_t* d_ids,
-                   float* d_scores, int32_t* d_counts, cudaStream_t st, const int32_t* given_lists) {
+// heap_k (>= k) is the size of the reference's TopKHeap, k the hits returned: they differ when
+// IvfFlatAdapter widens a search (candidateK = ceil(k * overQueryFactor)) and trims it to k,
+// which changes where the EUCLIDEAN early exit stops.
+int search_ivfflat(vx_index* ix, const float* dq, int nq, int k, int heap_k, int nprobe, float min_score,
+                   int32_t* d_ids, float* d_scores, int32_t* d_counts, cudaStream_t st, const int32_t* given_lists) {
   const int dim = ix->dim, Dp = ix->Dp_flat;
   const int probes = std::min(nprobe, ix->nlist);
-  const int K = (int)std::max<int64_t>(1, std::min<int64_t>(k, ix->n));
+  const int K = (int)std::max<int64_t>(1, std::min<int64_t>(std::max(k, heap_k), ix->n));
   if (!flat_list_supported(K)) return fail(VX_ERR_UNSUPPORTED, "k = %d is larger than the IVF-flat scan keeps (96)", K);
-  const size_t per_q = (size_t)ix->nlist * 4 + (size_t)Dp * 4 + (size_t)probes * (K * 8 + 8 + 12) + 64;
+  // Routed here (not given): SOAR spill targets widen each query's list to 2 * probes slots,
+  // and EUCLIDEAN takes the reference's early exit over the per-list results in route order.
+  const bool spill = !given_lists && ix->spill && ix->gamma > 0.0f;
+  const bool early_exit = !given_lists && ix->metric == VX_EUCLIDEAN && ix->radii;
+  const int width = spill ? 2 * probes : probes;
+  const size_t per_q = (size_t)ix->nlist * 4 + (size_t)Dp * 4 + (size_t)width * (K * 8 + 8 + 12 + 8) + 64;
   const int64_t qch = std::max<int64_t>(64, (int64_t)(scratch_budget() / per_q));
   Scratch S(st);
   int32_t* d_bad = S.alloc<int32_t>(1);
@@ -862,39 +870,47 @@ int search_ivfflat(vx_index* ix, const float* dq, int nq, int k, int nprobe, flo
     const float* dqc = dq + (size_t)q0 * dim;
     float* qn = T.alloc<float>((size_t)qc * dim);
     float* dist = T.alloc<float>((size_t)qc * ix->nlist);
-    int32_t* lists = T.alloc<int32_t>((size_t)qc * probes);
+    int32_t* routed = T.alloc<int32_t>((size_t)qc * probes);
+    int32_t* lists = routed;
+    float* ldist = nullptr;
     int32_t* counts = T.alloc<int32_t>(ix->nlist);
     int32_t* offsets = T.alloc<int32_t>(ix->nlist + 1);
     int32_t* cursor = T.alloc<int32_t>(ix->nlist);
-    int32_t* pairs = T.alloc<int32_t>((size_t)qc * probes);
+    int32_t* pairs = T.alloc<int32_t>((size_t)qc * width);
     float* qpad = T.alloc<float>((size_t)qc * Dp);
     float* qnorm = T.alloc<float>(qc);
-    float* tail = T.alloc<float>((size_t)qc * probes * 3);
-    uint64_t* out = T.alloc<uint64_t>((size_t)probes * qc * K);
-    uint32_t* out_cnt = T.alloc<uint32_t>((size_t)probes * qc);
+    float* tail = T.alloc<float>((size_t)qc * width * 3);
+    uint64_t* out = T.alloc<uint64_t>((size_t)width * qc * K);
+    uint32_t* out_cnt = T.alloc<uint32_t>((size_t)width * qc);
     uint64_t* keys = T.alloc<uint64_t>((size_t)qc * K);
     uint32_t* kcnt = T.alloc<uint32_t>(qc);
-    const int64_t maxg = (int64_t)qc * probes / kFlatGroup + ix->nlist + 1;
+    const int64_t maxg = (int64_t)qc * width / kFlatGroup + ix->nlist + 1;
     int2* groups = T.alloc<int2>((size_t)maxg);
     int32_t* ngroups = T.alloc<int32_t>(2);  // count, dispenser
-    uint64_t* qfloor = T.alloc<uint64_t>(qc);
+    uint64_t* qfloor = early_exit ? nullptr : T.alloc<uint64_t>(qc);
     if (given_lists) {
       VX_LAUNCH(1, launch_copy_lists(given_lists + (size_t)q0 * probes, qc * probes, ix->nlist, lists, d_bad, st));
     } else {
       VX_TIMED(VX_PROF_ROUTE, st, route_launches(dqc, dim, ix->cent, ix->nlist, ix->metric),
-               launch_route(dqc, qc, dim, ix->cent, ix->nlist, ix->metric, probes, qn, dist, lists, st));
+               launch_route(dqc, qc, dim, ix->cent, ix->nlist, ix->metric, probes, qn, dist, routed, st));
+      if (spill || early_exit) {
+        lists = T.alloc<int32_t>((size_t)qc * width);
+        ldist = T.alloc<float>((size_t)qc * width);
+        VX_LAUNCH(1, launch_route_expand(routed, qc, probes, dist, ix->nlist, ix->metric, spill ? ix->gamma : 0.0f,
+                                         spill ? ix->spill : nullptr, width, lists, ldist, st));
+      }
     }
     VX_LAUNCH(1, launch_pad_rows(dqc, qc, dim, dim, nullptr, Dp, qpad, st));
     if (ix->metric == VX_COSINE) VX_LAUNCH(1, launch_row_norms(qpad, qc, dim, Dp, qnorm, st));
-    VX_LAUNCH(3, launch_group_pairs(lists, ix->list_off, qc * probes, ix->nlist, counts, offsets, cursor, pairs, st));
-    VX_CUDA(cudaMemsetAsync(out_cnt, 0, (size_t)probes * qc * 4, st));
-    VX_CUDA(cudaMemsetAsync(qfloor, 0, (size_t)qc * 8, st));
+    VX_LAUNCH(3, launch_group_pairs(lists, ix->list_off, qc * width, ix->nlist, counts, offsets, cursor, pairs, st));
+    VX_CUDA(cudaMemsetAsync(out_cnt, 0, (size_t)width * qc * 4, st));
+    if (qfloor) VX_CUDA(cudaMemsetAsync(qfloor, 0, (size_t)qc * 8, st));
     VX_LAUNCH(1, launch_make_groups(counts, offsets, ix->list_order, ix->nlist, kFlatGroup, groups, ngroups, st));
     FlatListArgs a{};
     a.nq = qc;
     a.dim = dim;
     a.Dp = Dp;
-    a.nprobe = probes;
+    a.nprobe = width;
     a.metric = ix->metric;
     a.K = K;
     a.pairs = pairs;
@@ -912,8 +928,14 @@ int search_ivfflat(vx_index* ix, const float* dq, int nq, int k, int nprobe, flo
     a.out = out;
     a.out_cnt = out_cnt;
     a.floor = qfloor;
-    VX_TIMED(VX_PROF_ADC_SCAN, st, 2, launch_flat_list(a, (int64_t)qc * probes, ix->num_sms * 2, st));
-    VX_TIMED(VX_PROF_MERGE, st, 1, launch_merge_streams(out, out_cnt, probes, qc, qc, K, K, keys, kcnt, st));
+    VX_TIMED(VX_PROF_ADC_SCAN, st, 2, launch_flat_list(a, (int64_t)qc * width, ix->num_sms * 2, st));
+    if (early_exit) {
+      VX_TIMED(VX_PROF_MERGE, st, 1,
+               launch_ivf_early_exit(out, out_cnt, qc, width, K, lists, ldist, ix->radii, ix->metric, min_score, keys,
+                                     kcnt, st));
+    } else {
+      VX_TIMED(VX_PROF_MERGE, st, 1, launch_merge_streams(out, out_cnt, width, qc, qc, K, K, keys, kcnt, st));
+    }
     int32_t* oi = d_ids + (size_t)q0 * k;
     float* os = d_scores + (size_t)q0 * k;
     int32_t* oc = d_counts + q0;
@@ -933,7 +955,7 @@ int search_ivfpq(vx_index* ix, const float* dq, int nq, int k, int nprobe, int r
                  float min_score, int32_t* d_ids, float* d_scores, int32_t* d_counts,
                  cudaStream_t st, const int32_t* given_lists = nullptr) {
   if (ix->kind == VX_KIND_IVFFLAT)  // IvfIndex.search takes the flat scan when there is no PQ
-    return search_ivfflat(ix, dq, nq, k, nprobe, min_score, d_ids, d_scores, d_counts, st, given_lists);
+    return search_ivfflat(ix, dq, nq, k, k, nprobe, min_score, d_ids, d_scores, d_counts, st, given_lists);
   const int dim = ix->dim;
   const int probes = std::min(nprobe, ix->nlist);
   int64_t wide = std::min<int64_t>((int64_t)k * rescore, ix->n);
@@ -943,8 +965,11 @@ int search_ivfpq(vx_index* ix, const float* dq, int nq, int k, int nprobe, int r
   if (g.R < 0) return fail(VX_ERR_UNSUPPORTED, "k * rescoreFactor = %d is larger than supported", K);
   if (rescore > 1 && !ix->rows32)
     return fail(VX_ERR_UNSUPPORTED, "rescoreFactor > 1 needs the full-precision vectors at build");
-  // chunk queries: distances [qc][nlist] + outputs [nprobe][qc][K]
-  const size_t per_q = (size_t)ix->nlist * 4 + (size_t)probes * (K * 8 + 8) + 64;
+  // Routed here (not given): SOAR spill targets widen each query's list to 2 * probes slots.
+  const bool spill = !given_lists && ix->spill && ix->gamma > 0.0f;
+  const int width = spill ? 2 * probes : probes;
+  // chunk queries: distances [qc][nlist] + outputs [width][qc][K]
+  const size_t per_q = (size_t)ix->nlist * 4 + (size_t)width * (K * 8 + 8 + 12) + 64;
   int64_t qch = std::max<int64_t>(64, (int64_t)(scratch_budget() / per_q));
   Scratch S(st);
   int32_t* d_bad = S.alloc<int32_t>(1);
@@ -955,13 +980,14 @@ int search_ivfpq(vx_index* ix, const float* dq, int nq, int k, int nprobe, int r
     const float* dqc = dq + (size_t)q0 * dim;
     float* qn = T.alloc<float>((size_t)qc * dim);
     float* dist = T.alloc<float>((size_t)qc * ix->nlist);
-    int32_t* lists = T.alloc<int32_t>((size_t)qc * probes);
+    int32_t* routed = T.alloc<int32_t>((size_t)qc * probes);
+    int32_t* lists = routed;
     int32_t* counts = T.alloc<int32_t>(ix->nlist);
     int32_t* offsets = T.alloc<int32_t>(ix->nlist + 1);
     int32_t* cursor = T.alloc<int32_t>(ix->nlist);
-    int32_t* pairs = T.alloc<int32_t>((size_t)qc * probes);
-    uint64_t* out = T.alloc<uint64_t>((size_t)probes * qc * K);
-    uint32_t* out_cnt = T.alloc<uint32_t>((size_t)probes * qc);
+    int32_t* pairs = T.alloc<int32_t>((size_t)qc * width);
+    uint64_t* out = T.alloc<uint64_t>((size_t)width * qc * K);
+    uint32_t* out_cnt = T.alloc<uint32_t>((size_t)width * qc);
     uint64_t* keys = T.alloc<uint64_t>((size_t)qc * K);
     uint32_t* kcnt = T.alloc<uint32_t>(qc);
     if (given_lists) {
@@ -969,20 +995,26 @@ int search_ivfpq(vx_index* ix, const float* dq, int nq, int k, int nprobe, int r
       VX_LAUNCH(1, launch_copy_lists(given_lists + (size_t)q0 * probes, qc * probes, ix->nlist, lists, d_bad, st));
     } else {
       VX_TIMED(VX_PROF_ROUTE, st, route_launches(dqc, dim, ix->cent, ix->nlist, ix->metric),
-               launch_route(dqc, qc, dim, ix->cent, ix->nlist, ix->metric, probes, qn, dist, lists, st));
+               launch_route(dqc, qc, dim, ix->cent, ix->nlist, ix->metric, probes, qn, dist, routed, st));
+      if (spill) {
+        lists = T.alloc<int32_t>((size_t)qc * width);
+        float* ldist = T.alloc<float>((size_t)qc * width);
+        VX_LAUNCH(1, launch_route_expand(routed, qc, probes, dist, ix->nlist, ix->metric, ix->gamma, ix->spill, width,
+                                         lists, ldist, st));
+      }
     }
-    VX_LAUNCH(3, launch_group_pairs(lists, ix->list_off, qc * probes, ix->nlist, counts, offsets, cursor, pairs, st));
-    VX_CUDA(cudaMemsetAsync(out_cnt, 0, (size_t)probes * qc * 4, st));
+    VX_LAUNCH(3, launch_group_pairs(lists, ix->list_off, qc * width, ix->nlist, counts, offsets, cursor, pairs, st));
+    VX_CUDA(cudaMemsetAsync(out_cnt, 0, (size_t)width * qc * 4, st));
     AdcArgs a;
     a.nq = qc;
     a.dim = dim;
-    a.nprobe = probes;
+    a.nprobe = width;
     a.metric = ix->metric;
     a.M = ix->M;
     a.Ks = ix->Ks;
     a.Mp = ix->Mp;
     a.K = K;
-    a.npairs = (int64_t)qc * probes;
+    a.npairs = (int64_t)qc * width;
     a.pairs = pairs;
     a.pair_count = offsets + ix->nlist;
     a.lists = lists;
@@ -1002,7 +1034,7 @@ int search_ivfpq(vx_index* ix, const float* dq, int nq, int k, int nprobe, int r
     const int grid = ix->num_sms * 2;
     const StreamGeom gg = stream_geom(K, std::max(32, K));  // group buffers hold >= 2K keys
     if (use_adc_group() && adc_group_supported(ix->M, ix->Ks, dim) && gg.R > 0 && gg.R <= 9) {
-      const int64_t maxg = (int64_t)qc * probes / kAdcGroupQ + ix->nlist + 1;
+      const int64_t maxg = (int64_t)qc * width / kAdcGroupQ + ix->nlist + 1;
       int2* groups = T.alloc<int2>((size_t)maxg);
       int32_t* ngroups = T.alloc<int32_t>(2);  // count, dispenser
       uint64_t* qfloor = T.alloc<uint64_t>(qc);
@@ -1015,7 +1047,7 @@ int search_ivfpq(vx_index* ix, const float* dq, int nq, int k, int nprobe, int r
     } else {
       VX_TIMED(VX_PROF_ADC_SCAN, st, 1, launch_adc_scan(a, g.R, grid, st));
     }
-    VX_TIMED(VX_PROF_MERGE, st, 1, launch_merge_streams(out, out_cnt, probes, qc, qc, K, K, keys, kcnt, st));
+    VX_TIMED(VX_PROF_MERGE, st, 1, launch_merge_streams(out, out_cnt, width, qc, qc, K, K, keys, kcnt, st));
     int32_t* oi = d_ids + (size_t)q0 * k;
     float* os = d_scores + (size_t)q0 * k;
     int32_t* oc = d_counts + q0;
@@ -1223,7 +1255,10 @@ int search_batch_dev(vx_index* ix, const float* dq, int nq, int dim, int k, int 
       const int eff = sls > 0 ? sls : ix->nprobe;
       const int probes = oqf > 1.0f ? (int)std::min<int64_t>((int64_t)std::ceil((double)((float)eff * oqf)), ix->nlist)
                                     : std::min(eff, ix->nlist);
-      return search_ivfflat(ix, dq, nq, k, probes, -3.4028235e38f, d_ids, d_scores, d_counts, st, nullptr);
+      // the heap holds candidateK; only the EUCLIDEAN early exit depends on it
+      const int cand_k = oqf > 1.0f ? (int)std::ceil((double)((float)k * oqf)) : k;
+      const int heap_k = ix->metric == VX_EUCLIDEAN ? cand_k : k;
+      return search_ivfflat(ix, dq, nq, k, heap_k, probes, -3.4028235e38f, d_ids, d_scores, d_counts, st, nullptr);
     }
     default:
       return fail(VX_ERR_INVALID_ARGUMENT, "unknown index kind");
@@ -1774,11 +1809,45 @@ int vx_ivfflat_build(int32_t device, const float* centroids, int32_t nlist, int3
         if (ix->flat_norms) VX_LAUNCH(1, launch_row_norms(ix->flat_rows, nl, dim, ix->Dp_flat, ix->flat_norms, 0));
         VX_CUDA(cudaDeviceSynchronize());
       }
+      // BuoyIndex.computeRadii over the partitions (vx_ivf_set_buoy replaces them with a
+      // prebuilt BuoyIndex's own)
+      ix->radii = dev_alloc<float>(ix, (size_t)nlist);
+      VX_LAUNCH(1, launch_list_radii(ix->flat_rows, nl, dim, ix->Dp_flat, ix->list_off, nlist, ix->cent, ix->radii, 0));
+      VX_CUDA(cudaDeviceSynchronize());
     } catch (...) {
       free_index(ix);
       throw;
     }
     *out = ix;
+    return VX_OK;
+  });
+}
+
+int vx_ivf_set_buoy(vx_index* ix, const float* radii, const int32_t* spill_targets) {
+  return guarded([&]() -> int {
+    if (!ix) return fail(VX_ERR_NULL_POINTER, "index must not be null");
+    if (ix->kind != VX_KIND_IVFPQ && ix->kind != VX_KIND_IVFFLAT)
+      return fail(VX_ERR_UNSUPPORTED, "not an IVF index");
+    VX_CUDA(cudaSetDevice(ix->device));
+    if (radii) {
+      if (!ix->radii) ix->radii = dev_alloc<float>(ix, (size_t)ix->nlist);
+      VX_CUDA(cudaMemcpy(ix->radii, radii, (size_t)ix->nlist * 4, cudaMemcpyDefault));
+    }
+    if (spill_targets) {
+      if (!ix->spill) ix->spill = dev_alloc<int32_t>(ix, (size_t)ix->nlist);
+      VX_CUDA(cudaMemcpy(ix->spill, spill_targets, (size_t)ix->nlist * 4, cudaMemcpyDefault));
+    }
+    return VX_OK;
+  });
+}
+
+int vx_ivf_set_gamma(vx_index* ix, float gamma) {
+  return guarded([&]() -> int {
+    if (!ix) return fail(VX_ERR_NULL_POINTER, "index must not be null");
+    if (ix->kind != VX_KIND_IVFPQ && ix->kind != VX_KIND_IVFFLAT)
+      return fail(VX_ERR_UNSUPPORTED, "not an IVF index");
+    if (!(gamma >= 0.0f)) return fail(VX_ERR_INVALID_ARGUMENT, "gamma must be >= 0, got %g", (double)gamma);
+    ix->gamma = gamma;
     return VX_OK;
   });
 }

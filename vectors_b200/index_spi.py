@@ -461,6 +461,19 @@ class QuantizedFlatScanAdapter(IndexSpi):
         _check(N.lib().vx_scan_candidates(self._h.ptr, _ptr(q), len(q), q.shape[1], k, _ptr(ids), _ptr(sc), _ptr(cnt)))
         return _outcomes(ids, sc, cnt)
 
+    def scan_candidates_arrays(self, queries, k: int):
+        """selectApproximateCandidates through the host-buffer C ABI call, returning the flat
+        result arrays (ids [nq][k], scores [nq][k], counts [nq])."""
+        q = self._queries(queries, k)
+        ids, sc, cnt = self._alloc(len(q), k)
+        if self._n == 0:
+            ids.fill(-1)
+            sc.fill(0)
+            cnt.fill(0)
+            return ids, sc, cnt
+        _check(N.lib().vx_scan_candidates(self._h.ptr, _ptr(q), len(q), q.shape[1], k, _ptr(ids), _ptr(sc), _ptr(cnt)))
+        return ids, sc, cnt
+
     def scan_candidates_device(self, queries, k: int, stream=None):
         import torch
 
@@ -483,13 +496,30 @@ class IvfPqAdapter(IndexSpi):
     ``search_batch`` follows IvfPqAdapter.search (IvfPqAdapter.java:124-158); ``ivf_search`` is
     IvfIndex.search(IvfSearchRequest) (IvfIndex.java:170-171,539-619)."""
 
-    def __init__(self, nprobe: int = 32, rescore_factor: int = 1, device: int = 0):
+    def __init__(self, nprobe: int = 32, rescore_factor: int = 1, device: int = 0, gamma: float = 0.0):
         super().__init__(device)
         if nprobe <= 0:
             raise IllegalArgumentException(f"nprobe must be positive: {nprobe}")
         if rescore_factor < 1:
             raise IllegalArgumentException(f"rescoreFactor must be >= 1: {rescore_factor}")
-        self.nprobe, self.rescore_factor = nprobe, rescore_factor
+        if not gamma >= 0:
+            raise IllegalArgumentException(f"gamma must be >= 0, got {gamma}")
+        self.nprobe, self.rescore_factor, self.gamma = nprobe, rescore_factor, float(gamma)
+
+    def _apply_gamma(self):
+        if self.gamma != 0.0:
+            _check(N.lib().vx_ivf_set_gamma(self._h.ptr, self.gamma))
+
+    def set_buoy(self, radii=None, spill_targets=None):
+        """The prebuilt BuoyIndex's own state (IvfIndex.fromPrebuilt takes a BuoyIndex): cluster
+        radii (BuoyIndex.clusterRadii; the IVF-flat EUCLIDEAN early exit) and SOAR spill targets
+        (BuoyIndex.spillTargets, -1 = none).  None leaves that part unchanged."""
+        r = None if radii is None else np.ascontiguousarray(np.asarray(radii, dtype=np.float32))
+        sp = None if spill_targets is None else np.ascontiguousarray(np.asarray(spill_targets, dtype=np.int32))
+        for a, name in ((r, "radii"), (sp, "spill_targets")):
+            if a is not None and a.shape != (self._nlist,):
+                raise IllegalArgumentException(f"{name} must hold one entry per list ({self._nlist})")
+        _check(N.lib().vx_ivf_set_buoy(self._h.ptr, _ptr(r), _ptr(sp)))
 
     def build(self, vectors, metric):
         raise UnsupportedOperationException("k-means / PQ training is an offline step; use build_prebuilt")
@@ -516,6 +546,7 @@ class IvfPqAdapter(IndexSpi):
         )
         self._n, self._dim, self.metric = n, dim, SimilarityFunction(metric)
         self._nlist = nlist
+        self._apply_gamma()
 
     def load_graph_bin(self, data, metric=None, vectors=None):
         """Opens an IVF_PQ generation's graph.bin (IvfIndex.decode, as
@@ -532,6 +563,7 @@ class IvfPqAdapter(IndexSpi):
         self._n, self._dim = (info["count"] if v is None or info["m"] else v.shape[0]), info["dim"]
         self.metric = info["metric"] if metric is None else SimilarityFunction(metric)
         self._nlist = info["nlist"]
+        self._apply_gamma()
 
     def ivf_search(self, queries, k: int, nprobe: int, rescore_factor: int = 1, min_score: float = -3.4028235e38):
         q = self._queries(queries, k)
@@ -543,6 +575,22 @@ class IvfPqAdapter(IndexSpi):
                                     _ptr(ids), _ptr(sc), _ptr(cnt))
         )
         return _outcomes(ids, sc, cnt)
+
+    def ivf_search_arrays(self, queries, k: int, nprobe: int, rescore_factor: int = 1,
+                          min_score: float = -3.4028235e38):
+        """ivf_search through the host-buffer C ABI call, returning the flat result arrays."""
+        q = self._queries(queries, k)
+        ids, sc, cnt = self._alloc(len(q), k)
+        if self._n == 0:
+            ids.fill(-1)
+            sc.fill(0)
+            cnt.fill(0)
+            return ids, sc, cnt
+        _check(
+            N.lib().vx_ivfpq_search(self._h.ptr, _ptr(q), len(q), q.shape[1], k, nprobe, rescore_factor, float(min_score),
+                                    _ptr(ids), _ptr(sc), _ptr(cnt))
+        )
+        return ids, sc, cnt
 
     def ivf_search_device(self, queries, k: int, nprobe: int, rescore_factor: int = 1,
                           min_score: float = -3.4028235e38, stream=None):
@@ -604,8 +652,8 @@ class IvfFlatAdapter(IvfPqAdapter):
     IvfFlatAdapter.search (IvfFlatAdapter.java:102-140); ``ivf_search`` is IvfIndex.search's flat
     list scan (IvfIndex.java:170-289); the routing helpers are those of the IVF-PQ adapter."""
 
-    def __init__(self, nprobe: int = 32, device: int = 0):
-        super().__init__(nprobe=nprobe, rescore_factor=1, device=device)
+    def __init__(self, nprobe: int = 32, device: int = 0, gamma: float = 0.0):
+        super().__init__(nprobe=nprobe, rescore_factor=1, device=device, gamma=gamma)
 
     def build_prebuilt(self, centroids, list_offsets, list_ordinals, vectors, metric):
         cent = _as_matrix(centroids, "centroids")
@@ -626,6 +674,7 @@ class IvfFlatAdapter(IvfPqAdapter):
                                         int(metric), self.nprobe, C.byref(self._h.ptr)))
         self._n, self._dim, self.metric = n, dim, SimilarityFunction(metric)
         self._nlist = nlist
+        self._apply_gamma()
 
     def load_graph_bin(self, data, metric=None, vectors=None):
         """Opens an IVF_FLAT generation's graph.bin (VectorCollectionImpl.openIvfFlatAdapter):

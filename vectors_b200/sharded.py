@@ -37,17 +37,17 @@ def gather_and_merge(local_ids, local_scores, local_counts, offsets: Sequence[in
     world = dist.get_world_size(group)
     nq, kin = local_ids.shape
     dev = local_ids.device
-    gi = torch.empty((world, nq, kin), dtype=torch.int32, device=dev)
-    gs = torch.empty((world, nq, kin), dtype=torch.float32, device=dev)
-    gc = torch.empty((world, nq), dtype=torch.int32, device=dev)
+    # one collective: ids, score bits and the count of each query packed into an int32 row
+    packed = torch.cat([local_ids.to(torch.int32), local_scores.contiguous().view(torch.int32),
+                        local_counts.to(torch.int32).reshape(nq, 1)], 1)
+    g = torch.empty((world, nq, 2 * kin + 1), dtype=torch.int32, device=dev)
     if dev.type == "cuda":
-        dist.all_gather_into_tensor(gi, local_ids.contiguous(), group=group)
-        dist.all_gather_into_tensor(gs, local_scores.contiguous(), group=group)
-        dist.all_gather_into_tensor(gc, local_counts.contiguous(), group=group)
+        dist.all_gather_into_tensor(g, packed, group=group)
     else:  # gloo has no all_gather_into_tensor on every build: gather into per-rank views
-        dist.all_gather(list(gi.unbind(0)), local_ids.contiguous(), group=group)
-        dist.all_gather(list(gs.unbind(0)), local_scores.contiguous(), group=group)
-        dist.all_gather(list(gc.unbind(0)), local_counts.contiguous(), group=group)
+        dist.all_gather(list(g.unbind(0)), packed, group=group)
+    gi = g[:, :, :kin].contiguous()
+    gs = g[:, :, kin:2 * kin].contiguous().view(torch.float32)
+    gc = g[:, :, 2 * kin].contiguous()
     off = torch.tensor(list(offsets)[:world], dtype=torch.int64, device=dev)
     return (merge or merge_shards_device)(gi, gs, gc, off, k)
 
