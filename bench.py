@@ -187,6 +187,49 @@ def cpu_flat_baseline(db_sample, q_sample, total_rows, metric):
     return qps, th, dt
 
 
+def parity(got, ref, exact, rows):
+    """Compares a GPU result (ids [q][k], scores [q][k], counts [q]) with the oracle's on the same
+    queries and rows: ids must be identical, scores bit-exact (integer / code paths) or within
+    1e-4 relative (fp32 / fp16 paths)."""
+    gi, gs, gc = (np.asarray(a) for a in got)
+    ri, rs, rc = ref
+    ids_equal, bit, max_rel = True, True, 0.0
+    for i in range(len(rc)):
+        c = int(rc[i])
+        if int(gc[i]) != c or not np.array_equal(gi[i, :c], ri[i, :c]):
+            ids_equal = False
+            continue
+        if not np.array_equal(gs[i, :c], rs[i, :c]):
+            bit = False
+        if c:
+            a, b = gs[i, :c].astype(np.float64), rs[i, :c].astype(np.float64)
+            max_rel = max(max_rel, float(np.max(np.abs(a - b) / np.maximum(np.abs(b), 1e-30))))
+    return {"queries": int(len(rc)), "rows": int(rows), "against": "oracle (CPU restatement of the reference path)",
+            "bar": "ids equal, scores bit-exact" if exact else "ids equal, scores within 1e-4 relative",
+            "ids_equal": ids_equal, "scores_bit_exact": bit, "max_rel_score_diff": max_rel,
+            "ok": bool(ids_equal and (bit if exact else max_rel <= 1e-4))}
+
+
+def timed_oracle(fn):
+    """Runs one oracle call on all host threads; returns (result, seconds, threads)."""
+    th = os.cpu_count() or 1
+    t = time.perf_counter()
+    r = fn(th)
+    return r, time.perf_counter() - t, th
+
+
+def e2e_host(args, call, nq, h2d, d2h):
+    """End to end through a host-buffer C ABI call (queries copied in, results copied out inside
+    the timed region), one GPU: K blocking calls after one warm-up call, host wall clock."""
+    call()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        call()
+    dt = (time.perf_counter() - t0) / args.steps
+    return {"value": nq / dt, "unit": "queries/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+            "timing": "host wall clock around the blocking host-buffer call (one GPU)"}
+
+
 # ------------------------------------------------------------------ reference arm
 def run_reference(args, rank):
     if rank != 0:
@@ -316,15 +359,23 @@ def main():
     torch.cuda.empty_cache()
 
 
+    gm_events = []  # (start, end) around each step's all-gather + shard merge (N > 1)
+
     def flat_step():
         ids, sc, cnt = flat.search_batch_device(q_dev, k)
         if world == 1:
             return ids, sc, cnt
-        return gather_and_merge(ids, sc, cnt, offs, k)
+        e_a, e_b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e_a.record()
+        out = gather_and_merge(ids, sc, cnt, offs, k)
+        e_b.record()
+        gm_events.append((e_a, e_b))
+        return out
 
     for _ in range(args.warmup):
         flat_step()
     torch.cuda.synchronize()
+    gm_events.clear()
     barrier()
     launches0 = vx.kernel_launches()
     N.profile_reset()
@@ -348,11 +399,17 @@ def main():
     ms = max_over_ranks(ms_local)
     qps = nq / (ms / 1e3)
     per_rank = None
-    if world > 1:  # each rank's step time and scan time: load balance of the row shards
-        t = torch.tensor([ms_local, prof["gemm_scan"][0] / args.steps], dtype=torch.float64, device=dev)
-        g_ = torch.empty((world, 2), dtype=torch.float64, device=dev)
+    if world > 1:  # each rank's step time and its parts: load balance and the fixed per-rank work
+        slots = ["gemm_scan", "pilot", "merge", "rescore", "fallback"]
+        gm_ms = sum(a_.elapsed_time(b_) for a_, b_ in gm_events) / args.steps
+        vals = [ms_local] + [prof.get(sl, (0.0, 0))[0] / args.steps for sl in slots] + [gm_ms]
+        t = torch.tensor(vals, dtype=torch.float64, device=dev)
+        g_ = torch.empty((world, len(vals)), dtype=torch.float64, device=dev)
         dist.all_gather_into_tensor(g_, t)
-        per_rank = {"step_ms": g_[:, 0].tolist(), "gemm_scan_ms": g_[:, 1].tolist()}
+        per_rank = {"step_ms": g_[:, 0].tolist()}
+        for j, sl in enumerate(slots):
+            per_rank[sl + "_ms"] = g_[:, 1 + j].tolist()
+        per_rank["allgather_and_shard_merge_ms"] = g_[:, -1].tolist()
 
     # roofline of the dominant kernel: the tcgen05 scan (algorithmic flops 2 * nq * rows * dim)
     g_ms, g_n = prof["gemm_scan"]
@@ -403,6 +460,19 @@ def main():
     d2h = (nq * k * 8 + nq * 4) * (2 if world > 1 else 1)
     e2e = {"value": nq / e2e_s, "unit": "queries/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
            "timing": "host wall clock around the blocking host-buffer call, max over ranks"}
+
+    # ---- parity (rank 0, N=1): the same path on an index of the dataset's first rows, 64 queries
+    #      checked against the oracle (the 10M-row index itself is too large for the CPU check)
+    flat_parity = None
+    if cpu_sample is not None:
+        from oracle import oracle as O
+
+        sub = vx.FlatScanAdapter(device=local)
+        sub.build(cpu_sample, vx.SimilarityFunction.COSINE)
+        got = sub.search_batch_arrays(q_host[:64], k)
+        sub.close()
+        ref, _, _ = timed_oracle(lambda th: O.flat_search(cpu_sample, q_host[:64], FLAT["metric"], k, O.CANONICAL, th))
+        flat_parity = parity(got, ref, False, len(cpu_sample))
 
     # ---- CPU baseline (rank 0, N=1): the oracle on a bounded sample
     cpu = None
@@ -462,13 +532,14 @@ def main():
             "roofline": roofline,
             "cpu_baseline": cpu,
             "e2e": e2e,
+            "parity": flat_parity,
             "gpu_launches": launches,
             "clocks": clk,
-            "ivf_pq": ivf,
             "ivf_flat": ivfflat,
             "sq8": sq8,
             "bq": bq,
             "fp16": fp16,
+            "ivf_pq": ivf,  # last, so that a tail of the line keeps the second headline
         }
         print(json.dumps(line), flush=True)
     if world > 1:
@@ -579,6 +650,26 @@ def run_ivf(args, rank, world, local, dev, barrier, max_over_ranks, hbm_peak, pe
         per_rank = {"adc_ms": g_[:, 0].tolist()}
     # per GPU: this job's algorithmic bytes split over the ranks, over the slowest rank's scan
     achieved = bytes_step / world / (adc_ms / 1e3) / 1e9 if adc_ms > 0 else None
+    # shared-memory gather roof of the grouped ADC scan: each (four-query group, row, subspace)
+    # reads one 16-byte interleaved table entry, and a warp's 32 such reads take at least four
+    # 128-byte wavefronts; at 128 bytes per clock per SM that is this many seconds per step
+    pair_rows = bytes_step / (m + 4)
+    gather_bytes = pair_rows / 4.0 * m * 16.0 / world
+    smem_peak = 148 * 128 * 1.965e9  # bytes/s: 148 SMs x 128 B/clk x max SM clock (nominal)
+    smem_frac = (gather_bytes / smem_peak) / (adc_ms / 1e3) if adc_ms > 0 else None
+    par = cpu = e2e = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        from oracle import oracle as O
+
+        cent_h, loff_h, ord_h, books_h = (cent.cpu().numpy(), loff.cpu().numpy(), order.cpu().numpy(),
+                                          books.cpu().numpy().reshape(-1))
+        qs = qh[:256]
+        ref, dt, th = timed_oracle(lambda t: O.ivfpq_search(cent_h, loff_h, ord_h, m, ks, books_h, codes_h, qs, 0, k,
+                                                            P["nprobe"], 1, None, O.CANONICAL, t))
+        par = parity(a.ivf_search_arrays(qs, k, P["nprobe"]), ref, True, n)
+        cpu = {"value": len(qs) / dt, "unit": "queries/s", "cores": th, "kind": "port",
+               "sample": f"{len(qs)} queries over the same 10M-row index ({dt:.1f} s)"}
+        e2e = e2e_host(args, lambda: a.ivf_search_arrays(qh, k, P["nprobe"]), nq, nq * dim * 4, nq * (k * 8 + 4))
     a.close()
     return {
         "value": nq / (ms / 1e3),
@@ -593,7 +684,14 @@ def run_ivf(args, rank, world, local, dev, barrier, max_over_ranks, hbm_peak, pe
                      "algorithmic_bytes_per_step": bytes_step, "per": "GPU",
                      "sharding": "index replicated, queries split across ranks" if world > 1 else "single GPU",
                      "breakdown_ms_per_step": {kk: v[0] / args.steps for kk, v in prof.items() if v[1]},
-                     "per_rank": per_rank},
+                     "per_rank": per_rank,
+                     "smem_gather_roof": {"frac": smem_frac, "gather_bytes_per_step": gather_bytes,
+                                          "peak_bytes_per_s": smem_peak,
+                                          "peak_source": "nominal: 148 SMs x 128 B/clk x 1.965 GHz",
+                                          "note": "conflict-free minimum of the 16-byte four-query table reads"}},
+        "parity": par,
+        "cpu_baseline": cpu,
+        "e2e": e2e,
     }
 
 
@@ -675,18 +773,19 @@ def run_ivfflat(args, rank, world, local, dev, barrier, max_over_ranks, peak_kin
     ops = 2.0 * pair_rows * dim / world  # subtract + fused multiply-add per (query, row, dim)
     achieved = ops / (kms / 1e3) / 1e12 if kms > 0 else None
     peak = 148 * 128 * 1.965e9 / 1e12  # fp32 lanes x max SM clock, as instructions
-    cpu = None
+    cpu = par = e2e = None
     if rank == 0 and world == 1 and not args.no_cpu:  # the CPU baseline is a 1-GPU figure
         from oracle import oracle as O
 
-        th = os.cpu_count() or 1
         qs = qh[:64]
-        t = time.perf_counter()
-        O.ivfflat_search(cent.cpu().numpy(), loff.cpu().numpy(), order.cpu().numpy(), rows.cpu().numpy(), qs, 0, k,
-                         P["nprobe"], O.REFERENCE_HEAP, th)
-        dt = time.perf_counter() - t
+        cent_h, loff_h, ord_h, rows_h = cent.cpu().numpy(), loff.cpu().numpy(), order.cpu().numpy(), rows.cpu().numpy()
+        radii = O.ivf_radii(cent_h, loff_h, ord_h, rows_h)  # BuoyIndex.computeRadii, as the index holds them
+        ref, dt, th = timed_oracle(lambda t: O.ivfflat_search_full(cent_h, loff_h, ord_h, rows_h, radii, qs, 0, k,
+                                                                   P["nprobe"], nthreads=t))
+        par = parity(a.ivf_search_arrays(qs, k, P["nprobe"]), ref, True, n)
         cpu = {"value": len(qs) / dt, "unit": "queries/s", "cores": th, "kind": "port",
                "sample": f"{len(qs)} queries over the same index ({dt:.1f} s)"}
+        e2e = e2e_host(args, lambda: a.ivf_search_arrays(qh, k, P["nprobe"]), nq, nq * dim * 4, nq * (k * 8 + 4))
     a.close()
     del rows
     torch.cuda.empty_cache()
@@ -699,7 +798,9 @@ def run_ivfflat(args, rank, world, local, dev, barrier, max_over_ranks, peak_kin
                      "kernel": "flat_list_kernel (IVF-flat list scan)", "per": "GPU",
                      "peak_source": "nominal: 148 SMs x 128 fp32 lanes x 1.965 GHz",
                      "pair_rows_per_step": pair_rows, "breakdown_ms_per_step": br},
+        "parity": par,
         "cpu_baseline": cpu,
+        "e2e": e2e,
     }
 
 
@@ -740,6 +841,18 @@ def run_sq8(args, rank, world, local, dev, barrier, max_over_ranks, tc_sustained
         return ids if world == 1 else gather_and_merge(ids, sc, cnt, offs, k)[0]
 
     ms, kms, br = _timed_scan(args, world, dev, barrier, max_over_ranks, step, "gemm_scan")
+    par = cpu = e2e = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        from oracle import oracle as O
+
+        qh = q.cpu().numpy()
+        corr_h = corr.cpu().numpy()
+        ref, dt, th = timed_oracle(lambda t: O.sq8_search(codes, corr_h, mn, mx, qh[:64], O.DOT_PRODUCT, k,
+                                                          O.CANONICAL, t))
+        par = parity(a.scan_candidates_arrays(qh[:64], k), ref, True, n)
+        cpu = {"value": 64 / dt, "unit": "queries/s", "cores": th, "kind": "port",
+               "sample": f"64 queries over the same {n:,}-row index ({dt:.1f} s)"}
+        e2e = e2e_host(args, lambda: a.scan_candidates_arrays(qh, k), nq, nq * dim * 4, nq * (k * 8 + 4))
     a.close()
     ops = 2.0 * nq * (hi - lo) * dim  # int8 multiply-adds x 2 on this rank
     achieved = ops / (kms / 1e3) / 1e12 if kms > 0 else None
@@ -753,6 +866,9 @@ def run_sq8(args, rank, world, local, dev, barrier, max_over_ranks, tc_sustained
                      "kernel": "gemm_scan_kernel (tcgen05 kind::i8, fused top-K)", "per": "GPU",
                      "peak_source": f"2 x {peak_kind} dense bf16 sustained (int8 MMA runs at twice the bf16 rate)",
                      "breakdown_ms_per_step": br},
+        "parity": par,
+        "cpu_baseline": cpu,
+        "e2e": e2e,
     }
 
 
@@ -801,16 +917,29 @@ def run_bq(args, rank, world, local, dev, barrier, max_over_ranks, tc_sustained,
     comp = torch.randint(0, P["comps"], (nq,), generator=gq, device=dev)
     q = cent[comp] + P["sigma"] * torch.randn((nq, dim), generator=gq, device=dev)
     a = vx.QuantizedFlatScanAdapter(device=local)
-    a.build_bq(words.cpu().numpy().view(np.uint64), dim, vx.SimilarityFunction.DOT_PRODUCT)
+    words_h = words.cpu().numpy().view(np.uint64)
+    a.build_bq(words_h, dim, vx.SimilarityFunction.DOT_PRODUCT)
     del words
     torch.cuda.empty_cache()
+    check = rank == 0 and world == 1 and not args.no_cpu
+    qh = q.cpu().numpy()
 
     def step():
         ids, sc, cnt = a.scan_candidates_device(q, k)
         return ids if world == 1 else gather_and_merge(ids, sc, cnt, offs, k)[0]
 
     ms, kms, br = _timed_scan(args, world, dev, barrier, max_over_ranks, step, "gemm_scan")
+    par = cpu = e2e = None
+    if check:
+        from oracle import oracle as O
+
+        ref, dt, th = timed_oracle(lambda t: O.bq_search(words_h, dim, qh[:64], O.DOT_PRODUCT, k, O.CANONICAL, t))
+        par = parity(a.scan_candidates_arrays(qh[:64], k), ref, True, n)
+        cpu = {"value": 64 / dt, "unit": "queries/s", "cores": th, "kind": "port",
+               "sample": f"64 queries over the same {n:,}-row index ({dt:.1f} s)"}
+        e2e = e2e_host(args, lambda: a.scan_candidates_arrays(qh, k), nq, nq * dim * 4, nq * (k * 8 + 4))
     a.close()
+    del words_h
     rows = hi - lo
     if br.get("gemm_scan"):
         # tensor-core path: +-1 int8 operands, dot = D - 2h, exact int32 (2 ops per bit pair)
@@ -831,8 +960,8 @@ def run_bq(args, rank, world, local, dev, barrier, max_over_ranks, tc_sustained,
     # BBQ (BinaryMode.BBQ): 4-bit queries against the centroid-relative sign bits; rawAsymDot on
     # the int8 tensor cores (0/1 rows x 4-bit codes), or the popcount kernel without the operand
     b = vx.QuantizedFlatScanAdapter(device=local)
-    b.build_bbq(bbq_words.cpu().numpy().view(np.uint64), bbq_corr.cpu().numpy(), bbq_c.cpu().numpy(), dim,
-                vx.SimilarityFunction.DOT_PRODUCT)
+    bw_h, bc_h, bcent_h = bbq_words.cpu().numpy().view(np.uint64), bbq_corr.cpu().numpy(), bbq_c.cpu().numpy()
+    b.build_bbq(bw_h, bc_h, bcent_h, dim, vx.SimilarityFunction.DOT_PRODUCT)
     del bbq_words, bbq_corr
 
     def bstep():
@@ -840,6 +969,16 @@ def run_bq(args, rank, world, local, dev, barrier, max_over_ranks, tc_sustained,
         return ids if world == 1 else gather_and_merge(ids, sc, cnt, offs, k)[0]
 
     bms_step, bkms, bbr = _timed_scan(args, world, dev, barrier, max_over_ranks, bstep, "gemm_scan")
+    bpar = bcpu = be2e = None
+    if check:
+        from oracle import oracle as O
+
+        ref, dt, th = timed_oracle(lambda t: O.bbq_search(bw_h, bc_h, bcent_h, dim, qh[:64], O.DOT_PRODUCT, k,
+                                                          O.CANONICAL, t))
+        bpar = parity(b.scan_candidates_arrays(qh[:64], k), ref, True, nb)
+        bcpu = {"value": 64 / dt, "unit": "queries/s", "cores": th, "kind": "port",
+                "sample": f"64 queries over the same {nb:,}-row index ({dt:.1f} s)"}
+        be2e = e2e_host(args, lambda: b.scan_candidates_arrays(qh, k), nq, nq * dim * 4, nq * (k * 8 + 4))
     b.close()
     if bbr.get("gemm_scan"):
         dp8 = (dim + 127) // 128 * 128
@@ -859,11 +998,14 @@ def run_bq(args, rank, world, local, dev, barrier, max_over_ranks, tc_sustained,
     bbq = {"value": nq / (bms_step / 1e3), "unit": "queries/s", "ms_per_step": bms_step,
            "config": {"workload": f"BBQ candidate scan n={nb * world:,} x {dim} bits (4-bit queries) "
                                   f"queries={nq:,} k={k}"},
-           "roofline": broof}
+           "roofline": broof, "parity": bpar, "cpu_baseline": bcpu, "e2e": be2e}
     return {
         "value": nq / (ms / 1e3), "unit": "queries/s", "ms_per_step": ms,
         "config": {"workload": f"BQ sign-bit Hamming candidate scan n={n:,} x {dim} bits queries={nq:,} k={k}"},
         "roofline": roof,
+        "parity": par,
+        "cpu_baseline": cpu,
+        "e2e": e2e,
         "bbq": bbq,
     }
 
@@ -898,6 +1040,8 @@ def run_fp16(args, rank, world, local, dev, barrier, max_over_ranks, tc_sustaine
     q = q / q.norm(dim=1, keepdim=True)
     a = vx.QuantizedFlatScanAdapter(device=local)
     a.build_fp16(rows, vx.SimilarityFunction.DOT_PRODUCT)
+    check = rank == 0 and world == 1 and not args.no_cpu
+    sub_h = rows[: min(per, 1_000_000)].cpu().numpy().view(np.uint16) if check else None
     del rows, cent
     torch.cuda.empty_cache()
 
@@ -906,7 +1050,24 @@ def run_fp16(args, rank, world, local, dev, barrier, max_over_ranks, tc_sustaine
         return ids if world == 1 else gather_and_merge(ids, sc, cnt, offs, k)[0]
 
     ms, kms, br = _timed_scan(args, world, dev, barrier, max_over_ranks, step, "gemm_scan")
-    a.close()
+    par = cpu = e2e = None
+    if check:
+        from oracle import oracle as O
+
+        qh = q.cpu().numpy()
+        e2e = e2e_host(args, lambda: a.scan_candidates_arrays(qh, k), nq, nq * dim * 4, nq * (k * 8 + 4))
+        a.close()
+        # parity on an index of this GPU's first 1M rows (the CPU check of 12.5M rows would take minutes)
+        sub = vx.QuantizedFlatScanAdapter(device=local)
+        sub.build_fp16(sub_h, vx.SimilarityFunction.DOT_PRODUCT)
+        got = sub.scan_candidates_arrays(qh[:64], k)
+        sub.close()
+        ref, dt, th = timed_oracle(lambda t: O.fp16_search(sub_h, qh[:64], O.DOT_PRODUCT, k, O.CANONICAL, t))
+        par = parity(got, ref, False, len(sub_h))
+        cpu = {"value": 64 / dt * (len(sub_h) / per), "unit": "queries/s", "cores": th, "kind": "port",
+               "sample": f"64 queries x {len(sub_h):,} rows ({dt:.1f} s); QPS scaled by rows/{per:,}"}
+    else:
+        a.close()
     flops = 2.0 * nq * per * dim
     achieved = flops / (kms / 1e3) / 1e12 if kms > 0 else None
     return {
@@ -918,6 +1079,9 @@ def run_fp16(args, rank, world, local, dev, barrier, max_over_ranks, tc_sustaine
                      "frac": (achieved / tc_sustained) if achieved else None, "traffic": None, "per": "GPU",
                      "kernel": "gemm_scan_kernel (tcgen05 kind::f16, fused top-K)",
                      "peak_source": f"{peak_kind} dense bf16/fp16 sustained", "breakdown_ms_per_step": br},
+        "parity": par,
+        "cpu_baseline": cpu,
+        "e2e": e2e,
     }
 
 
