@@ -68,7 +68,8 @@ typedef enum vx_index_kind {
   VX_KIND_IVFPQ = 4, /* IndexType.IVF_PQ -> IvfPqAdapter / IvfIndex.pqSearch                 */
   VX_KIND_IVFFLAT = 5, /* IndexType.IVF_FLAT -> IvfFlatAdapter / IvfIndex.search (no PQ)      */
   VX_KIND_SQ4 = 6,     /* QuantizerKind.SQ4 -> QuantizedFlatScanAdapter(ScalarQuantizedVectors INT4) */
-  VX_KIND_BBQ = 7      /* QuantizerKind.BQ, BinaryMode.BBQ -> QuantizedFlatScanAdapter(BinaryQuantizedVectors) */
+  VX_KIND_BBQ = 7,     /* QuantizerKind.BQ, BinaryMode.BBQ -> QuantizedFlatScanAdapter(BinaryQuantizedVectors) */
+  VX_KIND_PQ = 8       /* QuantizerKind.PQ -> QuantizedFlatScanAdapter(PQVectors) */
 } vx_index_kind;
 
 typedef struct vx_index vx_index;
@@ -146,6 +147,16 @@ VX_API int vx_bq_build(int32_t device, const uint64_t* words, int64_t n, int32_t
 VX_API int vx_bbq_build(int32_t device, const uint64_t* words, const float* corrections, const float* centroid,
                         int64_t n, int32_t dim, int32_t metric, const float* vectors, int64_t row_stride,
                         vx_index** out);
+/* PQVectors (vectors-quantization/.../PQVectors.java:40-191) wrapped as in QuantizedFlatScanAdapter:
+ * a ProductQuantizer with m subspaces of ks centroids (ProductQuantizer.fromState), codebooks
+ * concatenated per subspace with computeSubspaceSizesAndOffsets' sizes (ProductQuantizer.java:686-700),
+ * the global centroid [dim] or NULL, codes [n][m] (host memory).  Scored as scoreFunctionFor does:
+ * buildADCTable of the query minus the global centroid, the sequential fp32 sum of the m entries,
+ * then the metric's PQVectors transform (COSINE with the centred query norm and the rows' summed
+ * centroid norms).  vectors (fp32, optional) enable the exact rescore of vx_search_batch. */
+VX_API int vx_pq_build(int32_t device, const float* codebooks, const float* global_centroid, const uint8_t* codes,
+                       int64_t n, int32_t dim, int32_t m, int32_t ks, int32_t metric, const float* vectors,
+                       int64_t row_stride, vx_index** out);
 /* IvfIndex.fromPrebuilt(buoy, partitions, vectors, metric, pq, codes)
  * (vectors-ivf/.../IvfIndex.java:343-351): centroids [nlist][dim]; partitions as CSR
  * (list_offsets[nlist+1], list_ordinals); PQ with m subspaces of ks centroids, codebooks
@@ -172,9 +183,10 @@ VX_API int vx_ivfflat_build(int32_t device, const float* centroids, int32_t nlis
  * quantized.bin as written by QuantizedVectorsCodec.encode and read by .decode
  * (vectors-db/.../storage/QuantizedVectorsCodec.java:91-192): little-endian, header magic 'VQTZ'
  * (FileFormat.java:77), version 1, QuantizerKind ordinal, dimension, vectorCount.  SQ8 / SQ4
- * (:224-296), BQ SIGN_BIT and BBQ (:425-518) and FP16 (:194-221) payloads build the index
- * vx_sq8_build / vx_sq4_build / vx_bq_build / vx_bbq_build / vx_fp16_build would; PQ, RABITQ, NVQ,
- * TURBOQUANT and EXTENDED_RABITQ return VX_ERR_UNSUPPORTED.  The collection's metric is not stored in the file.  vectors
+ * (:224-296), BQ SIGN_BIT and BBQ (:425-518), FP16 (:194-221) and PQ (:298-420) payloads build the
+ * index vx_sq8_build / vx_sq4_build / vx_bq_build / vx_bbq_build / vx_fp16_build / vx_pq_build would;
+ * PQ with subspaces other than computeSubspaceSizesAndOffsets', RABITQ, NVQ, TURBOQUANT and
+ * EXTENDED_RABITQ return VX_ERR_UNSUPPORTED.  The collection's metric is not stored in the file.  vectors
  * (optional) are the fp32 rows for the two-pass rescore, e.g. a mapped vectors.bin with
  * row_stride = alignUp(dim*4, 64)/4.  Malformed bytes return VX_ERR_FORMAT with the decoder's
  * message. */
@@ -230,7 +242,7 @@ VX_API int vx_search_batch_device(vx_index* index, const float* d_queries, int32
                            int32_t k, int32_t search_list_size, float over_query_factor,
                            int32_t* d_ids, float* d_scores, int32_t* d_counts, void* stream);
 /* QuantizedFlatScanAdapter.selectApproximateCandidates (QuantizedFlatScanAdapter.java:97-113):
- * the k best rows by the compressed ScoreFunction (SQ8 / BQ / FP16 scores), no rescore. */
+ * the k best rows by the compressed ScoreFunction (SQ8 / SQ4 / BQ / BBQ / FP16 / PQ scores), no rescore. */
 VX_API int vx_scan_candidates(vx_index* index, const float* queries, int32_t nq, int32_t dim, int32_t k,
                        int32_t* out_ids, float* out_scores, int32_t* out_counts);
 VX_API int vx_scan_candidates_device(vx_index* index, const float* d_queries, int32_t nq, int32_t dim,

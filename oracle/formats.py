@@ -75,6 +75,26 @@ def quantized_bin_bq(words, dim: int, bbq_centroid=None, bbq_corrections=None) -
     return _header(BQ, dim, n) + struct.pack("<i", BBQ) + cent.tobytes() + rec.tobytes()
 
 
+def quantized_bin_pq(codes, codebooks, dim: int, m: int, ks: int, global_centroid=None, subs=None) -> bytes:
+    """encodePQ: numSubspaces, numClusters, hasGlobalCentroid (+ the centroid), m (size, offset)
+    pairs (default computeSubspaceSizesAndOffsets), the codebooks concatenated per subspace, then
+    per vector its m code bytes."""
+    codes = np.ascontiguousarray(codes, dtype=np.uint8)
+    n = codes.shape[0]
+    if subs is None:
+        base, rem, o = dim // m, dim % m, 0
+        subs = []
+        for s_ in range(m):
+            sz = base + (1 if s_ < rem else 0)
+            subs.append((sz, o))
+            o += sz
+    out = _header(PQ, dim, n) + struct.pack("<iii", m, ks, 0 if global_centroid is None else 1)
+    if global_centroid is not None:
+        out += np.ascontiguousarray(global_centroid, dtype="<f4").tobytes()
+    out += b"".join(struct.pack("<ii", sz, so) for sz, so in subs)
+    return out + np.ascontiguousarray(codebooks, dtype="<f4").tobytes() + codes.tobytes()
+
+
 def quantized_bin_fp16(codes) -> bytes:
     """encodeFp16: no quantizer state; dim little-endian binary16 values per vector."""
     codes = np.ascontiguousarray(codes, dtype="<u2")

@@ -81,6 +81,7 @@ def lib() -> C.CDLL:
             "vo_bq_search": (None, [p, i64, i32, i32, p, i32, i32, i32, i32, p, p, p]),
             "vo_fp16_search": (None, [p, i64, i32, i32, p, i32, i32, i32, i32, p, p, p]),
             "vo_quantized_two_pass_search": (None, [i32, p, p, f32, f32, p, i64, i32, i32, p, i32, i32, f32, i32, i32, p, p, p]),
+            "vo_pq_flat_search": (None, [p, p, p, i64, i32, i32, i32, i32, p, i32, i32, i32, i32, p, p, p]),
             "vo_rescore_candidates": (None, [p, i32, i32, p, i32, p, i32, p, i32, i32, i32, p, p, p]),
             "vo_route": (None, [p, i32, i32, i32, p, i32, i32, i32, i32, p, p]),
             "vo_ivfpq_search": (None, [p, i32, i32, p, p, i32, i32, p, p, i64, i32, p, i32, i32, i32, i32, p, i32, i32, p, p, p]),
@@ -377,6 +378,18 @@ def quantized_two_pass(kind, qdata, qcorr, min_q, max_q, db, queries, metric, k,
     lib().vo_quantized_two_pass_search(kind, P(qdata), P(None if qcorr is None else f32(qcorr)), min_q, max_q, P(db),
                                        db.shape[0], db.shape[1], metric, P(q), q.shape[0], k, oqf, policy,
                                        nthreads or threads(), P(ids), P(sc), P(cnt))
+    return ids, sc, cnt
+
+
+def pq_flat_search(codebooks, codes, dim, m, ks, queries, metric, k, global_centroid=None, policy=CANONICAL,
+                   nthreads=None):
+    """QuantizedFlatScanAdapter over PQVectors: the k best rows by PQVectors' ADC score."""
+    q = f32(queries)
+    codes = np.ascontiguousarray(codes, np.uint8)
+    gc = None if global_centroid is None else f32(global_centroid)
+    ids, sc, cnt = _outs(q.shape[0], k)
+    lib().vo_pq_flat_search(P(f32(codebooks)), P(gc), P(codes), codes.shape[0], dim, m, ks, metric, P(q), q.shape[0], k,
+                            policy, nthreads or threads(), P(ids), P(sc), P(cnt))
     return ids, sc, cnt
 
 

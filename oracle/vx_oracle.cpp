@@ -1087,6 +1087,73 @@ void vo_fp16_search(const uint16_t* codes, int64_t n, int32_t dim, int32_t metri
             },
             ids, scores, counts);
 }
+// PQVectors.scoreFunctionFor (PQVectors.java:104-191) behind QuantizedFlatScanAdapter's
+// candidate heap: per query, ProductQuantizer.buildADCTable (ProductQuantizer.java:521-544) of
+// the query minus the global centroid (subInPlace, when the quantizer has one): dotProduct
+// entries for DOT_PRODUCT / COSINE / MAXIMUM_INNER_PRODUCT, squareDistance entries for
+// EUCLIDEAN; per row the sequential fp32 sum of the M entries, then
+//   DOT_PRODUCT  max((1 + sum) / 2, 0);  EUCLIDEAN  1 / (1 + sum);  MIP  scaleMaxInnerProductScore(sum);
+//   COSINE  dot / (|q - gc| * sqrt(sum of centroidNormSq[m][code[m]])), 0 when either norm is 0,
+//           then max((1 + cos) / 2, 0); centroidNormSq and |q - gc|^2 sequential sums of squares.
+// Codebooks concatenated per subspace with computeSubspaceSizesAndOffsets' sizes.
+void vo_pq_flat_search(const float* cb, const float* global_centroid, const uint8_t* codes, int64_t n, int32_t dim,
+                       int32_t m, int32_t ks, int32_t metric, const float* queries, int32_t nq, int32_t k,
+                       int32_t policy, int32_t nthreads, int32_t* ids, float* scores, int32_t* counts) {
+  std::vector<int32_t> so;
+  std::vector<int64_t> off = codebook_offsets(dim, m, ks, so);
+  std::vector<float> cnorm((size_t)m * ks);  // PQVectors.precomputeCentroidNormsSq (:73-89)
+  for (int s = 0; s < m; s++) {
+    const int sub = so[2 * s];
+    for (int c = 0; c < ks; c++) {
+      const float* cc = cb + off[s] + (size_t)c * sub;
+      float norm = 0.0f;
+      for (int d = 0; d < sub; d++) norm += cc[d] * cc[d];
+      cnorm[(size_t)s * ks + c] = norm;
+    }
+  }
+  const int kk = (int)std::min<int64_t>(k, n);
+  parallel_for(nq, nthreads, [&](int64_t lo, int64_t hi) {
+    std::vector<float> table((size_t)m * ks), qc(dim);
+    for (int64_t q = lo; q < hi; q++) {
+      const float* qq = queries + q * dim;
+      for (int d = 0; d < dim; d++) qc[d] = global_centroid ? qq[d] - global_centroid[d] : qq[d];
+      vo_pq_adc_table(qc.data(), dim, m, ks, cb, metric == VO_EUCLIDEAN ? 0 : 1, table.data());
+      float qnorm_sq = 0.0f;
+      for (int d = 0; d < dim; d++) qnorm_sq += qc[d] * qc[d];
+      const float qnorm = (float)std::sqrt((double)qnorm_sq);
+      auto score = [&](int64_t r) -> float {
+        const uint8_t* code = codes + r * m;
+        float sum = 0.0f, vsq = 0.0f;
+        for (int s = 0; s < m; s++) sum += table[(size_t)s * ks + code[s]];
+        switch (metric) {
+          case VO_EUCLIDEAN: return 1.0f / (1.0f + sum);
+          case VO_MAXIMUM_INNER_PRODUCT: return vo_scale_mip(sum);
+          case VO_COSINE: {
+            for (int s = 0; s < m; s++) vsq += cnorm[(size_t)s * ks + code[s]];
+            const float vnorm = (float)std::sqrt((double)vsq);
+            if (qnorm == 0.0f || vnorm == 0.0f) return 0.0f;
+            const float cosv = sum / (qnorm * vnorm);
+            return java_max((1.0f + cosv) / 2.0f, 0.0f);
+          }
+          default: return java_max((1.0f + sum) / 2.0f, 0.0f);
+        }
+      };
+      int32_t* oi = ids + q * k;
+      float* os = scores + q * k;
+      if (kk <= 0) {
+        counts[q] = 0;
+      } else if (policy == VO_POLICY_REFERENCE_HEAP) {
+        RefHeap h(kk);
+        for (int64_t r = 0; r < n; r++) h.offer((int32_t)r, score(r));
+        counts[q] = h.drain(oi, os);
+      } else {
+        CanonTopK h(kk);
+        for (int64_t r = 0; r < n; r++) h.offer((int32_t)r, score(r));
+        counts[q] = h.drain(oi, os);
+      }
+    }
+  });
+}
 // QuantizedFlatScanAdapter.search (QuantizedFlatScanAdapter.java:59-95).
 void vo_quantized_two_pass_search(int32_t kind, const void* qdata, const float* qcorr,
                                   float min_q, float max_q, const float* db, int64_t n,

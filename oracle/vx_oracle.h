@@ -139,6 +139,12 @@ void vo_bbq_search(const uint64_t* words, const float* corr, const float* cent, 
 void vo_fp16_search(const uint16_t* codes, int64_t n, int32_t dim, int32_t metric,
                     const float* queries, int32_t nq, int32_t k, int32_t policy, int32_t nthreads,
                     int32_t* ids, float* scores, int32_t* counts);
+/* PQVectors.scoreFunctionFor (PQVectors.java:104-191): the k best rows by the PQ score; codebooks
+ * concatenated per subspace (standard sizes), global_centroid NULL when the quantizer has none,
+ * codes [n][m]. */
+void vo_pq_flat_search(const float* codebooks, const float* global_centroid, const uint8_t* codes, int64_t n,
+                       int32_t dim, int32_t m, int32_t ks, int32_t metric, const float* queries, int32_t nq,
+                       int32_t k, int32_t policy, int32_t nthreads, int32_t* ids, float* scores, int32_t* counts);
 /* QuantizedFlatScanAdapter.search (QuantizedFlatScanAdapter.java:59-95): kind 0=SQ8 1=BQ 2=FP16;
  * qdata/qaux are the kind's codes (and SQ8 corrections / quantiles in qaux[0..1]). */
 void vo_quantized_two_pass_search(int32_t kind, const void* qdata, const float* qcorr,

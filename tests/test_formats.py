@@ -78,13 +78,39 @@ def test_quantized_kinds_not_served():
     big = np.zeros((2, 17), np.uint64)  # BBQ beyond 1024 dimensions is refused
     with pytest.raises(vx.UnsupportedOperationException, match="BBQ"):
         vx.quantized_bin_info(F.quantized_bin_bq(big, 1050, np.zeros(1050, np.float32), np.zeros((2, 3), np.float32)))
-    # a PQ payload: the header is validated, the kind is refused
+    # a PQ payload cut after the header: decodePQ's first ensureRemaining
     pq = struct.pack("<iiiii", F.MAGIC_QUANTIZED, 1, F.PQ, 16, 3)
-    with pytest.raises(vx.UnsupportedOperationException, match="PQ"):
+    with pytest.raises(vx.IOException, match="PQ quantizer state header"):
         vx.quantized_bin_info(pq)
     # a truncated BBQ file is still a format error, as in decodeBQ
     with pytest.raises(vx.IOException, match="BQ centroid"):
         vx.quantized_bin_info(struct.pack("<iiiiii", F.MAGIC_QUANTIZED, 1, F.BQ, 64, 4, F.BBQ))
+
+
+def test_quantized_pq_payload_decodes_as_decodePQ():
+    # QuantizedVectorsCodec.decodePQ (:367-420): state, optional global centroid, subspaces,
+    # codebooks, codes; its IOException reasons for each malformed part
+    dim, m, ks, n = 16, 4, 8, 3
+    cb = np.arange(ks * dim, dtype=np.float32)
+    codes = np.zeros((n, m), np.uint8)
+    assert vx.quantized_bin_info(F.quantized_bin_pq(codes, cb, dim, m, ks)) == (F.PQ, dim, n)
+    assert vx.quantized_bin_info(F.quantized_bin_pq(codes, cb, dim, m, ks, np.ones(dim, np.float32))) == (F.PQ, dim, n)
+    head = struct.pack("<iiiii", F.MAGIC_QUANTIZED, 1, F.PQ, dim, n)
+    with pytest.raises(vx.IOException, match="numSubspaces must be positive: 0"):
+        vx.quantized_bin_info(head + struct.pack("<iii", 0, ks, 0))
+    with pytest.raises(vx.IOException, match=r"numClusters must be in \[1, 256\]: 300"):
+        vx.quantized_bin_info(head + struct.pack("<iii", m, 300, 0))
+    with pytest.raises(vx.IOException, match="hasGlobalCentroid must be 0 or 1: 2"):
+        vx.quantized_bin_info(head + struct.pack("<iii", m, ks, 2))
+    with pytest.raises(vx.IOException, match="PQ globalCentroid"):
+        vx.quantized_bin_info(head + struct.pack("<iii", m, ks, 1))
+    with pytest.raises(vx.IOException, match="PQ codebook 0"):
+        vx.quantized_bin_info(head + struct.pack("<iii", m, ks, 0) + b"".join(struct.pack("<ii", 4, 4 * i) for i in range(m)))
+    with pytest.raises(vx.IOException, match="PQ vector data"):
+        vx.quantized_bin_info(F.quantized_bin_pq(codes, cb, dim, m, ks)[:-1])
+    odd = F.quantized_bin_pq(codes, cb, dim, m, ks, subs=[(5, 0), (3, 5), (4, 8), (4, 12)])
+    with pytest.raises(vx.UnsupportedOperationException, match="computeSubspaceSizesAndOffsets"):
+        vx.quantized_bin_info(odd)
 
 
 def test_quantized_accepts_paths_and_arrays(tmp_path):

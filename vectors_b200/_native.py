@@ -22,7 +22,7 @@ VX_ERR_UNSUPPORTED = 6
 VX_ERR_DEVICE_TIMEOUT = 7
 VX_ERR_FORMAT = 8
 
-VX_KIND_FLAT, VX_KIND_FP16, VX_KIND_SQ8, VX_KIND_BQ, VX_KIND_IVFPQ, VX_KIND_IVFFLAT, VX_KIND_SQ4, VX_KIND_BBQ = range(8)
+VX_KIND_FLAT, VX_KIND_FP16, VX_KIND_SQ8, VX_KIND_BQ, VX_KIND_IVFPQ, VX_KIND_IVFFLAT, VX_KIND_SQ4, VX_KIND_BBQ, VX_KIND_PQ = range(9)
 
 _P = C.c_void_p
 _I32 = C.c_int32
@@ -45,6 +45,7 @@ SIGNATURES = {
     "vx_sq4_build": [_I32, _P, _P, _I64, _I32, _F32, _F32, _I32, _P, _I64, _PP],
     "vx_bq_build": [_I32, _P, _I64, _I32, _I32, _P, _I64, _PP],
     "vx_bbq_build": [_I32, _P, _P, _P, _I64, _I32, _I32, _P, _I64, _PP],
+    "vx_pq_build": [_I32, _P, _P, _P, _I64, _I32, _I32, _I32, _I32, _P, _I64, _PP],
     "vx_ivfpq_build": [_I32, _P, _I32, _I32, _P, _P, _I32, _I32, _P, _P, _I64, _I32, _P, _I32, _I32, _PP],
     "vx_quantized_bin_info": [_P, _I64, _P, _P, _P],
     "vx_quantized_bin_build": [_I32, _P, _I64, _I32, _P, _I64, _PP],

@@ -88,6 +88,12 @@ struct QuantizedFile {
   int32_t dim = 0, count = 0;
   float min_q = 0, max_q = 0;  // SQ
   int bq_mode = 0;             // BinaryMode ordinal: 0 SIGN_BIT, 1 BBQ
+  // PQ: numSubspaces, numClusters, the global centroid's offset (0: none), the codebooks
+  // concatenated per subspace, and whether the subspaces are computeSubspaceSizesAndOffsets'
+  int32_t pq_m = 0, pq_ks = 0;
+  uint64_t pq_gc = 0;
+  std::vector<float> pq_codebooks;
+  bool pq_standard = true;
   uint64_t data = 0;           // offset of the per-vector records
 };
 
@@ -150,6 +156,43 @@ int parse_quantized(const uint8_t* bytes, int64_t len, QuantizedFile& f) {
     case kFp16:  // decodeFp16 (:211-221)
       if (int s = ensure(c, d * 2 * n, "FP16 vector data")) return s;
       break;
+    case kPq: {  // decodePQ (:367-420)
+      if (int s = ensure(c, 12, "PQ quantizer state header")) return s;
+      f.pq_m = c.i32();
+      f.pq_ks = c.i32();
+      const int32_t has_gc = c.i32();
+      if (f.pq_m <= 0) return failf(VX_ERR_FORMAT, "quantized.bin PQ numSubspaces must be positive: %d", f.pq_m);
+      if (f.pq_ks <= 0 || f.pq_ks > 256)
+        return failf(VX_ERR_FORMAT, "quantized.bin PQ numClusters must be in [1, 256]: %d", f.pq_ks);
+      if (has_gc == 1) {
+        if (int s = ensure(c, d * 4, "PQ globalCentroid")) return s;
+        f.pq_gc = c.pos;
+        c.pos += d * 4;
+      } else if (has_gc != 0) {
+        return failf(VX_ERR_FORMAT, "quantized.bin PQ hasGlobalCentroid must be 0 or 1: %d", has_gc);
+      }
+      const uint64_t m = (uint64_t)f.pq_m;
+      if (int s = ensure(c, m * 8, "PQ subspaceSizesAndOffsets")) return s;
+      std::vector<int32_t> sizes(m);
+      const int base = f.dim / f.pq_m, rem = f.dim % f.pq_m;
+      int expect_off = 0;
+      for (uint64_t i = 0; i < m; i++) {
+        sizes[i] = c.i32();
+        const int32_t off = c.i32();
+        if (sizes[i] != base + ((int)i < rem ? 1 : 0) || off != expect_off) f.pq_standard = false;
+        expect_off += sizes[i];
+      }
+      for (uint64_t i = 0; i < m; i++) {
+        if (sizes[i] < 0) return failf(VX_ERR_FORMAT, "quantized.bin PQ subspace %d has size %d", (int)i, sizes[i]);
+        const uint64_t len = (uint64_t)f.pq_ks * (uint64_t)sizes[i];
+        char what[48];
+        snprintf(what, sizeof(what), "PQ codebook %d", (int)i);
+        if (int s = ensure(c, len * 4, what)) return s;
+        for (uint64_t j = 0; j < len; j++) f.pq_codebooks.push_back(c.f32());
+      }
+      if (int s = ensure(c, n * m, "PQ vector data")) return s;
+      break;
+    }
     default:
       break;  // validated by the kinds this library serves only
   }
@@ -160,8 +203,11 @@ int parse_quantized(const uint8_t* bytes, int64_t len, QuantizedFile& f) {
 int unsupported_kind(const QuantizedFile& f) {
   if (f.kind == kBq && f.bq_mode == 1 && f.dim > 1024)
     return failf(VX_ERR_UNSUPPORTED, "quantized.bin BQ in BBQ mode is served up to 1024 dimensions, not %d", f.dim);
-  if (f.kind != kSq8 && f.kind != kSq4 && f.kind != kBq && f.kind != kFp16)
-    return failf(VX_ERR_UNSUPPORTED, "quantized.bin kind %s is not served here (SQ8, SQ4, BQ SIGN_BIT and FP16 are)",
+  if (f.kind == kPq && (!f.pq_standard || f.pq_m > f.dim))
+    return failf(VX_ERR_UNSUPPORTED, "quantized.bin PQ subspaces differ from computeSubspaceSizesAndOffsets");
+  if (f.kind != kSq8 && f.kind != kSq4 && f.kind != kBq && f.kind != kFp16 && f.kind != kPq)
+    return failf(VX_ERR_UNSUPPORTED,
+                 "quantized.bin kind %s is not served here (SQ8, SQ4, BQ SIGN_BIT and BBQ, FP16 and PQ are)",
                  kKindNames[f.kind]);
   return VX_OK;
 }
@@ -336,6 +382,16 @@ int vx_quantized_bin_build(int32_t device, const uint8_t* bytes, int64_t len, in
     if (int s = unsupported_kind(f)) return s;
     const uint8_t* data = bytes + f.data;
     const size_t n = (size_t)f.count, d = (size_t)f.dim;
+    if (f.kind == kPq) {
+      // little-endian floats, as the host; codes [count][numSubspaces] follow the codebooks
+      std::vector<float> gc;
+      if (f.pq_gc) {
+        gc.resize(d);
+        std::memcpy(gc.data(), bytes + f.pq_gc, d * 4);
+      }
+      return vx_pq_build(device, f.pq_codebooks.data(), f.pq_gc ? gc.data() : nullptr, n ? data : nullptr,
+                         (int64_t)n, f.dim, f.pq_m, f.pq_ks, metric, vectors, row_stride, out);
+    }
     if (f.kind == kSq8) {
       // records are (codes[dim], correction): split into the two arrays vx_sq8_build takes
       std::vector<int8_t> codes(n * d);

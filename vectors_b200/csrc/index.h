@@ -55,6 +55,8 @@ struct vx_index {
   int64_t* cb_off = nullptr;
   int32_t* sub = nullptr;
   int nprobe = 1, rescore = 1;
+  // PQ as a flat quantizer: each row's sum of centroidNormSq over its codes (COSINE)
+  float* pq_rnorm = nullptr;
   // BuoyIndex state (IVF-PQ and IVF-flat): cluster radii (the EUCLIDEAN early exit of the flat
   // list scan), SOAR spill targets (null: none) and the adapter's search-time gamma
   float* radii = nullptr;

@@ -414,6 +414,26 @@ struct WarpStream {
   }
 };
 
+// PQVectors' score of a row from its ADC sum (PQVectors.java:113-191): DOT_PRODUCT
+// max((1 + sum) / 2, 0); EUCLIDEAN 1 / (1 + sum); MAXIMUM_INNER_PRODUCT
+// scaleMaxInnerProductScore(sum); COSINE sum / (|q - gc| * (float) sqrt(vsq)) -> max((1 + cos) / 2, 0),
+// 0 when either norm is 0.  No fused multiply-add, as in Java.
+__device__ __forceinline__ float pq_flat_score(int metric, float sum, float qn, float vsq) {
+  float h;
+  switch (metric) {
+    case kEuclidean: return __fdiv_rn(1.0f, __fadd_rn(1.0f, sum));
+    case kMaxInnerProduct: return scale_mip(sum);
+    case kCosine: {
+      const float vn = (float)sqrt((double)vsq);
+      if (qn == 0.0f || vn == 0.0f) return 0.0f;
+      h = __fdiv_rn(__fadd_rn(1.0f, __fdiv_rn(sum, __fmul_rn(qn, vn))), 2.0f);
+      break;
+    }
+    default: h = __fdiv_rn(__fadd_rn(1.0f, sum), 2.0f); break;
+  }
+  return h >= 0.0f ? h : (h != h ? h : 0.0f);  // Math.max(h, 0f)
+}
+
 template <int R>
 __global__ void __launch_bounds__(256) adc_scan_kernel(AdcArgs a) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
@@ -439,7 +459,10 @@ __global__ void __launch_bounds__(256) adc_scan_kernel(AdcArgs a) {
     const float* c = a.cent + (size_t)l * a.dim;
     const bool l2 = a.metric == kEuclidean;
     __syncthreads();  // previous pair fully consumed the shared buffers
-    for (int i = threadIdx.x; i < a.dim; i += blockDim.x) s_res[i] = l2 ? __fsub_rn(qv[i], c[i]) : qv[i];
+    // IVF residual q - c for EUCLIDEAN (IvfIndex.java:570); PQ as a flat quantizer centres the
+    // query on the global centroid for every metric (buildADCTable's subInPlace)
+    for (int i = threadIdx.x; i < a.dim; i += blockDim.x)
+      s_res[i] = (l2 || a.pq_flat) ? __fsub_rn(qv[i], c[i]) : qv[i];
     if (warp == 0) {
       float base = 0.0f;
       if (!l2 && a.metric != kCosine) base = warp_dot(RowF32{qv}, RowF32{c}, a.dim);
@@ -475,7 +498,9 @@ __global__ void __launch_bounds__(256) adc_scan_kernel(AdcArgs a) {
           }
         }
         for (; m < a.M; m++) sum = __fadd_rn(sum, s_lut[m * a.Ks + code[m]]);
-        const float score = l2 ? -sum : __fadd_rn(base, sum);
+        const float score = a.pq_flat ? pq_flat_score(a.metric, sum, a.qnorm ? a.qnorm[q] : 0.0f,
+                                                      a.rnorm ? a.rnorm[r] : 0.0f)
+                                      : (l2 ? -sum : __fadd_rn(base, sum));
         key = float_key(score, (uint32_t)a.ordinals[r]);
       }
       ws.offer32(key, valid, C, a.K);
@@ -594,6 +619,7 @@ __global__ void __launch_bounds__(kAdcThreads, 2) adc_group_kernel(AdcArgs a) {
   __shared__ uint32_t s_wcnt[kAdcWarps][kAdcGroupQ];
   __shared__ int s_q[kAdcGroupQ], s_p[kAdcGroupQ];
   __shared__ float s_base[kAdcGroupQ];
+  __shared__ float s_qn[kAdcGroupQ];
   __shared__ uint64_t s_floor[kAdcGroupQ];
   __shared__ int s_gi;
   const int ng = a.ngroups[0];
@@ -619,6 +645,7 @@ __global__ void __launch_bounds__(kAdcThreads, 2) adc_group_kernel(AdcArgs a) {
       s_q[g] = q;
       s_p[g] = p;
       s_floor[g] = f;
+      s_qn[g] = (g < npq && a.qnorm) ? a.qnorm[q] : 0.0f;
     }
     __syncthreads();
     const int l = a.lists[(size_t)s_q[0] * a.nprobe + s_p[0]];
@@ -628,7 +655,8 @@ __global__ void __launch_bounds__(kAdcThreads, 2) adc_group_kernel(AdcArgs a) {
       float v = 0.0f;
       if (g < npq) {
         const float qv = a.queries[(size_t)s_q[g] * a.dim + d];
-        v = kDot ? qv : __fsub_rn(qv, c[d]);  // IvfIndex.java:570 residual
+        // IvfIndex.java:570 residual; PQ as a flat quantizer: the query minus the global centroid
+        v = (kDot && !a.pq_flat) ? qv : __fsub_rn(qv, c[d]);
       }
       s_res[i] = v;
     }
@@ -689,9 +717,11 @@ __global__ void __launch_bounds__(kAdcThreads, 2) adc_group_kernel(AdcArgs a) {
         const int64_t r = pass0 + threadIdx.x + (int64_t)kAdcThreads * j;
         const bool in = r < e;
         const uint32_t ord = in ? (uint32_t)a.ordinals[r] : 0u;
+        const float vsq = (in && a.rnorm) ? a.rnorm[r] : 0.0f;
 #pragma unroll
         for (int g = 0; g < kAdcGroupQ; g++) {
-          const float score = kDot ? __fadd_rn(s_base[g], ps[j][g]) : -ps[j][g];
+          const float score = a.pq_flat ? pq_flat_score(a.metric, ps[j][g], s_qn[g], vsq)
+                                        : (kDot ? __fadd_rn(s_base[g], ps[j][g]) : -ps[j][g]);
           const uint64_t key = float_key(score, ord);
           const bool pass = in && g < npq && key > wthr[g];
           const unsigned mk = __ballot_sync(0xFFFFFFFFu, pass);
@@ -1111,6 +1141,47 @@ __global__ void list_radii_kernel(const float* __restrict__ rows, int64_t n, int
   atomicMax(reinterpret_cast<int*>(radii + lo), __float_as_int(r));
 }
 
+// |q - gc| per query: one thread, the sequential sum of squares of PQVectors.cosineScoreFunction
+// (PQVectors.java:148-155; gc = 0 without a global centroid).
+__global__ void pq_query_norms_kernel(const float* __restrict__ queries, int nq, int dim, const float* __restrict__ gc,
+                                      float* __restrict__ out) {
+  const int q = blockIdx.x * blockDim.x + threadIdx.x;
+  if (q >= nq) return;
+  const float* v = queries + (size_t)q * dim;
+  float s = 0.0f;
+  for (int d = 0; d < dim; d++) {
+    const float x = __fsub_rn(v[d], gc[d]);
+    s = __fadd_rn(s, __fmul_rn(x, x));
+  }
+  out[q] = (float)sqrt((double)s);
+}
+
+// PQVectors.precomputeCentroidNormsSq (PQVectors.java:73-89): one thread per (subspace, centroid).
+__global__ void pq_centroid_norms_kernel(int M, int Ks, const int32_t* __restrict__ sub,
+                                         const float* __restrict__ codebooks, const int64_t* __restrict__ cb_off,
+                                         float* __restrict__ cnorm) {
+  const int e = blockIdx.x * blockDim.x + threadIdx.x;
+  if (e >= M * Ks) return;
+  const int m = e / Ks, c = e - m * Ks;
+  const int size = sub[2 * m];
+  const float* cb = codebooks + cb_off[m] + (size_t)c * size;
+  float s = 0.0f;
+  for (int d = 0; d < size; d++) s = __fadd_rn(s, __fmul_rn(cb[d], cb[d]));
+  cnorm[e] = s;
+}
+
+// Per row: vecNormSq = sum over subspaces, in order, of centroidNormSq[m][code[m]]
+// (PQVectors.java:160-166); one thread per row.
+__global__ void pq_row_norms_kernel(const uint8_t* __restrict__ codes, int64_t n, int M, int Mp, int Ks,
+                                    const float* __restrict__ cnorm, float* __restrict__ out) {
+  const int64_t r = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (r >= n) return;
+  const uint8_t* code = codes + r * Mp;
+  float s = 0.0f;
+  for (int m = 0; m < M; m++) s = __fadd_rn(s, cnorm[(size_t)m * Ks + code[m]]);
+  out[r] = s;
+}
+
 // IvfIndex.search's EUCLIDEAN early exit (IvfIndex.java:190-205) over the per-(probe, query)
 // results of the list scan (each list's own best K, no floors shared across lists): one warp
 // per query walks its listed clusters in route order, keeping the K best keys seen (the
@@ -1205,6 +1276,23 @@ cudaError_t launch_list_radii(const float* rows, int64_t n, int dim, int Dp, con
   cudaError_t e = cudaMemsetAsync(radii, 0, sizeof(float) * nlist, st);
   if (e != cudaSuccess || n <= 0) return e;
   list_radii_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(rows, n, dim, Dp, list_off, nlist, cent, radii);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_pq_query_norms(const float* queries, int nq, int dim, const float* gc, float* out,
+                                  cudaStream_t st) {
+  if (nq <= 0) return cudaSuccess;
+  pq_query_norms_kernel<<<(nq + 127) / 128, 128, 0, st>>>(queries, nq, dim, gc, out);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_pq_row_norms(const uint8_t* codes, int64_t n, int M, int Mp, int Ks, const int32_t* sub,
+                                const float* codebooks, const int64_t* cb_off, float* cnorm_scratch, float* out,
+                                cudaStream_t st) {
+  pq_centroid_norms_kernel<<<(M * Ks + 255) / 256, 256, 0, st>>>(M, Ks, sub, codebooks, cb_off, cnorm_scratch);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess || n <= 0) return e;
+  pq_row_norms_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(codes, n, M, Mp, Ks, cnorm_scratch, out);
   return cudaGetLastError();
 }
 

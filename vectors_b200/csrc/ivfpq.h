@@ -27,6 +27,11 @@ struct AdcArgs {
   const int2* groups;            // (first pair slot, pairs) of up to 4 pairs sharing one list
   int32_t* ngroups;              // [0] device count of groups, [1] the group dispenser
   uint64_t* floor;               // [nq] per-query admission floor shared across lists (zeroed)
+  // PQ as a flat quantizer (PQVectors, one list holding every row): tables of (query - global
+  // centroid) for every metric, and PQVectors' score of the sum instead of IvfIndex's
+  int pq_flat = 0;
+  const float* qnorm = nullptr;  // [nq] |query - global centroid| (COSINE)
+  const float* rnorm = nullptr;  // [n] per list-ordered row: sum of centroidNormSq[m][code[m]] (COSINE)
 };
 
 cudaError_t launch_route(const float* queries, int nq, int dim, const float* cent, int nlist,
@@ -81,6 +86,15 @@ cudaError_t launch_pad_rows(const float* src, int64_t n, int dim, int64_t src_st
 cudaError_t launch_row_norms(const float* rows, int64_t n, int dim, int Dp, float* out, cudaStream_t st);
 // flat_tail_kernel then flat_list_kernel (2 launches)
 cudaError_t launch_flat_list(const FlatListArgs& a, int64_t pair_slots, int grid, cudaStream_t st);
+
+// PQVectors (PQVectors.java:62-89, 148-166): |q - gc| per query (sequential sum of squares,
+// (float) Math.sqrt), and per row the sequential sum over subspaces of the centroids' squared
+// norms (centroidNormSq, each a sequential sum of squares over the subspace).
+cudaError_t launch_pq_query_norms(const float* queries, int nq, int dim, const float* gc, float* out,
+                                  cudaStream_t st);
+cudaError_t launch_pq_row_norms(const uint8_t* codes, int64_t n, int M, int Mp, int Ks, const int32_t* sub,
+                                const float* codebooks, const int64_t* cb_off, float* cnorm_scratch, float* out,
+                                cudaStream_t st);
 
 // CentroidIndex.routeWithSpillDistances' SOAR additions: lists [nq][probes] (ascending) and the
 // routing distances [nq][nlist] -> out_lists / out_dist [nq][width] (primaries, then spill

@@ -1149,6 +1149,112 @@ vx_index* flat_view(vx_index* ix) {
   return ix->flat;
 }
 
+// PQ as a flat quantizer (QuantizedFlatScanAdapter over PQVectors): every query's one "list"
+// holds all rows; the ADC kernels build (query - global centroid) tables and score rows with
+// PQVectors' transforms; the K best keys per query, then either the reference scores
+// (candidates) or the exact fp32 re-score of the two-pass search.
+int search_pq_flat(vx_index* ix, const float* dq, int nq, int K, int k_out, bool rescore, int32_t* d_ids,
+                   float* d_scores, int32_t* d_counts, cudaStream_t st) {
+  const int dim = ix->dim;
+  const StreamGeom g = stream_geom(K, 32);
+  if (g.R < 0) return fail(VX_ERR_UNSUPPORTED, "k=%d is larger than this build supports", K);
+  const StreamGeom gg = stream_geom(K, std::max(32, K));  // group buffers hold >= 2K keys
+  const bool grouped = use_adc_group() && adc_group_supported(ix->M, ix->Ks, dim) && gg.R > 0 && gg.R <= 9;
+  const size_t per_q = (size_t)K * 8 + 64;
+  const int64_t qch = std::max<int64_t>(64, (int64_t)(scratch_budget() / per_q));
+  for (int q0 = 0; q0 < nq; q0 += (int)qch) {
+    const int qc = (int)std::min<int64_t>(qch, nq - q0);
+    Scratch T(st);
+    const float* dqc = dq + (size_t)q0 * dim;
+    int32_t* lists = T.alloc<int32_t>(qc);
+    int32_t* counts = T.alloc<int32_t>(1);
+    int32_t* offsets = T.alloc<int32_t>(2);
+    int32_t* cursor = T.alloc<int32_t>(1);
+    int32_t* pairs = T.alloc<int32_t>(qc);
+    float* qnorm = T.alloc<float>(qc);
+    uint64_t* out = T.alloc<uint64_t>((size_t)qc * K);
+    uint32_t* out_cnt = T.alloc<uint32_t>(qc);
+    uint64_t* keys = T.alloc<uint64_t>((size_t)qc * K);
+    uint32_t* kcnt = T.alloc<uint32_t>(qc);
+    VX_CUDA(cudaMemsetAsync(lists, 0, (size_t)qc * 4, st));  // every query probes list 0
+    VX_CUDA(cudaMemsetAsync(out_cnt, 0, (size_t)qc * 4, st));
+    if (ix->metric == VX_COSINE) VX_LAUNCH(1, launch_pq_query_norms(dqc, qc, dim, ix->cent, qnorm, st));
+    VX_LAUNCH(3, launch_group_pairs(lists, ix->list_off, qc, 1, counts, offsets, cursor, pairs, st));
+    AdcArgs a;
+    a.nq = qc;
+    a.dim = dim;
+    a.nprobe = 1;
+    a.metric = ix->metric;
+    a.M = ix->M;
+    a.Ks = ix->Ks;
+    a.Mp = ix->Mp;
+    a.K = K;
+    a.npairs = qc;
+    a.pairs = pairs;
+    a.pair_count = offsets + 1;
+    a.lists = lists;
+    a.queries = dqc;
+    a.cent = ix->cent;
+    a.list_off = ix->list_off;
+    a.ordinals = ix->ordinals;
+    a.codes = ix->pq_codes;
+    a.codebooks = ix->codebooks;
+    a.cb_off = ix->cb_off;
+    a.sub = ix->sub;
+    a.out = out;
+    a.out_cnt = out_cnt;
+    a.groups = nullptr;
+    a.ngroups = nullptr;
+    a.floor = nullptr;
+    a.pq_flat = 1;
+    a.qnorm = ix->metric == VX_COSINE ? qnorm : nullptr;
+    a.rnorm = ix->pq_rnorm;
+    const int grid = ix->num_sms * 2;
+    if (grouped) {
+      int2* groups = T.alloc<int2>((size_t)qc / kAdcGroupQ + 2);
+      int32_t* ngroups = T.alloc<int32_t>(2);
+      uint64_t* qfloor = T.alloc<uint64_t>(qc);
+      VX_CUDA(cudaMemsetAsync(qfloor, 0, (size_t)qc * 8, st));
+      VX_LAUNCH(1, launch_make_groups(counts, offsets, nullptr, 1, kAdcGroupQ, groups, ngroups, st));
+      a.groups = groups;
+      a.ngroups = ngroups;
+      a.floor = qfloor;
+      VX_TIMED(VX_PROF_ADC_SCAN, st, 1, launch_adc_group(a, gg.R, grid, st));
+    } else {
+      VX_TIMED(VX_PROF_ADC_SCAN, st, 1, launch_adc_scan(a, g.R, grid, st));
+    }
+    VX_TIMED(VX_PROF_MERGE, st, 1, launch_merge_streams(out, out_cnt, 1, qc, qc, K, K, keys, kcnt, st));
+    int32_t* oi = d_ids + (size_t)q0 * k_out;
+    float* os = d_scores + (size_t)q0 * k_out;
+    int32_t* oc = d_counts + q0;
+    if (!rescore) {
+      VX_LAUNCH(1, launch_finish_keys(keys, kcnt, qc, K, k_out, kFinishFloatKey, ix->metric, dim, oi, os, oc, st));
+    } else {
+      RescoreArgs r{};
+      r.nq = qc;
+      r.dim = dim;
+      r.k = k_out;
+      r.Kc = K;
+      r.flavor = kFlavorFlat;
+      r.metric = ix->metric;
+      r.queries = dqc;
+      r.rows = ix->rows32;
+      r.row_stride = dim;
+      r.cand = keys;
+      r.cand_cnt = kcnt;
+      r.check_margin = 0;
+      r.n_rows = ix->n;
+      r.out_ids = oi;
+      r.out_scores = os;
+      r.out_counts = oc;
+      r.nflag = T.alloc<int32_t>(1);
+      r.flag_list = T.alloc<int32_t>(qc);
+      VX_LAUNCH(1, launch_rescore(r, false, st));
+    }
+  }
+  return VX_OK;
+}
+
 // FP16 two-pass: candidates by the fp16 score function, then exact fp32 re-score.
 int search_fp16_two_pass(vx_index* ix, const float* dq, int nq, int ck, int k, int32_t* d_ids,
                          float* d_scores, int32_t* d_counts, cudaStream_t st) {
@@ -1215,7 +1321,8 @@ int search_batch_dev(vx_index* ix, const float* dq, int nq, int dim, int k, int 
     case VX_KIND_SQ8:
     case VX_KIND_SQ4:
     case VX_KIND_BQ:
-    case VX_KIND_BBQ: {
+    case VX_KIND_BBQ:
+    case VX_KIND_PQ: {
       if (!ix->rows32)
         return fail(VX_ERR_UNSUPPORTED,
                     "searchBatch on a quantized index needs the full-precision vectors at build; "
@@ -1233,6 +1340,11 @@ int search_batch_dev(vx_index* ix, const float* dq, int nq, int dim, int k, int 
       if (ix->kind == VX_KIND_FP16) {
         return run_k([&](int kq, int32_t* i, float* s, int32_t* c) {
           return search_fp16_two_pass(ix, dq, nq, (int)ck, kq, i, s, c, st);
+        });
+      }
+      if (ix->kind == VX_KIND_PQ) {
+        return run_k([&](int kq, int32_t* i, float* s, int32_t* c) {
+          return search_pq_flat(ix, dq, nq, (int)ck, kq, true, i, s, c, st);
         });
       }
       return run_k([&](int kq, int32_t* i, float* s, int32_t* c) {
@@ -1658,6 +1770,47 @@ int vx_ivfpq_build(int32_t device, const float* centroids, int32_t nlist, int32_
                                  codes, n, metric, vectors, dim, nprobe, rescore_factor, out);
 }
 
+int vx_pq_build(int32_t device, const float* codebooks, const float* global_centroid, const uint8_t* codes, int64_t n,
+                int32_t dim, int32_t m, int32_t ks, int32_t metric, const float* vectors, int64_t row_stride,
+                vx_index** out) {
+  return guarded([&]() -> int {
+    if (!out) return fail(VX_ERR_NULL_POINTER, "out must not be null");
+    *out = nullptr;
+    if (!codebooks) return fail(VX_ERR_NULL_POINTER, "codebooks must not be null");
+    if (n > 0 && !codes) return fail(VX_ERR_NULL_POINTER, "codes must not be null");
+    if (n < 0 || n > INT32_MAX || dim <= 0)
+      return fail(VX_ERR_INVALID_ARGUMENT, "bad PQ shape n=%lld dim=%d", (long long)n, dim);
+    if (vectors && row_stride < dim)
+      return fail(VX_ERR_INVALID_ARGUMENT, "row_stride %lld < dimension %d", (long long)row_stride, dim);
+    // one list holding every row in ordinal order; the list's "centroid" is the global
+    // centroid (or zeros), which the flat-PQ tables subtract from every query
+    std::vector<float> cent((size_t)dim, 0.0f);
+    if (global_centroid) VX_CUDA(cudaMemcpy(cent.data(), global_centroid, (size_t)dim * 4, cudaMemcpyDefault));
+    const int64_t offs[2] = {0, n};
+    std::vector<int32_t> ords((size_t)std::max<int64_t>(n, 1));
+    for (int64_t i = 0; i < n; i++) ords[(size_t)i] = (int32_t)i;
+    vx_index* ix = nullptr;
+    int st = vx::ivfpq_build_strided(device, cent.data(), 1, dim, offs, ords.data(), m, ks, codebooks, codes, n,
+                                     metric, vectors, vectors ? row_stride : dim, 1, 1, &ix);
+    if (st != VX_OK) return st;
+    ix->kind = VX_KIND_PQ;
+    try {
+      if (metric == VX_COSINE && n > 0) {
+        ix->pq_rnorm = dev_alloc<float>(ix, (size_t)n);
+        DevTemp<float> cnorm((size_t)m * ks);
+        VX_LAUNCH(2, launch_pq_row_norms(ix->pq_codes, n, ix->M, ix->Mp, ix->Ks, ix->sub, ix->codebooks, ix->cb_off,
+                                         cnorm.p, ix->pq_rnorm, 0));
+        VX_CUDA(cudaDeviceSynchronize());
+      }
+    } catch (...) {
+      free_index(ix);
+      throw;
+    }
+    *out = ix;
+    return VX_OK;
+  });
+}
+
 }  // extern "C"
 
 namespace vx {
@@ -1893,8 +2046,8 @@ int vx_search_batch(vx_index* ix, const float* queries, int32_t nq, int32_t dim,
 static int scan_candidates_dev(vx_index* ix, const float* dq, int nq, int dim, int k, int32_t* di,
                                float* ds, int32_t* dc, cudaStream_t st) {
   if (ix->kind != VX_KIND_SQ8 && ix->kind != VX_KIND_SQ4 && ix->kind != VX_KIND_BQ && ix->kind != VX_KIND_BBQ &&
-      ix->kind != VX_KIND_FP16)
-    return fail(VX_ERR_UNSUPPORTED, "candidate scans apply to SQ8, BQ and FP16 indexes");
+      ix->kind != VX_KIND_FP16 && ix->kind != VX_KIND_PQ)
+    return fail(VX_ERR_UNSUPPORTED, "candidate scans apply to SQ8, SQ4, BQ, BBQ, FP16 and PQ indexes");
   if (ix->n == 0) {
     fill_empty(nq, k, di, ds, dc, st);
     return VX_OK;
@@ -1909,6 +2062,7 @@ static int scan_candidates_dev(vx_index* ix, const float* dq, int nq, int dim, i
     ts = S.alloc<float>((size_t)nq * kk);
   }
   int rc = (ix->kind == VX_KIND_FP16) ? search_gemm_exact(ix, dq, nq, kk, ti, ts, dc, st)
+           : (ix->kind == VX_KIND_PQ) ? search_pq_flat(ix, dq, nq, kk, kk, false, ti, ts, dc, st)
                                       : search_quantized_scan(ix, dq, nq, kk, kk, false, ti, ts, dc, st);
   if (rc != VX_OK) return rc;
   if (kk < k) {

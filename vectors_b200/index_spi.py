@@ -411,6 +411,27 @@ class QuantizedFlatScanAdapter(IndexSpi):
                                     C.byref(self._h.ptr)))
         self._n, self._dim, self.metric, self.kind = n, dim, SimilarityFunction(metric), "BBQ"
 
+    def build_pq(self, codes, codebooks, m: int, ks: int, metric, global_centroid=None, vectors=None):
+        """PQVectors (PQVectors.java:40-191): codes [n][m] (uint8), codebooks concatenated per
+        subspace (computeSubspaceSizesAndOffsets' sizes; ks * dim floats), the quantizer's global
+        centroid or None."""
+        codes = np.ascontiguousarray(np.asarray(codes, dtype=np.uint8))
+        cb = np.ascontiguousarray(np.asarray(codebooks, dtype=np.float32)).reshape(-1)
+        if codes.ndim != 2 or codes.shape[1] != m:
+            raise IllegalArgumentException(f"codes must be [n][{m}]")
+        if cb.size % ks:
+            raise IllegalArgumentException("codebooks must hold ks * dim floats")
+        n, dim = codes.shape[0], cb.size // ks
+        gc = None if global_centroid is None else np.ascontiguousarray(np.asarray(global_centroid, dtype=np.float32))
+        if gc is not None and gc.shape != (dim,):
+            raise IllegalArgumentException(f"global_centroid must hold {dim} floats")
+        v = None if vectors is None else _as_matrix(vectors, "vectors")
+        _expect_rows(v, n, dim)
+        self._h.close()
+        _check(N.lib().vx_pq_build(self.device, _ptr(cb), _ptr(gc), _ptr(codes), n, dim, m, ks, int(metric), _ptr(v),
+                                   dim, C.byref(self._h.ptr)))
+        self._n, self._dim, self.metric, self.kind = n, dim, SimilarityFunction(metric), "PQ"
+
     def build_fp16(self, codes, metric, vectors=None):
         """codes: [n][dim] binary16 bit patterns (numpy uint16, or a CUDA float16 / int16 tensor,
         copied on the device)."""
@@ -434,7 +455,7 @@ class QuantizedFlatScanAdapter(IndexSpi):
 
     def load_quantized_bin(self, data, metric, vectors=None):
         """Opens a persistent quantized.bin (QuantizedVectorsCodec.decode) as this adapter's index:
-        SQ8, SQ4, BQ (SIGN_BIT or BBQ) or FP16.  ``vectors`` are the fp32 rows for the two-pass rescore (a mapped
+        SQ8, SQ4, BQ (SIGN_BIT or BBQ), FP16 or PQ.  ``vectors`` are the fp32 rows for the two-pass rescore (a mapped
         vectors.bin view with its 64-byte row stride is taken as is)."""
         b = _file_bytes(data)
         kind, dim, n = quantized_bin_info(b)
@@ -443,7 +464,7 @@ class QuantizedFlatScanAdapter(IndexSpi):
         _check(N.lib().vx_quantized_bin_build(self.device, _ptr(b), b.size, int(metric), _ptr(v), stride,
                                               C.byref(self._h.ptr)))
         self._n, self._dim, self.metric = n, dim, SimilarityFunction(metric)
-        self.kind = {1: "SQ8", 2: "SQ4", 4: "BQ", 8: "FP16"}[kind]
+        self.kind = {1: "SQ8", 2: "SQ4", 3: "PQ", 4: "BQ", 8: "FP16"}[kind]
         if kind == 4:  # SIGN_BIT or BBQ: the index knows
             built = C.c_int32()
             _check(N.lib().vx_index_info(self._h.ptr, C.byref(built), None, None, None))
