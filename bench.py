@@ -657,6 +657,10 @@ def run_ivf(args, rank, world, local, dev, barrier, max_over_ranks, hbm_peak, pe
     gather_bytes = pair_rows / 4.0 * m * 16.0 / world
     smem_peak = 148 * 128 * 1.965e9  # bytes/s: 148 SMs x 128 B/clk x max SM clock (nominal)
     smem_frac = (gather_bytes / smem_peak) / (adc_ms / 1e3) if adc_ms > 0 else None
+    # with codes drawn at random, a quarter-warp's eight 16-byte reads land on 2.54 of the
+    # eight 16-byte bank groups' worth of wavefronts on average (the expected largest number
+    # of distinct codes sharing a bank group), not 1: the gather roof the data allows
+    random_frac = smem_frac * 2.5408 if smem_frac else None
     par = cpu = e2e = None
     if rank == 0 and world == 1 and not args.no_cpu:
         from oracle import oracle as O
@@ -688,7 +692,11 @@ def run_ivf(args, rank, world, local, dev, barrier, max_over_ranks, hbm_peak, pe
                      "smem_gather_roof": {"frac": smem_frac, "gather_bytes_per_step": gather_bytes,
                                           "peak_bytes_per_s": smem_peak,
                                           "peak_source": "nominal: 148 SMs x 128 B/clk x 1.965 GHz",
-                                          "note": "conflict-free minimum of the 16-byte four-query table reads"}},
+                                          "note": "conflict-free minimum of the 16-byte four-query table reads",
+                                          "random_code_frac": random_frac,
+                                          "random_code_note": "the same roof with the expected bank conflicts of "
+                                                              "uniformly random codes (2.54 wavefronts per "
+                                                              "quarter-warp read instead of 1)"}},
         "parity": par,
         "cpu_baseline": cpu,
         "e2e": e2e,

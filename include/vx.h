@@ -103,6 +103,12 @@ VX_API int vx_profile_reset(void);
 /* Test hook: the next vx_* call on this host thread fails with `status` before touching the
  * GPU (host-side fault injection; status 0 clears it). */
 VX_API int vx_debug_fail_next(int32_t status);
+/* Test hook: one kernel whose only thread waits, with the scan pipeline's bounded wait, on a
+ * barrier that nothing completes; after timeout_ms (1..10000) the wait gives up, the kernel
+ * records the timeout and returns, and the call returns VX_ERR_DEVICE_TIMEOUT -- the status a
+ * scan returns when one of its waits runs out.  The context stays usable.  No counterpart in the
+ * reference. */
+VX_API int vx_debug_wait_timeout(int32_t device, int32_t timeout_ms);
 
 /* ---- index construction (the handle owns device copies; inputs are not retained) ----- */
 /* Input arrays of the build calls may be host or device memory (unified addressing), except
@@ -143,7 +149,8 @@ VX_API int vx_bq_build(int32_t device, const uint64_t* words, int64_t n, int32_t
  * centred and quantised to 4 bits, rawAsymDot exactly (the 4-bit codes times a 0/1 int8 copy of
  * the bits on the int8 tensor cores, 8 bytes of device memory per stored bit, within the
  * VX_BQ_TENSOR_BYTES budget; above it, popcounts of the query's 4 bit planes), computeBbqDot and
- * the metric's transform in the Java float order.  dim <= 1024. */
+ * the metric's transform in the Java float order.  dim <= 2048 (above 1024 the int8 operand must
+ * fit VX_BQ_TENSOR_BYTES). */
 VX_API int vx_bbq_build(int32_t device, const uint64_t* words, const float* corrections, const float* centroid,
                         int64_t n, int32_t dim, int32_t metric, const float* vectors, int64_t row_stride,
                         vx_index** out);
@@ -175,7 +182,7 @@ VX_API int vx_ivfpq_build(int32_t device, const float* centroids, int32_t nlist,
  * floats apart (host or device; a mapped vectors.bin with alignUp(dim*4, 64)/4).
  * vx_search_batch follows IvfFlatAdapter.search (searchListSize overrides nprobe,
  * overQueryFactor > 1 widens the probes); vx_ivfpq_search* run IvfIndex.search's flat list scan
- * (their rescore_factor is ignored: the scan is exact) for k <= 96. */
+ * (their rescore_factor is ignored: the scan is exact) for k <= 256. */
 VX_API int vx_ivfflat_build(int32_t device, const float* centroids, int32_t nlist, int32_t dim,
                             const int64_t* list_offsets, const int32_t* list_ordinals, const float* vectors,
                             int64_t n, int64_t row_stride, int32_t metric, int32_t nprobe, vx_index** out);

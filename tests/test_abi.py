@@ -158,10 +158,10 @@ def test_build_argument_statuses_before_the_gpu():
     f = np.zeros(64, np.float32)
     w = np.zeros(64, np.uint64)
     p = lambda a: a.ctypes.data_as(C.c_void_p)  # noqa: E731
-    # BBQ: centroid required; more than 1024 dimensions unsupported
+    # BBQ: centroid required; more than 2048 dimensions unsupported
     assert L.vx_bbq_build(0, p(w), p(f), None, 1, 64, 1, None, 64, C.byref(out)) == N.VX_ERR_NULL_POINTER
-    assert L.vx_bbq_build(0, p(w), p(f), p(f), 1, 2000, 1, None, 2000, C.byref(out)) == N.VX_ERR_UNSUPPORTED
-    assert "1024" in N.last_error()
+    assert L.vx_bbq_build(0, p(w), p(f), p(f), 1, 3000, 1, None, 3000, C.byref(out)) == N.VX_ERR_UNSUPPORTED
+    assert "2048" in N.last_error()
     assert L.vx_bbq_build(0, p(w), p(f), p(f), 1, 0, 1, None, 0, C.byref(out)) == N.VX_ERR_INVALID_ARGUMENT
     # SQ4: codes required for a non-empty index
     assert L.vx_sq4_build(0, None, p(f), 4, 8, -1.0, 1.0, 1, None, 8, C.byref(out)) == N.VX_ERR_NULL_POINTER

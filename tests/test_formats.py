@@ -75,9 +75,12 @@ def test_quantized_kinds_not_served():
     words = np.zeros((4, 1), np.uint64)
     assert vx.quantized_bin_info(F.quantized_bin_bq(words, 64, np.zeros(64, np.float32),
                                                     np.zeros((4, 3), np.float32))) == (F.BQ, 64, 4)
-    big = np.zeros((2, 17), np.uint64)  # BBQ beyond 1024 dimensions is refused
+    wide = np.zeros((2, 17), np.uint64)  # BBQ up to 2048 dimensions is served
+    assert vx.quantized_bin_info(F.quantized_bin_bq(wide, 1050, np.zeros(1050, np.float32),
+                                                    np.zeros((2, 3), np.float32))) == (F.BQ, 1050, 2)
+    big = np.zeros((2, 33), np.uint64)  # beyond 2048 dimensions it is refused
     with pytest.raises(vx.UnsupportedOperationException, match="BBQ"):
-        vx.quantized_bin_info(F.quantized_bin_bq(big, 1050, np.zeros(1050, np.float32), np.zeros((2, 3), np.float32)))
+        vx.quantized_bin_info(F.quantized_bin_bq(big, 2100, np.zeros(2100, np.float32), np.zeros((2, 3), np.float32)))
     # a PQ payload cut after the header: decodePQ's first ensureRemaining
     pq = struct.pack("<iiiii", F.MAGIC_QUANTIZED, 1, F.PQ, 16, 3)
     with pytest.raises(vx.IOException, match="PQ quantizer state header"):

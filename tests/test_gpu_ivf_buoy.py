@@ -198,3 +198,23 @@ def test_graph_bin_carries_radii_and_spill_targets(oracle):
 def test_negative_gamma_is_rejected():
     with pytest.raises(vx.IllegalArgumentException, match="gamma"):
         vx.IvfPqAdapter(nprobe=4, gamma=-0.1)
+
+
+@pytest.mark.parametrize("metric", [0, 1])
+def test_ivfflat_large_k_with_early_exit(oracle, metric):
+    # k up to 256 per (query, list) on the list scan's widest candidate buffers
+    n, dim, nlist = 12000, 64, 16
+    db = oracle.gen_mixture(n, dim, 12, 0.3, SEED_C, SEED_DB, False)
+    q = oracle.gen_mixture(100, dim, 12, 0.3, SEED_C, SEED_Q, False)
+    cent = oracle.kmeans_train(db[:3000], nlist, 8, 42)
+    off, ords = oracle.build_ivf_lists(oracle.kmeans_assign(db, cent), nlist)
+    radii = (oracle.ivf_radii(cent, off, ords, db) * np.float32(0.6)).astype(np.float32)
+    a = vx.IvfFlatAdapter(nprobe=6)
+    a.build_prebuilt(cent, off, ords, db, vx.SimilarityFunction(metric))
+    a.set_buoy(radii=radii)
+    for k in (150, 256):
+        _same(a.ivf_search(q, k, 6), *oracle.ivfflat_search_full(cent, off, ords, db, radii, q, metric, k, 6),
+              f"ivfflat k={k} m={metric}")
+    with pytest.raises(vx.UnsupportedOperationException):
+        a.ivf_search(q, 257, 6)
+    a.close()

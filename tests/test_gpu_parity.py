@@ -322,7 +322,7 @@ def test_sq4_bit_exact(oracle, metric, n, dim, nq, k):
 # ------------------------------------------------------------------ BBQ
 @pytest.mark.parametrize("metric", [0, 1, 2, 3])
 @pytest.mark.parametrize("n,dim,nq,k", [(6000, 768, 40, 100), (2500, 100, 65, 10), (1000, 1024, 20, 5),
-                                        (90000, 256, 300, 100)])
+                                        (90000, 256, 300, 100), (3000, 1536, 30, 10), (2000, 2048, 20, 10)])
 def test_bbq_bit_exact(oracle, metric, n, dim, nq, k):
     # BinaryQuantizedVectors BBQ: 4-bit query codes against centroid-relative sign bits, the
     # exact asymmetric dot (int8 tensor cores), computeBbqDot and the metric transform in Java's

@@ -36,6 +36,7 @@ SIGNATURES = {
     "vx_device_count": [_P],
     "vx_kernel_launches": [_P],
     "vx_debug_fail_next": [_I32],
+    "vx_debug_wait_timeout": [_I32, _I32],
     "vx_profile_enable": [_I32],
     "vx_profile_read": [_I32, _P, _P],
     "vx_profile_reset": [],

@@ -201,8 +201,8 @@ int parse_quantized(const uint8_t* bytes, int64_t len, QuantizedFile& f) {
 }
 
 int unsupported_kind(const QuantizedFile& f) {
-  if (f.kind == kBq && f.bq_mode == 1 && f.dim > 1024)
-    return failf(VX_ERR_UNSUPPORTED, "quantized.bin BQ in BBQ mode is served up to 1024 dimensions, not %d", f.dim);
+  if (f.kind == kBq && f.bq_mode == 1 && f.dim > 2048)
+    return failf(VX_ERR_UNSUPPORTED, "quantized.bin BQ in BBQ mode is served up to 2048 dimensions, not %d", f.dim);
   if (f.kind == kPq && (!f.pq_standard || f.pq_m > f.dim))
     return failf(VX_ERR_UNSUPPORTED, "quantized.bin PQ subspaces differ from computeSubspaceSizesAndOffsets");
   if (f.kind != kSq8 && f.kind != kSq4 && f.kind != kBq && f.kind != kFp16 && f.kind != kPq)

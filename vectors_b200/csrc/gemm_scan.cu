@@ -663,7 +663,31 @@ cudaError_t launch_variant(int mode, const CUtensorMap& tmA, const CUtensorMap& 
   }
 }
 
+// The pipeline's bounded wait with nothing to wait for: one thread waits on an mbarrier that no
+// thread arrives on, gives up after timeout_ns (mbar_wait), records kDevWaitTimeout and the
+// kernel returns -- the give-up path of the scan's waits without the scan around it.
+__global__ void wait_probe_kernel(uint64_t timeout_ns, int32_t* err) {
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    abort_flag = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0 && !mbar_wait(&bar, 0, timeout_ns, &abort_flag)) {
+    abort_flag = 1;
+    record_error(err, kDevWaitTimeout);
+  }
+  __syncthreads();
+}
+
 }  // namespace
+
+cudaError_t launch_wait_probe(uint64_t timeout_ns, int32_t* err, cudaStream_t st) {
+  wait_probe_kernel<<<1, 32, 0, st>>>(timeout_ns, err);
+  return cudaGetLastError();
+}
 
 int gemm_scan_units(int64_t ntiles, int num_mblocks, int num_sms, bool two_sm) {
   const int64_t total = ntiles * (int64_t)num_mblocks;

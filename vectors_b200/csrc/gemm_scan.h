@@ -77,6 +77,8 @@ constexpr int gemm_scan_query_block(bool two_sm) { return two_sm ? 256 : 128; }
 constexpr int gemm_scan_db_box(bool two_sm) { return two_sm ? 128 : 256; }
 int gemm_scan_units(int64_t ntiles, int num_mblocks, int num_sms, bool two_sm);
 int gemm_scan_stream_R(int K);
+// One bounded wait that nothing completes (the scan's give-up path alone): err gets kDevWaitTimeout.
+cudaError_t launch_wait_probe(uint64_t timeout_ns, int32_t* err, cudaStream_t st);
 cudaError_t launch_gemm_scan(int mode, const CUtensorMap& tmA, const CUtensorMap& tmB,
                              const ScanArgs& a, int units, int R, bool two_sm, cudaStream_t st);
 

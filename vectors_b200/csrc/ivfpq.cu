@@ -1191,7 +1191,7 @@ __global__ void pq_row_norms_kernel(const uint8_t* __restrict__ codes, int64_t n
 // minScore test comes before heap.offer).  Other metrics (no early exit): every listed cluster
 // is merged.  The kept keys are written sorted descending.
 constexpr int kExitWarps = 8;
-constexpr int kExitR = 8;  // 256 key slots per warp >= 2 K (K <= 128)
+constexpr int kExitR = 16;  // 512 key slots per warp >= 2 K (K <= 256)
 
 __global__ void __launch_bounds__(kExitWarps * 32) ivf_early_exit_kernel(
     const uint64_t* __restrict__ out, const uint32_t* __restrict__ out_cnt, int nq, int width, int K,
@@ -1437,7 +1437,7 @@ cudaError_t launch_make_groups(const int32_t* counts, const int32_t* offsets, co
   return cudaGetLastError();
 }
 
-bool flat_list_supported(int K) { return K >= 1 && K <= 4 * 32 - kRtC; }
+bool flat_list_supported(int K) { return K >= 1 && K <= 9 * 32 - kRtC; }
 
 cudaError_t launch_pad_rows(const float* src, int64_t n, int dim, int64_t src_stride, const int32_t* map, int Dp,
                             float* dst, cudaStream_t st) {
@@ -1463,10 +1463,12 @@ cudaError_t launch_flat_list(const FlatListArgs& a, int64_t pair_slots, int grid
   else flat_tail_kernel<false><<<tgrid, 256, 0, st>>>(a);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  const int R = a.K <= 2 * 32 - kRtC ? 2 : 4;
+  // key slots per query 32 R >= K + one tile's 32; R = 9 (K up to 256) takes ~200 KB of shared
+  // memory, one CTA per SM
+  const int R = a.K <= 2 * 32 - kRtC ? 2 : a.K <= 4 * 32 - kRtC ? 4 : 9;
   const size_t smem = (size_t)2 * (kRtQ + kRtC) * kRtStride * sizeof(float) + (size_t)kFlGroup * 32 * R * 8;
-  auto kern = l2 ? (R == 2 ? flat_list_kernel<true, 2> : flat_list_kernel<true, 4>)
-                 : (R == 2 ? flat_list_kernel<false, 2> : flat_list_kernel<false, 4>);
+  auto kern = l2 ? (R == 2 ? flat_list_kernel<true, 2> : R == 4 ? flat_list_kernel<true, 4> : flat_list_kernel<true, 9>)
+                 : (R == 2 ? flat_list_kernel<false, 2> : R == 4 ? flat_list_kernel<false, 4> : flat_list_kernel<false, 9>);
   e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   kern<<<grid, 256, smem, st>>>(a);

@@ -79,7 +79,7 @@ struct FlatListArgs {
                               // (query, list) keeps its own best K (the early exit's input)
 };
 constexpr int kFlatGroup = 64;
-// Keys kept per (query, list) that the scan supports: K <= 96.
+// Keys kept per (query, list) that the scan supports: K <= 256.
 bool flat_list_supported(int K);
 cudaError_t launch_pad_rows(const float* src, int64_t n, int dim, int64_t src_stride, const int32_t* map, int Dp,
                             float* dst, cudaStream_t st);

@@ -853,7 +853,7 @@ int search_ivfflat(vx_index* ix, const float* dq, int nq, int k, int heap_k, int
   const int dim = ix->dim, Dp = ix->Dp_flat;
   const int probes = std::min(nprobe, ix->nlist);
   const int K = (int)std::max<int64_t>(1, std::min<int64_t>(std::max(k, heap_k), ix->n));
-  if (!flat_list_supported(K)) return fail(VX_ERR_UNSUPPORTED, "k = %d is larger than the IVF-flat scan keeps (96)", K);
+  if (!flat_list_supported(K)) return fail(VX_ERR_UNSUPPORTED, "k = %d is larger than the IVF-flat scan keeps (256)", K);
   // Routed here (not given): SOAR spill targets widen each query's list to 2 * probes slots,
   // and EUCLIDEAN takes the reference's early exit over the per-list results in route order.
   const bool spill = !given_lists && ix->spill && ix->gamma > 0.0f;
@@ -1418,6 +1418,21 @@ int vx_debug_fail_next(int32_t status) {
   return VX_OK;
 }
 
+int vx_debug_wait_timeout(int32_t device, int32_t timeout_ms) {
+  return guarded([&]() -> int {
+    if (timeout_ms < 1 || timeout_ms > 10000)
+      return fail(VX_ERR_INVALID_ARGUMENT, "timeout_ms must be in [1, 10000]: %d", timeout_ms);
+    int nsms = 0;
+    if (int s = check_device(device, &nsms)) return s;
+    cudaStream_t st = cudaStreamPerThread;
+    Scratch S(st);
+    int32_t* d_err = S.alloc<int32_t>(1);
+    VX_CUDA(cudaMemsetAsync(d_err, 0, 4, st));
+    VX_LAUNCH(1, launch_wait_probe((uint64_t)timeout_ms * 1000000ull, d_err, st));
+    return check_device_error(d_err, st);
+  });
+}
+
 int vx_kernel_launches(int64_t* count) {
   if (!count) return fail(VX_ERR_NULL_POINTER, "count must not be null");
   *count = g_launches.load();
@@ -1660,7 +1675,13 @@ int vx_bbq_build(int32_t device, const uint64_t* words, const float* corrections
     if (dim <= 0) return fail(VX_ERR_INVALID_ARGUMENT, "bad dimension %d", dim);
     const int nw = (dim + 63) / 64;
     const int nwp = bq_padded_words(nw);
-    if (nwp < 0 || !bbq_supported(nwp)) return fail(VX_ERR_UNSUPPORTED, "BBQ dimension %d exceeds 1024", dim);
+    if (nwp < 0) return fail(VX_ERR_UNSUPPORTED, "BBQ dimension %d exceeds 2048", dim);
+    // above 1024 dimensions only the int8 tensor operand serves BBQ (the popcount kernel keeps a
+    // query's four bit planes in registers, up to 16 words each)
+    if (!bbq_supported(nwp) && n > 0 && bq_tensor_budget() < (uint64_t)n * (uint64_t)round_up(dim, 128))
+      return fail(VX_ERR_UNSUPPORTED,
+                  "BBQ above 1024 dimensions is scanned on the int8 tensor operand, which exceeds "
+                  "VX_BQ_TENSOR_BYTES here (%lld rows x %d dims)", (long long)n, dim);
     if (vectors && row_stride < dim) return fail(VX_ERR_INVALID_ARGUMENT, "bad row stride");
     if (int s = check_metric(metric)) return s;
     int nsms = 0;
