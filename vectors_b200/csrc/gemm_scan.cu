@@ -131,6 +131,7 @@ struct TileStream {
   float tf;     // score of the admission threshold
   uint64_t t1;  // best admitted key
   uint64_t t2;  // second best admitted key
+  bool dirty;   // keys were appended or the buffer compacted: the state goes back to memory
 };
 
 // Slow path of one 32-column group, taken when some lane of the warp may admit a column:
@@ -152,7 +153,9 @@ __device__ __forceinline__ void offer_group(const ScanArgs& a, TileStream& ts, i
 #pragma unroll
     for (int i = 0; i < 8; i++) d[i] = make_uint4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
   }
+  ts.dirty |= pm != 0;
   const bool need = ts.st.cnt + (uint32_t)__popc(pm) > (uint32_t)a.C;
+  ts.dirty |= need;
   if (__any_sync(0xFFFFFFFFu, need)) {
     warp_compact_lanes<R>(need, ts.st.base, ts.st.cnt, ts.st.thr, (uint32_t)a.K);
     if (need && a.floor && ts.st.cnt == (uint32_t)a.K)
@@ -457,6 +460,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     float* s_col2 = s_col + 256;
     uint32_t* stage_row = stage_rows + (warp - 2) * (32 * kStageRowWords) + lane * kStageRowWords;
     const int64_t nt_first = p0 / a.num_mblocks;  // first row tile of this unit (row-major dealing)
+    int64_t cols_nt = -1;                         // row tile whose column data s_col holds
     int64_t t = 0;
     for (int64_t p = p0; p < p1; p++, t++) {
       int64_t nt;
@@ -465,7 +469,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const int acc = (int)(t & 1);
       const uint32_t acc_phase = (uint32_t)((t >> 1) & 1);
       const int64_t col0 = nt * BN;
-      if (kMode != kEpiF16Plain && kMode != kEpiBqHamming) {
+      // per-row column data: loaded when the row tile changes (a unit takes every query block
+      // of a row tile in turn)
+      if (kMode != kEpiF16Plain && kMode != kEpiBqHamming && nt != cols_nt) {
+        cols_nt = nt;
         __syncwarp();
         for (int i = lane; i < BN; i += 32) {
           const int64_t row = col0 + i;
@@ -499,6 +506,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       ts.st.thr = live ? a.thrs[sidx] : ~0ull;
       ts.t1 = (a.top1 && live) ? a.top1[sidx] : 0ull;
       ts.t2 = (a.top1 && live) ? a.top2[sidx] : 0ull;
+      ts.dirty = false;
       apply_floor(a, q, live, ts.st.thr);
       float qa = 0.0f;
       int32_t qi = 0;
@@ -527,21 +535,33 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const int64_t left = a.n - col0;
       const int valid = left < BN ? (int)left : BN;
       const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * BN);
-#pragma unroll 1
-      for (int g = 0; g < BN / 32; g++) {
+      // 32-column groups up to the last row (tile-uniform); the TMEM load of the next group is
+      // in flight while the current one is processed
+      const int ngroups = (valid + 31) / 32 < BN / 32 ? (valid + 31) / 32 : BN / 32;
+      auto process = [&](const uint32_t(&v)[32], int g) {
         const int c0 = g * 32;
-        if (c0 >= valid) break;  // groups past the last row (tile-uniform)
-        uint32_t v[32];
-        __syncwarp();
-        tmem_ld_32x32b_x32(taddr + (uint32_t)(g * 32), v);
-        tmem_ld_wait();
         const float m = group_max<kMode>(v, c0, s_col, s_col2, qa, qi, a.epi, qb);
         if (probe) {  // exact group maxima: the floor needs scores that rows reach
           if (active) a.probe[(size_t)q * a.probe_groups + (size_t)((col0 + c0) >> 5)] = m;
-          continue;
+          return;
         }
         if (__any_sync(0xFFFFFFFFu, m >= ts.tf))
           offer_group<kMode, R>(a, ts, q, active, v, c0, valid - c0, col0, s_col, s_col2, qa, qi, qb, stage_row);
+      };
+      uint32_t va[32], vb[32];
+      __syncwarp();
+      if (ngroups > 0) tmem_ld_32x32b_x32(taddr, va);
+#pragma unroll 1
+      for (int g = 0; g < ngroups; g += 2) {
+        __syncwarp();
+        tmem_ld_wait_v(va);
+        if (g + 1 < ngroups) tmem_ld_32x32b_x32(taddr + (uint32_t)((g + 1) * 32), vb);
+        process(va, g);
+        if (g + 1 >= ngroups) break;
+        __syncwarp();
+        tmem_ld_wait_v(vb);
+        if (g + 2 < ngroups) tmem_ld_32x32b_x32(taddr + (uint32_t)((g + 2) * 32), va);
+        process(vb, g + 1);
       }
       tc_fence_before();
       __syncwarp();
@@ -551,8 +571,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         else
           mbar_arrive(&tempty[acc]);
       }
-      if (live) {
-        a.cnts[sidx] = ts.st.cnt;
+      if (live && ts.dirty) {  // a threshold raised only by the shared floor is not stored: the
+        a.cnts[sidx] = ts.st.cnt;  // floor is applied again on the next load
         a.thrs[sidx] = ts.st.thr;
         if (a.top1) {
           a.top1[sidx] = ts.t1;
