@@ -35,6 +35,7 @@ FLAT = dict(n=10_000_000, dim=768, comps=64, sigma=0.3, nq=10_000, k=10, metric=
 IVF = dict(n=10_000_000, dim=768, comps=1024, sigma=0.3, nq=10_000, k=10, nlist=4096, m=96, ks=256,
            nprobe=32, train=500_000, pq_train=25_000)
 SEED_DB, SEED_Q, SEED_C = 0xC0FFEE01, 0xC0FFEE02, 0xC0FFEE03
+FLAT_TRAFFIC_FIXED, FLAT_TRAFFIC_PER_ROW = 2.03e9, 3024.0  # bytes per scan launch (measured, 10k queries)
 METRIC = "queries/sec, 10M x 768 FLAT COSINE top-10"
 CHUNK = 65536
 
@@ -430,11 +431,12 @@ def main():
         "breakdown_ms_per_step": {kk: v[0] / args.steps for kk, v in prof.items() if v[1]},
         "per_rank": per_rank,
     }
-    traffic_path = os.path.join(ROOT, "profiles", "flat_gemm_scan_traffic.json")
-    if os.path.exists(traffic_path):
-        with open(traffic_path) as f:
-            tr = json.load(f)
-        roofline["traffic"] = tr.get("bytes_per_launch_full_size")
+    # DRAM bytes of one scan launch: ncu's dram__bytes_read.sum + dram__bytes_write.sum at 600k and
+    # 2.4M rows (10k queries) fit 2.03 GB + 3,024 B per row; scaled to this rank's rows
+    roofline["traffic"] = FLAT_TRAFFIC_FIXED + FLAT_TRAFFIC_PER_ROW * (hi - lo)
+    roofline["traffic_source"] = ("ncu DRAM bytes of the scan at 600k and 2.4M rows, linear fit scaled to "
+                                  "this rank's rows")
+    roofline["algorithmic_bytes"] = 2.0 * (hi - lo) * dim + 2.0 * nq * dim
 
     # ---- end to end through the host-buffer C ABI (queries in, results out every step)
     q_np = q_pinned.numpy()

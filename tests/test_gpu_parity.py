@@ -537,3 +537,34 @@ def test_concurrent_searches_equal_serial(oracle):
             _same_outcomes(results[rep][j], serial[j], f"concurrent rep {rep} call {j}")
     f.close()
     s.close()
+
+
+# ------------------------------------------------------------------ wide candidate windows
+@pytest.mark.parametrize("kind", ["sq8", "bq", "bbq"])
+def test_candidate_windows_wider_than_one_stream(oracle, kind):
+    # more candidates per query than one stream keeps (1,023) are taken in passes below the
+    # previous pass's smallest key: k = 300 at overQueryFactor 4 (1,200 candidates, two passes)
+    # and a 2,100-candidate scan (three passes), against the oracle
+    n, dim = 30000, 128 if kind == "sq8" else 256
+    db, q = _data(oracle, n, dim, 20, normalize=kind != "bq")
+    a = vx.QuantizedFlatScanAdapter()
+    if kind == "sq8":
+        lo, hi = oracle.sq8_train(db)
+        codes, corr = oracle.sq8_encode_all(lo, hi, db)
+        a.build_sq8(codes, corr, lo, hi, vx.SimilarityFunction.DOT_PRODUCT, vectors=db)
+        scan = lambda kk: oracle.sq8_search(codes, corr, lo, hi, q, oracle.DOT_PRODUCT, kk)  # noqa: E731
+    elif kind == "bq":
+        words = oracle.bq_encode_all(db)
+        a.build_bq(words, dim, vx.SimilarityFunction.DOT_PRODUCT, vectors=db)
+        scan = lambda kk: oracle.bq_search(words, dim, q, oracle.DOT_PRODUCT, kk)  # noqa: E731
+    else:
+        cent = db.mean(0).astype(np.float32)
+        words, corr = oracle.bbq_encode_all(db, cent)
+        a.build_bbq(words, corr, cent, dim, vx.SimilarityFunction.DOT_PRODUCT, vectors=db)
+        scan = lambda kk: oracle.bbq_search(words, corr, cent, dim, q, oracle.DOT_PRODUCT, kk)  # noqa: E731
+    got = a.scan_candidates(q, 2100)
+    _check_float(got, *scan(2100), f"{kind} 2100 candidates", exact_scores=True)
+    two = a.search_batch(q, 300, 0, 4.0)
+    ci, cs, cc = scan(oracle.candidate_k(300, 4.0))
+    _check_float(two, *oracle.rescore_candidates(db, q, oracle.DOT_PRODUCT, ci, cc, 300), f"{kind} k=300 oqf=4")
+    a.close()

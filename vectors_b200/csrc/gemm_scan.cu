@@ -132,6 +132,7 @@ struct TileStream {
   uint64_t t1;  // best admitted key
   uint64_t t2;  // second best admitted key
   bool dirty;   // keys were appended or the buffer compacted: the state goes back to memory
+  uint64_t ceil;  // keys >= ceil are not admitted (~0: no bound)
 };
 
 // Slow path of one 32-column group, taken when some lane of the warp may admit a column:
@@ -169,7 +170,7 @@ __device__ __forceinline__ void offer_group(const ScanArgs& a, TileStream& ts, i
     const int col = c0 + j;
     const float sc = score_of<kMode>(stage_row[j], col, s_col, s_col2, qa, qi, a.epi.cm, qb);
     const uint64_t key = float_key(sc, (uint32_t)(col0 + col));
-    if (key > ts.st.thr) {
+    if (key > ts.st.thr && key < ts.ceil) {
       ts.st.base[ts.st.cnt++] = key;
       if (key > ts.t1) {
         ts.t2 = ts.t1;
@@ -507,6 +508,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       ts.t1 = (a.top1 && live) ? a.top1[sidx] : 0ull;
       ts.t2 = (a.top1 && live) ? a.top2[sidx] : 0ull;
       ts.dirty = false;
+      ts.ceil = (a.ceil && live) ? a.ceil[q] : ~0ull;
       apply_floor(a, q, live, ts.st.thr);
       float qa = 0.0f;
       int32_t qi = 0;

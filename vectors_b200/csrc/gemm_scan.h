@@ -65,6 +65,10 @@ struct ScanArgs {
   // group to probe[q][row / 32] (probe_groups per query) and keeps no candidate streams.
   float* probe;
   int probe_groups;
+  // Exclusive upper bound on the keys a stream admits, per query (nullable): a later pass of a
+  // search keeping more candidates than one stream holds takes the next keys below the last
+  // pass's smallest (no pilot sweep then: its group maxima ignore the bound).
+  const uint64_t* ceil = nullptr;
   int32_t* err;       // device error word
   uint64_t timeout_ns;
   EpiParams epi;

@@ -69,6 +69,11 @@ cudaError_t launch_min_score(const float* scores, int nq, int k, float min_score
 cudaError_t launch_finish_keys(const uint64_t* keys, const uint32_t* cnt, int nq, int K, int k_out,
                                int kind, int metric, int dim, int32_t* ids, float* scores,
                                int32_t* counts, cudaStream_t st);
+// Candidate searches wider than one stream, pass by pass (merge.cu).
+cudaError_t launch_pass_ceilings(const uint64_t* keys, const uint32_t* cnt, int nq, int K, int got, uint64_t* ceil,
+                                 cudaStream_t st);
+cudaError_t launch_pass_append(uint64_t* keys, uint32_t* cnt, int nq, int K, int got, const uint64_t* keys2,
+                               const uint32_t* cnt2, int K2, cudaStream_t st);
 cudaError_t launch_merge_shards(int nshards, const int64_t* offsets, const int32_t* sids,
                                 const float* ssc, const int32_t* scnt, int kin, int nq, int k,
                                 int32_t* ids, float* scores, int32_t* counts, cudaStream_t st);

@@ -258,6 +258,40 @@ cudaError_t launch_finish_keys(const uint64_t* keys, const uint32_t* cnt, int nq
   return cudaGetLastError();
 }
 
+// Passes of a candidate search wider than one stream: ceil[q] = the smallest key kept so far
+// when the query's previous pass was full (there may be more rows below it), else 0 (none).
+__global__ void pass_ceilings_kernel(const uint64_t* __restrict__ keys, const uint32_t* __restrict__ cnt, int nq,
+                                     int K, int got, uint64_t* __restrict__ ceil) {
+  const int q = blockIdx.x * blockDim.x + threadIdx.x;
+  if (q >= nq) return;
+  ceil[q] = cnt[q] == (uint32_t)got ? keys[(size_t)q * K + got - 1] : 0ull;
+}
+
+// Appends a pass's sorted keys (all below the query's ceiling) after the keys kept so far.
+__global__ void pass_append_kernel(uint64_t* __restrict__ keys, uint32_t* __restrict__ cnt, int nq, int K, int got,
+                                   const uint64_t* __restrict__ keys2, const uint32_t* __restrict__ cnt2, int K2) {
+  const int q = blockIdx.x;
+  if (cnt[q] != (uint32_t)got) return;  // the earlier passes already hold every row
+  const uint32_t c2 = cnt2[q];
+  for (uint32_t i = threadIdx.x; i < c2; i += blockDim.x) keys[(size_t)q * K + got + i] = keys2[(size_t)q * K2 + i];
+  __syncthreads();
+  if (threadIdx.x == 0) cnt[q] = (uint32_t)got + c2;
+}
+
+cudaError_t launch_pass_ceilings(const uint64_t* keys, const uint32_t* cnt, int nq, int K, int got, uint64_t* ceil,
+                                 cudaStream_t st) {
+  if (nq <= 0) return cudaSuccess;
+  pass_ceilings_kernel<<<(nq + 255) / 256, 256, 0, st>>>(keys, cnt, nq, K, got, ceil);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_pass_append(uint64_t* keys, uint32_t* cnt, int nq, int K, int got, const uint64_t* keys2,
+                               const uint32_t* cnt2, int K2, cudaStream_t st) {
+  if (nq <= 0) return cudaSuccess;
+  pass_append_kernel<<<nq, 128, 0, st>>>(keys, cnt, nq, K, got, keys2, cnt2, K2);
+  return cudaGetLastError();
+}
+
 // Cross-shard merge: shard s contributes shard_counts[s*nq+q] (ordinal, score) pairs for
 // query q at [(s*nq+q)*kin]; ordinals are shifted by offsets[s].  Output: the k best by
 // (score desc, ordinal asc), the canonical order of TopK.select.

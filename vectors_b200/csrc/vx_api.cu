@@ -424,6 +424,8 @@ void exact_fallback(vx_index* ix, const float* dq, int nq_chunk, int dim, int k,
 }
 
 constexpr int kMaxCandidates = 1000;  // largest window the R=33 stream geometry holds
+constexpr int kStreamKeysMax = 1023;  // keys one candidate stream keeps (R = 33)
+constexpr int kQuantizedKeysMax = 8 * kStreamKeysMax;  // quantized candidates per query, in passes
 
 int candidate_width(int k, int64_t n) {
   // Approximate candidates per query in the first pass: enough headroom above k for the
@@ -469,7 +471,7 @@ void scan_and_merge(int mode, const CUtensorMap& tmq, const CUtensorMap& tmrows,
     a.top2 = tops + (size_t)units * Qp;
     VX_CUDA(cudaMemsetAsync(tops, 0, (size_t)2 * units * Qp * 8, st));
   }
-  if (probe && a.n > 2 * kPilotRows && a.K <= kPilotRows / 32 && use_pilot()) {
+  if (probe && !a.ceil && a.n > 2 * kPilotRows && a.K <= kPilotRows / 32 && use_pilot()) {
     // probe sweep over the first kPilotRows rows: group maxima only, then the floors
     ScanArgs p = a;
     p.n = kPilotRows;
@@ -669,7 +671,14 @@ int search_quantized_scan(vx_index* ix, const float* dq, int nq, int K, int k_ou
       ((ix->kind == VX_KIND_BQ || ix->kind == VX_KIND_BBQ) && ix->codes8)) {
     const bool bq = ix->kind == VX_KIND_BQ;    // +-1 operands, Hamming epilogue
     const bool bbq = ix->kind == VX_KIND_BBQ;  // 0/1 rows x 4-bit query codes, BBQ epilogue
-    const int R = gemm_scan_stream_R(K);
+    // More candidates than one stream keeps (kStreamKeysMax) are taken in passes: each later
+    // pass admits only keys below the previous pass's smallest, so the passes' sorted keys
+    // concatenate into the K best.
+    if (K > kQuantizedKeysMax)
+      return fail(VX_ERR_UNSUPPORTED, "%d candidates per query is more than the %d this build keeps", K,
+                  kQuantizedKeysMax);
+    const int KP = std::min(K, kStreamKeysMax);  // keys per pass
+    const int R = gemm_scan_stream_R(KP);
     if (R < 0) return fail(VX_ERR_UNSUPPORTED, "k=%d is larger than this build supports", K);
     const int C = 32 * R;
     const int64_t ntiles = (ix->n + 255) / 256;
@@ -705,6 +714,9 @@ int search_quantized_scan(vx_index* ix, const float* dq, int nq, int K, int k_ou
     float* probe = S.alloc<float>((size_t)QpMax * (kPilotRows / 32));
     uint64_t* keys = S.alloc<uint64_t>((size_t)qmax * K);
     uint32_t* kcnt = S.alloc<uint32_t>(qmax);
+    uint64_t* keys2 = K > KP ? S.alloc<uint64_t>((size_t)qmax * KP) : nullptr;  // one later pass
+    uint32_t* kcnt2 = K > KP ? S.alloc<uint32_t>(qmax) : nullptr;
+    uint64_t* ceil = K > KP ? S.alloc<uint64_t>(QpMax) : nullptr;
     int32_t* nflag = S.alloc<int32_t>(1);
     int32_t* flag_list = S.alloc<int32_t>(qmax);
     for (int q0 = 0; q0 < nq; q0 += (int)qch) {
@@ -730,7 +742,7 @@ int search_quantized_scan(vx_index* ix, const float* dq, int nq, int K, int k_ou
       a.num_mblocks = mblocks;
       a.kchunks = ix->Dp8 / 128;
       a.ntiles = ntiles;
-      a.K = K;
+      a.K = KP;
       a.C = C;
       a.bufs = bufs;
       a.cnts = cnts;
@@ -747,7 +759,25 @@ int search_quantized_scan(vx_index* ix, const float* dq, int nq, int K, int k_ou
       a.epi.bits = dim;
       a.epi.bbq_rows = ix->bbq_epi;
       a.epi.bbq_q = qinfo;
-      scan_and_merge(mode, tmq, ix->tm_codes8, a, units, R, Qp, floor, tops, probe, keys, kcnt, st);
+      if (K == KP) {
+        scan_and_merge(mode, tmq, ix->tm_codes8, a, units, R, Qp, floor, tops, probe, keys, kcnt, st);
+      } else {
+        // first pass into a KP-wide buffer, re-strided to K; then passes below the ceilings
+        scan_and_merge(mode, tmq, ix->tm_codes8, a, units, R, Qp, floor, tops, probe, keys2, kcnt2, st);
+        VX_CUDA(cudaMemcpy2DAsync(keys, (size_t)K * 8, keys2, (size_t)KP * 8, (size_t)KP * 8, qc,
+                                  cudaMemcpyDeviceToDevice, st));
+        VX_CUDA(cudaMemcpyAsync(kcnt, kcnt2, (size_t)qc * 4, cudaMemcpyDeviceToDevice, st));
+        for (int got = KP; got < K; got += KP) {
+          const int K2 = std::min(KP, K - got);
+          VX_CUDA(cudaMemsetAsync(ceil, 0, (size_t)Qp * 8, st));
+          VX_LAUNCH(1, launch_pass_ceilings(keys, kcnt, qc, K, got, ceil, st));
+          ScanArgs b = a;
+          b.K = K2;
+          b.ceil = ceil;
+          scan_and_merge(mode, tmq, ix->tm_codes8, b, units, R, Qp, floor, tops, probe, keys2, kcnt2, st);
+          VX_LAUNCH(1, launch_pass_append(keys, kcnt, qc, K, got, keys2, kcnt2, K2, st));
+        }
+      }
       if (rescore) {
         RescoreArgs r{};
         r.nq = qc;
