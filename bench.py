@@ -361,6 +361,7 @@ def main():
 
 
     gm_events = []  # (start, end) around each step's all-gather + shard merge (N > 1)
+    offs_dev = torch.tensor(offs[:world], dtype=torch.int64, device=dev)
 
     def flat_step():
         ids, sc, cnt = flat.search_batch_device(q_dev, k)
@@ -368,7 +369,7 @@ def main():
             return ids, sc, cnt
         e_a, e_b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e_a.record()
-        out = gather_and_merge(ids, sc, cnt, offs, k)
+        out = gather_and_merge(ids, sc, cnt, offs_dev, k)
         e_b.record()
         gm_events.append((e_a, e_b))
         return out
@@ -562,6 +563,7 @@ def run_ivf(args, rank, world, local, dev, barrier, max_over_ranks, hbm_peak, pe
     n, dim, nlist, m, ks = args.ivf_n, P["dim"], args.ivf_nlist, P["m"], P["ks"]
     offs = vx.shard_offsets(n, world)
     lo, hi = offs[rank], offs[rank + 1]
+    offs_dev = torch.tensor(offs[:world], dtype=torch.int64, device=dev)
     cent_mix = centres(P["comps"], dim, SEED_C ^ 0x1F)
     g = torch.Generator(device=dev)
     g.manual_seed(42)
@@ -826,6 +828,7 @@ def run_sq8(args, rank, world, local, dev, barrier, max_over_ranks, tc_sustained
     n, dim, nq, k = args.sq8_n, P["dim"], P["nq"], P["k"]
     offs = vx.shard_offsets(n, world)
     lo, hi = offs[rank], offs[rank + 1]
+    offs_dev = torch.tensor(offs[:world], dtype=torch.int64, device=dev)
     cent = centres(P["comps"], dim, SEED_C ^ 0x5A)
     x = torch.from_numpy(gen_rows(lo, hi - lo, dim, cent, P["sigma"], SEED_DB ^ 0x5A, True)).to(dev)
     # ScalarQuantizer encoding (global quantile pair, codes 0..127, per-row correction), as data
@@ -848,7 +851,7 @@ def run_sq8(args, rank, world, local, dev, barrier, max_over_ranks, tc_sustained
 
     def step():
         ids, sc, cnt = a.scan_candidates_device(q, k)
-        return ids if world == 1 else gather_and_merge(ids, sc, cnt, offs, k)[0]
+        return ids if world == 1 else gather_and_merge(ids, sc, cnt, offs_dev, k)[0]
 
     ms, kms, br = _timed_scan(args, world, dev, barrier, max_over_ranks, step, "gemm_scan")
     par = cpu = e2e = None
@@ -893,6 +896,7 @@ def run_bq(args, rank, world, local, dev, barrier, max_over_ranks, tc_sustained,
     n, dim, nq, k = args.bq_n, P["dim"], P["nq"], P["k"]
     offs = vx.shard_offsets(n, world)
     lo, hi = offs[rank], offs[rank + 1]
+    offs_dev = torch.tensor(offs[:world], dtype=torch.int64, device=dev)
     g = torch.Generator(device=dev)
     g.manual_seed(0xB0 + 0)  # the same centres on every rank
     cent = torch.randn((P["comps"], dim), generator=g, device=dev)
@@ -936,7 +940,7 @@ def run_bq(args, rank, world, local, dev, barrier, max_over_ranks, tc_sustained,
 
     def step():
         ids, sc, cnt = a.scan_candidates_device(q, k)
-        return ids if world == 1 else gather_and_merge(ids, sc, cnt, offs, k)[0]
+        return ids if world == 1 else gather_and_merge(ids, sc, cnt, offs_dev, k)[0]
 
     ms, kms, br = _timed_scan(args, world, dev, barrier, max_over_ranks, step, "gemm_scan")
     par = cpu = e2e = None
@@ -976,7 +980,7 @@ def run_bq(args, rank, world, local, dev, barrier, max_over_ranks, tc_sustained,
 
     def bstep():
         ids, sc, cnt = b.scan_candidates_device(q, k)
-        return ids if world == 1 else gather_and_merge(ids, sc, cnt, offs, k)[0]
+        return ids if world == 1 else gather_and_merge(ids, sc, cnt, offs_dev, k)[0]
 
     bms_step, bkms, bbr = _timed_scan(args, world, dev, barrier, max_over_ranks, bstep, "gemm_scan")
     bpar = bcpu = be2e = None
@@ -1032,6 +1036,7 @@ def run_fp16(args, rank, world, local, dev, barrier, max_over_ranks, tc_sustaine
     P = FP16
     per, dim, nq, k = args.fp16_n, P["dim"], P["nq"], P["k"]
     offs = [per * r for r in range(world + 1)]
+    offs_dev = torch.tensor(offs[:world], dtype=torch.int64, device=dev)
     g = torch.Generator(device=dev)
     g.manual_seed(0xF16)  # the same centres on every rank
     cent = torch.randn((P["comps"], dim), generator=g, device=dev)
@@ -1057,7 +1062,7 @@ def run_fp16(args, rank, world, local, dev, barrier, max_over_ranks, tc_sustaine
 
     def step():
         ids, sc, cnt = a.scan_candidates_device(q, k)
-        return ids if world == 1 else gather_and_merge(ids, sc, cnt, offs, k)[0]
+        return ids if world == 1 else gather_and_merge(ids, sc, cnt, offs_dev, k)[0]
 
     ms, kms, br = _timed_scan(args, world, dev, barrier, max_over_ranks, step, "gemm_scan")
     par = cpu = e2e = None

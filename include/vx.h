@@ -225,6 +225,12 @@ VX_API int vx_ivf_graph_build(int32_t device, const uint8_t* bytes, int64_t len,
  * builds take both from the file.  The IVF-flat EUCLIDEAN search stops early with them as
  * IvfIndex.search does (IvfIndex.java:190-205).  Must not overlap searches on the index. */
 VX_API int vx_ivf_set_buoy(vx_index* index, const float* radii, const int32_t* spill_targets);
+/* ClusterPartition.keyDimensions of an IVF-flat index's partitions (IvfIndex.build with
+ * harmonyKeyDims > 0): key_dim_counts [nlist], the number of key dimensions of each list (0 =
+ * none; NULL clears).  A EUCLIDEAN search that reaches such a list with a full heap scores its rows
+ * with squareDistance, as scanPartitionWithHarmony does (IvfIndex.java:214-216,279-289); graph.bin
+ * builds read the counts from the file.  Must not overlap searches on the index. */
+VX_API int vx_ivf_set_key_dims(vx_index* index, const int32_t* key_dim_counts);
 /* The adapter's SOAR spill ratio at search time (IvfPqAdapter / IvfFlatAdapter gamma,
  * IvfSearchRequest.gamma >= 0, IvfSearchRequest.java:40; default 0 = no spill).  With gamma > 0
  * and spill targets set, vx_search_batch and vx_ivfpq_search* route with

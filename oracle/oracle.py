@@ -87,7 +87,7 @@ def lib() -> C.CDLL:
             "vo_ivfpq_search": (None, [p, i32, i32, p, p, i32, i32, p, p, i64, i32, p, i32, i32, i32, i32, p, i32, i32, p, p, p]),
             "vo_ivfflat_search": (None, [p, i32, i32, p, p, p, i64, i32, p, i32, i32, i32, i32, i32, p, p, p]),
             "vo_ivfpq_search_spill": (None, [p, i32, i32, p, p, i32, i32, p, p, i64, i32, p, i32, i32, i32, f32, p, i32, p, i32, p, p, p]),
-            "vo_ivfflat_search_spill": (None, [p, i32, i32, p, p, p, i32, p, p, i32, i32, i32, f32, p, i32, p, p, p]),
+            "vo_ivfflat_search_spill": (None, [p, i32, i32, p, p, p, i32, p, p, i32, i32, i32, f32, p, p, p, i32, p, p, p]),
             "vo_ivfflat_search_early_exit": (None, [p, i32, i32, p, p, p, i64, i32, p, p, i32, i32, i32, i32, i32, p, p,
                                                     p]),
             "vo_ivf_radii": (None, [p, i32, i32, p, p, p, p]),
@@ -473,17 +473,26 @@ def ivfpq_search_spill(centroids, list_offsets, list_ordinals, m, ks, codebooks,
 
 
 def ivfflat_search_full(centroids, list_offsets, list_ordinals, vectors, radii, queries, metric, k, nprobe, gamma=0.0,
-                        spill_targets=None, nthreads=None):
-    """IvfIndex.search without PQ as the reference runs it: SOAR spill routing (gamma > 0) and,
-    for EUCLIDEAN, the early exit against `radii` (None: every probed list scanned)."""
+                        spill_targets=None, key_dims=None, nthreads=None):
+    """IvfIndex.search without PQ as the reference runs it: SOAR spill routing (gamma > 0), for
+    EUCLIDEAN the early exit against `radii` (None: every probed list scanned), and the HARMONY
+    scan of partitions with key dimensions (`key_dims`: one list of dimensions, or None, per list)."""
     c, q, v = f32(centroids), f32(queries), f32(vectors)
     off = np.ascontiguousarray(list_offsets, np.int64)
     ords = np.ascontiguousarray(list_ordinals, np.int32)
     r = None if radii is None else f32(radii)
     sp = None if spill_targets is None else np.ascontiguousarray(spill_targets, np.int32)
+    kd_off = kd = None
+    if key_dims is not None:
+        sizes = [0 if d is None else len(d) for d in key_dims]
+        kd_off = np.zeros(len(key_dims) + 1, np.int64)
+        kd_off[1:] = np.cumsum(sizes)
+        kd = np.ascontiguousarray(np.concatenate([np.asarray(d, np.int32) for d in key_dims if d is not None]
+                                                 or [np.zeros(0, np.int32)]), np.int32)
     ids, sc, cnt = _outs(q.shape[0], k)
     lib().vo_ivfflat_search_spill(P(c), c.shape[0], c.shape[1], P(off), P(ords), P(v), metric, P(r), P(q), q.shape[0],
-                                  k, nprobe, float(gamma), P(sp), nthreads or threads(), P(ids), P(sc), P(cnt))
+                                  k, nprobe, float(gamma), P(sp), P(kd_off), P(kd), nthreads or threads(), P(ids), P(sc),
+                                  P(cnt))
     return ids, sc, cnt
 
 

@@ -1506,10 +1506,16 @@ void vo_ivfpq_search_spill(const float* cent, int32_t nlist, int32_t dim, const 
 // larger radius leaves a smaller bound, so it can miss a closer row that scanning every probed
 // cluster (vo_ivfflat_search) finds.  Not restated: the HARMONY key-dimension path (:207-212,
 // scanPartitionWithHarmony :279-289) of partitions built with key dimensions.
+// HARMONY (kd_off / kd: each partition's key dimensions as CSR, nullable): for EUCLIDEAN, a
+// partition with key dimensions met with a full heap is scanned by scanPartitionWithHarmony
+// (IvfIndex.java:214-216,279-289): each row's partialSquaredDistance over the key dimensions
+// (DimensionAnalysis.java:96-104, sequential) skips it when >= the heap's worst distance, else its
+// score is -squareDistance(query, row) (not the batched order).
 static void ivfflat_search(const float* cent, int32_t nlist, int32_t dim, const int64_t* loff, const int32_t* lord,
                            const float* vectors, int32_t metric, const float* radii, const float* queries,
                            int32_t nq, int32_t k, int32_t nprobe, float gamma, const int32_t* spill, int32_t policy,
-                           int32_t nthreads, int32_t* ids, float* scores, int32_t* counts) {
+                           int32_t nthreads, int32_t* ids, float* scores, int32_t* counts,
+                           const int64_t* kd_off = nullptr, const int32_t* kd = nullptr) {
   const IvfRoute route = ivf_route(cent, nlist, dim, metric, queries, nq, nprobe, gamma, spill, policy, nthreads);
   const bool euclid = metric == VO_EUCLIDEAN, cosine = metric == VO_COSINE;
   parallel_for(nq, nthreads, [&](int64_t lo, int64_t hi) {
@@ -1535,6 +1541,29 @@ static void ivfflat_search(const float* cent, int32_t nlist, int32_t dim, const 
           }
         }
         int64_t b = loff[cid], e = loff[cid + 1];
+        const bool ref_heap = policy == VO_POLICY_REFERENCE_HEAP;
+        const bool full_now = ref_heap ? rh.size == rh.cap : (int)ch.v.size() == ch.cap;
+        if (euclid && kd_off && kd_off[cid + 1] > kd_off[cid] && full_now) {
+          for (int64_t i = b; i < e; i++) {
+            const int32_t o = lord[i];
+            const float* v = vectors + (int64_t)o * dim;
+            float partial = 0.0f;
+            for (int64_t t = kd_off[cid]; t < kd_off[cid + 1]; t++) {
+              const float df = qq[kd[t]] - v[kd[t]];
+              partial += df * df;
+            }
+            const float worst = ref_heap ? rh.sc[0] : ch.v.front().first;
+            if (partial >= -worst) continue;
+            const float sc = -vo_square_distance(qq, v, dim);
+            if (sc < -3.4028235e38f) continue;
+            if (ref_heap) {
+              if (sc > rh.sc[0]) rh.offer(o, sc);
+            } else {
+              ch.offer(o, sc);
+            }
+          }
+          continue;
+        }
         for (int64_t s0 = b; s0 < e; s0 += 64) {
           const int cnt = (int)std::min<int64_t>(64, e - s0);
           for (int j = 0; j < cnt; j++)
@@ -1588,9 +1617,10 @@ void vo_ivfflat_search_early_exit(const float* cent, int32_t nlist, int32_t dim,
 void vo_ivfflat_search_spill(const float* cent, int32_t nlist, int32_t dim, const int64_t* loff, const int32_t* lord,
                              const float* vectors, int32_t metric, const float* radii, const float* queries,
                              int32_t nq, int32_t k, int32_t nprobe, float gamma, const int32_t* spill_targets,
-                             int32_t nthreads, int32_t* ids, float* scores, int32_t* counts) {
+                             const int64_t* kd_off, const int32_t* kd, int32_t nthreads, int32_t* ids, float* scores,
+                             int32_t* counts) {
   ivfflat_search(cent, nlist, dim, loff, lord, vectors, metric, radii, queries, nq, k, nprobe, gamma, spill_targets,
-                 VO_POLICY_CANONICAL, nthreads, ids, scores, counts);
+                 VO_POLICY_CANONICAL, nthreads, ids, scores, counts, kd_off, kd);
 }
 // BuoyIndex.computeRadii / euclideanDist (BuoyIndex.java:175-183,220-227).
 void vo_ivf_radii(const float* cent, int32_t nlist, int32_t dim, const int64_t* loff, const int32_t* lord,

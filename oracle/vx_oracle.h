@@ -189,13 +189,14 @@ void vo_ivfpq_search_spill(const float* centroids, int32_t nlist, int32_t dim, c
                            const uint8_t* codes, int64_t n, int32_t metric, const float* queries, int32_t nq,
                            int32_t k, int32_t nprobe, float gamma, const int32_t* spill_targets, int32_t rescore,
                            const float* vectors, int32_t nthreads, int32_t* ids, float* scores, int32_t* counts);
-/* IvfIndex.search without PQ in full: SOAR spill routing (gamma > 0), and for EUCLIDEAN the
- * early exit against radii (NULL radii: every probed cluster scanned) (canonical ranking). */
+/* IvfIndex.search without PQ in full: SOAR spill routing (gamma > 0), for EUCLIDEAN the early
+ * exit against radii (NULL radii: every probed cluster scanned) and the HARMONY scan of partitions
+ * with key dimensions (kd_off[nlist + 1] / kd: CSR, NULL: none) (canonical ranking). */
 void vo_ivfflat_search_spill(const float* centroids, int32_t nlist, int32_t dim, const int64_t* list_offsets,
                              const int32_t* list_ordinals, const float* vectors, int32_t metric, const float* radii,
                              const float* queries, int32_t nq, int32_t k, int32_t nprobe, float gamma,
-                             const int32_t* spill_targets, int32_t nthreads, int32_t* ids, float* scores,
-                             int32_t* counts);
+                             const int32_t* spill_targets, const int64_t* kd_off, const int32_t* kd,
+                             int32_t nthreads, int32_t* ids, float* scores, int32_t* counts);
 void vo_ivfflat_search_early_exit(const float* centroids, int32_t nlist, int32_t dim,
                                   const int64_t* list_offsets, const int32_t* list_ordinals,
                                   const float* vectors, int64_t n, int32_t metric, const float* radii,

@@ -109,8 +109,12 @@ def test_ivf_flat_graph_bin_opens_the_same_index(oracle, metric):
     assert got.size() == 8000
     ref = vx.IvfFlatAdapter(nprobe=5)
     ref.build_prebuilt(cent, off, ords, db, vx.SimilarityFunction(metric))
+    ref.set_key_dims([[1, 2]] + [None] * 19)
     _same(got.ivf_search(q, 10, 5), ref.ivf_search(q, 10, 5), f"ivf-flat graph.bin m={metric}")
-    ids, sc, cnt = oracle.ivfflat_search_full(cent, off, ords, db, radii, q, metric, 10, 5)
+    # list 0 carries HARMONY key dimensions: the file's index scans it with squareDistance once
+    # a query's heap is full, the array-built one (no key dimensions) does not
+    ids, sc, cnt = oracle.ivfflat_search_full(cent, off, ords, db, radii, q, metric, 10, 5,
+                                              key_dims=[[1, 2]] + [None] * 19)
     for i, o in enumerate(got.search_batch(q, 10)):
         assert list(o.ordinals) == list(ids[i, : cnt[i]]), f"ivf-flat graph.bin m={metric} query {i}"
     got.close()

@@ -218,3 +218,28 @@ def test_ivfflat_large_k_with_early_exit(oracle, metric):
     with pytest.raises(vx.UnsupportedOperationException):
         a.ivf_search(q, 257, 6)
     a.close()
+
+
+@pytest.mark.parametrize("k", [8, 40])
+def test_harmony_partitions_scanned_with_square_distance(oracle, k):
+    # partitions with key dimensions (IvfIndex.build's harmonyKeyDims): once a query's heap is
+    # full, the reference scores their rows with squareDistance instead of the batched order
+    n, dim, nlist = 9000, 100, 16
+    db = oracle.gen_mixture(n, dim, 12, 0.3, SEED_C, SEED_DB, False)
+    q = oracle.gen_mixture(120, dim, 12, 0.3, SEED_C, SEED_Q, False)
+    cent = oracle.kmeans_train(db[:3000], nlist, 8, 42)
+    off, ords = oracle.build_ivf_lists(oracle.kmeans_assign(db, cent), nlist)
+    rng = np.random.default_rng(11)
+    key_dims = [list(rng.choice(dim, 6, replace=False)) if l % 3 != 1 else None for l in range(nlist)]
+    radii = oracle.ivf_radii(cent, off, ords, db)
+    a = vx.IvfFlatAdapter(nprobe=6)
+    a.build_prebuilt(cent, off, ords, db, vx.SimilarityFunction.EUCLIDEAN)
+    a.set_key_dims(key_dims)
+    got = a.ivf_search(q, k, 6)
+    want = oracle.ivfflat_search_full(cent, off, ords, db, radii, q, 0, k, 6, key_dims=key_dims)
+    plain = oracle.ivfflat_search_full(cent, off, ords, db, radii, q, 0, k, 6)
+    assert sum(not np.array_equal(want[1][j], plain[1][j]) for j in range(len(q))) > 0
+    _same(got, *want, f"harmony k={k}")
+    a.set_key_dims(None)  # cleared: the batched scan everywhere again
+    _same(a.ivf_search(q, k, 6), *plain, f"harmony cleared k={k}")
+    a.close()

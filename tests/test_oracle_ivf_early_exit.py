@@ -105,3 +105,66 @@ def test_ordered_merge_of_list_top_k_reproduces_the_break(oracle, case):
     for j in range(len(q)):
         assert [i for _, i in got[j]] == list(want[0][j, : want[2][j]]), j
         assert [s for s, _ in got[j]] == list(want[1][j, : want[2][j]]), j
+
+
+def _harmony_model(oracle, cent, off, ords, db, radii, q, k, nprobe, key_dims, skip=True):
+    """IvfIndex.search (EUCLIDEAN) restated here: clusters in route order with the early exit; a
+    cluster with key dimensions met with a full heap takes scanPartitionWithHarmony -- rows whose
+    partial distance over the key dimensions reaches the worst are skipped (skip=False scores
+    them anyway), the rest are scored -squareDistance; other clusters the batched scan."""
+    lids, dists = oracle.route(cent, q, oracle.EUCLIDEAN, nprobe)
+    out = []
+    for j in range(len(q)):
+        kept = []
+        for p_ in range(nprobe):
+            cid = int(lids[j, p_])
+            if len(kept) == k:
+                lb = np.float32(np.float32(np.sqrt(np.float64(dists[j, p_]))) - radii[cid])
+                if lb > 0 and np.float32(lb * lb) >= -kept[-1][0]:
+                    break
+            b, e = int(off[cid]), int(off[cid + 1])
+            if key_dims[cid] is not None and len(kept) == k:
+                for o in ords[b:e]:
+                    partial = np.float32(0)
+                    for d in key_dims[cid]:
+                        df = np.float32(q[j, d] - db[o, d])
+                        partial = np.float32(partial + np.float32(df * df))
+                    if skip and partial >= -kept[-1][0]:
+                        continue
+                    s = np.float32(-oracle.square_distance(q[j], db[o]))
+                    kept = sorted(kept + [(s, int(o))], key=lambda t: (-t[0], t[1]))[:k]
+                continue
+            if e == b:
+                continue
+            one = np.array([0, e - b], np.int64)
+            ids, sc, cnt = oracle.ivfflat_search(cent[cid:cid + 1], one, ords[b:e], db, q[j:j + 1], oracle.EUCLIDEAN, k, 1)
+            kept = sorted(kept + [(sc[0, i], int(ids[0, i])) for i in range(cnt[0])], key=lambda t: (-t[0], t[1]))[:k]
+        out.append(kept)
+    return out
+
+
+def test_harmony_scan_of_partitions_with_key_dimensions(oracle):
+    # partitions with key dimensions met with a full heap are scanned row by row with
+    # squareDistance after the partial-distance skip; the skip drops only rows that could not
+    # enter the heap here, so scoring them anyway gives the same results
+    rng = np.random.default_rng(4)
+    dim, nlist = 100, 10  # 100 dims: squareDistance and the batched order round differently
+    cent = (2.0 * rng.standard_normal((nlist, dim))).astype(np.float32)
+    assign = rng.integers(0, nlist, 3000).astype(np.int32)
+    db = (cent[assign] + rng.standard_normal((3000, dim))).astype(np.float32)
+    off, ords = oracle.build_ivf_lists(assign, nlist)
+    q = (2.0 * rng.standard_normal((25, dim))).astype(np.float32)
+    radii = oracle.ivf_radii(cent, off, ords, db)
+    key_dims = [list(rng.choice(dim, 4, replace=False)) if l % 2 == 0 else None for l in range(nlist)]
+    k, nprobe = 8, 6
+    got = oracle.ivfflat_search_full(cent, off, ords, db, radii, q, oracle.EUCLIDEAN, k, nprobe, key_dims=key_dims)
+    want = _harmony_model(oracle, cent, off, ords, db, radii, q, k, nprobe, key_dims)
+    noskip = _harmony_model(oracle, cent, off, ords, db, radii, q, k, nprobe, key_dims, skip=False)
+    plain = oracle.ivfflat_search_full(cent, off, ords, db, radii, q, oracle.EUCLIDEAN, k, nprobe)
+    changed = 0
+    for j in range(len(q)):
+        assert list(got[0][j, :got[2][j]]) == [i for _, i in want[j]], j
+        assert list(got[1][j, :got[2][j]]) == [s for s, _ in want[j]], j
+        assert want[j] == noskip[j], j
+        changed += not np.array_equal(got[1][j], plain[1][j])
+    assert changed > 0  # squareDistance scores differ from the batched order's somewhere

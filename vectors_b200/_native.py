@@ -55,6 +55,7 @@ SIGNATURES = {
     "vx_ivfflat_build": [_I32, _P, _I32, _I32, _P, _P, _P, _I64, _I64, _I32, _I32, _PP],
     "vx_ivf_set_buoy": [_P, _P, _P],
     "vx_ivf_set_gamma": [_P, _F32],
+    "vx_ivf_set_key_dims": [_P, _P],
     "vx_index_info": [_P, _P, _P, _P, _P],
     "vx_index_free": [_P],
     "vx_search_batch": [_P, _P, _I32, _I32, _I32, _I32, _F32, _P, _P, _P],

@@ -220,6 +220,7 @@ struct IvfFile {
   std::vector<float> radii;           // [nlist] cluster radii (the EUCLIDEAN early exit)
   std::vector<int64_t> offsets;       // [nlist + 1]
   std::vector<int32_t> ordinals;      // partitions, concatenated
+  std::vector<int32_t> key_dims;      // [nlist] HARMONY key dimension count of each partition
   bool pq = false;
   int32_t m = 0, ks = 0;
   bool global_centroid = false;
@@ -287,9 +288,10 @@ int parse_ivf(const uint8_t* bytes, int64_t len, IvfFile& f) {
     f.ordinals.resize(at + (size_t)size);  // grows geometrically (an exact reserve per partition would not)
     for (int32_t i = 0; i < size; i++) f.ordinals[at + (size_t)i] = c.i32();
     f.offsets[(size_t)p + 1] = f.offsets[(size_t)p] + size;
-    const int32_t kd = c.i32();  // HARMONY key dimensions (0 = none): not used by pqSearch
+    const int32_t kd = c.i32();  // HARMONY key dimensions (0 = none): IVF-flat only, pqSearch ignores them
     if (kd < 0 || c.remaining() / 4 < (uint64_t)kd) return underflow("partition key dimensions");
     c.pos += (uint64_t)kd * 4;
+    f.key_dims.push_back(kd);
   }
   // pqFlag: absent on files written before IVF-PQ (treated as 0), else 0 or 1
   const int flag = c.remaining() > 0 ? c.u8() : 0;
@@ -486,8 +488,10 @@ int vx_ivf_graph_build(int32_t device, const uint8_t* bytes, int64_t len, int32_
                                vectors ? row_stride : f.dim, nprobe, rescore_factor, out);
     }
     if (st != VX_OK) return st;
-    // the buoy's own radii and spill targets, as IvfIndex.decode restores them (BuoyIndex.decode)
+    // the buoy's own radii and spill targets, as IvfIndex.decode restores them (BuoyIndex.decode),
+    // and which IVF-flat partitions carry HARMONY key dimensions
     st = vx_ivf_set_buoy(*out, f.radii.data(), f.spill.data());
+    if (st == VX_OK && !f.pq) st = vx_ivf_set_key_dims(*out, f.key_dims.data());
     if (st != VX_OK) {
       vx_index_free(*out);
       *out = nullptr;

@@ -62,6 +62,9 @@ struct vx_index {
   float* radii = nullptr;
   int32_t* spill = nullptr;
   float gamma = 0.0f;
+  // IVF-flat partitions built with HARMONY key dimensions (nullable): scanned with
+  // squareDistance once a query's heap is full (EUCLIDEAN)
+  uint8_t* keyed = nullptr;
   // IVF-flat: list-ordered rows zero-padded to Dp floats, their dotProduct(v, v) (COSINE)
   float* flat_rows = nullptr;
   float* flat_norms = nullptr;

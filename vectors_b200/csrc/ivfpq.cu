@@ -1196,7 +1196,8 @@ constexpr int kExitR = 16;  // 512 key slots per warp >= 2 K (K <= 256)
 __global__ void __launch_bounds__(kExitWarps * 32) ivf_early_exit_kernel(
     const uint64_t* __restrict__ out, const uint32_t* __restrict__ out_cnt, int nq, int width, int K,
     const int32_t* __restrict__ lists, const float* __restrict__ ldist, const float* __restrict__ radii, int euclid,
-    uint64_t min_key, uint64_t* __restrict__ keys, uint32_t* __restrict__ kcnt) {
+    uint64_t min_key, const uint64_t* __restrict__ harm, const uint32_t* __restrict__ harm_cnt,
+    const uint8_t* __restrict__ keyed, uint64_t* __restrict__ keys, uint32_t* __restrict__ kcnt) {
   __shared__ uint64_t s_buf[kExitWarps][32 * kExitR];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int q = blockIdx.x * kExitWarps + warp;
@@ -1214,8 +1215,10 @@ __global__ void __launch_bounds__(kExitWarps * 32) ivf_early_exit_kernel(
       if (lb > 0.0f && __fmul_rn(lb, lb) >= -worst_score) break;
     }
     const size_t slot = (size_t)p * nq + q;
-    const uint32_t c = out_cnt[slot];
-    const uint64_t* src = out + slot * K;
+    // a list with key dimensions met with a full heap: scanPartitionWithHarmony's results
+    const bool harmony = euclid && keyed && keyed[cid] && n == (uint32_t)K;
+    const uint32_t c = harmony ? harm_cnt[slot] : out_cnt[slot];
+    const uint64_t* src = (harmony ? harm : out) + slot * K;
     for (uint32_t i0 = 0; i0 < c; i0 += 32) {
       const uint32_t i = i0 + lane;
       const uint64_t key = i < c ? src[i] : kEmptyKey;
@@ -1260,6 +1263,60 @@ __global__ void __launch_bounds__(kExitWarps * 32) ivf_early_exit_kernel(
   if (lane == 0) kcnt[q] = n;
 }
 
+// HARMONY lists (IvfIndex.scanPartitionWithHarmony, IvfIndex.java:279-289): the rows of a keyed
+// list scored -squareDistance(query, row) in the reference's order (warp_sqdist), one CTA per
+// (query, slot) of a keyed list; each warp scores 32 rows one after another (lane j keeps row j's
+// key), offers them to its candidate buffer, and the warps' buffers merge into the K best.  The
+// reference first skips rows whose partial distance over the key dimensions reaches the heap's
+// worst; such rows' full distances reach it too, so they could not enter the heap (TopKHeap
+// admits only better scores) and scoring them changes nothing.
+template <int R>
+__global__ void __launch_bounds__(256) harmony_list_kernel(HarmonyArgs a) {
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  constexpr int nwarps = 8, C = 32 * R;
+  uint64_t* s_wbuf = reinterpret_cast<uint64_t*>(smem_raw);  // [8][C]
+  uint64_t* s_merge = s_wbuf + (size_t)nwarps * C;            // [2][8 K]
+  const uint32_t mcap = (uint32_t)(nwarps * a.K);
+  uint32_t* s_red = reinterpret_cast<uint32_t*>(s_merge + 2 * (size_t)mcap);
+  uint32_t* s_counter = s_red + 32;
+  const int64_t pair = blockIdx.x;
+  const int q = (int)(pair / a.width), p = (int)(pair % a.width);
+  const size_t slot = (size_t)p * a.nq + q;
+  const int l = a.lists[(size_t)q * a.width + p];
+  if (l < 0 || !a.keyed[l]) {
+    if (threadIdx.x == 0) a.out_cnt[slot] = 0;
+    return;
+  }
+  const int64_t b = a.list_off[l], e = a.list_off[l + 1];
+  const float* qv = a.queries + (size_t)q * a.Dp;
+  WarpStream<R> ws{s_wbuf + (size_t)warp * C, 0u, 0ull};
+  for (int64_t r0 = b + (int64_t)warp * 32; r0 < e; r0 += (int64_t)nwarps * 32) {
+    uint64_t mine = 0;
+    const int nr = (int)((e - r0) < 32 ? (e - r0) : 32);
+    for (int j = 0; j < nr; j++) {
+      const float d = warp_sqdist(RowF32{qv}, RowF32{a.rows + (size_t)(r0 + j) * a.Dp}, a.dim);
+      if (lane == j) mine = float_key(-d, (uint32_t)a.ordinals[r0 + j]);
+    }
+    ws.offer32(mine, lane < nr, C, a.K);
+  }
+  __syncwarp();
+  if (ws.cnt > (uint32_t)a.K) warp_compact_one<R>(ws.buf, ws.cnt, (uint32_t)a.K, ws.thr, ws.cnt);
+  __syncwarp();
+  if (lane == 0) s_red[warp] = ws.cnt;
+  __syncthreads();
+  uint32_t at = 0, total = 0;
+  for (int i = 0; i < nwarps; i++) {
+    at += i < warp ? s_red[i] : 0u;
+    total += s_red[i];
+  }
+  for (uint32_t i = lane; i < ws.cnt; i += 32) s_merge[at + i] = ws.buf[i];
+  __syncthreads();
+  const uint32_t n = block_keep_top(s_merge, total, (uint32_t)a.K, s_merge + mcap, s_red, s_counter);
+  for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) a.out[slot * a.K + i] = s_merge[i];
+  if (threadIdx.x == 0) a.out_cnt[slot] = n;
+}
+
 }  // namespace
 
 cudaError_t launch_route_expand(const int32_t* lists, int nq, int probes, const float* dist, int nlist, int metric,
@@ -1296,18 +1353,44 @@ cudaError_t launch_pq_row_norms(const uint8_t* codes, int64_t n, int M, int Mp, 
   return cudaGetLastError();
 }
 
+cudaError_t launch_harmony_lists(const HarmonyArgs& a, cudaStream_t st) {
+  const int64_t pairs = (int64_t)a.nq * a.width;
+  if (pairs <= 0) return cudaSuccess;
+  const StreamGeom g = stream_geom(a.K, 32);
+  const size_t smem = (size_t)8 * g.C * 8 + (size_t)2 * 8 * a.K * 8 + 33 * 4 + 16;
+#define VX_HARM_CASE(RR)                                                                              \
+  case RR: {                                                                                          \
+    cudaError_t e = cudaFuncSetAttribute(harmony_list_kernel<RR>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
+                                         (int)smem);                                                  \
+    if (e != cudaSuccess) return e;                                                                   \
+    harmony_list_kernel<RR><<<(unsigned)pairs, 256, smem, st>>>(a);                                   \
+    return cudaGetLastError();                                                                        \
+  }
+  switch (g.R) {
+    VX_HARM_CASE(2)
+    VX_HARM_CASE(3)
+    VX_HARM_CASE(5)
+    VX_HARM_CASE(9)
+    VX_HARM_CASE(17)
+    default: return cudaErrorInvalidValue;
+  }
+#undef VX_HARM_CASE
+}
+
 bool early_exit_supported(int K) { return K >= 1 && 2 * K <= 32 * kExitR; }
 
 cudaError_t launch_ivf_early_exit(const uint64_t* out, const uint32_t* out_cnt, int nq, int width, int K,
                                   const int32_t* lists, const float* ldist, const float* radii, int metric,
-                                  float min_score, uint64_t* keys, uint32_t* kcnt, cudaStream_t st) {
+                                  float min_score, const uint64_t* harm, const uint32_t* harm_cnt,
+                                  const uint8_t* keyed, uint64_t* keys, uint32_t* kcnt, cudaStream_t st) {
   if (nq <= 0) return cudaSuccess;
   if (!early_exit_supported(K)) return cudaErrorInvalidValue;
   // keys scoring >= min_score are those >= (order bits of min_score) << 32; -0.0 == 0.0 as in Java
   const float m = min_score == 0.0f ? -0.0f : min_score;
   const uint64_t min_key = (uint64_t)float_order_bits(m) << 32;
   ivf_early_exit_kernel<<<(nq + kExitWarps - 1) / kExitWarps, kExitWarps * 32, 0, st>>>(
-      out, out_cnt, nq, width, K, lists, ldist, radii, metric == kEuclidean ? 1 : 0, min_key, keys, kcnt);
+      out, out_cnt, nq, width, K, lists, ldist, radii, metric == kEuclidean ? 1 : 0, min_key, harm, harm_cnt, keyed,
+      keys, kcnt);
   return cudaGetLastError();
 }
 

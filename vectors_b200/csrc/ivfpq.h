@@ -107,9 +107,26 @@ cudaError_t launch_list_radii(const float* rows, int64_t n, int dim, int Dp, con
                               const float* cent, float* radii, cudaStream_t st);
 // The per-(probe, query) list results merged per query in route order, with IvfIndex.search's
 // EUCLIDEAN early exit (other metrics: a plain merge); keys [nq][K] sorted descending, kcnt [nq].
+// harm / harm_cnt / keyed (nullable): the HARMONY results of lists with key dimensions, taken
+// instead of out when the query's heap is full at that list.
 bool early_exit_supported(int K);
 cudaError_t launch_ivf_early_exit(const uint64_t* out, const uint32_t* out_cnt, int nq, int width, int K,
                                   const int32_t* lists, const float* ldist, const float* radii, int metric,
-                                  float min_score, uint64_t* keys, uint32_t* kcnt, cudaStream_t st);
+                                  float min_score, const uint64_t* harm, const uint32_t* harm_cnt,
+                                  const uint8_t* keyed, uint64_t* keys, uint32_t* kcnt, cudaStream_t st);
+// HARMONY (IvfIndex.scanPartitionWithHarmony): for every (query, slot) whose list is keyed, the K
+// best rows by -squareDistance(query, row) in the reference's order -> harm [width][nq][K].
+struct HarmonyArgs {
+  int nq, width, K, dim, Dp;
+  const int32_t* lists;       // [nq][width]
+  const uint8_t* keyed;       // [nlist]
+  const int64_t* list_off;
+  const int32_t* ordinals;    // list-ordered
+  const float* rows;          // [n][Dp] list-ordered, zero padded
+  const float* queries;       // [nq][Dp] zero padded
+  uint64_t* out;              // [width][nq][K]
+  uint32_t* out_cnt;          // [width][nq]
+};
+cudaError_t launch_harmony_lists(const HarmonyArgs& a, cudaStream_t st);
 
 }  // namespace vx

@@ -918,6 +918,9 @@ int search_ivfflat(vx_index* ix, const float* dq, int nq, int k, int heap_k, int
     int2* groups = T.alloc<int2>((size_t)maxg);
     int32_t* ngroups = T.alloc<int32_t>(2);  // count, dispenser
     uint64_t* qfloor = early_exit ? nullptr : T.alloc<uint64_t>(qc);
+    const bool harmony = early_exit && ix->keyed;
+    uint64_t* harm = harmony ? T.alloc<uint64_t>((size_t)width * qc * K) : nullptr;
+    uint32_t* harm_cnt = harmony ? T.alloc<uint32_t>((size_t)width * qc) : nullptr;
     if (given_lists) {
       VX_LAUNCH(1, launch_copy_lists(given_lists + (size_t)q0 * probes, qc * probes, ix->nlist, lists, d_bad, st));
     } else {
@@ -959,10 +962,27 @@ int search_ivfflat(vx_index* ix, const float* dq, int nq, int k, int heap_k, int
     a.out_cnt = out_cnt;
     a.floor = qfloor;
     VX_TIMED(VX_PROF_ADC_SCAN, st, 2, launch_flat_list(a, (int64_t)qc * width, ix->num_sms * 2, st));
+    if (harmony) {
+      HarmonyArgs h{};
+      h.nq = qc;
+      h.width = width;
+      h.K = K;
+      h.dim = dim;
+      h.Dp = Dp;
+      h.lists = lists;
+      h.keyed = ix->keyed;
+      h.list_off = ix->list_off;
+      h.ordinals = ix->ordinals;
+      h.rows = ix->flat_rows;
+      h.queries = qpad;
+      h.out = harm;
+      h.out_cnt = harm_cnt;
+      VX_TIMED(VX_PROF_ADC_SCAN, st, 1, launch_harmony_lists(h, st));
+    }
     if (early_exit) {
       VX_TIMED(VX_PROF_MERGE, st, 1,
-               launch_ivf_early_exit(out, out_cnt, qc, width, K, lists, ldist, ix->radii, ix->metric, min_score, keys,
-                                     kcnt, st));
+               launch_ivf_early_exit(out, out_cnt, qc, width, K, lists, ldist, ix->radii, ix->metric, min_score, harm,
+                                     harm_cnt, ix->keyed, keys, kcnt, st));
     } else {
       VX_TIMED(VX_PROF_MERGE, st, 1, launch_merge_streams(out, out_cnt, width, qc, qc, K, K, keys, kcnt, st));
     }
@@ -2041,6 +2061,30 @@ int vx_ivf_set_buoy(vx_index* ix, const float* radii, const int32_t* spill_targe
       if (!ix->spill) ix->spill = dev_alloc<int32_t>(ix, (size_t)ix->nlist);
       VX_CUDA(cudaMemcpy(ix->spill, spill_targets, (size_t)ix->nlist * 4, cudaMemcpyDefault));
     }
+    return VX_OK;
+  });
+}
+
+int vx_ivf_set_key_dims(vx_index* ix, const int32_t* key_dim_counts) {
+  return guarded([&]() -> int {
+    if (!ix) return fail(VX_ERR_NULL_POINTER, "index must not be null");
+    if (ix->kind != VX_KIND_IVFFLAT) return fail(VX_ERR_UNSUPPORTED, "not an IVF-flat index");
+    VX_CUDA(cudaSetDevice(ix->device));
+    bool any = false;
+    std::vector<uint8_t> flags((size_t)ix->nlist, 0);
+    if (key_dim_counts)
+      for (int l = 0; l < ix->nlist; l++) {
+        if (key_dim_counts[l] < 0) return fail(VX_ERR_INVALID_ARGUMENT, "negative key dimension count for list %d", l);
+        flags[(size_t)l] = key_dim_counts[l] > 0;
+        any |= key_dim_counts[l] > 0;
+      }
+    if (!any) {
+      ix->keyed = nullptr;  // the array (if any) stays owned by the index until it is freed
+      return VX_OK;
+    }
+    uint8_t* d = dev_alloc<uint8_t>(ix, (size_t)ix->nlist);
+    VX_CUDA(cudaMemcpy(d, flags.data(), (size_t)ix->nlist, cudaMemcpyHostToDevice));
+    ix->keyed = d;
     return VX_OK;
   });
 }

@@ -697,6 +697,18 @@ class IvfFlatAdapter(IvfPqAdapter):
         self._nlist = nlist
         self._apply_gamma()
 
+    def set_key_dims(self, key_dims):
+        """ClusterPartition.keyDimensions per list (HARMONY; None or an empty list = none): a
+        EUCLIDEAN search reaching such a list with a full heap scores its rows with
+        squareDistance (IvfIndex.scanPartitionWithHarmony)."""
+        counts = None
+        if key_dims is not None:
+            counts = np.ascontiguousarray(
+                [0 if d is None else (int(d) if np.isscalar(d) else len(d)) for d in key_dims], np.int32)
+            if counts.shape != (self._nlist,):
+                raise IllegalArgumentException(f"key_dims must hold one entry per list ({self._nlist})")
+        _check(N.lib().vx_ivf_set_key_dims(self._h.ptr, _ptr(counts)))
+
     def load_graph_bin(self, data, metric=None, vectors=None):
         """Opens an IVF_FLAT generation's graph.bin (VectorCollectionImpl.openIvfFlatAdapter):
         centroids and partitions from the file, rows from ``vectors`` (required; e.g. a mapped

@@ -27,7 +27,8 @@ def shard_range(n: int, rank: int, world: int) -> tuple[int, int]:
 def gather_and_merge(local_ids, local_scores, local_counts, offsets: Sequence[int], k: int,
                      group=None, merge: Optional[Callable] = None):
     """All-gathers every rank's (ids [nq][kin], scores [nq][kin], counts [nq]) tensors and
-    merges them into the global top-k.  `offsets` holds each shard's first ordinal; `merge`
+    merges them into the global top-k.  `offsets` holds each shard's first ordinal (a sequence,
+    or an int64 tensor on the device, which spares a host-to-device copy per call); `merge`
     defaults to the device merge (vx_merge_shards_device) and is called as
     merge(ids [S][nq][kin], scores [S][nq][kin], counts [S][nq], offsets tensor, k).
     Every rank takes the same collective steps and returns the same merged result."""
@@ -48,7 +49,10 @@ def gather_and_merge(local_ids, local_scores, local_counts, offsets: Sequence[in
     gi = g[:, :, :kin].contiguous()
     gs = g[:, :, kin:2 * kin].contiguous().view(torch.float32)
     gc = g[:, :, 2 * kin].contiguous()
-    off = torch.tensor(list(offsets)[:world], dtype=torch.int64, device=dev)
+    if isinstance(offsets, torch.Tensor):  # a device tensor prepared once: no host copy per call
+        off = offsets[:world].to(device=dev, dtype=torch.int64)
+    else:
+        off = torch.tensor(list(offsets)[:world], dtype=torch.int64, device=dev)
     return (merge or merge_shards_device)(gi, gs, gc, off, k)
 
 
