@@ -1,6 +1,6 @@
 """Child process for test_gpu_scan_variants.py: the scan variant is chosen by environment
 variables that the library reads once per process (VX_GEMM_1SM, VX_SCAN_PILOT, VX_SCAN_POOL,
-VX_BQ_TENSOR_BYTES, VX_ADC_GROUPED), so each variant runs in a process of its own.
+VX_BQ_TENSOR_BYTES, VX_ADC_GROUPED, VX_EPI_WARPS), so each variant runs in a process of its own.
 Exits 0 when FLAT, SQ8, BQ and BBQ results (or, with the argument "ivf", IVF-PQ results) match
 the oracle."""
 import sys
@@ -42,11 +42,14 @@ def main():
     for metric in (0, 2):
         f = vx.FlatScanAdapter()
         f.build(db, vx.SimilarityFunction(metric))
-        got = f.search_batch(q, 10)
-        ids, sc, cnt = O.flat_search(db, q, metric, 10)
-        for i, o in enumerate(got):
-            assert list(o.ordinals) == list(ids[i, : cnt[i]]), f"flat m={metric} query {i}"
-            np.testing.assert_allclose(o.scores, sc[i, : cnt[i]], rtol=1e-4, atol=0)
+        # k = 10, 100, 300: streams of 288, 544 and 1056 keys (544 on the 8-epilogue-warp build by
+        # default, on the 4-warp one under VX_EPI_WARPS=4)
+        for k in (10, 100, 300):
+            got = f.search_batch(q, k)
+            ids, sc, cnt = O.flat_search(db, q, metric, k)
+            for i, o in enumerate(got):
+                assert list(o.ordinals) == list(ids[i, : cnt[i]]), f"flat m={metric} k={k} query {i}"
+                np.testing.assert_allclose(o.scores, sc[i, : cnt[i]], rtol=1e-4, atol=0)
         f.close()
     lo, hi = O.sq8_train(db)
     codes, corr = O.sq8_encode_all(lo, hi, db)

@@ -40,7 +40,6 @@ using namespace sm100;
 
 constexpr int BN = 256;        // database rows per tile (TMEM columns per accumulator)
 constexpr int BK_BYTES = 128;  // bytes of K per stage row
-constexpr int NUM_THREADS = 192;
 constexpr int TMEM_COLS = 512;
 constexpr int kStageRowWords = 36;  // per-lane staging row: 32 values + 4 words of padding
                                     // (16-byte stores of 8 lanes hit 8 distinct bank quads)
@@ -279,19 +278,21 @@ __device__ __forceinline__ bool pool_check_due(int64_t li) {
   return li < 8 ? (li == 0 || li == 1 || li == 3 || li == 7) : ((li & 7) == 7);
 }
 
-template <bool kI8, int kMode, int R, bool k2Sm>
-__global__ void __launch_bounds__(NUM_THREADS, 1)
+template <bool kI8, int kMode, int R, bool k2Sm, int kEpi>
+__global__ void __launch_bounds__(64 + 32 * kEpi, 1)
     gemm_scan_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const ScanArgs a) {
   using G = Geo<k2Sm, cols_of(kMode)>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  constexpr int n_epi = kEpi;  // epilogue warps: 4, or 8 (two per TMEM lane quarter)
+  const int n_stages = a.stages;
   uint8_t* stages = smem;
-  float* s_cols = (float*)(smem + (size_t)G::kStages * G::kStageBytes);  // [4 warps][kCols][256]
-  uint32_t* stage_rows = (uint32_t*)(s_cols + 4 * cols_of(kMode) * 256);  // [4 warps][32 lanes][36]
-  uint64_t* full = (uint64_t*)(stage_rows + 4 * 32 * kStageRowWords);
-  uint64_t* empty = full + G::kStages;
-  uint64_t* tfull = empty + G::kStages;
+  float* s_cols = (float*)(smem + (size_t)n_stages * G::kStageBytes);  // [epilogue warps][kCols][256]
+  uint32_t* stage_rows = (uint32_t*)(s_cols + n_epi * cols_of(kMode) * 256);  // [epilogue warps][32][36]
+  uint64_t* full = (uint64_t*)(stage_rows + n_epi * 32 * kStageRowWords);
+  uint64_t* empty = full + n_stages;
+  uint64_t* tfull = empty + n_stages;
   uint64_t* tempty = tfull + 2;
   uint32_t* tmem_slot = (uint32_t*)(tempty + 2);
   volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
@@ -306,13 +307,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   const int64_t p1 = total * (unit + 1) / units;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < G::kStages; s++) {
+    for (int s = 0; s < n_stages; s++) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
     for (int b = 0; b < 2; b++) {
       mbar_init(&tfull[b], 1);
-      mbar_init(&tempty[b], k2Sm ? 8 : 4);  // the epilogue warps of every CTA of the MMA
+      mbar_init(&tempty[b], k2Sm ? 2 * n_epi : n_epi);  // the epilogue warps of every CTA of the MMA
     }
     *abort_flag = 0;
     fence_mbar_init();
@@ -376,7 +377,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           }
           used |= 1u << stage;
           last_par = (last_par & ~(1u << stage)) | (phase << stage);
-          if (++stage == G::kStages) {
+          if (++stage == n_stages) {
             stage = 0;
             phase ^= 1u;
           }
@@ -387,7 +388,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const uint64_t until = globaltimer_ns() + a.timeout_ns;
         for (;;) {
           bool all = true;
-          for (int s = 0; s < G::kStages; s++)
+          for (int s = 0; s < n_stages; s++)
             if ((used >> s) & 1u)
               if (!mbar_try_wait(&full[s], (last_par >> s) & 1u)) all = false;
           if (all || globaltimer_ns() > until) break;
@@ -439,7 +440,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             mma_commit_pair_mc(&empty[stage], (uint16_t)0x3);
           else
             mma_commit(&empty[stage]);
-          if (++stage == G::kStages) {
+          if (++stage == n_stages) {
             stage = 0;
             phase ^= 1u;
           }
@@ -452,8 +453,16 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       }
     }
   } else {
-    // ---------------- epilogue: warps 2..5, one query (TMEM lane) per thread
+    // ---------------- epilogue: warps 2.., one query (TMEM lane) per thread; with 8 epilogue
+    // warps two share each TMEM lane quarter, warp 2 + i taking the first half of every tile's
+    // columns and warp 6 + i the second, each with its own candidate stream per query
     const int quarter = warp & 3;
+    const int halves = n_epi >> 2;
+    const int half = (warp - 2) >> 2;
+    const int gpw = (BN / 32) / halves;  // 32-column groups per warp
+    const int g_lo = half * gpw;
+    const int nstreams = units * halves;
+    const int my_stream = unit * halves + half;
     const int row_in_block = (int)rank * 128 + quarter * 32 + lane;
     const int Qp = a.num_mblocks * G::kQueriesPerTile;
     const uint32_t tempty0 = k2Sm ? mapa_shared(smem_addr(&tempty[0]), 0) : smem_addr(&tempty[0]);
@@ -475,7 +484,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       if (kMode != kEpiF16Plain && kMode != kEpiBqHamming && nt != cols_nt) {
         cols_nt = nt;
         __syncwarp();
-        for (int i = lane; i < BN; i += 32) {
+        for (int i = g_lo * 32 + lane; i < (g_lo + gpw) * 32; i += 32) {
           const int64_t row = col0 + i;
           const bool in = row < a.n;
           if (kMode == kEpiF16Scaled || kMode == kEpiF16L2) {
@@ -497,7 +506,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       }
       const int q = mb * G::kQueriesPerTile + row_in_block;
       const bool active = q < a.nq;
-      const size_t sidx = (size_t)unit * Qp + (size_t)q;
+      const size_t sidx = (size_t)my_stream * Qp + (size_t)q;
       // Stream state does not depend on the accumulator: load it before waiting.
       const bool probe = a.probe != nullptr;
       const bool live = active && !probe;
@@ -539,7 +548,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * BN);
       // 32-column groups up to the last row (tile-uniform); the TMEM load of the next group is
       // in flight while the current one is processed
-      const int ngroups = (valid + 31) / 32 < BN / 32 ? (valid + 31) / 32 : BN / 32;
+      const int g_end = (valid + 31) / 32 < g_lo + gpw ? (valid + 31) / 32 : g_lo + gpw;
       auto process = [&](const uint32_t(&v)[32], int g) {
         const int c0 = g * 32;
         const float m = group_max<kMode>(v, c0, s_col, s_col2, qa, qi, a.epi, qb);
@@ -552,17 +561,17 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       };
       uint32_t va[32], vb[32];
       __syncwarp();
-      if (ngroups > 0) tmem_ld_32x32b_x32(taddr, va);
+      if (g_lo < g_end) tmem_ld_32x32b_x32(taddr + (uint32_t)(g_lo * 32), va);
 #pragma unroll 1
-      for (int g = 0; g < ngroups; g += 2) {
+      for (int g = g_lo; g < g_end; g += 2) {
         __syncwarp();
         tmem_ld_wait_v(va);
-        if (g + 1 < ngroups) tmem_ld_32x32b_x32(taddr + (uint32_t)((g + 1) * 32), vb);
+        if (g + 1 < g_end) tmem_ld_32x32b_x32(taddr + (uint32_t)((g + 1) * 32), vb);
         process(va, g);
-        if (g + 1 >= ngroups) break;
+        if (g + 1 >= g_end) break;
         __syncwarp();
         tmem_ld_wait_v(vb);
-        if (g + 2 < ngroups) tmem_ld_32x32b_x32(taddr + (uint32_t)((g + 2) * 32), va);
+        if (g + 2 < g_end) tmem_ld_32x32b_x32(taddr + (uint32_t)((g + 2) * 32), va);
         process(vb, g + 1);
       }
       tc_fence_before();
@@ -588,7 +597,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const uint64_t* arr = a.pool_j == 1 ? a.top1 : a.top2;
         __syncwarp();
         int c = 0;
-        for (int u = 0; u < units; u++) c += __ldcg((const unsigned long long*)arr + (size_t)u * Qp + q) >= mine;
+        for (int u = 0; u < nstreams; u++) c += __ldcg((const unsigned long long*)arr + (size_t)u * Qp + q) >= mine;
         if (active && mine != 0 && c >= a.pool_g)
           atomicMax((unsigned long long*)&a.floor[q], (unsigned long long)mine);
       }
@@ -598,7 +607,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       for (int mb = 0; mb < a.num_mblocks; mb++) {
         const int q = mb * G::kQueriesPerTile + row_in_block;
         const bool active = q < a.nq;
-        const size_t sidx = (size_t)unit * Qp + (size_t)q;
+        const size_t sidx = (size_t)my_stream * Qp + (size_t)q;
         uint64_t* base = a.bufs + sidx * (size_t)a.C;
         uint32_t cnt = active ? a.cnts[sidx] : 0u;
         uint64_t thr = active ? a.thrs[sidx] : ~0ull;
@@ -627,20 +636,33 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   }
 }
 
-template <bool kI8, int kMode, int R, bool k2Sm>
-cudaError_t launch_one(const CUtensorMap& tmA, const CUtensorMap& tmB, const ScanArgs& a, int grid,
+// Shared memory of one CTA with `stages` ring stages and `epi` epilogue warps.
+template <bool k2Sm, int kCols>
+constexpr size_t scan_smem(int stages, int epi) {
+  return 1024 + (size_t)stages * Geo<k2Sm, kCols>::kStageBytes + (size_t)epi * kCols * 256 * sizeof(float) +
+         (size_t)epi * 32 * kStageRowWords * sizeof(uint32_t) + 256;
+}
+
+template <bool kI8, int kMode, int R, bool k2Sm, int kEpi>
+cudaError_t launch_one(const CUtensorMap& tmA, const CUtensorMap& tmB, const ScanArgs& args, int grid,
                        cudaStream_t st) {
-  auto kern = gemm_scan_kernel<kI8, kMode, R, k2Sm>;
-  const size_t smem = Geo<k2Sm, cols_of(kMode)>::kSmem;
+  auto kern = gemm_scan_kernel<kI8, kMode, R, k2Sm, kEpi>;
+  using G = Geo<k2Sm, cols_of(kMode)>;
+  ScanArgs a = args;
+  // the deepest ring that fits next to the epilogue warps' staging (at most the 4-warp depth)
+  a.stages = G::kStages;
+  while (a.stages > 2 && scan_smem<k2Sm, cols_of(kMode)>(a.stages, kEpi) > 232448) a.stages--;
+  const size_t smem = scan_smem<k2Sm, cols_of(kMode)>(a.stages, kEpi);
+  const int threads = 64 + 32 * kEpi;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   if (!k2Sm) {
-    kern<<<grid, NUM_THREADS, smem, st>>>(tmA, tmB, a);
+    kern<<<grid, threads, smem, st>>>(tmA, tmB, a);
     return cudaGetLastError();
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)grid);
-  cfg.blockDim = dim3(NUM_THREADS);
+  cfg.blockDim = dim3(threads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
@@ -656,12 +678,21 @@ cudaError_t launch_one(const CUtensorMap& tmA, const CUtensorMap& tmB, const Sca
 template <bool kI8, int kMode, bool k2Sm>
 cudaError_t launch_mode(const CUtensorMap& tmA, const CUtensorMap& tmB, const ScanArgs& a, int grid,
                         int R, cudaStream_t st) {
+  if (a.epi_warps == 8) {
+    // built only where gemm_scan_epi8 says so: fp16 scans with 17-row streams (the 320-thread
+    // block leaves 168 registers a thread, enough for R = 17 with 16-36 spilled bytes)
+    if constexpr (!kI8) {
+      if (R == 17) return launch_one<kI8, kMode, 17, k2Sm, 8>(tmA, tmB, a, grid, st);
+    }
+    return cudaErrorInvalidValue;
+  }
+  if (a.epi_warps != 4) return cudaErrorInvalidValue;
   switch (R) {
-    case 3: return launch_one<kI8, kMode, 3, k2Sm>(tmA, tmB, a, grid, st);
-    case 5: return launch_one<kI8, kMode, 5, k2Sm>(tmA, tmB, a, grid, st);
-    case 9: return launch_one<kI8, kMode, 9, k2Sm>(tmA, tmB, a, grid, st);
-    case 17: return launch_one<kI8, kMode, 17, k2Sm>(tmA, tmB, a, grid, st);
-    case 33: return launch_one<kI8, kMode, 33, k2Sm>(tmA, tmB, a, grid, st);
+    case 3: return launch_one<kI8, kMode, 3, k2Sm, 4>(tmA, tmB, a, grid, st);
+    case 5: return launch_one<kI8, kMode, 5, k2Sm, 4>(tmA, tmB, a, grid, st);
+    case 9: return launch_one<kI8, kMode, 9, k2Sm, 4>(tmA, tmB, a, grid, st);
+    case 17: return launch_one<kI8, kMode, 17, k2Sm, 4>(tmA, tmB, a, grid, st);
+    case 33: return launch_one<kI8, kMode, 33, k2Sm, 4>(tmA, tmB, a, grid, st);
     default: return cudaErrorInvalidValue;
   }
 }
@@ -716,6 +747,10 @@ int gemm_scan_units(int64_t ntiles, int num_mblocks, int num_sms, bool two_sm) {
   int64_t u = two_sm ? num_sms / 2 : num_sms;
   if (u > total) u = total;
   return (int)(u < 1 ? 1 : u);
+}
+
+bool gemm_scan_epi8(int mode, int R) {
+  return (mode == kEpiF16Plain || mode == kEpiF16Scaled || mode == kEpiF16L2) && R == 17;
 }
 
 int gemm_scan_stream_R(int K) {

@@ -69,6 +69,11 @@ struct ScanArgs {
   // search keeping more candidates than one stream holds takes the next keys below the last
   // pass's smallest (no pilot sweep then: its group maxima ignore the bound).
   const uint64_t* ceil = nullptr;
+  // Epilogue warps per CTA: 4 (one per TMEM lane quarter, every column of a tile) or 8 (two per
+  // lane quarter, each half of the columns, each with its own candidate streams: units * 2
+  // streams per query).  stages: depth of the TMA ring (set by the launcher).
+  int epi_warps = 4;
+  int stages = 0;
   int32_t* err;       // device error word
   uint64_t timeout_ns;
   EpiParams epi;
@@ -81,6 +86,10 @@ constexpr int gemm_scan_query_block(bool two_sm) { return two_sm ? 256 : 128; }
 constexpr int gemm_scan_db_box(bool two_sm) { return two_sm ? 128 : 256; }
 int gemm_scan_units(int64_t ntiles, int num_mblocks, int num_sms, bool two_sm);
 int gemm_scan_stream_R(int K);
+// Whether the 8-epilogue-warp build exists for this mode and stream size: fp16 scans with
+// R = 17 (544-key streams), where the per-tile top-K work outweighs the smaller ring and the
+// 168-register cap of a 320-thread block.
+bool gemm_scan_epi8(int mode, int R);
 // One bounded wait that nothing completes (the scan's give-up path alone): err gets kDevWaitTimeout.
 cudaError_t launch_wait_probe(uint64_t timeout_ns, int32_t* err, cudaStream_t st);
 cudaError_t launch_gemm_scan(int mode, const CUtensorMap& tmA, const CUtensorMap& tmB,

@@ -180,6 +180,18 @@ bool use_pilot() {
   return v;
 }
 
+// Epilogue warps of the tcgen05 scan: 8 (two per TMEM lane quarter, each half of a tile's
+// columns) where that build exists -- fp16 scans with 544-key streams (the FP16 k = 100 scan:
+// 15 % faster than 4) -- else 4.  VX_EPI_WARPS=4 picks 4 there too.
+int epi_warps_for(int mode, int K) {
+  static const int forced = [] {
+    const char* e = getenv("VX_EPI_WARPS");
+    return (e && (*e == '4' || *e == '8')) ? *e - '0' : 0;
+  }();
+  if (!gemm_scan_epi8(mode, gemm_scan_stream_R(K))) return 4;
+  return forced ? forced : 8;
+}
+
 // Pooled admission floors (ScanArgs::top1) unless VX_SCAN_POOL=0.
 bool use_pool() {
   static const bool v = [] {
@@ -463,13 +475,15 @@ void scan_and_merge(int mode, const CUtensorMap& tmq, const CUtensorMap& tmrows,
   a.probe_groups = 0;
   // Pooled floors need K <= 2 * (streams per query); each stream then contributes its best
   // (pool_j = 1) or second best (pool_j = 2) key.
+  // candidate streams per query: one per unit and epilogue half (8 epilogue warps: two)
+  const int streams = units * (a.epi_warps / 4);
   a.top1 = a.top2 = nullptr;
-  a.pool_j = a.K <= units ? 1 : (a.K <= 2 * units ? 2 : 0);
+  a.pool_j = a.K <= streams ? 1 : (a.K <= 2 * streams ? 2 : 0);
   a.pool_g = a.pool_j ? (a.K + a.pool_j - 1) / a.pool_j : 0;
   if (a.pool_j && tops && use_pool()) {
     a.top1 = tops;
-    a.top2 = tops + (size_t)units * Qp;
-    VX_CUDA(cudaMemsetAsync(tops, 0, (size_t)2 * units * Qp * 8, st));
+    a.top2 = tops + (size_t)streams * Qp;
+    VX_CUDA(cudaMemsetAsync(tops, 0, (size_t)2 * streams * Qp * 8, st));
   }
   if (probe && !a.ceil && a.n > 2 * kPilotRows && a.K <= kPilotRows / 32 && use_pilot()) {
     // probe sweep over the first kPilotRows rows: group maxima only, then the floors
@@ -483,11 +497,11 @@ void scan_and_merge(int mode, const CUtensorMap& tmq, const CUtensorMap& tmrows,
     const int punits = (int)std::min<int64_t>((int64_t)p.ntiles * a.num_mblocks, units);
     VX_TIMED(VX_PROF_PILOT, st, 2, launch_probe_sweep(mode, tmq, tmrows, p, punits, R, two_sm, floor, a.K, st));
   }
-  VX_CUDA(cudaMemsetAsync(a.cnts, 0, (size_t)units * Qp * 4, st));
-  VX_CUDA(cudaMemsetAsync(a.thrs, 0, (size_t)units * Qp * 8, st));
+  VX_CUDA(cudaMemsetAsync(a.cnts, 0, (size_t)streams * Qp * 4, st));
+  VX_CUDA(cudaMemsetAsync(a.thrs, 0, (size_t)streams * Qp * 8, st));
   VX_TIMED(VX_PROF_GEMM_SCAN, st, 1, launch_gemm_scan(mode, tmq, tmrows, a, units, R, two_sm, st));
   VX_TIMED(VX_PROF_MERGE, st, 1,
-           launch_merge_streams(a.bufs, a.cnts, units, a.nq, Qp, a.C, a.K, cand, cand_cnt, st, floor));
+           launch_merge_streams(a.bufs, a.cnts, streams, a.nq, Qp, a.C, a.K, cand, cand_cnt, st, floor));
 }
 
 // One approximate pass with Kc candidates per query followed by the exact re-score; queries
@@ -515,14 +529,15 @@ int gemm_exact_pass(vx_index* ix, const float* dq, int nq, int k, int Kc, int32_
   // query chunk sized by the scratch budget
   const bool two_sm = gemm_two_sm();
   const int QB = gemm_scan_query_block(two_sm);
-  const int U0 = gemm_scan_units(ntiles, 1 << 20, ix->num_sms, two_sm);
+  const int EW = epi_warps_for(mode, Kc);
+  const int U0 = gemm_scan_units(ntiles, 1 << 20, ix->num_sms, two_sm) * (EW / 4);  // streams per query
   int64_t qch = (int64_t)(scratch_budget() / ((size_t)U0 * (C * 8 + 12)));
   qch = std::max<int64_t>(QB, qch / QB * QB);
   // Buffers are sized once for the largest chunk and reused, so repeated calls draw blocks
   // of one size from the stream-ordered pool.
   const int qmax = (int)std::min<int64_t>(qch, std::max(nq, 1));
   const int QpMax = (qmax + QB - 1) / QB * QB;
-  const int unitsMax = gemm_scan_units(ntiles, QpMax / QB, ix->num_sms, two_sm);
+  const int unitsMax = gemm_scan_units(ntiles, QpMax / QB, ix->num_sms, two_sm) * (EW / 4);  // streams
   const int nchunks = (int)((nq + qch - 1) / qch);
   Scratch S(st);
   int32_t* d_err = S.alloc<int32_t>(1);
@@ -570,6 +585,7 @@ int gemm_exact_pass(vx_index* ix, const float* dq, int nq, int k, int Kc, int32_
     a.thrs = thrs;
     a.err = d_err;
     a.timeout_ns = wait_timeout_ns();
+    a.epi_warps = EW;
     a.epi.xnorm = ix->rowscale;
     a.epi.rowsq = ix->rowsq;
     a.epi.qscale = qnorm;
@@ -684,9 +700,6 @@ int search_quantized_scan(vx_index* ix, const float* dq, int nq, int K, int k_ou
     const int64_t ntiles = (ix->n + 255) / 256;
     const bool two_sm = gemm_two_sm();
     const int QB = gemm_scan_query_block(two_sm);
-    const int U0 = gemm_scan_units(ntiles, 1 << 20, ix->num_sms, two_sm);
-    int64_t qch = (int64_t)(scratch_budget() / ((size_t)U0 * (C * 8 + 12)));
-    qch = std::max<int64_t>(QB, qch / QB * QB);
     const int mode = bq ? kEpiBqHamming
                      : bbq ? (ix->metric == VX_EUCLIDEAN ? kEpiBbqL2
                               : ix->metric == VX_MAXIMUM_INNER_PRODUCT ? kEpiBbqMip
@@ -697,10 +710,14 @@ int search_quantized_scan(vx_index* ix, const float* dq, int nq, int K, int k_ou
                                                               : kEpiSq8Dot;
     const Sq8Consts kc =
         (bq || bbq) ? Sq8Consts{0.f, 0.f, 0.f, 0.f, 0.f} : sq8_consts(ix->min_q, ix->max_q, ix->sq_max);
+    const int EW = epi_warps_for(mode, KP);
+    const int U0 = gemm_scan_units(ntiles, 1 << 20, ix->num_sms, two_sm) * (EW / 4);  // streams per query
+    int64_t qch = (int64_t)(scratch_budget() / ((size_t)U0 * (C * 8 + 12)));
+    qch = std::max<int64_t>(QB, qch / QB * QB);
     // sized once for the largest chunk and reused by every chunk
     const int qmax = (int)std::min<int64_t>(qch, std::max(nq, 1));
     const int QpMax = (qmax + QB - 1) / QB * QB;
-    const int unitsMax = gemm_scan_units(ntiles, QpMax / QB, ix->num_sms, two_sm);
+    const int unitsMax = gemm_scan_units(ntiles, QpMax / QB, ix->num_sms, two_sm) * (EW / 4);  // streams
     int8_t* qcodes = S.alloc<int8_t>((size_t)QpMax * ix->Dp8);
     float* qcorr = S.alloc<float>(QpMax);
     int32_t* qsq = S.alloc<int32_t>(QpMax);
@@ -749,6 +766,7 @@ int search_quantized_scan(vx_index* ix, const float* dq, int nq, int K, int k_ou
       a.thrs = thrs;
       a.err = d_err;
       a.timeout_ns = wait_timeout_ns();
+      a.epi_warps = EW;
       a.epi.xnorm = nullptr;
       a.epi.rowsq = nullptr;
       a.epi.qscale = qcorr;
