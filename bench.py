@@ -953,8 +953,40 @@ def run_bq(args, rank, world, local, dev, barrier, max_over_ranks, tc_sustained,
                "sample": f"64 queries over the same {n:,}-row index ({dt:.1f} s)"}
         e2e = e2e_host(args, lambda: a.scan_candidates_arrays(qh, k), nq, nq * dim * 4, nq * (k * 8 + 4))
     a.close()
+    # The same rows as an index above the int8 operand budget: packed bits alone on the device
+    # (128 B per row instead of 1,152), the tensor scan over row windows whose +-1 operand is
+    # expanded at search time (VX_BQ_WINDOW_BYTES, default 4 GiB: 4,194,304 rows per window).
+    saved = os.environ.get("VX_BQ_TENSOR_BYTES")
+    os.environ["VX_BQ_TENSOR_BYTES"] = "0"
+    try:
+        aw = vx.QuantizedFlatScanAdapter(device=local)
+        aw.build_bq(words_h, dim, vx.SimilarityFunction.DOT_PRODUCT)
+    finally:
+        if saved is None:
+            del os.environ["VX_BQ_TENSOR_BYTES"]
+        else:
+            os.environ["VX_BQ_TENSOR_BYTES"] = saved
+
+    def wstep():
+        ids, sc, cnt = aw.scan_candidates_device(q, k)
+        return ids if world == 1 else gather_and_merge(ids, sc, cnt, offs_dev, k)[0]
+
+    wms, wkms, wbr = _timed_scan(args, world, dev, barrier, max_over_ranks, wstep, "gemm_scan")
+    wpar = parity(aw.scan_candidates_arrays(qh[:64], k), ref, True, n) if check else None
+    aw.close()
     del words_h
     rows = hi - lo
+    dp8w = (dim + 127) // 128 * 128
+    wach = 2.0 * nq * rows * dp8w / (wkms / 1e3) / 1e12 if wkms > 0 else None
+    windowed = {"value": nq / (wms / 1e3), "unit": "queries/s", "ms_per_step": wms,
+                "config": {"index_bytes_per_row": dim // 8, "window_bytes": 4 << 30,
+                           "note": "index above the int8 operand budget (VX_BQ_TENSOR_BYTES=0): bits only, "
+                                   "+-1 operand expanded per row window at search time"},
+                "roofline": {"bound": "tensor (int8)", "achieved": wach, "peak": 2.0 * tc_sustained, "unit": "TOP/s",
+                             "frac": (wach / (2.0 * tc_sustained)) if wach else None,
+                             "kernel": "gemm_scan_kernel per row window (+ the window's bit expansion)",
+                             "breakdown_ms_per_step": wbr},
+                "parity": wpar}
     if br.get("gemm_scan"):
         # tensor-core path: +-1 int8 operands, dot = D - 2h, exact int32 (2 ops per bit pair)
         dp8 = (dim + 127) // 128 * 128
@@ -1020,6 +1052,7 @@ def run_bq(args, rank, world, local, dev, barrier, max_over_ranks, tc_sustained,
         "parity": par,
         "cpu_baseline": cpu,
         "e2e": e2e,
+        "windowed": windowed,
         "bbq": bbq,
     }
 

@@ -140,17 +140,23 @@ VX_API int vx_sq4_build(int32_t device, const uint8_t* packed, const float* corr
                         int32_t dim, float min_quantile, float max_quantile, int32_t metric,
                         const float* vectors, int64_t row_stride, vx_index** out);
 /* BinaryQuantizedVectors SIGN_BIT (BinaryQuantizedVectors.java:40-107): words [n][ceil(dim/64)]
- * as produced by BinaryQuantizer.packBits + bytesToLongs (BinaryQuantizer.java:207-232). */
+ * as produced by BinaryQuantizer.packBits + bytesToLongs (BinaryQuantizer.java:207-232).  Scanned
+ * on the int8 tensor cores against a +-1 copy of the bits: kept whole (8 bytes per stored bit)
+ * within VX_BQ_TENSOR_BYTES, else expanded one row window at a time during each search (scratch
+ * of at most VX_BQ_WINDOW_BYTES); with windows off (VX_BQ_WINDOW_BYTES=0) by the popcount scan.
+ * Both budgets are read from the environment at each build. */
 VX_API int vx_bq_build(int32_t device, const uint64_t* words, int64_t n, int32_t dim, int32_t metric,
                 const float* vectors, int64_t row_stride, vx_index** out);
 /* BinaryQuantizedVectors BBQ (BinaryQuantizedVectors.java:110-275, BinaryQuantizer.java:199-270):
  * words [n][ceil(dim/64)] of the centroid-relative sign bits, corrections [n][3] =
  * (|v - c|^2, vl, width), the centroid [dim].  Scored as bbqScoreFunction does: the query
  * centred and quantised to 4 bits, rawAsymDot exactly (the 4-bit codes times a 0/1 int8 copy of
- * the bits on the int8 tensor cores, 8 bytes of device memory per stored bit, within the
- * VX_BQ_TENSOR_BYTES budget; above it, popcounts of the query's 4 bit planes), computeBbqDot and
- * the metric's transform in the Java float order.  dim <= 2048 (above 1024 the int8 operand must
- * fit VX_BQ_TENSOR_BYTES). */
+ * the bits on the int8 tensor cores: kept whole, 8 bytes of device memory per stored bit, within
+ * the VX_BQ_TENSOR_BYTES budget; above it expanded one row window at a time during each search,
+ * in scratch of at most VX_BQ_WINDOW_BYTES; with windows off (VX_BQ_WINDOW_BYTES=0), popcounts
+ * of the query's 4 bit planes), computeBbqDot and the metric's transform in the Java float order.
+ * dim <= 2048 (above 1024 only the tensor scan serves BBQ: windows must be on when the whole
+ * operand exceeds VX_BQ_TENSOR_BYTES). */
 VX_API int vx_bbq_build(int32_t device, const uint64_t* words, const float* corrections, const float* centroid,
                         int64_t n, int32_t dim, int32_t metric, const float* vectors, int64_t row_stride,
                         vx_index** out);

@@ -1,8 +1,9 @@
 """Child process for test_gpu_scan_variants.py: the scan variant is chosen by environment
 variables that the library reads once per process (VX_GEMM_1SM, VX_SCAN_PILOT, VX_SCAN_POOL,
-VX_BQ_TENSOR_BYTES, VX_ADC_GROUPED, VX_EPI_WARPS), so each variant runs in a process of its own.
+VX_BQ_TENSOR_BYTES, VX_BQ_WINDOW_BYTES, VX_ADC_GROUPED, VX_EPI_WARPS), so each variant runs in a process of its own.
 Exits 0 when FLAT, SQ8, BQ and BBQ results (or, with the argument "ivf", IVF-PQ results) match
 the oracle."""
+import os
 import sys
 
 import numpy as np
@@ -63,11 +64,15 @@ def main():
     words = O.bq_encode_all(db)
     b = vx.QuantizedFlatScanAdapter()
     b.build_bq(words, 96, vx.SimilarityFunction.DOT_PRODUCT)
-    got = b.scan_candidates(q, 100)
-    ids, sc, cnt = O.bq_search(words, 96, q, O.DOT_PRODUCT, 100)
-    for i, o in enumerate(got):
-        assert list(o.ordinals) == list(ids[i, : cnt[i]]), f"bq query {i}"
-        assert np.array_equal(o.scores, sc[i, : cnt[i]]), f"bq query {i} scores"
+    # k = 1,200: wider than one candidate stream (1,023 keys), so the tensor scan takes two passes
+    # (the popcount scan keeps up to 1,023 keys and refuses it)
+    popcount = os.environ.get("VX_BQ_TENSOR_BYTES") == "0" and os.environ.get("VX_BQ_WINDOW_BYTES") == "0"
+    for k in (100,) if popcount else (100, 1200):
+        got = b.scan_candidates(q, k)
+        ids, sc, cnt = O.bq_search(words, 96, q, O.DOT_PRODUCT, k)
+        for i, o in enumerate(got):
+            assert list(o.ordinals) == list(ids[i, : cnt[i]]), f"bq k={k} query {i}"
+            assert np.array_equal(o.scores, sc[i, : cnt[i]]), f"bq k={k} query {i} scores"
     cent = db.mean(0).astype(np.float32)
     bw, bc = O.bbq_encode_all(db, cent)
     for metric in (0, 2):

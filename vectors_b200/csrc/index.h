@@ -43,6 +43,9 @@ struct vx_index {
   // BBQ on the int8 tensor-core scan (with codes8 = the 0/1 bits): per-row epilogue records
   // (vl, width, vl * D + width * pop, |v - c| for COSINE or |v - c|^2)
   float4* bbq_epi = nullptr;
+  // BQ / BBQ above the int8 operand's budget: the tensor-core scan expands the bits of one row
+  // window at a time (codes8 stays null)
+  bool bq_windows = false;
   // IVF-PQ
   float* cent = nullptr;
   int nlist = 0;

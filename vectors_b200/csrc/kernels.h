@@ -74,6 +74,12 @@ cudaError_t launch_pass_ceilings(const uint64_t* keys, const uint32_t* cnt, int 
                                  cudaStream_t st);
 cudaError_t launch_pass_append(uint64_t* keys, uint32_t* cnt, int nq, int K, int got, const uint64_t* keys2,
                                const uint32_t* cnt2, int K2, cudaStream_t st);
+// Row windows of a BQ / BBQ scan (merge.cu): the best K keys so far (run: global ordinals;
+// null on the first window) merged with one window's sorted keys (ordinals local to the window,
+// shifted by base) into out; seed[q] = the next window's admission floor.
+cudaError_t launch_window_merge(const uint64_t* run, const uint32_t* run_cnt, const uint64_t* win,
+                                const uint32_t* win_cnt, int nq, int K, uint32_t base, uint64_t* out,
+                                uint32_t* out_cnt, uint64_t* seed, cudaStream_t st);
 cudaError_t launch_merge_shards(int nshards, const int64_t* offsets, const int32_t* sids,
                                 const float* ssc, const int32_t* scnt, int kin, int nq, int k,
                                 int32_t* ids, float* scores, int32_t* counts, cudaStream_t st);

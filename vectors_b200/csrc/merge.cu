@@ -292,6 +292,49 @@ cudaError_t launch_pass_append(uint64_t* keys, uint32_t* cnt, int nq, int K, int
   return cudaGetLastError();
 }
 
+// Row windows: both inputs hold a query's keys in descending order; a window key's ordinal is
+// local, and make_key stores 0xFFFFFFFF - id, so key - base carries the ordinal id + base.  The
+// windows come in ordinal order, so a later row whose score equals the K-th kept key's ranks
+// below it (TopK.select's ordinal tie rule): seed (the K-th key with every id bit set) admits in
+// the next window only higher scores (and local ordinal 0 at an equal score, which the next
+// merge ranks correctly).  One thread per query.
+__global__ void window_merge_kernel(const uint64_t* __restrict__ run, const uint32_t* __restrict__ run_cnt,
+                                    const uint64_t* __restrict__ win, const uint32_t* __restrict__ win_cnt, int nq,
+                                    int K, uint32_t base, uint64_t* __restrict__ out, uint32_t* __restrict__ out_cnt,
+                                    uint64_t* __restrict__ seed) {
+  const int q = blockIdx.x * blockDim.x + threadIdx.x;
+  if (q >= nq) return;
+  const uint32_t cr = run ? min(run_cnt[q], (uint32_t)K) : 0u;
+  const uint32_t cw = min(win_cnt[q], (uint32_t)K);
+  const uint64_t* r = run + (size_t)q * K;
+  const uint64_t* w = win + (size_t)q * K;
+  uint64_t* o = out + (size_t)q * K;
+  uint32_t i = 0, j = 0, n = 0;
+  uint64_t a = cr ? r[0] : kEmptyKey;
+  uint64_t b = cw ? w[0] - base : kEmptyKey;
+  while (n < (uint32_t)K && (i < cr || j < cw)) {
+    if (i < cr && (j >= cw || a > b)) {
+      o[n++] = a;
+      a = ++i < cr ? r[i] : kEmptyKey;
+    } else {
+      o[n++] = b;
+      b = ++j < cw ? w[j] - base : kEmptyKey;
+    }
+  }
+  for (uint32_t t = n; t < (uint32_t)K; t++) o[t] = kEmptyKey;
+  out_cnt[q] = n;
+  seed[q] = n == (uint32_t)K ? (o[K - 1] | 0xFFFFFFFFull) : 0ull;
+}
+
+cudaError_t launch_window_merge(const uint64_t* run, const uint32_t* run_cnt, const uint64_t* win,
+                                const uint32_t* win_cnt, int nq, int K, uint32_t base, uint64_t* out,
+                                uint32_t* out_cnt, uint64_t* seed, cudaStream_t st) {
+  if (nq <= 0) return cudaSuccess;
+  window_merge_kernel<<<(nq + 127) / 128, 128, 0, st>>>(run, run_cnt, win, win_cnt, nq, K, base, out, out_cnt,
+                                                        seed);
+  return cudaGetLastError();
+}
+
 // Cross-shard merge: shard s contributes shard_counts[s*nq+q] (ordinal, score) pairs for
 // query q at [(s*nq+q)*kin]; ordinals are shifted by offsets[s].  Output: the k best by
 // (score desc, ordinal asc), the canonical order of TopK.select.

@@ -249,23 +249,33 @@ Sq8Consts sq8_consts(float min_q, float max_q, int max_value) {
   return k;
 }
 
-// One thread per 4 output bytes of a row (Dp8 is a multiple of 128, so of 4).
+// Four bits -> four bytes: bit j of b lands in bit 0 of byte j (b * 0x00204081 places copies of b
+// at bit offsets 0, 7, 14 and 21, so bit j of the copy at 7j sits at bit 8j).
+__device__ __forceinline__ uint32_t spread4(uint32_t b) { return (b * 0x00204081u) & 0x01010101u; }
+
+// One thread per 16 output bytes of a row (Dp8 is a multiple of 128, so of 16): the 16 bits at
+// column c0 of one word, set -> 1, clear -> `clear` (-1 or 0), columns >= dim -> 0; one 16-byte
+// store.  Row windows of the tensor scan run this at search time, so it is a plain stream
+// (8 bytes of bits read per 128 bytes written, the bit word shared by four threads through L1).
 __global__ void bq_words_to_i8_kernel(const uint64_t* __restrict__ words, int64_t n, int nwp, int dim,
                                       int Dp8, int8_t clear, int8_t* __restrict__ dst) {
   const int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
-  const int per_row = Dp8 / 4;
+  const int per_row = Dp8 / 16;
   if (t >= n * per_row) return;
   const int64_t r = t / per_row;
-  const int c0 = (int)(t - r * per_row) * 4;
-  uint32_t out = 0;
+  const int c0 = (int)(t - r * per_row) * 16;
+  const int nvalid = min(max(dim - c0, 0), 16);
+  const uint32_t vm = nvalid >= 16 ? 0xFFFFu : ((1u << nvalid) - 1u);
+  const uint32_t bits = nvalid > 0 ? (uint32_t)(words[r * nwp + (c0 >> 6)] >> (c0 & 63)) & vm : 0u;
+  const uint32_t fill = (uint32_t)(uint8_t)clear;  // 0xFF or 0: per byte, no carries below
+  uint32_t o[4];
 #pragma unroll
   for (int j = 0; j < 4; j++) {
-    const int c = c0 + j;
-    int8_t v = 0;
-    if (c < dim) v = ((words[r * nwp + (c >> 6)] >> (c & 63)) & 1ull) ? (int8_t)1 : clear;
-    out |= (uint32_t)(uint8_t)v << (8 * j);
+    const uint32_t m = spread4((bits >> (4 * j)) & 0xFu);
+    const uint32_t valid = spread4((vm >> (4 * j)) & 0xFu);
+    o[j] = m | ((m ^ valid) * fill);  // set: 0x01; clear and valid: fill; past dim: 0
   }
-  reinterpret_cast<uint32_t*>(dst + r * Dp8)[c0 / 4] = out;
+  reinterpret_cast<uint4*>(dst + r * Dp8)[c0 / 16] = make_uint4(o[0], o[1], o[2], o[3]);
 }
 
 __global__ void bq_queries_to_i8_kernel(const float* __restrict__ q, int nq, int dim, int Dp8,
@@ -281,7 +291,7 @@ __global__ void bq_queries_to_i8_kernel(const float* __restrict__ q, int nq, int
 cudaError_t launch_bq_words_to_i8(const uint64_t* words, int64_t n, int nwp, int dim, int Dp8, int8_t* dst,
                                   cudaStream_t st, bool zero_one) {
   if (n <= 0) return cudaSuccess;
-  const int64_t total = n * (Dp8 / 4);
+  const int64_t total = n * (Dp8 / 16);
   bq_words_to_i8_kernel<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(words, n, nwp, dim, Dp8,
                                                                          zero_one ? (int8_t)0 : (int8_t)-1, dst);
   return cudaGetLastError();

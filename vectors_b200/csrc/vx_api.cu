@@ -202,13 +202,26 @@ bool use_pool() {
 }
 
 // BQ indexes also keep a +-1 int8 copy of the bits (8x the storage) for the tensor-core
-// Hamming scan while it fits VX_BQ_TENSOR_BYTES (default 64 GiB; 0 keeps the popcount scan).
+// Hamming scan while it fits VX_BQ_TENSOR_BYTES (default 64 GiB), read at each build.
 uint64_t bq_tensor_budget() {
-  static const uint64_t v = [] {
-    const char* e = getenv("VX_BQ_TENSOR_BYTES");
-    return (e && *e) ? (uint64_t)strtoull(e, nullptr, 10) : (uint64_t)64 << 30;
-  }();
-  return v;
+  const char* e = getenv("VX_BQ_TENSOR_BYTES");
+  return (e && *e) ? (uint64_t)strtoull(e, nullptr, 10) : (uint64_t)64 << 30;
+}
+
+// BQ / BBQ indexes above that budget keep only their bits (and BBQ's 16-byte epilogue records)
+// and expand one window of rows at a time to the int8 operand, in a search-time scratch buffer of
+// at most VX_BQ_WINDOW_BYTES (default 4 GiB; 0 leaves such indexes on the popcount scans), read at
+// each build (whether windows are used) and search (their size).
+uint64_t bq_window_bytes() {
+  const char* e = getenv("VX_BQ_WINDOW_BYTES");
+  return (e && *e) ? (uint64_t)strtoull(e, nullptr, 10) : (uint64_t)4 << 30;
+}
+
+// Rows per window: whole 256-row tiles within the window budget (at least one tile).
+int64_t bq_window_rows(int64_t n, int Dp8) {
+  int64_t w = (int64_t)(bq_window_bytes() / (uint64_t)Dp8) / 256 * 256;
+  w = std::max<int64_t>(w, 256);
+  return std::min<int64_t>(w, n);
 }
 
 // IVF-PQ scans use the grouped ADC kernel where the shape allows unless VX_ADC_GROUPED=0.
@@ -464,11 +477,17 @@ cudaError_t launch_probe_sweep(int mode, const CUtensorMap& tmq, const CUtensorM
   return e;
 }
 
+// seed (nullable, device [Qp]): initial admission floors known from earlier row windows; the
+// probe sweep is skipped then.
 void scan_and_merge(int mode, const CUtensorMap& tmq, const CUtensorMap& tmrows, ScanArgs a,
                     int units, int R, int Qp, uint64_t* floor, uint64_t* tops, float* probe,
-                    uint64_t* cand, uint32_t* cand_cnt, cudaStream_t st) {
+                    uint64_t* cand, uint32_t* cand_cnt, cudaStream_t st, const uint64_t* seed = nullptr) {
   const bool two_sm = gemm_two_sm();
-  VX_CUDA(cudaMemsetAsync(floor, 0, (size_t)Qp * 8, st));
+  if (seed) {
+    VX_CUDA(cudaMemcpyAsync(floor, seed, (size_t)Qp * 8, cudaMemcpyDeviceToDevice, st));
+  } else {
+    VX_CUDA(cudaMemsetAsync(floor, 0, (size_t)Qp * 8, st));
+  }
   a.floor = floor;
   a.m_major = 0;
   a.probe = nullptr;
@@ -485,7 +504,7 @@ void scan_and_merge(int mode, const CUtensorMap& tmq, const CUtensorMap& tmrows,
     a.top2 = tops + (size_t)streams * Qp;
     VX_CUDA(cudaMemsetAsync(tops, 0, (size_t)2 * streams * Qp * 8, st));
   }
-  if (probe && !a.ceil && a.n > 2 * kPilotRows && a.K <= kPilotRows / 32 && use_pilot()) {
+  if (probe && !seed && !a.ceil && a.n > 2 * kPilotRows && a.K <= kPilotRows / 32 && use_pilot()) {
     // probe sweep over the first kPilotRows rows: group maxima only, then the floors
     ScanArgs p = a;
     p.n = kPilotRows;
@@ -675,8 +694,10 @@ int search_gemm_exact(vx_index* ix, const float* dq, int nq, int k, int32_t* d_i
 }
 
 // SQ8 / SQ4 / BQ / BBQ: exact quantized scores; K best per query (optionally re-scored in fp32).
-// The int8 tensor-core scan serves every kind whose rows have an int8 operand (codes8); BQ and
-// BBQ indexes built without one (VX_BQ_TENSOR_BYTES below their size) take the popcount scans.
+// The int8 tensor-core scan serves every kind: over the whole int8 operand (codes8) where the
+// index keeps one, else (BQ / BBQ above VX_BQ_TENSOR_BYTES) over row windows expanded from the
+// bits at search time.  With windows switched off (VX_BQ_WINDOW_BYTES=0) such indexes take the
+// popcount scans.
 int search_quantized_scan(vx_index* ix, const float* dq, int nq, int K, int k_out, bool rescore,
                           int32_t* d_ids, float* d_scores, int32_t* d_counts, cudaStream_t st) {
   const int dim = ix->dim;
@@ -684,7 +705,7 @@ int search_quantized_scan(vx_index* ix, const float* dq, int nq, int K, int k_ou
   int32_t* d_err = S.alloc<int32_t>(1);
   VX_CUDA(cudaMemsetAsync(d_err, 0, 4, st));
   if (ix->kind == VX_KIND_SQ8 || ix->kind == VX_KIND_SQ4 ||
-      ((ix->kind == VX_KIND_BQ || ix->kind == VX_KIND_BBQ) && ix->codes8)) {
+      ((ix->kind == VX_KIND_BQ || ix->kind == VX_KIND_BBQ) && (ix->codes8 || ix->bq_windows))) {
     const bool bq = ix->kind == VX_KIND_BQ;    // +-1 operands, Hamming epilogue
     const bool bbq = ix->kind == VX_KIND_BBQ;  // 0/1 rows x 4-bit query codes, BBQ epilogue
     // More candidates than one stream keeps (kStreamKeysMax) are taken in passes: each later
@@ -736,11 +757,20 @@ int search_quantized_scan(vx_index* ix, const float* dq, int nq, int K, int k_ou
     uint64_t* ceil = K > KP ? S.alloc<uint64_t>(QpMax) : nullptr;
     int32_t* nflag = S.alloc<int32_t>(1);
     int32_t* flag_list = S.alloc<int32_t>(qmax);
+    // row windows: the int8 operand of win_rows rows, one window's keys, the other half of the
+    // running keys' double buffer, the floors carried between windows
+    const bool windowed = ix->bq_windows && !ix->codes8;
+    const int64_t win_rows = windowed ? bq_window_rows(ix->n, ix->Dp8) : 0;
+    int8_t* win8 = windowed ? S.alloc<int8_t>((size_t)win_rows * ix->Dp8) : nullptr;
+    uint64_t* wkeys = windowed ? S.alloc<uint64_t>((size_t)qmax * K) : nullptr;
+    uint32_t* wcnt = windowed ? S.alloc<uint32_t>(qmax) : nullptr;
+    uint64_t* keys_alt = windowed ? S.alloc<uint64_t>((size_t)qmax * K) : nullptr;
+    uint32_t* kcnt_alt = windowed ? S.alloc<uint32_t>(qmax) : nullptr;
+    uint64_t* wseed = windowed ? S.alloc<uint64_t>(QpMax) : nullptr;
     for (int q0 = 0; q0 < nq; q0 += (int)qch) {
       const int qc = (int)std::min<int64_t>(qch, nq - q0);
       const int mblocks = (qc + QB - 1) / QB;
       const int Qp = mblocks * QB;
-      const int units = gemm_scan_units(ntiles, mblocks, ix->num_sms, two_sm);
       const float* dqc = dq + (size_t)q0 * dim;
       VX_CUDA(cudaMemsetAsync(qcodes + (size_t)qc * ix->Dp8, 0, (size_t)(Qp - qc) * ix->Dp8, st));
       if (bq) {
@@ -777,23 +807,60 @@ int search_quantized_scan(vx_index* ix, const float* dq, int nq, int K, int k_ou
       a.epi.bits = dim;
       a.epi.bbq_rows = ix->bbq_epi;
       a.epi.bbq_q = qinfo;
-      if (K == KP) {
-        scan_and_merge(mode, tmq, ix->tm_codes8, a, units, R, Qp, floor, tops, probe, keys, kcnt, st);
-      } else {
-        // first pass into a KP-wide buffer, re-strided to K; then passes below the ceilings
-        scan_and_merge(mode, tmq, ix->tm_codes8, a, units, R, Qp, floor, tops, probe, keys2, kcnt2, st);
-        VX_CUDA(cudaMemcpy2DAsync(keys, (size_t)K * 8, keys2, (size_t)KP * 8, (size_t)KP * 8, qc,
+      // The K best keys of rows [0, rows) of the int8 operand behind tmrows into out: one scan,
+      // or (K wider than a stream) a first pass into a KP-wide buffer, re-strided to K, then
+      // passes below the ceilings.  seed: admission floors from earlier row windows (nullable).
+      auto select = [&](const CUtensorMap& tmrows, int64_t rows, const float4* epi_rows, const uint64_t* seed,
+                        uint64_t* out, uint32_t* out_cnt) {
+        ScanArgs w = a;
+        w.n = rows;
+        w.ntiles = (rows + 255) / 256;
+        w.epi.bbq_rows = epi_rows;
+        const int wunits = gemm_scan_units(w.ntiles, mblocks, ix->num_sms, two_sm);
+        if (K == KP) {
+          scan_and_merge(mode, tmq, tmrows, w, wunits, R, Qp, floor, tops, probe, out, out_cnt, st, seed);
+          return;
+        }
+        scan_and_merge(mode, tmq, tmrows, w, wunits, R, Qp, floor, tops, probe, keys2, kcnt2, st, seed);
+        VX_CUDA(cudaMemcpy2DAsync(out, (size_t)K * 8, keys2, (size_t)KP * 8, (size_t)KP * 8, qc,
                                   cudaMemcpyDeviceToDevice, st));
-        VX_CUDA(cudaMemcpyAsync(kcnt, kcnt2, (size_t)qc * 4, cudaMemcpyDeviceToDevice, st));
+        VX_CUDA(cudaMemcpyAsync(out_cnt, kcnt2, (size_t)qc * 4, cudaMemcpyDeviceToDevice, st));
         for (int got = KP; got < K; got += KP) {
           const int K2 = std::min(KP, K - got);
           VX_CUDA(cudaMemsetAsync(ceil, 0, (size_t)Qp * 8, st));
-          VX_LAUNCH(1, launch_pass_ceilings(keys, kcnt, qc, K, got, ceil, st));
-          ScanArgs b = a;
+          VX_LAUNCH(1, launch_pass_ceilings(out, out_cnt, qc, K, got, ceil, st));
+          ScanArgs b = w;
           b.K = K2;
           b.ceil = ceil;
-          scan_and_merge(mode, tmq, ix->tm_codes8, b, units, R, Qp, floor, tops, probe, keys2, kcnt2, st);
-          VX_LAUNCH(1, launch_pass_append(keys, kcnt, qc, K, got, keys2, kcnt2, K2, st));
+          scan_and_merge(mode, tmq, tmrows, b, wunits, R, Qp, floor, tops, probe, keys2, kcnt2, st, seed);
+          VX_LAUNCH(1, launch_pass_append(out, out_cnt, qc, K, got, keys2, kcnt2, K2, st));
+        }
+      };
+      if (!windowed) {
+        select(ix->tm_codes8, ix->n, ix->bbq_epi, nullptr, keys, kcnt);
+      } else {
+        // Row windows (BQ / BBQ above VX_BQ_TENSOR_BYTES): each window's bits are expanded to
+        // the int8 operand in a scratch buffer, scanned, and merged into the running K best;
+        // every window after the first admits only keys above the K-th best of those before.
+        const int nwin = (int)((ix->n + win_rows - 1) / win_rows);
+        VX_CUDA(cudaMemsetAsync(wseed, 0, (size_t)QpMax * 8, st));
+        const uint64_t* run = nullptr;
+        const uint32_t* run_cnt = nullptr;
+        for (int wi = 0; wi < nwin; wi++) {
+          const int64_t b0 = (int64_t)wi * win_rows;
+          const int64_t rows = std::min<int64_t>(win_rows, ix->n - b0);
+          VX_LAUNCH(1, launch_bq_words_to_i8(ix->words + (size_t)b0 * ix->nw_pad, rows, ix->nw_pad, dim, ix->Dp8,
+                                             win8, st, bbq));
+          CUtensorMap tmw;
+          make_tmap(&tmw, win8, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, ix->Dp8, rows, gemm_scan_db_box(two_sm));
+          select(tmw, rows, bbq ? ix->bbq_epi + b0 : nullptr, wi ? wseed : nullptr, wkeys, wcnt);
+          // alternate buffers so that the last window's merge lands in keys
+          const bool to_keys = (nwin - 1 - wi) % 2 == 0;
+          uint64_t* dst = to_keys ? keys : keys_alt;
+          uint32_t* dst_cnt = to_keys ? kcnt : kcnt_alt;
+          VX_LAUNCH(1, launch_window_merge(run, run_cnt, wkeys, wcnt, qc, K, (uint32_t)b0, dst, dst_cnt, wseed, st));
+          run = dst;
+          run_cnt = dst_cnt;
         }
       }
       if (rescore) {
@@ -1745,11 +1812,13 @@ int vx_bbq_build(int32_t device, const uint64_t* words, const float* corrections
     const int nwp = bq_padded_words(nw);
     if (nwp < 0) return fail(VX_ERR_UNSUPPORTED, "BBQ dimension %d exceeds 2048", dim);
     // above 1024 dimensions only the int8 tensor operand serves BBQ (the popcount kernel keeps a
-    // query's four bit planes in registers, up to 16 words each)
-    if (!bbq_supported(nwp) && n > 0 && bq_tensor_budget() < (uint64_t)n * (uint64_t)round_up(dim, 128))
+    // query's four bit planes in registers, up to 16 words each): whole, or in row windows
+    if (!bbq_supported(nwp) && n > 0 && bq_tensor_budget() < (uint64_t)n * (uint64_t)round_up(dim, 128) &&
+        bq_window_bytes() == 0)
       return fail(VX_ERR_UNSUPPORTED,
                   "BBQ above 1024 dimensions is scanned on the int8 tensor operand, which exceeds "
-                  "VX_BQ_TENSOR_BYTES here (%lld rows x %d dims)", (long long)n, dim);
+                  "VX_BQ_TENSOR_BYTES here (%lld rows x %d dims) with row windows off (VX_BQ_WINDOW_BYTES=0)",
+                  (long long)n, dim);
     if (vectors && row_stride < dim) return fail(VX_ERR_INVALID_ARGUMENT, "bad row stride");
     if (int s = check_metric(metric)) return s;
     int nsms = 0;
@@ -1777,15 +1846,21 @@ int vx_bbq_build(int32_t device, const uint64_t* words, const float* corrections
         VX_CUDA(cudaDeviceSynchronize());
         // 0/1 int8 operand and epilogue records for the tensor-core scan (8 bytes per bit)
         const int Dp8 = (int)round_up(dim, 128);
-        if (bq_tensor_budget() >= (uint64_t)n * Dp8) {
+        const bool whole = bq_tensor_budget() >= (uint64_t)n * Dp8;
+        if (whole || bq_window_bytes() > 0) {
+          // the epilogue records always; the operand itself whole, or per row window at search time
           ix->Dp8 = Dp8;
-          ix->codes8 = dev_alloc<int8_t>(ix, (size_t)n * Dp8);
           ix->bbq_epi = dev_alloc<float4>(ix, (size_t)n);
-          VX_LAUNCH(1, launch_bq_words_to_i8(ix->words, n, nwp, dim, Dp8, ix->codes8, 0, true));
           VX_LAUNCH(1, launch_bbq_epi_rows(ix->bbq_rows, n, dim, metric, ix->bbq_epi, 0));
+          if (whole) {
+            ix->codes8 = dev_alloc<int8_t>(ix, (size_t)n * Dp8);
+            VX_LAUNCH(1, launch_bq_words_to_i8(ix->words, n, nwp, dim, Dp8, ix->codes8, 0, true));
+            make_tmap(&ix->tm_codes8, ix->codes8, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, Dp8, n,
+                      gemm_scan_db_box(gemm_two_sm()));
+          } else {
+            ix->bq_windows = true;
+          }
           VX_CUDA(cudaDeviceSynchronize());
-          make_tmap(&ix->tm_codes8, ix->codes8, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, Dp8, n,
-                    gemm_scan_db_box(gemm_two_sm()));
         }
         if (vectors) ix->rows32 = upload_rows32(ix, vectors, n, dim, row_stride);
       }
@@ -1827,7 +1902,8 @@ int vx_bq_build(int32_t device, const uint64_t* words, int64_t n, int32_t dim, i
         VX_CUDA(cudaMemset(ix->words, 0, (size_t)n * nwp * 8));
         VX_CUDA(cudaMemcpy2D(ix->words, (size_t)nwp * 8, words, (size_t)nw * 8, (size_t)nw * 8, (size_t)n,
                              cudaMemcpyDefault));
-        // +-1 int8 operand for the tensor-core Hamming scan (8 bytes per bit of storage)
+        // +-1 int8 operand for the tensor-core Hamming scan (8 bytes per bit of storage): whole
+        // within VX_BQ_TENSOR_BYTES, else expanded per row window at search time
         const int Dp8 = (int)round_up(dim, 128);
         if (bq_tensor_budget() >= (uint64_t)n * Dp8) {
           ix->Dp8 = Dp8;
@@ -1836,6 +1912,9 @@ int vx_bq_build(int32_t device, const uint64_t* words, int64_t n, int32_t dim, i
           VX_CUDA(cudaDeviceSynchronize());
           make_tmap(&ix->tm_codes8, ix->codes8, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, Dp8, n,
                     gemm_scan_db_box(gemm_two_sm()));
+        } else if (bq_window_bytes() > 0) {
+          ix->Dp8 = Dp8;
+          ix->bq_windows = true;
         }
         if (vectors) ix->rows32 = upload_rows32(ix, vectors, n, dim, row_stride);
       }
