@@ -284,7 +284,8 @@ def main():
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--n", type=int, default=FLAT["n"])
+    ap.add_argument("--n", "--flat-n", dest="n", type=int, default=FLAT["n"],
+                    help="FLAT rows (--flat-n under torchrun, whose own options take --n)")
     ap.add_argument("--nq", type=int, default=FLAT["nq"])
     ap.add_argument("--no-ivf", action="store_true")
     ap.add_argument("--no-quant", action="store_true", help="skip the SQ8, BQ and FP16 scan legs")
@@ -298,6 +299,9 @@ def main():
     ap.add_argument("--ivf-n", type=int, default=IVF["n"])
     ap.add_argument("--ivf-nlist", type=int, default=IVF["nlist"], help="smaller cases for profiling keep n/nlist")
     ap.add_argument("--ivf-nq", type=int, default=IVF["nq"])
+    ap.add_argument("--ivf-split", default="auto", choices=["auto", "pair", "query"],
+                    help="IVF-PQ at N > 1: deal (query, list) pairs, split the queries, or auto (queries at "
+                         "2 ranks, pairs from 4)")
     ap.add_argument("--ref-rows", type=int, default=1_000_000)
     ap.add_argument("--ref-queries", type=int, default=256)
     args = ap.parse_args()
@@ -557,7 +561,7 @@ def run_ivf(args, rank, world, local, dev, barrier, max_over_ranks, hbm_peak, pe
 
     import vectors_b200 as vx
     from vectors_b200 import _native as N
-    from vectors_b200.sharded import gather_rows, search_query_sharded
+    from vectors_b200.sharded import gather_rows, ivf_search_pair_split, search_query_sharded
 
     P = IVF
     n, dim, nlist, m, ks = args.ivf_n, P["dim"], args.ivf_nlist, P["m"], P["ks"]
@@ -620,13 +624,20 @@ def run_ivf(args, rank, world, local, dev, barrier, max_over_ranks, hbm_peak, pe
     probed = dq.topk(P["nprobe"], largest=False).indices
     bytes_step = float(counts[probed].sum().item()) * (m + 4)
 
+    # auto: the split that measured faster at this rank count (one-GPU emulation of the ranks'
+    # own work at 2 / 4 / 8 ranks, and 2 B200s): queries at 2 ranks, pairs from 4 up, where the
+    # query slices leave most four-query table groups part-filled
+    split = args.ivf_split if args.ivf_split != "auto" else ("query" if world <= 2 else "pair")
+
     def step():
         if world == 1:
             return a.ivf_search_device(q, k, P["nprobe"])[0]
-        # replicated index: each rank answers its slice of the queries; results all-gathered
-        # (dealing whole lists to ranks is unbalanced on this data: two hub lists carry more
-        # than an eighth of the work at 8 GPUs)
-        return search_query_sharded(lambda qs: a.ivf_search_device(qs, k, P["nprobe"]), q)[0]
+        if split == "query":
+            # replicated index: each rank answers its slice of the queries; results all-gathered
+            return search_query_sharded(lambda qs: a.ivf_search_device(qs, k, P["nprobe"]), q)[0]
+        # replicated index, (query, list) pairs dealt to ranks in four-pair table groups: every
+        # list (the hub lists near every query included) split evenly, full groups on every rank
+        return ivf_search_pair_split(a, q, k, P["nprobe"])[0]
 
     for _ in range(args.warmup):
         step()
@@ -690,7 +701,9 @@ def run_ivf(args, rank, world, local, dev, barrier, max_over_ranks, hbm_peak, pe
                      "frac": (achieved / hbm_peak) if achieved else None, "traffic": None,
                      "kernel": "adc_group_kernel (grouped ADC list scan)", "peak_source": f"{peak_kind} HBM copy",
                      "algorithmic_bytes_per_step": bytes_step, "per": "GPU",
-                     "sharding": "index replicated, queries split across ranks" if world > 1 else "single GPU",
+                     "sharding": ("single GPU" if world == 1 else "index replicated, queries split across ranks"
+                                  if split == "query" else
+                                  "index replicated, (query, list) pairs dealt across ranks in four-pair groups"),
                      "breakdown_ms_per_step": {kk: v[0] / args.steps for kk, v in prof.items() if v[1]},
                      "per_rank": per_rank,
                      "smem_gather_roof": {"frac": smem_frac, "gather_bytes_per_step": gather_bytes,

@@ -468,6 +468,35 @@ def test_ivfpq_balanced_masks_equal_unsharded(oracle):
     assert torch.equal(mi, ref[0]) and torch.equal(ms, ref[1]) and torch.equal(mc, ref[2])
 
 
+@pytest.mark.parametrize("world", [2, 3])
+def test_ivfpq_pair_split_equals_unsplit(oracle, world):
+    # vectors_b200.sharded.ivf_search_pair_split, the ranks emulated on one GPU: every list's
+    # pairs dealt over the ranks in four-pair table groups, each rank scans its pairs only
+    import torch
+
+    from vectors_b200.sharded import deal_pairs
+
+    db, q, cent, off, ords, cb, codes = _ivf(oracle, dim=128, nlist=32, m=16)
+    a = vx.IvfPqAdapter(nprobe=8)
+    a.build_prebuilt(cent, off, ords, cb, codes, 16, 256, vx.SimilarityFunction.EUCLIDEAN)
+    qd = torch.from_numpy(q).cuda()
+    ref = a.ivf_search_device(qd, 10, 8)
+    lists = a.route_device(qd, 8)
+    parts = [a.ivf_search_routed_device(qd, 10, 8, deal_pairs(lists, r, world)) for r in range(world)]
+    ids = torch.stack([p_[0] for p_ in parts])
+    sc = torch.stack([p_[1] for p_ in parts])
+    cnt = torch.stack([p_[2] for p_ in parts])
+    mi, ms, mc = vx.merge_shards_device(ids, sc, cnt, torch.zeros(world, dtype=torch.int64), 10)
+    torch.cuda.synchronize()
+    assert torch.equal(mi, ref[0]) and torch.equal(ms, ref[1]) and torch.equal(mc, ref[2])
+    ids_o, sc_o, cnt_o = oracle.ivfpq_search(cent, off, ords, 16, 256, cb, codes, q, oracle.EUCLIDEAN, 10, 8)
+    assert np.array_equal(mc.cpu().numpy(), cnt_o)
+    for i in range(q.shape[0]):
+        assert list(mi[i, : cnt_o[i]].cpu().numpy()) == list(ids_o[i, : cnt_o[i]])
+        assert np.array_equal(ms[i, : cnt_o[i]].cpu().numpy(), sc_o[i, : cnt_o[i]])
+    a.close()
+
+
 def test_ivfpq_routing_matches_oracle(oracle):
     db, q, cent, off, ords, cb, codes = _ivf(oracle)
     lids, _ = oracle.route(cent, q, oracle.EUCLIDEAN, 8)

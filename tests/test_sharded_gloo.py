@@ -153,3 +153,103 @@ def test_assign_lists_deals_every_list_once_and_balances(world):
     loads = torch.zeros(world, dtype=torch.float64).index_add_(0, owner, work)
     # within one list's work of the mean
     assert float(loads.max() - loads.mean()) <= float(work.max())
+
+
+@pytest.mark.parametrize("world", [1, 2, 3, 8])
+def test_deal_pairs_gives_each_pair_to_one_rank_and_splits_every_list(world):
+    # the pair deal of ivf_search_pair_split: a hub list probed by every query is split evenly
+    import torch
+
+    from vectors_b200.sharded import deal_pairs
+
+    g = torch.Generator().manual_seed(7 + world)
+    lists = torch.randint(-1, 50, (997, 8), generator=g, dtype=torch.int32)
+    lists[:, 0] = 5  # probed by every query
+    parts = [deal_pairs(lists, r, world) for r in range(world)]
+    owned = torch.stack([(p >= 0).int() for p in parts]).sum(0)
+    assert torch.equal(owned, (lists >= 0).int())  # every pair exactly once, none invented
+    for r, p in enumerate(parts):
+        assert p.dtype == lists.dtype and torch.equal(torch.where(p >= 0, p, lists), lists)
+        assert torch.equal(p, deal_pairs(lists.clone(), r, world))  # deterministic
+    for lst in range(50):
+        c = [int((p == lst).sum()) for p in parts]
+        assert max(c) - min(c) <= 4, (lst, c)  # within one four-pair table group
+
+
+class _ListScanFake:
+    """Stands in for IvfPqAdapter on the CPU: routing to the nprobe nearest centroids, and a
+    routed search that scores every row of a query's given lists (-|q - x|^2 in float32) and
+    keeps the k best by (score desc, ordinal asc)."""
+
+    def __init__(self, db, cent, assign):
+        self.db, self.cent, self.assign = db, cent, assign
+
+    def route_device(self, qs, nprobe):
+        import torch
+
+        q = qs.numpy()
+        d = ((q[:, None, :] - self.cent[None, :, :]) ** 2).sum(2)
+        return torch.from_numpy(np.argsort(d, axis=1, kind="stable")[:, :nprobe].astype(np.int32))
+
+    def ivf_search_routed_device(self, qs, k, nprobe, lists, rescore_factor):
+        import torch
+
+        q, L = qs.numpy(), lists.numpy()
+        ids = np.full((q.shape[0], k), -1, np.int32)
+        sc = np.zeros((q.shape[0], k), np.float32)
+        cnt = np.zeros(q.shape[0], np.int32)
+        for i in range(q.shape[0]):
+            rows = np.nonzero(np.isin(self.assign, L[i][L[i] >= 0]))[0]
+            s = -((self.db[rows] - q[i]) ** 2).sum(1).astype(np.float32)
+            o = np.lexsort((rows, -s))[:k]
+            ids[i, : len(o)], sc[i, : len(o)], cnt[i] = rows[o], s[o], len(o)
+        return torch.from_numpy(ids), torch.from_numpy(sc), torch.from_numpy(cnt)
+
+
+def _pair_split_worker(rank, world, port, out_dir):
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    try:
+        import vectors_b200.sharded as S
+        from oracle import oracle as O
+
+        db = O.gen_mixture(1500, 16, 6, 0.4, SEEDS[0], SEEDS[1], False)
+        q = O.gen_mixture(41, 16, 6, 0.4, SEEDS[0], SEEDS[2], False)
+        cent = db[:12].copy()
+        assign = np.argmin(((db[:, None, :] - cent[None]) ** 2).sum(2), 1)
+        fake = _ListScanFake(db, cent, assign)
+
+        def merge(gi, gs, gc, off, k):
+            r = O.merge_shards(off.numpy(), gi.numpy(), gs.numpy(), gc.numpy(), k)
+            return tuple(torch.from_numpy(np.ascontiguousarray(x)) for x in r)
+
+        real = S.gather_and_merge
+        S.gather_and_merge = lambda *a, **kw: real(*a, merge=merge, **kw)
+        try:
+            mi, ms, mc = S.ivf_search_pair_split(fake, torch.from_numpy(q), 9, 4)
+        finally:
+            S.gather_and_merge = real
+        ref = fake.ivf_search_routed_device(torch.from_numpy(q), 9, 4, fake.route_device(torch.from_numpy(q), 4), 1)
+        ok = all(np.array_equal(a.numpy(), b.numpy()) for a, b in zip((mi, ms, mc), ref))
+        with open(os.path.join(out_dir, f"rank{rank}"), "w") as f:
+            f.write("ok" if ok else "mismatch")
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_rank_gloo_pair_split_search_matches_unsplit():
+    # ivf_search_pair_split: queries routed per rank, lists all-gathered, pairs dealt, per-rank
+    # top-k merged; equals the search over every routed pair on one rank
+    import torch.multiprocessing as mp
+
+    with tempfile.TemporaryDirectory() as d:
+        mp.start_processes(_pair_split_worker, args=(2, _free_port(), d), nprocs=2, join=True, start_method="spawn")
+        for r in range(2):
+            with open(os.path.join(d, f"rank{r}")) as f:
+                assert f.read() == "ok", f"rank {r}"

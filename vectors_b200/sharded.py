@@ -15,7 +15,7 @@ from typing import Callable, Optional, Sequence
 from .index_spi import merge_shards_device, shard_offsets
 
 __all__ = ["shard_range", "gather_and_merge", "gather_rows", "ivf_search_sharded", "search_query_sharded",
-           "assign_lists", "ivf_search_balanced"]
+           "assign_lists", "ivf_search_balanced", "deal_pairs", "ivf_search_pair_split"]
 
 
 def shard_range(n: int, rank: int, world: int) -> tuple[int, int]:
@@ -131,8 +131,10 @@ def ivf_search_balanced(adapter, queries, k: int, nprobe: int, list_rows, group=
     lists -- full four-query table groups, no table built twice -- before the per-rank top-k
     lists are merged.  `list_rows` is a device tensor of the lists' row counts.  A list is never
     split, so a batch whose work concentrates in a few lists (centroids near every query, as
-    in high-dimensional Gaussian mixtures) stays unbalanced; search_query_sharded is the robust
-    choice there."""
+    in high-dimensional Gaussian mixtures) stays unbalanced; ivf_search_pair_split splits them.
+    With rescore_factor > 1 each rank re-scores its own k * rescore_factor best, which can keep
+    a row that is not among the k * rescore_factor best of the whole index (IvfIndex.pqSearch
+    re-scores those only); search_query_sharded keeps the reference's results there."""
     import torch
     import torch.distributed as dist
 
@@ -145,4 +147,47 @@ def ivf_search_balanced(adapter, queries, k: int, nprobe: int, list_rows, group=
     owner = assign_lists(pairs, list_rows, world)
     mine = torch.where((lists >= 0) & (owner[lists.clamp_min(0).long()] == rank), lists, torch.full_like(lists, -1))
     ids, sc, cnt = adapter.ivf_search_routed_device(queries, k, nprobe, mine, rescore_factor)
+    return gather_and_merge(ids, sc, cnt, [0] * (world + 1), k, group)
+
+
+def deal_pairs(lists, rank: int, world: int, group_size: int = 4):
+    """Deals one routed batch's (query, list) pairs to ranks: lists [nq][nprobe] (int32, -1 for
+    none) -> the same shape with the pairs of other ranks set to -1.  The pairs of each list, in
+    query order, are cut into runs of `group_size` (the ADC scan's table group: one table build
+    serves a run) and the runs are dealt round-robin, starting at rank (list id mod world), so
+    every list -- the hub lists near every query included -- is split evenly over the ranks and
+    every rank scans full groups.  Deterministic: all ranks derive the same deal from the same
+    all-gathered lists, and every pair goes to exactly one rank."""
+    import torch
+
+    flat = lists.reshape(-1).long()
+    valid = flat >= 0
+    big = torch.iinfo(torch.int64).max
+    key = torch.where(valid, flat, torch.full_like(flat, big))
+    order = torch.sort(key, stable=True).indices  # by list, then by pair index (query order)
+    sk = key[order]
+    pos = torch.arange(sk.shape[0], device=sk.device) - torch.searchsorted(sk, sk)  # rank within its list
+    owner_sorted = torch.remainder(pos // group_size + torch.where(sk == big, 0, sk), world)
+    owner = torch.empty_like(owner_sorted)
+    owner[order] = owner_sorted
+    mine = torch.where(valid & (owner == rank), flat, torch.full_like(flat, -1))
+    return mine.to(lists.dtype).reshape(lists.shape)
+
+
+def ivf_search_pair_split(adapter, queries, k: int, nprobe: int, group=None):
+    """IVF-PQ search over an index replicated on every rank, split by (query, list) pair: each
+    rank routes its slice of the queries, the routed lists are all-gathered, deal_pairs gives
+    every rank an even share of every list's pairs in whole four-query table groups, each rank
+    scans its pairs for the whole batch, and the per-rank top-k lists are merged.  Every pair is
+    scanned once, so the merged top-k is the single-GPU result (IvfIndex.pqSearch keeps the k
+    best of all probed lists).  rescore_factor 1 only: with a re-score, a rank's own
+    k * rescore_factor best need not be among the whole index's (use search_query_sharded)."""
+    import torch.distributed as dist
+
+    rank, world = dist.get_rank(group), dist.get_world_size(group)
+    nq = queries.shape[0]
+    lo, hi = shard_range(nq, rank, world)
+    lists = gather_rows(adapter.route_device(queries[lo:hi], nprobe), nq, group)
+    mine = deal_pairs(lists, rank, world)
+    ids, sc, cnt = adapter.ivf_search_routed_device(queries, k, nprobe, mine, 1)
     return gather_and_merge(ids, sc, cnt, [0] * (world + 1), k, group)
