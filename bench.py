@@ -219,9 +219,17 @@ def timed_oracle(fn):
     return r, time.perf_counter() - t, th
 
 
+def pinned(x):
+    """A page-locked copy of a host array (the end-to-end calls copy their queries from it)."""
+    import torch
+
+    return torch.from_numpy(np.ascontiguousarray(x)).pin_memory().numpy()
+
+
 def e2e_host(args, call, nq, h2d, d2h):
-    """End to end through a host-buffer C ABI call (queries copied in, results copied out inside
-    the timed region), one GPU: K blocking calls after one warm-up call, host wall clock."""
+    """End to end through a host-buffer C ABI call (queries copied in from page-locked memory,
+    results copied out inside the timed region), one GPU: K blocking calls after one warm-up
+    call, host wall clock."""
     call()
     t0 = time.perf_counter()
     for _ in range(args.steps):
@@ -688,7 +696,8 @@ def run_ivf(args, rank, world, local, dev, barrier, max_over_ranks, hbm_peak, pe
         par = parity(a.ivf_search_arrays(qs, k, P["nprobe"]), ref, True, n)
         cpu = {"value": len(qs) / dt, "unit": "queries/s", "cores": th, "kind": "port",
                "sample": f"{len(qs)} queries over the same 10M-row index ({dt:.1f} s)"}
-        e2e = e2e_host(args, lambda: a.ivf_search_arrays(qh, k, P["nprobe"]), nq, nq * dim * 4, nq * (k * 8 + 4))
+        qp = pinned(qh)
+        e2e = e2e_host(args, lambda: a.ivf_search_arrays(qp, k, P["nprobe"]), nq, nq * dim * 4, nq * (k * 8 + 4))
     a.close()
     return {
         "value": nq / (ms / 1e3),
@@ -810,7 +819,8 @@ def run_ivfflat(args, rank, world, local, dev, barrier, max_over_ranks, peak_kin
         par = parity(a.ivf_search_arrays(qs, k, P["nprobe"]), ref, True, n)
         cpu = {"value": len(qs) / dt, "unit": "queries/s", "cores": th, "kind": "port",
                "sample": f"{len(qs)} queries over the same index ({dt:.1f} s)"}
-        e2e = e2e_host(args, lambda: a.ivf_search_arrays(qh, k, P["nprobe"]), nq, nq * dim * 4, nq * (k * 8 + 4))
+        qp = pinned(qh)
+        e2e = e2e_host(args, lambda: a.ivf_search_arrays(qp, k, P["nprobe"]), nq, nq * dim * 4, nq * (k * 8 + 4))
     a.close()
     del rows
     torch.cuda.empty_cache()
@@ -878,7 +888,8 @@ def run_sq8(args, rank, world, local, dev, barrier, max_over_ranks, tc_sustained
         par = parity(a.scan_candidates_arrays(qh[:64], k), ref, True, n)
         cpu = {"value": 64 / dt, "unit": "queries/s", "cores": th, "kind": "port",
                "sample": f"64 queries over the same {n:,}-row index ({dt:.1f} s)"}
-        e2e = e2e_host(args, lambda: a.scan_candidates_arrays(qh, k), nq, nq * dim * 4, nq * (k * 8 + 4))
+        qp = pinned(qh)
+        e2e = e2e_host(args, lambda: a.scan_candidates_arrays(qp, k), nq, nq * dim * 4, nq * (k * 8 + 4))
     a.close()
     ops = 2.0 * nq * (hi - lo) * dim  # int8 multiply-adds x 2 on this rank
     achieved = ops / (kms / 1e3) / 1e12 if kms > 0 else None
@@ -964,7 +975,8 @@ def run_bq(args, rank, world, local, dev, barrier, max_over_ranks, tc_sustained,
         par = parity(a.scan_candidates_arrays(qh[:64], k), ref, True, n)
         cpu = {"value": 64 / dt, "unit": "queries/s", "cores": th, "kind": "port",
                "sample": f"64 queries over the same {n:,}-row index ({dt:.1f} s)"}
-        e2e = e2e_host(args, lambda: a.scan_candidates_arrays(qh, k), nq, nq * dim * 4, nq * (k * 8 + 4))
+        qp = pinned(qh)
+        e2e = e2e_host(args, lambda: a.scan_candidates_arrays(qp, k), nq, nq * dim * 4, nq * (k * 8 + 4))
     a.close()
     # The same rows as an index above the int8 operand budget: packed bits alone on the device
     # (128 B per row instead of 1,152), the tensor scan over row windows whose +-1 operand is
@@ -1037,7 +1049,8 @@ def run_bq(args, rank, world, local, dev, barrier, max_over_ranks, tc_sustained,
         bpar = parity(b.scan_candidates_arrays(qh[:64], k), ref, True, nb)
         bcpu = {"value": 64 / dt, "unit": "queries/s", "cores": th, "kind": "port",
                 "sample": f"64 queries over the same {nb:,}-row index ({dt:.1f} s)"}
-        be2e = e2e_host(args, lambda: b.scan_candidates_arrays(qh, k), nq, nq * dim * 4, nq * (k * 8 + 4))
+        qp = pinned(qh)
+        be2e = e2e_host(args, lambda: b.scan_candidates_arrays(qp, k), nq, nq * dim * 4, nq * (k * 8 + 4))
     b.close()
     if bbr.get("gemm_scan"):
         dp8 = (dim + 127) // 128 * 128
@@ -1116,7 +1129,8 @@ def run_fp16(args, rank, world, local, dev, barrier, max_over_ranks, tc_sustaine
         from oracle import oracle as O
 
         qh = q.cpu().numpy()
-        e2e = e2e_host(args, lambda: a.scan_candidates_arrays(qh, k), nq, nq * dim * 4, nq * (k * 8 + 4))
+        qp = pinned(qh)
+        e2e = e2e_host(args, lambda: a.scan_candidates_arrays(qp, k), nq, nq * dim * 4, nq * (k * 8 + 4))
         a.close()
         # parity on an index of this GPU's first 1M rows (the CPU check of 12.5M rows would take minutes)
         sub = vx.QuantizedFlatScanAdapter(device=local)

@@ -86,7 +86,6 @@ __device__ __forceinline__ void apply_floor(const ScanArgs& a, int q, bool activ
   }
 }
 
-// Ranking score of one accumulator value in epilogue mode kMode (gemm_scan.h).
 // BBQ: computeBbqDot of one accumulator value (rawAsymDot) against the staged row record
 // s_col[col] = vl, s_col[256 + col] = width, s_col[512 + col] = vl * D + width * pop
 // (s_col[768 + col] = |v - c| or |v - c|^2); qb holds the lane's query (queryMin,
@@ -96,32 +95,53 @@ __device__ __forceinline__ float bbq_approx_at(uint32_t v, int col, const float*
   return bbq_approx(qb.x, qb.y, qb.z, s_col[col], s_col[256 + col], s_col[512 + col], __int2float_rn((int32_t)v));
 }
 
+// Ranking score of one accumulator value in epilogue mode kMode (gemm_scan.h), split into a
+// per-column inner quantity and a monotone tail applied to it: group_max computes every
+// column's inner quantity once and leaves it in the accumulator registers in place of the raw
+// value, so the admission slow path applies only the tail.  Inner quantities: F16Plain /
+// F16Scaled / F16L2 / BbqCos the score (no tail); Sq8Dot / Sq8Mip adj = rawDot *
+// constMultiplier + queryCorrection + correction[ordinal]; Sq8L2 the integer squared distance;
+// BqHamming the raw +-1 dot; BbqDot / BbqMip computeBbqDot; BbqL2 the clamped distance term.
 template <int kMode>
-__device__ __forceinline__ float score_of(uint32_t v, int col, const float* s_col, const float* s_col2,
-                                          float qa, int32_t qi, float cm, const float4& qb) {
-  if (kMode == kEpiF16Plain) return __uint_as_float(v);
-  if (kMode == kEpiBbqDot) return bbq_dot_score(bbq_approx_at(v, col, s_col, qb));
-  if (kMode == kEpiBbqMip) return scale_mip(bbq_approx_at(v, col, s_col, qb));
-  if (kMode == kEpiBbqL2) return bbq_l2_score(bbq_l2_adj(bbq_approx_at(v, col, s_col, qb), qb.w, s_col[768 + col]));
-  if (kMode == kEpiBbqCos) return bbq_cos_score(bbq_approx_at(v, col, s_col, qb), qb.w, s_col[768 + col]);
-  if (kMode == kEpiF16Scaled) return __uint_as_float(v) * s_col[col];
-  if (kMode == kEpiF16L2) return fmaf(qa * s_col[col], __uint_as_float(v), -s_col2[col]);
-  if (kMode == kEpiSq8Dot || kMode == kEpiSq8Mip) {
-    // rawDot * constMultiplier + queryCorrection + corrections[ordinal]
-    const float adj = __fadd_rn(__fadd_rn(__fmul_rn(__int2float_rn((int32_t)v), cm), qa), s_col[col]);
-    if (kMode == kEpiSq8Dot) {
-      const float h = __fmul_rn(__fadd_rn(1.0f, adj), 0.5f);  // (1f + adj) / 2f
-      return h >= 0.0f ? h : (h != h ? h : 0.0f);             // Math.max(h, 0f)
-    }
-    return scale_mip(adj);
+__device__ __forceinline__ uint32_t inner_of(uint32_t v, int col, const float* s_col, const float* s_col2,
+                                             float qa, int32_t qi, float cm, const float4& qb) {
+  if constexpr (kMode == kEpiBbqDot || kMode == kEpiBbqMip) {
+    return __float_as_uint(bbq_approx_at(v, col, s_col, qb));
+  } else if constexpr (kMode == kEpiBbqL2) {
+    return __float_as_uint(bbq_l2_adj(bbq_approx_at(v, col, s_col, qb), qb.w, s_col[768 + col]));
+  } else if constexpr (kMode == kEpiBbqCos) {
+    return __float_as_uint(bbq_cos_score(bbq_approx_at(v, col, s_col, qb), qb.w, s_col[768 + col]));
+  } else if constexpr (kMode == kEpiF16Scaled) {
+    return __float_as_uint(__uint_as_float(v) * s_col[col]);
+  } else if constexpr (kMode == kEpiF16L2) {
+    return __float_as_uint(fmaf(qa * s_col[col], __uint_as_float(v), -s_col2[col]));
+  } else if constexpr (kMode == kEpiSq8Dot || kMode == kEpiSq8Mip) {
+    return __float_as_uint(__fadd_rn(__fadd_rn(__fmul_rn(__int2float_rn((int32_t)v), cm), qa), s_col[col]));
+  } else if constexpr (kMode == kEpiSq8L2) {
+    return (uint32_t)(qi + __float_as_int(s_col[col]) - 2 * (int32_t)v);
+  } else {  // F16Plain, BqHamming
+    return v;
   }
-  if (kMode == kEpiBqHamming) {
-    // +-1 operands: dot = (agreeing bits) - (differing bits) = D - 2h; qi carries D
-    return -(float)((qi - (int32_t)v) >> 1);
+}
+
+template <int kMode>
+__device__ __forceinline__ float tail_of(uint32_t x, int32_t qi, float cm) {
+  if constexpr (kMode == kEpiSq8Dot) {
+    const float h = __fmul_rn(__fadd_rn(1.0f, __uint_as_float(x)), 0.5f);  // (1f + adj) / 2f
+    return h >= 0.0f ? h : (h != h ? h : 0.0f);                            // Math.max(h, 0f)
+  } else if constexpr (kMode == kEpiSq8Mip || kMode == kEpiBbqMip) {
+    return scale_mip(__uint_as_float(x));
+  } else if constexpr (kMode == kEpiSq8L2) {
+    return __fdiv_rn(1.0f, __fadd_rn(1.0f, __fmul_rn(__int2float_rn((int32_t)x), cm)));
+  } else if constexpr (kMode == kEpiBqHamming) {
+    return -(float)((qi - (int32_t)x) >> 1);
+  } else if constexpr (kMode == kEpiBbqDot) {
+    return bbq_dot_score(__uint_as_float(x));
+  } else if constexpr (kMode == kEpiBbqL2) {
+    return bbq_l2_score(__uint_as_float(x));
+  } else {
+    return __uint_as_float(x);
   }
-  // kEpiSq8L2: sum (q-v)^2 = sum q^2 + sum v^2 - 2 q.v, exact in int32
-  const int32_t sq = qi + __float_as_int(s_col[col]) - 2 * (int32_t)v;
-  return __fdiv_rn(1.0f, __fadd_rn(1.0f, __fmul_rn(__int2float_rn(sq), cm)));
 }
 
 // Per-lane state of one query's stream during a tile.
@@ -135,18 +155,16 @@ struct TileStream {
 };
 
 // Slow path of one 32-column group, taken when some lane of the warp may admit a column:
-// builds the lane's pass mask, stages the lane's 32 values in its private shared-memory row
-// (so that the append loop can index them), compacts first when the stream could overflow,
-// then appends the passing columns in ascending order.
+// builds the lane's pass mask from the inner quantities group_max left in v[], stages them in
+// the lane's private shared-memory row (so that the append loop can index them), compacts
+// first when the stream could overflow, then appends the passing columns in ascending order.
 template <int kMode, int R>
 __device__ __forceinline__ void offer_group(const ScanArgs& a, TileStream& ts, int q, bool active,
                                             const uint32_t (&v)[32], int c0, int limit, int64_t col0,
-                                            const float* s_col, const float* s_col2, float qa, int32_t qi,
-                                            const float4& qb, uint32_t* stage_row) {
+                                            int32_t qi, uint32_t* stage_row) {
   uint32_t pm = 0;
 #pragma unroll
-  for (int j = 0; j < 32; j++)
-    pm |= (score_of<kMode>(v[j], c0 + j, s_col, s_col2, qa, qi, a.epi.cm, qb) >= ts.tf ? 1u : 0u) << j;
+  for (int j = 0; j < 32; j++) pm |= (tail_of<kMode>(v[j], qi, a.epi.cm) >= ts.tf ? 1u : 0u) << j;
   if (limit < 32) pm &= limit <= 0 ? 0u : (0xFFFFFFFFu >> (32 - limit));  // rows beyond n
   if (pm) {
     uint4* d = reinterpret_cast<uint4*>(stage_row);
@@ -167,7 +185,7 @@ __device__ __forceinline__ void offer_group(const ScanArgs& a, TileStream& ts, i
     const int j = __ffs(pm) - 1;
     pm &= pm - 1;
     const int col = c0 + j;
-    const float sc = score_of<kMode>(stage_row[j], col, s_col, s_col2, qa, qi, a.epi.cm, qb);
+    const float sc = tail_of<kMode>(stage_row[j], qi, a.epi.cm);
     const uint64_t key = float_key(sc, (uint32_t)(col0 + col));
     if (key > ts.st.thr && key < ts.ceil) {
       ts.st.base[ts.st.cnt++] = key;
@@ -181,94 +199,40 @@ __device__ __forceinline__ void offer_group(const ScanArgs& a, TileStream& ts, i
   }
 }
 
-// Largest score of a 32-column group (pairwise tree: one epilogue warp per scheduler, so the
-// dependency depth matters more than the operation count).  The integer modes take the
-// extreme of the cheapest exact inner quantity (BQ: the raw dot; SQ8: adj or the integer
-// squared distance) and apply the score's monotone tail once; the result is exact.
-__device__ __forceinline__ int32_t imax_tree32(const uint32_t (&v)[32]) {
-  int32_t m[16];
-#pragma unroll
-  for (int i = 0; i < 16; i++) m[i] = max((int32_t)v[2 * i], (int32_t)v[2 * i + 1]);
-#pragma unroll
-  for (int w = 8; w >= 1; w >>= 1)
-#pragma unroll
-    for (int i = 0; i < w; i++) m[i] = max(m[i], m[i + w]);
-  return m[0];
-}
-
+// Largest score of a 32-column group, exact: every column's inner quantity (left in v[] for the
+// admission slow path), their extreme (largest; smallest for the integer squared distance and
+// the clamped BBQ distance term, never NaN, whose scores fall as they grow) by a pairwise tree
+// (one epilogue warp per scheduler, so the dependency depth matters more than the operation
+// count), and the monotone tail of that extreme.
 template <int kMode>
-__device__ __forceinline__ float group_max(const uint32_t (&v)[32], int c0, const float* s_col,
-                                           const float* s_col2, float qa, int32_t qi, const EpiParams& e,
-                                           const float4& qb) {
-  if constexpr (kMode == kEpiBqHamming) {
-    return score_of<kMode>((uint32_t)imax_tree32(v), 0, s_col, s_col2, qa, qi, e.cm, qb);
-  } else if constexpr (kMode == kEpiBbqDot || kMode == kEpiBbqMip) {
-    // exact: the largest computeBbqDot, then the non-decreasing tail
-    float m[16];
+__device__ __forceinline__ float group_max(uint32_t (&v)[32], int c0, const float* s_col, const float* s_col2,
+                                           float qa, int32_t qi, const EpiParams& e, const float4& qb) {
 #pragma unroll
-    for (int i = 0; i < 16; i++)
-      m[i] = fmaxf(bbq_approx_at(v[2 * i], c0 + 2 * i, s_col, qb), bbq_approx_at(v[2 * i + 1], c0 + 2 * i + 1, s_col, qb));
-#pragma unroll
-    for (int w = 8; w >= 1; w >>= 1)
-#pragma unroll
-      for (int i = 0; i < w; i++) m[i] = fmaxf(m[i], m[i + w]);
-    return kMode == kEpiBbqDot ? bbq_dot_score(m[0]) : scale_mip(m[0]);
-  } else if constexpr (kMode == kEpiBbqL2) {
-    // exact: the smallest clamped distance term (never NaN), then the non-increasing tail
-    float m[16];
-#pragma unroll
-    for (int i = 0; i < 16; i++)
-      m[i] = fminf(bbq_l2_adj(bbq_approx_at(v[2 * i], c0 + 2 * i, s_col, qb), qb.w, s_col[768 + c0 + 2 * i]),
-                   bbq_l2_adj(bbq_approx_at(v[2 * i + 1], c0 + 2 * i + 1, s_col, qb), qb.w,
-                              s_col[768 + c0 + 2 * i + 1]));
-#pragma unroll
-    for (int w = 8; w >= 1; w >>= 1)
-#pragma unroll
-      for (int i = 0; i < w; i++) m[i] = fminf(m[i], m[i + w]);
-    return bbq_l2_score(m[0]);
-  } else if constexpr (kMode == kEpiSq8Dot || kMode == kEpiSq8Mip) {
-    // exact: the largest adj = raw * cm + queryCorrection + correction, then the monotone tail
-    float m[16];
-#pragma unroll
-    for (int i = 0; i < 16; i++) {
-      const float a0 = __fadd_rn(__fadd_rn(__fmul_rn(__int2float_rn((int32_t)v[2 * i]), e.cm), qa), s_col[c0 + 2 * i]);
-      const float a1 =
-          __fadd_rn(__fadd_rn(__fmul_rn(__int2float_rn((int32_t)v[2 * i + 1]), e.cm), qa), s_col[c0 + 2 * i + 1]);
-      m[i] = fmaxf(a0, a1);
-    }
-#pragma unroll
-    for (int w = 8; w >= 1; w >>= 1)
-#pragma unroll
-      for (int i = 0; i < w; i++) m[i] = fmaxf(m[i], m[i + w]);
-    const float adj = m[0];
-    if (kMode == kEpiSq8Dot) {
-      const float h = __fmul_rn(__fadd_rn(1.0f, adj), 0.5f);
-      return h >= 0.0f ? h : (h != h ? h : 0.0f);
-    }
-    return scale_mip(adj);
-  } else if constexpr (kMode == kEpiSq8L2) {
-    // exact: the smallest integer squared distance, then the monotone tail
+  for (int j = 0; j < 32; j++) v[j] = inner_of<kMode>(v[j], c0 + j, s_col, s_col2, qa, qi, e.cm, qb);
+  if constexpr (kMode == kEpiBqHamming || kMode == kEpiSq8L2) {
+    constexpr bool kMin = kMode == kEpiSq8L2;
     int32_t m[16];
 #pragma unroll
     for (int i = 0; i < 16; i++)
-      m[i] = min(qi + __float_as_int(s_col[c0 + 2 * i]) - 2 * (int32_t)v[2 * i],
-                 qi + __float_as_int(s_col[c0 + 2 * i + 1]) - 2 * (int32_t)v[2 * i + 1]);
+      m[i] = kMin ? min((int32_t)v[2 * i], (int32_t)v[2 * i + 1]) : max((int32_t)v[2 * i], (int32_t)v[2 * i + 1]);
 #pragma unroll
     for (int w = 8; w >= 1; w >>= 1)
 #pragma unroll
-      for (int i = 0; i < w; i++) m[i] = min(m[i], m[i + w]);
-    return __fdiv_rn(1.0f, __fadd_rn(1.0f, __fmul_rn(__int2float_rn(m[0]), e.cm)));
+      for (int i = 0; i < w; i++) m[i] = kMin ? min(m[i], m[i + w]) : max(m[i], m[i + w]);
+    return tail_of<kMode>((uint32_t)m[0], qi, e.cm);
   } else {
+    constexpr bool kMin = kMode == kEpiBbqL2;
     float m[16];
 #pragma unroll
-    for (int i = 0; i < 16; i++)
-      m[i] = fmaxf(score_of<kMode>(v[2 * i], c0 + 2 * i, s_col, s_col2, qa, qi, e.cm, qb),
-                   score_of<kMode>(v[2 * i + 1], c0 + 2 * i + 1, s_col, s_col2, qa, qi, e.cm, qb));
+    for (int i = 0; i < 16; i++) {
+      const float x0 = __uint_as_float(v[2 * i]), x1 = __uint_as_float(v[2 * i + 1]);
+      m[i] = kMin ? fminf(x0, x1) : fmaxf(x0, x1);
+    }
 #pragma unroll
     for (int w = 8; w >= 1; w >>= 1)
 #pragma unroll
-      for (int i = 0; i < w; i++) m[i] = fmaxf(m[i], m[i + w]);
-    return m[0];
+      for (int i = 0; i < w; i++) m[i] = kMin ? fminf(m[i], m[i + w]) : fmaxf(m[i], m[i + w]);
+    return tail_of<kMode>(__float_as_uint(m[0]), qi, e.cm);
   }
 }
 
@@ -549,7 +513,7 @@ __global__ void __launch_bounds__(64 + 32 * kEpi, 1)
       // 32-column groups up to the last row (tile-uniform); the TMEM load of the next group is
       // in flight while the current one is processed
       const int g_end = (valid + 31) / 32 < g_lo + gpw ? (valid + 31) / 32 : g_lo + gpw;
-      auto process = [&](const uint32_t(&v)[32], int g) {
+      auto process = [&](uint32_t(&v)[32], int g) {
         const int c0 = g * 32;
         const float m = group_max<kMode>(v, c0, s_col, s_col2, qa, qi, a.epi, qb);
         if (probe) {  // exact group maxima: the floor needs scores that rows reach
@@ -557,7 +521,7 @@ __global__ void __launch_bounds__(64 + 32 * kEpi, 1)
           return;
         }
         if (__any_sync(0xFFFFFFFFu, m >= ts.tf))
-          offer_group<kMode, R>(a, ts, q, active, v, c0, valid - c0, col0, s_col, s_col2, qa, qi, qb, stage_row);
+          offer_group<kMode, R>(a, ts, q, active, v, c0, valid - c0, col0, qi, stage_row);
       };
       uint32_t va[32], vb[32];
       __syncwarp();
