@@ -154,17 +154,37 @@ struct TileStream {
   uint64_t ceil;  // keys >= ceil are not admitted (~0: no bound)
 };
 
+// SQ8 DOT_PRODUCT / COSINE: a bound below the smallest adj whose score max((1 + adj) / 2, 0)
+// reaches tf.  For tf > 0 such an adj has fl(1 + adj) >= 2 tf, so adj >= 2 tf - 1 less half an
+// ulp of 2 tf; the margin (|2 tf| + 1) 2^-20 covers that and the rounding of 2 tf - 1 many
+// times over.  tf <= 0 (or NaN): every score reaches it (NaN scores never: NaN >= x is false
+// either way).  tf >= 1e38, where 2 tf overflows: tf itself (2 tf - 1 > tf).
+__device__ __forceinline__ float sq8dot_adj_bound(float tf) {
+  if (!(tf > 0.0f)) return -INFINITY;
+  if (!(tf < 1.0e38f)) return tf;
+  const float two = 2.0f * tf;
+  return __fsub_rn(__fsub_rn(two, 1.0f), __fmul_rn(fabsf(two) + 1.0f, 9.5367431640625e-7f));
+}
+
 // Slow path of one 32-column group, taken when some lane of the warp may admit a column:
-// builds the lane's pass mask from the inner quantities group_max left in v[], stages them in
+// builds the lane's pass mask from the inner quantities group_max left in v[] (SQ8 DOT: against
+// a bound in adj itself, a superset of the columns that reach the threshold), stages them in
 // the lane's private shared-memory row (so that the append loop can index them), compacts
-// first when the stream could overflow, then appends the passing columns in ascending order.
+// first when the stream could overflow, then appends, in ascending column order, the passing
+// columns whose exact keys clear the threshold.
 template <int kMode, int R>
 __device__ __forceinline__ void offer_group(const ScanArgs& a, TileStream& ts, int q, bool active,
                                             const uint32_t (&v)[32], int c0, int limit, int64_t col0,
                                             int32_t qi, uint32_t* stage_row) {
   uint32_t pm = 0;
+  if constexpr (kMode == kEpiSq8Dot) {
+    const float lo = sq8dot_adj_bound(ts.tf);
 #pragma unroll
-  for (int j = 0; j < 32; j++) pm |= (tail_of<kMode>(v[j], qi, a.epi.cm) >= ts.tf ? 1u : 0u) << j;
+    for (int j = 0; j < 32; j++) pm |= (__uint_as_float(v[j]) >= lo ? 1u : 0u) << j;
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; j++) pm |= (tail_of<kMode>(v[j], qi, a.epi.cm) >= ts.tf ? 1u : 0u) << j;
+  }
   if (limit < 32) pm &= limit <= 0 ? 0u : (0xFFFFFFFFu >> (32 - limit));  // rows beyond n
   if (pm) {
     uint4* d = reinterpret_cast<uint4*>(stage_row);
