@@ -166,12 +166,24 @@ __device__ __forceinline__ float sq8dot_adj_bound(float tf) {
   return __fsub_rn(__fsub_rn(two, 1.0f), __fmul_rn(fabsf(two) + 1.0f, 9.5367431640625e-7f));
 }
 
+// BQ: the smallest raw +-1 dot whose Hamming score -((D - raw) >> 1) can reach tf.  raw = D - 2h
+// for a distance h in [0, D], so -h >= tf iff h <= floor(-tf) iff raw >= D - 2 floor(-tf) (one
+// less keeps every raw of D's parity).  tf > 0, NaN or +inf (inactive lane): none; -tf at or
+// above 2^24 (tf = -inf before any key): all.
+__device__ __forceinline__ int32_t bq_min_raw(float tf, int32_t d) {
+  const float u = -tf;
+  if (!(u >= 0.0f)) return d + 1;
+  if (u >= 16777216.0f) return -d;
+  return d - 2 * (int32_t)floorf(u) - 1;
+}
+
 // Slow path of one 32-column group, taken when some lane of the warp may admit a column:
-// builds the lane's pass mask from the inner quantities group_max left in v[] (SQ8 DOT: against
-// a bound in adj itself, a superset of the columns that reach the threshold), stages them in
-// the lane's private shared-memory row (so that the append loop can index them), compacts
-// first when the stream could overflow, then appends, in ascending column order, the passing
-// columns whose exact keys clear the threshold.
+// builds the lane's pass mask from the inner quantities group_max left in v[] (SQ8 DOT, BBQ DOT
+// and BQ: against a bound in the inner quantity itself, a superset of the columns that reach
+// the threshold),
+// stages them in the lane's private shared-memory row (so that the append loop can index
+// them), compacts first when the stream could overflow, then appends, in ascending column
+// order, the passing columns whose exact keys clear the threshold.
 template <int kMode, int R>
 __device__ __forceinline__ void offer_group(const ScanArgs& a, TileStream& ts, int q, bool active,
                                             const uint32_t (&v)[32], int c0, int limit, int64_t col0,
@@ -181,6 +193,20 @@ __device__ __forceinline__ void offer_group(const ScanArgs& a, TileStream& ts, i
     const float lo = sq8dot_adj_bound(ts.tf);
 #pragma unroll
     for (int j = 0; j < 32; j++) pm |= (__uint_as_float(v[j]) >= lo ? 1u : 0u) << j;
+  } else if constexpr (kMode == kEpiBqHamming) {
+    const int32_t lo = bq_min_raw(ts.tf, qi);
+#pragma unroll
+    for (int j = 0; j < 32; j++) pm |= ((int32_t)v[j] >= lo ? 1u : 0u) << j;
+  } else if constexpr (kMode == kEpiBbqDot) {
+    // max((1 + approx) / 2, 0) with NaN -> 0: above 0 the same bound as SQ8 DOT; at or below 0
+    // every column (a NaN approx included) reaches the threshold
+    const float lo = sq8dot_adj_bound(ts.tf);
+    if (ts.tf > 0.0f) {
+#pragma unroll
+      for (int j = 0; j < 32; j++) pm |= (__uint_as_float(v[j]) >= lo ? 1u : 0u) << j;
+    } else {
+      pm = 0xFFFFFFFFu;
+    }
   } else {
 #pragma unroll
     for (int j = 0; j < 32; j++) pm |= (tail_of<kMode>(v[j], qi, a.epi.cm) >= ts.tf ? 1u : 0u) << j;
