@@ -288,6 +288,29 @@ VX_API int vx_ivfpq_search_routed_device(vx_index* index, const float* d_queries
                                   int32_t k, int32_t nprobe, int32_t rescore_factor, float min_score,
                                   const int32_t* d_lists, int32_t* d_ids, float* d_scores,
                                   int32_t* d_counts, void* stream);
+/* IvfIndex.search (IvfIndex.java:170-226) on an IVF-flat index split across GPUs by (query,
+ * list) pair, in three steps whose results equal vx_ivfpq_search_device's (same lists, same
+ * early exit).  Routing: as vx_ivf_route_device, plus each routed list's distance
+ * (d_list_dist [nq][min(nprobe, nlist)], the value the early exit's triangle bound reads,
+ * IvfIndex.java:198-205).  Scan: the list scan of the slots of d_lists [nq][min(nprobe, nlist)]
+ * that hold a list id (-1: a slot another GPU scans) into per-slot results d_pair_keys
+ * [min(nprobe, nlist)][nq][min(k, n)] (64-bit keys: order-preserving score bits above
+ * 0xFFFFFFFF - ordinal) and d_pair_counts [min(nprobe, nlist)][nq]; the other slots are zeroed,
+ * so adding the buffers of GPUs that scanned disjoint slots (an NCCL sum all-reduce) combines
+ * them.  Merge: the combined per-slot results taken in route order with the EUCLIDEAN early
+ * exit when the index holds BuoyIndex radii (else the k best of all slots), then minScore, into
+ * d_ids / d_scores [nq][k] and d_counts [nq].  Not for partitions with HARMONY key dimensions
+ * or k above 256 (VX_ERR_UNSUPPORTED); no SOAR spill (gamma is not applied). */
+VX_API int vx_ivf_route_dist_device(vx_index* index, const float* d_queries, int32_t nq, int32_t dim,
+                                    int32_t nprobe, int32_t* d_lists, float* d_list_dist, void* stream);
+VX_API int vx_ivfflat_scan_pairs_device(vx_index* index, const float* d_queries, int32_t nq, int32_t dim,
+                                        int32_t k, int32_t nprobe, const int32_t* d_lists,
+                                        uint64_t* d_pair_keys, uint32_t* d_pair_counts, void* stream);
+VX_API int vx_ivfflat_merge_pairs_device(vx_index* index, int32_t nq, int32_t k, int32_t nprobe,
+                                         const int32_t* d_lists, const float* d_list_dist,
+                                         const uint64_t* d_pair_keys, const uint32_t* d_pair_counts,
+                                         float min_score, int32_t* d_ids, float* d_scores, int32_t* d_counts,
+                                         void* stream);
 
 /* No counterpart in the reference.  The sign-bit BQ candidate scan of vx_scan_candidates_device
  * for callers that must not allocate device memory while searching (a host that reserves its

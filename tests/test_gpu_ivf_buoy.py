@@ -243,3 +243,63 @@ def test_harmony_partitions_scanned_with_square_distance(oracle, k):
     a.set_key_dims(None)  # cleared: the batched scan everywhere again
     _same(a.ivf_search(q, k, 6), *plain, f"harmony cleared k={k}")
     a.close()
+
+
+@pytest.mark.parametrize("world", [1, 2, 3])
+def test_ivfflat_pair_split_equals_unsplit_with_early_exit(oracle, world):
+    # vectors_b200.sharded.ivfflat_search_pair_split, the ranks emulated on one GPU: each rank
+    # scans its share of every list's pairs into per-slot results, the slots are added up and
+    # merged in route order with the early exit -- on clusters where the break changes most
+    # results, the same ordinals and scores as the unsplit search and the oracle
+    import torch
+
+    from vectors_b200.sharded import deal_pairs
+
+    rng = np.random.default_rng(1)
+    cent = (10.0 * rng.standard_normal((16, 3))).astype(np.float32)
+    sig = np.array([0.2, 0.3, 0.5, 4.0, 6.0, 8.0, 0.4, 2.0] * 2, np.float32)
+    assign = rng.integers(0, 16, 6000)
+    db = (cent[assign] + sig[assign, None] * rng.standard_normal((6000, 3))).astype(np.float32)
+    off, ords = oracle.build_ivf_lists(assign.astype(np.int32), 16)
+    q = (10.0 * rng.standard_normal((700, 3))).astype(np.float32)
+    a = vx.IvfFlatAdapter(nprobe=8)
+    a.build_prebuilt(cent, off, ords, db, vx.SimilarityFunction.EUCLIDEAN)
+    qd = torch.from_numpy(q).cuda()
+    ref = a.ivf_search_device(qd, 5, 8)
+    lists, dist = a.route_dist_device(qd, 8)
+    assert torch.equal(lists, a.route_device(qd, 8))
+    keys = cnt = None
+    for r in range(world):
+        kr, cr = a.scan_pairs_device(qd, 5, 8, deal_pairs(lists, r, world, 64))
+        keys = kr if keys is None else keys + kr
+        cnt = cr if cnt is None else cnt + cr
+    mi, ms, mc = a.merge_pairs_device(5, 8, lists, dist, keys, cnt)
+    torch.cuda.synchronize()
+    assert torch.equal(mi, ref[0]) and torch.equal(ms, ref[1]) and torch.equal(mc, ref[2])
+    radii = oracle.ivf_radii(cent, off, ords, db)
+    ids, sc, n = oracle.ivfflat_search_full(cent, off, ords, db, radii, q, oracle.EUCLIDEAN, 5, 8)
+    every = oracle.ivfflat_search(cent, off, ords, db, q, oracle.EUCLIDEAN, 5, 8)
+    assert sum(not np.array_equal(every[0][j], ids[j]) for j in range(len(q))) > len(q) // 10  # the break fires
+    assert np.array_equal(mc.cpu().numpy(), n)
+    for i in range(len(q)):
+        assert list(mi[i, : n[i]].cpu().numpy()) == list(ids[i, : n[i]]), f"query {i}"
+        assert np.array_equal(ms[i, : n[i]].cpu().numpy(), sc[i, : n[i]]), f"query {i} scores"
+    a.close()
+
+
+def test_ivfflat_pair_split_refuses_harmony_partitions(oracle):
+    import torch
+
+    rng = np.random.default_rng(2)
+    db = rng.standard_normal((500, 8)).astype(np.float32)
+    cent = db[:4].copy()
+    assign = np.argmin(((db[:, None, :] - cent[None]) ** 2).sum(2), 1).astype(np.int32)
+    off, ords = oracle.build_ivf_lists(assign, 4)
+    a = vx.IvfFlatAdapter(nprobe=4)
+    a.build_prebuilt(cent, off, ords, db, vx.SimilarityFunction.EUCLIDEAN)
+    a.set_key_dims([2, None, None, 3])
+    qd = torch.from_numpy(db[:10]).cuda()
+    lists, _ = a.route_dist_device(qd, 4)
+    with pytest.raises(vx.UnsupportedOperationException):
+        a.scan_pairs_device(qd, 5, 4, lists)
+    a.close()

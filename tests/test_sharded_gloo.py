@@ -253,3 +253,90 @@ def test_two_rank_gloo_pair_split_search_matches_unsplit():
         for r in range(2):
             with open(os.path.join(d, f"rank{r}")) as f:
                 assert f.read() == "ok", f"rank {r}"
+
+
+class _SlotFake:
+    """Stands in for IvfFlatAdapter's pair steps on the CPU: per-slot results are the rows of the
+    slot's list scored -|q - x|^2 as int64 keys (score bits above 0xFFFFFFFF - ordinal), and the
+    merge keeps the k best keys of all slots."""
+
+    def __init__(self, db, cent, assign):
+        self.db, self.cent, self.assign = db, cent, assign
+
+    def route_dist_device(self, qs, nprobe):
+        import torch
+
+        d = ((qs.numpy()[:, None, :] - self.cent[None]) ** 2).sum(2).astype(np.float32)
+        o = np.argsort(d, axis=1, kind="stable")[:, :nprobe]
+        return torch.from_numpy(o.astype(np.int32)), torch.from_numpy(np.take_along_axis(d, o, 1))
+
+    @staticmethod
+    def _key(score, ordinal):
+        b = np.float32(score).view(np.uint32).astype(np.uint64)
+        b = np.where(b >> np.uint64(31), ~b & np.uint64(0xFFFFFFFF), b | np.uint64(0x80000000))
+        return ((b << np.uint64(32)) | (np.uint64(0xFFFFFFFF) - np.uint64(ordinal))).astype(np.uint64)
+
+    def scan_pairs_device(self, qs, k, nprobe, lists):
+        import torch
+
+        q, L = qs.numpy(), lists.numpy()
+        keys = np.zeros((L.shape[1], q.shape[0], k), np.uint64)
+        cnt = np.zeros((L.shape[1], q.shape[0]), np.int32)
+        for i in range(q.shape[0]):
+            for s in range(L.shape[1]):
+                if L[i, s] < 0:
+                    continue
+                rows = np.nonzero(self.assign == L[i, s])[0]
+                kk = np.sort(self._key(-((self.db[rows] - q[i]) ** 2).sum(1), rows))[::-1][:k]
+                keys[s, i, : len(kk)], cnt[s, i] = kk, len(kk)
+        return torch.from_numpy(keys.view(np.int64)), torch.from_numpy(cnt)
+
+    def merge_pairs_device(self, k, nprobe, lists, dist, keys, counts):
+        import torch
+
+        ky, ct = keys.numpy().view(np.uint64), counts.numpy()
+        best = np.zeros((ky.shape[1], k), np.uint64)
+        for i in range(ky.shape[1]):
+            allk = np.concatenate([ky[s, i, : ct[s, i]] for s in range(ky.shape[0])])
+            top = np.sort(allk)[::-1][:k]
+            best[i, : len(top)] = top
+        return torch.from_numpy(best.view(np.int64))
+
+
+def _flat_split_worker(rank, world, port, out_dir):
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    try:
+        from oracle import oracle as O
+        from vectors_b200.sharded import ivfflat_search_pair_split
+
+        db = O.gen_mixture(900, 12, 5, 0.4, SEEDS[0], SEEDS[1], False)
+        q = O.gen_mixture(37, 12, 5, 0.4, SEEDS[0], SEEDS[2], False)
+        cent = db[:9].copy()
+        assign = np.argmin(((db[:, None, :] - cent[None]) ** 2).sum(2), 1)
+        fake = _SlotFake(db, cent, assign)
+        got = ivfflat_search_pair_split(fake, torch.from_numpy(q), 6, 4)
+        lists, dd = fake.route_dist_device(torch.from_numpy(q), 4)
+        ref = fake.merge_pairs_device(6, 4, lists, dd, *fake.scan_pairs_device(torch.from_numpy(q), 6, 4, lists))
+        with open(os.path.join(out_dir, f"rank{rank}"), "w") as f:
+            f.write("ok" if torch.equal(got, ref) else "mismatch")
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_rank_gloo_ivfflat_pair_split_matches_unsplit():
+    # ivfflat_search_pair_split: routed lists and distances all-gathered, pairs dealt in runs of
+    # 64, disjoint per-slot results combined by a sum all-reduce, merged on every rank
+    import torch.multiprocessing as mp
+
+    with tempfile.TemporaryDirectory() as d:
+        mp.start_processes(_flat_split_worker, args=(2, _free_port(), d), nprocs=2, join=True, start_method="spawn")
+        for r in range(2):
+            with open(os.path.join(d, f"rank{r}")) as f:
+                assert f.read() == "ok", f"rank {r}"

@@ -66,6 +66,9 @@ SIGNATURES = {
     "vx_ivfpq_search_device": [_P, _P, _I32, _I32, _I32, _I32, _I32, _F32, _P, _P, _P, _P],
     "vx_ivf_route_device": [_P, _P, _I32, _I32, _I32, _P, _P],
     "vx_ivfpq_search_routed_device": [_P, _P, _I32, _I32, _I32, _I32, _I32, _F32, _P, _P, _P, _P, _P],
+    "vx_ivf_route_dist_device": [_P, _P, _I32, _I32, _I32, _P, _P, _P],
+    "vx_ivfflat_scan_pairs_device": [_P, _P, _I32, _I32, _I32, _I32, _P, _P, _P, _P],
+    "vx_ivfflat_merge_pairs_device": [_P, _I32, _I32, _I32, _P, _P, _P, _P, _F32, _P, _P, _P, _P],
     "vx_merge_shards_device": [_I32, _I32, _P, _P, _P, _P, _I32, _I32, _I32, _P, _P, _P, _P],
     "vx_bq_scan_candidates_noalloc": [_P, _P, _I32, _I32, _I32, _P, _P, _P, _P],
 }

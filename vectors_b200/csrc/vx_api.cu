@@ -963,6 +963,56 @@ int search_quantized_scan(vx_index* ix, const float* dq, int nq, int K, int k_ou
 // heap_k (>= k) is the size of the reference's TopKHeap, k the hits returned: they differ when
 // IvfFlatAdapter widens a search (candidateK = ceil(k * overQueryFactor)) and trims it to k,
 // which changes where the EUCLIDEAN early exit stops.
+// The IVF-flat list scan of one chunk's (query, slot) pairs: out [width][qc][K] keys and out_cnt
+// [width][qc] per slot (lists [qc][width]; -1: no list).  qfloor (nullable, zeroed here): each
+// query's K-th best key over the lists scanned so far, which bounds admission in its later
+// lists -- null where every list's own K best are needed (the EUCLIDEAN early exit).  Returns
+// the zero-padded queries [qc][Dp] (the HARMONY scan reads them too).
+float* ivfflat_scan(vx_index* ix, const float* dqc, int qc, int width, int K, const int32_t* lists, uint64_t* qfloor,
+                    uint64_t* out, uint32_t* out_cnt, Scratch& T, cudaStream_t st) {
+  const int dim = ix->dim, Dp = ix->Dp_flat;
+  int32_t* counts = T.alloc<int32_t>(ix->nlist);
+  int32_t* offsets = T.alloc<int32_t>(ix->nlist + 1);
+  int32_t* cursor = T.alloc<int32_t>(ix->nlist);
+  int32_t* pairs = T.alloc<int32_t>((size_t)qc * width);
+  float* qpad = T.alloc<float>((size_t)qc * Dp);
+  float* qnorm = T.alloc<float>(qc);
+  float* tail = T.alloc<float>((size_t)qc * width * 3);
+  const int64_t maxg = (int64_t)qc * width / kFlatGroup + ix->nlist + 1;
+  int2* groups = T.alloc<int2>((size_t)maxg);
+  int32_t* ngroups = T.alloc<int32_t>(2);  // count, dispenser
+  VX_LAUNCH(1, launch_pad_rows(dqc, qc, dim, dim, nullptr, Dp, qpad, st));
+  if (ix->metric == VX_COSINE) VX_LAUNCH(1, launch_row_norms(qpad, qc, dim, Dp, qnorm, st));
+  VX_LAUNCH(3, launch_group_pairs(lists, ix->list_off, qc * width, ix->nlist, counts, offsets, cursor, pairs, st));
+  VX_CUDA(cudaMemsetAsync(out_cnt, 0, (size_t)width * qc * 4, st));
+  if (qfloor) VX_CUDA(cudaMemsetAsync(qfloor, 0, (size_t)qc * 8, st));
+  VX_LAUNCH(1, launch_make_groups(counts, offsets, ix->list_order, ix->nlist, kFlatGroup, groups, ngroups, st));
+  FlatListArgs a{};
+  a.nq = qc;
+  a.dim = dim;
+  a.Dp = Dp;
+  a.nprobe = width;
+  a.metric = ix->metric;
+  a.K = K;
+  a.pairs = pairs;
+  a.pair_count = offsets + ix->nlist;
+  a.groups = groups;
+  a.ngroups = ngroups;
+  a.lists = lists;
+  a.queries = qpad;
+  a.qnorm = qnorm;
+  a.list_off = ix->list_off;
+  a.ordinals = ix->ordinals;
+  a.rows = ix->flat_rows;
+  a.rnorm = ix->flat_norms;
+  a.tail = tail;
+  a.out = out;
+  a.out_cnt = out_cnt;
+  a.floor = qfloor;
+  VX_TIMED(VX_PROF_ADC_SCAN, st, 2, launch_flat_list(a, (int64_t)qc * width, ix->num_sms * 2, st));
+  return qpad;
+}
+
 int search_ivfflat(vx_index* ix, const float* dq, int nq, int k, int heap_k, int nprobe, float min_score,
                    int32_t* d_ids, float* d_scores, int32_t* d_counts, cudaStream_t st, const int32_t* given_lists) {
   const int dim = ix->dim, Dp = ix->Dp_flat;
@@ -988,20 +1038,10 @@ int search_ivfflat(vx_index* ix, const float* dq, int nq, int k, int heap_k, int
     int32_t* routed = T.alloc<int32_t>((size_t)qc * probes);
     int32_t* lists = routed;
     float* ldist = nullptr;
-    int32_t* counts = T.alloc<int32_t>(ix->nlist);
-    int32_t* offsets = T.alloc<int32_t>(ix->nlist + 1);
-    int32_t* cursor = T.alloc<int32_t>(ix->nlist);
-    int32_t* pairs = T.alloc<int32_t>((size_t)qc * width);
-    float* qpad = T.alloc<float>((size_t)qc * Dp);
-    float* qnorm = T.alloc<float>(qc);
-    float* tail = T.alloc<float>((size_t)qc * width * 3);
     uint64_t* out = T.alloc<uint64_t>((size_t)width * qc * K);
     uint32_t* out_cnt = T.alloc<uint32_t>((size_t)width * qc);
     uint64_t* keys = T.alloc<uint64_t>((size_t)qc * K);
     uint32_t* kcnt = T.alloc<uint32_t>(qc);
-    const int64_t maxg = (int64_t)qc * width / kFlatGroup + ix->nlist + 1;
-    int2* groups = T.alloc<int2>((size_t)maxg);
-    int32_t* ngroups = T.alloc<int32_t>(2);  // count, dispenser
     uint64_t* qfloor = early_exit ? nullptr : T.alloc<uint64_t>(qc);
     const bool harmony = early_exit && ix->keyed;
     uint64_t* harm = harmony ? T.alloc<uint64_t>((size_t)width * qc * K) : nullptr;
@@ -1018,35 +1058,7 @@ int search_ivfflat(vx_index* ix, const float* dq, int nq, int k, int heap_k, int
                                          spill ? ix->spill : nullptr, width, lists, ldist, st));
       }
     }
-    VX_LAUNCH(1, launch_pad_rows(dqc, qc, dim, dim, nullptr, Dp, qpad, st));
-    if (ix->metric == VX_COSINE) VX_LAUNCH(1, launch_row_norms(qpad, qc, dim, Dp, qnorm, st));
-    VX_LAUNCH(3, launch_group_pairs(lists, ix->list_off, qc * width, ix->nlist, counts, offsets, cursor, pairs, st));
-    VX_CUDA(cudaMemsetAsync(out_cnt, 0, (size_t)width * qc * 4, st));
-    if (qfloor) VX_CUDA(cudaMemsetAsync(qfloor, 0, (size_t)qc * 8, st));
-    VX_LAUNCH(1, launch_make_groups(counts, offsets, ix->list_order, ix->nlist, kFlatGroup, groups, ngroups, st));
-    FlatListArgs a{};
-    a.nq = qc;
-    a.dim = dim;
-    a.Dp = Dp;
-    a.nprobe = width;
-    a.metric = ix->metric;
-    a.K = K;
-    a.pairs = pairs;
-    a.pair_count = offsets + ix->nlist;
-    a.groups = groups;
-    a.ngroups = ngroups;
-    a.lists = lists;
-    a.queries = qpad;
-    a.qnorm = qnorm;
-    a.list_off = ix->list_off;
-    a.ordinals = ix->ordinals;
-    a.rows = ix->flat_rows;
-    a.rnorm = ix->flat_norms;
-    a.tail = tail;
-    a.out = out;
-    a.out_cnt = out_cnt;
-    a.floor = qfloor;
-    VX_TIMED(VX_PROF_ADC_SCAN, st, 2, launch_flat_list(a, (int64_t)qc * width, ix->num_sms * 2, st));
+    float* qpad = ivfflat_scan(ix, dqc, qc, width, K, lists, qfloor, out, out_cnt, T, st);
     if (harmony) {
       HarmonyArgs h{};
       h.nq = qc;
@@ -1082,6 +1094,71 @@ int search_ivfflat(vx_index* ix, const float* dq, int nq, int k, int heap_k, int
     VX_CUDA(cudaMemcpyAsync(&h_bad, d_bad, 4, cudaMemcpyDeviceToHost, st));
     VX_CUDA(cudaStreamSynchronize(st));
     if (h_bad) return fail(VX_ERR_INVALID_ARGUMENT, "%d routed list ids are outside [-1, nlist)", h_bad);
+  }
+  return VX_OK;
+}
+
+// IVF-flat split across GPUs by (query, list) pair: the scan of the pairs a rank owns (every
+// query's slots in lists [nq][width], -1 for the slots of other ranks) into per-slot results,
+// and the merge of all ranks' per-slot results (summed: each slot's keys come from one rank, the
+// others hold zeros) in route order with the reference's early exit.  Together they give
+// search_ivfflat's results for the same routed lists and distances.
+int ivfflat_scan_pairs(vx_index* ix, const float* dq, int nq, int K, int width, const int32_t* lists,
+                       uint64_t* pair_keys, uint32_t* pair_counts, cudaStream_t st) {
+  const bool early_exit = ix->metric == VX_EUCLIDEAN && ix->radii;
+  Scratch T(st);
+  int32_t* checked = T.alloc<int32_t>((size_t)nq * width);
+  int32_t* d_bad = T.alloc<int32_t>(1);
+  VX_CUDA(cudaMemsetAsync(d_bad, 0, 4, st));
+  VX_LAUNCH(1, launch_copy_lists(lists, nq * width, ix->nlist, checked, d_bad, st));
+  uint64_t* qfloor = early_exit ? nullptr : T.alloc<uint64_t>(nq);
+  VX_CUDA(cudaMemsetAsync(pair_keys, 0, (size_t)width * nq * K * 8, st));
+  ivfflat_scan(ix, dq, nq, width, K, checked, qfloor, pair_keys, pair_counts, T, st);
+  int32_t h_bad = 0;
+  VX_CUDA(cudaMemcpyAsync(&h_bad, d_bad, 4, cudaMemcpyDeviceToHost, st));
+  VX_CUDA(cudaStreamSynchronize(st));
+  if (h_bad) return fail(VX_ERR_INVALID_ARGUMENT, "%d routed list ids are outside [-1, nlist)", h_bad);
+  return VX_OK;
+}
+
+int ivfflat_merge_pairs(vx_index* ix, int nq, int k, int K, int width, const int32_t* lists, const float* ldist,
+                        const uint64_t* pair_keys, const uint32_t* pair_counts, float min_score, int32_t* d_ids,
+                        float* d_scores, int32_t* d_counts, cudaStream_t st) {
+  Scratch T(st);
+  uint64_t* keys = T.alloc<uint64_t>((size_t)nq * K);
+  uint32_t* kcnt = T.alloc<uint32_t>(nq);
+  if (ix->metric == VX_EUCLIDEAN && ix->radii) {
+    VX_TIMED(VX_PROF_MERGE, st, 1,
+             launch_ivf_early_exit(pair_keys, pair_counts, nq, width, K, lists, ldist, ix->radii, ix->metric,
+                                   min_score, nullptr, nullptr, nullptr, keys, kcnt, st));
+  } else {
+    VX_TIMED(VX_PROF_MERGE, st, 1, launch_merge_streams(pair_keys, pair_counts, width, nq, nq, K, K, keys, kcnt, st));
+  }
+  VX_LAUNCH(1, launch_finish_keys(keys, kcnt, nq, K, k, kFinishFloatKey, ix->metric, ix->dim, d_ids, d_scores,
+                                  d_counts, st));
+  VX_LAUNCH(1, launch_min_score(d_scores, nq, k, min_score, d_counts, st));
+  return VX_OK;
+}
+
+// Routing with each routed list's distance (the early exit's bound needs it): lists and
+// distances [nq][min(nprobe, nlist)], nearest first, no SOAR spill.
+int route_ivf_dist(vx_index* ix, const float* dq, int nq, int nprobe, int32_t* d_lists, float* d_dist,
+                   cudaStream_t st) {
+  const int dim = ix->dim;
+  const int probes = std::min(nprobe, ix->nlist);
+  const size_t per_q = (size_t)ix->nlist * 4 + (size_t)dim * 4 + (size_t)probes * 4 + 64;
+  const int64_t qch = std::max<int64_t>(64, (int64_t)(scratch_budget() / per_q));
+  for (int q0 = 0; q0 < nq; q0 += (int)qch) {
+    const int qc = (int)std::min<int64_t>(qch, nq - q0);
+    Scratch T(st);
+    const float* dqc = dq + (size_t)q0 * dim;
+    float* qn = T.alloc<float>((size_t)qc * dim);
+    float* dist = T.alloc<float>((size_t)qc * ix->nlist);
+    int32_t* routed = T.alloc<int32_t>((size_t)qc * probes);
+    VX_TIMED(VX_PROF_ROUTE, st, route_launches(dqc, dim, ix->cent, ix->nlist, ix->metric),
+             launch_route(dqc, qc, dim, ix->cent, ix->nlist, ix->metric, probes, qn, dist, routed, st));
+    VX_LAUNCH(1, launch_route_expand(routed, qc, probes, dist, ix->nlist, ix->metric, 0.0f, nullptr, probes,
+                                     d_lists + (size_t)q0 * probes, d_dist + (size_t)q0 * probes, st));
   }
   return VX_OK;
 }
@@ -2342,6 +2419,66 @@ int vx_ivfpq_search_routed_device(vx_index* ix, const float* d_queries, int32_t 
       return VX_OK;
     }
     return search_ivfpq(ix, d_queries, nq, k, nprobe, rf, min_score, d_ids, d_scores, d_counts, st, d_lists);
+  });
+}
+
+int vx_ivf_route_dist_device(vx_index* ix, const float* d_queries, int32_t nq, int32_t dim, int32_t nprobe,
+                             int32_t* d_lists, float* d_list_dist, void* stream) {
+  return guarded([&]() -> int {
+    if (!ix) return fail(VX_ERR_NULL_POINTER, "index must not be null");
+    if (!d_queries || !d_lists || !d_list_dist) return fail(VX_ERR_NULL_POINTER, "null buffer");
+    if (ix->kind != VX_KIND_IVFPQ && ix->kind != VX_KIND_IVFFLAT) return fail(VX_ERR_UNSUPPORTED, "not an IVF index");
+    if (nq <= 0) return fail(VX_ERR_INVALID_ARGUMENT, "queries must not be empty");
+    if (dim != ix->dim)
+      return fail(VX_ERR_INVALID_ARGUMENT, "Query dimension %d does not match index dimension %d", dim, ix->dim);
+    if (nprobe < 1) return fail(VX_ERR_INVALID_ARGUMENT, "nprobe must be >= 1, got %d", nprobe);
+    VX_CUDA(cudaSetDevice(ix->device));
+    return route_ivf_dist(ix, d_queries, nq, nprobe, d_lists, d_list_dist, (cudaStream_t)stream);
+  });
+}
+
+// Shared checks of the two pair entry points: an IVF-flat index the split serves, k in range.
+static int check_pair_split(vx_index* ix, int32_t nq, int32_t k, int32_t nprobe) {
+  if (!ix) return fail(VX_ERR_NULL_POINTER, "index must not be null");
+  if (ix->kind != VX_KIND_IVFFLAT) return fail(VX_ERR_UNSUPPORTED, "not an IVF-flat index");
+  if (nq <= 0) return fail(VX_ERR_INVALID_ARGUMENT, "queries must not be empty");
+  if (k <= 0) return fail(VX_ERR_INVALID_ARGUMENT, "k must be positive: %d", k);
+  if (nprobe < 1) return fail(VX_ERR_INVALID_ARGUMENT, "nprobe must be >= 1, got %d", nprobe);
+  if (ix->n == 0) return fail(VX_ERR_UNSUPPORTED, "the pair split needs a non-empty index");
+  if (ix->keyed) return fail(VX_ERR_UNSUPPORTED, "partitions with HARMONY key dimensions are searched whole (vx_search_batch)");
+  const int K = (int)std::min<int64_t>(k, ix->n);
+  if (!flat_list_supported(K) || !early_exit_supported(K))
+    return fail(VX_ERR_UNSUPPORTED, "k = %d is larger than the IVF-flat scan keeps (256)", K);
+  return VX_OK;
+}
+
+int vx_ivfflat_scan_pairs_device(vx_index* ix, const float* d_queries, int32_t nq, int32_t dim, int32_t k,
+                                 int32_t nprobe, const int32_t* d_lists, uint64_t* d_pair_keys,
+                                 uint32_t* d_pair_counts, void* stream) {
+  return guarded([&]() -> int {
+    if (int s = check_pair_split(ix, nq, k, nprobe)) return s;
+    if (!d_queries || !d_lists || !d_pair_keys || !d_pair_counts) return fail(VX_ERR_NULL_POINTER, "null buffer");
+    if (dim != ix->dim)
+      return fail(VX_ERR_INVALID_ARGUMENT, "Query dimension %d does not match index dimension %d", dim, ix->dim);
+    VX_CUDA(cudaSetDevice(ix->device));
+    const int K = (int)std::min<int64_t>(k, ix->n);
+    return ivfflat_scan_pairs(ix, d_queries, nq, K, std::min(nprobe, ix->nlist), d_lists, d_pair_keys, d_pair_counts,
+                              (cudaStream_t)stream);
+  });
+}
+
+int vx_ivfflat_merge_pairs_device(vx_index* ix, int32_t nq, int32_t k, int32_t nprobe, const int32_t* d_lists,
+                                  const float* d_list_dist, const uint64_t* d_pair_keys,
+                                  const uint32_t* d_pair_counts, float min_score, int32_t* d_ids, float* d_scores,
+                                  int32_t* d_counts, void* stream) {
+  return guarded([&]() -> int {
+    if (int s = check_pair_split(ix, nq, k, nprobe)) return s;
+    if (!d_lists || !d_list_dist || !d_pair_keys || !d_pair_counts || !d_ids || !d_scores || !d_counts)
+      return fail(VX_ERR_NULL_POINTER, "null buffer");
+    VX_CUDA(cudaSetDevice(ix->device));
+    const int K = (int)std::min<int64_t>(k, ix->n);
+    return ivfflat_merge_pairs(ix, nq, k, K, std::min(nprobe, ix->nlist), d_lists, d_list_dist, d_pair_keys,
+                               d_pair_counts, min_score, d_ids, d_scores, d_counts, (cudaStream_t)stream);
   });
 }
 

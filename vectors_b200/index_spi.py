@@ -697,6 +697,63 @@ class IvfFlatAdapter(IvfPqAdapter):
         self._nlist = nlist
         self._apply_gamma()
 
+    def route_dist_device(self, queries, nprobe: int, stream=None):
+        """Routing with distances: (lists int32, distances float32) [nq][min(nprobe, nlist)],
+        nearest first -- the first step of a search split by (query, list) pair across GPUs."""
+        import torch
+
+        q = queries.contiguous()
+        nq = q.shape[0]
+        w = max(1, min(nprobe, self._nlist))
+        lists = torch.empty((nq, w), dtype=torch.int32, device=q.device)
+        dist = torch.empty((nq, w), dtype=torch.float32, device=q.device)
+        st = stream if stream is not None else torch.cuda.current_stream(q.device).cuda_stream
+        _check(N.lib().vx_ivf_route_dist_device(self._h.ptr, C.c_void_p(q.data_ptr()), nq, q.shape[1], nprobe,
+                                                C.c_void_p(lists.data_ptr()), C.c_void_p(dist.data_ptr()),
+                                                C.c_void_p(st)))
+        return lists, dist
+
+    def scan_pairs_device(self, queries, k: int, nprobe: int, lists, stream=None):
+        """The list scan of the slots of ``lists`` that hold a list id (-1: scanned elsewhere):
+        per-slot keys (int64 view of the 64-bit keys) [w][nq][min(k, n)] and counts (int32)
+        [w][nq], zero in the other slots, so buffers of disjoint slot sets add up."""
+        import torch
+
+        q = queries.contiguous()
+        lst = lists.contiguous()
+        nq = q.shape[0]
+        w = max(1, min(nprobe, self._nlist))
+        if lst.dtype != torch.int32 or tuple(lst.shape) != (nq, w):
+            raise IllegalArgumentException("lists must be an int32 [nq][min(nprobe, nlist)] tensor")
+        kk = max(1, min(k, self._n))
+        keys = torch.empty((w, nq, kk), dtype=torch.int64, device=q.device)
+        cnt = torch.empty((w, nq), dtype=torch.int32, device=q.device)
+        st = stream if stream is not None else torch.cuda.current_stream(q.device).cuda_stream
+        _check(N.lib().vx_ivfflat_scan_pairs_device(self._h.ptr, C.c_void_p(q.data_ptr()), nq, q.shape[1], k, nprobe,
+                                                    C.c_void_p(lst.data_ptr()), C.c_void_p(keys.data_ptr()),
+                                                    C.c_void_p(cnt.data_ptr()), C.c_void_p(st)))
+        return keys, cnt
+
+    def merge_pairs_device(self, k: int, nprobe: int, lists, dist, keys, counts, min_score: float = -3.4028235e38,
+                           stream=None):
+        """The per-slot results of every slot (combined over the GPUs that scanned them) merged
+        per query in route order with IvfIndex.search's EUCLIDEAN early exit (radii held by the
+        index), then minScore: (ids, scores, counts) as ivf_search_device returns them."""
+        import torch
+
+        lst, dst, ky, ct = lists.contiguous(), dist.contiguous(), keys.contiguous(), counts.contiguous()
+        nq = lst.shape[0]
+        ids = torch.empty((nq, k), dtype=torch.int32, device=lst.device)
+        sc = torch.empty((nq, k), dtype=torch.float32, device=lst.device)
+        cnt = torch.empty((nq,), dtype=torch.int32, device=lst.device)
+        st = stream if stream is not None else torch.cuda.current_stream(lst.device).cuda_stream
+        _check(N.lib().vx_ivfflat_merge_pairs_device(self._h.ptr, nq, k, nprobe, C.c_void_p(lst.data_ptr()),
+                                                     C.c_void_p(dst.data_ptr()), C.c_void_p(ky.data_ptr()),
+                                                     C.c_void_p(ct.data_ptr()), float(min_score),
+                                                     C.c_void_p(ids.data_ptr()), C.c_void_p(sc.data_ptr()),
+                                                     C.c_void_p(cnt.data_ptr()), C.c_void_p(st)))
+        return ids, sc, cnt
+
     def set_key_dims(self, key_dims):
         """ClusterPartition.keyDimensions per list (HARMONY; None or an empty list = none): a
         EUCLIDEAN search reaching such a list with a full heap scores its rows with

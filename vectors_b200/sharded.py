@@ -15,7 +15,8 @@ from typing import Callable, Optional, Sequence
 from .index_spi import merge_shards_device, shard_offsets
 
 __all__ = ["shard_range", "gather_and_merge", "gather_rows", "ivf_search_sharded", "search_query_sharded",
-           "assign_lists", "ivf_search_balanced", "deal_pairs", "ivf_search_pair_split"]
+           "assign_lists", "ivf_search_balanced", "deal_pairs", "ivf_search_pair_split",
+           "ivfflat_search_pair_split"]
 
 
 def shard_range(n: int, rank: int, world: int) -> tuple[int, int]:
@@ -191,3 +192,26 @@ def ivf_search_pair_split(adapter, queries, k: int, nprobe: int, group=None):
     mine = deal_pairs(lists, rank, world)
     ids, sc, cnt = adapter.ivf_search_routed_device(queries, k, nprobe, mine, 1)
     return gather_and_merge(ids, sc, cnt, [0] * (world + 1), k, group)
+
+
+def ivfflat_search_pair_split(adapter, queries, k: int, nprobe: int, group=None):
+    """IVF-flat search (IvfIndex.search, IvfIndex.java:170-226) over an index replicated on
+    every rank, split by (query, list) pair: each rank routes its slice of the queries (lists and
+    their distances), both are all-gathered, deal_pairs gives every rank an even share of every
+    list's pairs in runs of 64 (the list scan's query group), each rank scans its pairs into
+    per-slot results, a sum all-reduce combines them (each slot's keys come from one rank, the
+    others hold zeros), and every rank merges all slots per query in route order with the
+    EUCLIDEAN early exit -- the single-GPU result for the same routing.  Not for partitions with
+    HARMONY key dimensions (the library refuses them)."""
+    import torch.distributed as dist
+
+    rank, world = dist.get_rank(group), dist.get_world_size(group)
+    nq = queries.shape[0]
+    lo, hi = shard_range(nq, rank, world)
+    l_loc, d_loc = adapter.route_dist_device(queries[lo:hi], nprobe)
+    lists = gather_rows(l_loc, nq, group)
+    ldist = gather_rows(d_loc, nq, group)
+    keys, cnt = adapter.scan_pairs_device(queries, k, nprobe, deal_pairs(lists, rank, world, 64))
+    dist.all_reduce(keys, op=dist.ReduceOp.SUM, group=group)
+    dist.all_reduce(cnt, op=dist.ReduceOp.SUM, group=group)
+    return adapter.merge_pairs_device(k, nprobe, lists, ldist, keys, cnt)
