@@ -307,6 +307,9 @@ def main():
     ap.add_argument("--ivf-n", type=int, default=IVF["n"])
     ap.add_argument("--ivf-nlist", type=int, default=IVF["nlist"], help="smaller cases for profiling keep n/nlist")
     ap.add_argument("--ivf-nq", type=int, default=IVF["nq"])
+    ap.add_argument("--ivfflat-split", default="auto", choices=["auto", "pair", "query"],
+                    help="IVF-flat at N > 1: deal (query, list) pairs, split the queries, or auto (queries "
+                         "at 2 ranks, pairs from 4)")
     ap.add_argument("--ivf-split", default="auto", choices=["auto", "pair", "query"],
                     help="IVF-PQ at N > 1: deal (query, list) pairs, split the queries, or auto (queries at "
                          "2 ranks, pairs from 4)")
@@ -765,12 +768,12 @@ def _timed_scan(args, world, dev, barrier, max_over_ranks, step, slot):
 def run_ivfflat(args, rank, world, local, dev, barrier, max_over_ranks, peak_kind):
     """IVF-flat (IvfIndex.search without PQ), 1M x 768 EUCLIDEAN, nlist 1024, nprobe 32, 10k
     queries, top-10: routing, then the exact list scan in the reference's batched fp32 order
-    (CUDA cores: the scores must be the reference's to the bit).  The index is replicated and
-    the queries split across ranks, as for IVF-PQ."""
+    (CUDA cores: the scores must be the reference's to the bit).  The index is replicated; the
+    queries (2 ranks) or the (query, list) pairs (4 and more) are split across ranks."""
     import torch
 
     import vectors_b200 as vx
-    from vectors_b200.sharded import search_query_sharded
+    from vectors_b200.sharded import ivfflat_search_pair_split, search_query_sharded
 
     P = IVFFLAT
     n, dim, nlist, nq, k = args.ivfflat_n, P["dim"], P["nlist"], P["nq"], P["k"]
@@ -798,10 +801,18 @@ def run_ivfflat(args, rank, world, local, dev, barrier, max_over_ranks, peak_kin
     probed = torch.cdist(q, cent).topk(P["nprobe"], largest=False).indices
     pair_rows = float(counts[probed].sum().item())
 
+    # auto: the split that measured faster at this rank count (one-GPU emulation of each rank's
+    # own work at 2 / 4 / 8 ranks, and 2 B200s): queries at 2 ranks (1.66M against 1.64M queries/s
+    # on 2 GPUs), from 4 the (query, list) pair split -- every rank scans an even share of every
+    # list's pairs in full 64-query groups, the per-slot results meet in one sum all-reduce
+    split = args.ivfflat_split if args.ivfflat_split != "auto" else ("query" if world <= 2 else "pair")
+
     def step():
         if world == 1:
             return a.ivf_search_device(q, k, P["nprobe"])[0]
-        return search_query_sharded(lambda qs: a.ivf_search_device(qs, k, P["nprobe"]), q)[0]
+        if split == "query":
+            return search_query_sharded(lambda qs: a.ivf_search_device(qs, k, P["nprobe"]), q)[0]
+        return ivfflat_search_pair_split(a, q, k, P["nprobe"])[0]
 
     ms, kms, br = _timed_scan(args, world, dev, barrier, max_over_ranks, step, "adc_scan")
     ops = 2.0 * pair_rows * dim / world  # subtract + fused multiply-add per (query, row, dim)
@@ -832,7 +843,11 @@ def run_ivfflat(args, rank, world, local, dev, barrier, max_over_ranks, peak_kin
                      "unit": "T fp32 ops/s", "frac": (achieved / peak) if achieved else None, "traffic": None,
                      "kernel": "flat_list_kernel (IVF-flat list scan)", "per": "GPU",
                      "peak_source": "nominal: 148 SMs x 128 fp32 lanes x 1.965 GHz",
-                     "pair_rows_per_step": pair_rows, "breakdown_ms_per_step": br},
+                     "pair_rows_per_step": pair_rows, "breakdown_ms_per_step": br,
+                     "sharding": ("single GPU" if world == 1 else "index replicated, queries split across ranks"
+                                  if split == "query" else
+                                  "index replicated, (query, list) pairs dealt across ranks in 64-pair groups, "
+                                  "per-slot results summed (NCCL all-reduce) and merged in route order")},
         "parity": par,
         "cpu_baseline": cpu,
         "e2e": e2e,

@@ -377,6 +377,33 @@ def test_ivfflat_matches_oracle(oracle, metric, dim, nq, k):
     a.close()
 
 
+@pytest.mark.parametrize("metric", [0, 1, 2, 3])
+@pytest.mark.parametrize("k", [10, 100])
+def test_ivfflat_long_lists_in_row_parts_match_oracle(oracle, metric, k):
+    # lists of ~5,000 rows: each is scanned as row parts of 1,024 rows (several groups per list,
+    # a part's K best merged per pair afterwards), and the last part holds the list's trailing
+    # batch; the EUCLIDEAN early exit then runs on the merged per-list results
+    n, nlist, dim = 40_000, 8, 64
+    db = oracle.gen_mixture(n, dim, 8, 0.3, SEED_C, SEED_DB, metric == 2)
+    q = oracle.gen_mixture(150, dim, 8, 0.3, SEED_C, SEED_Q, metric == 2)
+    cent = oracle.kmeans_train(db[:8000], nlist, 8, 42)
+    off, ords = oracle.build_ivf_lists(oracle.kmeans_assign(db, cent), nlist)
+    assert np.diff(off).max() > 2048
+    a = vx.IvfFlatAdapter(nprobe=4)
+    a.build_prebuilt(cent, off, ords, db, vx.SimilarityFunction(metric))
+    got = a.ivf_search(q, k, 4)
+    radii = oracle.ivf_radii(cent, off, ords, db)
+    ids, sc, cnt = oracle.ivfflat_search_full(cent, off, ords, db, radii, q, metric, k, 4)
+    for i, o in enumerate(got):
+        c = cnt[i]
+        assert list(o.ordinals) == list(ids[i, :c]), f"ivfflat parts m={metric} k={k} query {i}"
+        if metric == 2:
+            np.testing.assert_allclose(o.scores, sc[i, :c], rtol=1e-6, atol=0)
+        else:
+            assert np.array_equal(o.scores, sc[i, :c]), f"ivfflat parts m={metric} k={k} query {i} scores"
+    a.close()
+
+
 def _same_outcomes(x, y, tag):
     for i, (u, v) in enumerate(zip(x, y)):
         assert np.array_equal(u.ordinals, v.ordinals) and np.array_equal(u.scores, v.scores), f"{tag} query {i}"

@@ -51,6 +51,7 @@ struct vx_index {
   int nlist = 0;
   int64_t* list_off = nullptr;
   int32_t* list_order = nullptr;  // list ids by row count, longest first (ties by id)
+  int64_t max_list_rows = 0;      // rows of the longest list
   int32_t* ordinals = nullptr;
   uint8_t* pq_codes = nullptr;
   int M = 0, Ks = 0, Mp = 0;

@@ -544,9 +544,12 @@ constexpr int kMChunk = 16;  // subspaces per table chunk
 constexpr int kRowsPerThread = 12;
 constexpr int kRowsPerPass = kAdcThreads * kRowsPerThread;
 
-// Lists in `order` (null: by id), each cut into groups of up to wmax consecutive pairs.
+// Lists in `order` (null: by id), each cut into groups of up to wmax consecutive pairs; with
+// rmax > 0 (the IVF-flat scan) a list longer than rmax rows also into row parts of rmax rows,
+// every pair group once per part: group = (first pair, pairs | part << 8).
 __global__ void make_groups_kernel(const int32_t* __restrict__ counts, const int32_t* __restrict__ offsets,
-                                   const int32_t* __restrict__ order, int nlist, int wmax, int2* __restrict__ groups,
+                                   const int32_t* __restrict__ order, int nlist, int wmax,
+                                   const int64_t* __restrict__ list_off, int rmax, int2* __restrict__ groups,
                                    int32_t* __restrict__ ngroups) {
   __shared__ uint32_t s_red[32];
   __shared__ int32_t s_carry;
@@ -557,7 +560,8 @@ __global__ void make_groups_kernel(const int32_t* __restrict__ counts, const int
     const int i = base + threadIdx.x;
     const int l = i < nlist ? (order ? order[i] : i) : 0;
     const int c = i < nlist ? counts[l] : 0;
-    const int g = (c + wmax - 1) / wmax;
+    const int parts = (rmax > 0 && i < nlist) ? max(1, (int)((list_off[l + 1] - list_off[l] + rmax - 1) / rmax)) : 1;
+    const int g = (c + wmax - 1) / wmax * parts;
     int incl = g;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
@@ -572,7 +576,10 @@ __global__ void make_groups_kernel(const int32_t* __restrict__ counts, const int
       total += (int)s_red[i];
     }
     const int first = before + incl - g;
-    for (int j = 0; j < g; j++) groups[first + j] = make_int2(offsets[l] + j * wmax, min(wmax, c - j * wmax));
+    for (int j = 0; j < g; j++) {
+      const int run = j / parts, part = j - run * parts;
+      groups[first + j] = make_int2(offsets[l] + run * wmax, min(wmax, c - run * wmax) | (part << 8));
+    }
     __syncthreads();
     if (threadIdx.x == 0) s_carry += total;
     __syncthreads();
@@ -916,7 +923,8 @@ __global__ void __launch_bounds__(256, 2) flat_list_kernel(FlatListArgs a) {
     const int gi = s_gi;
     if (gi >= ng) break;
     const int2 grp = a.groups[gi];
-    const int npq = grp.y;
+    const int npq = grp.y & 0xFF;
+    const int part = grp.y >> 8;  // row part of a list longer than a.rmax rows
     if (threadIdx.x < kFlGroup) {
       const int g = threadIdx.x;
       int q = 0, p = 0;
@@ -942,7 +950,12 @@ __global__ void __launch_bounds__(256, 2) flat_list_kernel(FlatListArgs a) {
     const int tail_begin = last + ((n - last) & ~3);
     const float* rows = a.rows + (size_t)b * a.Dp;
     const int nu = npq > 48 ? 4 : (npq + 15) / 16;  // 16-query slices holding pairs
-    for (int r0 = 0; r0 < n; r0 += kRtC) {
+    // this group's rows: the whole list, or part `part` of rmax rows (a multiple of 64, so that
+    // a 32-row tile never straddles two parts and the last 64-row batch lies in the last part)
+    const bool parted = a.rmax > 0 && n > a.rmax;
+    const int r_lo = parted ? part * a.rmax : 0;
+    const int r_hi = parted ? min(n, r_lo + a.rmax) : n;
+    for (int r0 = r_lo; r0 < r_hi; r0 += kRtC) {
       uint64_t acc[4][2][4];  // accumulator lanes (2p, 2p + 1) packed in acc[.][.][p]
 #pragma unroll
       for (int u = 0; u < 4; u++)
@@ -1051,10 +1064,13 @@ __global__ void __launch_bounds__(256, 2) flat_list_kernel(FlatListArgs a) {
         t = warp_min_u64(mn);
       }
       const int q = s_query[g];
-      const size_t sidx = (size_t)s_probe[g] * a.nq + q;
-      for (uint32_t i = lane; i < c; i += 32) a.out[sidx * a.K + i] = kb[i];
+      // a part's K best go to the pair's part slot (merged afterwards); the K-th of a part is a
+      // valid floor too (K rows of the list reach it)
+      const size_t sidx = parted ? (size_t)s_slot[g] * a.pmax + part : (size_t)s_probe[g] * a.nq + q;
+      uint64_t* dst = parted ? a.part_out : a.out;
+      for (uint32_t i = lane; i < c; i += 32) dst[sidx * a.K + i] = kb[i];
       if (lane == 0) {
-        a.out_cnt[sidx] = c;
+        (parted ? a.part_cnt : a.out_cnt)[sidx] = c;
         if (a.floor && c == (uint32_t)a.K) atomicMax((unsigned long long*)&a.floor[q], (unsigned long long)t);
       }
     }
@@ -1511,12 +1527,79 @@ bool adc_group_supported(int M, int Ks, int dim) {
 }
 
 cudaError_t launch_make_groups(const int32_t* counts, const int32_t* offsets, const int32_t* order, int nlist,
-                               int wmax, int2* groups, int32_t* ngroups, cudaStream_t st) {
-  if (wmax < 1) return cudaErrorInvalidValue;
+                               int wmax, int2* groups, int32_t* ngroups, cudaStream_t st, const int64_t* list_off,
+                               int rmax) {
+  if (wmax < 1 || wmax > 255 || (rmax > 0 && !list_off)) return cudaErrorInvalidValue;
   // ngroups[1] is the dispenser the scan kernels take groups from
   cudaError_t e = cudaMemsetAsync(ngroups + 1, 0, sizeof(int32_t), st);
   if (e != cudaSuccess) return e;
-  make_groups_kernel<<<1, 1024, 0, st>>>(counts, offsets, order, nlist, wmax, groups, ngroups);
+  make_groups_kernel<<<1, 1024, 0, st>>>(counts, offsets, order, nlist, wmax, list_off, rmax, groups, ngroups);
+  return cudaGetLastError();
+}
+
+// Row parts of one (query, list) pair: the union of its parts' K best (each part at most K keys,
+// unsorted; ordinals distinct across parts) cut to the K best and written to the pair's slot of
+// out.  One warp per pair position; pairs of single-part lists were written by the scan itself.
+// The parts' keys are first packed to the front of the pair's part area (held in registers in
+// between), then shrunk in place by warp_compact_one.
+template <int R>
+__global__ void flat_parts_merge_kernel(FlatListArgs a) {
+  const int lane = threadIdx.x & 31;
+  const int64_t w = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  if (w >= *a.pair_count) return;
+  const int32_t pair = a.pairs[w];
+  const int l = a.lists[pair];
+  const int n = (int)(a.list_off[l + 1] - a.list_off[l]);
+  if (!(a.rmax > 0 && n > a.rmax)) return;
+  const int parts = (n + a.rmax - 1) / a.rmax;
+  uint64_t* base = a.part_out + (size_t)w * a.pmax * a.K;
+  const uint32_t* cnt = a.part_cnt + (size_t)w * a.pmax;
+  uint64_t e[R];
+  uint32_t mine = 0;
+#pragma unroll
+  for (int r = 0; r < R; r++) {
+    const int i = lane + 32 * r;
+    const int j = i / a.K, o = i - j * a.K;
+    const bool ok = j < parts && o < (int)cnt[j];
+    e[r] = ok ? base[i] : kEmptyKey;
+    mine += ok ? 1u : 0u;
+  }
+  uint32_t incl = mine;
+#pragma unroll
+  for (int d = 1; d < 32; d <<= 1) {
+    const uint32_t v = __shfl_up_sync(0xFFFFFFFFu, incl, d);
+    if (lane >= d) incl += v;
+  }
+  const uint32_t total = __shfl_sync(0xFFFFFFFFu, incl, 31);
+  uint32_t pos = incl - mine;
+  __syncwarp();
+#pragma unroll
+  for (int r = 0; r < R; r++) {
+    const int i = lane + 32 * r;
+    const int j = i / a.K, o = i - j * a.K;
+    if (j < parts && o < (int)cnt[j]) base[pos++] = e[r];
+  }
+  __syncwarp();
+  uint32_t c = total;
+  uint64_t t = 0;
+  if (c > (uint32_t)a.K) warp_compact_one<R>(base, c, (uint32_t)a.K, t, c);
+  const int q = pair / a.nprobe, p = pair - q * a.nprobe;
+  const size_t sidx = (size_t)p * a.nq + q;
+  for (uint32_t i = lane; i < c; i += 32) a.out[sidx * a.K + i] = base[i];
+  if (lane == 0) a.out_cnt[sidx] = c;
+}
+
+cudaError_t launch_flat_parts_merge(const FlatListArgs& a, int64_t pair_slots, cudaStream_t st) {
+  if (pair_slots <= 0 || a.rmax <= 0 || a.pmax <= 1) return cudaSuccess;
+  const int keys = a.pmax * a.K;
+  if (keys > kFlatPartKeysMax) return cudaErrorInvalidValue;
+  const unsigned grid = (unsigned)((pair_slots * 32 + 255) / 256);
+  if (keys <= 32) flat_parts_merge_kernel<1><<<grid, 256, 0, st>>>(a);
+  else if (keys <= 64) flat_parts_merge_kernel<2><<<grid, 256, 0, st>>>(a);
+  else if (keys <= 128) flat_parts_merge_kernel<4><<<grid, 256, 0, st>>>(a);
+  else if (keys <= 256) flat_parts_merge_kernel<8><<<grid, 256, 0, st>>>(a);
+  else if (keys <= 512) flat_parts_merge_kernel<16><<<grid, 256, 0, st>>>(a);
+  else flat_parts_merge_kernel<32><<<grid, 256, 0, st>>>(a);
   return cudaGetLastError();
 }
 

@@ -51,11 +51,14 @@ cudaError_t launch_adc_scan(const AdcArgs& a, int R, int grid, cudaStream_t st);
 // pairs sharing a list are taken up to four at a time.
 constexpr int kAdcGroupQ = 4;
 bool adc_group_supported(int M, int Ks, int dim);
-// Groups of up to `wmax` consecutive pairs of one list: groups[i] = (first pair slot, pairs),
-// lists taken in `order` (null: by id; longest first balances the scans).  ngroups[0] is the
-// count and ngroups[1] the dispenser the grouped scans take groups from (zeroed here).
+// Groups of up to `wmax` (<= 255) consecutive pairs of one list: groups[i] = (first pair slot,
+// pairs), lists taken in `order` (null: by id; longest first balances the scans).  With rmax > 0
+// a list of more than rmax rows (list_off) gives each pair group once per row part of rmax
+// rows: groups[i].y = pairs | part << 8.  ngroups[0] is the count and ngroups[1] the dispenser
+// the grouped scans take groups from (zeroed here).
 cudaError_t launch_make_groups(const int32_t* counts, const int32_t* offsets, const int32_t* order, int nlist,
-                               int wmax, int2* groups, int32_t* ngroups, cudaStream_t st);
+                               int wmax, int2* groups, int32_t* ngroups, cudaStream_t st,
+                               const int64_t* list_off = nullptr, int rmax = 0);
 cudaError_t launch_adc_group(const AdcArgs& a, int R, int grid, cudaStream_t st);
 
 // IVF-flat list scan (IvfIndex.search without PQ): pairs grouped by list, up to 64 per group.
@@ -77,6 +80,13 @@ struct FlatListArgs {
   uint32_t* out_cnt;          // [nprobe][nq]
   uint64_t* floor;            // [nq] per-query admission floor across lists (zeroed); null: each
                               // (query, list) keeps its own best K (the early exit's input)
+  // Row parts (rmax > 0): a list of more than rmax rows is scanned by one group per part of rmax
+  // rows (a multiple of 64), so that no single group bounds the kernel; each part's K best go to
+  // part_out [pair position][pmax][K] / part_cnt [pair position][pmax] (pair position: index into
+  // pairs) and launch_flat_parts_merge combines the parts into out.
+  int rmax, pmax;
+  uint64_t* part_out;
+  uint32_t* part_cnt;
 };
 constexpr int kFlatGroup = 64;
 // Keys kept per (query, list) that the scan supports: K <= 256.
@@ -86,6 +96,10 @@ cudaError_t launch_pad_rows(const float* src, int64_t n, int dim, int64_t src_st
 cudaError_t launch_row_norms(const float* rows, int64_t n, int dim, int Dp, float* out, cudaStream_t st);
 // flat_tail_kernel then flat_list_kernel (2 launches)
 cudaError_t launch_flat_list(const FlatListArgs& a, int64_t pair_slots, int grid, cudaStream_t st);
+// The row parts of every pair whose list has more than one (a.rmax > 0): the K best of the
+// parts' keys into out / out_cnt, one warp per pair; pmax * K <= kFlatPartKeysMax.
+constexpr int kFlatPartKeysMax = 1024;
+cudaError_t launch_flat_parts_merge(const FlatListArgs& a, int64_t pair_slots, cudaStream_t st);
 
 // PQVectors (PQVectors.java:62-89, 148-166): |q - gc| per query (sequential sum of squares,
 // (float) Math.sqrt), and per row the sequential sum over subspaces of the centroids' squared

@@ -337,6 +337,8 @@ float* upload_rows32(vx_index* ix, const float* host, int64_t n, int dim, int64_
 int32_t* upload_list_order(vx_index* ix, const int64_t* list_offsets, int nlist) {
   std::vector<int32_t> order(nlist);
   for (int l = 0; l < nlist; l++) order[l] = l;
+  ix->max_list_rows = 0;
+  for (int l = 0; l < nlist; l++) ix->max_list_rows = std::max(ix->max_list_rows, list_offsets[l + 1] - list_offsets[l]);
   std::stable_sort(order.begin(), order.end(), [&](int32_t x, int32_t y) {
     return list_offsets[x + 1] - list_offsets[x] > list_offsets[y + 1] - list_offsets[y];
   });
@@ -963,6 +965,9 @@ int search_quantized_scan(vx_index* ix, const float* dq, int nq, int K, int k_ou
 // heap_k (>= k) is the size of the reference's TopKHeap, k the hits returned: they differ when
 // IvfFlatAdapter widens a search (candidateK = ceil(k * overQueryFactor)) and trims it to k,
 // which changes where the EUCLIDEAN early exit stops.
+constexpr int64_t kFlatPartRows = 1024;              // rows per part of a long list (a multiple of 64)
+constexpr size_t kFlatPartBytes = (size_t)512 << 20;  // cap on the parts' key buffer of one chunk
+
 // The IVF-flat list scan of one chunk's (query, slot) pairs: out [width][qc][K] keys and out_cnt
 // [width][qc] per slot (lists [qc][width]; -1: no list).  qfloor (nullable, zeroed here): each
 // query's K-th best key over the lists scanned so far, which bounds admission in its later
@@ -978,15 +983,34 @@ float* ivfflat_scan(vx_index* ix, const float* dqc, int qc, int width, int K, co
   float* qpad = T.alloc<float>((size_t)qc * Dp);
   float* qnorm = T.alloc<float>(qc);
   float* tail = T.alloc<float>((size_t)qc * width * 3);
-  const int64_t maxg = (int64_t)qc * width / kFlatGroup + ix->nlist + 1;
+  // Lists longer than kFlatPartRows rows are scanned in row parts (one group per part), so that
+  // the longest list does not bound the kernel; the parts' results take pmax * K keys per pair
+  // slot, kept within kFlatPartBytes (fewer, longer parts when that would be exceeded).
+  const size_t slots = (size_t)qc * width;
+  int rmax = 0, pmax = 1;
+  if (ix->max_list_rows > kFlatPartRows) {
+    const int64_t cap = std::max<int64_t>(
+        1, std::min<int64_t>((int64_t)(kFlatPartBytes / (slots * (size_t)K * 8 + 1)), kFlatPartKeysMax / K));
+    int64_t r = kFlatPartRows;
+    while ((ix->max_list_rows + r - 1) / r > cap) r *= 2;
+    if ((ix->max_list_rows + r - 1) / r > 1) {
+      rmax = (int)r;
+      pmax = (int)((ix->max_list_rows + r - 1) / r);
+    }
+  }
+  const int64_t maxg = ((int64_t)qc * width / kFlatGroup + ix->nlist + 1) * pmax;
   int2* groups = T.alloc<int2>((size_t)maxg);
   int32_t* ngroups = T.alloc<int32_t>(2);  // count, dispenser
+  uint64_t* part_out = pmax > 1 ? T.alloc<uint64_t>(slots * pmax * K) : nullptr;
+  uint32_t* part_cnt = pmax > 1 ? T.alloc<uint32_t>(slots * pmax) : nullptr;
   VX_LAUNCH(1, launch_pad_rows(dqc, qc, dim, dim, nullptr, Dp, qpad, st));
   if (ix->metric == VX_COSINE) VX_LAUNCH(1, launch_row_norms(qpad, qc, dim, Dp, qnorm, st));
   VX_LAUNCH(3, launch_group_pairs(lists, ix->list_off, qc * width, ix->nlist, counts, offsets, cursor, pairs, st));
   VX_CUDA(cudaMemsetAsync(out_cnt, 0, (size_t)width * qc * 4, st));
+  if (part_cnt) VX_CUDA(cudaMemsetAsync(part_cnt, 0, slots * pmax * 4, st));
   if (qfloor) VX_CUDA(cudaMemsetAsync(qfloor, 0, (size_t)qc * 8, st));
-  VX_LAUNCH(1, launch_make_groups(counts, offsets, ix->list_order, ix->nlist, kFlatGroup, groups, ngroups, st));
+  VX_LAUNCH(1, launch_make_groups(counts, offsets, ix->list_order, ix->nlist, kFlatGroup, groups, ngroups, st,
+                                  ix->list_off, rmax));
   FlatListArgs a{};
   a.nq = qc;
   a.dim = dim;
@@ -1009,7 +1033,12 @@ float* ivfflat_scan(vx_index* ix, const float* dqc, int qc, int width, int K, co
   a.out = out;
   a.out_cnt = out_cnt;
   a.floor = qfloor;
+  a.rmax = rmax;
+  a.pmax = pmax;
+  a.part_out = part_out;
+  a.part_cnt = part_cnt;
   VX_TIMED(VX_PROF_ADC_SCAN, st, 2, launch_flat_list(a, (int64_t)qc * width, ix->num_sms * 2, st));
+  if (pmax > 1) VX_LAUNCH(1, launch_flat_parts_merge(a, (int64_t)qc * width, st));
   return qpad;
 }
 
