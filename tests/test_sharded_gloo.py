@@ -112,6 +112,8 @@ def _qshard_worker(rank, world, port, nq, out_dir):
         q = O.gen_mixture(nq, 48, 8, 0.3, SEEDS[0], SEEDS[2], True)
 
         def search(qs):
+            if qs.shape[0] == 0:
+                raise ValueError("queries must not be empty")  # as the library refuses them
             ids, sc, cnt = O.flat_search(db, qs.numpy(), O.DOT_PRODUCT, 7)
             return torch.from_numpy(ids), torch.from_numpy(sc), torch.from_numpy(cnt)
 
@@ -125,7 +127,7 @@ def _qshard_worker(rank, world, port, nq, out_dir):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("nq", [9, 10])
+@pytest.mark.parametrize("nq", [9, 10, 1])
 def test_two_rank_gloo_query_sharded_search(nq):
     # the replicated-index mode of the IVF-PQ benchmark: queries split, results all-gathered
     import torch.multiprocessing as mp
@@ -187,6 +189,8 @@ class _ListScanFake:
     def route_device(self, qs, nprobe):
         import torch
 
+        if qs.shape[0] == 0:
+            raise ValueError("queries must not be empty")  # as the library refuses them
         q = qs.numpy()
         d = ((q[:, None, :] - self.cent[None, :, :]) ** 2).sum(2)
         return torch.from_numpy(np.argsort(d, axis=1, kind="stable")[:, :nprobe].astype(np.int32))
@@ -206,7 +210,7 @@ class _ListScanFake:
         return torch.from_numpy(ids), torch.from_numpy(sc), torch.from_numpy(cnt)
 
 
-def _pair_split_worker(rank, world, port, out_dir):
+def _pair_split_worker(rank, world, port, out_dir, nq=41):
     import datetime
 
     import torch
@@ -220,7 +224,7 @@ def _pair_split_worker(rank, world, port, out_dir):
         from oracle import oracle as O
 
         db = O.gen_mixture(1500, 16, 6, 0.4, SEEDS[0], SEEDS[1], False)
-        q = O.gen_mixture(41, 16, 6, 0.4, SEEDS[0], SEEDS[2], False)
+        q = O.gen_mixture(nq, 16, 6, 0.4, SEEDS[0], SEEDS[2], False)
         cent = db[:12].copy()
         assign = np.argmin(((db[:, None, :] - cent[None]) ** 2).sum(2), 1)
         fake = _ListScanFake(db, cent, assign)
@@ -243,13 +247,16 @@ def _pair_split_worker(rank, world, port, out_dir):
         dist.destroy_process_group()
 
 
-def test_two_rank_gloo_pair_split_search_matches_unsplit():
+@pytest.mark.parametrize("nq", [41, 1])
+def test_two_rank_gloo_pair_split_search_matches_unsplit(nq):
     # ivf_search_pair_split: queries routed per rank, lists all-gathered, pairs dealt, per-rank
-    # top-k merged; equals the search over every routed pair on one rank
+    # top-k merged; equals the search over every routed pair on one rank (one query: a rank
+    # with an empty slice still takes part in the collectives)
     import torch.multiprocessing as mp
 
     with tempfile.TemporaryDirectory() as d:
-        mp.start_processes(_pair_split_worker, args=(2, _free_port(), d), nprocs=2, join=True, start_method="spawn")
+        mp.start_processes(_pair_split_worker, args=(2, _free_port(), d, nq), nprocs=2, join=True,
+                           start_method="spawn")
         for r in range(2):
             with open(os.path.join(d, f"rank{r}")) as f:
                 assert f.read() == "ok", f"rank {r}"
@@ -266,6 +273,8 @@ class _SlotFake:
     def route_dist_device(self, qs, nprobe):
         import torch
 
+        if qs.shape[0] == 0:
+            raise ValueError("queries must not be empty")  # as the library refuses them
         d = ((qs.numpy()[:, None, :] - self.cent[None]) ** 2).sum(2).astype(np.float32)
         o = np.argsort(d, axis=1, kind="stable")[:, :nprobe]
         return torch.from_numpy(o.astype(np.int32)), torch.from_numpy(np.take_along_axis(d, o, 1))
@@ -303,7 +312,7 @@ class _SlotFake:
         return torch.from_numpy(best.view(np.int64))
 
 
-def _flat_split_worker(rank, world, port, out_dir):
+def _flat_split_worker(rank, world, port, out_dir, nq=37):
     import datetime
 
     import torch
@@ -317,7 +326,7 @@ def _flat_split_worker(rank, world, port, out_dir):
         from vectors_b200.sharded import ivfflat_search_pair_split
 
         db = O.gen_mixture(900, 12, 5, 0.4, SEEDS[0], SEEDS[1], False)
-        q = O.gen_mixture(37, 12, 5, 0.4, SEEDS[0], SEEDS[2], False)
+        q = O.gen_mixture(nq, 12, 5, 0.4, SEEDS[0], SEEDS[2], False)
         cent = db[:9].copy()
         assign = np.argmin(((db[:, None, :] - cent[None]) ** 2).sum(2), 1)
         fake = _SlotFake(db, cent, assign)
@@ -330,13 +339,15 @@ def _flat_split_worker(rank, world, port, out_dir):
         dist.destroy_process_group()
 
 
-def test_two_rank_gloo_ivfflat_pair_split_matches_unsplit():
+@pytest.mark.parametrize("nq", [37, 1])
+def test_two_rank_gloo_ivfflat_pair_split_matches_unsplit(nq):
     # ivfflat_search_pair_split: routed lists and distances all-gathered, pairs dealt in runs of
     # 64, disjoint per-slot results combined by a sum all-reduce, merged on every rank
     import torch.multiprocessing as mp
 
     with tempfile.TemporaryDirectory() as d:
-        mp.start_processes(_flat_split_worker, args=(2, _free_port(), d), nprocs=2, join=True, start_method="spawn")
+        mp.start_processes(_flat_split_worker, args=(2, _free_port(), d, nq), nprocs=2, join=True,
+                           start_method="spawn")
         for r in range(2):
             with open(os.path.join(d, f"rank{r}")) as f:
                 assert f.read() == "ok", f"rank {r}"

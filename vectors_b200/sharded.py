@@ -25,6 +25,16 @@ def shard_range(n: int, rank: int, world: int) -> tuple[int, int]:
     return offs[rank], offs[rank + 1]
 
 
+def _slice_call(fn, queries, lo: int, hi: int):
+    """fn(queries[lo:hi]); a rank whose slice is empty (fewer queries than ranks) calls fn on one
+    query and keeps none of its rows -- the library refuses empty batches, and every rank must
+    still reach the collectives that follow with tensors of the right trailing shape."""
+    if hi > lo:
+        return fn(queries[lo:hi])
+    out = fn(queries[:1])
+    return tuple(t[:0] for t in out) if isinstance(out, tuple) else out[:0]
+
+
 def gather_and_merge(local_ids, local_scores, local_counts, offsets: Sequence[int], k: int,
                      group=None, merge: Optional[Callable] = None):
     """All-gathers every rank's (ids [nq][kin], scores [nq][kin], counts [nq]) tensors and
@@ -86,7 +96,8 @@ def ivf_search_sharded(adapter, queries, k: int, nprobe: int, offsets: Sequence[
 
     rank, world = dist.get_rank(group), dist.get_world_size(group)
     lo, hi = shard_range(queries.shape[0], rank, world)
-    lists = gather_rows(adapter.route_device(queries[lo:hi], nprobe), queries.shape[0], group)
+    lists = gather_rows(_slice_call(lambda qs: adapter.route_device(qs, nprobe), queries, lo, hi),
+                        queries.shape[0], group)
     ids, sc, cnt = adapter.ivf_search_routed_device(queries, k, nprobe, lists, rescore_factor)
     return gather_and_merge(ids, sc, cnt, offsets, k, group)
 
@@ -101,7 +112,7 @@ def search_query_sharded(search, queries, group=None):
     rank, world = dist.get_rank(group), dist.get_world_size(group)
     nq = queries.shape[0]
     lo, hi = shard_range(nq, rank, world)
-    ids, sc, cnt = search(queries[lo:hi])
+    ids, sc, cnt = _slice_call(search, queries, lo, hi)
     return gather_rows(ids, nq, group), gather_rows(sc, nq, group), gather_rows(cnt, nq, group)
 
 
@@ -142,7 +153,7 @@ def ivf_search_balanced(adapter, queries, k: int, nprobe: int, list_rows, group=
     rank, world = dist.get_rank(group), dist.get_world_size(group)
     nq = queries.shape[0]
     lo, hi = shard_range(nq, rank, world)
-    lists = gather_rows(adapter.route_device(queries[lo:hi], nprobe), nq, group)
+    lists = gather_rows(_slice_call(lambda qs: adapter.route_device(qs, nprobe), queries, lo, hi), nq, group)
     flat = lists.reshape(-1).long()
     pairs = torch.bincount(flat[flat >= 0], minlength=list_rows.shape[0])
     owner = assign_lists(pairs, list_rows, world)
@@ -188,7 +199,7 @@ def ivf_search_pair_split(adapter, queries, k: int, nprobe: int, group=None):
     rank, world = dist.get_rank(group), dist.get_world_size(group)
     nq = queries.shape[0]
     lo, hi = shard_range(nq, rank, world)
-    lists = gather_rows(adapter.route_device(queries[lo:hi], nprobe), nq, group)
+    lists = gather_rows(_slice_call(lambda qs: adapter.route_device(qs, nprobe), queries, lo, hi), nq, group)
     mine = deal_pairs(lists, rank, world)
     ids, sc, cnt = adapter.ivf_search_routed_device(queries, k, nprobe, mine, 1)
     return gather_and_merge(ids, sc, cnt, [0] * (world + 1), k, group)
@@ -208,7 +219,7 @@ def ivfflat_search_pair_split(adapter, queries, k: int, nprobe: int, group=None)
     rank, world = dist.get_rank(group), dist.get_world_size(group)
     nq = queries.shape[0]
     lo, hi = shard_range(nq, rank, world)
-    l_loc, d_loc = adapter.route_dist_device(queries[lo:hi], nprobe)
+    l_loc, d_loc = _slice_call(lambda qs: adapter.route_dist_device(qs, nprobe), queries, lo, hi)
     lists = gather_rows(l_loc, nq, group)
     ldist = gather_rows(d_loc, nq, group)
     keys, cnt = adapter.scan_pairs_device(queries, k, nprobe, deal_pairs(lists, rank, world, 64))
