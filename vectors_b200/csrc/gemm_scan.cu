@@ -283,10 +283,10 @@ __device__ __forceinline__ float group_max(uint32_t (&v)[32], int c0, const floa
 }
 
 // Pooled-floor check after row tile li (0-based) of a unit's range: right after its first
-// tiles, then every 16th (every 4th and every 8th measured slower: the checks' loads cost more
+// tiles, then every 32nd (every 4th, 8th and 16th measured slower: the checks' loads cost more
 // than the earlier floors save).
 __device__ __forceinline__ bool pool_check_due(int64_t li) {
-  return li < 16 ? (li == 0 || li == 1 || li == 3 || li == 7 || li == 15) : ((li & 15) == 15);
+  return li < 32 ? (li == 0 || li == 1 || li == 3 || li == 7 || li == 15 || li == 31) : ((li & 31) == 31);
 }
 
 template <bool kI8, int kMode, int R, bool k2Sm, int kEpi>
@@ -602,7 +602,7 @@ __global__ void __launch_bounds__(64 + 32 * kEpi, 1)
         }
       }
       // Pooled floor: propose this stream's j-th best key when enough streams of the query
-      // match it (staggered: each unit checks every 16th row tile).
+      // match it (staggered: each unit checks every 32nd row tile).
       if (a.top1 && pool_check_due(nt - nt_first)) {
         const uint64_t mine = a.pool_j == 1 ? ts.t1 : ts.t2;
         const uint64_t* arr = a.pool_j == 1 ? a.top1 : a.top2;
