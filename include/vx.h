@@ -300,7 +300,8 @@ VX_API int vx_ivfpq_search_routed_device(vx_index* index, const float* d_queries
  * them.  Merge: the combined per-slot results taken in route order with the EUCLIDEAN early
  * exit when the index holds BuoyIndex radii (else the k best of all slots), then minScore, into
  * d_ids / d_scores [nq][k] and d_counts [nq].  Not for partitions with HARMONY key dimensions
- * or k above 256 (VX_ERR_UNSUPPORTED); no SOAR spill (gamma is not applied). */
+ * or k above 256 (VX_ERR_UNSUPPORTED); no SOAR spill (gamma is not applied).  The scan takes
+ * the whole batch in one pass (its scratch grows with nq); callers split very large batches. */
 VX_API int vx_ivf_route_dist_device(vx_index* index, const float* d_queries, int32_t nq, int32_t dim,
                                     int32_t nprobe, int32_t* d_lists, float* d_list_dist, void* stream);
 VX_API int vx_ivfflat_scan_pairs_device(vx_index* index, const float* d_queries, int32_t nq, int32_t dim,

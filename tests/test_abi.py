@@ -178,3 +178,19 @@ def test_build_argument_statuses_before_the_gpu():
                               C.byref(out)) == N.VX_ERR_INVALID_ARGUMENT
     assert "out of range" in N.last_error()
     assert not out.value
+
+
+def test_pair_split_entry_points_check_arguments_before_the_gpu():
+    # vx_ivf_route_dist_device / vx_ivfflat_scan_pairs_device / vx_ivfflat_merge_pairs_device:
+    # null handles and buffers are refused before any device work
+    import ctypes as C
+
+    import vectors_b200._native as N
+
+    L = N.lib()
+    buf = np.zeros(64, np.float32).ctypes.data_as(C.c_void_p)
+    assert L.vx_ivf_route_dist_device(None, buf, 1, 4, 1, buf, buf, None) == N.VX_ERR_NULL_POINTER
+    assert L.vx_ivfflat_scan_pairs_device(None, buf, 1, 4, 1, 1, buf, buf, buf, None) == N.VX_ERR_NULL_POINTER
+    assert L.vx_ivfflat_merge_pairs_device(None, 1, 1, 1, buf, buf, buf, buf, 0.0, buf, buf, buf,
+                                           None) == N.VX_ERR_NULL_POINTER
+    assert "null" in N.last_error()

@@ -2475,6 +2475,8 @@ static int check_pair_split(vx_index* ix, int32_t nq, int32_t k, int32_t nprobe)
   if (nprobe < 1) return fail(VX_ERR_INVALID_ARGUMENT, "nprobe must be >= 1, got %d", nprobe);
   if (ix->n == 0) return fail(VX_ERR_UNSUPPORTED, "the pair split needs a non-empty index");
   if (ix->keyed) return fail(VX_ERR_UNSUPPORTED, "partitions with HARMONY key dimensions are searched whole (vx_search_batch)");
+  if ((int64_t)nq * std::min(nprobe, ix->nlist) > INT32_MAX)
+    return fail(VX_ERR_INVALID_ARGUMENT, "nq * nprobe slots exceed one call (%d queries): split the batch", nq);
   const int K = (int)std::min<int64_t>(k, ix->n);
   if (!flat_list_supported(K) || !early_exit_supported(K))
     return fail(VX_ERR_UNSUPPORTED, "k = %d is larger than the IVF-flat scan keeps (256)", K);
